@@ -1,0 +1,128 @@
+"""Native sm_100a operators.
+
+`native()` returns the compiled extension; every wrapper here calls it directly, so a missing
+build fails loudly on a CUDA machine instead of silently running a PyTorch fallback.  The
+pure-PyTorch restatements of the same ops live in `saelens_b200.ops.reference` and serve as
+the CPU oracle in tests.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from saelens_b200.ops._build import load as _load
+from saelens_b200.ops.status import StatusWord
+
+__all__ = [
+    "native",
+    "available",
+    "gemm_tn",
+    "row_topk",
+    "decode_mse",
+    "StatusWord",
+]
+
+
+def native():
+    return _load()
+
+
+def available() -> bool:
+    """True when the extension is built and a CUDA device is present."""
+    if not torch.cuda.is_available():
+        return False
+    try:
+        _load()
+    except ImportError:
+        return False
+    return True
+
+
+def gemm_tn(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    scale: torch.Tensor | None = None,
+    relu: bool = False,
+    out: torch.Tensor | None = None,
+    chunk_max: bool = False,
+    status: StatusWord | None = None,
+    max_ctas: int = 0,
+) -> tuple[torch.Tensor | None, torch.Tensor | None]:
+    """`epilogue(a @ b.T)` on the tcgen05 tensor cores.
+
+    a: [M, K] bf16, b: [N, K] bf16 (K contiguous, K % 64 == 0, N % 256 == 0).
+    Epilogue: `(acc + bias) * scale`, optional ReLU, rounded to bf16.  With `chunk_max` it also
+    returns the max of every 32-column chunk ([M, N/32] bf16).
+    """
+    M, N = a.shape[0], b.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
+    cmax = torch.empty(M, N // 32, dtype=torch.bfloat16, device=a.device) if chunk_max else None
+    st = status or StatusWord(a.device)
+    native().gemm_tn_bf16(a, b, bias, scale, relu, out, cmax, st.tensor, max_ctas)
+    if status is None:
+        st.check("gemm_tn")
+    return out, cmax
+
+
+def row_topk(
+    h: torch.Tensor,
+    cmax: torch.Tensor,
+    k: int,
+    k_dev: torch.Tensor | None = None,
+    mask_words: torch.Tensor | None = None,
+    status: StatusWord | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Exact per-row top-k of bf16 `h` ([M, N]) using its chunk maxima `cmax` ([M, N/32]).
+
+    Returns (values fp32 [M, k], indices int32 [M, k]); unused slots hold index -1.
+    Ties at the k-th value are broken by the smaller column index.
+    """
+    M = h.shape[0]
+    vals = torch.empty(M, k, dtype=torch.float32, device=h.device)
+    idx = torch.empty(M, k, dtype=torch.int32, device=h.device)
+    st = status or StatusWord(h.device)
+    native().row_topk(h, cmax, k, k_dev, mask_words, vals, idx, st.tensor)
+    if status is None:
+        st.check("row_topk")
+    return vals, idx
+
+
+def decode_mse(
+    vals: torch.Tensor,
+    idx: torch.Tensor,
+    w: torch.Tensor,
+    target: torch.Tensor,
+    inv_scale: torch.Tensor | None = None,
+    bias: torch.Tensor | None = None,
+    relu: bool = True,
+    want_out: bool = True,
+    want_resid: bool = False,
+    grad_coef: float = 0.0,
+    grad_coef_dev: torch.Tensor | None = None,
+    want_bsum: bool = False,
+) -> dict[str, torch.Tensor]:
+    """Sparse decode `sum_i a_i w[idx_i] + bias` and its squared error against `target`."""
+    M, D = target.shape
+    dev = target.device
+    res: dict[str, torch.Tensor] = {}
+    out = torch.empty(M, D, dtype=torch.bfloat16, device=dev) if want_out else None
+    resid = torch.empty(M, D, dtype=torch.bfloat16, device=dev) if want_resid else None
+    dx = torch.empty(M, D, dtype=torch.bfloat16, device=dev) if (grad_coef != 0.0) else None
+    loss_row = torch.empty(M, dtype=torch.float32, device=dev)
+    bsum = torch.zeros(D, dtype=torch.float32, device=dev) if want_bsum else None
+    native().decode_mse(
+        vals, idx, relu, inv_scale, w, bias, target, out, resid, dx, grad_coef_dev,
+        float(grad_coef), loss_row, bsum,
+    )
+    res["loss_row"] = loss_row
+    if out is not None:
+        res["out"] = out
+    if resid is not None:
+        res["resid"] = resid
+    if dx is not None:
+        res["dxhat"] = dx
+    if bsum is not None:
+        res["bsum"] = bsum
+    return res

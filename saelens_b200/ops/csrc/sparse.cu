@@ -1,0 +1,604 @@
+// Sparse (k-active) decode, MSE, latent-major (CSC) gradient assembly for TopK-family SAEs.
+//
+// Reference path being replaced (sae_lens/saes/topk_sae.py:645-674, sae.py:986-996):
+//   feature_acts = scatter(relu(topk(hidden_pre)))            # dense [B, d_sae]
+//   sae_out      = (feature_acts / ||W_dec||) @ W_dec + b_dec  # dense GEMM, B x d_sae x d_in
+//   mse          = ((sae_out - x)^2).sum(-1).mean()
+//   backward: dense GEMMs for dW_dec, dFeature, dW_enc and dSaeIn.
+// Here every product touches only the k selected latents of each row:
+//   decode:  x_hat[b] = sum_i a[b,i] W_dec[idx[b,i]] + b_dec,   a = relu(h) / ||W_dec||
+//   grads:   for each latent j over the rows b that selected it (CSC lists)
+//              gW_dec[j] = sum_b a[b,j] dXhat[b]
+//              dz[b,j]   = <dXhat[b], W_dec[j]> * 1[a>0]
+//              gW_enc[j] = sum_b dz[b,j] (x[b] - b_dec),   gb_enc[j] = sum_b dz[b,j]
+//            (the ||W_dec|| factors cancel exactly between the top-k rescale and the decode)
+//   b_dec:   gb_dec = sum_b dXhat[b] - sum_j gb_enc[j] W_enc[j]
+// An auxiliary pair list (dead-latent aux-k loss) uses raw coefficients h/||W_dec|| (no ReLU)
+// and its own residual-gradient rows; it is merged into the same CSC pass.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace sb {
+namespace sparse {
+
+constexpr int DEC_THREADS = 128;
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float* f) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 t = __bfloat1622float2(h[j]);
+    f[2 * j] = t.x;
+    f[2 * j + 1] = t.y;
+  }
+}
+__device__ __forceinline__ uint4 f32_to_bf16x8(const float* f) {
+  uint4 u;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+    w[j] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return u;
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int w = 0; w < int(blockDim.x >> 5); ++w) t += red[w];
+  return t;
+}
+
+// ---------------------------------------------------------------------------------------
+// decode + MSE.  One CTA per row (grid-stride).  VPT = 8-element vectors per thread.
+//   coef mode: relu=1 -> a = relu(val) * inv_scale[idx]; relu=0 -> a = val * inv_scale[idx]
+//   err = x_hat - target;  dxhat = err * grad_coef;  loss_row[b] = sum err^2
+//   bsum (optional, fp32 [D]) += sum_b dxhat[b]   (for the b_dec gradient)
+// ---------------------------------------------------------------------------------------
+template <int VPT>
+__global__ void __launch_bounds__(DEC_THREADS)
+    decode_mse_kernel(const float* __restrict__ vals, const int* __restrict__ idx, int k,
+                      int64_t ldk, int relu, const float* __restrict__ inv_scale,
+                      const __nv_bfloat16* __restrict__ W, int64_t ldw,
+                      const float* __restrict__ bias, const __nv_bfloat16* __restrict__ target,
+                      int64_t ldt, __nv_bfloat16* __restrict__ out, int64_t ldo,
+                      __nv_bfloat16* __restrict__ resid, int64_t ldr,
+                      __nv_bfloat16* __restrict__ dxhat, int64_t ldd, const float* grad_coef_dev,
+                      float grad_coef, float* __restrict__ loss_row, float* __restrict__ bsum,
+                      int M, int D) {
+  extern __shared__ float dsm[];
+  float* s_a = dsm;                                  // k
+  int* s_i = reinterpret_cast<int*>(dsm + k);        // k
+  float* red = dsm + 2 * k;                          // 32
+  const int nvec = D >> 3;
+  const int t = threadIdx.x;
+  float bacc[VPT][8];
+#pragma unroll
+  for (int v = 0; v < VPT; ++v)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) bacc[v][e] = 0.f;
+  const float gcoef = grad_coef_dev ? grad_coef * __ldg(grad_coef_dev) : grad_coef;
+
+  for (int row = blockIdx.x; row < M; row += gridDim.x) {
+    __syncthreads();
+    for (int i = t; i < k; i += DEC_THREADS) {
+      const int j = idx[int64_t(row) * ldk + i];
+      float a = 0.f;
+      if (j >= 0) {
+        const float v = vals[int64_t(row) * ldk + i];
+        a = (relu ? fmaxf(v, 0.f) : v) * (inv_scale ? __ldg(inv_scale + j) : 1.f);
+      }
+      s_a[i] = a;
+      s_i[i] = (a != 0.f) ? j : -1;
+    }
+    __syncthreads();
+    float acc[VPT][8];
+#pragma unroll
+    for (int v = 0; v < VPT; ++v)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[v][e] = 0.f;
+    int i = 0;
+    for (; i + 2 <= k; i += 2) {
+      const int j0 = s_i[i], j1 = s_i[i + 1];
+      const float a0 = s_a[i], a1 = s_a[i + 1];
+      uint4 w0[VPT], w1[VPT];
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        const int vi = t + v * DEC_THREADS;
+        w0[v] = (j0 >= 0 && vi < nvec)
+                    ? __ldg(reinterpret_cast<const uint4*>(W + int64_t(j0) * ldw) + vi)
+                    : make_uint4(0, 0, 0, 0);
+        w1[v] = (j1 >= 0 && vi < nvec)
+                    ? __ldg(reinterpret_cast<const uint4*>(W + int64_t(j1) * ldw) + vi)
+                    : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        float f0[8], f1[8];
+        bf16x8_to_f32(w0[v], f0);
+        bf16x8_to_f32(w1[v], f1);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[v][e] += a0 * f0[e] + a1 * f1[e];
+      }
+    }
+    for (; i < k; ++i) {
+      const int j0 = s_i[i];
+      if (j0 < 0) continue;
+      const float a0 = s_a[i];
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        const int vi = t + v * DEC_THREADS;
+        if (vi < nvec) {
+          float f0[8];
+          bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(W + int64_t(j0) * ldw) + vi), f0);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[v][e] += a0 * f0[e];
+        }
+      }
+    }
+    float lsum = 0.f;
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int vi = t + v * DEC_THREADS;
+      if (vi >= nvec) continue;
+      float xh[8], tg[8];
+      if (bias) {
+        const float4* b4 = reinterpret_cast<const float4*>(bias) + 2 * vi;
+        const float4 b0 = __ldg(b4), b1 = __ldg(b4 + 1);
+        xh[0] = acc[v][0] + b0.x; xh[1] = acc[v][1] + b0.y; xh[2] = acc[v][2] + b0.z; xh[3] = acc[v][3] + b0.w;
+        xh[4] = acc[v][4] + b1.x; xh[5] = acc[v][5] + b1.y; xh[6] = acc[v][6] + b1.z; xh[7] = acc[v][7] + b1.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xh[e] = acc[v][e];
+      }
+      if (out) reinterpret_cast<uint4*>(out + int64_t(row) * ldo)[vi] = f32_to_bf16x8(xh);
+      bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(target + int64_t(row) * ldt) + vi), tg);
+      float err[8], g[8], rs[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        err[e] = xh[e] - tg[e];
+        lsum += err[e] * err[e];
+        g[e] = err[e] * gcoef;
+        rs[e] = -err[e];
+      }
+      if (resid) reinterpret_cast<uint4*>(resid + int64_t(row) * ldr)[vi] = f32_to_bf16x8(rs);
+      if (dxhat) {
+        const uint4 gq = f32_to_bf16x8(g);
+        reinterpret_cast<uint4*>(dxhat + int64_t(row) * ldd)[vi] = gq;
+        if (bsum) {
+          float gr[8];
+          bf16x8_to_f32(gq, gr);  // sum exactly what the latent gradients consume
+#pragma unroll
+          for (int e = 0; e < 8; ++e) bacc[v][e] += gr[e];
+        }
+      }
+    }
+    const float tot = block_sum(lsum, red);
+    if (t == 0 && loss_row) loss_row[row] = tot;
+  }
+  if (bsum) {
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int vi = t + v * DEC_THREADS;
+      if (vi < nvec)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) atomicAdd(bsum + 8 * vi + e, bacc[v][e]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// CSC build.  Pair p (= b * k + i for the main list, M*k + b*k_aux + i for the aux list) is
+// kept when its coefficient is non-zero.
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ bool pair_live(const float* vals, const int* idx, int64_t p, int relu,
+                                          int& j) {
+  j = idx[p];
+  if (j < 0) return false;
+  const float v = vals[p];
+  return relu ? (v > 0.f) : (v != 0.f);
+}
+
+__global__ void csc_count_kernel(const float* __restrict__ vals, const int* __restrict__ idx,
+                                 int64_t n_main, const float* __restrict__ aux_vals,
+                                 const int* __restrict__ aux_idx, int64_t n_aux,
+                                 int* __restrict__ counts, int* __restrict__ fire_counts) {
+  const int64_t total = n_main + n_aux;
+  for (int64_t p = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; p < total;
+       p += int64_t(gridDim.x) * blockDim.x) {
+    int j;
+    const bool main = p < n_main;
+    const bool live = main ? pair_live(vals, idx, p, 1, j) : pair_live(aux_vals, aux_idx, p - n_main, 0, j);
+    if (live) {
+      atomicAdd(counts + j, 1);
+      if (main && fire_counts) atomicAdd(fire_counts + j, 1);
+    }
+  }
+}
+
+__global__ void csc_fill_kernel(const float* __restrict__ vals, const int* __restrict__ idx,
+                                int64_t n_main, const float* __restrict__ aux_vals,
+                                const int* __restrict__ aux_idx, int64_t n_aux,
+                                const int64_t* __restrict__ colptr, int* __restrict__ cursor,
+                                int64_t* __restrict__ pairs) {
+  const int64_t total = n_main + n_aux;
+  for (int64_t p = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; p < total;
+       p += int64_t(gridDim.x) * blockDim.x) {
+    int j;
+    const bool main = p < n_main;
+    const bool live = main ? pair_live(vals, idx, p, 1, j) : pair_live(aux_vals, aux_idx, p - n_main, 0, j);
+    if (live) {
+      const int pos = atomicAdd(cursor + j, 1);
+      pairs[colptr[j] + pos] = p;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// latent gradients.  One CTA (128 threads) per latent, grid-stride over latents.
+// ---------------------------------------------------------------------------------------
+constexpr int LG_THREADS = 128;
+constexpr int LG_MAX_CHUNK = 256;  // entries whose dot products are staged at once
+
+struct LatentGradArgs {
+  const int64_t* colptr;
+  const int64_t* pairs;
+  int64_t n_main;
+  int k, k_aux;
+  const float* vals;       // [M, k]
+  const float* aux_vals;   // [M, k_aux]
+  const float* inv_scale;  // [N] or nullptr
+  const __nv_bfloat16* dxhat;   // [M, D]  main-loss gradient rows
+  const __nv_bfloat16* daux;    // [M, D]  aux-loss gradient rows (or nullptr)
+  const __nv_bfloat16* x;       // [M, D]  raw input
+  const float* b_dec;           // [D] (subtracted from x for the encoder input) or nullptr
+  const __nv_bfloat16* W_dec;   // [N, D]
+  const __nv_bfloat16* W_enc;   // [N, D] (latent-major)
+  __nv_bfloat16* gW_dec;        // [N, D]
+  __nv_bfloat16* gW_enc;        // [N, D]
+  float* gb_enc;                // [N]
+  float* bterm;                 // [D]  += sum_j gb_enc[j] W_enc[j]
+  float* sumsq;                 // [1]  += squared norm of the three gradients
+  const int* fire_counts;       // [N] live main pairs per latent (firing statistics)
+  float* act_freq;              // [N] += fire count (or nullptr)
+  float* since_fired;           // [N] = 0 if fired else +1 (or nullptr)
+  int64_t ldx;
+  int N, D;
+};
+
+template <int VPT>
+__global__ void __launch_bounds__(LG_THREADS) latent_grad_kernel(LatentGradArgs a) {
+  __shared__ float s_dz[LG_MAX_CHUNK];
+  __shared__ float s_coef[LG_MAX_CHUNK];
+  __shared__ int64_t s_row[LG_MAX_CHUNK];
+  __shared__ int s_aux[LG_MAX_CHUNK];
+  __shared__ float red[32];
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int nvec = a.D >> 3;
+  float bt[VPT][8];
+  float bdec[VPT][8];
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int vi = t + v * LG_THREADS;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      bt[v][e] = 0.f;
+      bdec[v][e] = (a.b_dec && vi < nvec) ? a.b_dec[8 * vi + e] : 0.f;
+    }
+  }
+  float sq = 0.f;
+
+  for (int j = blockIdx.x; j < a.N; j += gridDim.x) {
+    const int64_t beg = a.colptr[j], end = a.colptr[j + 1];
+    if (t == 0) {
+      if (a.fire_counts) {
+        const int fc = a.fire_counts[j];
+        if (a.act_freq) a.act_freq[j] += float(fc);
+        if (a.since_fired) a.since_fired[j] = fc > 0 ? 0.f : a.since_fired[j] + 1.f;
+      }
+    }
+    if (beg == end) {
+      if (t == 0) a.gb_enc[j] = 0.f;
+      continue;
+    }
+    const float isc = a.inv_scale ? a.inv_scale[j] : 1.f;
+    // W_dec row slice in registers (fp32)
+    float wd[VPT][8];
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int vi = t + v * LG_THREADS;
+      if (vi < nvec)
+        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(a.W_dec + int64_t(j) * a.D) + vi), wd[v]);
+      else
+#pragma unroll
+        for (int e = 0; e < 8; ++e) wd[v][e] = 0.f;
+    }
+    float gd[VPT][8], ge[VPT][8];
+#pragma unroll
+    for (int v = 0; v < VPT; ++v)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) gd[v][e] = ge[v][e] = 0.f;
+    float gbe = 0.f;
+
+    for (int64_t c0 = beg; c0 < end; c0 += LG_MAX_CHUNK) {
+      const int cn = int((end - c0) < int64_t(LG_MAX_CHUNK) ? (end - c0) : int64_t(LG_MAX_CHUNK));
+      __syncthreads();
+      for (int e = t; e < cn; e += LG_THREADS) {
+        const int64_t p = a.pairs[c0 + e];
+        if (p < a.n_main) {
+          s_row[e] = p / a.k;
+          s_coef[e] = fmaxf(a.vals[p], 0.f) * isc;
+          s_aux[e] = 0;
+        } else {
+          const int64_t q = p - a.n_main;
+          s_row[e] = q / a.k_aux;
+          s_coef[e] = a.aux_vals[q] * isc;
+          s_aux[e] = 1;
+        }
+      }
+      __syncthreads();
+      // phase 1: dot products <gradrow, W_dec[j]>, one warp per entry
+      for (int e = warp; e < cn; e += LG_THREADS / 32) {
+        const __nv_bfloat16* grow = (s_aux[e] ? a.daux : a.dxhat) + s_row[e] * int64_t(a.D);
+        float d = 0.f;
+        for (int vi = lane; vi < nvec; vi += 32) {
+          float g[8], w[8];
+          bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(grow) + vi), g);
+          bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(a.W_dec + int64_t(j) * a.D) + vi), w);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) d += g[q] * w[q];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        if (lane == 0) s_dz[e] = d;  // main pairs are live only where a > 0, so no mask needed
+      }
+      __syncthreads();
+      // phase 2: accumulate gW_dec, gW_enc
+      for (int e = 0; e < cn; ++e) {
+        const float coef = s_coef[e];
+        const float dz = s_dz[e];
+        gbe += dz;
+        const __nv_bfloat16* grow = (s_aux[e] ? a.daux : a.dxhat) + s_row[e] * int64_t(a.D);
+        const __nv_bfloat16* xrow = a.x + s_row[e] * a.ldx;
+#pragma unroll
+        for (int v = 0; v < VPT; ++v) {
+          const int vi = t + v * LG_THREADS;
+          if (vi < nvec) {
+            float g[8], xv[8];
+            bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(grow) + vi), g);
+            bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(xrow) + vi), xv);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              gd[v][q] += coef * g[q];
+              ge[v][q] += dz * (xv[q] - bdec[v][q]);
+            }
+          }
+        }
+      }
+    }
+    // write gradient rows (bf16) and accumulate their squared norm
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int vi = t + v * LG_THREADS;
+      if (vi < nvec) {
+        const uint4 qd = f32_to_bf16x8(gd[v]);
+        const uint4 qe = f32_to_bf16x8(ge[v]);
+        reinterpret_cast<uint4*>(a.gW_dec + int64_t(j) * a.D)[vi] = qd;
+        reinterpret_cast<uint4*>(a.gW_enc + int64_t(j) * a.D)[vi] = qe;
+        float rd[8], re[8];
+        bf16x8_to_f32(qd, rd);
+        bf16x8_to_f32(qe, re);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) sq += rd[q] * rd[q] + re[q] * re[q];
+        if (a.bterm) {
+          float we[8];
+          bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(a.W_enc + int64_t(j) * a.D) + vi), we);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) bt[v][q] += gbe * we[q];
+        }
+      }
+    }
+    if (t == 0) {
+      a.gb_enc[j] = gbe;
+      sq += gbe * gbe;
+    }
+  }
+  if (a.bterm) {
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int vi = t + v * LG_THREADS;
+      if (vi < nvec)
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (bt[v][q] != 0.f) atomicAdd(a.bterm + 8 * vi + q, bt[v][q]);
+    }
+  }
+  const float tot = block_sum(sq, red);
+  if (t == 0 && a.sumsq) atomicAdd(a.sumsq, tot);
+}
+
+}  // namespace sparse
+
+static inline int pick_vpt(int64_t D, int threads) {
+  const int64_t need = (D / 8 + threads - 1) / threads;
+  if (need <= 1) return 1;
+  if (need <= 2) return 2;
+  if (need <= 4) return 4;
+  TORCH_CHECK(need <= 8, "d_in too large for the sparse kernels (max 8192)");
+  return 8;
+}
+
+static int sm_count() {
+  int dev, n;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  C10_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+  return n;
+}
+
+void decode_mse(const torch::Tensor& vals, const torch::Tensor& idx, bool relu,
+                const c10::optional<torch::Tensor>& inv_scale, const torch::Tensor& W,
+                const c10::optional<torch::Tensor>& bias, const torch::Tensor& target,
+                const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& resid,
+                const c10::optional<torch::Tensor>& dxhat, const c10::optional<torch::Tensor>& grad_coef_dev,
+                double grad_coef, const c10::optional<torch::Tensor>& loss_row,
+                const c10::optional<torch::Tensor>& bsum) {
+  TORCH_CHECK(vals.scalar_type() == at::kFloat && idx.scalar_type() == at::kInt && vals.dim() == 2 &&
+                  vals.sizes() == idx.sizes() && vals.is_contiguous() && idx.is_contiguous(),
+              "decode_mse: vals fp32 / idx int32 [M, k]");
+  TORCH_CHECK(W.scalar_type() == at::kBFloat16 && W.dim() == 2 && W.stride(1) == 1, "decode_mse: W");
+  const int64_t M = vals.size(0), k = vals.size(1), D = W.size(1);
+  TORCH_CHECK(D % 8 == 0 && W.stride(0) % 8 == 0, "decode_mse: d_in must be a multiple of 8");
+  TORCH_CHECK(target.scalar_type() == at::kBFloat16 && target.size(0) == M && target.size(1) == D &&
+                  target.stride(1) == 1 && target.stride(0) % 8 == 0,
+              "decode_mse: target bf16 [M, D]");
+  auto chk_out = [&](const c10::optional<torch::Tensor>& o, const char* name) -> __nv_bfloat16* {
+    if (!o) return nullptr;
+    TORCH_CHECK(o->scalar_type() == at::kBFloat16 && o->size(0) == M && o->size(1) == D &&
+                    o->stride(1) == 1 && o->stride(0) % 8 == 0,
+                "decode_mse: bad ", name);
+    return reinterpret_cast<__nv_bfloat16*>(o->data_ptr());
+  };
+  __nv_bfloat16* po = chk_out(out, "out");
+  __nv_bfloat16* pr = chk_out(resid, "resid");
+  __nv_bfloat16* pd = chk_out(dxhat, "dxhat");
+  const float* pinv = nullptr;
+  if (inv_scale) {
+    TORCH_CHECK(inv_scale->scalar_type() == at::kFloat && inv_scale->numel() == W.size(0), "decode_mse: inv_scale");
+    pinv = inv_scale->data_ptr<float>();
+  }
+  const float* pb = nullptr;
+  if (bias) {
+    TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->numel() == D, "decode_mse: bias");
+    pb = bias->data_ptr<float>();
+  }
+  const float* pgc = nullptr;
+  if (grad_coef_dev) pgc = grad_coef_dev->data_ptr<float>();
+  float* pl = loss_row ? loss_row->data_ptr<float>() : nullptr;
+  float* pbs = bsum ? bsum->data_ptr<float>() : nullptr;
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(vals.device());
+  const int vpt = pick_vpt(D, sparse::DEC_THREADS);
+  const int64_t grid = std::min<int64_t>(M, int64_t(sm_count()) * 8);
+  const size_t smem = size_t(2 * k + 32) * 4;
+  auto stream = at::cuda::getCurrentCUDAStream();
+#define SB_DEC(V)                                                                                  \
+  sparse::decode_mse_kernel<V><<<dim3(grid), dim3(sparse::DEC_THREADS), smem, stream>>>(           \
+      vals.data_ptr<float>(), idx.data_ptr<int>(), int(k), vals.stride(0), relu ? 1 : 0, pinv,      \
+      reinterpret_cast<const __nv_bfloat16*>(W.data_ptr()), W.stride(0), pb,                      \
+      reinterpret_cast<const __nv_bfloat16*>(target.data_ptr()), target.stride(0), po,             \
+      out ? out->stride(0) : 0, pr, resid ? resid->stride(0) : 0, pd, dxhat ? dxhat->stride(0) : 0, \
+      pgc, float(grad_coef), pl, pbs, int(M), int(D))
+  switch (vpt) {
+    case 1: SB_DEC(1); break;
+    case 2: SB_DEC(2); break;
+    case 4: SB_DEC(4); break;
+    default: SB_DEC(8); break;
+  }
+#undef SB_DEC
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Builds the latent-major pair lists.  Returns nothing; fills counts [N] (int32), colptr
+// [N+1] (int64), pairs [nnz_capacity] (int64) and fire_counts [N] (int32, main pairs only).
+void csc_count(const torch::Tensor& vals, const torch::Tensor& idx,
+               const c10::optional<torch::Tensor>& aux_vals, const c10::optional<torch::Tensor>& aux_idx,
+               const torch::Tensor& counts, const c10::optional<torch::Tensor>& fire_counts) {
+  const at::cuda::CUDAGuard guard(vals.device());
+  const int64_t n_main = vals.numel();
+  const int64_t n_aux = aux_vals ? aux_vals->numel() : 0;
+  const int64_t total = n_main + n_aux;
+  if (total == 0) return;
+  const int64_t grid = std::min<int64_t>((total + 255) / 256, int64_t(sm_count()) * 16);
+  sparse::csc_count_kernel<<<dim3(grid), dim3(256), 0, at::cuda::getCurrentCUDAStream()>>>(
+      vals.data_ptr<float>(), idx.data_ptr<int>(), n_main,
+      aux_vals ? aux_vals->data_ptr<float>() : nullptr, aux_idx ? aux_idx->data_ptr<int>() : nullptr,
+      n_aux, counts.data_ptr<int>(), fire_counts ? fire_counts->data_ptr<int>() : nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void csc_fill(const torch::Tensor& vals, const torch::Tensor& idx,
+              const c10::optional<torch::Tensor>& aux_vals, const c10::optional<torch::Tensor>& aux_idx,
+              const torch::Tensor& colptr, const torch::Tensor& cursor, const torch::Tensor& pairs) {
+  const at::cuda::CUDAGuard guard(vals.device());
+  const int64_t n_main = vals.numel();
+  const int64_t n_aux = aux_vals ? aux_vals->numel() : 0;
+  const int64_t total = n_main + n_aux;
+  if (total == 0) return;
+  TORCH_CHECK(colptr.scalar_type() == at::kLong && pairs.scalar_type() == at::kLong &&
+                  cursor.scalar_type() == at::kInt,
+              "csc_fill: dtypes");
+  const int64_t grid = std::min<int64_t>((total + 255) / 256, int64_t(sm_count()) * 16);
+  sparse::csc_fill_kernel<<<dim3(grid), dim3(256), 0, at::cuda::getCurrentCUDAStream()>>>(
+      vals.data_ptr<float>(), idx.data_ptr<int>(), n_main,
+      aux_vals ? aux_vals->data_ptr<float>() : nullptr, aux_idx ? aux_idx->data_ptr<int>() : nullptr,
+      n_aux, colptr.data_ptr<int64_t>(), cursor.data_ptr<int>(), pairs.data_ptr<int64_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const torch::Tensor& vals,
+                 const c10::optional<torch::Tensor>& aux_vals, const c10::optional<torch::Tensor>& inv_scale,
+                 const torch::Tensor& dxhat, const c10::optional<torch::Tensor>& daux,
+                 const torch::Tensor& x, const c10::optional<torch::Tensor>& b_dec,
+                 const torch::Tensor& W_dec, const torch::Tensor& W_enc, const torch::Tensor& gW_dec,
+                 const torch::Tensor& gW_enc, const torch::Tensor& gb_enc,
+                 const c10::optional<torch::Tensor>& bterm, const c10::optional<torch::Tensor>& sumsq,
+                 const c10::optional<torch::Tensor>& fire_counts,
+                 const c10::optional<torch::Tensor>& act_freq,
+                 const c10::optional<torch::Tensor>& since_fired) {
+  const at::cuda::CUDAGuard guard(vals.device());
+  const int64_t N = W_dec.size(0), D = W_dec.size(1);
+  TORCH_CHECK(W_dec.is_contiguous() && W_enc.is_contiguous() && gW_dec.is_contiguous() &&
+                  gW_enc.is_contiguous() && W_enc.size(0) == N && W_enc.size(1) == D,
+              "latent_grad: weights must be contiguous [N, D]");
+  TORCH_CHECK(dxhat.is_contiguous() && dxhat.size(1) == D && x.stride(1) == 1 && x.stride(0) % 8 == 0,
+              "latent_grad: dxhat / x layout");
+  TORCH_CHECK(D % 8 == 0, "latent_grad: d_in must be a multiple of 8");
+  sparse::LatentGradArgs a{};
+  a.colptr = colptr.data_ptr<int64_t>();
+  a.pairs = pairs.data_ptr<int64_t>();
+  a.n_main = vals.numel();
+  a.k = int(vals.size(1));
+  a.k_aux = aux_vals ? int(aux_vals->size(1)) : 1;
+  a.vals = vals.data_ptr<float>();
+  a.aux_vals = aux_vals ? aux_vals->data_ptr<float>() : nullptr;
+  a.inv_scale = inv_scale ? inv_scale->data_ptr<float>() : nullptr;
+  a.dxhat = reinterpret_cast<const __nv_bfloat16*>(dxhat.data_ptr());
+  a.daux = daux ? reinterpret_cast<const __nv_bfloat16*>(daux->data_ptr()) : nullptr;
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  a.ldx = x.stride(0);
+  a.b_dec = b_dec ? b_dec->data_ptr<float>() : nullptr;
+  a.W_dec = reinterpret_cast<const __nv_bfloat16*>(W_dec.data_ptr());
+  a.W_enc = reinterpret_cast<const __nv_bfloat16*>(W_enc.data_ptr());
+  a.gW_dec = reinterpret_cast<__nv_bfloat16*>(gW_dec.data_ptr());
+  a.gW_enc = reinterpret_cast<__nv_bfloat16*>(gW_enc.data_ptr());
+  a.gb_enc = gb_enc.data_ptr<float>();
+  a.bterm = bterm ? bterm->data_ptr<float>() : nullptr;
+  a.sumsq = sumsq ? sumsq->data_ptr<float>() : nullptr;
+  a.fire_counts = fire_counts ? fire_counts->data_ptr<int>() : nullptr;
+  a.act_freq = act_freq ? act_freq->data_ptr<float>() : nullptr;
+  a.since_fired = since_fired ? since_fired->data_ptr<float>() : nullptr;
+  a.N = int(N);
+  a.D = int(D);
+  if (N == 0) return;
+  const int vpt = pick_vpt(D, sparse::LG_THREADS);
+  const int64_t grid = std::min<int64_t>(N, int64_t(sm_count()) * 8);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  switch (vpt) {
+    case 1: sparse::latent_grad_kernel<1><<<dim3(grid), dim3(sparse::LG_THREADS), 0, stream>>>(a); break;
+    case 2: sparse::latent_grad_kernel<2><<<dim3(grid), dim3(sparse::LG_THREADS), 0, stream>>>(a); break;
+    case 4: sparse::latent_grad_kernel<4><<<dim3(grid), dim3(sparse::LG_THREADS), 0, stream>>>(a); break;
+    default: sparse::latent_grad_kernel<8><<<dim3(grid), dim3(sparse::LG_THREADS), 0, stream>>>(a); break;
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace sb

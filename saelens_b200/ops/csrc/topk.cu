@@ -1,0 +1,312 @@
+// Row-wise exact top-k over bf16 pre-activations, pruned by per-chunk maxima.
+//
+// Replaces `torch.topk(hidden_pre, k, dim=-1, sorted=False)` + ReLU + scatter
+// (sae_lens/saes/topk_sae.py:99-145) and the dead-latent top-k of the aux loss
+// (sae_lens/saes/topk_sae.py:787-813).  No dense [B, d_sae] activation tensor is produced: the
+// output is k (value, index) pairs per row.
+//
+// Algorithm (one CTA per row):
+//  1. The encoder GEMM epilogue stored the max of every 32-column chunk.  The k-th largest
+//     chunk max `klb` is a lower bound on the row's k-th largest value (k distinct chunks
+//     each hold a value >= klb), so only chunks whose max >= klb can contribute.
+//  2. Those chunks (about k of them) are read from H and every value >= klb is appended to a
+//     shared-memory candidate list.
+//  3. Two 8-bit radix-select passes over the 16-bit order-preserving keys give the exact k-th
+//     largest key; values above it are emitted, and ties at it are broken by the smaller
+//     column index so the selection is deterministic.
+//  If the candidate list overflows (pathological ties), the row is selected directly from H
+//  with the same radix select and an index-ordered tie scan.
+// An optional column bitmask (one bit per column, 1 = eligible) restricts the selection to
+// dead latents for the aux-k loss; the effective k can come from device memory so that the
+// number of dead latents never has to be read on the host.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace sb {
+namespace topk {
+
+constexpr int THREADS = 256;
+constexpr int CAP = 8192;
+constexpr int MAX_NC = 32768;  // chunk keys cached in shared memory (N <= 1,048,576)
+
+struct Sel {
+  uint32_t key;   // k-th largest key
+  int greater;    // number of keys strictly greater
+};
+
+// Warp 0: with hist[] over 256 bins, find the highest bin b with count(bins >= b) >= k.
+// Writes sh[0] = b, sh[1] = count(bins > b).
+__device__ __forceinline__ void scan_hist_desc(const uint32_t* hist, int k, uint32_t* sh) {
+  const int lane = threadIdx.x & 31;
+  uint32_t local[8];
+  uint32_t s = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    local[j] = hist[255 - 8 * lane - j];
+    s += local[j];
+  }
+  uint32_t incl = s;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += y;
+  }
+  const uint32_t excl = incl - s;
+  const unsigned m = __ballot_sync(0xffffffffu, excl < uint32_t(k) && uint32_t(k) <= incl);
+  const int src = m ? __ffs(m) - 1 : -1;
+  if (lane == src) {
+    uint32_t cum = excl;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (cum + local[j] >= uint32_t(k)) {
+        sh[0] = 255 - 8 * lane - j;
+        sh[1] = cum;
+        break;
+      }
+      cum += local[j];
+    }
+  }
+  if (src < 0 && lane == 0) {  // k larger than the population: select everything
+    sh[0] = 0;
+    sh[1] = 0;
+  }
+}
+
+// Block-wide: k-th largest of n 16-bit keys (keys with bit 16 set are "absent").
+template <typename LoadKey>
+__device__ Sel block_select16(int n, int k, LoadKey load, uint32_t* hist, uint32_t* sh) {
+  for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const uint32_t key = load(i);
+    if (key < 0x10000u) atomicAdd(&hist[key >> 8], 1u);
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) scan_hist_desc(hist, k, sh);
+  __syncthreads();
+  const uint32_t b1 = sh[0];
+  const int above1 = int(sh[1]);
+  __syncthreads();
+  for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const uint32_t key = load(i);
+    if (key < 0x10000u && (key >> 8) == b1) atomicAdd(&hist[key & 0xffu], 1u);
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) scan_hist_desc(hist, k - above1, sh);
+  __syncthreads();
+  Sel r;
+  r.key = (b1 << 8) | sh[0];
+  r.greater = above1 + int(sh[1]);
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ bool col_ok(const uint32_t* mask, int col) {
+  return mask == nullptr || ((__ldg(mask + (col >> 5)) >> (col & 31)) & 1u);
+}
+
+__global__ void __launch_bounds__(THREADS)
+    row_topk_kernel(const __nv_bfloat16* __restrict__ H, int64_t ldh,
+                    const __nv_bfloat16* __restrict__ cmax, int64_t ldc, int N, int k_max,
+                    const int* __restrict__ k_dev, const uint32_t* __restrict__ mask,
+                    float* __restrict__ out_val, int* __restrict__ out_idx, int64_t ldo,
+                    int* status) {
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t sh[4];
+  __shared__ int n_cand, n_out;
+  extern __shared__ uint8_t dyn[];
+  const int NC = N >> 5;
+  uint16_t* ckeys = reinterpret_cast<uint16_t*>(dyn);
+  uint32_t* cand_key = reinterpret_cast<uint32_t*>(dyn + ((NC * 2 + 15) & ~15));
+  int* cand_idx = reinterpret_cast<int*>(cand_key + CAP);
+
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint16_t* hrow = reinterpret_cast<const uint16_t*>(H + int64_t(row) * ldh);
+  const uint16_t* crow = reinterpret_cast<const uint16_t*>(cmax + int64_t(row) * ldc);
+  float* vrow = out_val + int64_t(row) * ldo;
+  int* irow = out_idx + int64_t(row) * ldo;
+
+  int k = k_max;
+  if (k_dev) k = min(k, *k_dev);
+  // padding for rows with fewer eligible columns than k_max
+  for (int i = tid; i < k_max; i += THREADS) {
+    vrow[i] = 0.f;
+    irow[i] = -1;
+  }
+  if (k <= 0) return;
+
+  // chunk keys (an all-masked chunk gets key 0, the smallest possible)
+  for (int c = tid; c < NC; c += THREADS) {
+    uint32_t key = bf16_to_key(crow[c]);
+    if (mask && __ldg(mask + c) == 0u) key = 0u;
+    ckeys[c] = uint16_t(key);
+  }
+  if (tid == 0) {
+    n_cand = 0;
+    n_out = 0;
+  }
+  __syncthreads();
+
+  uint32_t klb = 0;
+  if (NC > k) {
+    klb = block_select16(NC, k, [&](int i) { return uint32_t(ckeys[i]); }, hist, sh).key;
+  }
+
+  // collect candidates: warps sweep 32 chunks at a time
+  for (int base = warp * 32; base < NC; base += THREADS) {
+    const int c = base + lane;
+    const bool is_cand = c < NC && uint32_t(ckeys[c]) >= klb;
+    unsigned m = __ballot_sync(0xffffffffu, is_cand);
+    while (m) {
+      const int bit = __ffs(m) - 1;
+      m &= m - 1;
+      const int col = (base + bit) * 32 + lane;
+      const uint32_t key = bf16_to_key(hrow[col]);
+      const bool keep = key >= klb && col_ok(mask, col);
+      const unsigned km = __ballot_sync(0xffffffffu, keep);
+      int basepos = 0;
+      if (lane == 0 && km) basepos = atomicAdd(&n_cand, __popc(km));
+      basepos = __shfl_sync(0xffffffffu, basepos, 0);
+      const int pos = basepos + __popc(km & ((1u << lane) - 1u));
+      if (keep && pos < CAP) {
+        cand_key[pos] = key;
+        cand_idx[pos] = col;
+      }
+    }
+  }
+  __syncthreads();
+  const int C = n_cand;
+
+  if (C <= CAP) {
+    const int kk = min(k, C);
+    const Sel r = block_select16(C, kk, [&](int i) { return cand_key[i]; }, hist, sh);
+    const int need_ties = kk - r.greater;
+    for (int i = tid; i < C; i += THREADS) {
+      const uint32_t key = cand_key[i];
+      bool take = key > r.key;
+      if (!take && key == r.key) {
+        const int my = cand_idx[i];
+        int rank = 0;
+        for (int j = 0; j < C; ++j) rank += (cand_key[j] == r.key && cand_idx[j] < my) ? 1 : 0;
+        take = rank < need_ties;
+      }
+      if (take) {
+        const int p = atomicAdd(&n_out, 1);
+        if (p < k_max) {
+          vrow[p] = key16_to_float(key);
+          irow[p] = cand_idx[i];
+        }
+      }
+    }
+    return;
+  }
+
+  // ---- overflow fallback: exact select straight from H, ties in index order ----
+  if (tid == 0 && status) atomicCAS(status, 0, 0);  // (no error: the fallback is exact)
+  auto load_full = [&](int i) -> uint32_t {
+    return col_ok(mask, i) ? bf16_to_key(hrow[i]) : 0x10000u;
+  };
+  int eligible = N;
+  if (mask) {
+    __shared__ int n_el;
+    if (tid == 0) n_el = 0;
+    __syncthreads();
+    int cnt = 0;
+    for (int c = tid; c < NC; c += THREADS) cnt += __popc(__ldg(mask + c));
+    atomicAdd(&n_el, cnt);
+    __syncthreads();
+    eligible = n_el;
+  }
+  const int kk = min(k, eligible);
+  const Sel r = block_select16(N, kk, load_full, hist, sh);
+  const int need_ties = kk - r.greater;
+  __shared__ int warp_tot[THREADS / 32];
+  __shared__ int running;
+  if (tid == 0) running = 0;
+  __syncthreads();
+  for (int base = 0; base < N; base += THREADS) {
+    const int col = base + tid;
+    const uint32_t key = col < N ? load_full(col) : 0x10000u;
+    const bool gt = key < 0x10000u && key > r.key;
+    const bool tie = key < 0x10000u && key == r.key;
+    const unsigned tm = __ballot_sync(0xffffffffu, tie);
+    if (lane == 0) warp_tot[warp] = __popc(tm);
+    __syncthreads();
+    int before = running;
+    for (int w = 0; w < warp; ++w) before += warp_tot[w];
+    before += __popc(tm & ((1u << lane) - 1u));
+    const bool take = gt || (tie && before < need_ties);
+    if (take) {
+      const int p = atomicAdd(&n_out, 1);
+      if (p < k_max) {
+        vrow[p] = key16_to_float(key);
+        irow[p] = col;
+      }
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int tot = 0;
+      for (int w = 0; w < THREADS / 32; ++w) tot += warp_tot[w];
+      running += tot;
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace topk
+
+// H [M, N] bf16, cmax [M, N/32] bf16 -> (val fp32 [M, k_max], idx int32 [M, k_max]).
+// `k_dev` (int32 scalar on device) optionally lowers k below k_max; `mask` (int32 bit words,
+// [N/32]) optionally restricts the eligible columns.  Unused output slots hold idx -1, val 0.
+void row_topk(const torch::Tensor& H, const torch::Tensor& cmax, int64_t k_max,
+              const c10::optional<torch::Tensor>& k_dev, const c10::optional<torch::Tensor>& mask,
+              const torch::Tensor& out_val, const torch::Tensor& out_idx, const torch::Tensor& status) {
+  TORCH_CHECK(H.is_cuda() && H.scalar_type() == at::kBFloat16 && H.dim() == 2 && H.stride(1) == 1,
+              "row_topk: H must be a CUDA bf16 matrix with contiguous rows");
+  const int64_t M = H.size(0), N = H.size(1);
+  TORCH_CHECK(N % 32 == 0 && N / 32 <= topk::MAX_NC, "row_topk: N must be a multiple of 32 and <= 2^20");
+  TORCH_CHECK(cmax.scalar_type() == at::kBFloat16 && cmax.size(0) == M && cmax.size(1) == N / 32 &&
+                  cmax.stride(1) == 1,
+              "row_topk: bad cmax");
+  TORCH_CHECK(k_max >= 1 && k_max <= N, "row_topk: k out of range");
+  TORCH_CHECK(out_val.scalar_type() == at::kFloat && out_idx.scalar_type() == at::kInt &&
+                  out_val.size(0) == M && out_val.size(1) == k_max && out_idx.size(0) == M &&
+                  out_idx.size(1) == k_max && out_val.is_contiguous() && out_idx.is_contiguous(),
+              "row_topk: bad outputs");
+  const int* kd = nullptr;
+  if (k_dev) {
+    TORCH_CHECK(k_dev->scalar_type() == at::kInt && k_dev->numel() == 1, "row_topk: k_dev");
+    kd = k_dev->data_ptr<int>();
+  }
+  const uint32_t* mk = nullptr;
+  if (mask) {
+    TORCH_CHECK(mask->scalar_type() == at::kInt && mask->numel() == N / 32 && mask->is_contiguous(),
+                "row_topk: mask must be int32 [N/32]");
+    mk = reinterpret_cast<const uint32_t*>(mask->data_ptr<int>());
+  }
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(H.device());
+  const int NC = int(N / 32);
+  const size_t smem = ((NC * 2 + 15) & ~15) + size_t(topk::CAP) * 8;
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(topk::row_topk_kernel,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(((topk::MAX_NC * 2 + 15) & ~15) + topk::CAP * 8)));
+    attr = true;
+  }
+  topk::row_topk_kernel<<<dim3(M), dim3(topk::THREADS), smem, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(H.data_ptr()), H.stride(0),
+      reinterpret_cast<const __nv_bfloat16*>(cmax.data_ptr()), cmax.stride(0), int(N), int(k_max),
+      kd, mk, out_val.data_ptr<float>(), out_idx.data_ptr<int>(), out_val.stride(0),
+      status.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace sb
