@@ -1,0 +1,114 @@
+"""Directory of pretrained SAE releases (release -> HF repo, per-SAE folders and metadata).
+
+Same YAML schema as the reference's directory (sae_lens/loading/pretrained_saes_directory.py:
+release keys with `repo_id`, `model`, `conversion_func`, `saes: [{id, path, l0,
+variance_explained, neuronpedia, norm_scaling_factor}]`, `config_overrides`).  The package ships a
+small directory; point `SAELENS_B200_PRETRAINED_YAML` at a larger file (for example the
+reference's full directory) to extend it, or call `register_release`.
+"""
+
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass
+from functools import cache
+from importlib.resources import files
+from typing import Any
+
+import yaml
+
+
+@dataclass
+class PretrainedSAELookup:
+    release: str
+    repo_id: str
+    model: str
+    conversion_func: str | None
+    saes_map: dict[str, str]
+    expected_var_explained: dict[str, float]
+    expected_l0: dict[str, float]
+    neuronpedia_id: dict[str, str | None]
+    norm_scaling_factor: dict[str, float]
+    config_overrides: dict[str, Any] | None
+
+
+_EXTRA: dict[str, PretrainedSAELookup] = {}
+
+
+def _parse(data: dict[str, Any]) -> dict[str, PretrainedSAELookup]:
+    out: dict[str, PretrainedSAELookup] = {}
+    for release, value in (data or {}).items():
+        if "saes" not in value:
+            raise KeyError(f"Missing 'saes' key in {release}")
+        saes, ve, l0, npd, nsf = {}, {}, {}, {}, {}
+        for info in value["saes"]:
+            sid = info["id"]
+            saes[sid] = info["path"]
+            ve[sid] = info.get("variance_explained", 1.0)
+            l0[sid] = info.get("l0", 0.0)
+            npd[sid] = info.get("neuronpedia")
+            if "norm_scaling_factor" in info:
+                nsf[sid] = info["norm_scaling_factor"]
+        out[release] = PretrainedSAELookup(
+            release=release, repo_id=value["repo_id"], model=value["model"],
+            conversion_func=value.get("conversion_func"), saes_map=saes, expected_var_explained=ve,
+            expected_l0=l0, neuronpedia_id=npd, norm_scaling_factor=nsf,
+            config_overrides=value.get("config_overrides"),
+        )
+    return out
+
+
+@cache
+def _load_files() -> dict[str, PretrainedSAELookup]:
+    directory: dict[str, PretrainedSAELookup] = {}
+    with files("saelens_b200.loading").joinpath("pretrained_saes.yaml").open("r") as f:
+        directory.update(_parse(yaml.safe_load(f)))
+    extra = os.environ.get("SAELENS_B200_PRETRAINED_YAML")
+    if extra and os.path.exists(extra):
+        with open(extra) as f:
+            directory.update(_parse(yaml.safe_load(f)))
+    return directory
+
+
+def get_pretrained_saes_directory() -> dict[str, PretrainedSAELookup]:
+    return {**_load_files(), **_EXTRA}
+
+
+def register_release(release: str, entry: dict[str, Any]) -> None:
+    """Add a release at runtime (same schema as one YAML entry)."""
+    _EXTRA.update(_parse({release: entry}))
+
+
+def get_norm_scaling_factor(release: str, sae_id: str) -> float | None:
+    info = get_pretrained_saes_directory().get(release)
+    return None if info is None else info.norm_scaling_factor.get(sae_id)
+
+
+def get_repo_id_and_folder_name(release: str, sae_id: str) -> tuple[str, str]:
+    info = get_pretrained_saes_directory().get(release)
+    if info is None:
+        return release, sae_id
+    if sae_id not in info.saes_map:
+        raise ValueError(f"SAE ID '{sae_id}' not found in release '{release}'")
+    return info.repo_id, info.saes_map[sae_id]
+
+
+def get_config_overrides(release: str, sae_id: str) -> dict[str, Any]:
+    info = get_pretrained_saes_directory().get(release)
+    out: dict[str, Any] = {}
+    if info is not None:
+        out = {**(info.config_overrides or {})}
+        if sae_id in info.neuronpedia_id:
+            out["neuronpedia_id"] = info.neuronpedia_id[sae_id]
+    return out
+
+
+def get_conversion_loader_name(release: str) -> str:
+    info = get_pretrained_saes_directory().get(release)
+    if info is not None and info.conversion_func is not None:
+        return info.conversion_func
+    return "sae_lens"
+
+
+def get_releases_for_repo_id(repo_id: str) -> list[str]:
+    return [r for r, v in get_pretrained_saes_directory().items() if v.repo_id == repo_id]

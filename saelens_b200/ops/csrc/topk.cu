@@ -141,16 +141,16 @@ __global__ void __launch_bounds__(THREADS)
   }
   if (k <= 0) return;
 
-  // chunk keys (an all-masked chunk gets key 0, the smallest possible)
-  for (int c = tid; c < NC; c += THREADS) {
-    uint32_t key = bf16_to_key(crow[c]);
-    if (mask && __ldg(mask + c) == 0u) key = 0u;
-    ckeys[c] = uint16_t(key);
-  }
+  // Fast path (no column mask): chunk maxima bound the k-th value from below.  With a mask the
+  // unmasked chunk maxima are no bound for the eligible columns, so masked rows go straight to
+  // the exact full-row path below.
   if (tid == 0) {
     n_cand = 0;
     n_out = 0;
   }
+  __syncthreads();
+  if (mask == nullptr) {
+  for (int c = tid; c < NC; c += THREADS) ckeys[c] = uint16_t(bf16_to_key(crow[c]));
   __syncthreads();
 
   uint32_t klb = 0;
@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(THREADS)
       m &= m - 1;
       const int col = (base + bit) * 32 + lane;
       const uint32_t key = bf16_to_key(hrow[col]);
-      const bool keep = key >= klb && col_ok(mask, col);
+      const bool keep = key >= klb;
       const unsigned km = __ballot_sync(0xffffffffu, keep);
       int basepos = 0;
       if (lane == 0 && km) basepos = atomicAdd(&n_cand, __popc(km));
@@ -206,9 +206,9 @@ __global__ void __launch_bounds__(THREADS)
     }
     return;
   }
+  }  // fast path
 
   // ---- overflow fallback: exact select straight from H, ties in index order ----
-  if (tid == 0 && status) atomicCAS(status, 0, 0);  // (no error: the fallback is exact)
   auto load_full = [&](int i) -> uint32_t {
     return col_ok(mask, i) ? bf16_to_key(hrow[i]) : 0x10000u;
   };

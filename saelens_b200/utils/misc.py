@@ -1,0 +1,83 @@
+"""Small helpers shared across the package (dtype names, dataclass filtering, temp dirs)."""
+
+from __future__ import annotations
+
+import dataclasses
+import tempfile
+from collections.abc import Iterator
+from contextlib import contextmanager
+from pathlib import Path
+from typing import Any
+
+import torch
+
+DTYPE_MAP: dict[str, torch.dtype] = {
+    "float32": torch.float32,
+    "float64": torch.float64,
+    "float16": torch.float16,
+    "bfloat16": torch.bfloat16,
+    "torch.float32": torch.float32,
+    "torch.float64": torch.float64,
+    "torch.float16": torch.float16,
+    "torch.bfloat16": torch.bfloat16,
+    "fp32": torch.float32,
+    "fp16": torch.float16,
+    "bf16": torch.bfloat16,
+}
+
+
+def str_to_dtype(dtype: str | torch.dtype) -> torch.dtype:
+    if isinstance(dtype, torch.dtype):
+        return dtype
+    try:
+        return DTYPE_MAP[dtype]
+    except KeyError as e:
+        raise ValueError(f"unknown dtype {dtype!r}; expected one of {sorted(DTYPE_MAP)}") from e
+
+
+def dtype_to_str(dtype: torch.dtype | str) -> str:
+    if isinstance(dtype, str):
+        return dtype_to_str(str_to_dtype(dtype))
+    for name in ("float32", "float64", "float16", "bfloat16"):
+        if DTYPE_MAP[name] == dtype:
+            return name
+    raise ValueError(f"unsupported dtype {dtype}")
+
+
+def filter_valid_dataclass_fields(data: dict[str, Any], cls: Any,
+                                  whitelist: list[str] | None = None) -> dict[str, Any]:
+    """Keep only the keys of `data` that are init fields of dataclass `cls`."""
+    names = {f.name for f in dataclasses.fields(cls) if f.init}
+    if whitelist:
+        names |= set(whitelist)
+    return {k: v for k, v in data.items() if k in names}
+
+
+@contextmanager
+def path_or_tmp_dir(path: str | Path | None) -> Iterator[Path]:
+    if path is None:
+        with tempfile.TemporaryDirectory() as d:
+            yield Path(d)
+    else:
+        yield Path(path)
+
+
+def get_special_token_ids(tokenizer: Any) -> list[int]:
+    ids: set[int] = set()
+    for attr in ("bos_token_id", "eos_token_id", "pad_token_id", "unk_token_id", "sep_token_id"):
+        v = getattr(tokenizer, attr, None)
+        if v is not None:
+            ids.add(int(v))
+    extra = getattr(tokenizer, "all_special_ids", None)
+    if extra:
+        ids.update(int(i) for i in extra)
+    return sorted(ids)
+
+
+def extract_stop_at_layer_from_hook_name(hook_name: str) -> int | None:
+    """`blocks.6.hook_resid_pre` -> 7: the LM forward can stop after the hook's layer."""
+    parts = hook_name.split(".")
+    for i, p in enumerate(parts):
+        if p == "blocks" and i + 1 < len(parts) and parts[i + 1].isdigit():
+            return int(parts[i + 1]) + 1
+    return None

@@ -1,0 +1,142 @@
+"""The fused native TopK training step against a plain PyTorch fp32 restatement."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _setup(d_in=256, d_sae=2048, k=32, B=512, seed=0, b_dec_scale=0.05):
+    from saelens_b200.models.topk import TopKTrainingSAE, TopKTrainingSAEConfig
+
+    torch.manual_seed(seed)
+    sae = TopKTrainingSAE(TopKTrainingSAEConfig(d_in=d_in, d_sae=d_sae, k=k, device="cuda"))
+    with torch.no_grad():
+        sae.b_enc.normal_(0, 0.01)
+        sae.b_dec.normal_(0, b_dec_scale)
+        sae.W_enc.add_(torch.randn_like(sae.W_enc) * 0.01)
+    x = torch.randn(B, d_in, device="cuda")
+    return sae, x
+
+
+def _oracle(w_enc_bf16, w_dec_bf16, b_enc, b_dec, x_bf16, idx, k):
+    """fp32 autograd of the reference TopK training loss for a given per-row selection."""
+    We = w_enc_bf16.float().T.clone().requires_grad_(True)  # [d_in, d_sae]
+    Wd = w_dec_bf16.float().clone().requires_grad_(True)
+    be = b_enc.float().clone().requires_grad_(True)
+    bd = b_dec.float().clone().requires_grad_(True)
+    x = x_bf16.float()
+    sae_in = x - bd
+    pre = sae_in @ We + be
+    norm = Wd.norm(dim=-1)
+    h = pre * norm
+    sel = torch.gather(h, 1, idx.long())
+    acts = torch.zeros_like(h).scatter(1, idx.long(), sel.relu())
+    out = (acts / norm) @ Wd + bd
+    mse = (out - x).pow(2).sum(-1).mean()
+    mse.backward()
+    return mse.detach(), h.detach(), {"W_enc": We.grad, "W_dec": Wd.grad, "b_enc": be.grad, "b_dec": bd.grad}
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
+
+
+def test_engine_gradients_match_fp32_autograd():
+    from saelens_b200.training.engine import FusedTopKEngine
+
+    sae, x = _setup()
+    eng = FusedTopKEngine(sae, lr=1e-3)
+    xb = x.to(torch.bfloat16)
+    w_enc0, w_dec0 = eng.w_enc.clone(), eng.w_dec.clone()
+    b_enc0, b_dec0 = eng.p_benc.clone(), eng.p_bdec.clone()
+    res = eng.step(xb, update=False)
+    torch.cuda.synchronize()
+    eng.status.check()
+    mse, h, grads = _oracle(w_enc0, w_dec0, b_enc0, b_dec0, xb, res.topk_idx, eng.k)
+    # selection is a valid top-k of the fp32 pre-activations up to bf16 rounding of H
+    kth = torch.topk(h, eng.k, dim=-1).values[:, -1:]
+    chosen = torch.gather(h, 1, res.topk_idx.long())
+    assert (chosen >= kth - 0.02 * kth.abs() - 1e-3).all()
+    assert abs(res.mse_loss.item() - mse.item()) <= 2e-2 * mse.item()
+    assert _rel(eng.g_dec, grads["W_dec"]) < 2e-2
+    assert _rel(eng.g_enc, grads["W_enc"].T) < 2e-2
+    assert _rel(eng.g_benc, grads["b_enc"]) < 2e-2
+
+
+def test_engine_adam_step_matches_torch_adam():
+    from saelens_b200.training.engine import FusedTopKEngine
+
+    sae, x = _setup(seed=1)
+    eng = FusedTopKEngine(sae, lr=1e-3)
+    xb = x.to(torch.bfloat16)
+    w_enc0, w_dec0 = eng.w_enc.clone(), eng.w_dec.clone()
+    b_enc0, b_dec0 = eng.p_benc.clone(), eng.p_bdec.clone()
+    p_enc0, p_dec0 = eng.p_enc.clone(), eng.p_dec.clone()
+    res = eng.step(xb, update=True)
+    torch.cuda.synchronize()
+    _, _, grads = _oracle(w_enc0, w_dec0, b_enc0, b_dec0, xb, res.topk_idx, eng.k)
+    # torch reference: clip_grad_norm_(1.0) then one Adam step from the same fp32 masters
+    params = {"W_enc": p_enc0.T.clone(), "W_dec": p_dec0.clone(), "b_enc": b_enc0.clone(), "b_dec": b_dec0.clone()}
+    ps = [torch.nn.Parameter(v) for v in params.values()]
+    for p, name in zip(ps, params):
+        p.grad = grads[name].float().clone()
+    total = torch.nn.utils.clip_grad_norm_(ps, 1.0)
+    assert abs(eng.grad_norm().item() - total.item()) <= 2e-2 * total.item()
+    opt = torch.optim.Adam(ps, lr=1e-3)
+    opt.step()
+    # first Adam step moves every parameter with a non-negligible gradient by ~lr
+    for p, name, got in zip(ps, params, [eng.p_enc.T, eng.p_dec, eng.p_benc, eng.p_bdec]):
+        d_ref = p.detach() - params[name]
+        d_got = got - params[name]
+        big = grads[name].abs() > 1e-3 * grads[name].abs().max()
+        agree = (torch.sign(d_ref[big]) == torch.sign(d_got[big])).float().mean().item()
+        assert agree > 0.99, (name, agree)
+        assert torch.allclose(d_got[big], d_ref[big], atol=2e-4, rtol=0.05), name
+
+
+def test_engine_training_reduces_loss_and_tracks_stats():
+    from saelens_b200.training.engine import FusedTopKEngine
+
+    sae, x = _setup(d_in=512, d_sae=4096, k=32, B=1024, seed=2)
+    eng = FusedTopKEngine(sae, lr=2e-3)
+    xb = x.to(torch.bfloat16)
+    act = torch.zeros(4096, device="cuda")
+    since = torch.zeros(4096, device="cuda")
+    losses = [eng.step(xb, act_freq=act, since_fired=since).loss.item() for _ in range(30)]
+    torch.cuda.synchronize()
+    eng.status.check()
+    assert all(math.isfinite(v) for v in losses)
+    assert losses[-1] < 0.7 * losses[0]
+    assert int(act.sum().item()) > 0
+    assert ((since == 0) == (eng.fire_counts > 0)).all()
+
+
+def test_engine_aux_loss_matches_reference():
+    from saelens_b200.training.engine import FusedTopKEngine
+
+    sae, x = _setup(d_in=256, d_sae=1024, k=16, B=256, seed=3)
+    import copy
+
+    ref_sae = copy.deepcopy(sae)
+    eng = FusedTopKEngine(sae, lr=1e-3)
+    xb = x.to(torch.bfloat16)
+    dead = torch.zeros(1024, dtype=torch.bool, device="cuda")
+    dead[::3] = True
+    res = eng.step(xb, dead_mask=dead, run_aux=True, update=False)
+    torch.cuda.synchronize()
+    eng.status.check()
+    # reference aux loss from the module math with bf16-rounded weights
+    with torch.no_grad():
+        ref_sae.W_enc.copy_(eng.w_enc.float().T)
+        ref_sae.W_dec.copy_(eng.w_dec.float())
+        ref_sae.b_dec.copy_(eng.p_bdec)
+        ref_sae.b_enc.copy_(eng.p_benc)
+    from saelens_b200.models.sae import TrainStepInput
+
+    out = ref_sae.training_forward_pass(TrainStepInput(sae_in=xb.float(), coefficients={}, dead_neuron_mask=dead))
+    ref_aux = out.losses["auxiliary_reconstruction_loss"].item()
+    assert ref_aux > 0
+    assert abs(res.aux_loss.item() - ref_aux) <= 5e-2 * ref_aux
