@@ -102,18 +102,21 @@ struct RowArgs {
   int update;                     // 0: only recompute scale / bias_eff
 };
 
-constexpr int ROW_THREADS = 128;
+constexpr int ROW_THREADS = 256;  // 8 warps, one latent row per warp
+constexpr int ROW_UNROLL = 4;
 
-__device__ __forceinline__ void process_vec4(float* P, float* Mm, float* V, __nv_bfloat16* W,
-                                             const __nv_bfloat16* G, int64_t off, bool has_g,
-                                             float c, const Hyper& h, int update, float4& wq) {
-  float4 p = *reinterpret_cast<float4*>(P + off);
+// Adam on 4 consecutive elements of one row; streaming (evict-first) loads and stores since
+// every byte of optimizer state is touched exactly once per step.
+__device__ __forceinline__ float4 adam_vec4(float* P, float* Mm, float* V, __nv_bfloat16* W,
+                                            const __nv_bfloat16* G, int64_t off, bool has_g, float c,
+                                            const Hyper& h, int update) {
+  float4 p = __ldcs(reinterpret_cast<const float4*>(P + off));
   if (update) {
-    float4 m = *reinterpret_cast<float4*>(Mm + off);
-    float4 v = *reinterpret_cast<float4*>(V + off);
+    float4 m = __ldcs(reinterpret_cast<const float4*>(Mm + off));
+    float4 v = __ldcs(reinterpret_cast<const float4*>(V + off));
     float g0 = 0.f, g1 = 0.f, g2 = 0.f, g3 = 0.f;
     if (has_g) {
-      const uint2 gr = *reinterpret_cast<const uint2*>(G + off);
+      const uint2 gr = __ldcs(reinterpret_cast<const uint2*>(G + off));
       const __nv_bfloat162* g2p = reinterpret_cast<const __nv_bfloat162*>(&gr);
       const float2 a = __bfloat1622float2(g2p[0]), b = __bfloat1622float2(g2p[1]);
       g0 = a.x * c; g1 = a.y * c; g2 = b.x * c; g3 = b.y * c;
@@ -122,42 +125,57 @@ __device__ __forceinline__ void process_vec4(float* P, float* Mm, float* V, __nv
     adam_update(p.y, m.y, v.y, g1, h);
     adam_update(p.z, m.z, v.z, g2, h);
     adam_update(p.w, m.w, v.w, g3, h);
-    *reinterpret_cast<float4*>(P + off) = p;
-    *reinterpret_cast<float4*>(Mm + off) = m;
-    *reinterpret_cast<float4*>(V + off) = v;
+    __stcs(reinterpret_cast<float4*>(P + off), p);
+    __stcs(reinterpret_cast<float4*>(Mm + off), m);
+    __stcs(reinterpret_cast<float4*>(V + off), v);
   }
   __nv_bfloat162 lo = __floats2bfloat162_rn(p.x, p.y), hi = __floats2bfloat162_rn(p.z, p.w);
   uint2 o;
   o.x = *reinterpret_cast<uint32_t*>(&lo);
   o.y = *reinterpret_cast<uint32_t*>(&hi);
-  *reinterpret_cast<uint2*>(W + off) = o;
+  *reinterpret_cast<uint2*>(W + off) = o;  // the bf16 copy is read by the next GEMM: keep in L2
   const float2 a = __bfloat1622float2(lo), b = __bfloat1622float2(hi);
-  wq = make_float4(a.x, a.y, b.x, b.y);
+  return make_float4(a.x, a.y, b.x, b.y);
 }
 
 __global__ void __launch_bounds__(ROW_THREADS) rows_kernel(RowArgs a, Hyper h) {
-  __shared__ float red[32];
-  const float c = a.update ? clip_coef(nullptr, 0.f) * (a.clip ? *a.clip : 1.f) : 1.f;
+  const float c = (a.update && a.clip) ? *a.clip : 1.f;
   const int nv4 = a.D >> 2;
-  for (int j = blockIdx.x; j < a.N; j += gridDim.x) {
+  const int lane = threadIdx.x & 31;
+  const int warps_total = gridDim.x * (ROW_THREADS / 32);
+  for (int j = blockIdx.x * (ROW_THREADS / 32) + (threadIdx.x >> 5); j < a.N; j += warps_total) {
     const bool has_g = a.update && a.colptr && (a.colptr[j + 1] > a.colptr[j]);
     const int64_t base = int64_t(j) * a.D;
     float nrm = 0.f, dot = 0.f;
-#pragma unroll 2
-    for (int s = threadIdx.x; s < nv4; s += ROW_THREADS) {
-      const int64_t off = base + 4 * int64_t(s);
-      float4 wq;
-      process_vec4(a.pd, a.md, a.vd, a.wd, a.gd, off, has_g, c, h, a.update, wq);
-      nrm += wq.x * wq.x + wq.y * wq.y + wq.z * wq.z + wq.w * wq.w;
-      process_vec4(a.pe, a.me, a.ve, a.we, a.ge, off, has_g, c, h, a.update, wq);
-      if (a.b_dec) {
-        const float4 bd = *reinterpret_cast<const float4*>(a.b_dec + 4 * s);
-        dot += wq.x * bd.x + wq.y * bd.y + wq.z * bd.z + wq.w * bd.w;
+    for (int s0 = lane; s0 < nv4; s0 += 32 * ROW_UNROLL) {
+      float4 wd[ROW_UNROLL], we[ROW_UNROLL];
+#pragma unroll
+      for (int u = 0; u < ROW_UNROLL; ++u) {
+        const int s = s0 + 32 * u;
+        if (s < nv4) {
+          const int64_t off = base + 4 * int64_t(s);
+          wd[u] = adam_vec4(a.pd, a.md, a.vd, a.wd, a.gd, off, has_g, c, h, a.update);
+          we[u] = adam_vec4(a.pe, a.me, a.ve, a.we, a.ge, off, has_g, c, h, a.update);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < ROW_UNROLL; ++u) {
+        const int s = s0 + 32 * u;
+        if (s < nv4) {
+          nrm += wd[u].x * wd[u].x + wd[u].y * wd[u].y + wd[u].z * wd[u].z + wd[u].w * wd[u].w;
+          if (a.b_dec) {
+            const float4 bd = __ldg(reinterpret_cast<const float4*>(a.b_dec) + s);
+            dot += we[u].x * bd.x + we[u].y * bd.y + we[u].z * bd.z + we[u].w * bd.w;
+          }
+        }
       }
     }
-    const float n2 = block_sum(nrm, red);
-    const float dt = block_sum(dot, red);
-    if (threadIdx.x == 0) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      nrm += __shfl_xor_sync(0xffffffffu, nrm, o);
+      dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    }
+    if (lane == 0) {
       float pb = a.pb[j];
       if (a.update) {
         float mb = a.mb[j], vb = a.vb[j];
@@ -167,10 +185,10 @@ __global__ void __launch_bounds__(ROW_THREADS) rows_kernel(RowArgs a, Hyper h) {
         a.mb[j] = mb;
         a.vb[j] = vb;
       }
-      const float nr = sqrtf(n2);
+      const float nr = sqrtf(nrm);
       if (a.scale) a.scale[j] = nr;
       if (a.inv_scale) a.inv_scale[j] = 1.f / nr;
-      if (a.bias_eff) a.bias_eff[j] = pb - dt;
+      if (a.bias_eff) a.bias_eff[j] = pb - dot;
     }
   }
 }
@@ -252,7 +270,7 @@ void adam_rows(const torch::Tensor& pd, const torch::Tensor& md, const torch::Te
   a.update = update ? 1 : 0;
   TORCH_CHECK(!update || (a.gd && a.ge && a.gb && a.colptr), "adam_rows: gradients required for update");
   if (N == 0) return;
-  const int64_t grid = std::min<int64_t>(N, int64_t(sm_count_adam()) * 8);
+  const int64_t grid = std::min<int64_t>((N + 7) / 8, int64_t(sm_count_adam()) * 8);
   adam::rows_kernel<<<dim3(grid), dim3(adam::ROW_THREADS), 0, at::cuda::getCurrentCUDAStream()>>>(
       a, make_hyper(lr, beta1, beta2, eps, std::max<int64_t>(step, 1), 0.0));
   C10_CUDA_KERNEL_LAUNCH_CHECK();

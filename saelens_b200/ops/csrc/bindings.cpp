@@ -47,6 +47,15 @@ void adam_rows(const torch::Tensor& pd, const torch::Tensor& md, const torch::Te
                const c10::optional<torch::Tensor>& scale, const c10::optional<torch::Tensor>& inv_scale,
                const c10::optional<torch::Tensor>& bias_eff, double lr, double beta1, double beta2,
                double eps, int64_t step, bool update);
+void topk_merge(const torch::Tensor& cand_val, const torch::Tensor& cand_idx, int64_t n_local, int64_t rank,
+                const c10::optional<torch::Tensor>& k_dev, const torch::Tensor& out_val,
+                const torch::Tensor& out_idx);
+void decode_partial(const torch::Tensor& vals, const torch::Tensor& idx, bool relu,
+                    const c10::optional<torch::Tensor>& inv_scale, const torch::Tensor& W, const torch::Tensor& out);
+void finish_mse(const torch::Tensor& xsum, const c10::optional<torch::Tensor>& bias, const torch::Tensor& target,
+                const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& resid,
+                const c10::optional<torch::Tensor>& dxhat, const c10::optional<torch::Tensor>& grad_coef_dev,
+                double grad_coef, const torch::Tensor& loss_row, const c10::optional<torch::Tensor>& bsum);
 }  // namespace sb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -59,4 +68,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("latent_grad", &sb::latent_grad);
   m.def("adam_bdec", &sb::adam_bdec);
   m.def("adam_rows", &sb::adam_rows);
+  m.def("topk_merge", &sb::topk_merge);
+  m.def("decode_partial", &sb::decode_partial);
+  m.def("finish_mse", &sb::finish_mse);
 }

@@ -87,7 +87,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // ----------------------------------------------------------------------------------------
-// TMA (no multicast anywhere in this library)
+// TMA loads: every copy targets only the issuing CTA's own shared memory
 // ----------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

@@ -106,29 +106,35 @@ __global__ void __launch_bounds__(DEC_THREADS)
     for (int v = 0; v < VPT; ++v)
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[v][e] = 0.f;
+    constexpr int U = 4;  // selected latents whose rows are in flight together
     int i = 0;
-    for (; i + 2 <= k; i += 2) {
-      const int j0 = s_i[i], j1 = s_i[i + 1];
-      const float a0 = s_a[i], a1 = s_a[i + 1];
-      uint4 w0[VPT], w1[VPT];
+    for (; i + U <= k; i += U) {
+      int jj[U];
+      float aa[U];
 #pragma unroll
-      for (int v = 0; v < VPT; ++v) {
-        const int vi = t + v * DEC_THREADS;
-        w0[v] = (j0 >= 0 && vi < nvec)
-                    ? __ldg(reinterpret_cast<const uint4*>(W + int64_t(j0) * ldw) + vi)
-                    : make_uint4(0, 0, 0, 0);
-        w1[v] = (j1 >= 0 && vi < nvec)
-                    ? __ldg(reinterpret_cast<const uint4*>(W + int64_t(j1) * ldw) + vi)
-                    : make_uint4(0, 0, 0, 0);
+      for (int u = 0; u < U; ++u) {
+        jj[u] = s_i[i + u];
+        aa[u] = s_a[i + u];
       }
+      uint4 w[U][VPT];
 #pragma unroll
-      for (int v = 0; v < VPT; ++v) {
-        float f0[8], f1[8];
-        bf16x8_to_f32(w0[v], f0);
-        bf16x8_to_f32(w1[v], f1);
+      for (int u = 0; u < U; ++u)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[v][e] += a0 * f0[e] + a1 * f1[e];
-      }
+        for (int v = 0; v < VPT; ++v) {
+          const int vi = t + v * DEC_THREADS;
+          w[u][v] = (jj[u] >= 0 && vi < nvec)
+                        ? __ldg(reinterpret_cast<const uint4*>(W + int64_t(jj[u]) * ldw) + vi)
+                        : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int v = 0; v < VPT; ++v) {
+          float f[8];
+          bf16x8_to_f32(w[u][v], f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[v][e] += aa[u] * f[e];
+        }
     }
     for (; i < k; ++i) {
       const int j0 = s_i[i];
@@ -197,6 +203,140 @@ __global__ void __launch_bounds__(DEC_THREADS)
 }
 
 // ---------------------------------------------------------------------------------------
+// Tensor-parallel pieces of the decode.  `decode_partial` writes this rank's partial
+// reconstruction sum_i a_i W_dec[idx_i] (fp32, no bias) for every row; after the partials are
+// reduce-scattered, `finish_mse` adds b_dec and produces the loss, dL/dx_hat, the residual and
+// the column sum for the b_dec gradient on this rank's rows.
+// ---------------------------------------------------------------------------------------
+template <int VPT>
+__global__ void __launch_bounds__(DEC_THREADS)
+    decode_partial_kernel(const float* __restrict__ vals, const int* __restrict__ idx, int k, int64_t ldk,
+                          int relu, const float* __restrict__ inv_scale, const __nv_bfloat16* __restrict__ W,
+                          int64_t ldw, float* __restrict__ out, int64_t ldo, int M, int D) {
+  extern __shared__ float dsm[];
+  float* s_a = dsm;
+  int* s_i = reinterpret_cast<int*>(dsm + k);
+  const int nvec = D >> 3;
+  const int t = threadIdx.x;
+  for (int row = blockIdx.x; row < M; row += gridDim.x) {
+    __syncthreads();
+    for (int i = t; i < k; i += DEC_THREADS) {
+      const int j = idx[int64_t(row) * ldk + i];
+      float a = 0.f;
+      if (j >= 0) {
+        const float v = vals[int64_t(row) * ldk + i];
+        a = (relu ? fmaxf(v, 0.f) : v) * (inv_scale ? __ldg(inv_scale + j) : 1.f);
+      }
+      s_a[i] = a;
+      s_i[i] = (a != 0.f) ? j : -1;
+    }
+    __syncthreads();
+    float acc[VPT][8];
+#pragma unroll
+    for (int v = 0; v < VPT; ++v)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[v][e] = 0.f;
+    constexpr int U = 4;
+    int i = 0;
+    for (; i + U <= k; i += U) {
+      uint4 w[U][VPT];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int jj = s_i[i + u];
+#pragma unroll
+        for (int v = 0; v < VPT; ++v) {
+          const int vi = t + v * DEC_THREADS;
+          w[u][v] = (jj >= 0 && vi < nvec) ? __ldg(reinterpret_cast<const uint4*>(W + int64_t(jj) * ldw) + vi)
+                                           : make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const float aa = s_a[i + u];
+#pragma unroll
+        for (int v = 0; v < VPT; ++v) {
+          float f[8];
+          bf16x8_to_f32(w[u][v], f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[v][e] += aa * f[e];
+        }
+      }
+    }
+    for (; i < k; ++i) {
+      const int jj = s_i[i];
+      if (jj < 0) continue;
+      const float aa = s_a[i];
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        const int vi = t + v * DEC_THREADS;
+        if (vi < nvec) {
+          float f[8];
+          bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(W + int64_t(jj) * ldw) + vi), f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[v][e] += aa * f[e];
+        }
+      }
+    }
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int vi = t + v * DEC_THREADS;
+      if (vi < nvec) {
+        float4* o = reinterpret_cast<float4*>(out + int64_t(row) * ldo) + 2 * vi;
+        o[0] = make_float4(acc[v][0], acc[v][1], acc[v][2], acc[v][3]);
+        o[1] = make_float4(acc[v][4], acc[v][5], acc[v][6], acc[v][7]);
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(DEC_THREADS)
+    finish_mse_kernel(const float* __restrict__ xsum, int64_t lds, const float* __restrict__ bias,
+                      const __nv_bfloat16* __restrict__ target, int64_t ldt, __nv_bfloat16* __restrict__ out,
+                      __nv_bfloat16* __restrict__ resid, __nv_bfloat16* __restrict__ dxhat,
+                      const float* grad_coef_dev, float grad_coef, float* __restrict__ loss_row,
+                      float* __restrict__ bsum, int M, int D) {
+  __shared__ float red[32];
+  const int nvec = D >> 3;
+  const float gcoef = grad_coef_dev ? grad_coef * __ldg(grad_coef_dev) : grad_coef;
+  for (int row = blockIdx.x; row < M; row += gridDim.x) {
+    float lsum = 0.f;
+    for (int vi = threadIdx.x; vi < nvec; vi += DEC_THREADS) {
+      const float4* xs = reinterpret_cast<const float4*>(xsum + int64_t(row) * lds) + 2 * vi;
+      const float4 a0 = xs[0], a1 = xs[1];
+      float xh[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      if (bias) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xh[e] += __ldg(bias + 8 * vi + e);
+      }
+      float tg[8];
+      bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(target + int64_t(row) * ldt) + vi), tg);
+      float err[8], g[8], rs[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        err[e] = xh[e] - tg[e];
+        lsum += err[e] * err[e];
+        g[e] = err[e] * gcoef;
+        rs[e] = -err[e];
+      }
+      if (out) reinterpret_cast<uint4*>(out + int64_t(row) * D)[vi] = f32_to_bf16x8(xh);
+      if (resid) reinterpret_cast<uint4*>(resid + int64_t(row) * D)[vi] = f32_to_bf16x8(rs);
+      if (dxhat) {
+        const uint4 gq = f32_to_bf16x8(g);
+        reinterpret_cast<uint4*>(dxhat + int64_t(row) * D)[vi] = gq;
+        if (bsum) {
+          float gr[8];
+          bf16x8_to_f32(gq, gr);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) atomicAdd(bsum + 8 * vi + e, gr[e]);
+        }
+      }
+    }
+    const float tot = block_sum(lsum, red);
+    if (threadIdx.x == 0 && loss_row) loss_row[row] = tot;
+  }
+}
+
+// ---------------------------------------------------------------------------------------
 // CSC build.  Pair p (= b * k + i for the main list, M*k + b*k_aux + i for the aux list) is
 // kept when its coefficient is non-zero.
 // ---------------------------------------------------------------------------------------
@@ -244,10 +384,13 @@ __global__ void csc_fill_kernel(const float* __restrict__ vals, const int* __res
 }
 
 // ---------------------------------------------------------------------------------------
-// latent gradients.  One CTA (128 threads) per latent, grid-stride over latents.
+// latent gradients.  One CTA (256 threads) per latent, grid-stride over latents.  Entries of a
+// latent are processed in groups of LG_GROUP: every thread loads its slice of all the group's
+// gradient rows at once (many loads in flight), accumulates gW_dec and its partial dot products,
+// one block reduction yields the group's dz, then the group's input rows are loaded for gW_enc.
 // ---------------------------------------------------------------------------------------
-constexpr int LG_THREADS = 128;
-constexpr int LG_MAX_CHUNK = 256;  // entries whose dot products are staged at once
+constexpr int LG_THREADS = 256;
+constexpr int LG_GROUP = 4;
 
 struct LatentGradArgs {
   const int64_t* colptr;
@@ -276,51 +419,39 @@ struct LatentGradArgs {
 };
 
 template <int VPT>
-__global__ void __launch_bounds__(LG_THREADS) latent_grad_kernel(LatentGradArgs a) {
-  __shared__ float s_dz[LG_MAX_CHUNK];
-  __shared__ float s_coef[LG_MAX_CHUNK];
-  __shared__ int64_t s_row[LG_MAX_CHUNK];
-  __shared__ int s_aux[LG_MAX_CHUNK];
+__global__ void __launch_bounds__(LG_THREADS, 2) latent_grad_kernel(LatentGradArgs a) {
+  __shared__ float s_coef[LG_GROUP];
+  __shared__ int64_t s_row[LG_GROUP];
+  __shared__ int s_aux[LG_GROUP];
+  __shared__ float s_red[LG_THREADS / 32][LG_GROUP];
   __shared__ float red[32];
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int nvec = a.D >> 3;
   float bt[VPT][8];
-  float bdec[VPT][8];
 #pragma unroll
-  for (int v = 0; v < VPT; ++v) {
-    const int vi = t + v * LG_THREADS;
+  for (int v = 0; v < VPT; ++v)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      bt[v][e] = 0.f;
-      bdec[v][e] = (a.b_dec && vi < nvec) ? a.b_dec[8 * vi + e] : 0.f;
-    }
-  }
+    for (int e = 0; e < 8; ++e) bt[v][e] = 0.f;
   float sq = 0.f;
 
   for (int j = blockIdx.x; j < a.N; j += gridDim.x) {
     const int64_t beg = a.colptr[j], end = a.colptr[j + 1];
-    if (t == 0) {
-      if (a.fire_counts) {
-        const int fc = a.fire_counts[j];
-        if (a.act_freq) a.act_freq[j] += float(fc);
-        if (a.since_fired) a.since_fired[j] = fc > 0 ? 0.f : a.since_fired[j] + 1.f;
-      }
+    if (t == 0 && a.fire_counts) {
+      const int fc = a.fire_counts[j];
+      if (a.act_freq) a.act_freq[j] += float(fc);
+      if (a.since_fired) a.since_fired[j] = fc > 0 ? 0.f : a.since_fired[j] + 1.f;
     }
     if (beg == end) {
       if (t == 0) a.gb_enc[j] = 0.f;
       continue;
     }
     const float isc = a.inv_scale ? a.inv_scale[j] : 1.f;
-    // W_dec row slice in registers (fp32)
-    float wd[VPT][8];
+    uint4 wraw[VPT];
 #pragma unroll
     for (int v = 0; v < VPT; ++v) {
       const int vi = t + v * LG_THREADS;
-      if (vi < nvec)
-        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(a.W_dec + int64_t(j) * a.D) + vi), wd[v]);
-      else
-#pragma unroll
-        for (int e = 0; e < 8; ++e) wd[v][e] = 0.f;
+      wraw[v] = vi < nvec ? __ldg(reinterpret_cast<const uint4*>(a.W_dec + int64_t(j) * a.D) + vi)
+                          : make_uint4(0, 0, 0, 0);
     }
     float gd[VPT][8], ge[VPT][8];
 #pragma unroll
@@ -329,63 +460,114 @@ __global__ void __launch_bounds__(LG_THREADS) latent_grad_kernel(LatentGradArgs 
       for (int e = 0; e < 8; ++e) gd[v][e] = ge[v][e] = 0.f;
     float gbe = 0.f;
 
-    for (int64_t c0 = beg; c0 < end; c0 += LG_MAX_CHUNK) {
-      const int cn = int((end - c0) < int64_t(LG_MAX_CHUNK) ? (end - c0) : int64_t(LG_MAX_CHUNK));
-      __syncthreads();
-      for (int e = t; e < cn; e += LG_THREADS) {
-        const int64_t p = a.pairs[c0 + e];
+    for (int64_t c0 = beg; c0 < end; c0 += LG_GROUP) {
+      const int cn = int((end - c0) < int64_t(LG_GROUP) ? (end - c0) : int64_t(LG_GROUP));
+      __syncthreads();  // previous group's s_* reads are done
+      if (t < cn) {
+        const int64_t p = a.pairs[c0 + t];
         if (p < a.n_main) {
-          s_row[e] = p / a.k;
-          s_coef[e] = fmaxf(a.vals[p], 0.f) * isc;
-          s_aux[e] = 0;
+          s_row[t] = p / a.k;
+          s_coef[t] = fmaxf(a.vals[p], 0.f) * isc;
+          s_aux[t] = 0;
         } else {
           const int64_t q = p - a.n_main;
-          s_row[e] = q / a.k_aux;
-          s_coef[e] = a.aux_vals[q] * isc;
-          s_aux[e] = 1;
+          s_row[t] = q / a.k_aux;
+          s_coef[t] = a.aux_vals[q] * isc;
+          s_aux[t] = 1;
         }
       }
       __syncthreads();
-      // phase 1: dot products <gradrow, W_dec[j]>, one warp per entry
-      for (int e = warp; e < cn; e += LG_THREADS / 32) {
-        const __nv_bfloat16* grow = (s_aux[e] ? a.daux : a.dxhat) + s_row[e] * int64_t(a.D);
-        float d = 0.f;
-        for (int vi = lane; vi < nvec; vi += 32) {
-          float g[8], w[8];
-          bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(grow) + vi), g);
-          bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(a.W_dec + int64_t(j) * a.D) + vi), w);
+      // gradient rows of the whole group in flight at once
+      uint4 graw[LG_GROUP][VPT];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) d += g[q] * w[q];
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-        if (lane == 0) s_dz[e] = d;  // main pairs are live only where a > 0, so no mask needed
-      }
-      __syncthreads();
-      // phase 2: accumulate gW_dec, gW_enc
-      for (int e = 0; e < cn; ++e) {
-        const float coef = s_coef[e];
-        const float dz = s_dz[e];
-        gbe += dz;
-        const __nv_bfloat16* grow = (s_aux[e] ? a.daux : a.dxhat) + s_row[e] * int64_t(a.D);
-        const __nv_bfloat16* xrow = a.x + s_row[e] * a.ldx;
+      for (int e = 0; e < LG_GROUP; ++e) {
+        const __nv_bfloat16* grow = e < cn ? (s_aux[e] ? a.daux : a.dxhat) + s_row[e] * int64_t(a.D) : nullptr;
 #pragma unroll
         for (int v = 0; v < VPT; ++v) {
           const int vi = t + v * LG_THREADS;
-          if (vi < nvec) {
-            float g[8], xv[8];
-            bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(grow) + vi), g);
-            bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(xrow) + vi), xv);
+          graw[e][v] = (e < cn && vi < nvec) ? __ldg(reinterpret_cast<const uint4*>(grow) + vi)
+                                             : make_uint4(0, 0, 0, 0);
+        }
+      }
+      float pd[LG_GROUP];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              gd[v][q] += coef * g[q];
-              ge[v][q] += dz * (xv[q] - bdec[v][q]);
-            }
+      for (int e = 0; e < LG_GROUP; ++e) {
+        const float coef = e < cn ? s_coef[e] : 0.f;
+        float d = 0.f;
+#pragma unroll
+        for (int v = 0; v < VPT; ++v) {
+          float g[8], w[8];
+          bf16x8_to_f32(graw[e][v], g);
+          bf16x8_to_f32(wraw[v], w);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            gd[v][q] += coef * g[q];
+            d += g[q] * w[q];
           }
+        }
+        pd[e] = d;
+      }
+#pragma unroll
+      for (int e = 0; e < LG_GROUP; ++e) {
+        float d = pd[e];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        if (lane == 0) s_red[warp][e] = d;
+      }
+      __syncthreads();
+      float dz[LG_GROUP];
+#pragma unroll
+      for (int e = 0; e < LG_GROUP; ++e) {
+        float d = 0.f;
+#pragma unroll
+        for (int w = 0; w < LG_THREADS / 32; ++w) d += s_red[w][e];
+        dz[e] = e < cn ? d : 0.f;  // main pairs are live only where a > 0: no extra mask needed
+        gbe += dz[e];
+      }
+      // encoder gradient: input rows of the group in flight at once
+      uint4 xraw[LG_GROUP][VPT];
+#pragma unroll
+      for (int e = 0; e < LG_GROUP; ++e) {
+        const __nv_bfloat16* xrow = e < cn ? a.x + s_row[e] * a.ldx : nullptr;
+#pragma unroll
+        for (int v = 0; v < VPT; ++v) {
+          const int vi = t + v * LG_THREADS;
+          xraw[e][v] = (e < cn && vi < nvec) ? __ldg(reinterpret_cast<const uint4*>(xrow) + vi)
+                                             : make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        const int vi = t + v * LG_THREADS;
+        float bd[8];
+        if (a.b_dec && vi < nvec) {
+          const float4 b0 = __ldg(reinterpret_cast<const float4*>(a.b_dec) + 2 * vi);
+          const float4 b1 = __ldg(reinterpret_cast<const float4*>(a.b_dec) + 2 * vi + 1);
+          bd[0] = b0.x; bd[1] = b0.y; bd[2] = b0.z; bd[3] = b0.w;
+          bd[4] = b1.x; bd[5] = b1.y; bd[6] = b1.z; bd[7] = b1.w;
+        } else {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) bd[q] = 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < LG_GROUP; ++e) {
+          float xv[8];
+          bf16x8_to_f32(xraw[e][v], xv);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) ge[v][q] += dz[e] * (xv[q] - bd[q]);
         }
       }
     }
-    // write gradient rows (bf16) and accumulate their squared norm
+    // write gradient rows (bf16), squared norm of what Adam will read, b_dec term
+    uint4 weraw[VPT];
+    if (a.bterm) {
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        const int vi = t + v * LG_THREADS;
+        weraw[v] = vi < nvec ? __ldg(reinterpret_cast<const uint4*>(a.W_enc + int64_t(j) * a.D) + vi)
+                             : make_uint4(0, 0, 0, 0);
+      }
+    }
 #pragma unroll
     for (int v = 0; v < VPT; ++v) {
       const int vi = t + v * LG_THREADS;
@@ -401,7 +583,7 @@ __global__ void __launch_bounds__(LG_THREADS) latent_grad_kernel(LatentGradArgs 
         for (int q = 0; q < 8; ++q) sq += rd[q] * rd[q] + re[q] * re[q];
         if (a.bterm) {
           float we[8];
-          bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(a.W_enc + int64_t(j) * a.D) + vi), we);
+          bf16x8_to_f32(weraw[v], we);
 #pragma unroll
           for (int q = 0; q < 8; ++q) bt[v][q] += gbe * we[q];
         }
@@ -590,7 +772,7 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
   a.D = int(D);
   if (N == 0) return;
   const int vpt = pick_vpt(D, sparse::LG_THREADS);
-  const int64_t grid = std::min<int64_t>(N, int64_t(sm_count()) * 8);
+  const int64_t grid = std::min<int64_t>(N, int64_t(sm_count()) * 4);
   auto stream = at::cuda::getCurrentCUDAStream();
   switch (vpt) {
     case 1: sparse::latent_grad_kernel<1><<<dim3(grid), dim3(sparse::LG_THREADS), 0, stream>>>(a); break;
@@ -598,6 +780,57 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
     case 4: sparse::latent_grad_kernel<4><<<dim3(grid), dim3(sparse::LG_THREADS), 0, stream>>>(a); break;
     default: sparse::latent_grad_kernel<8><<<dim3(grid), dim3(sparse::LG_THREADS), 0, stream>>>(a); break;
   }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void decode_partial(const torch::Tensor& vals, const torch::Tensor& idx, bool relu,
+                    const c10::optional<torch::Tensor>& inv_scale, const torch::Tensor& W, const torch::Tensor& out) {
+  TORCH_CHECK(vals.is_contiguous() && idx.is_contiguous() && vals.scalar_type() == at::kFloat &&
+                  idx.scalar_type() == at::kInt, "decode_partial: vals/idx");
+  TORCH_CHECK(out.scalar_type() == at::kFloat && out.is_contiguous() && out.size(1) == W.size(1), "decode_partial: out");
+  const int64_t M = vals.size(0), k = vals.size(1), D = W.size(1);
+  TORCH_CHECK(D % 8 == 0 && W.stride(1) == 1, "decode_partial: W");
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(vals.device());
+  const int vpt = pick_vpt(D, sparse::DEC_THREADS);
+  const int64_t grid = std::min<int64_t>(M, int64_t(sm_count()) * 8);
+  const size_t smem = size_t(2 * k) * 4;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const float* pinv = inv_scale ? inv_scale->data_ptr<float>() : nullptr;
+#define SB_DP(V) sparse::decode_partial_kernel<V><<<dim3(grid), dim3(sparse::DEC_THREADS), smem, stream>>>( \
+      vals.data_ptr<float>(), idx.data_ptr<int>(), int(k), vals.stride(0), relu ? 1 : 0, pinv,                  \
+      reinterpret_cast<const __nv_bfloat16*>(W.data_ptr()), W.stride(0), out.data_ptr<float>(), out.stride(0),  \
+      int(M), int(D))
+  switch (vpt) {
+    case 1: SB_DP(1); break;
+    case 2: SB_DP(2); break;
+    case 4: SB_DP(4); break;
+    default: SB_DP(8); break;
+  }
+#undef SB_DP
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void finish_mse(const torch::Tensor& xsum, const c10::optional<torch::Tensor>& bias, const torch::Tensor& target,
+                const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& resid,
+                const c10::optional<torch::Tensor>& dxhat, const c10::optional<torch::Tensor>& grad_coef_dev,
+                double grad_coef, const torch::Tensor& loss_row, const c10::optional<torch::Tensor>& bsum) {
+  TORCH_CHECK(xsum.scalar_type() == at::kFloat && xsum.stride(1) == 1 && xsum.stride(0) % 8 == 0, "finish_mse: xsum");
+  const int64_t M = xsum.size(0), D = xsum.size(1);
+  TORCH_CHECK(target.size(0) == M && target.size(1) == D && target.stride(1) == 1, "finish_mse: target");
+  for (const auto* o : {&out, &resid, &dxhat})
+    if (*o) TORCH_CHECK((*o)->is_contiguous() && (*o)->size(0) == M && (*o)->size(1) == D, "finish_mse: outputs");
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(xsum.device());
+  const int64_t grid = std::min<int64_t>(M, int64_t(sm_count()) * 8);
+  sparse::finish_mse_kernel<<<dim3(grid), dim3(sparse::DEC_THREADS), 0, at::cuda::getCurrentCUDAStream()>>>(
+      xsum.data_ptr<float>(), xsum.stride(0), bias ? bias->data_ptr<float>() : nullptr,
+      reinterpret_cast<const __nv_bfloat16*>(target.data_ptr()), target.stride(0),
+      out ? reinterpret_cast<__nv_bfloat16*>(out->data_ptr()) : nullptr,
+      resid ? reinterpret_cast<__nv_bfloat16*>(resid->data_ptr()) : nullptr,
+      dxhat ? reinterpret_cast<__nv_bfloat16*>(dxhat->data_ptr()) : nullptr,
+      grad_coef_dev ? grad_coef_dev->data_ptr<float>() : nullptr, float(grad_coef), loss_row.data_ptr<float>(),
+      bsum ? bsum->data_ptr<float>() : nullptr, int(M), int(D));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -259,7 +259,95 @@ __global__ void __launch_bounds__(THREADS)
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// Tensor-parallel merge.  Every rank holds the per-row top-k of its own latent shard; after an
+// all-gather of those candidates (cand_* [S, M, k], shard s owning global columns
+// [s*n_local, (s+1)*n_local)), the global top-k of a row is the top-k of its S*k candidates.
+// This kernel computes it for every row and keeps, in this rank's own (vals, idx), only the
+// entries that made the global cut (the others become idx -1).  Ties at the k-th value are
+// broken by the smaller global column index, matching the single-GPU kernel.
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(THREADS)
+    topk_merge_kernel(const float* __restrict__ cand_val, const int* __restrict__ cand_idx, int S, int M,
+                      int k, int64_t n_local, int rank, const int* __restrict__ k_dev,
+                      float* __restrict__ out_val, int* __restrict__ out_idx) {
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t sh[4];
+  extern __shared__ uint8_t dyn[];
+  const int C = S * k;
+  uint32_t* key = reinterpret_cast<uint32_t*>(dyn);
+  int64_t* gidx = reinterpret_cast<int64_t*>(dyn + ((size_t(C) * 4 + 15) & ~size_t(15)));
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  int kk = k;
+  if (k_dev) kk = min(kk, *k_dev);
+  __shared__ int n_valid;
+  if (tid == 0) n_valid = 0;
+  __syncthreads();
+  int nv = 0;
+  for (int c = tid; c < C; c += THREADS) {
+    const int s = c / k, i = c - s * k;
+    const int64_t off = (int64_t(s) * M + row) * k + i;
+    const int li = cand_idx[off];
+    if (li >= 0) {
+      const uint32_t bits = __float_as_uint(cand_val[off]) >> 16;  // values are exact bf16
+      key[c] = bf16_to_key(uint16_t(bits));
+      gidx[c] = int64_t(s) * n_local + li;
+      ++nv;
+    } else {
+      key[c] = 0x10000u;
+      gidx[c] = -1;
+    }
+  }
+  atomicAdd(&n_valid, nv);
+  __syncthreads();
+  kk = min(kk, n_valid);
+  float* vrow = out_val + int64_t(row) * k;
+  int* irow = out_idx + int64_t(row) * k;
+  if (kk <= 0) {
+    for (int i = tid; i < k; i += THREADS) irow[i] = -1;
+    return;
+  }
+  const Sel r = block_select16(C, kk, [&](int i) { return key[i]; }, hist, sh);
+  const int need_ties = kk - r.greater;
+  // decide this rank's own candidates
+  for (int i = tid; i < k; i += THREADS) {
+    const int c = rank * k + i;
+    const uint32_t kc = key[c];
+    bool keep = kc < 0x10000u && kc > r.key;
+    if (!keep && kc == r.key) {
+      const int64_t my = gidx[c];
+      int rk = 0;
+      for (int j = 0; j < C; ++j) rk += (key[j] == r.key && gidx[j] < my) ? 1 : 0;
+      keep = rk < need_ties;
+    }
+    if (!keep) irow[i] = -1;
+    (void)vrow;
+  }
+}
+
 }  // namespace topk
+
+void topk_merge(const torch::Tensor& cand_val, const torch::Tensor& cand_idx, int64_t n_local, int64_t rank,
+                const c10::optional<torch::Tensor>& k_dev, const torch::Tensor& out_val,
+                const torch::Tensor& out_idx) {
+  TORCH_CHECK(cand_val.dim() == 3 && cand_val.sizes() == cand_idx.sizes() && cand_val.is_contiguous() &&
+                  cand_idx.is_contiguous() && cand_val.scalar_type() == at::kFloat &&
+                  cand_idx.scalar_type() == at::kInt,
+              "topk_merge: candidates must be contiguous fp32/int32 [S, M, k]");
+  const int64_t S = cand_val.size(0), M = cand_val.size(1), k = cand_val.size(2);
+  TORCH_CHECK(out_val.size(0) == M && out_val.size(1) == k && out_idx.is_contiguous(), "topk_merge: outputs");
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(cand_val.device());
+  const size_t smem = ((size_t(S * k) * 4 + 15) & ~size_t(15)) + size_t(S * k) * 8;
+  TORCH_CHECK(smem <= 227 * 1024, "topk_merge: S*k too large for one CTA");
+  C10_CUDA_CHECK(cudaFuncSetAttribute(topk::topk_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      int(smem)));
+  topk::topk_merge_kernel<<<dim3(M), dim3(topk::THREADS), smem, at::cuda::getCurrentCUDAStream()>>>(
+      cand_val.data_ptr<float>(), cand_idx.data_ptr<int>(), int(S), int(M), int(k), n_local, int(rank),
+      k_dev ? k_dev->data_ptr<int>() : nullptr, out_val.data_ptr<float>(), out_idx.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 
 // H [M, N] bf16, cmax [M, N/32] bf16 -> (val fp32 [M, k_max], idx int32 [M, k_max]).
 // `k_dev` (int32 scalar on device) optionally lowers k below k_max; `mask` (int32 bit words,

@@ -1,0 +1,229 @@
+"""Latent-sharded tensor-parallel TopK training step on several B200s.
+
+Each of the S ranks owns d_sae/S latents (W_enc^T / W_dec rows, b_enc) plus a replica of b_dec,
+and receives B/S rows of the batch (row-sharded input; `input_layout="replicated"` accepts the
+full batch on every rank instead, as the reference's TP path does).  One step
+(reference semantics: sae_lens/saes/topk_sae.py:615-674 with sae_lens/distributed.py:404-461):
+
+  1. all-gather the input rows                       X [B, d_in]
+  2. local encoder GEMM + per-row top-k of the shard  (k candidates per row and rank)
+  3. all-gather the candidates (S*k per row instead of the reference's B x d_sae all-gather of
+     pre-activations), exact global top-k per row; each rank keeps its own winners
+  4. local sparse decode -> reduce-scatter of the fp32 partial reconstructions to row owners,
+     then b_dec add + MSE + dL/dx_hat on owned rows
+  5. all-gather dL/dx_hat, local latent gradients (CSC)
+  6. one all-reduce of [sum_b dL/dx_hat, sum_j gb_enc W_enc, grad sq-norm, loss] (2*d_in+3
+     floats), then b_dec gradient, clip and Adam exactly as on one GPU
+
+The collectives here are NCCL; `saelens_b200.parallel.fused` provides the peer-memory kernels
+that fuse steps 1-2 and 4 with their compute.
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+import torch
+import torch.distributed as dist
+
+from saelens_b200.parallel.profiling import nccl_nvtx_range
+from saelens_b200.training.engine import EngineStepResult, FusedTopKEngine
+
+
+class TPTopKEngine(FusedTopKEngine):
+    def __init__(self, sae: Any, lr: float, group: dist.ProcessGroup, beta1: float = 0.9, beta2: float = 0.999,
+                 eps: float = 1e-8, max_grad_norm: float = 1.0, input_layout: str = "row_sharded",
+                 h_buffer_bytes: int = 8 << 30):
+        if input_layout not in ("row_sharded", "replicated"):
+            raise ValueError("input_layout must be 'row_sharded' or 'replicated'")
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.size = dist.get_world_size(group)
+        self.input_layout = input_layout
+        super().__init__(sae, lr=lr, beta1=beta1, beta2=beta2, eps=eps, max_grad_norm=max_grad_norm,
+                         h_buffer_bytes=h_buffer_bytes)
+        self.n_local = self.N
+        self.collectives = 0
+
+    # ------------------------------------------------------------------ helpers
+    def _ag(self, out: torch.Tensor, inp: torch.Tensor, name: str) -> None:
+        with nccl_nvtx_range(f"nccl:tp_{name}_all_gather", self.group):
+            dist.all_gather_into_tensor(out, inp.contiguous(), group=self.group)
+        self.collectives += 1
+
+    def _local_rows(self, x: torch.Tensor) -> torch.Tensor:
+        if self.input_layout == "replicated":
+            B = x.shape[0]
+            if B % self.size:
+                raise ValueError(f"batch {B} not divisible by tp size {self.size}")
+            b = B // self.size
+            return x[self.rank * b : (self.rank + 1) * b]
+        return x
+
+    def _global_topk(self, vals: torch.Tensor, idx: torch.Tensor, k: int, k_dev: torch.Tensor | None) -> None:
+        """Keep in (vals, idx) only this rank's entries of the global per-row top-k."""
+        B = vals.shape[0]
+        cv = torch.empty(self.size * B, k, dtype=torch.float32, device=self.device)
+        ci = torch.empty(self.size * B, k, dtype=torch.int32, device=self.device)
+        self._ag(cv, vals, "topk_candidates")
+        self._ag(ci, idx, "topk_candidate_idx")
+        self.native.topk_merge(cv.view(self.size, B, k), ci.view(self.size, B, k), self.n_local, self.rank,
+                               k_dev, vals, idx)
+        self.launches += 1
+
+    # ------------------------------------------------------------------ the step
+    @torch.no_grad()
+    def step(self, x: torch.Tensor, lr: float | None = None, dead_mask: torch.Tensor | None = None,
+             want_sae_out: bool = False, act_freq: torch.Tensor | None = None,
+             since_fired: torch.Tensor | None = None, run_aux: bool = False,
+             update: bool = True) -> EngineStepResult:
+        nat, dev = self.native, self.device
+        D, N, k, S = self.D, self.N, self.k, self.size
+        x_own = self._local_rows(x)
+        xb_own = x_own if (x_own.dtype == torch.bfloat16 and x_own.is_contiguous()) else \
+            x_own.to(torch.bfloat16).contiguous()
+        Bo = xb_own.shape[0]
+        B = Bo * S
+        self._mark("start")
+        # 1. input rows of every rank
+        if self.input_layout == "replicated" and x.dtype == torch.bfloat16 and x.is_contiguous():
+            X = x
+        else:
+            X = torch.empty(B, D, dtype=torch.bfloat16, device=dev)
+            self._ag(X, xb_own, "input_rows")
+        self._mark("input_all_gather")
+
+        # aux decision must be identical on every rank: reduce the dead count
+        aux_on = False
+        if run_aux and dead_mask is not None:
+            nd = dead_mask.to(torch.bool).sum().to(torch.float32).reshape(1)
+            with nccl_nvtx_range("nccl:tp_dead_count_all_reduce", self.group):
+                dist.all_reduce(nd, group=self.group)
+            self.collectives += 1
+            num_dead_total = int(nd.item())
+            aux_on = num_dead_total > 0
+        k_aux = D // 2
+
+        # 2. local encoder + local top-k
+        R = self._row_chunk(B)
+        H = torch.empty(min(R, B), N, dtype=torch.bfloat16, device=dev)
+        cm = torch.empty(min(R, B), N // 32, dtype=torch.bfloat16, device=dev)
+        vals = torch.empty(B, k, dtype=torch.float32, device=dev)
+        idx = torch.empty(B, k, dtype=torch.int32, device=dev)
+        if aux_on:
+            assert dead_mask is not None
+            dm = dead_mask.to(torch.bool)
+            k_aux_total = min(k_aux, num_dead_total)
+            k_aux_dev = torch.tensor([k_aux_total], dtype=torch.int32, device=dev)
+            aux_scale = min(num_dead_total / k_aux, 1.0)
+            bits = dm.view(N // 32, 32).to(torch.int64) << torch.arange(32, device=dev, dtype=torch.int64)
+            w = bits.sum(1)
+            mask_words = torch.where(w >= 2**31, w - 2**32, w).to(torch.int32).contiguous()
+            local_dead = min(int(dm.sum().item()), k_aux_total)
+            aux_vals = torch.empty(B, k_aux, dtype=torch.float32, device=dev)
+            aux_idx = torch.empty(B, k_aux, dtype=torch.int32, device=dev)
+            k_loc_dev = torch.tensor([local_dead], dtype=torch.int32, device=dev)
+        for r0 in range(0, B, R):
+            r1 = min(B, r0 + R)
+            h, c = H[: r1 - r0], cm[: r1 - r0]
+            nat.gemm_tn_bf16(X[r0:r1], self.w_enc, self.bias_eff, self.scale if self.rescale else None, False,
+                             h, c, self.status.tensor, 0)
+            self._mark("encoder_gemm")
+            nat.row_topk(h, c, k, None, None, vals[r0:r1], idx[r0:r1], self.status.tensor)
+            self._mark("row_topk")
+            self.launches += 2
+            if aux_on:
+                nat.row_topk(h, c, k_aux, k_loc_dev, mask_words, aux_vals[r0:r1], aux_idx[r0:r1], self.status.tensor)
+                self.launches += 1
+        del H, cm
+
+        # 3. global top-k from the shards' candidates
+        self._global_topk(vals, idx, k, None)
+        if aux_on:
+            self._global_topk(aux_vals, aux_idx, k_aux, k_aux_dev)
+        self._mark("topk_exchange")
+
+        # 4. partial decode -> reduce-scatter -> b_dec + MSE on owned rows
+        part = torch.empty(B, D, dtype=torch.float32, device=dev)
+        nat.decode_partial(vals, idx, True, self.inv_scale if self.rescale else None, self.w_dec, part)
+        xsum = torch.empty(Bo, D, dtype=torch.float32, device=dev)
+        with nccl_nvtx_range("nccl:tp_decode_reduce_scatter", self.group):
+            dist.reduce_scatter_tensor(xsum, part, group=self.group)
+        self.collectives += 1
+        sae_out = torch.empty(Bo, D, dtype=torch.bfloat16, device=dev) if (want_sae_out or aux_on) else None
+        resid = torch.empty(Bo, D, dtype=torch.bfloat16, device=dev) if aux_on else None
+        dx_own = torch.empty(Bo, D, dtype=torch.bfloat16, device=dev)
+        loss_row = torch.empty(Bo, dtype=torch.float32, device=dev)
+        red = torch.zeros(2 * D + 3, dtype=torch.float32, device=dev)  # [bsum | bterm | sumsq | mse | aux]
+        bsum, bterm = red[:D], red[D : 2 * D]
+        nat.finish_mse(xsum, self.p_bdec, xb_own, sae_out, resid, dx_own, None, 2.0 / B, loss_row, bsum)
+        self.launches += 2
+        self._mark("decode_reduce_scatter_mse")
+        dX = torch.empty(B, D, dtype=torch.bfloat16, device=dev)
+        self._ag(dX, dx_own, "dxhat")
+
+        daux = None
+        if aux_on:
+            assert resid is not None
+            part.zero_()
+            nat.decode_partial(aux_vals, aux_idx, False, self.inv_scale if self.rescale else None, self.w_dec, part)
+            asum = torch.empty(Bo, D, dtype=torch.float32, device=dev)
+            with nccl_nvtx_range("nccl:tp_aux_decode_reduce_scatter", self.group):
+                dist.reduce_scatter_tensor(asum, part, group=self.group)
+            self.collectives += 1
+            da_own = torch.empty(Bo, D, dtype=torch.bfloat16, device=dev)
+            aux_row = torch.empty(Bo, dtype=torch.float32, device=dev)
+            nat.finish_mse(asum, None, resid, None, None, da_own, None, 2.0 * self.aux_coef * aux_scale / B,
+                           aux_row, None)
+            self.launches += 2
+            red[2 * D + 2] = aux_row.sum()
+            daux = torch.empty(B, D, dtype=torch.bfloat16, device=dev)
+            self._ag(daux, da_own, "aux_grad")
+        del part
+
+        # 5. CSC + local latent gradients
+        self.counts.zero_()
+        self.fire_counts.zero_()
+        self.cursor.zero_()
+        nat.csc_count(vals, idx, aux_vals if aux_on else None, aux_idx if aux_on else None, self.counts,
+                      self.fire_counts)
+        torch.cumsum(self.counts, 0, out=self.colptr[1:])
+        pairs = torch.empty(B * k + (B * k_aux if aux_on else 0), dtype=torch.int64, device=dev)
+        nat.csc_fill(vals, idx, aux_vals if aux_on else None, aux_idx if aux_on else None, self.colptr,
+                     self.cursor, pairs)
+        self._mark("csc_build")
+        sumsq = red[2 * D : 2 * D + 1]
+        nat.latent_grad(self.colptr, pairs, vals, aux_vals if aux_on else None,
+                        self.inv_scale if self.rescale else None, dX, daux, X,
+                        self.p_bdec if self.apply_b_dec else None, self.w_dec, self.w_enc, self.g_dec, self.g_enc,
+                        self.g_benc, bterm if self.apply_b_dec else None, sumsq, self.fire_counts, act_freq,
+                        since_fired)
+        self.launches += 3
+        self._mark("latent_grad")
+
+        # 6. one all-reduce for b_dec grad terms, grad norm and losses
+        red[2 * D + 1] = loss_row.sum()
+        with nccl_nvtx_range("nccl:tp_grad_terms_all_reduce", self.group):
+            dist.all_reduce(red, group=self.group)
+        self.collectives += 1
+        self._mark("grad_all_reduce")
+        mse = red[2 * D + 1] / B
+        aux_loss = (self.aux_coef * aux_scale * red[2 * D + 2] / B) if aux_on else torch.zeros((), device=dev)
+        if update:
+            self.step_count += 1
+            cur_lr = self.lr if lr is None else lr
+            sq = red[2 * D : 2 * D + 1]
+            nat.adam_bdec(bsum, bterm if self.apply_b_dec else None, self.g_bdec, sq, self.clip, self.p_bdec,
+                          self.m_bdec, self.v_bdec, cur_lr, self.beta1, self.beta2, self.eps, self.step_count,
+                          self.max_grad_norm, True)
+            nat.adam_rows(self.p_dec, self.m_dec, self.v_dec, self.p_enc, self.m_enc, self.v_enc, self.w_dec,
+                          self.w_enc, self.g_dec, self.g_enc, self.p_benc, self.m_benc, self.v_benc, self.g_benc,
+                          self.colptr, self.clip, self.p_bdec if self.apply_b_dec else None, self.scale,
+                          self.inv_scale, self.bias_eff, cur_lr, self.beta1, self.beta2, self.eps, self.step_count,
+                          True)
+            self.launches += 2
+            self.sumsq = sq
+            self._mark("adam")
+        self.last_loss = mse + aux_loss
+        return EngineStepResult(loss=mse + aux_loss, mse_loss=mse, aux_loss=aux_loss, sae_out=sae_out,
+                                topk_vals=vals, topk_idx=idx, fire_counts=self.fire_counts)

@@ -157,7 +157,6 @@ def run_e2e(s: BenchSetup, steps: int, warmup: int) -> dict[str, Any]:
     local = BenchSetup(**{**s.__dict__, "batch": rows_local})
     sae = _materialise_local(_build_sae(s), s)
     if s.world > 1:
-        sae.shard_info = (dist.group.WORLD,)
         sae._tp_group = dist.group.WORLD
     cfg = SAETrainerConfig(
         n_checkpoints=0, checkpoint_path=None, save_final_checkpoint=False, output_path=None,
@@ -170,7 +169,7 @@ def run_e2e(s: BenchSetup, steps: int, warmup: int) -> dict[str, Any]:
         feature_sampling_window=2000, logger=LoggingConfig(log_to_wandb=False), sae_engine="native",
     )
     data = PinnedBatches(local)
-    trainer = SAETrainer(cfg, sae, data)
+    trainer = SAETrainer(cfg, sae, data, tp_input_layout="row_sharded")
     trainer.fit_steps(warmup)
     torch.cuda.synchronize()
     _barrier(s.world)

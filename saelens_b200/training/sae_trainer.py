@@ -87,8 +87,12 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
     def __init__(self, cfg: SAETrainerConfig, sae: Any, data_provider: DataProvider,
                  evaluator: Evaluator | None = None, save_checkpoint_fn: SaveCheckpointFn | None = None,
                  dp_group: dist.ProcessGroup | None = None, token_count_weighted_dp: bool = False,
-                 base_sae: Any = None, append_logs: bool = False) -> None:
+                 base_sae: Any = None, append_logs: bool = False,
+                 tp_input_layout: str = "replicated") -> None:
         self.sae = sae
+        # "replicated": every TP rank receives the same full batch (reference semantics);
+        # "row_sharded": each TP rank receives its 1/tp slice of the batch rows.
+        self.tp_input_layout = tp_input_layout
         self._base_sae = base_sae if base_sae is not None else sae
         self._is_fsdp = _is_fsdp(sae)
         self._is_ddp = _is_ddp(sae)
@@ -146,7 +150,13 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
         if want != "torch" and not (self._is_ddp or self._is_fsdp) and dp_group is None:
             from saelens_b200.training.engine import FusedTopKEngine, engine_supported
 
-            if engine_supported(self._base_sae):
+            tp_group = getattr(self._base_sae, "_tp_group", None)
+            if engine_supported(self._base_sae) and tp_group is not None:
+                from saelens_b200.parallel.tp_engine import TPTopKEngine
+
+                self.engine = TPTopKEngine(self._base_sae, lr=cfg.lr, group=tp_group, beta1=cfg.adam_beta1,
+                                           beta2=cfg.adam_beta2, input_layout=tp_input_layout)
+            elif engine_supported(self._base_sae):
                 self.engine = FusedTopKEngine(self._base_sae, lr=cfg.lr, beta1=cfg.adam_beta1,
                                               beta2=cfg.adam_beta2)
             elif want == "native":
@@ -250,7 +260,10 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
             return None
         self._maybe_sync()
         timing = self._consume_data_provider_timing()
-        self.n_training_samples += batch.shape[0]
+        rows = batch.shape[0]
+        if self.engine is not None and getattr(self.engine, "input_layout", "") == "row_sharded":
+            rows *= self.engine.size
+        self.n_training_samples += rows
         scaled = self.activation_scaler(batch)
         self._maybe_sync()
         t0 = time.perf_counter()

@@ -80,7 +80,7 @@ def test_engine_adam_step_matches_torch_adam():
     _, _, grads = _oracle(w_enc0, w_dec0, b_enc0, b_dec0, xb, res.topk_idx, eng.k)
     # torch reference: clip_grad_norm_(1.0) then one Adam step from the same fp32 masters
     params = {"W_enc": p_enc0.T.clone(), "W_dec": p_dec0.clone(), "b_enc": b_enc0.clone(), "b_dec": b_dec0.clone()}
-    ps = [torch.nn.Parameter(v) for v in params.values()]
+    ps = [torch.nn.Parameter(v.clone()) for v in params.values()]
     for p, name in zip(ps, params):
         p.grad = grads[name].float().clone()
     total = torch.nn.utils.clip_grad_norm_(ps, 1.0)

@@ -1,0 +1,79 @@
+"""Tensor-parallel native step (2 ranks over NCCL) against the single-GPU native step."""
+
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _build(d_in, d_sae, k, device):
+    from saelens_b200.models.topk import TopKTrainingSAE, TopKTrainingSAEConfig
+
+    torch.manual_seed(7)
+    sae = TopKTrainingSAE(TopKTrainingSAEConfig(d_in=d_in, d_sae=d_sae, k=k, device=device))
+    with torch.no_grad():
+        sae.b_enc.normal_(0, 0.01)
+        sae.b_dec.normal_(0, 0.05)
+    return sae
+
+
+def _worker(rank, world, port, d_in, d_sae, k, B, out_dir):
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    from saelens_b200.parallel.tp_engine import TPTopKEngine
+
+    sae = _build(d_in, d_sae, k, f"cuda:{rank}")
+    sae.shard_weights(dist.group.WORLD)
+    eng = TPTopKEngine(sae, lr=1e-3, group=dist.group.WORLD)
+    g = torch.Generator(device="cpu").manual_seed(11)
+    x = torch.randn(B, d_in, generator=g).to(torch.bfloat16)
+    rows = x[rank * (B // world) : (rank + 1) * (B // world)].cuda()
+    losses = []
+    for _ in range(3):
+        losses.append(float(eng.step(rows).loss))
+    torch.cuda.synchronize()
+    eng.status.check()
+    torch.save({"losses": losses, "p_dec": eng.p_dec.cpu(), "p_enc": eng.p_enc.cpu(), "p_bdec": eng.p_bdec.cpu()},
+               os.path.join(out_dir, f"rank{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_matches_single_gpu(tmp_path):
+    import torch.multiprocessing as mp
+
+    from saelens_b200.training.engine import FusedTopKEngine
+
+    d_in, d_sae, k, B = 256, 2048, 32, 512
+    mp.spawn(_worker, args=(2, _free_port(), d_in, d_sae, k, B, str(tmp_path)), nprocs=2, join=True)
+    sae = _build(d_in, d_sae, k, "cuda:0")
+    eng = FusedTopKEngine(sae, lr=1e-3)
+    g = torch.Generator(device="cpu").manual_seed(11)
+    x = torch.randn(B, d_in, generator=g).to(torch.bfloat16).cuda()
+    ref_losses = [float(eng.step(x).loss) for _ in range(3)]
+    r = [torch.load(tmp_path / f"rank{i}.pt") for i in range(2)]
+    for a, b in zip(r[0]["losses"], ref_losses):
+        assert abs(a - b) <= 1e-3 * abs(b), (r[0]["losses"], ref_losses)
+    assert r[0]["losses"] == r[1]["losses"]
+    n = d_sae // 2
+    for i in range(2):
+        assert torch.allclose(r[i]["p_dec"], eng.p_dec[i * n : (i + 1) * n].cpu(), atol=2e-5, rtol=1e-3)
+        assert torch.allclose(r[i]["p_enc"], eng.p_enc[i * n : (i + 1) * n].cpu(), atol=2e-5, rtol=1e-3)
+        assert torch.allclose(r[i]["p_bdec"], eng.p_bdec.cpu(), atol=2e-5, rtol=1e-3)
