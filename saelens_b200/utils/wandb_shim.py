@@ -17,6 +17,11 @@ except Exception:  # noqa: BLE001
 AVAILABLE = _wandb is not None
 
 
+def _live() -> bool:
+    """True when a real wandb run is active; otherwise calls go to the offline JSONL log."""
+    return _wandb is not None and getattr(_wandb, "run", None) is not None
+
+
 def _log_path() -> str:
     d = os.environ.get("SAELENS_B200_WANDB_DIR", "wandb_offline")
     os.makedirs(d, exist_ok=True)
@@ -43,6 +48,8 @@ class Histogram:
     def __init__(self, values: Any):
         import numpy as np
 
+        self._values = values
+
         arr = np.asarray(values, dtype=float)
         self.summary = {"n": int(arr.size), "mean": float(arr.mean()) if arr.size else 0.0,
                         "min": float(arr.min()) if arr.size else 0.0, "max": float(arr.max()) if arr.size else 0.0}
@@ -65,7 +72,7 @@ def init(**kwargs: Any) -> Any:
 
 
 def log(data: dict[str, Any], step: int | None = None) -> None:
-    if _wandb is not None:
+    if _live():
         _wandb.log(data, step=step)
         return
     with open(_log_path(), "a") as f:
@@ -73,7 +80,7 @@ def log(data: dict[str, Any], step: int | None = None) -> None:
 
 
 def log_artifact(art: Artifact, aliases: list[str] | None = None) -> None:
-    if _wandb is not None:
+    if _live():
         a = _wandb.Artifact(art.name, type=art.type, metadata=art.metadata)
         for p in art.files:
             a.add_file(p)
@@ -85,5 +92,5 @@ def log_artifact(art: Artifact, aliases: list[str] | None = None) -> None:
 
 
 def finish() -> None:
-    if _wandb is not None:
+    if _live():
         _wandb.finish()
