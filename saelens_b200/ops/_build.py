@@ -25,6 +25,7 @@ SOURCES = [
     "topk.cu",
     "sparse.cu",
     "adam.cu",
+    "noalloc_csc.cu",
 ]
 
 NVCC_FLAGS = [
