@@ -1,0 +1,433 @@
+"""Activation-producing language models with TransformerLens-style hook names.
+
+One decoder-only implementation covers the producer families the reference drives (GPT-2
+through TransformerLens; Llama / Mistral / Gemma-2 / Qwen2 through its vLLM fork, whose hook map
+is sae_lens/vllm_model.py:235-364): learned or rotary positions, LayerNorm or RMSNorm, GELU or
+gated (SwiGLU / GeGLU) MLPs, grouped-query attention with optional q/k/v bias, Gemma-2's
+embedding scale, sandwich norms and logit soft-capping.
+
+Hooks (per block i): `hook_resid_pre`, `ln1.hook_normalized`, `attn.hook_q/k/v` (before RoPE),
+`attn.hook_z` (per-head attention output), `hook_attn_out`, `hook_resid_mid`, `ln2.hook_normalized`,
+`mlp.hook_pre` (gate branch before the activation), `mlp.hook_post`, `hook_mlp_out`,
+`hook_resid_post`; plus `hook_embed`, `hook_pos_embed`, `ln_final.hook_normalized`.
+`run_with_cache(tokens, names_filter, stop_at_layer=n)` runs only blocks [0, n), which is how the
+SAE data pipeline stops right after the hooked layer.
+
+On CUDA with bf16 weights, the q/k/v, output and MLP projections run on this package's tcgen05
+GEMM (`saelens_b200.ops.gemm_tn`); attention uses `scaled_dot_product_attention`.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import asdict, dataclass, field
+from typing import Any
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from saelens_b200.utils.hooks import HookedRootModule, HookPoint
+
+
+@dataclass
+class LMConfig:
+    n_layers: int
+    d_model: int
+    n_heads: int
+    d_mlp: int
+    d_vocab: int
+    n_ctx: int
+    d_head: int | None = None
+    n_key_value_heads: int | None = None
+    architecture: str = "llama"          # gpt2 | llama | gemma2 | qwen2 | mistral
+    normalization: str = "RMS"            # LN | RMS
+    positional: str = "rotary"            # standard | rotary
+    act_fn: str = "silu"                  # gelu | gelu_new | gelu_pytorch_tanh | silu
+    gated_mlp: bool = True
+    qkv_bias: bool = False
+    attn_out_bias: bool = False
+    mlp_bias: bool = False
+    rotary_base: float = 10000.0
+    eps: float = 1e-5
+    tie_embeddings: bool = False
+    embed_scale: bool = False              # Gemma: embeddings * sqrt(d_model)
+    sandwich_norm: bool = False            # Gemma-2: post-attention / post-MLP norms
+    rms_one_plus: bool = False             # Gemma: weight applied as (1 + w)
+    attn_softcap: float | None = None
+    final_softcap: float | None = None
+    query_pre_attn_scalar: float | None = None
+    model_name: str = "custom"
+    dtype: str = "bfloat16"
+    init_std: float = 0.02
+
+    def __post_init__(self) -> None:
+        if self.d_head is None:
+            self.d_head = self.d_model // self.n_heads
+        if self.n_key_value_heads is None:
+            self.n_key_value_heads = self.n_heads
+        if self.n_heads % self.n_key_value_heads:
+            raise ValueError("n_heads must be a multiple of n_key_value_heads")
+
+    def to_dict(self) -> dict[str, Any]:
+        return asdict(self)
+
+
+def _preset(**kw: Any) -> LMConfig:
+    return LMConfig(**kw)
+
+
+PRESETS: dict[str, dict[str, Any]] = {
+    # GPT-2 small
+    "gpt2": dict(n_layers=12, d_model=768, n_heads=12, d_mlp=3072, d_vocab=50257, n_ctx=1024, architecture="gpt2",
+                 normalization="LN", positional="standard", act_fn="gelu_new", gated_mlp=False, qkv_bias=True,
+                 attn_out_bias=True, mlp_bias=True, tie_embeddings=True, model_name="gpt2"),
+    "tiny-stories-1M": dict(n_layers=8, d_model=64, n_heads=16, d_mlp=256, d_vocab=50257, n_ctx=2048,
+                            architecture="gpt2", normalization="LN", positional="standard", act_fn="gelu_new",
+                            gated_mlp=False, qkv_bias=True, attn_out_bias=True, mlp_bias=True,
+                            model_name="tiny-stories-1M"),
+    "gelu-2l": dict(n_layers=2, d_model=512, n_heads=8, d_mlp=2048, d_vocab=48262, n_ctx=1024, architecture="gpt2",
+                    normalization="LN", positional="standard", act_fn="gelu", gated_mlp=False, qkv_bias=True,
+                    attn_out_bias=True, mlp_bias=True, model_name="gelu-2l"),
+    # Llama-3-8B
+    "meta-llama/Meta-Llama-3-8B": dict(n_layers=32, d_model=4096, n_heads=32, n_key_value_heads=8, d_mlp=14336,
+                                       d_vocab=128256, n_ctx=8192, rotary_base=500000.0,
+                                       model_name="meta-llama/Meta-Llama-3-8B"),
+    "meta-llama/Llama-3.1-8B": dict(n_layers=32, d_model=4096, n_heads=32, n_key_value_heads=8, d_mlp=14336,
+                                    d_vocab=128256, n_ctx=8192, rotary_base=500000.0,
+                                    model_name="meta-llama/Llama-3.1-8B"),
+    # Gemma-2-9B
+    "google/gemma-2-9b": dict(n_layers=42, d_model=3584, n_heads=16, n_key_value_heads=8, d_head=256, d_mlp=14336,
+                              d_vocab=256000, n_ctx=8192, architecture="gemma2", act_fn="gelu_pytorch_tanh",
+                              embed_scale=True, sandwich_norm=True, rms_one_plus=True, eps=1e-6,
+                              attn_softcap=50.0, final_softcap=30.0, query_pre_attn_scalar=256.0,
+                              tie_embeddings=True, model_name="google/gemma-2-9b"),
+    # Qwen-14B (Qwen1.5 / Qwen2 layout)
+    "Qwen/Qwen1.5-14B": dict(n_layers=40, d_model=5120, n_heads=40, d_mlp=13696, d_vocab=152064, n_ctx=8192,
+                             architecture="qwen2", qkv_bias=True, rotary_base=1000000.0, eps=1e-6,
+                             model_name="Qwen/Qwen1.5-14B"),
+    "Qwen/Qwen2.5-14B": dict(n_layers=48, d_model=5120, n_heads=40, n_key_value_heads=8, d_mlp=13824,
+                             d_vocab=152064, n_ctx=8192, architecture="qwen2", qkv_bias=True,
+                             rotary_base=1000000.0, eps=1e-6, model_name="Qwen/Qwen2.5-14B"),
+}
+PRESETS["gpt2-small"] = PRESETS["gpt2"]
+PRESETS["llama-3-8b"] = PRESETS["meta-llama/Meta-Llama-3-8B"]
+PRESETS["gemma-2-9b"] = PRESETS["google/gemma-2-9b"]
+PRESETS["qwen-14b"] = PRESETS["Qwen/Qwen2.5-14B"]
+
+
+def preset_config(name: str, **overrides: Any) -> LMConfig:
+    if name not in PRESETS:
+        raise KeyError(f"unknown model preset {name!r}; known: {sorted(PRESETS)}")
+    return LMConfig(**{**PRESETS[name], **overrides})
+
+
+# ------------------------------------------------------------------------------ layers
+class NativeLinear(nn.Module):
+    """y = x W^T + b with W [out, in]; the tcgen05 GEMM on CUDA bf16 when the shape allows."""
+
+    def __init__(self, d_in: int, d_out: int, bias: bool, dtype: torch.dtype, device: Any = None):
+        super().__init__()
+        self.weight = nn.Parameter(torch.empty(d_out, d_in, dtype=dtype, device=device))
+        self.bias = nn.Parameter(torch.zeros(d_out, dtype=dtype, device=device)) if bias else None
+        self._native_ok = d_out % 256 == 0 and d_in % 64 == 0
+        self._bias_f32: torch.Tensor | None = None
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        w = self.weight
+        if (self._native_ok and x.is_cuda and w.dtype == torch.bfloat16 and x.dtype == torch.bfloat16
+                and not torch.is_grad_enabled()):
+            from saelens_b200 import ops
+
+            if ops.available():
+                shp = x.shape
+                x2 = x.reshape(-1, shp[-1])
+                if not x2.is_contiguous():
+                    x2 = x2.contiguous()
+                b = None
+                if self.bias is not None:
+                    if self._bias_f32 is None or self._bias_f32.device != w.device:
+                        self._bias_f32 = self.bias.detach().float().contiguous()
+                    b = self._bias_f32
+                out, _ = ops.gemm_tn(x2, w, bias=b)
+                return out.view(*shp[:-1], w.shape[0])
+        return F.linear(x, w, self.bias)
+
+    def _load_from_state_dict(self, *args: Any, **kwargs: Any) -> None:
+        self._bias_f32 = None
+        super()._load_from_state_dict(*args, **kwargs)
+
+
+class Norm(nn.Module):
+    def __init__(self, cfg: LMConfig, dtype: torch.dtype):
+        super().__init__()
+        self.rms = cfg.normalization == "RMS"
+        self.eps = cfg.eps
+        self.one_plus = cfg.rms_one_plus
+        self.w = nn.Parameter(torch.zeros(cfg.d_model, dtype=dtype) if self.one_plus else torch.ones(cfg.d_model, dtype=dtype))
+        self.b = None if self.rms else nn.Parameter(torch.zeros(cfg.d_model, dtype=dtype))
+        self.hook_normalized = HookPoint()
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        xf = x.float()
+        if self.rms:
+            y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
+            w = (1.0 + self.w.float()) if self.one_plus else self.w.float()
+            y = y * w
+        else:
+            y = F.layer_norm(xf, (xf.shape[-1],), self.w.float(), self.b.float() if self.b is not None else None, self.eps)
+        return self.hook_normalized(y.to(x.dtype))
+
+
+def _act(name: str, x: torch.Tensor) -> torch.Tensor:
+    if name == "silu":
+        return F.silu(x)
+    if name in ("gelu_new", "gelu_pytorch_tanh"):
+        return F.gelu(x, approximate="tanh")
+    if name == "gelu":
+        return F.gelu(x)
+    if name == "relu":
+        return F.relu(x)
+    raise ValueError(f"unknown activation {name}")
+
+
+def rotary_tables(n_pos: int, d: int, base: float, device: Any, dtype: torch.dtype = torch.float32):
+    inv = 1.0 / (base ** (torch.arange(0, d, 2, device=device, dtype=torch.float32) / d))
+    t = torch.arange(n_pos, device=device, dtype=torch.float32)
+    f = torch.outer(t, inv)
+    return torch.cos(f).to(dtype), torch.sin(f).to(dtype)
+
+
+def apply_rotary(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """x [B, S, H, d]; rotate-half convention (first half paired with second half)."""
+    d2 = x.shape[-1] // 2
+    x1, x2 = x[..., :d2].float(), x[..., d2:].float()
+    c = cos[None, :, None, :]
+    s = sin[None, :, None, :]
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1).to(x.dtype)
+
+
+class Attention(nn.Module):
+    def __init__(self, cfg: LMConfig, dtype: torch.dtype):
+        super().__init__()
+        self.cfg = cfg
+        H, KV, dh = cfg.n_heads, cfg.n_key_value_heads, cfg.d_head
+        assert dh is not None and KV is not None
+        self.q = NativeLinear(cfg.d_model, H * dh, cfg.qkv_bias, dtype)
+        self.k = NativeLinear(cfg.d_model, KV * dh, cfg.qkv_bias, dtype)
+        self.v = NativeLinear(cfg.d_model, KV * dh, cfg.qkv_bias, dtype)
+        self.o = NativeLinear(H * dh, cfg.d_model, cfg.attn_out_bias, dtype)
+        self.hook_q, self.hook_k, self.hook_v = HookPoint(), HookPoint(), HookPoint()
+        self.hook_z = HookPoint()
+        self.hook_rot_q, self.hook_rot_k = HookPoint(), HookPoint()
+        self.scale = 1.0 / math.sqrt(cfg.query_pre_attn_scalar if cfg.query_pre_attn_scalar else dh)
+
+    def forward(self, x: torch.Tensor, rot: tuple[torch.Tensor, torch.Tensor] | None) -> torch.Tensor:
+        B, S, _ = x.shape
+        H, KV, dh = self.cfg.n_heads, self.cfg.n_key_value_heads, self.cfg.d_head
+        q = self.hook_q(self.q(x).view(B, S, H, dh))
+        k = self.hook_k(self.k(x).view(B, S, KV, dh))
+        v = self.hook_v(self.v(x).view(B, S, KV, dh))
+        if rot is not None:
+            q = self.hook_rot_q(apply_rotary(q, *rot))
+            k = self.hook_rot_k(apply_rotary(k, *rot))
+        qh, kh, vh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+        if KV != H:
+            rep = H // KV
+            kh = kh.repeat_interleave(rep, dim=1)
+            vh = vh.repeat_interleave(rep, dim=1)
+        if self.cfg.attn_softcap:
+            sc = (qh.float() @ kh.float().transpose(-1, -2)) * self.scale
+            sc = self.cfg.attn_softcap * torch.tanh(sc / self.cfg.attn_softcap)
+            mask = torch.ones(S, S, dtype=torch.bool, device=x.device).tril()
+            sc = sc.masked_fill(~mask, float("-inf"))
+            z = (torch.softmax(sc, dim=-1) @ vh.float()).to(x.dtype)
+        else:
+            z = F.scaled_dot_product_attention(qh, kh, vh, is_causal=True, scale=self.scale)
+        z = self.hook_z(z.transpose(1, 2))  # [B, S, H, dh]
+        return self.o(z.reshape(B, S, H * dh))
+
+
+class MLP(nn.Module):
+    def __init__(self, cfg: LMConfig, dtype: torch.dtype):
+        super().__init__()
+        self.cfg = cfg
+        self.gated = cfg.gated_mlp
+        if self.gated:
+            self.gate = NativeLinear(cfg.d_model, cfg.d_mlp, cfg.mlp_bias, dtype)
+        self.up = NativeLinear(cfg.d_model, cfg.d_mlp, cfg.mlp_bias, dtype)
+        self.down = NativeLinear(cfg.d_mlp, cfg.d_model, cfg.mlp_bias, dtype)
+        self.hook_pre = HookPoint()
+        self.hook_post = HookPoint()
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.gated:
+            pre = self.hook_pre(self.gate(x))
+            post = self.hook_post(_act(self.cfg.act_fn, pre) * self.up(x))
+        else:
+            pre = self.hook_pre(self.up(x))
+            post = self.hook_post(_act(self.cfg.act_fn, pre))
+        return self.down(post)
+
+
+class Block(nn.Module):
+    def __init__(self, cfg: LMConfig, dtype: torch.dtype):
+        super().__init__()
+        self.cfg = cfg
+        self.ln1 = Norm(cfg, dtype)
+        self.attn = Attention(cfg, dtype)
+        self.ln2 = Norm(cfg, dtype)
+        self.mlp = MLP(cfg, dtype)
+        if cfg.sandwich_norm:
+            self.ln1_post = Norm(cfg, dtype)
+            self.ln2_post = Norm(cfg, dtype)
+        self.hook_resid_pre = HookPoint()
+        self.hook_attn_out = HookPoint()
+        self.hook_resid_mid = HookPoint()
+        self.hook_mlp_out = HookPoint()
+        self.hook_resid_post = HookPoint()
+
+    def forward(self, x: torch.Tensor, rot: tuple[torch.Tensor, torch.Tensor] | None) -> torch.Tensor:
+        x = self.hook_resid_pre(x)
+        a = self.attn(self.ln1(x), rot)
+        if self.cfg.sandwich_norm:
+            a = self.ln1_post(a)
+        a = self.hook_attn_out(a)
+        x = self.hook_resid_mid(x + a)
+        m = self.mlp(self.ln2(x))
+        if self.cfg.sandwich_norm:
+            m = self.ln2_post(m)
+        m = self.hook_mlp_out(m)
+        return self.hook_resid_post(x + m)
+
+
+class HookedLM(HookedRootModule):
+    """Decoder-only LM whose activations can be cached or edited by hook name."""
+
+    def __init__(self, cfg: LMConfig, device: Any = None, init: bool = True, tokenizer: Any = None):
+        super().__init__()
+        self.cfg = cfg
+        dtype = getattr(torch, cfg.dtype)
+        self.embed = nn.Embedding(cfg.d_vocab, cfg.d_model, dtype=dtype)
+        self.hook_embed = HookPoint()
+        if cfg.positional == "standard":
+            self.pos_embed = nn.Embedding(cfg.n_ctx, cfg.d_model, dtype=dtype)
+            self.hook_pos_embed = HookPoint()
+        self.blocks = nn.ModuleList([Block(cfg, dtype) for _ in range(cfg.n_layers)])
+        self.ln_final = Norm(cfg, dtype)
+        self.unembed = None if cfg.tie_embeddings else NativeLinear(cfg.d_model, cfg.d_vocab, False, dtype)
+        self.tokenizer = tokenizer
+        self._rot: tuple[torch.Tensor, torch.Tensor] | None = None
+        if init:
+            self.init_weights()
+        if device is not None:
+            self.to(device)
+        self.setup()
+
+    # ---------------------------------------------------------------- construction
+    @classmethod
+    def from_preset(cls, name: str, device: Any = None, seed: int | None = None, **overrides: Any) -> HookedLM:
+        if seed is not None:
+            torch.manual_seed(seed)
+        return cls(preset_config(name, **overrides), device=device)
+
+    @torch.no_grad()
+    def init_weights(self) -> None:
+        std = self.cfg.init_std
+        for name, p in self.named_parameters():
+            if p.dim() >= 2:
+                p.normal_(0.0, std)
+                if name.endswith(("o.weight", "down.weight")):
+                    p.mul_(1.0 / math.sqrt(2 * self.cfg.n_layers))
+            elif name.endswith(".b") or name.endswith("bias"):
+                p.zero_()
+
+    @property
+    def W_U(self) -> torch.Tensor:
+        return self.embed.weight if self.unembed is None else self.unembed.weight
+
+    @property
+    def device(self) -> torch.device:
+        return self.embed.weight.device
+
+    # ---------------------------------------------------------------- forward
+    def _rotary(self, S: int) -> tuple[torch.Tensor, torch.Tensor] | None:
+        if self.cfg.positional != "rotary":
+            return None
+        dev = self.embed.weight.device
+        if self._rot is None or self._rot[0].shape[0] < S or self._rot[0].device != dev:
+            self._rot = rotary_tables(max(S, self.cfg.n_ctx), self.cfg.d_head or 0, self.cfg.rotary_base, dev)
+        return self._rot[0][:S], self._rot[1][:S]
+
+    def forward(self, tokens: torch.Tensor, return_type: str | None = "logits",
+                stop_at_layer: int | None = None, start_at_layer: int | None = None,
+                residual: torch.Tensor | None = None) -> torch.Tensor | None:
+        if isinstance(tokens, str) or (isinstance(tokens, list) and tokens and isinstance(tokens[0], str)):
+            tokens = self.to_tokens(tokens)
+        if start_at_layer is None:
+            tokens = tokens.to(self.embed.weight.device)
+            if tokens.dim() == 1:
+                tokens = tokens.unsqueeze(0)
+            S = tokens.shape[1]
+            x = self.hook_embed(self.embed(tokens))
+            if self.cfg.embed_scale:
+                x = x * torch.tensor(math.sqrt(self.cfg.d_model), dtype=x.dtype, device=x.device)
+            if self.cfg.positional == "standard":
+                pos = torch.arange(S, device=tokens.device)
+                x = x + self.hook_pos_embed(self.pos_embed(pos))[None]
+            start = 0
+        else:
+            assert residual is not None
+            x, S, start = residual, residual.shape[1], start_at_layer
+        rot = self._rotary(S)
+        end = self.cfg.n_layers if stop_at_layer is None else min(stop_at_layer, self.cfg.n_layers)
+        for blk in self.blocks[start:end]:
+            x = blk(x, rot)
+        if stop_at_layer is not None and stop_at_layer < self.cfg.n_layers:
+            return x
+        if return_type is None:
+            return None
+        x = self.ln_final(x)
+        if return_type == "residual":
+            return x
+        logits = x @ self.W_U.T if self.unembed is None else self.unembed(x)
+        if self.cfg.final_softcap:
+            logits = self.cfg.final_softcap * torch.tanh(logits.float() / self.cfg.final_softcap)
+        if return_type == "logits":
+            return logits
+        if return_type == "loss":
+            return self.loss_fn(logits, tokens)
+        if return_type == "both":
+            return logits, self.loss_fn(logits, tokens)  # type: ignore[return-value]
+        raise ValueError(f"unknown return_type {return_type}")
+
+    @staticmethod
+    def loss_fn(logits: torch.Tensor, tokens: torch.Tensor, per_token: bool = False) -> torch.Tensor:
+        lp = torch.log_softmax(logits.float(), dim=-1)[:, :-1]
+        nll = -lp.gather(-1, tokens[:, 1:].unsqueeze(-1)).squeeze(-1)
+        return nll if per_token else nll.mean()
+
+    # ---------------------------------------------------------------- tokenizer helpers
+    def to_tokens(self, text: str | list[str], prepend_bos: bool = True, truncate: bool = True) -> torch.Tensor:
+        if self.tokenizer is None:
+            raise ValueError("this model has no tokenizer attached")
+        texts = [text] if isinstance(text, str) else text
+        ids = [self.tokenizer.encode(t) for t in texts]
+        bos = getattr(self.tokenizer, "bos_token_id", None)
+        if prepend_bos and bos is not None:
+            ids = [[bos] + i for i in ids]
+        if truncate:
+            ids = [i[: self.cfg.n_ctx] for i in ids]
+        L = max(len(i) for i in ids)
+        pad = getattr(self.tokenizer, "pad_token_id", None) or 0
+        out = torch.full((len(ids), L), pad, dtype=torch.long)
+        for r, i in enumerate(ids):
+            out[r, : len(i)] = torch.tensor(i)
+        return out.to(self.device)
+
+    def to_string(self, tokens: torch.Tensor) -> str | list[str]:
+        if self.tokenizer is None:
+            raise ValueError("this model has no tokenizer attached")
+        if tokens.dim() == 1:
+            return self.tokenizer.decode(tokens.tolist())
+        return [self.tokenizer.decode(t.tolist()) for t in tokens]
