@@ -1,0 +1,289 @@
+"""`LanguageModelSAETrainingRunner`: train an SAE on a language model's activations end to end
+(API of sae_lens/llm_sae_training_runner.py).
+
+run(): process groups (when launched with torchrun) -> producer LM -> ActivationsStore ->
+TrainingSAE (optionally sharded over `sae_tp_size` ranks, replicated over `sae_dp_size` ranks
+with manual / DDP / FSDP gradient sync) -> SAETrainer.fit() -> final inference SAE, feature
+sparsity and `runner_cfg.json`.  On CUDA, TopK SAEs train on the fused native engine.
+SIGINT/SIGTERM checkpoint the run before exiting.
+
+Command line: `python -m saelens_b200.runners.llm_sae_training_runner --architecture topk --d_in ...`
+(every config field is a `--field value` flag; nested SAE fields are plain flags too).
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import signal
+import sys
+from dataclasses import fields
+from pathlib import Path
+from typing import Any
+
+import torch
+import torch.distributed as dist
+
+from saelens_b200 import logger
+from saelens_b200.config import LanguageModelSAERunnerConfig, LoggingConfig
+from saelens_b200.constants import ACTIVATIONS_STORE_STATE_FILENAME, RUNNER_CFG_FILENAME, SPARSITY_FILENAME
+from saelens_b200.models.sae import TrainingSAE, TrainingSAEConfig
+from saelens_b200.registry import get_sae_training_class
+from saelens_b200.training.activations_store import ActivationsStore
+from saelens_b200.training.sae_trainer import SAETrainer
+
+
+class InterruptedException(Exception):
+    pass
+
+
+def _interrupt(*_a: Any) -> None:
+    raise InterruptedException()
+
+
+class LanguageModelSAETrainingRunner:
+    def __init__(self, cfg: LanguageModelSAERunnerConfig[Any], override_dataset: Any = None,
+                 override_model: Any = None, override_sae: TrainingSAE[Any] | None = None,
+                 resume_from_checkpoint: str | Path | None = None, sae_tp_size: int = 1, sae_dp_size: int = 1,
+                 vllm_tp_size: int = 1, vllm_dp_size: int = 1, use_shard_routing: bool = False,
+                 streaming_mode: bool | None = None, token_count_weighted_dp: bool = False):
+        self.cfg = cfg
+        self.override_dataset = override_dataset
+        self.override_model = override_model
+        self.override_sae = override_sae
+        self.resume_from_checkpoint = resume_from_checkpoint or cfg.resume_from_checkpoint
+        self.sae_tp_size, self.sae_dp_size = sae_tp_size, sae_dp_size
+        self.vllm_tp_size, self.vllm_dp_size = vllm_tp_size, vllm_dp_size
+        self.use_shard_routing = use_shard_routing
+        self.streaming_mode = cfg.streaming_mode if streaming_mode is None else streaming_mode
+        self.token_count_weighted_dp = token_count_weighted_dp
+        self.tp_group: dist.ProcessGroup | None = None
+        self.dp_group: dist.ProcessGroup | None = None
+        self._init_distributed()
+        self.model = override_model if override_model is not None else self._load_model()
+        shard, nshard = (self._dp_rank(), self.sae_dp_size) if self.sae_dp_size > 1 else (0, 1)
+        self.activations_store = ActivationsStore.from_config(self.model, cfg, override_dataset=override_dataset,
+                                                              shard_index=shard, num_shards=nshard)
+        self.sae = override_sae if override_sae is not None else self._build_sae()
+        if self.tp_group is not None and hasattr(self.sae, "shard_weights"):
+            self.sae.shard_weights(self.tp_group)
+        self.wrapped = self._wrap_dp(self.sae)
+
+    # ---------------------------------------------------------------- setup
+    def _init_distributed(self) -> None:
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        if world <= 1 or (self.sae_tp_size == 1 and self.sae_dp_size == 1):
+            return
+        if not dist.is_initialized():
+            backend = "nccl" if self.cfg.device.startswith("cuda") else "gloo"
+            if backend == "nccl":
+                torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+            dist.init_process_group(backend)
+        from saelens_b200.parallel import distributed as D
+
+        D.init_distributed(sae_tp_size=self.sae_tp_size, sae_dp_size=self.sae_dp_size,
+                           vllm_tp_size=max(self.vllm_tp_size, 1), vllm_dp_size=max(self.vllm_dp_size, self.sae_dp_size))
+        self.tp_group = D.get_sae_tp_group() if self.sae_tp_size > 1 else None
+        self.dp_group = D.get_sae_dp_group() if self.sae_dp_size > 1 else None
+
+    def _dp_rank(self) -> int:
+        return dist.get_rank(self.dp_group) if self.dp_group is not None else 0
+
+    def _load_model(self) -> Any:
+        from saelens_b200.models.lm.load_model import load_model
+
+        return load_model(self.cfg.model_class_name, self.cfg.model_name, device=self.cfg.device,
+                          model_from_pretrained_kwargs=self.cfg.model_from_pretrained_kwargs)
+
+    def _build_sae(self) -> TrainingSAE[Any]:
+        cfg = self.cfg
+        if cfg.from_pretrained_path is not None:
+            sae = TrainingSAE.load_from_disk(cfg.from_pretrained_path, device=cfg.device)
+        else:
+            sae_cfg = type(cfg.sae).from_sae_runner_config(cfg)
+            sae_cfg.device = cfg.device
+            sae_cfg.dtype = cfg.dtype
+            torch.manual_seed(cfg.seed)
+            sae = get_sae_training_class(sae_cfg.architecture())[0](sae_cfg)
+        return sae
+
+    def _wrap_dp(self, sae: TrainingSAE[Any]) -> Any:
+        if self.dp_group is None or self.cfg.sae_dp_mode == "manual":
+            return sae
+        if self.cfg.sae_dp_mode == "ddp":
+            from torch.nn.parallel import DistributedDataParallel as DDP
+
+            kw: dict[str, Any] = {"process_group": self.dp_group}
+            for k in ("broadcast_buffers", "find_unused_parameters", "gradient_as_bucket_view", "static_graph",
+                      "bucket_cap_mb"):
+                v = getattr(self.cfg, f"ddp_{k}")
+                if v is not None:
+                    kw[k] = v
+            if sae.W_dec.is_cuda:
+                kw["device_ids"] = [sae.W_dec.device.index]
+            return DDP(sae, **kw)
+        if self.tp_group is not None:
+            raise ValueError("sae_dp_mode='fsdp' cannot be combined with sae_tp_size > 1")
+        from torch.distributed.fsdp import FullyShardedDataParallel as FSDP
+        from torch.distributed.fsdp import ShardingStrategy
+
+        return FSDP(sae, process_group=self.dp_group, sharding_strategy=ShardingStrategy.FULL_SHARD,
+                    use_orig_params=True, device_id=sae.W_dec.device if sae.W_dec.is_cuda else None)
+
+    # ---------------------------------------------------------------- run
+    def run(self) -> TrainingSAE[Any]:
+        cfg = self.cfg
+        if cfg.logger.log_to_wandb and self._is_writer():
+            from saelens_b200.utils import wandb_shim as wandb
+
+            wandb.init(project=cfg.logger.wandb_project, entity=cfg.logger.wandb_entity, name=cfg.logger.run_name,
+                       id=cfg.logger.wandb_id, config=cfg.to_dict())
+        trainer = SAETrainer(
+            cfg=cfg.to_sae_trainer_config(), sae=self.wrapped, base_sae=self.sae, data_provider=self.activations_store,
+            evaluator=self._evaluator(), save_checkpoint_fn=self._save_checkpoint_extras, dp_group=self.dp_group,
+            token_count_weighted_dp=self.token_count_weighted_dp,
+        )
+        self.trainer = trainer
+        if self.resume_from_checkpoint is not None:
+            ck = Path(self.resume_from_checkpoint)
+            self.sae.load_weights_from_checkpoint(ck)
+            if trainer.engine is not None:
+                trainer.engine.refresh()
+            trainer.load_trainer_state(ck)
+            if (ck / ACTIVATIONS_STORE_STATE_FILENAME).exists():
+                self.activations_store.load_from_checkpoint(ck)
+        old_int = signal.signal(signal.SIGINT, _interrupt)
+        old_term = signal.signal(signal.SIGTERM, _interrupt)
+        try:
+            sae = trainer.fit()
+        except (KeyboardInterrupt, InterruptedException):
+            logger.warning("interrupted: saving a checkpoint before exiting")
+            trainer.save_checkpoint(checkpoint_name=f"interrupted_{trainer.n_training_samples}")
+            raise
+        finally:
+            signal.signal(signal.SIGINT, old_int)
+            signal.signal(signal.SIGTERM, old_term)
+        self.save_final_sae(sae, trainer)
+        if cfg.logger.log_to_wandb and self._is_writer():
+            from saelens_b200.utils import wandb_shim as wandb
+
+            wandb.finish()
+        return sae
+
+    def _evaluator(self) -> Any:
+        from saelens_b200.evals import LLMSaeEvaluator
+
+        return LLMSaeEvaluator(self.model, self.activations_store, self.cfg.n_eval_batches,
+                               self.cfg.eval_batch_size_prompts)
+
+    def _is_writer(self) -> bool:
+        tp = dist.get_rank(self.tp_group) if self.tp_group is not None else 0
+        dp = dist.get_rank(self.dp_group) if self.dp_group is not None else 0
+        return tp == 0 and dp == 0
+
+    def _save_checkpoint_extras(self, checkpoint_path: Path | None) -> None:
+        if checkpoint_path is None:
+            return
+        self.activations_store.save_to_checkpoint(checkpoint_path)
+        with open(Path(checkpoint_path) / RUNNER_CFG_FILENAME, "w") as f:
+            json.dump(self.cfg.to_dict(), f, default=str)
+
+    def save_final_sae(self, sae: TrainingSAE[Any], trainer: SAETrainer[Any]) -> Path | None:
+        if self.cfg.output_path is None:
+            return None
+        out = Path(self.cfg.output_path)
+        out.mkdir(parents=True, exist_ok=True)
+        sae.save_inference_model(out)
+        if self._is_writer():
+            from safetensors.torch import save_file
+
+            save_file({"sparsity": trainer.log_feature_sparsity}, out / SPARSITY_FILENAME)
+            with open(out / RUNNER_CFG_FILENAME, "w") as f:
+                json.dump(self.cfg.to_dict(), f, default=str)
+        return out
+
+
+SAETrainingRunner = LanguageModelSAETrainingRunner
+
+
+# ------------------------------------------------------------------------------ CLI
+def _coerce(tp: Any, raw: str) -> Any:
+    s = str(tp)
+    if raw.lower() in ("none", "null") and ("None" in s or "Optional" in s):
+        return None
+    if "bool" in s and raw.lower() in ("true", "false", "1", "0", "yes", "no"):
+        return raw.lower() in ("true", "1", "yes")
+    if s.startswith("dict") or "dict[" in s:
+        return json.loads(raw)
+    if "tuple" in s:
+        return tuple(None if x in ("", "None") else int(x) for x in raw.strip("()").split(",") if x.strip() != "" or True)
+    if "list[int]" in s and raw.startswith("["):
+        return json.loads(raw)
+    if "int" in s and "float" not in s and "str" not in s:
+        try:
+            return int(raw)
+        except ValueError:
+            pass
+    if "float" in s:
+        try:
+            return float(raw)
+        except ValueError:
+            pass
+    if "int" in s:
+        try:
+            return int(raw)
+        except ValueError:
+            pass
+    return raw
+
+
+def _parse_cfg_args(args: list[str]) -> LanguageModelSAERunnerConfig[Any]:
+    """`--architecture <arch>` selects the SAE training config; every other `--field value` is a
+    runner, logger or SAE config field."""
+    kv: dict[str, str] = {}
+    i = 0
+    while i < len(args):
+        a = args[i]
+        if not a.startswith("--"):
+            raise SystemExit(f"unexpected argument {a!r}")
+        key = a[2:].replace("-", "_")
+        if "=" in key:
+            key, val = key.split("=", 1)
+            i += 1
+        elif i + 1 < len(args) and not args[i + 1].startswith("--"):
+            val = args[i + 1]
+            i += 2
+        else:
+            val = "true"
+            i += 1
+        kv[key] = val
+    arch = kv.pop("architecture", "standard")
+    sae_cfg_cls = get_sae_training_class(arch)[1]
+    sae_f = {f.name: f.type for f in fields(sae_cfg_cls)}
+    run_f = {f.name: f.type for f in fields(LanguageModelSAERunnerConfig)}
+    log_f = {f.name: f.type for f in fields(LoggingConfig)}
+    sae_kw, run_kw, log_kw = {}, {}, {}
+    for k, v in kv.items():
+        if k in sae_f and k not in ("device", "dtype"):
+            sae_kw[k] = _coerce(sae_f[k], v)
+        elif k in run_f:
+            run_kw[k] = _coerce(run_f[k], v)
+        elif k in log_f:
+            log_kw[k] = _coerce(log_f[k], v)
+        elif k in sae_f:
+            sae_kw[k] = _coerce(sae_f[k], v)
+        else:
+            raise SystemExit(f"unknown option --{k}")
+    if "d_in" not in sae_kw or "d_sae" not in sae_kw:
+        raise SystemExit("--d_in and --d_sae are required")
+    sae_cfg: TrainingSAEConfig = sae_cfg_cls(**sae_kw)
+    return LanguageModelSAERunnerConfig(sae=sae_cfg, logger=LoggingConfig(**log_kw), **run_kw)
+
+
+def _run_cli(args: list[str]) -> None:
+    cfg = _parse_cfg_args(args)
+    LanguageModelSAETrainingRunner(cfg).run()
+
+
+if __name__ == "__main__":
+    _run_cli(sys.argv[1:])
