@@ -1,0 +1,89 @@
+"""CacheActivationsRunner -> cached-activation training, PretokenizeRunner, MultiSAETrainer."""
+
+import json
+
+import numpy as np
+import torch
+
+from saelens_b200.config import CacheActivationsRunnerConfig, LoggingConfig, PretokenizeRunnerConfig, SAETrainerConfig
+from saelens_b200.models.lm import HookedLM, preset_config
+from saelens_b200.models.standard import StandardTrainingSAE, StandardTrainingSAEConfig
+from saelens_b200.models.topk import TopKTrainingSAE, TopKTrainingSAEConfig
+from saelens_b200.runners.cache_activations_runner import CacheActivationsRunner
+from saelens_b200.runners.pretokenize_runner import PretokenizeRunner
+from saelens_b200.training.activations_store import ActivationsStore
+from saelens_b200.training.multi_sae_trainer import MultiSAETrainer
+
+
+def _lm():
+    torch.manual_seed(0)
+    return HookedLM(preset_config("gpt2", n_layers=2, d_model=64, n_heads=4, d_mlp=128, d_vocab=500, n_ctx=64,
+                                  dtype="float32"))
+
+
+def test_cache_activations_roundtrip(tmp_path):
+    cfg = CacheActivationsRunnerConfig(dataset_path="synthetic:uniform:500:32", model_name="gpt2", model_batch_size=4,
+                                       hook_name="blocks.0.hook_resid_post", d_in=64, training_tokens=16 * 40,
+                                       context_size=16, new_cached_activations_path=str(tmp_path / "cache"),
+                                       device="cpu", buffer_size_gb=16 * 10 * 64 * 4 / 1e9, shuffle=False)
+    lm = _lm()
+    out = CacheActivationsRunner(cfg, override_model=lm).run()
+    info = json.loads((out / "cache_info.json").read_text())
+    assert info["total_tokens"] == 16 * 40 and info["n_shards"] == len(list(out.glob("*.safetensors"))) > 1
+    from safetensors.torch import load_file
+
+    sd = load_file(str(sorted(out.glob("*.safetensors"))[0]))
+    toks = sd["token_ids"][:2].long()
+    _, cache = lm.run_with_cache(toks, names_filter="blocks.0.hook_resid_post")
+    assert torch.allclose(sd["activations"][:2], cache["blocks.0.hook_resid_post"], atol=1e-5)
+    store = ActivationsStore(model=lm, dataset=None, hook_name="blocks.0.hook_resid_post", context_size=16, d_in=64,
+                             n_batches_in_buffer=2, total_training_tokens=640, store_batch_size_prompts=4,
+                             train_batch_size_tokens=32, cached_activations_path=str(out), activations_mixing_fraction=0)
+    assert next(store).shape == (32, 64)
+
+
+class _Tok:
+    bos_token_id, eos_token_id, sep_token_id = 1, 2, 3
+
+    def encode(self, s):
+        return [10 + (ord(c) % 50) for c in s]
+
+
+def test_pretokenize(tmp_path):
+    cfg = PretokenizeRunnerConfig(tokenizer_name="char", context_size=8, save_path=str(tmp_path / "pt"), shuffle=False)
+    data = [{"text": "hello world"}, {"text": "sparse autoencoders"}, {"text": "b200"}]
+    out = PretokenizeRunner(cfg, tokenizer=_Tok(), override_dataset=data).run()
+    arr = np.load(out / "tokens.npy")
+    assert arr.shape[1] == 8 and (arr[:, 0] == 1).all()
+    meta = json.loads((out / "sae_lens.json").read_text())
+    assert meta["context_size"] == 8 and meta["n_rows"] == len(arr)
+
+
+def test_multi_sae_trainer_two_hooks(tmp_path):
+    cfg = SAETrainerConfig(
+        n_checkpoints=0, checkpoint_path=None, save_final_checkpoint=False, output_path=None, save_mse_every_n_steps=0,
+        save_timing_every_n_steps=0, save_memory_every_n_steps=0, synchronize_timing=False,
+        multi_sae_backward_order="largest_first", multi_sae_stats_sync_mode="immediate", multi_sae_stats_sync_interval=1,
+        total_training_samples=32 * 20, device="cpu", autocast=False, lr=1e-3, lr_end=1e-4,
+        lr_scheduler_name="constant", lr_warm_up_steps=0, adam_beta1=0.9, adam_beta2=0.999, lr_decay_steps=0,
+        n_restart_cycles=1, train_batch_size_samples=32, dead_feature_window=5, feature_sampling_window=10,
+        logger=LoggingConfig(log_to_wandb=False))
+    saes = {"a": StandardTrainingSAE(StandardTrainingSAEConfig(d_in=16, d_sae=32)),
+            "b": TopKTrainingSAE(TopKTrainingSAEConfig(d_in=16, d_sae=64, k=4))}
+    g = torch.Generator().manual_seed(0)
+
+    def gen():
+        while True:
+            yield {"a": torch.randn(32, 16, generator=g), "b": torch.randn(32, 16, generator=g)}
+
+    for mode in ("combined", "sequential"):
+        tr = MultiSAETrainer(hook_names=["a", "b"], sae_by_hook=saes, data_provider=gen(), cfg=cfg, backward_mode=mode)
+        tr.fit()
+        assert tr.n_training_steps == 20
+    tr.save_final(tmp_path / "final")
+    tr.save_checkpoint(tmp_path / "ck")
+    man = json.loads((tmp_path / "final" / "multi_sae_manifest.json").read_text())
+    assert man["hook_names"] == ["a", "b"]
+    tr2 = MultiSAETrainer(hook_names=["a", "b"], sae_by_hook=saes, data_provider=gen(), cfg=cfg)
+    tr2.load_trainer_state(tmp_path / "ck")
+    assert tr2.n_training_steps == 20
