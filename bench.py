@@ -43,6 +43,8 @@ def _parse() -> argparse.Namespace:
     p.add_argument("--k", type=int, default=128)
     p.add_argument("--batch", type=int, default=16384)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--tp-exchange", choices=["p2p", "nccl"], default="p2p",
+                   help="TP exchanges: fused NVLink peer-memory kernels (default) or NCCL collectives")
     return p.parse_args()
 
 
@@ -133,7 +135,8 @@ def main() -> None:
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
 
-    setup = BenchSetup(d_in=args.d_in, d_sae=args.d_sae, k=args.k, batch=args.batch, world=world, rank=rank)
+    setup = BenchSetup(d_in=args.d_in, d_sae=args.d_sae, k=args.k, batch=args.batch, world=world, rank=rank,
+                       tp_exchange=args.tp_exchange)
     sampler = ClockSampler(list(range(torch.cuda.device_count()))[:world] if world > 1 else [local]) if rank == 0 else None
     dev = run_device_timed(setup, args.steps, args.warmup, sampler)
     e2e = None if args.no_e2e else run_e2e(setup, args.steps, args.warmup)
@@ -147,7 +150,7 @@ def main() -> None:
             "vs_baseline": None if BASELINE_VALUE is None else value / BASELINE_VALUE,
             "dtype": "bf16", "data": "synthetic: N(0,1) activations scaled to norm sqrt(d_in); random-init SAE",
             "config": {"model": f"TopK SAE d_in {args.d_in} d_sae {args.d_sae} k {args.k} (latent-sharded TP{world})",
-                       "global_batch": args.batch, "seq_len": None, "parallelism": f"tp{world}",
+                       "global_batch": args.batch, "seq_len": None, "parallelism": f"tp{world}" + (f"-{args.tp_exchange}" if world > 1 else ""),
                        "l2": "per-step working set (>17 GB of weights, 128 MB input) exceeds the 126 MB L2",
                        "optimizer": "Adam, fp32 master + fp32 moments, clip 1.0"},
             "clocks": dev.get("clocks"),

@@ -211,6 +211,9 @@ class LanguageModelSAERunnerConfig(Generic[T_TRAINING_SAE_CONFIG]):
     # B200 engine knobs (no counterpart in the reference): use the fused native TopK-family
     # training step on CUDA when available ("auto"), always ("native") or never ("torch").
     sae_engine: Literal["auto", "native", "torch"] = "auto"
+    # Tensor-parallel exchanges of the native engine: NVLink peer-memory kernels fused with the
+    # compute ("p2p") or NCCL collectives between kernels ("nccl").
+    tp_exchange: Literal["p2p", "nccl"] = "p2p"
 
     def __post_init__(self) -> None:
         if self.multi_sae_seed_mode not in ("same", "offset"):
@@ -340,7 +343,7 @@ class LanguageModelSAERunnerConfig(Generic[T_TRAINING_SAE_CONFIG]):
             lr_decay_steps=self.lr_decay_steps, n_restart_cycles=self.n_restart_cycles,
             train_batch_size_samples=self.train_batch_size_tokens,
             dead_feature_window=self.dead_feature_window, feature_sampling_window=self.feature_sampling_window,
-            logger=self.logger, sae_engine=self.sae_engine,
+            logger=self.logger, sae_engine=self.sae_engine, tp_exchange=self.tp_exchange,
         )
 
 
@@ -486,6 +489,7 @@ class SAETrainerConfig:
     feature_sampling_window: int
     logger: LoggingConfig
     sae_engine: Literal["auto", "native", "torch"] = "auto"
+    tp_exchange: Literal["p2p", "nccl"] = "p2p"
 
     @property
     def total_training_steps(self) -> int:

@@ -26,6 +26,8 @@ SOURCES = [
     "sparse.cu",
     "adam.cu",
     "noalloc_csc.cu",
+    "p2p.cu",
+    "symm.cpp",
 ]
 
 NVCC_FLAGS = [

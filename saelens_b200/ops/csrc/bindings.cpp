@@ -1,6 +1,9 @@
 // Python bindings of the saelens_b200 native kernels (module `saelens_b200.ops._C`).
 #include <torch/extension.h>
 
+#include <tuple>
+#include <vector>
+
 namespace sb {
 void gemm_tn_bf16(const torch::Tensor& A, const torch::Tensor& B, const c10::optional<torch::Tensor>& bias,
                   const c10::optional<torch::Tensor>& scale, bool relu,
@@ -31,7 +34,8 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
                  const c10::optional<torch::Tensor>& bterm, const c10::optional<torch::Tensor>& sumsq,
                  const c10::optional<torch::Tensor>& fire_counts,
                  const c10::optional<torch::Tensor>& act_freq,
-                 const c10::optional<torch::Tensor>& since_fired);
+                 const c10::optional<torch::Tensor>& since_fired, const torch::Tensor& idx,
+                 const c10::optional<torch::Tensor>& aux_idx);
 void adam_bdec(const c10::optional<torch::Tensor>& bsum, const c10::optional<torch::Tensor>& bterm,
                const torch::Tensor& gb_dec, const c10::optional<torch::Tensor>& sumsq,
                const c10::optional<torch::Tensor>& clip_out, const torch::Tensor& p, const torch::Tensor& m,
@@ -56,6 +60,34 @@ void finish_mse(const torch::Tensor& xsum, const c10::optional<torch::Tensor>& b
                 const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& resid,
                 const c10::optional<torch::Tensor>& dxhat, const c10::optional<torch::Tensor>& grad_coef_dev,
                 double grad_coef, const torch::Tensor& loss_row, const c10::optional<torch::Tensor>& bsum);
+void gemm_ag_tn_bf16(const torch::Tensor& x_own, const std::vector<int64_t>& peer_bases, int64_t rank,
+                     int64_t x_off, int64_t flag_off, int64_t total_rows, int64_t m_base, int64_t M,
+                     bool push, int64_t epoch, const torch::Tensor& B, const c10::optional<torch::Tensor>& bias,
+                     const c10::optional<torch::Tensor>& scale, bool relu, const c10::optional<torch::Tensor>& out,
+                     const c10::optional<torch::Tensor>& cmax, const torch::Tensor& status,
+                     const torch::Tensor& ticket, int64_t max_ctas);
+void decode_rs(const torch::Tensor& vals, const torch::Tensor& idx, bool relu,
+               const c10::optional<torch::Tensor>& inv_scale, const torch::Tensor& W,
+               const std::vector<int64_t>& peer_bases, int64_t rank, int64_t land_off, int64_t lcnt_off,
+               int64_t dx_off, int64_t dcnt_off, int64_t epoch, const c10::optional<torch::Tensor>& bias,
+               const torch::Tensor& target, const c10::optional<torch::Tensor>& out,
+               const c10::optional<torch::Tensor>& resid, const c10::optional<torch::Tensor>& grad_coef_dev,
+               double grad_coef, const torch::Tensor& loss_row, const c10::optional<torch::Tensor>& bsum,
+               const torch::Tensor& ticket, const torch::Tensor& status);
+void topk_exchange_merge(const torch::Tensor& vals, const torch::Tensor& idx, int64_t n_local,
+                         const c10::optional<torch::Tensor>& k_dev, const std::vector<int64_t>& peer_bases,
+                         int64_t rank, int64_t cv_off, int64_t ci_off, int64_t cnt_off, int64_t epoch,
+                         const torch::Tensor& ticket, const torch::Tensor& status);
+std::vector<int64_t> p2p_allreduce_sizes(int64_t n, int64_t elem_bytes, int64_t world);
+void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64_t>& peer_bases, int64_t rank,
+                   int64_t land_off, int64_t cnt_off, int64_t out_off, int64_t flag_off, int64_t epoch,
+                   const torch::Tensor& ticket, const torch::Tensor& status);
+void p2p_wait_flags(const torch::Tensor& flags, int64_t target, const torch::Tensor& status);
+std::tuple<int64_t, torch::Tensor> symm_alloc(int64_t nbytes);
+int64_t symm_open(const torch::Tensor& handle);
+void symm_close(int64_t addr);
+void symm_free(int64_t addr);
+torch::Tensor tensor_at(int64_t addr, std::vector<int64_t> sizes, torch::ScalarType dtype, int64_t device);
 }  // namespace sb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -71,4 +103,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("topk_merge", &sb::topk_merge);
   m.def("decode_partial", &sb::decode_partial);
   m.def("finish_mse", &sb::finish_mse);
+  m.def("gemm_ag_tn_bf16", &sb::gemm_ag_tn_bf16);
+  m.def("decode_rs", &sb::decode_rs);
+  m.def("topk_exchange_merge", &sb::topk_exchange_merge);
+  m.def("p2p_allreduce_sizes", &sb::p2p_allreduce_sizes);
+  m.def("p2p_allreduce", &sb::p2p_allreduce);
+  m.def("p2p_wait_flags", &sb::p2p_wait_flags);
+  m.def("symm_alloc", &sb::symm_alloc);
+  m.def("symm_open", &sb::symm_open);
+  m.def("symm_close", &sb::symm_close);
+  m.def("symm_free", &sb::symm_free);
+  m.def("tensor_at", &sb::tensor_at);
 }

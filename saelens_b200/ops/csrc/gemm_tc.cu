@@ -14,11 +14,23 @@
 // `hidden_pre * W_dec.norm(dim=-1)` (sae_lens/saes/topk_sae.py:626-630): with bias = b_enc -
 // W_enc^T b_dec (b_dec folded, so A is the raw input) and scale = ||W_dec[j]||.  The chunk
 // maxima let the row top-k kernel skip every 32-column chunk that cannot hold a top-k value.
+//
+// All-gather fused variant (tensor-parallel encoder, AG=true): A is the full input [B, K] in
+// this rank's symmetric slab, of which only the rank's own rows [r*Bo, (r+1)*Bo) exist when
+// the kernel starts.  Two extra warps per CTA push the own rows, one 128-row tile at a time, into
+// every rank's slab over NVLink and publish a per-tile epoch flag on the receiver.  The TMA
+// producer waits (acquire, bounded) for the flag of each m-tile before loading it, and the tile
+// order starts with the rank's own rows, then the next rank's, so the transfers overlap the
+// tensor-core work instead of preceding it (the reference all-gathers first and multiplies
+// after: sae_lens/distributed.py:404-461 around sae_lens/saes/topk_sae.py:626).
 #include <ATen/cuda/CUDAContext.h>
+#include <cstdlib>
+#include <string>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "p2p.cuh"
 #include "tmap.h"
 
 namespace sb {
@@ -33,6 +45,9 @@ constexpr int B_TILE_BYTES = BN * BK * 2;
 constexpr int STAGE_BYTES = A_TILE_BYTES + B_TILE_BYTES;
 constexpr int NUM_EPI_WARPS = 4;
 constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
+constexpr int NUM_COPY_WARPS = 2;  // all-gather pushers (AG variant only)
+constexpr int NUM_THREADS_AG = NUM_THREADS + 32 * NUM_COPY_WARPS;
+constexpr int MAX_MTILES = 4096;   // ready bitmap capacity of the AG producer (524288 rows)
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int GROUP_N = 16;  // n-tiles per raster group (L2 reuse of A and B)
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
@@ -47,18 +62,129 @@ struct Epi {
   int64_t ldc;
 };
 
-__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mt, int& nt) {
+// All-gather fusion parameters (byte offsets inside the symmetric slabs).
+struct Ag {
+  p2p::Peers P;
+  const __nv_bfloat16* src;  // this rank's rows [Bo, K] (any device memory)
+  int64_t x_off;             // offset of the full input [B, K] bf16 in every slab
+  int64_t flag_off;          // offset of the per-m-tile epoch flags [B / BM] u32
+  int rows_per_rank;         // Bo (multiple of BM)
+  int m_base;                // first global row of this launch's A (multiple of BM)
+  int rot;                   // m-tile rotation so that the tile walk starts at the own rows
+  int push;                  // 1: this launch pushes the own rows (first launch of a step)
+  uint32_t epoch;
+  int* ticket;               // push-item counter, zero at launch: items go to whichever CTAs run
+};
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mt, int& nt, int rot = 0) {
   const int group = t / (num_m * GROUP_N);
   const int first_n = group * GROUP_N;
   const int gsize = min(GROUP_N, num_n - first_n);
   const int r = t - group * num_m * GROUP_N;
   mt = r / gsize;
+  if (rot) mt = (mt + rot) % num_m;
   nt = first_n + r % gsize;
 }
 
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+// Epilogue of one accumulator tile: this thread's TMEM lane `trow` holds output row `row`
+// (columns nt*BN .. nt*BN+255): bias, per-column scale, ReLU, bf16 store, 32-column maxima.
+__device__ __forceinline__ void epilogue_tile(const Epi& ep, uint32_t trow, int row, int M, int nt) {
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(trow + c * 32, r);
+    tmem_ld_wait();
+    const int col0 = nt * BN + c * 32;
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    if (ep.bias) {
+      const float4* b4 = reinterpret_cast<const float4*>(ep.bias + col0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 b = __ldg(b4 + j);
+        v[4 * j] += b.x;
+        v[4 * j + 1] += b.y;
+        v[4 * j + 2] += b.z;
+        v[4 * j + 3] += b.w;
+      }
+    }
+    if (ep.scale) {
+      const float4* s4 = reinterpret_cast<const float4*>(ep.scale + col0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 s = __ldg(s4 + j);
+        v[4 * j] *= s.x;
+        v[4 * j + 1] *= s.y;
+        v[4 * j + 2] *= s.z;
+        v[4 * j + 3] *= s.w;
+      }
+    }
+    if (ep.relu) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
+    }
+    uint32_t packed[16];
+    float cm = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+      packed[j] = *reinterpret_cast<uint32_t*>(&h2);
+      cm = fmaxf(cm, fmaxf(__low2float(h2), __high2float(h2)));
+    }
+    if (row < M) {
+      if (ep.out) {
+        uint4* dst = reinterpret_cast<uint4*>(ep.out + int64_t(row) * ep.ldo + col0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
+                              packed[4 * j + 3]);
+      }
+      if (ep.cmax) ep.cmax[int64_t(row) * ep.ldc + (col0 >> 5)] = __float2bfloat16_rn(cm);
+    }
+  }
+}
+
+// All-gather pushers (two warps, ct = 0..63): claim (distance d, own m-tile j) items from the
+// launch's ticket counter, copy own rows [j*BM, (j+1)*BM) into the slab of rank (r - d) mod S,
+// which consumes them d-th in its rotated tile walk, and publish the tile's epoch flag there.
+__device__ __forceinline__ void ag_push(const Ag& ag, int K, int ct) {
+  if (!ag.push) return;
+  __shared__ int s_item;
+  const int S = ag.P.world, r = ag.P.rank;
+  const int mtpr = ag.rows_per_rank / BM;
+  const int64_t vec_per_tile = int64_t(BM) * K / 8;
+  while (true) {
+    if (ct == 0) s_item = atomicAdd(ag.ticket, 1);
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * NUM_COPY_WARPS) : "memory");
+    const int item = s_item;
+    if (item >= S * mtpr) break;
+    const int d = item / mtpr, j = item - d * mtpr;
+    const int dst = (r - d + S) % S;
+    const uint4* src = reinterpret_cast<const uint4*>(ag.src + int64_t(j) * BM * K);
+    uint4* out = reinterpret_cast<uint4*>(p2p::at<__nv_bfloat16>(ag.P, dst, ag.x_off) +
+                                          (int64_t(r) * ag.rows_per_rank + int64_t(j) * BM) * K);
+    int64_t v = ct;
+    for (; v + 3 * 64 < vec_per_tile; v += 4 * 64) {
+      const uint4 a0 = __ldg(src + v), a1 = __ldg(src + v + 64), a2 = __ldg(src + v + 128),
+                  a3 = __ldg(src + v + 192);
+      out[v] = a0;
+      out[v + 64] = a1;
+      out[v + 128] = a2;
+      out[v + 192] = a3;
+    }
+    for (; v < vec_per_tile; v += 64) out[v] = __ldg(src + v);
+    __threadfence_system();
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * NUM_COPY_WARPS) : "memory");
+    if (ct == 0)
+      st_release_sys_u32(p2p::at<uint32_t>(ag.P, dst, ag.flag_off) + (r * mtpr + j), ag.epoch);
+  }
+}
+
+template <bool AG>
+__global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   int M, int N, int K, Epi ep, int* status) {
+                   int M, int N, int K, Epi ep, int* status, const __grid_constant__ Ag ag) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -70,6 +196,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* tempty_bar = tfull_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  __shared__ uint32_t ready_bits[AG ? MAX_MTILES / 32 : 1];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -90,6 +217,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
+  if (AG)
+    for (int i = threadIdx.x; i < MAX_MTILES / 32; i += blockDim.x) ready_bits[i] = 0;
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
@@ -110,7 +239,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int mt, nt;
-        tile_coords(t, num_m, num_n, mt, nt);
+        tile_coords(t, num_m, num_n, mt, nt, AG ? ag.rot : 0);
+        if (AG) {
+          const int gm = ag.m_base / BM + mt;
+          if (!(ready_bits[gm >> 5] & (1u << (gm & 31)))) {
+            const uint32_t* f = p2p::at<uint32_t>(ag.P, ag.P.rank, ag.flag_off) + gm;
+            if (!wait_geq_sys(f, ag.epoch, status, kTimeoutPeerFlag)) {
+              *abort_flag = 1;
+              ok = false;
+              break;
+            }
+            fence_proxy_async_global();
+            ready_bits[gm >> 5] |= 1u << (gm & 31);
+          }
+        }
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -169,73 +311,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (ok) umma_commit(&tfull_bar[acc]);
       }
     }
+  } else if (AG && warp >= 2 + NUM_EPI_WARPS) {
+    // ------------------------------ all-gather pushers ------------------------
+    // Item i = (distance d, own m-tile j): copy own rows [j*BM, (j+1)*BM) into the slab of
+    // rank (r - d) mod S, which consumes them d-th in its rotated tile walk; then publish.
+    ag_push(ag, K, threadIdx.x - 32 * (2 + NUM_EPI_WARPS));
   } else {
     // ------------------------------ epilogue ----------------------------------
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     uint32_t tc = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tc) {
       int mt, nt;
-      tile_coords(t, num_m, num_n, mt, nt);
+      tile_coords(t, num_m, num_n, mt, nt, AG ? ag.rot : 0);
       const int acc = tc & 1;
       const uint32_t aph = (tc >> 1) & 1;
       if (!mbar_wait_bounded(&tfull_bar[acc], aph, abort_flag, status, kTimeoutEpilogue)) break;
       tc_fence_after();
       const int row = mt * BM + q * 32 + lane;
       const uint32_t trow = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(trow + c * 32, r);
-        tmem_ld_wait();
-        const int col0 = nt * BN + c * 32;
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        if (ep.bias) {
-          const float4* b4 = reinterpret_cast<const float4*>(ep.bias + col0);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float4 b = __ldg(b4 + j);
-            v[4 * j] += b.x;
-            v[4 * j + 1] += b.y;
-            v[4 * j + 2] += b.z;
-            v[4 * j + 3] += b.w;
-          }
-        }
-        if (ep.scale) {
-          const float4* s4 = reinterpret_cast<const float4*>(ep.scale + col0);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float4 s = __ldg(s4 + j);
-            v[4 * j] *= s.x;
-            v[4 * j + 1] *= s.y;
-            v[4 * j + 2] *= s.z;
-            v[4 * j + 3] *= s.w;
-          }
-        }
-        if (ep.relu) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
-        }
-        uint32_t packed[16];
-        float cm = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-          packed[j] = *reinterpret_cast<uint32_t*>(&h2);
-          cm = fmaxf(cm, fmaxf(__low2float(h2), __high2float(h2)));
-        }
-        if (row < M) {
-          if (ep.out) {
-            uint4* dst = reinterpret_cast<uint4*>(ep.out + int64_t(row) * ep.ldo + col0);
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
-                                  packed[4 * j + 3]);
-          }
-          if (ep.cmax) ep.cmax[int64_t(row) * ep.ldc + (col0 >> 5)] = __float2bfloat16_rn(cm);
-        }
-      }
+      epilogue_tile(ep, trow, row, M, nt);
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
     }
@@ -246,6 +340,191 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// CTA-pair variant (cluster of 2, tcgen05 cta_group::2): a pair computes a 256 x 256 tile.
+// CTA r of the pair stages rows [r*128, r*128+128) of the A tile and rows [r*128, r*128+128) of
+// the B tile (i.e. output columns) per k-block, so each SM streams half as much B as the
+// single-CTA kernel for the same tensor work; 6 stages of 32 KB.  The leader CTA (rank 0) issues
+// the M=256 MMAs over both CTAs' shared memory; each CTA's TMEM holds its 128 output rows x 256
+// columns.  Barriers: "stage full" lives in the leader (both CTAs' loads count on it), "stage
+// empty" and "accumulator full" in both CTAs (the leader's commits arrive on both), "accumulator
+// empty" in the leader (all 8 epilogue warps of the pair arrive on it).
+// ------------------------------------------------------------------------------------------
+constexpr int PSTAGES = 6;
+constexpr int PA_BYTES = 128 * BK * 2;
+constexpr int PB_BYTES = 128 * BK * 2;
+constexpr int PSTAGE_BYTES = PA_BYTES + PB_BYTES;
+constexpr int PSMEM_BYTES = PSTAGES * PSTAGE_BYTES + 1024 + 256;
+
+template <bool AG>
+__global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
+                     int N, int K, Epi ep, int* status, const __grid_constant__ Ag ag) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + PSTAGES * PA_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + PSTAGES * PB_BYTES);
+  uint64_t* empty_bar = full_bar + PSTAGES;
+  uint64_t* tfull_bar = empty_bar + PSTAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  __shared__ uint32_t ready_bits[AG ? MAX_MTILES / 32 : 1];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t cta = cluster_ctarank();
+  const bool leader = cta == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int num_m = (M + 2 * BM - 1) / (2 * BM);
+  const int num_n = N / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PSTAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 2 * NUM_EPI_WARPS);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (AG)
+    for (int i = threadIdx.x; i < MAX_MTILES / 32; i += blockDim.x) ready_bits[i] = 0;
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers are initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer (both CTAs) ------------------
+    if (elect_one()) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += npairs) {
+        int mt, nt;
+        tile_coords(t, num_m, num_n, mt, nt, AG ? ag.rot : 0);
+        if (AG) {
+          const int gm = ag.m_base / BM + 2 * mt + int(cta);
+          if (!(ready_bits[gm >> 5] & (1u << (gm & 31)))) {
+            const uint32_t* f = p2p::at<uint32_t>(ag.P, ag.P.rank, ag.flag_off) + gm;
+            if (!wait_geq_sys(f, ag.epoch, status, kTimeoutPeerFlag)) {
+              *abort_flag = 1;
+              ok = false;
+              break;
+            }
+            fence_proxy_async_global();
+            ready_bits[gm >> 5] |= 1u << (gm & 31);
+          }
+        }
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % PSTAGES;
+          const uint32_t ph = (it / PSTAGES) & 1;
+          if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1, abort_flag, status, kTimeoutTmaProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = mapa_shared(smem_u32(&full_bar[s]), 0);
+          if (leader) mbar_arrive_expect_tx(&full_bar[s], 2 * PSTAGE_BYTES);
+          tma_load_2d_pair(sA + s * PA_BYTES, &tmA, fb, kb * BK, mt * 2 * BM + int(cta) * BM);
+          tma_load_2d_pair(sB + s * PB_BYTES, &tmB, fb, kb * BK, nt * BN + int(cta) * 128);
+        }
+      }
+      if (!ok && leader) {
+        const uint32_t first = it > PSTAGES ? it - PSTAGES : 0;
+        for (uint32_t j = first; j < it; ++j) {
+          volatile int dummy = 0;
+          mbar_wait_bounded(&full_bar[j % PSTAGES], (j / PSTAGES) & 1, &dummy, nullptr, 0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer (leader CTA) -------------------
+    if (leader && elect_one()) {
+      const uint32_t idesc = make_idesc_bf16_f32(2 * BM, BN);
+      uint32_t it = 0, tc = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += npairs, ++tc) {
+        const int acc = tc & 1;
+        const uint32_t aph = (tc >> 1) & 1;
+        if (!mbar_wait_bounded(&tempty_bar[acc], aph ^ 1, abort_flag, status, kTimeoutMmaTmemEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % PSTAGES;
+          const uint32_t ph = (it / PSTAGES) & 1;
+          if (!mbar_wait_bounded(&full_bar[s], ph, abort_flag, status, kTimeoutMmaFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * PA_BYTES);
+          const uint32_t b_addr = smem_u32(sB + s * PB_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            umma_bf16_ss_pair(d_tmem, make_sdesc_sw128_kmajor(a_addr + k * 32),
+                              make_sdesc_sw128_kmajor(b_addr + k * 32), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          const uint32_t eb = smem_u32(&empty_bar[s]);
+          umma_commit_pair(eb);
+          umma_commit_pair(mapa_shared(eb, 1));
+        }
+        if (ok) {
+          const uint32_t fb = smem_u32(&tfull_bar[acc]);
+          umma_commit_pair(fb);
+          umma_commit_pair(mapa_shared(fb, 1));
+        }
+      }
+    }
+  } else if (AG && warp >= 2 + NUM_EPI_WARPS) {
+    ag_push(ag, K, threadIdx.x - 32 * (2 + NUM_EPI_WARPS));
+  } else if (warp >= 2) {
+    // ------------------------------ epilogue (both CTAs) ----------------------
+    const int q = warp & 3;
+    uint32_t tc = 0;
+    for (int t = pair; t < num_tiles; t += npairs, ++tc) {
+      int mt, nt;
+      tile_coords(t, num_m, num_n, mt, nt, AG ? ag.rot : 0);
+      const int acc = tc & 1;
+      const uint32_t aph = (tc >> 1) & 1;
+      if (!mbar_wait_bounded(&tfull_bar[acc], aph, abort_flag, status, kTimeoutEpilogue)) break;
+      tc_fence_after();
+      const int row = mt * 2 * BM + int(cta) * BM + q * 32 + lane;
+      const uint32_t trow = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
+      epilogue_tile(ep, trow, row, M, nt);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its pair may still touch its shared memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 
@@ -264,23 +543,9 @@ static int num_sms_cached() {
   return n;
 }
 
-// out = epilogue(A @ B^T).  A: [M, K] bf16 (row stride lda), B: [N, K] bf16.  Optional
-// bias/scale fp32 [N].  Returns nothing; writes `out` [M, N] bf16 and/or `cmax` [M, N/32] bf16.
-void gemm_tn_bf16(const torch::Tensor& A, const torch::Tensor& B, const c10::optional<torch::Tensor>& bias,
-                  const c10::optional<torch::Tensor>& scale, bool relu,
-                  const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& cmax,
-                  const torch::Tensor& status, int64_t max_ctas) {
-  TORCH_CHECK(A.is_cuda() && B.is_cuda(), "gemm_tn_bf16: CUDA tensors required");
-  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16,
-              "gemm_tn_bf16: bf16 operands required");
-  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm_tn_bf16: shape");
-  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1, "gemm_tn_bf16: K must be contiguous");
-  const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
-  TORCH_CHECK(K % gemm::BK == 0, "gemm_tn_bf16: K must be a multiple of 64, got ", K);
-  TORCH_CHECK(N % gemm::BN == 0, "gemm_tn_bf16: N must be a multiple of 256, got ", N);
-  TORCH_CHECK(M >= 1 && M < (1ll << 31) && N < (1ll << 31), "gemm_tn_bf16: size");
-  const at::cuda::CUDAGuard guard(A.device());
-
+static gemm::Epi make_epi(int64_t M, int64_t N, const c10::optional<torch::Tensor>& bias,
+                          const c10::optional<torch::Tensor>& scale, bool relu,
+                          const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& cmax) {
   gemm::Epi ep{};
   if (out) {
     TORCH_CHECK(out->scalar_type() == at::kBFloat16 && out->size(0) == M && out->size(1) == N &&
@@ -307,28 +572,139 @@ void gemm_tn_bf16(const torch::Tensor& A, const torch::Tensor& B, const c10::opt
     ep.scale = scale->data_ptr<float>();
   }
   ep.relu = relu ? 1 : 0;
+  return ep;
+}
 
-  CUtensorMap tA = make_tmap_2d(A.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K,
-                                A.stride(0) * 2, gemm::BM, gemm::BK,
-                                CU_TENSOR_MAP_SWIZZLE_128B);
-  CUtensorMap tB = make_tmap_2d(B.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K,
-                                B.stride(0) * 2, gemm::BN, gemm::BK,
-                                CU_TENSOR_MAP_SWIZZLE_128B);
+// CTA-pair kernel unless disabled (SAELENS_B200_GEMM_PAIR=0) or M is too small to fill pairs.
+static bool use_pair(int64_t M) {
+  static const bool off = [] {
+    const char* e = std::getenv("SAELENS_B200_GEMM_PAIR");
+    return e && std::string(e) == "0";
+  }();
+  return !off && M >= 2 * gemm::BM;
+}
 
-  static bool attr_set = false;
-  if (!attr_set) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm::gemm_tn_kernel,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        gemm::SMEM_BYTES));
-    attr_set = true;
-  }
-  const int64_t tiles = ((M + gemm::BM - 1) / gemm::BM) * (N / gemm::BN);
-  int64_t grid = std::min<int64_t>(tiles, num_sms_cached());
-  if (max_ctas > 0) grid = std::min<int64_t>(grid, max_ctas);
+template <bool AG>
+static void launch_gemm(const void* a_ptr, int64_t lda, int64_t M, const torch::Tensor& B, const gemm::Epi& ep,
+                        const torch::Tensor& status, int64_t max_ctas, const gemm::Ag& ag, bool pair) {
+  const int64_t K = B.size(1), N = B.size(0);
+  const int box_rows = pair ? 128 : gemm::BN;
+  CUtensorMap tA = make_tmap_2d(const_cast<void*>(a_ptr), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, lda * 2,
+                                gemm::BM, gemm::BK, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tB = make_tmap_2d(B.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, B.stride(0) * 2,
+                                box_rows, gemm::BK, CU_TENSOR_MAP_SWIZZLE_128B);
   auto stream = at::cuda::getCurrentCUDAStream();
-  gemm::gemm_tn_kernel<<<dim3(grid), dim3(gemm::NUM_THREADS), gemm::SMEM_BYTES, stream>>>(
-      tA, tB, int(M), int(N), int(K), ep, status.data_ptr<int>());
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const int threads = AG ? gemm::NUM_THREADS_AG : gemm::NUM_THREADS;
+  int* st = status.data_ptr<int>();
+  const int iM = int(M), iN = int(N), iK = int(K);
+  if (!pair) {
+    static bool attr_set = false;
+    if (!attr_set) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(gemm::gemm_tn_kernel<AG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          gemm::SMEM_BYTES));
+      attr_set = true;
+    }
+    const int64_t tiles = ((M + gemm::BM - 1) / gemm::BM) * (N / gemm::BN);
+    int64_t grid = std::min<int64_t>(tiles, num_sms_cached());
+    if (max_ctas > 0) grid = std::min<int64_t>(grid, max_ctas);
+    gemm::gemm_tn_kernel<AG><<<dim3(grid), dim3(threads), gemm::SMEM_BYTES, stream>>>(tA, tB, iM, iN, iK, ep, st,
+                                                                                         ag);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
+  auto kern = gemm::gemm_pair_kernel<AG>;
+  static int max_pairs = -1;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = gemm::PSMEM_BYTES;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (max_pairs < 0) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::PSMEM_BYTES));
+    cfg.gridDim = dim3(2 * (num_sms_cached() / 2));
+    int n = 0;
+    C10_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    max_pairs = std::max(1, n);
+  }
+  const int64_t tiles = ((M + 2 * gemm::BM - 1) / (2 * gemm::BM)) * (N / gemm::BN);
+  int64_t pairs = std::min<int64_t>(tiles, max_pairs);
+  if (max_ctas > 0) pairs = std::max<int64_t>(1, std::min<int64_t>(pairs, max_ctas / 2));
+  cfg.gridDim = dim3(unsigned(2 * pairs));
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tA, tB, iM, iN, iK, ep, st, ag));
+}
+
+// out = epilogue(A @ B^T).  A: [M, K] bf16 (row stride lda), B: [N, K] bf16.  Optional
+// bias/scale fp32 [N].  Returns nothing; writes `out` [M, N] bf16 and/or `cmax` [M, N/32] bf16.
+void gemm_tn_bf16(const torch::Tensor& A, const torch::Tensor& B, const c10::optional<torch::Tensor>& bias,
+                  const c10::optional<torch::Tensor>& scale, bool relu,
+                  const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& cmax,
+                  const torch::Tensor& status, int64_t max_ctas) {
+  TORCH_CHECK(A.is_cuda() && B.is_cuda(), "gemm_tn_bf16: CUDA tensors required");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16,
+              "gemm_tn_bf16: bf16 operands required");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm_tn_bf16: shape");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1, "gemm_tn_bf16: K must be contiguous");
+  const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(K % gemm::BK == 0, "gemm_tn_bf16: K must be a multiple of 64, got ", K);
+  TORCH_CHECK(N % gemm::BN == 0, "gemm_tn_bf16: N must be a multiple of 256, got ", N);
+  TORCH_CHECK(M >= 1 && M < (1ll << 31) && N < (1ll << 31), "gemm_tn_bf16: size");
+  const at::cuda::CUDAGuard guard(A.device());
+  const gemm::Epi ep = make_epi(M, N, bias, scale, relu, out, cmax);
+  launch_gemm<false>(A.data_ptr(), A.stride(0), M, B, ep, status, max_ctas, gemm::Ag{}, use_pair(M));
+}
+
+// All-gather fused encoder GEMM over rows [m_base, m_base + M) of the full input that lives at
+// byte offset `x_off` of every rank's symmetric slab (`peer_bases[r]` = rank r's slab address).
+// `x_own` [Bo, K] is this rank's part; with `push` the kernel also distributes it to every rank.
+// Waits (bounded) for the epoch flag of each m-tile at `flag_off` before reading it.
+void gemm_ag_tn_bf16(const torch::Tensor& x_own, const std::vector<int64_t>& peer_bases, int64_t rank,
+                     int64_t x_off, int64_t flag_off, int64_t total_rows, int64_t m_base, int64_t M,
+                     bool push, int64_t epoch, const torch::Tensor& B, const c10::optional<torch::Tensor>& bias,
+                     const c10::optional<torch::Tensor>& scale, bool relu, const c10::optional<torch::Tensor>& out,
+                     const c10::optional<torch::Tensor>& cmax, const torch::Tensor& status,
+                     const torch::Tensor& ticket, int64_t max_ctas) {
+  const int64_t S = int64_t(peer_bases.size());
+  TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "gemm_ag: bad group");
+  TORCH_CHECK(x_own.is_cuda() && x_own.scalar_type() == at::kBFloat16 && x_own.is_contiguous(),
+              "gemm_ag: x_own must be contiguous CUDA bf16");
+  TORCH_CHECK(B.scalar_type() == at::kBFloat16 && B.stride(1) == 1 && B.size(1) == x_own.size(1),
+              "gemm_ag: weight");
+  const int64_t Bo = x_own.size(0), K = x_own.size(1), N = B.size(0);
+  TORCH_CHECK(Bo * S == total_rows, "gemm_ag: total_rows must be world * own rows");
+  TORCH_CHECK(Bo % gemm::BM == 0 && m_base % gemm::BM == 0 && M % gemm::BM == 0 && M >= gemm::BM &&
+                  m_base + M <= total_rows,
+              "gemm_ag: rows must be multiples of 128");
+  TORCH_CHECK(total_rows / gemm::BM <= gemm::MAX_MTILES, "gemm_ag: too many rows");
+  TORCH_CHECK(K % gemm::BK == 0 && N % gemm::BN == 0, "gemm_ag: K % 64 and N % 256");
+  TORCH_CHECK(x_off % 16 == 0 && flag_off % 4 == 0, "gemm_ag: slab offsets must be aligned");
+  const at::cuda::CUDAGuard guard(x_own.device());
+  const gemm::Epi ep = make_epi(M, N, bias, scale, relu, out, cmax);
+  gemm::Ag ag{};
+  ag.P = p2p::make_peers(peer_bases, rank);
+  ag.src = reinterpret_cast<const __nv_bfloat16*>(x_own.data_ptr());
+  ag.x_off = x_off;
+  ag.flag_off = flag_off;
+  ag.rows_per_rank = int(Bo);
+  ag.m_base = int(m_base);
+  const int64_t own0 = rank * Bo;
+  const bool pair = use_pair(M) && Bo % (2 * gemm::BM) == 0 && M % (2 * gemm::BM) == 0 &&
+                    m_base % (2 * gemm::BM) == 0;
+  const int64_t tile_rows = pair ? 2 * gemm::BM : gemm::BM;
+  const int num_m = int(M / tile_rows);
+  ag.rot = (own0 >= m_base && own0 < m_base + M) ? int((own0 - m_base) / tile_rows) % num_m : 0;
+  ag.push = push ? 1 : 0;
+  ag.epoch = uint32_t(epoch);
+  TORCH_CHECK(ticket.is_cuda() && ticket.scalar_type() == at::kInt && ticket.numel() >= 1, "gemm_ag: ticket");
+  ag.ticket = ticket.data_ptr<int>();
+  if (push) C10_CUDA_CHECK(cudaMemsetAsync(ag.ticket, 0, sizeof(int), at::cuda::getCurrentCUDAStream()));
+  const char* a_ptr = reinterpret_cast<const char*>(peer_bases[rank]) + x_off + m_base * K * 2;
+  launch_gemm<true>(a_ptr, K, M, B, ep, status, max_ctas, ag, pair);
 }
 
 }  // namespace sb

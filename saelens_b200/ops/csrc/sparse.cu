@@ -16,10 +16,13 @@
 // An auxiliary pair list (dead-latent aux-k loss) uses raw coefficients h/||W_dec|| (no ReLU)
 // and its own residual-gradient rows; it is merged into the same CSC pass.
 #include <ATen/cuda/CUDAContext.h>
+#include <cstdlib>
+#include <string>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "p2p.cuh"
 
 namespace sb {
 namespace sparse {
@@ -208,6 +211,74 @@ __global__ void __launch_bounds__(DEC_THREADS)
 // reduce-scattered, `finish_mse` adds b_dec and produces the loss, dL/dx_hat, the residual and
 // the column sum for the b_dec gradient on this rank's rows.
 // ---------------------------------------------------------------------------------------
+// acc = sum_i a_i W[idx_i] for one row (no bias): coefficients are staged in s_a / s_i
+// (k floats + k ints of shared memory); the caller owns the barriers around reuse of s_a/s_i.
+template <int VPT>
+__device__ __forceinline__ void decode_row_partial(int row, const float* __restrict__ vals,
+                                                   const int* __restrict__ idx, int k, int64_t ldk, int relu,
+                                                   const float* __restrict__ inv_scale,
+                                                   const __nv_bfloat16* __restrict__ W, int64_t ldw, int nvec,
+                                                   float* s_a, int* s_i, float (&acc)[VPT][8]) {
+  const int t = threadIdx.x;
+  __syncthreads();
+  for (int i = t; i < k; i += DEC_THREADS) {
+    const int j = idx[int64_t(row) * ldk + i];
+    float a = 0.f;
+    if (j >= 0) {
+      const float v = vals[int64_t(row) * ldk + i];
+      a = (relu ? fmaxf(v, 0.f) : v) * (inv_scale ? __ldg(inv_scale + j) : 1.f);
+    }
+    s_a[i] = a;
+    s_i[i] = (a != 0.f) ? j : -1;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int v = 0; v < VPT; ++v)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[v][e] = 0.f;
+  constexpr int U = 4;
+  int i = 0;
+  for (; i + U <= k; i += U) {
+    uint4 w[U][VPT];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int jj = s_i[i + u];
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        const int vi = t + v * DEC_THREADS;
+        w[u][v] = (jj >= 0 && vi < nvec) ? __ldg(reinterpret_cast<const uint4*>(W + int64_t(jj) * ldw) + vi)
+                                         : make_uint4(0, 0, 0, 0);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const float aa = s_a[i + u];
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        float f[8];
+        bf16x8_to_f32(w[u][v], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[v][e] += aa * f[e];
+      }
+    }
+  }
+  for (; i < k; ++i) {
+    const int jj = s_i[i];
+    if (jj < 0) continue;
+    const float aa = s_a[i];
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int vi = t + v * DEC_THREADS;
+      if (vi < nvec) {
+        float f[8];
+        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(W + int64_t(jj) * ldw) + vi), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[v][e] += aa * f[e];
+      }
+    }
+  }
+}
+
 template <int VPT>
 __global__ void __launch_bounds__(DEC_THREADS)
     decode_partial_kernel(const float* __restrict__ vals, const int* __restrict__ idx, int k, int64_t ldk,
@@ -219,64 +290,8 @@ __global__ void __launch_bounds__(DEC_THREADS)
   const int nvec = D >> 3;
   const int t = threadIdx.x;
   for (int row = blockIdx.x; row < M; row += gridDim.x) {
-    __syncthreads();
-    for (int i = t; i < k; i += DEC_THREADS) {
-      const int j = idx[int64_t(row) * ldk + i];
-      float a = 0.f;
-      if (j >= 0) {
-        const float v = vals[int64_t(row) * ldk + i];
-        a = (relu ? fmaxf(v, 0.f) : v) * (inv_scale ? __ldg(inv_scale + j) : 1.f);
-      }
-      s_a[i] = a;
-      s_i[i] = (a != 0.f) ? j : -1;
-    }
-    __syncthreads();
     float acc[VPT][8];
-#pragma unroll
-    for (int v = 0; v < VPT; ++v)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[v][e] = 0.f;
-    constexpr int U = 4;
-    int i = 0;
-    for (; i + U <= k; i += U) {
-      uint4 w[U][VPT];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int jj = s_i[i + u];
-#pragma unroll
-        for (int v = 0; v < VPT; ++v) {
-          const int vi = t + v * DEC_THREADS;
-          w[u][v] = (jj >= 0 && vi < nvec) ? __ldg(reinterpret_cast<const uint4*>(W + int64_t(jj) * ldw) + vi)
-                                           : make_uint4(0, 0, 0, 0);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const float aa = s_a[i + u];
-#pragma unroll
-        for (int v = 0; v < VPT; ++v) {
-          float f[8];
-          bf16x8_to_f32(w[u][v], f);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[v][e] += aa * f[e];
-        }
-      }
-    }
-    for (; i < k; ++i) {
-      const int jj = s_i[i];
-      if (jj < 0) continue;
-      const float aa = s_a[i];
-#pragma unroll
-      for (int v = 0; v < VPT; ++v) {
-        const int vi = t + v * DEC_THREADS;
-        if (vi < nvec) {
-          float f[8];
-          bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(W + int64_t(jj) * ldw) + vi), f);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[v][e] += aa * f[e];
-        }
-      }
-    }
+    decode_row_partial<VPT>(row, vals, idx, k, ldk, relu, inv_scale, W, ldw, nvec, s_a, s_i, acc);
 #pragma unroll
     for (int v = 0; v < VPT; ++v) {
       const int vi = t + v * DEC_THREADS;
@@ -608,6 +623,419 @@ __global__ void __launch_bounds__(LG_THREADS, 2) latent_grad_kernel(LatentGradAr
   if (t == 0 && a.sumsq) atomicAdd(a.sumsq, tot);
 }
 
+
+// ---------------------------------------------------------------------------------------
+// Fused tensor-parallel decode: one launch per rank, all ranks running concurrently.
+//   phase A (tickets [0, B/RB)): this rank's partial reconstruction of RB consecutive rows
+//           (from its own winners), stored straight into the row owner's landing area
+//           land[src = this rank][row - owner*Bo] with NVLink P2P stores, then one release-add
+//           on the owner's arrival counter of that row block.
+//   phase B (tickets [B/RB, B/RB + Bo/RB)): for a row block this rank owns, wait until all S
+//           sources arrived, reduce the S partials in rank order, add b_dec, and produce
+//           loss_row, sae_out, the residual, dL/dx_hat and its column sum; dL/dx_hat rows are
+//           stored into EVERY rank's dx buffer and published with one epoch flag per block.
+// Tickets come from one counter, so a phase-B block is claimed only after every phase-A block
+// has been claimed by a CTA that is running: no wait depends on a CTA that is not resident.
+// Phase A walks the owners starting at rank+1, so at any moment the ranks push to different
+// receivers.  Replaces the reference's dense decode + reduce-scatter + loss
+// (sae_lens/distributed.py:404-461, sae_lens/saes/topk_sae.py:645-674).
+// ---------------------------------------------------------------------------------------
+constexpr int RS_RB = 16;
+
+struct DecodeRsArgs {
+  const float* vals;
+  const int* idx;
+  int k;
+  int64_t ldk;
+  int relu;
+  const float* inv_scale;
+  const __nv_bfloat16* W;
+  int64_t ldw;
+  int B, Bo, D;
+  p2p::Peers P;
+  int64_t land_off, lcnt_off, dx_off, dcnt_off;  // slab byte offsets; dx_off < 0: no broadcast
+  uint32_t epoch;
+  const float* bias;
+  const __nv_bfloat16* target;
+  int64_t ldt;
+  __nv_bfloat16* out;
+  __nv_bfloat16* resid;
+  const float* grad_coef_dev;
+  float grad_coef;
+  float* loss_row;
+  float* bsum;
+  int* ticket;
+  int* status;
+};
+
+template <int VPT>
+__global__ void __launch_bounds__(DEC_THREADS) decode_rs_kernel(const __grid_constant__ DecodeRsArgs a) {
+  extern __shared__ float dsm[];
+  float* s_a = dsm;
+  int* s_i = reinterpret_cast<int*>(dsm + a.k);
+  float* red = dsm + 2 * a.k;
+  __shared__ int s_tk, s_ok;
+  const int t = threadIdx.x;
+  const int S = a.P.world, r = a.P.rank, D = a.D;
+  const int nvec = D >> 3;
+  const int nbo = a.Bo / RS_RB, nA = a.B / RS_RB, nT = nA + nbo;
+  const float gcoef = a.grad_coef_dev ? a.grad_coef * __ldg(a.grad_coef_dev) : a.grad_coef;
+  float bacc[VPT][8];
+#pragma unroll
+  for (int v = 0; v < VPT; ++v)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) bacc[v][e] = 0.f;
+
+  while (true) {
+    __syncthreads();
+    if (t == 0) s_tk = atomicAdd(a.ticket, 1);
+    __syncthreads();
+    const int tk = s_tk;
+    if (tk >= nT) break;
+    if (tk < nA) {
+      // ---------------- phase A: partial rows -> owner ----------------
+      const int blk = (tk + (r + 1) * nbo) % nA;
+      const int o = blk / nbo, lb = blk - o * nbo;
+      float* land = p2p::at<float>(a.P, o, a.land_off) + (int64_t(r) * a.Bo + int64_t(lb) * RS_RB) * D;
+      for (int rr = 0; rr < RS_RB; ++rr) {
+        float acc[VPT][8];
+        decode_row_partial<VPT>(blk * RS_RB + rr, a.vals, a.idx, a.k, a.ldk, a.relu, a.inv_scale, a.W, a.ldw,
+                                nvec, s_a, s_i, acc);
+#pragma unroll
+        for (int v = 0; v < VPT; ++v) {
+          const int vi = t + v * DEC_THREADS;
+          if (vi < nvec) {
+            float4* o4 = reinterpret_cast<float4*>(land + int64_t(rr) * D) + 2 * vi;
+            o4[0] = make_float4(acc[v][0], acc[v][1], acc[v][2], acc[v][3]);
+            o4[1] = make_float4(acc[v][4], acc[v][5], acc[v][6], acc[v][7]);
+          }
+        }
+      }
+      __threadfence_system();
+      __syncthreads();
+      if (t == 0) red_release_sys_add_u32(p2p::at<uint32_t>(a.P, o, a.lcnt_off) + lb, 1u);
+    } else {
+      // ---------------- phase B: reduce owned rows, loss, dL/dx_hat -> everyone ----------------
+      const int ob = tk - nA;
+      if (t == 0)
+        s_ok = wait_geq_sys(p2p::at<uint32_t>(a.P, r, a.lcnt_off) + ob, uint32_t(S) * a.epoch, a.status,
+                            kTimeoutPeerFlag)
+                   ? 1
+                   : 0;
+      __syncthreads();
+      if (!s_ok) continue;
+      const float* land = p2p::at<float>(a.P, r, a.land_off);
+      for (int rr = 0; rr < RS_RB; ++rr) {
+        const int row = ob * RS_RB + rr;  // local row
+        float lsum = 0.f;
+#pragma unroll
+        for (int v = 0; v < VPT; ++v) {
+          const int vi = t + v * DEC_THREADS;
+          if (vi >= nvec) continue;
+          float xh[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) xh[e] = 0.f;
+          for (int src = 0; src < S; ++src) {
+            const float4* p4 = reinterpret_cast<const float4*>(land + (int64_t(src) * a.Bo + row) * D) + 2 * vi;
+            const float4 p0 = __ldcg(p4), p1 = __ldcg(p4 + 1);
+            xh[0] += p0.x; xh[1] += p0.y; xh[2] += p0.z; xh[3] += p0.w;
+            xh[4] += p1.x; xh[5] += p1.y; xh[6] += p1.z; xh[7] += p1.w;
+          }
+          if (a.bias) {
+            const float4* b4 = reinterpret_cast<const float4*>(a.bias) + 2 * vi;
+            const float4 b0 = __ldg(b4), b1 = __ldg(b4 + 1);
+            xh[0] += b0.x; xh[1] += b0.y; xh[2] += b0.z; xh[3] += b0.w;
+            xh[4] += b1.x; xh[5] += b1.y; xh[6] += b1.z; xh[7] += b1.w;
+          }
+          float tg[8], err[8], g[8], rs[8];
+          bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(a.target + int64_t(row) * a.ldt) + vi), tg);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            err[e] = xh[e] - tg[e];
+            lsum += err[e] * err[e];
+            g[e] = err[e] * gcoef;
+            rs[e] = -err[e];
+          }
+          if (a.out) reinterpret_cast<uint4*>(a.out + int64_t(row) * D)[vi] = f32_to_bf16x8(xh);
+          if (a.resid) reinterpret_cast<uint4*>(a.resid + int64_t(row) * D)[vi] = f32_to_bf16x8(rs);
+          const uint4 gq = f32_to_bf16x8(g);
+          if (a.dx_off >= 0) {
+            const int64_t off = (int64_t(r) * a.Bo + row) * D;
+            for (int d = 0; d < S; ++d)
+              reinterpret_cast<uint4*>(p2p::at<__nv_bfloat16>(a.P, d, a.dx_off) + off)[vi] = gq;
+          }
+          if (a.bsum) {
+            float gr[8];
+            bf16x8_to_f32(gq, gr);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) bacc[v][e] += gr[e];
+          }
+        }
+        const float tot = block_sum(lsum, red);
+        if (t == 0 && a.loss_row) a.loss_row[row] = tot;
+      }
+      if (a.dx_off >= 0) {
+        __threadfence_system();
+        __syncthreads();
+        if (t == 0)
+          for (int d = 0; d < S; ++d)
+            st_release_sys_u32(p2p::at<uint32_t>(a.P, d, a.dcnt_off) + (r * nbo + ob), a.epoch);
+      }
+    }
+  }
+  if (a.bsum) {
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int vi = t + v * DEC_THREADS;
+      if (vi < nvec)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) atomicAdd(a.bsum + 8 * vi + e, bacc[v][e]);
+    }
+  }
+}
+
+
+// ---------------------------------------------------------------------------------------
+// latent gradients, two passes over the CSC pair lists (the pairs of a latent are contiguous):
+//  pass 1 (pair_dz_kernel, one warp per pair): row b, coefficient a and
+//         dz = <dL/dx_hat[b], W_dec[j]> of every pair, stored in CSC order.  The dot product is
+//         the only reduction over d_in; after it every column is independent.
+//  pass 2 (latent_rows_kernel, one warp per (latent, d_in slice), slice fixed per warp):
+//         gW_dec[j] = sum a dXhat[b], gW_enc[j] = sum dz (x[b] - b_dec), gb_enc[j] = sum dz, the
+//         firing statistics, the squared gradient norm and per-warp partials of the b_dec term
+//         sum_j gb_enc[j] W_enc[j]; col_reduce_kernel sums those partials into bterm.
+// No block barrier sits on the per-latent path, so many latents' loads are in flight per SM.
+// ---------------------------------------------------------------------------------------
+constexpr int LR_THREADS = 256;
+constexpr int LR_WARPS = LR_THREADS / 32;
+
+struct PairDzArgs {
+  const int64_t* pairs;
+  const int64_t* n_live;  // colptr + N: number of live pairs (only that prefix of `pairs` is filled)
+  int64_t P, n_main;
+  int k, k_aux;
+  const float* vals;
+  const int* idx;
+  const float* aux_vals;
+  const int* aux_idx;
+  const float* inv_scale;
+  const __nv_bfloat16* dxhat;
+  const __nv_bfloat16* daux;
+  const __nv_bfloat16* W_dec;
+  int D;
+  int* prow;      // [P] row | (aux << 31)
+  float* pcoef;   // [P]
+  float* pdz;     // [P]
+};
+
+__global__ void __launch_bounds__(LR_THREADS) pair_dz_kernel(const __grid_constant__ PairDzArgs a) {
+  constexpr int U = 8;  // 16-byte loads in flight per lane and operand
+  const int lane = threadIdx.x & 31;
+  const int nvec = a.D >> 3;
+  const int64_t nw = int64_t(gridDim.x) * LR_WARPS;
+  const int64_t live = min(*a.n_live, a.P);
+  for (int64_t pos = (int64_t(blockIdx.x) * LR_THREADS + threadIdx.x) >> 5; pos < live; pos += nw) {
+    const int64_t p = a.pairs[pos];
+    int64_t b;
+    int j, aux;
+    float coef;
+    if (p < a.n_main) {
+      b = p / a.k;
+      j = a.idx[p];
+      coef = fmaxf(a.vals[p], 0.f);
+      aux = 0;
+    } else {
+      const int64_t q = p - a.n_main;
+      b = q / a.k_aux;
+      j = a.aux_idx[q];
+      coef = a.aux_vals[q];
+      aux = 1;
+    }
+    if (a.inv_scale) coef *= __ldg(a.inv_scale + j);
+    const uint4* g4 = reinterpret_cast<const uint4*>((aux ? a.daux : a.dxhat) + b * int64_t(a.D));
+    const uint4* w4 = reinterpret_cast<const uint4*>(a.W_dec + int64_t(j) * a.D);
+    float d = 0.f;
+    for (int v0 = lane; v0 < nvec; v0 += 32 * U) {
+      uint4 g[U], w[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int vi = v0 + 32 * u;
+        g[u] = vi < nvec ? __ldg(g4 + vi) : make_uint4(0, 0, 0, 0);
+        w[u] = vi < nvec ? __ldg(w4 + vi) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float gf[8], wf[8];
+        bf16x8_to_f32(g[u], gf);
+        bf16x8_to_f32(w[u], wf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) d += gf[e] * wf[e];
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+    if (lane == 0) {
+      a.prow[pos] = int(b) | (aux << 31);
+      a.pcoef[pos] = coef;
+      a.pdz[pos] = d;
+    }
+  }
+}
+
+struct LatentRowsArgs {
+  const int64_t* colptr;
+  const int* prow;
+  const float* pcoef;
+  const float* pdz;
+  const __nv_bfloat16* dxhat;
+  const __nv_bfloat16* daux;
+  const __nv_bfloat16* x;
+  int64_t ldx;
+  const float* b_dec;
+  const __nv_bfloat16* W_enc;
+  __nv_bfloat16* gW_dec;
+  __nv_bfloat16* gW_enc;
+  float* gb_enc;
+  float* bpart;   // [total warps, slice width] b_dec-term partials (or nullptr)
+  float* sumsq;
+  const int* fire_counts;
+  float* act_freq;
+  float* since_fired;
+  int N, D, nslices;
+};
+
+template <int VPL>
+__global__ void __launch_bounds__(LR_THREADS, 2) latent_rows_kernel(const __grid_constant__ LatentRowsArgs a) {
+  __shared__ float red[32];
+  const int lane = threadIdx.x & 31;
+  const int nvec = a.D >> 3;
+  const int gw = (blockIdx.x * LR_THREADS + threadIdx.x) >> 5;
+  const int tw = gridDim.x * LR_WARPS;
+  const int sl = gw % a.nslices;
+  const int vbase = sl * 32 * VPL + lane;
+  float bd[VPL][8], bt[VPL][8];
+#pragma unroll
+  for (int u = 0; u < VPL; ++u) {
+    const int vi = vbase + 32 * u;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) bd[u][e] = bt[u][e] = 0.f;
+    if (a.b_dec && vi < nvec) {
+      const float4 b0 = __ldg(reinterpret_cast<const float4*>(a.b_dec) + 2 * vi);
+      const float4 b1 = __ldg(reinterpret_cast<const float4*>(a.b_dec) + 2 * vi + 1);
+      bd[u][0] = b0.x; bd[u][1] = b0.y; bd[u][2] = b0.z; bd[u][3] = b0.w;
+      bd[u][4] = b1.x; bd[u][5] = b1.y; bd[u][6] = b1.z; bd[u][7] = b1.w;
+    }
+  }
+  float sq = 0.f;
+  for (int j = gw / a.nslices; j < a.N; j += tw / a.nslices) {
+    const int64_t beg = a.colptr[j], end = a.colptr[j + 1];
+    if (sl == 0 && lane == 0 && a.fire_counts) {
+      const int fc = a.fire_counts[j];
+      if (a.act_freq) a.act_freq[j] += float(fc);
+      if (a.since_fired) a.since_fired[j] = fc > 0 ? 0.f : a.since_fired[j] + 1.f;
+    }
+    if (beg == end) {
+      if (sl == 0 && lane == 0) a.gb_enc[j] = 0.f;
+      continue;
+    }
+    float gd[VPL][8], ge[VPL][8];
+#pragma unroll
+    for (int u = 0; u < VPL; ++u)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) gd[u][e] = ge[u][e] = 0.f;
+    float gbe = 0.f;
+    for (int64_t pos = beg; pos < end; pos += 2) {
+      const bool two = pos + 1 < end;
+      const int r0 = a.prow[pos], r1 = two ? a.prow[pos + 1] : r0;
+      const float c0 = a.pcoef[pos], c1 = two ? a.pcoef[pos + 1] : 0.f;
+      const float z0 = a.pdz[pos], z1 = two ? a.pdz[pos + 1] : 0.f;
+      const __nv_bfloat16* g0 = ((r0 < 0) ? a.daux : a.dxhat) + int64_t(r0 & 0x7fffffff) * a.D;
+      const __nv_bfloat16* g1 = ((r1 < 0) ? a.daux : a.dxhat) + int64_t(r1 & 0x7fffffff) * a.D;
+      const __nv_bfloat16* x0 = a.x + int64_t(r0 & 0x7fffffff) * a.ldx;
+      const __nv_bfloat16* x1 = a.x + int64_t(r1 & 0x7fffffff) * a.ldx;
+      uint4 G0[VPL], G1[VPL], X0[VPL], X1[VPL];
+#pragma unroll
+      for (int u = 0; u < VPL; ++u) {
+        const int vi = vbase + 32 * u;
+        const bool ok = vi < nvec;
+        G0[u] = ok ? __ldg(reinterpret_cast<const uint4*>(g0) + vi) : make_uint4(0, 0, 0, 0);
+        X0[u] = ok ? __ldg(reinterpret_cast<const uint4*>(x0) + vi) : make_uint4(0, 0, 0, 0);
+        G1[u] = (ok && two) ? __ldg(reinterpret_cast<const uint4*>(g1) + vi) : make_uint4(0, 0, 0, 0);
+        X1[u] = (ok && two) ? __ldg(reinterpret_cast<const uint4*>(x1) + vi) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < VPL; ++u) {
+        float f0[8], f1[8], y0[8], y1[8];
+        bf16x8_to_f32(G0[u], f0);
+        bf16x8_to_f32(G1[u], f1);
+        bf16x8_to_f32(X0[u], y0);
+        bf16x8_to_f32(X1[u], y1);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          gd[u][e] += c0 * f0[e] + c1 * f1[e];
+          ge[u][e] += z0 * (y0[e] - bd[u][e]) + z1 * (y1[e] - bd[u][e]);
+        }
+      }
+      gbe += z0 + z1;
+    }
+    uint4 WE[VPL];
+    if (a.bpart) {
+#pragma unroll
+      for (int u = 0; u < VPL; ++u) {
+        const int vi = vbase + 32 * u;
+        WE[u] = vi < nvec ? __ldg(reinterpret_cast<const uint4*>(a.W_enc + int64_t(j) * a.D) + vi)
+                          : make_uint4(0, 0, 0, 0);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < VPL; ++u) {
+      const int vi = vbase + 32 * u;
+      if (vi < nvec) {
+        const uint4 qd = f32_to_bf16x8(gd[u]);
+        const uint4 qe = f32_to_bf16x8(ge[u]);
+        reinterpret_cast<uint4*>(a.gW_dec + int64_t(j) * a.D)[vi] = qd;
+        reinterpret_cast<uint4*>(a.gW_enc + int64_t(j) * a.D)[vi] = qe;
+        float rd[8], re[8];
+        bf16x8_to_f32(qd, rd);
+        bf16x8_to_f32(qe, re);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sq += rd[e] * rd[e] + re[e] * re[e];
+        if (a.bpart) {
+          float we[8];
+          bf16x8_to_f32(WE[u], we);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) bt[u][e] += gbe * we[e];
+        }
+      }
+    }
+    if (sl == 0 && lane == 0) {
+      a.gb_enc[j] = gbe;
+      sq += gbe * gbe;
+    }
+  }
+  if (a.bpart) {
+    float* dst = a.bpart + int64_t(gw) * (32 * VPL * 8);
+#pragma unroll
+    for (int u = 0; u < VPL; ++u) {
+      float4* d4 = reinterpret_cast<float4*>(dst + (u * 32 + lane) * 8);
+      d4[0] = make_float4(bt[u][0], bt[u][1], bt[u][2], bt[u][3]);
+      d4[1] = make_float4(bt[u][4], bt[u][5], bt[u][6], bt[u][7]);
+    }
+  }
+  const float tot = block_sum(sq, red);
+  if (threadIdx.x == 0 && a.sumsq) atomicAdd(a.sumsq, tot);
+}
+
+// bterm[d] += sum over the warps w with slice(d) of bpart[w][d - slice start]
+__global__ void col_reduce_kernel(const float* __restrict__ bpart, int tw, int nslices, int sw, int D,
+                                  float* __restrict__ bterm) {
+  for (int d = blockIdx.x * blockDim.x + threadIdx.x; d < D; d += gridDim.x * blockDim.x) {
+    const int s = d / sw, c = d - s * sw;
+    float acc = 0.f;
+    for (int w = s; w < tw; w += nslices) acc += bpart[int64_t(w) * sw + c];
+    bterm[d] += acc;
+  }
+}
 }  // namespace sparse
 
 static inline int pick_vpt(int64_t D, int threads) {
@@ -726,7 +1154,7 @@ void csc_fill(const torch::Tensor& vals, const torch::Tensor& idx,
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const torch::Tensor& vals,
+static void latent_grad_v1(const torch::Tensor& colptr, const torch::Tensor& pairs, const torch::Tensor& vals,
                  const c10::optional<torch::Tensor>& aux_vals, const c10::optional<torch::Tensor>& inv_scale,
                  const torch::Tensor& dxhat, const c10::optional<torch::Tensor>& daux,
                  const torch::Tensor& x, const c10::optional<torch::Tensor>& b_dec,
@@ -783,6 +1211,116 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Two-pass latent gradients (pair_dz_kernel + latent_rows_kernel); `idx` / `aux_idx` give the
+// latent of every main / aux pair.  Same contract as the single-pass kernel.
+void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const torch::Tensor& vals,
+                 const c10::optional<torch::Tensor>& aux_vals, const c10::optional<torch::Tensor>& inv_scale,
+                 const torch::Tensor& dxhat, const c10::optional<torch::Tensor>& daux,
+                 const torch::Tensor& x, const c10::optional<torch::Tensor>& b_dec,
+                 const torch::Tensor& W_dec, const torch::Tensor& W_enc, const torch::Tensor& gW_dec,
+                 const torch::Tensor& gW_enc, const torch::Tensor& gb_enc,
+                 const c10::optional<torch::Tensor>& bterm, const c10::optional<torch::Tensor>& sumsq,
+                 const c10::optional<torch::Tensor>& fire_counts,
+                 const c10::optional<torch::Tensor>& act_freq,
+                 const c10::optional<torch::Tensor>& since_fired, const torch::Tensor& idx,
+                 const c10::optional<torch::Tensor>& aux_idx) {
+  static const bool v1 = [] {
+    const char* e = std::getenv("SAELENS_B200_LATENT_GRAD");
+    return e && std::string(e) == "v1";
+  }();
+  if (v1) {
+    latent_grad_v1(colptr, pairs, vals, aux_vals, inv_scale, dxhat, daux, x, b_dec, W_dec, W_enc, gW_dec, gW_enc,
+                   gb_enc, bterm, sumsq, fire_counts, act_freq, since_fired);
+    return;
+  }
+  const at::cuda::CUDAGuard guard(vals.device());
+  const int64_t N = W_dec.size(0), D = W_dec.size(1);
+  TORCH_CHECK(W_dec.is_contiguous() && W_enc.is_contiguous() && gW_dec.is_contiguous() &&
+                  gW_enc.is_contiguous() && W_enc.size(0) == N && W_enc.size(1) == D,
+              "latent_grad: weights must be contiguous [N, D]");
+  TORCH_CHECK(dxhat.is_contiguous() && dxhat.size(1) == D && x.stride(1) == 1 && x.stride(0) % 8 == 0,
+              "latent_grad: dxhat / x layout");
+  TORCH_CHECK(D % 8 == 0 && D <= 8192, "latent_grad: d_in must be a multiple of 8 and at most 8192");
+  TORCH_CHECK(idx.is_contiguous() && idx.scalar_type() == at::kInt && idx.sizes() == vals.sizes(), "latent_grad: idx");
+  TORCH_CHECK(x.size(0) < (int64_t(1) << 31), "latent_grad: too many rows");
+  if (N == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int64_t P = pairs.numel();
+  auto opt_f = vals.options().dtype(at::kFloat);
+  auto prow = torch::empty({std::max<int64_t>(P, 1)}, vals.options().dtype(at::kInt));
+  auto pcoef = torch::empty({std::max<int64_t>(P, 1)}, opt_f);
+  auto pdz = torch::empty({std::max<int64_t>(P, 1)}, opt_f);
+  if (P > 0) {
+    sparse::PairDzArgs pa{};
+    pa.pairs = pairs.data_ptr<int64_t>();
+    TORCH_CHECK(colptr.numel() == N + 1 && colptr.scalar_type() == at::kLong, "latent_grad: colptr");
+    pa.n_live = colptr.data_ptr<int64_t>() + N;
+    pa.P = P;
+    pa.n_main = vals.numel();
+    pa.k = int(vals.size(1));
+    pa.k_aux = aux_vals ? int(aux_vals->size(1)) : 1;
+    pa.vals = vals.data_ptr<float>();
+    pa.idx = idx.data_ptr<int>();
+    pa.aux_vals = aux_vals ? aux_vals->data_ptr<float>() : nullptr;
+    pa.aux_idx = aux_idx ? aux_idx->data_ptr<int>() : nullptr;
+    pa.inv_scale = inv_scale ? inv_scale->data_ptr<float>() : nullptr;
+    pa.dxhat = reinterpret_cast<const __nv_bfloat16*>(dxhat.data_ptr());
+    pa.daux = daux ? reinterpret_cast<const __nv_bfloat16*>(daux->data_ptr()) : nullptr;
+    pa.W_dec = reinterpret_cast<const __nv_bfloat16*>(W_dec.data_ptr());
+    pa.D = int(D);
+    pa.prow = prow.data_ptr<int>();
+    pa.pcoef = pcoef.data_ptr<float>();
+    pa.pdz = pdz.data_ptr<float>();
+    const int64_t grid = std::min<int64_t>((P + sparse::LR_WARPS - 1) / sparse::LR_WARPS, int64_t(sm_count()) * 8);
+    sparse::pair_dz_kernel<<<dim3(grid), dim3(sparse::LR_THREADS), 0, stream>>>(pa);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  const int nvec = int(D / 8);
+  int ns = 1;
+  while (ns < 8 && ns * 64 < nvec) ns *= 2;
+  const int vpl = (nvec + 32 * ns - 1) / (32 * ns);
+  const int sw = 32 * vpl * 8;
+  const int grid = sm_count() * 2;
+  const int tw = grid * sparse::LR_WARPS;
+  torch::Tensor bpart;
+  if (bterm) bpart = torch::empty({int64_t(tw) * sw}, opt_f);
+  sparse::LatentRowsArgs a{};
+  a.colptr = colptr.data_ptr<int64_t>();
+  a.prow = prow.data_ptr<int>();
+  a.pcoef = pcoef.data_ptr<float>();
+  a.pdz = pdz.data_ptr<float>();
+  a.dxhat = reinterpret_cast<const __nv_bfloat16*>(dxhat.data_ptr());
+  a.daux = daux ? reinterpret_cast<const __nv_bfloat16*>(daux->data_ptr()) : nullptr;
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  a.ldx = x.stride(0);
+  a.b_dec = b_dec ? b_dec->data_ptr<float>() : nullptr;
+  a.W_enc = reinterpret_cast<const __nv_bfloat16*>(W_enc.data_ptr());
+  a.gW_dec = reinterpret_cast<__nv_bfloat16*>(gW_dec.data_ptr());
+  a.gW_enc = reinterpret_cast<__nv_bfloat16*>(gW_enc.data_ptr());
+  a.gb_enc = gb_enc.data_ptr<float>();
+  a.bpart = bterm ? bpart.data_ptr<float>() : nullptr;
+  a.sumsq = sumsq ? sumsq->data_ptr<float>() : nullptr;
+  a.fire_counts = fire_counts ? fire_counts->data_ptr<int>() : nullptr;
+  a.act_freq = act_freq ? act_freq->data_ptr<float>() : nullptr;
+  a.since_fired = since_fired ? since_fired->data_ptr<float>() : nullptr;
+  a.N = int(N);
+  a.D = int(D);
+  a.nslices = ns;
+  switch (vpl) {
+    case 1: sparse::latent_rows_kernel<1><<<dim3(grid), dim3(sparse::LR_THREADS), 0, stream>>>(a); break;
+    case 2: sparse::latent_rows_kernel<2><<<dim3(grid), dim3(sparse::LR_THREADS), 0, stream>>>(a); break;
+    case 3: sparse::latent_rows_kernel<3><<<dim3(grid), dim3(sparse::LR_THREADS), 0, stream>>>(a); break;
+    default: sparse::latent_rows_kernel<4><<<dim3(grid), dim3(sparse::LR_THREADS), 0, stream>>>(a); break;
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (bterm) {
+    TORCH_CHECK(bterm->numel() == D && bterm->scalar_type() == at::kFloat, "latent_grad: bterm");
+    sparse::col_reduce_kernel<<<dim3(int((D + 255) / 256)), dim3(256), 0, stream>>>(
+        bpart.data_ptr<float>(), tw, ns, sw, int(D), bterm->data_ptr<float>());
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+}
+
 void decode_partial(const torch::Tensor& vals, const torch::Tensor& idx, bool relu,
                     const c10::optional<torch::Tensor>& inv_scale, const torch::Tensor& W, const torch::Tensor& out) {
   TORCH_CHECK(vals.is_contiguous() && idx.is_contiguous() && vals.scalar_type() == at::kFloat &&
@@ -831,6 +1369,85 @@ void finish_mse(const torch::Tensor& xsum, const c10::optional<torch::Tensor>& b
       dxhat ? reinterpret_cast<__nv_bfloat16*>(dxhat->data_ptr()) : nullptr,
       grad_coef_dev ? grad_coef_dev->data_ptr<float>() : nullptr, float(grad_coef), loss_row.data_ptr<float>(),
       bsum ? bsum->data_ptr<float>() : nullptr, int(M), int(D));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Fused TP decode (see decode_rs_kernel).  vals/idx [B, k] hold this rank's winners (local
+// latent ids); target [Bo, D] are the rank's own input rows (or the aux residual).  Slab
+// offsets: land fp32 [S, Bo, D], lcnt u32 [Bo/16], dx bf16 [B, D] (dx_off < 0: none), dcnt u32
+// [B/16].  `epoch` counts the launches that used these buffers (1, 2, ...).
+void decode_rs(const torch::Tensor& vals, const torch::Tensor& idx, bool relu,
+               const c10::optional<torch::Tensor>& inv_scale, const torch::Tensor& W,
+               const std::vector<int64_t>& peer_bases, int64_t rank, int64_t land_off, int64_t lcnt_off,
+               int64_t dx_off, int64_t dcnt_off, int64_t epoch, const c10::optional<torch::Tensor>& bias,
+               const torch::Tensor& target, const c10::optional<torch::Tensor>& out,
+               const c10::optional<torch::Tensor>& resid, const c10::optional<torch::Tensor>& grad_coef_dev,
+               double grad_coef, const torch::Tensor& loss_row, const c10::optional<torch::Tensor>& bsum,
+               const torch::Tensor& ticket, const torch::Tensor& status) {
+  const int64_t S = int64_t(peer_bases.size());
+  TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "decode_rs: bad group");
+  TORCH_CHECK(vals.is_contiguous() && idx.is_contiguous() && vals.scalar_type() == at::kFloat &&
+                  idx.scalar_type() == at::kInt && vals.sizes() == idx.sizes(),
+              "decode_rs: vals/idx");
+  const int64_t B = vals.size(0), k = vals.size(1), D = W.size(1);
+  TORCH_CHECK(W.scalar_type() == at::kBFloat16 && W.stride(1) == 1 && D % 8 == 0 && D <= 8 * 8 * sparse::DEC_THREADS,
+              "decode_rs: W");
+  TORCH_CHECK(B % (S * sparse::RS_RB) == 0, "decode_rs: batch must be a multiple of 16 * world");
+  const int64_t Bo = B / S;
+  TORCH_CHECK(target.scalar_type() == at::kBFloat16 && target.size(0) == Bo && target.size(1) == D &&
+                  target.stride(1) == 1,
+              "decode_rs: target");
+  for (const auto* o : {&out, &resid})
+    if (*o) TORCH_CHECK((*o)->is_contiguous() && (*o)->size(0) == Bo && (*o)->size(1) == D, "decode_rs: outputs");
+  TORCH_CHECK(loss_row.numel() == Bo && loss_row.scalar_type() == at::kFloat, "decode_rs: loss_row");
+  if (bias) TORCH_CHECK(bias->numel() == D && bias->scalar_type() == at::kFloat, "decode_rs: bias");
+  if (bsum) TORCH_CHECK(bsum->numel() == D && bsum->scalar_type() == at::kFloat, "decode_rs: bsum");
+  TORCH_CHECK(land_off % 16 == 0 && (dx_off < 0 || dx_off % 16 == 0), "decode_rs: offsets");
+  const at::cuda::CUDAGuard guard(vals.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  sparse::DecodeRsArgs a{};
+  a.vals = vals.data_ptr<float>();
+  a.idx = idx.data_ptr<int>();
+  a.k = int(k);
+  a.ldk = k;
+  a.relu = relu ? 1 : 0;
+  a.inv_scale = inv_scale ? inv_scale->data_ptr<float>() : nullptr;
+  a.W = reinterpret_cast<const __nv_bfloat16*>(W.data_ptr());
+  a.ldw = W.stride(0);
+  a.B = int(B);
+  a.Bo = int(Bo);
+  a.D = int(D);
+  a.P = p2p::make_peers(peer_bases, rank);
+  a.land_off = land_off;
+  a.lcnt_off = lcnt_off;
+  a.dx_off = dx_off;
+  a.dcnt_off = dcnt_off;
+  a.epoch = uint32_t(epoch);
+  a.bias = bias ? bias->data_ptr<float>() : nullptr;
+  a.target = reinterpret_cast<const __nv_bfloat16*>(target.data_ptr());
+  a.ldt = target.stride(0);
+  a.out = out ? reinterpret_cast<__nv_bfloat16*>(out->data_ptr()) : nullptr;
+  a.resid = resid ? reinterpret_cast<__nv_bfloat16*>(resid->data_ptr()) : nullptr;
+  a.grad_coef_dev = grad_coef_dev ? grad_coef_dev->data_ptr<float>() : nullptr;
+  a.grad_coef = float(grad_coef);
+  a.loss_row = loss_row.data_ptr<float>();
+  a.bsum = bsum ? bsum->data_ptr<float>() : nullptr;
+  a.ticket = ticket.data_ptr<int>();
+  a.status = status.data_ptr<int>();
+  C10_CUDA_CHECK(cudaMemsetAsync(a.ticket, 0, sizeof(int), stream));
+  const size_t smem = size_t(2 * k + 32) * 4;
+  const int64_t tickets = B / sparse::RS_RB + Bo / sparse::RS_RB;
+  const int nvec = int(D / 8);
+  auto launch = [&](auto kern) {
+    int occ = 0;
+    C10_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, sparse::DEC_THREADS, smem));
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(tickets, int64_t(sm_count()) * std::max(occ, 1)));
+    kern<<<dim3(grid), dim3(sparse::DEC_THREADS), smem, stream>>>(a);
+  };
+  if (nvec <= sparse::DEC_THREADS) launch(sparse::decode_rs_kernel<1>);
+  else if (nvec <= 2 * sparse::DEC_THREADS) launch(sparse::decode_rs_kernel<2>);
+  else if (nvec <= 4 * sparse::DEC_THREADS) launch(sparse::decode_rs_kernel<4>);
+  else launch(sparse::decode_rs_kernel<8>);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -24,6 +24,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "p2p.cuh"
 
 namespace sb {
 namespace topk {
@@ -267,30 +268,24 @@ __global__ void __launch_bounds__(THREADS)
 // entries that made the global cut (the others become idx -1).  Ties at the k-th value are
 // broken by the smaller global column index, matching the single-GPU kernel.
 // ---------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(THREADS)
-    topk_merge_kernel(const float* __restrict__ cand_val, const int* __restrict__ cand_idx, int S, int M,
-                      int k, int64_t n_local, int rank, const int* __restrict__ k_dev,
-                      float* __restrict__ out_val, int* __restrict__ out_idx) {
-  __shared__ uint32_t hist[256];
-  __shared__ uint32_t sh[4];
-  extern __shared__ uint8_t dyn[];
+// Merge one row.  Candidate (s, i) of the row is at cv[s * s_stride + i] / ci[...]; the own
+// candidates' output slots irow[i] become -1 when they miss the global cut.  key / gidx are
+// S*k-entry shared arrays.  Starts with a barrier, so it may be called once per row in a loop.
+__device__ __forceinline__ void merge_row(const float* cv, const int* ci, int64_t s_stride, int S, int k,
+                                          int64_t n_local, int rank, int kk, int* irow, uint32_t* key,
+                                          int64_t* gidx, uint32_t* hist, uint32_t* sh, int* n_valid) {
   const int C = S * k;
-  uint32_t* key = reinterpret_cast<uint32_t*>(dyn);
-  int64_t* gidx = reinterpret_cast<int64_t*>(dyn + ((size_t(C) * 4 + 15) & ~size_t(15)));
-  const int row = blockIdx.x;
   const int tid = threadIdx.x;
-  int kk = k;
-  if (k_dev) kk = min(kk, *k_dev);
-  __shared__ int n_valid;
-  if (tid == 0) n_valid = 0;
+  __syncthreads();
+  if (tid == 0) *n_valid = 0;
   __syncthreads();
   int nv = 0;
   for (int c = tid; c < C; c += THREADS) {
     const int s = c / k, i = c - s * k;
-    const int64_t off = (int64_t(s) * M + row) * k + i;
-    const int li = cand_idx[off];
+    const int64_t off = int64_t(s) * s_stride + i;
+    const int li = __ldcg(ci + off);
     if (li >= 0) {
-      const uint32_t bits = __float_as_uint(cand_val[off]) >> 16;  // values are exact bf16
+      const uint32_t bits = __float_as_uint(__ldcg(cv + off)) >> 16;  // values are exact bf16
       key[c] = bf16_to_key(uint16_t(bits));
       gidx[c] = int64_t(s) * n_local + li;
       ++nv;
@@ -299,18 +294,15 @@ __global__ void __launch_bounds__(THREADS)
       gidx[c] = -1;
     }
   }
-  atomicAdd(&n_valid, nv);
+  atomicAdd(n_valid, nv);
   __syncthreads();
-  kk = min(kk, n_valid);
-  float* vrow = out_val + int64_t(row) * k;
-  int* irow = out_idx + int64_t(row) * k;
+  kk = min(kk, *n_valid);
   if (kk <= 0) {
     for (int i = tid; i < k; i += THREADS) irow[i] = -1;
     return;
   }
   const Sel r = block_select16(C, kk, [&](int i) { return key[i]; }, hist, sh);
   const int need_ties = kk - r.greater;
-  // decide this rank's own candidates
   for (int i = tid; i < k; i += THREADS) {
     const int c = rank * k + i;
     const uint32_t kc = key[c];
@@ -322,7 +314,106 @@ __global__ void __launch_bounds__(THREADS)
       keep = rk < need_ties;
     }
     if (!keep) irow[i] = -1;
-    (void)vrow;
+  }
+}
+
+__global__ void __launch_bounds__(THREADS)
+    topk_merge_kernel(const float* __restrict__ cand_val, const int* __restrict__ cand_idx, int S, int M,
+                      int k, int64_t n_local, int rank, const int* __restrict__ k_dev,
+                      float* __restrict__ out_val, int* __restrict__ out_idx) {
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t sh[4];
+  __shared__ int n_valid;
+  extern __shared__ uint8_t dyn[];
+  uint32_t* key = reinterpret_cast<uint32_t*>(dyn);
+  int64_t* gidx = reinterpret_cast<int64_t*>(dyn + ((size_t(S * k) * 4 + 15) & ~size_t(15)));
+  const int row = blockIdx.x;
+  int kk = k;
+  if (k_dev) kk = min(kk, *k_dev);
+  (void)out_val;
+  merge_row(cand_val + int64_t(row) * k, cand_idx + int64_t(row) * k, int64_t(M) * k, S, k, n_local, rank, kk,
+            out_idx + int64_t(row) * k, key, gidx, hist, sh, &n_valid);
+}
+
+// ---------------------------------------------------------------------------------------
+// Fused candidate all-gather + merge over NVLink (one launch per rank, ranks concurrent).
+//   phase A (tickets [0, B/RB)): copy RB rows of this rank's candidates into slot [rank] of
+//           every rank's candidate area (P2P stores), then release-add each receiver's arrival
+//           counter of that row block.
+//   phase B (tickets [B/RB, 2B/RB)): wait until all S slots of a row block arrived, then merge
+//           its rows as topk_merge does, reading the S candidate lists from local memory.
+// Slab layout: cand values fp32 [S, B, k] at cv_off, indices int32 [S, B, k] at ci_off, counters
+// u32 [B/RB] at cnt_off.  Replaces the all-gather + merge of the TP top-k (the reference gathers
+// the full [B, d_sae] pre-activations instead: sae_lens/distributed.py:404-461).
+// ---------------------------------------------------------------------------------------
+constexpr int XM_RB = 16;
+
+struct XMergeArgs {
+  const float* vals;
+  int* idx;  // in: own candidates (local ids); out: -1 where they miss the global cut
+  int B, k;
+  int64_t n_local;
+  const int* k_dev;
+  p2p::Peers P;
+  int64_t cv_off, ci_off, cnt_off;
+  uint32_t epoch;
+  int* ticket;
+  int* status;
+};
+
+__global__ void __launch_bounds__(THREADS) topk_exchange_merge_kernel(const __grid_constant__ XMergeArgs a) {
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t sh[4];
+  __shared__ int n_valid, s_tk, s_ok;
+  extern __shared__ uint8_t dyn[];
+  const int S = a.P.world, r = a.P.rank, k = a.k;
+  uint32_t* key = reinterpret_cast<uint32_t*>(dyn);
+  int64_t* gidx = reinterpret_cast<int64_t*>(dyn + ((size_t(S * k) * 4 + 15) & ~size_t(15)));
+  const int t = threadIdx.x;
+  const int nA = a.B / XM_RB;
+  int kk = k;
+  if (a.k_dev) kk = min(kk, *a.k_dev);
+  while (true) {
+    __syncthreads();
+    if (t == 0) s_tk = atomicAdd(a.ticket, 1);
+    __syncthreads();
+    const int tk = s_tk;
+    if (tk >= 2 * nA) break;
+    if (tk < nA) {
+      const int blk = tk;
+      const int64_t row0 = int64_t(blk) * XM_RB;
+      const int nv4 = XM_RB * k / 4;  // 16-byte vectors per block and array
+      const uint4* sv = reinterpret_cast<const uint4*>(a.vals + row0 * k);
+      const uint4* si = reinterpret_cast<const uint4*>(a.idx + row0 * k);
+      for (int dd = 1; dd <= S; ++dd) {
+        const int d = (r + dd) % S;
+        uint4* dv = reinterpret_cast<uint4*>(p2p::at<float>(a.P, d, a.cv_off) + (int64_t(r) * a.B + row0) * k);
+        uint4* di = reinterpret_cast<uint4*>(p2p::at<int>(a.P, d, a.ci_off) + (int64_t(r) * a.B + row0) * k);
+        for (int v = t; v < nv4; v += THREADS) {
+          dv[v] = __ldcg(sv + v);
+          di[v] = __ldcg(si + v);
+        }
+      }
+      __threadfence_system();
+      __syncthreads();
+      if (t < S) red_release_sys_add_u32(p2p::at<uint32_t>(a.P, t, a.cnt_off) + blk, 1u);
+    } else {
+      const int blk = tk - nA;
+      if (t == 0)
+        s_ok = wait_geq_sys(p2p::at<uint32_t>(a.P, r, a.cnt_off) + blk, uint32_t(S) * a.epoch, a.status,
+                            kTimeoutPeerFlag)
+                   ? 1
+                   : 0;
+      __syncthreads();
+      if (!s_ok) continue;
+      const float* cv = p2p::at<float>(a.P, r, a.cv_off);
+      const int* ci = p2p::at<int>(a.P, r, a.ci_off);
+      for (int rr = 0; rr < XM_RB; ++rr) {
+        const int64_t row = int64_t(blk) * XM_RB + rr;
+        merge_row(cv + row * k, ci + row * k, int64_t(a.B) * k, S, k, a.n_local, r, kk, a.idx + row * k, key,
+                  gidx, hist, sh, &n_valid);
+      }
+    }
   }
 }
 
@@ -394,6 +485,53 @@ void row_topk(const torch::Tensor& H, const torch::Tensor& cmax, int64_t k_max,
       reinterpret_cast<const __nv_bfloat16*>(cmax.data_ptr()), cmax.stride(0), int(N), int(k_max),
       kd, mk, out_val.data_ptr<float>(), out_idx.data_ptr<int>(), out_val.stride(0),
       status.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Fused candidate exchange + merge (see topk_exchange_merge_kernel).  vals/idx [B, k]: this
+// rank's per-row top-k of its shard (local ids); on return idx is -1 wherever an entry missed
+// the global top-k.  `epoch` counts the launches that used these slab buffers (1, 2, ...).
+void topk_exchange_merge(const torch::Tensor& vals, const torch::Tensor& idx, int64_t n_local,
+                         const c10::optional<torch::Tensor>& k_dev, const std::vector<int64_t>& peer_bases,
+                         int64_t rank, int64_t cv_off, int64_t ci_off, int64_t cnt_off, int64_t epoch,
+                         const torch::Tensor& ticket, const torch::Tensor& status) {
+  const int64_t S = int64_t(peer_bases.size());
+  TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "topk_exchange_merge: bad group");
+  TORCH_CHECK(vals.is_contiguous() && idx.is_contiguous() && vals.scalar_type() == at::kFloat &&
+                  idx.scalar_type() == at::kInt && vals.sizes() == idx.sizes(),
+              "topk_exchange_merge: vals/idx");
+  const int64_t B = vals.size(0), k = vals.size(1);
+  TORCH_CHECK(B % topk::XM_RB == 0, "topk_exchange_merge: batch must be a multiple of 16");
+  TORCH_CHECK(cv_off % 16 == 0 && ci_off % 16 == 0, "topk_exchange_merge: offsets");
+  const size_t smem = ((size_t(S * k) * 4 + 15) & ~size_t(15)) + size_t(S * k) * 8;
+  TORCH_CHECK(smem <= 200 * 1024, "topk_exchange_merge: S*k too large for one CTA");
+  const at::cuda::CUDAGuard guard(vals.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  topk::XMergeArgs a{};
+  a.vals = vals.data_ptr<float>();
+  a.idx = idx.data_ptr<int>();
+  a.B = int(B);
+  a.k = int(k);
+  a.n_local = n_local;
+  a.k_dev = k_dev ? k_dev->data_ptr<int>() : nullptr;
+  a.P = p2p::make_peers(peer_bases, rank);
+  a.cv_off = cv_off;
+  a.ci_off = ci_off;
+  a.cnt_off = cnt_off;
+  a.epoch = uint32_t(epoch);
+  a.ticket = ticket.data_ptr<int>();
+  a.status = status.data_ptr<int>();
+  C10_CUDA_CHECK(cudaMemsetAsync(a.ticket, 0, sizeof(int), stream));
+  C10_CUDA_CHECK(cudaFuncSetAttribute(topk::topk_exchange_merge_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  int occ = 0;
+  C10_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, topk::topk_exchange_merge_kernel,
+                                                               topk::THREADS, smem));
+  int dev = 0, nsm = 0;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  C10_CUDA_CHECK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(2 * B / topk::XM_RB, int64_t(nsm) * std::max(occ, 1)));
+  topk::topk_exchange_merge_kernel<<<dim3(grid), dim3(topk::THREADS), smem, stream>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -15,8 +15,15 @@ full batch on every rank instead, as the reference's TP path does).  One step
   6. one all-reduce of [sum_b dL/dx_hat, sum_j gb_enc W_enc, grad sq-norm, loss] (2*d_in+3
      floats), then b_dec gradient, clip and Adam exactly as on one GPU
 
-The collectives here are NCCL; `saelens_b200.parallel.fused` provides the peer-memory kernels
-that fuse steps 1-2 and 4 with their compute.
+Two implementations of the exchanges share the compute kernels:
+
+* `fused=True` (default on CUDA): every exchange is a peer-memory kernel over NVLink with the
+  compute it serves: the input all-gather runs inside the tcgen05 encoder GEMM (copy warps push
+  the own rows, the TMA producer waits per m-tile), the candidate all-gather inside the merge,
+  the reduce-scatter of partial reconstructions inside the decode (with b_dec, MSE and the
+  dL/dx_hat broadcast), and the statistics all-reduce is a two-shot P2P kernel.  No NCCL call
+  runs inside a step.
+* `fused=False`: the same step with NCCL collectives between the kernels (the baseline).
 """
 
 from __future__ import annotations
@@ -27,13 +34,78 @@ import torch
 import torch.distributed as dist
 
 from saelens_b200.parallel.profiling import nccl_nvtx_range
+from saelens_b200.parallel.symm_heap import SlabBuffer, SymmetricHeap, slab_bytes_needed
 from saelens_b200.training.engine import EngineStepResult, FusedTopKEngine
+
+
+class _AllReduceBufs:
+    """Slab areas of one two-shot P2P all-reduce of `n` elements."""
+
+    def __init__(self, heap: SymmetricHeap, nat: Any, n: int, dtype: torch.dtype):
+        esz = torch.empty((), dtype=dtype).element_size()
+        land, cnt, out, flag = nat.p2p_allreduce_sizes(n, esz, heap.world)
+        self.n = n
+        self.land = heap.alloc_bytes(land)
+        self.cnt = heap.alloc_bytes(cnt)
+        self.out_buf = heap.alloc((out // esz,), dtype)
+        self.flag = heap.alloc_bytes(flag)
+        self.out = heap.local(self.out_buf)[:n]
+
+    @staticmethod
+    def nbytes(nat: Any, n: int, esz: int, world: int) -> list[int]:
+        return list(nat.p2p_allreduce_sizes(n, esz, world))
+
+
+class _FusedBufs:
+    """Peer-memory buffers of the fused TP step for one batch size (main or aux exchanges)."""
+
+    def __init__(self, group: dist.ProcessGroup, nat: Any, B: int, D: int, k: int, world: int,
+                 with_input: bool):
+        Bo = B // world
+        f4, i4, b2 = 4, 4, 2
+        sizes = []
+        if with_input:
+            sizes += [B * D * b2, (B // 128) * 4]
+        sizes += [world * B * k * f4, world * B * k * i4, (B // 16) * 4,   # candidates
+                  world * Bo * D * f4, (Bo // 16) * 4, B * D * b2, (B // 16) * 4]  # decode
+        if with_input:
+            sizes += _AllReduceBufs.nbytes(nat, 2 * D + 3, 4, world) + _AllReduceBufs.nbytes(nat, 1, 4, world)
+        heap = SymmetricHeap(group, slab_bytes_needed(sizes) + 4096)
+        self.heap = heap
+        self.B, self.Bo, self.k = B, Bo, k
+        if with_input:
+            self.x: SlabBuffer | None = heap.alloc((B, D), torch.bfloat16)
+            self.ag_flags = heap.alloc(B // 128, torch.int32)
+        else:
+            self.x = None
+        self.cv = heap.alloc((world, B, k), torch.float32)
+        self.ci = heap.alloc((world, B, k), torch.int32)
+        self.ccnt = heap.alloc(B // 16, torch.int32)
+        self.land = heap.alloc((world, Bo, D), torch.float32)
+        self.lcnt = heap.alloc(Bo // 16, torch.int32)
+        self.dx = heap.alloc((B, D), torch.bfloat16)
+        self.dcnt = heap.alloc(B // 16, torch.int32)
+        self.dx_local = heap.local(self.dx)
+        self.dcnt_local = heap.local(self.dcnt)
+        self.x_local = heap.local(self.x) if self.x is not None else None
+        if with_input:
+            self.red = _AllReduceBufs(heap, nat, 2 * D + 3, torch.float32)
+            self.dead = _AllReduceBufs(heap, nat, 1, torch.float32)
+        self.epochs: dict[str, int] = {}
+
+    def next_epoch(self, name: str) -> int:
+        e = self.epochs.get(name, 0) + 1
+        self.epochs[name] = e
+        return e
+
+    def close(self) -> None:
+        self.heap.close()
 
 
 class TPTopKEngine(FusedTopKEngine):
     def __init__(self, sae: Any, lr: float, group: dist.ProcessGroup, beta1: float = 0.9, beta2: float = 0.999,
                  eps: float = 1e-8, max_grad_norm: float = 1.0, input_layout: str = "row_sharded",
-                 h_buffer_bytes: int = 8 << 30):
+                 h_buffer_bytes: int = 8 << 30, fused: bool = True):
         if input_layout not in ("row_sharded", "replicated"):
             raise ValueError("input_layout must be 'row_sharded' or 'replicated'")
         self.group = group
@@ -44,6 +116,31 @@ class TPTopKEngine(FusedTopKEngine):
                          h_buffer_bytes=h_buffer_bytes)
         self.n_local = self.N
         self.collectives = 0
+        self.fused = bool(fused) and self.size <= 8
+        self._fb: _FusedBufs | None = None
+        self._fb_aux: _FusedBufs | None = None
+        self._ticket = torch.zeros(4, dtype=torch.int32, device=self.device)
+
+    def close(self) -> None:
+        """Release the peer-memory slabs (collective)."""
+        for b in (self._fb, self._fb_aux):
+            if b is not None:
+                b.close()
+        self._fb = self._fb_aux = None
+
+    def _fused_bufs(self, B: int) -> _FusedBufs:
+        if self._fb is None or self._fb.B != B:
+            if self._fb is not None:
+                self._fb.close()
+            self._fb = _FusedBufs(self.group, self.native, B, self.D, self.k, self.size, with_input=True)
+        return self._fb
+
+    def _fused_aux_bufs(self, B: int, k_aux: int) -> _FusedBufs:
+        if self._fb_aux is None or self._fb_aux.B != B:
+            if self._fb_aux is not None:
+                self._fb_aux.close()
+            self._fb_aux = _FusedBufs(self.group, self.native, B, self.D, k_aux, self.size, with_input=False)
+        return self._fb_aux
 
     # ------------------------------------------------------------------ helpers
     def _ag(self, out: torch.Tensor, inp: torch.Tensor, name: str) -> None:
@@ -77,6 +174,8 @@ class TPTopKEngine(FusedTopKEngine):
              want_sae_out: bool = False, act_freq: torch.Tensor | None = None,
              since_fired: torch.Tensor | None = None, run_aux: bool = False,
              update: bool = True) -> EngineStepResult:
+        if self.fused:
+            return self._step_fused(x, lr, dead_mask, want_sae_out, act_freq, since_fired, run_aux, update)
         nat, dev = self.native, self.device
         D, N, k, S = self.D, self.N, self.k, self.size
         x_own = self._local_rows(x)
@@ -197,7 +296,7 @@ class TPTopKEngine(FusedTopKEngine):
                         self.inv_scale if self.rescale else None, dX, daux, X,
                         self.p_bdec if self.apply_b_dec else None, self.w_dec, self.w_enc, self.g_dec, self.g_enc,
                         self.g_benc, bterm if self.apply_b_dec else None, sumsq, self.fire_counts, act_freq,
-                        since_fired)
+                        since_fired, idx, aux_idx if aux_on else None)
         self.launches += 3
         self._mark("latent_grad")
 
@@ -223,6 +322,159 @@ class TPTopKEngine(FusedTopKEngine):
                           True)
             self.launches += 2
             self.sumsq = sq
+            self._mark("adam")
+        self.last_loss = mse + aux_loss
+        return EngineStepResult(loss=mse + aux_loss, mse_loss=mse, aux_loss=aux_loss, sae_out=sae_out,
+                                topk_vals=vals, topk_idx=idx, fire_counts=self.fire_counts)
+
+    # ------------------------------------------------------------------ fused (peer-memory) step
+    def _step_fused(self, x: torch.Tensor, lr: float | None, dead_mask: torch.Tensor | None, want_sae_out: bool,
+                    act_freq: torch.Tensor | None, since_fired: torch.Tensor | None, run_aux: bool,
+                    update: bool) -> EngineStepResult:
+        nat, dev = self.native, self.device
+        D, N, k, S, r = self.D, self.N, self.k, self.size, self.rank
+        st, tk = self.status.tensor, self._ticket
+        x_own = self._local_rows(x)
+        xb_own = x_own if (x_own.dtype == torch.bfloat16 and x_own.is_contiguous()) else \
+            x_own.to(torch.bfloat16).contiguous()
+        Bo = xb_own.shape[0]
+        B = Bo * S
+        if Bo % 128:
+            raise ValueError(f"fused TP step needs a per-rank batch that is a multiple of 128, got {Bo}")
+        fb = self._fused_bufs(B)
+        bases = fb.heap.bases
+        ep = fb.next_epoch("main")
+        self._mark("start")
+
+        aux_on = False
+        k_aux = D // 2
+        if run_aux and dead_mask is not None:
+            nd = dead_mask.to(torch.bool).sum().to(torch.float32).reshape(1)
+            nat.p2p_allreduce(nd, 1.0, bases, r, fb.dead.land, fb.dead.cnt, fb.dead.out_buf.offset, fb.dead.flag,
+                              fb.next_epoch("dead"), tk, st)
+            self.launches += 1
+            num_dead_total = int(fb.dead.out.item())
+            aux_on = num_dead_total > 0
+
+        # 1-2. all-gather fused encoder GEMM + local top-k
+        R = self._row_chunk(B)
+        H = torch.empty(min(R, B), N, dtype=torch.bfloat16, device=dev)
+        cm = torch.empty(min(R, B), N // 32, dtype=torch.bfloat16, device=dev)
+        vals = torch.empty(B, k, dtype=torch.float32, device=dev)
+        idx = torch.empty(B, k, dtype=torch.int32, device=dev)
+        if aux_on:
+            assert dead_mask is not None
+            dm = dead_mask.to(torch.bool)
+            k_aux_total = min(k_aux, num_dead_total)
+            k_aux_dev = torch.tensor([k_aux_total], dtype=torch.int32, device=dev)
+            aux_scale = min(num_dead_total / k_aux, 1.0)
+            bits = dm.view(N // 32, 32).to(torch.int64) << torch.arange(32, device=dev, dtype=torch.int64)
+            w = bits.sum(1)
+            mask_words = torch.where(w >= 2**31, w - 2**32, w).to(torch.int32).contiguous()
+            local_dead = min(int(dm.sum().item()), k_aux_total)
+            aux_vals = torch.empty(B, k_aux, dtype=torch.float32, device=dev)
+            aux_idx = torch.empty(B, k_aux, dtype=torch.int32, device=dev)
+            k_loc_dev = torch.tensor([local_dead], dtype=torch.int32, device=dev)
+        assert fb.x is not None
+        for r0 in range(0, B, R):
+            r1 = min(B, r0 + R)
+            h, c = H[: r1 - r0], cm[: r1 - r0]
+            nat.gemm_ag_tn_bf16(xb_own, bases, r, fb.x.offset, fb.ag_flags.offset, B, r0, r1 - r0, r0 == 0, ep,
+                                self.w_enc, self.bias_eff, self.scale if self.rescale else None, False, h, c, st,
+                                tk, 0)
+            self._mark("ag_encoder_gemm")
+            nat.row_topk(h, c, k, None, None, vals[r0:r1], idx[r0:r1], st)
+            self._mark("row_topk")
+            self.launches += 2
+            if aux_on:
+                nat.row_topk(h, c, k_aux, k_loc_dev, mask_words, aux_vals[r0:r1], aux_idx[r0:r1], st)
+                self.launches += 1
+        del H, cm
+        X = fb.x_local
+
+        # 3. candidate all-gather fused with the global merge
+        nat.topk_exchange_merge(vals, idx, self.n_local, None, bases, r, fb.cv.offset, fb.ci.offset,
+                                fb.ccnt.offset, ep, tk, st)
+        self.launches += 1
+        if aux_on:
+            fa = self._fused_aux_bufs(B, k_aux)
+            ep_aux = fa.next_epoch("aux")
+            nat.topk_exchange_merge(aux_vals, aux_idx, self.n_local, k_aux_dev, fa.heap.bases, r, fa.cv.offset,
+                                    fa.ci.offset, fa.ccnt.offset, ep_aux, tk, st)
+            self.launches += 1
+        self._mark("topk_exchange_merge")
+
+        # 4. decode fused with the reduce-scatter, b_dec, MSE and the dL/dx_hat all-gather
+        sae_out = torch.empty(Bo, D, dtype=torch.bfloat16, device=dev) if (want_sae_out or aux_on) else None
+        resid = torch.empty(Bo, D, dtype=torch.bfloat16, device=dev) if aux_on else None
+        loss_row = torch.empty(Bo, dtype=torch.float32, device=dev)
+        red = torch.zeros(2 * D + 3, dtype=torch.float32, device=dev)  # [bsum | bterm | sumsq | mse | aux]
+        bsum, bterm = red[:D], red[D : 2 * D]
+        nat.decode_rs(vals, idx, True, self.inv_scale if self.rescale else None, self.w_dec, bases, r,
+                      fb.land.offset, fb.lcnt.offset, fb.dx.offset, fb.dcnt.offset, ep, self.p_bdec, xb_own,
+                      sae_out, resid, None, 2.0 / B, loss_row, bsum, tk, st)
+        self.launches += 1
+        daux = None
+        if aux_on:
+            assert resid is not None
+            aux_row = torch.empty(Bo, dtype=torch.float32, device=dev)
+            nat.decode_rs(aux_vals, aux_idx, False, self.inv_scale if self.rescale else None, self.w_dec,
+                          fa.heap.bases, r, fa.land.offset, fa.lcnt.offset, fa.dx.offset, fa.dcnt.offset, ep_aux,
+                          None, resid, None, None, None, 2.0 * self.aux_coef * aux_scale / B, aux_row, None, tk, st)
+            self.launches += 1
+            red[2 * D + 2] = aux_row.sum()
+            daux = fa.dx_local
+        self._mark("decode_reduce_scatter_mse")
+
+        # 5. CSC + local latent gradients (after every rank's dL/dx_hat rows arrived)
+        nat.p2p_wait_flags(fb.dcnt_local, ep, st)
+        self.launches += 1
+        if aux_on:
+            nat.p2p_wait_flags(fa.dcnt_local, ep_aux, st)
+            self.launches += 1
+        dX = fb.dx_local
+        self.counts.zero_()
+        self.fire_counts.zero_()
+        self.cursor.zero_()
+        nat.csc_count(vals, idx, aux_vals if aux_on else None, aux_idx if aux_on else None, self.counts,
+                      self.fire_counts)
+        torch.cumsum(self.counts, 0, out=self.colptr[1:])
+        pairs = torch.empty(B * k + (B * k_aux if aux_on else 0), dtype=torch.int64, device=dev)
+        nat.csc_fill(vals, idx, aux_vals if aux_on else None, aux_idx if aux_on else None, self.colptr,
+                     self.cursor, pairs)
+        self._mark("csc_build")
+        sumsq = red[2 * D : 2 * D + 1]
+        nat.latent_grad(self.colptr, pairs, vals, aux_vals if aux_on else None,
+                        self.inv_scale if self.rescale else None, dX, daux, X,
+                        self.p_bdec if self.apply_b_dec else None, self.w_dec, self.w_enc, self.g_dec, self.g_enc,
+                        self.g_benc, bterm if self.apply_b_dec else None, sumsq, self.fire_counts, act_freq,
+                        since_fired, idx, aux_idx if aux_on else None)
+        self.launches += 3
+        self._mark("latent_grad")
+
+        # 6. one P2P all-reduce for b_dec grad terms, grad norm and losses
+        red[2 * D + 1] = loss_row.sum()
+        nat.p2p_allreduce(red, 1.0, bases, r, fb.red.land, fb.red.cnt, fb.red.out_buf.offset, fb.red.flag, ep,
+                          tk, st)
+        self.launches += 1
+        red = fb.red.out
+        self._mark("grad_all_reduce")
+        mse = red[2 * D + 1] / B
+        aux_loss = (self.aux_coef * aux_scale * red[2 * D + 2] / B) if aux_on else torch.zeros((), device=dev)
+        if update:
+            self.step_count += 1
+            cur_lr = self.lr if lr is None else lr
+            sq = red[2 * D : 2 * D + 1]
+            nat.adam_bdec(red[:D], red[D : 2 * D] if self.apply_b_dec else None, self.g_bdec, sq, self.clip,
+                          self.p_bdec, self.m_bdec, self.v_bdec, cur_lr, self.beta1, self.beta2, self.eps,
+                          self.step_count, self.max_grad_norm, True)
+            nat.adam_rows(self.p_dec, self.m_dec, self.v_dec, self.p_enc, self.m_enc, self.v_enc, self.w_dec,
+                          self.w_enc, self.g_dec, self.g_enc, self.p_benc, self.m_benc, self.v_benc, self.g_benc,
+                          self.colptr, self.clip, self.p_bdec if self.apply_b_dec else None, self.scale,
+                          self.inv_scale, self.bias_eff, cur_lr, self.beta1, self.beta2, self.eps, self.step_count,
+                          True)
+            self.launches += 2
+            self.sumsq = sq.clone()  # the slab area is rewritten by the next step
             self._mark("adam")
         self.last_loss = mse + aux_loss
         return EngineStepResult(loss=mse + aux_loss, mse_loss=mse, aux_loss=aux_loss, sae_out=sae_out,

@@ -25,6 +25,7 @@ class BenchSetup:
     world: int
     rank: int
     lr: float = 5e-5
+    tp_exchange: str = "p2p"  # "p2p": fused NVLink kernels; "nccl": NCCL collectives between kernels
 
 
 def _build_sae(s: BenchSetup) -> Any:
@@ -74,7 +75,7 @@ def _make_engine(s: BenchSetup) -> Any:
         return FusedTopKEngine(sae, lr=s.lr)
     from saelens_b200.parallel.tp_engine import TPTopKEngine
 
-    return TPTopKEngine(sae, lr=s.lr, group=dist.group.WORLD)
+    return TPTopKEngine(sae, lr=s.lr, group=dist.group.WORLD, fused=s.tp_exchange == "p2p")
 
 
 def _free(*objs: Any) -> None:
@@ -127,6 +128,8 @@ def run_device_timed(s: BenchSetup, steps: int, warmup: int, sampler: Any = None
     launches = (eng.launches - launches0) // max(steps, 1)
     out = {"ms_per_step": ms, "gpu_launches": int(launches * steps), "clocks": clocks,
            "loss": float(eng.last_loss) if getattr(eng, "last_loss", None) is not None else None}
+    if hasattr(eng, "close"):
+        eng.close()
     del eng, xs
     _free()
     return out
@@ -167,6 +170,7 @@ def run_e2e(s: BenchSetup, steps: int, warmup: int) -> dict[str, Any]:
         lr_scheduler_name="constant", lr_warm_up_steps=0, adam_beta1=0.9, adam_beta2=0.999, lr_decay_steps=0,
         n_restart_cycles=1, train_batch_size_samples=s.batch, dead_feature_window=1000,
         feature_sampling_window=2000, logger=LoggingConfig(log_to_wandb=False), sae_engine="native",
+        tp_exchange=s.tp_exchange,
     )
     data = PinnedBatches(local)
     trainer = SAETrainer(cfg, sae, data, tp_input_layout="row_sharded")
@@ -182,6 +186,8 @@ def run_e2e(s: BenchSetup, steps: int, warmup: int) -> dict[str, Any]:
     _barrier(s.world)
     ms = _max_over_ranks(t0.elapsed_time(t1) / steps, s.world)
     h2d = rows_local * s.d_in * 2
+    if hasattr(trainer.engine, "close"):
+        trainer.engine.close()
     del trainer, sae, data
     _free()
     return {"ms_per_step": ms, "h2d_bytes": h2d, "d2h_bytes": 4}

@@ -181,6 +181,9 @@ class FusedTopKEngine:
         self.p_bdec.copy_(b_dec)
         self.refresh()
 
+    def close(self) -> None:
+        """Release resources shared with other ranks (none on one GPU)."""
+
     def _mark(self, name: str) -> None:
         if self._phase_timing:
             ev = torch.cuda.Event(enable_timing=True)
@@ -307,7 +310,7 @@ class FusedTopKEngine:
                         self.inv_scale if self.rescale else None, dxhat, daux, xb,
                         self.p_bdec if self.apply_b_dec else None, self.w_dec, self.w_enc, self.g_dec,
                         self.g_enc, self.g_benc, bterm if self.apply_b_dec else None, self.sumsq,
-                        self.fire_counts, act_freq, since_fired)
+                        self.fire_counts, act_freq, since_fired, idx, aux_idx if aux_on else None)
         self.launches += 3
         self._mark("latent_grad")
 

@@ -155,7 +155,8 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
                 from saelens_b200.parallel.tp_engine import TPTopKEngine
 
                 self.engine = TPTopKEngine(self._base_sae, lr=cfg.lr, group=tp_group, beta1=cfg.adam_beta1,
-                                           beta2=cfg.adam_beta2, input_layout=tp_input_layout)
+                                           beta2=cfg.adam_beta2, input_layout=tp_input_layout,
+                                           fused=getattr(cfg, "tp_exchange", "p2p") == "p2p")
             elif engine_supported(self._base_sae):
                 self.engine = FusedTopKEngine(self._base_sae, lr=cfg.lr, beta1=cfg.adam_beta1,
                                               beta2=cfg.adam_beta2)

@@ -1,4 +1,5 @@
-"""Tensor-parallel native step (2 ranks over NCCL) against the single-GPU native step."""
+"""Tensor-parallel native step (2 ranks; fused NVLink kernels or NCCL exchanges) against the
+single-GPU native step, with and without the dead-latent aux loss."""
 
 import os
 import socket
@@ -28,7 +29,11 @@ def _build(d_in, d_sae, k, device):
     return sae
 
 
-def _worker(rank, world, port, d_in, d_sae, k, B, out_dir):
+def _dead_mask(d_sae, device):
+    return (torch.arange(d_sae, device=device) % 3) == 0
+
+
+def _worker(rank, world, port, d_in, d_sae, k, B, out_dir, exchange):
     import torch.distributed as dist
     from datetime import timedelta
 
@@ -40,15 +45,19 @@ def _worker(rank, world, port, d_in, d_sae, k, B, out_dir):
 
     sae = _build(d_in, d_sae, k, f"cuda:{rank}")
     sae.shard_weights(dist.group.WORLD)
-    eng = TPTopKEngine(sae, lr=1e-3, group=dist.group.WORLD)
+    eng = TPTopKEngine(sae, lr=1e-3, group=dist.group.WORLD, fused=exchange == "p2p")
     g = torch.Generator(device="cpu").manual_seed(11)
     x = torch.randn(B, d_in, generator=g).to(torch.bfloat16)
     rows = x[rank * (B // world) : (rank + 1) * (B // world)].cuda()
+    n = d_sae // world
+    dead = _dead_mask(d_sae, f"cuda:{rank}")[rank * n : (rank + 1) * n]
     losses = []
-    for _ in range(3):
-        losses.append(float(eng.step(rows).loss))
+    for i in range(5):
+        res = eng.step(rows, dead_mask=dead, run_aux=(i == 2))
+        losses.append(float(res.loss))
     torch.cuda.synchronize()
     eng.status.check()
+    eng.close()
     torch.save({"losses": losses, "p_dec": eng.p_dec.cpu(), "p_enc": eng.p_enc.cpu(), "p_bdec": eng.p_bdec.cpu()},
                os.path.join(out_dir, f"rank{rank}.pt"))
     dist.barrier()
@@ -56,24 +65,36 @@ def _worker(rank, world, port, d_in, d_sae, k, B, out_dir):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp2_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
+def test_tp2_matches_single_gpu(tmp_path, exchange):
     import torch.multiprocessing as mp
 
     from saelens_b200.training.engine import FusedTopKEngine
 
     d_in, d_sae, k, B = 256, 2048, 32, 512
-    mp.spawn(_worker, args=(2, _free_port(), d_in, d_sae, k, B, str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _free_port(), d_in, d_sae, k, B, str(tmp_path), exchange), nprocs=2, join=True)
     sae = _build(d_in, d_sae, k, "cuda:0")
     eng = FusedTopKEngine(sae, lr=1e-3)
     g = torch.Generator(device="cpu").manual_seed(11)
     x = torch.randn(B, d_in, generator=g).to(torch.bfloat16).cuda()
-    ref_losses = [float(eng.step(x).loss) for _ in range(3)]
+    dead = _dead_mask(d_sae, "cuda:0")
+    ref_losses = [float(eng.step(x, dead_mask=dead, run_aux=(i == 2)).loss) for i in range(5)]
     r = [torch.load(tmp_path / f"rank{i}.pt") for i in range(2)]
     for a, b in zip(r[0]["losses"], ref_losses):
         assert abs(a - b) <= 1e-3 * abs(b), (r[0]["losses"], ref_losses)
     assert r[0]["losses"] == r[1]["losses"]
     n = d_sae // 2
+
+    def close(got, want, name):
+        # Adam normalises every coordinate, so a gradient that differs in its last bits (the TP
+        # step sums partial reconstructions and gradient pairs in another order) can move a
+        # near-zero coordinate by up to lr per step; everything else must agree tightly.
+        d = (got - want).abs()
+        bad = d > (2e-5 + 1e-3 * want.abs())
+        frac = bad.float().mean().item()
+        assert d.max().item() <= 5 * 1e-3 and frac < 2e-3, (name, d.max().item(), frac)
+
     for i in range(2):
-        assert torch.allclose(r[i]["p_dec"], eng.p_dec[i * n : (i + 1) * n].cpu(), atol=2e-5, rtol=1e-3)
-        assert torch.allclose(r[i]["p_enc"], eng.p_enc[i * n : (i + 1) * n].cpu(), atol=2e-5, rtol=1e-3)
-        assert torch.allclose(r[i]["p_bdec"], eng.p_bdec.cpu(), atol=2e-5, rtol=1e-3)
+        close(r[i]["p_dec"], eng.p_dec[i * n : (i + 1) * n].cpu(), f"p_dec{i}")
+        close(r[i]["p_enc"], eng.p_enc[i * n : (i + 1) * n].cpu(), f"p_enc{i}")
+        close(r[i]["p_bdec"], eng.p_bdec.cpu(), f"p_bdec{i}")
