@@ -35,7 +35,7 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
                  const c10::optional<torch::Tensor>& fire_counts,
                  const c10::optional<torch::Tensor>& act_freq,
                  const c10::optional<torch::Tensor>& since_fired, const torch::Tensor& idx,
-                 const c10::optional<torch::Tensor>& aux_idx);
+                 const c10::optional<torch::Tensor>& aux_idx, int64_t j0, int64_t j1, bool zero_empty);
 void adam_bdec(const c10::optional<torch::Tensor>& bsum, const c10::optional<torch::Tensor>& bterm,
                const torch::Tensor& gb_dec, const c10::optional<torch::Tensor>& sumsq,
                const c10::optional<torch::Tensor>& clip_out, const torch::Tensor& p, const torch::Tensor& m,
@@ -81,13 +81,20 @@ void topk_exchange_merge(const torch::Tensor& vals, const torch::Tensor& idx, in
 std::vector<int64_t> p2p_allreduce_sizes(int64_t n, int64_t elem_bytes, int64_t world);
 void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64_t>& peer_bases, int64_t rank,
                    int64_t land_off, int64_t cnt_off, int64_t out_off, int64_t flag_off, int64_t epoch,
-                   const torch::Tensor& ticket, const torch::Tensor& status);
+                   const torch::Tensor& ticket, const torch::Tensor& status, int64_t sq_off);
 void p2p_wait_flags(const torch::Tensor& flags, int64_t target, const torch::Tensor& status);
 std::tuple<int64_t, torch::Tensor> symm_alloc(int64_t nbytes);
 int64_t symm_open(const torch::Tensor& handle);
 void symm_close(int64_t addr);
 void symm_free(int64_t addr);
 torch::Tensor tensor_at(int64_t addr, std::vector<int64_t> sizes, torch::ScalarType dtype, int64_t device);
+void p2p_route_rows(const torch::Tensor& src, const torch::Tensor& routes, const std::vector<int64_t>& peer_bases,
+                    int64_t rank, int64_t land_off, int64_t rows_cap, int64_t slot, int64_t cnt_off,
+                    int64_t cnt_slot, int64_t free_off, const std::vector<int64_t>& free_slots, int64_t mode,
+                    double scale, int64_t epoch, const torch::Tensor& status);
+void p2p_wait_targets(const torch::Tensor& counters, const torch::Tensor& targets, const torch::Tensor& status);
+void p2p_signal(const std::vector<int64_t>& peer_bases, int64_t rank, int64_t off, int64_t index,
+                int64_t rank_mask, int64_t value);
 }  // namespace sb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -97,7 +104,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_mse", &sb::decode_mse);
   m.def("csc_count", &sb::csc_count);
   m.def("csc_fill", &sb::csc_fill);
-  m.def("latent_grad", &sb::latent_grad);
+  m.def("latent_grad", &sb::latent_grad, py::arg("colptr"), py::arg("pairs"), py::arg("vals"), py::arg("aux_vals"),
+        py::arg("inv_scale"), py::arg("dxhat"), py::arg("daux"), py::arg("x"), py::arg("b_dec"), py::arg("W_dec"),
+        py::arg("W_enc"), py::arg("gW_dec"), py::arg("gW_enc"), py::arg("gb_enc"), py::arg("bterm"),
+        py::arg("sumsq"), py::arg("fire_counts"), py::arg("act_freq"), py::arg("since_fired"), py::arg("idx"),
+        py::arg("aux_idx"), py::arg("j0") = 0, py::arg("j1") = -1, py::arg("zero_empty") = false);
   m.def("adam_bdec", &sb::adam_bdec);
   m.def("adam_rows", &sb::adam_rows);
   m.def("topk_merge", &sb::topk_merge);
@@ -107,8 +118,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_rs", &sb::decode_rs);
   m.def("topk_exchange_merge", &sb::topk_exchange_merge);
   m.def("p2p_allreduce_sizes", &sb::p2p_allreduce_sizes);
-  m.def("p2p_allreduce", &sb::p2p_allreduce);
+  m.def("p2p_allreduce", &sb::p2p_allreduce, py::arg("x"), py::arg("scale"), py::arg("peer_bases"),
+        py::arg("rank"), py::arg("land_off"), py::arg("cnt_off"), py::arg("out_off"), py::arg("flag_off"),
+        py::arg("epoch"), py::arg("ticket"), py::arg("status"), py::arg("sq_off") = -1);
   m.def("p2p_wait_flags", &sb::p2p_wait_flags);
+  m.def("p2p_route_rows", &sb::p2p_route_rows);
+  m.def("p2p_wait_targets", &sb::p2p_wait_targets);
+  m.def("p2p_signal", &sb::p2p_signal);
   m.def("symm_alloc", &sb::symm_alloc);
   m.def("symm_open", &sb::symm_open);
   m.def("symm_close", &sb::symm_close);

@@ -55,6 +55,7 @@ struct ArArgs {
   int64_t cnt_off;   // u32 [nch]
   int64_t out_off;   // T [nch * CHUNK]
   int64_t flag_off;  // u32 [nch]
+  int64_t sq_off;    // fp32 [nch]: per-chunk sum of squares of the result, on every rank (< 0: none)
   uint32_t epoch;
   int* ticket;
   int* status;
@@ -63,6 +64,7 @@ struct ArArgs {
 template <class T>
 __global__ void __launch_bounds__(AR_THREADS) allreduce_kernel(const __grid_constant__ ArArgs a) {
   __shared__ int s_tk, s_ok;
+  __shared__ float s_red[AR_THREADS / 32];
   const int t = threadIdx.x;
   const int S = a.P.world, r = a.P.rank;
   const int64_t nch = (a.n + AR_CHUNK - 1) / AR_CHUNK;
@@ -103,11 +105,25 @@ __global__ void __launch_bounds__(AR_THREADS) allreduce_kernel(const __grid_cons
       const int64_t e0 = c * AR_CHUNK;
       const int64_t len = min(int64_t(AR_CHUNK), a.n - e0);
       const T* land = at<T>(a.P, r, a.land_off) + (c / S) * AR_CHUNK;
+      float sq = 0.f;
       for (int64_t e = t; e < len; e += AR_THREADS) {
         float acc = 0.f;
         for (int s = 0; s < S; ++s) acc += Elt<T>::ld(land + int64_t(s) * per_owner * AR_CHUNK + e);
         const T v = Elt<T>::from_f(acc * a.scale);
+        const float vr = Elt<T>::to_f(v);
+        sq += vr * vr;
         for (int d = 0; d < S; ++d) at<T>(a.P, (r + d) % S, a.out_off)[e0 + e] = v;
+      }
+      if (a.sq_off >= 0) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        if ((t & 31) == 0) s_red[t >> 5] = sq;
+        __syncthreads();
+        if (t == 0) {
+          float tot = 0.f;
+          for (int w = 0; w < AR_THREADS / 32; ++w) tot += s_red[w];
+          for (int d = 0; d < S; ++d) at<float>(a.P, d, a.sq_off)[c] = tot;
+        }
       }
       __threadfence_system();
       __syncthreads();
@@ -124,6 +140,147 @@ __global__ void wait_flags_kernel(const uint32_t* flags, int64_t n, uint32_t tar
     wait_geq_sys(flags + i, target, status, kTimeoutPeerFlag);
 }
 
+
+// ---------------------------------------------------------------------------------------
+// Row routing: the producer-to-consumer all-to-all of activation rows (shard routing), with the
+// activation normalisation and the bf16 cast fused into the NVLink stores.  Each route sends a
+// contiguous run of the producer's rows to a row offset of one consumer's landing buffer (in
+// that consumer's slab, slot `slot` of a double buffer).  CTAs take RR-row chunks; after a chunk
+// a release-add on the consumer's arrival counter for this producer publishes it.  Before
+// writing slot s for epoch e >= 3 the kernel waits (bounded) until every destination consumer
+// released epoch e - 2, which used the same slot.
+// Normalisation: mode 0 none, 1 multiply by `scale`, 2 rescale every row to L2 norm `scale`.
+// Reference path replaced: NCCL batch_isend_irecv per route + cast/normalise passes
+// (sae_lens/training/activations_store.py:1482-1606, 1063; activation_scaler.py:16-23).
+// ---------------------------------------------------------------------------------------
+constexpr int RT_THREADS = 128;
+constexpr int RT_RR = 8;
+constexpr int RT_MAX_ROUTES = 16;
+constexpr int RT_U = 8;  // vectors of 8 per thread: rows up to 8 * 8 * RT_THREADS = 8192 wide
+
+struct RouteArgs {
+  const void* src;
+  int src_f32;
+  int64_t ld_src;
+  int D;
+  int n_routes;
+  int r_src[RT_MAX_ROUTES];    // first source row
+  int r_rows[RT_MAX_ROUTES];   // rows
+  int r_rank[RT_MAX_ROUTES];   // destination rank
+  int r_dst[RT_MAX_ROUTES];    // first destination row in the consumer's landing slot
+  int r_chunk0[RT_MAX_ROUTES + 1];
+  Peers P;
+  int64_t land_off;       // bf16 [2][rows_cap][D] on every consumer
+  int64_t rows_cap;
+  int slot;
+  int64_t cnt_off;        // u32 [n_producer_slots] on every consumer
+  int cnt_slot;           // this producer's counter index on the consumers
+  int64_t free_off;       // u32 [n_consumer_slots] on every producer: last epoch each consumer released
+  int free_slot[RT_MAX_ROUTES];
+  int mode;
+  float scale;
+  uint32_t epoch;
+  int* status;
+};
+
+__global__ void __launch_bounds__(RT_THREADS) route_rows_kernel(const __grid_constant__ RouteArgs a) {
+  __shared__ float s_red[RT_THREADS / 32];
+  __shared__ int s_ok;
+  const int t = threadIdx.x;
+  const int nvec = a.D >> 3;
+  if (a.epoch >= 3) {
+    if (t == 0) {
+      bool ok = true;
+      for (int i = 0; i < a.n_routes && ok; ++i)
+        ok = wait_geq_sys(at<uint32_t>(a.P, a.P.rank, a.free_off) + a.free_slot[i], a.epoch - 2, a.status,
+                          kTimeoutPeerFlag);
+      s_ok = ok ? 1 : 0;
+    }
+    __syncthreads();
+    if (!s_ok) return;
+  }
+  const int nchunks = a.r_chunk0[a.n_routes];
+  for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    int ri = 0;
+    while (c >= a.r_chunk0[ri + 1]) ++ri;
+    const int row0 = (c - a.r_chunk0[ri]) * RT_RR;
+    const int nr = min(RT_RR, a.r_rows[ri] - row0);
+    const int dst_rank = a.r_rank[ri];
+    __nv_bfloat16* land = at<__nv_bfloat16>(a.P, dst_rank, a.land_off) + (int64_t(a.slot) * a.rows_cap) * a.D;
+    for (int rr = 0; rr < nr; ++rr) {
+      const int64_t srow = a.r_src[ri] + row0 + rr;
+      const int64_t drow = a.r_dst[ri] + row0 + rr;
+      float v[8 * RT_U];  // the row, 8 elements per vector, RT_U vectors per thread
+      float ss = 0.f;
+#pragma unroll
+      for (int u = 0; u < RT_U; ++u) {
+        const int vi = u * RT_THREADS + t;
+        if (vi < nvec) {
+          if (a.src_f32) {
+            const float4* s4 =
+                reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.src) + srow * a.ld_src) + 2 * vi;
+            const float4 x0 = __ldg(s4), x1 = __ldg(s4 + 1);
+            v[8 * u + 0] = x0.x; v[8 * u + 1] = x0.y; v[8 * u + 2] = x0.z; v[8 * u + 3] = x0.w;
+            v[8 * u + 4] = x1.x; v[8 * u + 5] = x1.y; v[8 * u + 6] = x1.z; v[8 * u + 7] = x1.w;
+          } else {
+            const uint4 q = __ldg(
+                reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.src) + srow * a.ld_src) + vi);
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&q);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __bfloat1622float2(h[e]);
+              v[8 * u + 2 * e] = f.x;
+              v[8 * u + 2 * e + 1] = f.y;
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ss += v[8 * u + e] * v[8 * u + e];
+        }
+      }
+      float mul = a.mode == 1 ? a.scale : 1.f;
+      if (a.mode == 2) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if ((t & 31) == 0) s_red[t >> 5] = ss;
+        __syncthreads();
+        float tot = 0.f;
+        for (int w = 0; w < RT_THREADS / 32; ++w) tot += s_red[w];
+        __syncthreads();
+        mul = tot > 0.f ? a.scale * rsqrtf(tot) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < RT_U; ++u) {
+        const int vi = u * RT_THREADS + t;
+        if (vi < nvec) {
+          uint4 q;
+          uint32_t* w = reinterpret_cast<uint32_t*>(&q);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * u + 2 * e] * mul, v[8 * u + 2 * e + 1] * mul);
+            w[e] = *reinterpret_cast<uint32_t*>(&h);
+          }
+          reinterpret_cast<uint4*>(land + drow * a.D)[vi] = q;
+        }
+      }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (t == 0) red_release_sys_add_u32(at<uint32_t>(a.P, dst_rank, a.cnt_off) + a.cnt_slot, 1u);
+  }
+}
+
+__global__ void wait_targets_kernel(const uint32_t* counters, const int64_t* targets, int n, int* status) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    wait_geq_sys(counters + i, uint32_t(targets[i]), status, kTimeoutPeerFlag);
+}
+
+__global__ void signal_kernel(Peers P, int64_t off, int index, int n_ranks_mask, uint32_t value) {
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int r = 0; r < P.world; ++r)
+      if (n_ranks_mask & (1 << r)) st_release_sys_u32(at<uint32_t>(P, r, off) + index, value);
+  }
+}
 }  // namespace p2p
 
 static int p2p_sm_count() {
@@ -143,9 +300,11 @@ std::vector<int64_t> p2p_allreduce_sizes(int64_t n, int64_t elem_bytes, int64_t 
 
 // Sum `x` (fp32 or bf16, [n]) over the group, times `scale`; the result lands in the `out` area
 // of every rank's slab (offset out_off, same dtype).  Offsets are those of p2p_allreduce_sizes.
+// With sq_off >= 0, every rank also receives the sum of squares of each result chunk (fp32
+// [nch] at sq_off), e.g. for the norm of an averaged gradient.
 void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64_t>& peer_bases, int64_t rank,
                    int64_t land_off, int64_t cnt_off, int64_t out_off, int64_t flag_off, int64_t epoch,
-                   const torch::Tensor& ticket, const torch::Tensor& status) {
+                   const torch::Tensor& ticket, const torch::Tensor& status, int64_t sq_off) {
   const int64_t S = int64_t(peer_bases.size());
   TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "p2p_allreduce: bad group");
   TORCH_CHECK(x.is_cuda() && x.is_contiguous() && (x.scalar_type() == at::kFloat || x.scalar_type() == at::kBFloat16),
@@ -164,6 +323,7 @@ void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64
   a.cnt_off = cnt_off;
   a.out_off = out_off;
   a.flag_off = flag_off;
+  a.sq_off = sq_off;
   a.epoch = uint32_t(epoch);
   a.ticket = ticket.data_ptr<int>();
   a.status = status.data_ptr<int>();
@@ -186,6 +346,86 @@ void p2p_wait_flags(const torch::Tensor& flags, int64_t target, const torch::Ten
   const int64_t grid = std::min<int64_t>((n + 255) / 256, 64);
   p2p::wait_flags_kernel<<<dim3(grid), dim3(256), 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const uint32_t*>(flags.data_ptr<int>()), n, uint32_t(target), status.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Route rows of `src` ([rows, D] fp32 or bf16) to consumers: routes = int64 [n, 4] rows of
+// (first source row, rows, destination rank, first destination row).  Writes bf16 rows into slot
+// `slot` of each consumer's landing area (land_off, capacity rows_cap) and counts RR-row chunks
+// on counter `cnt_slot` at cnt_off of the consumer.  free_slots[i] is the index, in this rank's
+// free flags at free_off, of route i's consumer.
+void p2p_route_rows(const torch::Tensor& src, const torch::Tensor& routes, const std::vector<int64_t>& peer_bases,
+                    int64_t rank, int64_t land_off, int64_t rows_cap, int64_t slot, int64_t cnt_off,
+                    int64_t cnt_slot, int64_t free_off, const std::vector<int64_t>& free_slots, int64_t mode,
+                    double scale, int64_t epoch, const torch::Tensor& status) {
+  TORCH_CHECK(src.is_cuda() && src.dim() == 2 && src.stride(1) == 1 &&
+                  (src.scalar_type() == at::kFloat || src.scalar_type() == at::kBFloat16),
+              "p2p_route_rows: src must be a CUDA fp32/bf16 matrix with contiguous rows");
+  TORCH_CHECK(routes.device().is_cpu() && routes.scalar_type() == at::kLong && routes.dim() == 2 &&
+                  routes.size(1) == 4 && routes.size(0) <= p2p::RT_MAX_ROUTES,
+              "p2p_route_rows: routes must be a CPU int64 [n <= 16, 4] table");
+  const int64_t D = src.size(1);
+  TORCH_CHECK(D % 8 == 0 && D <= p2p::RT_U * 8 * p2p::RT_THREADS,
+              "p2p_route_rows: d must be a multiple of 8 and <= 8192");
+  TORCH_CHECK(mode >= 0 && mode <= 2, "p2p_route_rows: mode");
+  TORCH_CHECK(int64_t(free_slots.size()) == routes.size(0), "p2p_route_rows: free_slots");
+  const at::cuda::CUDAGuard guard(src.device());
+  p2p::RouteArgs a{};
+  a.src = src.data_ptr();
+  a.src_f32 = src.scalar_type() == at::kFloat ? 1 : 0;
+  a.ld_src = src.stride(0);
+  a.D = int(D);
+  a.n_routes = int(routes.size(0));
+  auto R = routes.accessor<int64_t, 2>();
+  int chunks = 0;
+  for (int i = 0; i < a.n_routes; ++i) {
+    a.r_src[i] = int(R[i][0]);
+    a.r_rows[i] = int(R[i][1]);
+    a.r_rank[i] = int(R[i][2]);
+    a.r_dst[i] = int(R[i][3]);
+    TORCH_CHECK(R[i][0] >= 0 && R[i][0] + R[i][1] <= src.size(0) && R[i][3] >= 0 && R[i][3] + R[i][1] <= rows_cap &&
+                    R[i][2] >= 0 && R[i][2] < int64_t(peer_bases.size()),
+                "p2p_route_rows: route ", i, " out of range");
+    a.r_chunk0[i] = chunks;
+    chunks += int((R[i][1] + p2p::RT_RR - 1) / p2p::RT_RR);
+    a.free_slot[i] = int(free_slots[i]);
+  }
+  a.r_chunk0[a.n_routes] = chunks;
+  a.P = p2p::make_peers(peer_bases, rank);
+  a.land_off = land_off;
+  a.rows_cap = rows_cap;
+  a.slot = int(slot);
+  a.cnt_off = cnt_off;
+  a.cnt_slot = int(cnt_slot);
+  a.free_off = free_off;
+  a.mode = int(mode);
+  a.scale = float(scale);
+  a.epoch = uint32_t(epoch);
+  a.status = status.data_ptr<int>();
+  if (chunks == 0) return;
+  const int grid = std::min(chunks, p2p_sm_count() * 4);
+  p2p::route_rows_kernel<<<dim3(grid), dim3(p2p::RT_THREADS), 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Wait (bounded, stream-ordered) until counters[i] >= targets[i] (targets: CUDA int64).
+void p2p_wait_targets(const torch::Tensor& counters, const torch::Tensor& targets, const torch::Tensor& status) {
+  TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && targets.is_cuda() &&
+                  targets.scalar_type() == at::kLong && targets.numel() <= counters.numel(),
+              "p2p_wait_targets");
+  const at::cuda::CUDAGuard guard(counters.device());
+  p2p::wait_targets_kernel<<<1, 64, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const uint32_t*>(counters.data_ptr<int>()), targets.data_ptr<int64_t>(),
+      int(targets.numel()), status.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Stream-ordered release store of `value` into flag `index` at `off` of every rank in rank_mask.
+void p2p_signal(const std::vector<int64_t>& peer_bases, int64_t rank, int64_t off, int64_t index,
+                int64_t rank_mask, int64_t value) {
+  p2p::Peers P = p2p::make_peers(peer_bases, rank);
+  p2p::signal_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(P, off, int(index), int(rank_mask),
+                                                                       uint32_t(value));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

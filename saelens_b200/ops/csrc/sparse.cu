@@ -811,7 +811,8 @@ constexpr int LR_WARPS = LR_THREADS / 32;
 
 struct PairDzArgs {
   const int64_t* pairs;
-  const int64_t* n_live;  // colptr + N: number of live pairs (only that prefix of `pairs` is filled)
+  const int64_t* pos_begin;  // colptr + j0: first pair position of the latent range
+  const int64_t* pos_end;    // colptr + j1: end of the range (only live pairs are ever listed)
   int64_t P, n_main;
   int k, k_aux;
   const float* vals;
@@ -833,8 +834,9 @@ __global__ void __launch_bounds__(LR_THREADS) pair_dz_kernel(const __grid_consta
   const int lane = threadIdx.x & 31;
   const int nvec = a.D >> 3;
   const int64_t nw = int64_t(gridDim.x) * LR_WARPS;
-  const int64_t live = min(*a.n_live, a.P);
-  for (int64_t pos = (int64_t(blockIdx.x) * LR_THREADS + threadIdx.x) >> 5; pos < live; pos += nw) {
+  const int64_t pend = min(*a.pos_end, a.P);
+  for (int64_t pos = *a.pos_begin + ((int64_t(blockIdx.x) * LR_THREADS + threadIdx.x) >> 5); pos < pend;
+       pos += nw) {
     const int64_t p = a.pairs[pos];
     int64_t b;
     int j, aux;
@@ -902,6 +904,8 @@ struct LatentRowsArgs {
   float* act_freq;
   float* since_fired;
   int N, D, nslices;
+  int j0, j1;      // latent range of this launch
+  int zero_empty;  // write zero gradient rows for latents without a live pair (dense consumers)
 };
 
 template <int VPL>
@@ -927,7 +931,7 @@ __global__ void __launch_bounds__(LR_THREADS, 2) latent_rows_kernel(const __grid
     }
   }
   float sq = 0.f;
-  for (int j = gw / a.nslices; j < a.N; j += tw / a.nslices) {
+  for (int j = a.j0 + gw / a.nslices; j < a.j1; j += tw / a.nslices) {
     const int64_t beg = a.colptr[j], end = a.colptr[j + 1];
     if (sl == 0 && lane == 0 && a.fire_counts) {
       const int fc = a.fire_counts[j];
@@ -936,6 +940,16 @@ __global__ void __launch_bounds__(LR_THREADS, 2) latent_rows_kernel(const __grid
     }
     if (beg == end) {
       if (sl == 0 && lane == 0) a.gb_enc[j] = 0.f;
+      if (a.zero_empty) {
+#pragma unroll
+        for (int u = 0; u < VPL; ++u) {
+          const int vi = vbase + 32 * u;
+          if (vi < nvec) {
+            reinterpret_cast<uint4*>(a.gW_dec + int64_t(j) * a.D)[vi] = make_uint4(0, 0, 0, 0);
+            reinterpret_cast<uint4*>(a.gW_enc + int64_t(j) * a.D)[vi] = make_uint4(0, 0, 0, 0);
+          }
+        }
+      }
       continue;
     }
     float gd[VPL][8], ge[VPL][8];
@@ -1223,12 +1237,13 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
                  const c10::optional<torch::Tensor>& fire_counts,
                  const c10::optional<torch::Tensor>& act_freq,
                  const c10::optional<torch::Tensor>& since_fired, const torch::Tensor& idx,
-                 const c10::optional<torch::Tensor>& aux_idx) {
+                 const c10::optional<torch::Tensor>& aux_idx, int64_t j0, int64_t j1, bool zero_empty) {
   static const bool v1 = [] {
     const char* e = std::getenv("SAELENS_B200_LATENT_GRAD");
     return e && std::string(e) == "v1";
   }();
-  if (v1) {
+  if (j1 < 0) j1 = W_dec.size(0);
+  if (v1 && j0 == 0 && j1 == W_dec.size(0) && !zero_empty) {
     latent_grad_v1(colptr, pairs, vals, aux_vals, inv_scale, dxhat, daux, x, b_dec, W_dec, W_enc, gW_dec, gW_enc,
                    gb_enc, bterm, sumsq, fire_counts, act_freq, since_fired);
     return;
@@ -1254,7 +1269,9 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
     sparse::PairDzArgs pa{};
     pa.pairs = pairs.data_ptr<int64_t>();
     TORCH_CHECK(colptr.numel() == N + 1 && colptr.scalar_type() == at::kLong, "latent_grad: colptr");
-    pa.n_live = colptr.data_ptr<int64_t>() + N;
+    TORCH_CHECK(j0 >= 0 && j0 <= j1 && j1 <= N, "latent_grad: latent range");
+    pa.pos_begin = colptr.data_ptr<int64_t>() + j0;
+    pa.pos_end = colptr.data_ptr<int64_t>() + j1;
     pa.P = P;
     pa.n_main = vals.numel();
     pa.k = int(vals.size(1));
@@ -1306,6 +1323,9 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
   a.N = int(N);
   a.D = int(D);
   a.nslices = ns;
+  a.j0 = int(j0);
+  a.j1 = int(j1);
+  a.zero_empty = zero_empty ? 1 : 0;
   switch (vpl) {
     case 1: sparse::latent_rows_kernel<1><<<dim3(grid), dim3(sparse::LR_THREADS), 0, stream>>>(a); break;
     case 2: sparse::latent_rows_kernel<2><<<dim3(grid), dim3(sparse::LR_THREADS), 0, stream>>>(a); break;

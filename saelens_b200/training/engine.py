@@ -59,6 +59,30 @@ def _round_up(x: int, m: int) -> int:
     return (x + m - 1) // m * m
 
 
+@dataclass
+class _StepState:
+    """Forward results handed from the forward half of a step to the gradient/optimizer half."""
+
+    B: int
+    xb: torch.Tensor
+    vals: torch.Tensor
+    idx: torch.Tensor
+    aux_on: bool
+    aux_vals: torch.Tensor | None
+    aux_idx: torch.Tensor | None
+    dxhat: torch.Tensor
+    daux: torch.Tensor | None
+    bsum: torch.Tensor
+    pairs: torch.Tensor
+    mse: torch.Tensor
+    aux_loss: torch.Tensor
+    sae_out: torch.Tensor | None
+    act_freq: torch.Tensor | None
+    since_fired: torch.Tensor | None
+    lr: float | None
+    update: bool
+
+
 class FusedTopKEngine:
     """Owns the optimizer state of a (possibly latent-sharded) TopK SAE and steps it natively."""
 
@@ -303,22 +327,26 @@ class FusedTopKEngine:
                      self.cursor, pairs)
         self._mark("csc_build")
 
-        # 6. latent gradients + statistics
+        return self._grads_and_update(_StepState(
+            B=B, xb=xb, vals=vals, idx=idx, aux_on=aux_on, aux_vals=aux_vals if aux_on else None,
+            aux_idx=aux_idx if aux_on else None, dxhat=dxhat, daux=daux, bsum=bsum, pairs=pairs, mse=mse,
+            aux_loss=aux_loss, sae_out=sae_out, act_freq=act_freq, since_fired=since_fired, lr=lr, update=update))
+
+    def _grads_and_update(self, st: "_StepState") -> EngineStepResult:
+        """Latent gradients, firing statistics, clip and Adam (steps 6-8 of the step)."""
+        nat, dev, D = self.native, self.device, self.D
         self.sumsq.zero_()
         bterm = torch.zeros(D, dtype=torch.float32, device=dev)
-        nat.latent_grad(self.colptr, pairs, vals, aux_vals if aux_on else None,
-                        self.inv_scale if self.rescale else None, dxhat, daux, xb,
-                        self.p_bdec if self.apply_b_dec else None, self.w_dec, self.w_enc, self.g_dec,
-                        self.g_enc, self.g_benc, bterm if self.apply_b_dec else None, self.sumsq,
-                        self.fire_counts, act_freq, since_fired, idx, aux_idx if aux_on else None)
+        nat.latent_grad(self.colptr, st.pairs, st.vals, st.aux_vals, self.inv_scale if self.rescale else None,
+                        st.dxhat, st.daux, st.xb, self.p_bdec if self.apply_b_dec else None, self.w_dec,
+                        self.w_enc, self.g_dec, self.g_enc, self.g_benc, bterm if self.apply_b_dec else None,
+                        self.sumsq, self.fire_counts, st.act_freq, st.since_fired, st.idx, st.aux_idx)
         self.launches += 3
         self._mark("latent_grad")
-
-        # 7-8. clip + Adam
-        if update:
+        if st.update:
             self.step_count += 1
-            cur_lr = self.lr if lr is None else lr
-            nat.adam_bdec(bsum, bterm if self.apply_b_dec else None, self.g_bdec, self.sumsq, self.clip,
+            cur_lr = self.lr if st.lr is None else st.lr
+            nat.adam_bdec(st.bsum, bterm if self.apply_b_dec else None, self.g_bdec, self.sumsq, self.clip,
                           self.p_bdec, self.m_bdec, self.v_bdec, cur_lr, self.beta1, self.beta2, self.eps,
                           self.step_count, self.max_grad_norm, True)
             nat.adam_rows(self.p_dec, self.m_dec, self.v_dec, self.p_enc, self.m_enc, self.v_enc, self.w_dec,
@@ -328,11 +356,12 @@ class FusedTopKEngine:
                           self.step_count, True)
             self.launches += 2
             self._mark("adam")
-        self.last_loss = mse + aux_loss
+        self.last_loss = st.mse + st.aux_loss
         if self._phase_timing and len(self._phase_events) > 64:
             self._flush_phases()
-        return EngineStepResult(loss=mse + aux_loss, mse_loss=mse, aux_loss=aux_loss, sae_out=sae_out,
-                                topk_vals=vals, topk_idx=idx, fire_counts=self.fire_counts)
+        return EngineStepResult(loss=st.mse + st.aux_loss, mse_loss=st.mse, aux_loss=st.aux_loss,
+                                sae_out=st.sae_out, topk_vals=st.vals, topk_idx=st.idx,
+                                fire_counts=self.fire_counts)
 
     def grad_norm(self) -> torch.Tensor:
         return self.sumsq.sqrt()

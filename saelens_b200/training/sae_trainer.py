@@ -147,7 +147,20 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
         # ---- engine selection
         self.engine: Any = None
         want = getattr(cfg, "sae_engine", "auto")
-        if want != "torch" and not (self._is_ddp or self._is_fsdp) and dp_group is None:
+        self._engine_stats_global = False  # engine firing statistics already cover every DP rank
+        if want != "torch" and not self._is_fsdp and (dp_group is not None or self._is_ddp):
+            from saelens_b200.training.engine import engine_supported
+
+            group = dp_group if dp_group is not None else getattr(sae, "process_group", None) or dist.group.WORLD
+            if engine_supported(self._base_sae) and getattr(self._base_sae, "_tp_group", None) is None:
+                from saelens_b200.parallel.ddp_engine import DDPTopKEngine
+
+                self.engine = DDPTopKEngine(self._base_sae, lr=cfg.lr, group=group, beta1=cfg.adam_beta1,
+                                            beta2=cfg.adam_beta2)
+                self._engine_stats_global = True
+            elif want == "native":
+                raise ValueError("sae_engine='native' requested but this SAE/device is not supported by the fused engine")
+        elif want != "torch" and not (self._is_ddp or self._is_fsdp) and dp_group is None:
             from saelens_b200.training.engine import FusedTopKEngine, engine_supported
 
             tp_group = getattr(self._base_sae, "_tp_group", None)
@@ -301,7 +314,7 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
 
     def _sparsity_window_tick(self) -> None:
         if (self.n_training_steps + 1) % self.cfg.feature_sampling_window == 0:
-            if self.dp_group is not None:
+            if self.dp_group is not None and not self._engine_stats_global:
                 with nccl_nvtx_range("nccl:sae_dp_sparsity_all_reduce", self.dp_group):
                     dist.all_reduce(self.act_freq_scores, op=dist.ReduceOp.SUM, group=self.dp_group)
                 self.n_frac_active_samples *= dist.get_world_size(self.dp_group)
@@ -316,7 +329,8 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
         res = self.engine.step(sae_in, lr=self.current_lr(), dead_mask=self.dead_neurons if run_aux else None,
                                want_sae_out=want_out, act_freq=self.act_freq_scores,
                                since_fired=self.n_forward_passes_since_fired, run_aux=run_aux)
-        self.n_frac_active_samples += self.cfg.train_batch_size_samples
+        world = dist.get_world_size(self.engine.group) if self._engine_stats_global else 1
+        self.n_frac_active_samples += self.cfg.train_batch_size_samples * world
         self.lr_scheduler.step()
         for s in self.coefficient_schedulers.values():
             s.step()
