@@ -106,13 +106,39 @@ __global__ void __launch_bounds__(AR_THREADS) allreduce_kernel(const __grid_cons
       const int64_t len = min(int64_t(AR_CHUNK), a.n - e0);
       const T* land = at<T>(a.P, r, a.land_off) + (c / S) * AR_CHUNK;
       float sq = 0.f;
-      for (int64_t e = t; e < len; e += AR_THREADS) {
-        float acc = 0.f;
-        for (int s = 0; s < S; ++s) acc += Elt<T>::ld(land + int64_t(s) * per_owner * AR_CHUNK + e);
-        const T v = Elt<T>::from_f(acc * a.scale);
-        const float vr = Elt<T>::to_f(v);
-        sq += vr * vr;
-        for (int d = 0; d < S; ++d) at<T>(a.P, (r + d) % S, a.out_off)[e0 + e] = v;
+      if (len == AR_CHUNK) {
+        // 16-byte vectors: V elements per thread and step, S loads and S stores of 16 bytes
+        constexpr int V = 16 / sizeof(T);
+        for (int v = t; v < AR_CHUNK / V; v += AR_THREADS) {
+          float acc[V];
+#pragma unroll
+          for (int i = 0; i < V; ++i) acc[i] = 0.f;
+          for (int s = 0; s < S; ++s) {
+            const uint4 q = __ldcg(reinterpret_cast<const uint4*>(land + int64_t(s) * per_owner * AR_CHUNK) + v);
+            const T* qe = reinterpret_cast<const T*>(&q);
+#pragma unroll
+            for (int i = 0; i < V; ++i) acc[i] += Elt<T>::to_f(qe[i]);
+          }
+          uint4 o;
+          T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+          for (int i = 0; i < V; ++i) {
+            oe[i] = Elt<T>::from_f(acc[i] * a.scale);
+            const float vr = Elt<T>::to_f(oe[i]);
+            sq += vr * vr;
+          }
+          for (int d = 0; d < S; ++d)
+            reinterpret_cast<uint4*>(at<T>(a.P, (r + d) % S, a.out_off) + e0)[v] = o;
+        }
+      } else {
+        for (int64_t e = t; e < len; e += AR_THREADS) {
+          float acc = 0.f;
+          for (int s = 0; s < S; ++s) acc += Elt<T>::ld(land + int64_t(s) * per_owner * AR_CHUNK + e);
+          const T v = Elt<T>::from_f(acc * a.scale);
+          const float vr = Elt<T>::to_f(v);
+          sq += vr * vr;
+          for (int d = 0; d < S; ++d) at<T>(a.P, (r + d) % S, a.out_off)[e0 + e] = v;
+        }
       }
       if (a.sq_off >= 0) {
 #pragma unroll
@@ -309,7 +335,7 @@ void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64
   TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "p2p_allreduce: bad group");
   TORCH_CHECK(x.is_cuda() && x.is_contiguous() && (x.scalar_type() == at::kFloat || x.scalar_type() == at::kBFloat16),
               "p2p_allreduce: contiguous fp32/bf16 CUDA tensor required");
-  TORCH_CHECK(land_off % 16 == 0 && out_off % 16 == 0, "p2p_allreduce: offsets");
+  TORCH_CHECK(land_off % 16 == 0 && out_off % 16 == 0, "p2p_allreduce: offsets must be 16-byte aligned");
   const int64_t n = x.numel();
   if (n == 0) return;
   const at::cuda::CUDAGuard guard(x.device());

@@ -1,0 +1,196 @@
+"""Measurement cases behind the committed profile summaries (run on a CUDA machine).
+
+    python -m saelens_b200.perf_cases phases [--tp-exchange p2p|nccl] [--d-sae N]
+        Per-phase CUDA-event times of the training step (one GPU, or several under
+        torch.distributed.run: latent-sharded tensor parallel).
+    python -m saelens_b200.perf_cases fused-case [--steps 2]
+        Small fused tensor-parallel step with a world size of 1 (d_in 4096, d_sae 32768, k 128,
+        batch 4096; about 2 GB on the device), the case used for ncu captures of the fused kernels.
+    python -m saelens_b200.perf_cases gemm [--pair 0|1]
+        Encoder GEMM numerics against fp32 and CUDA-event TFLOP/s on the benchmark shapes.
+    python -m saelens_b200.perf_cases ddp [--d-sae 131072 --k 64 --batch 8192 --steps 10]
+        Data-parallel TopK step (replicated SAE, P2P gradient all-reduce) under
+        torch.distributed.run: ms/step (max over ranks) and per-phase times.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+from datetime import timedelta
+
+
+def _init_dist() -> tuple[int, int, int]:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29533")
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def phases(args: argparse.Namespace) -> None:
+    os.environ["SAELENS_B200_PHASE_TIMING"] = "1"
+    import torch
+    import torch.distributed as dist
+
+    from saelens_b200.training.bench_driver import BenchSetup, _make_engine, synthetic_batch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = 0
+    if world > 1:
+        world, rank, _ = _init_dist()
+    s = BenchSetup(d_in=4096, d_sae=args.d_sae, k=128, batch=16384, world=world, rank=rank,
+                   tp_exchange=args.tp_exchange)
+    eng = _make_engine(s)
+    x = synthetic_batch(BenchSetup(**{**s.__dict__, "batch": 16384 // world}), 1 + rank, device="cuda")
+    for _ in range(3):
+        eng.step(x)
+    eng.phase_times_ms()
+    n = 5
+    for _ in range(n):
+        eng.step(x)
+    t = eng.phase_times_ms()
+    print(rank, args.tp_exchange if world > 1 else "single",
+          json.dumps({k: round(v / n, 3) for k, v in t.items()}), "total_ms", round(sum(t.values()) / n, 2),
+          flush=True)
+    eng.status.check()
+    eng.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def fused_case(args: argparse.Namespace) -> None:
+    import torch
+    import torch.distributed as dist
+
+    _init_dist()
+    from saelens_b200.parallel.tp_engine import TPTopKEngine
+    from saelens_b200.training.bench_driver import BenchSetup, _build_sae, _materialise_local, synthetic_batch
+
+    s = BenchSetup(d_in=4096, d_sae=32768, k=128, batch=4096, world=1, rank=0)
+    sae = _materialise_local(_build_sae(s), s)
+    eng = TPTopKEngine(sae, lr=5e-5, group=dist.group.WORLD, fused=True)
+    x = synthetic_batch(s, 1, device="cuda")
+    for _ in range(args.steps):
+        eng.step(x)
+    torch.cuda.synchronize()
+    eng.status.check()
+    print(json.dumps({"ok": True, "loss": float(eng.last_loss)}))
+    eng.close()
+    dist.destroy_process_group()
+
+
+def gemm(args: argparse.Namespace) -> None:
+    os.environ["SAELENS_B200_GEMM_PAIR"] = str(args.pair)
+    import torch
+
+    from saelens_b200.ops import native
+    from saelens_b200.ops.status import StatusWord
+
+    nat = native()
+    st = StatusWord("cuda")
+    torch.manual_seed(0)
+    print("pair" if args.pair else "single", flush=True)
+    for M, N, K, relu, timing in ((256, 256, 64, False, False), (512, 1024, 256, False, False),
+                                  (300, 512, 128, True, False), (4096, 32768, 4096, False, True),
+                                  (4096, 262144, 4096, False, True)):
+        A = (torch.randn(M, K, device="cuda") * 0.5).to(torch.bfloat16)
+        B = (torch.randn(N, K, device="cuda") * 0.5).to(torch.bfloat16)
+        bias = torch.randn(N, device="cuda")
+        scale = torch.rand(N, device="cuda") + 0.5
+        out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        cm = torch.empty(M, N // 32, dtype=torch.bfloat16, device="cuda")
+        nat.gemm_tn_bf16(A, B, bias, scale, relu, out, cm, st.tensor, 0)
+        torch.cuda.synchronize()
+        ref = (A.float() @ B.float().T + bias) * scale
+        if relu:
+            ref = ref.relu()
+        err = ((out.float() - ref).abs().max() / ref.abs().max()).item()
+        line = f"M={M} N={N} K={K} status={st.code()} rel_max_err={err:.2e}"
+        if timing and st.code() == 0:
+            for _ in range(3):
+                nat.gemm_tn_bf16(A, B, bias, scale, relu, out, cm, st.tensor, 0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(10):
+                nat.gemm_tn_bf16(A, B, bias, scale, relu, out, cm, st.tensor, 0)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / 10
+            line += f" ms={ms:.3f} TFLOPs={2 * M * N * K / ms / 1e9:.1f}"
+        print(line, flush=True)
+        st.check("gemm")
+
+
+def ddp(args: argparse.Namespace) -> None:
+    os.environ["SAELENS_B200_PHASE_TIMING"] = "1"
+    import torch
+    import torch.distributed as dist
+
+    from saelens_b200.models.topk import TopKTrainingSAE, TopKTrainingSAEConfig
+    from saelens_b200.parallel.ddp_engine import DDPTopKEngine
+    from saelens_b200.training.bench_driver import BenchSetup, synthetic_batch
+
+    world, rank, local = _init_dist()
+    torch.manual_seed(1234)
+    sae = TopKTrainingSAE(TopKTrainingSAEConfig(d_in=4096, d_sae=args.d_sae, k=args.k, device=f"cuda:{local}"))
+    eng = DDPTopKEngine(sae, lr=5e-5, group=dist.group.WORLD, segments=args.segments)
+    s = BenchSetup(d_in=4096, d_sae=args.d_sae, k=args.k, batch=args.batch, world=1, rank=rank)
+    xs = [synthetic_batch(s, 10 * i + rank, device="cuda") for i in range(2)]
+    for i in range(3):
+        eng.step(xs[i % 2])
+    eng.phase_times_ms()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        eng.step(xs[i % 2])
+    e1.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device="cuda")
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    t = eng.phase_times_ms()
+    eng.status.check()
+    if rank == 0:
+        print(json.dumps({"world": world, "d_sae": args.d_sae, "k": args.k, "batch_per_gpu": args.batch,
+                          "ms_per_step": round(float(ms.item()), 3),
+                          "tokens_per_s": round(args.batch * world * 1000.0 / float(ms.item()), 1),
+                          "phases_ms": {k: round(v / args.steps, 3) for k, v in t.items()}}), flush=True)
+    eng.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def main() -> None:
+    p = argparse.ArgumentParser(prog="python -m saelens_b200.perf_cases")
+    sub = p.add_subparsers(dest="cmd", required=True)
+    a = sub.add_parser("phases")
+    a.add_argument("--tp-exchange", choices=["p2p", "nccl"], default="p2p")
+    a.add_argument("--d-sae", type=int, default=1048576)
+    b = sub.add_parser("fused-case")
+    b.add_argument("--steps", type=int, default=2)
+    c = sub.add_parser("gemm")
+    c.add_argument("--pair", type=int, choices=[0, 1], default=1)
+    d = sub.add_parser("ddp")
+    d.add_argument("--d-sae", type=int, default=131072)
+    d.add_argument("--k", type=int, default=64)
+    d.add_argument("--batch", type=int, default=8192)
+    d.add_argument("--steps", type=int, default=10)
+    d.add_argument("--segments", type=int, default=4)
+    args = p.parse_args()
+    {"phases": phases, "fused-case": fused_case, "gemm": gemm, "ddp": ddp}[args.cmd](args)
+
+
+if __name__ == "__main__":
+    main()

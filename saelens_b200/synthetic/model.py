@@ -1,0 +1,342 @@
+"""SyntheticModel: a serialisable bundle of feature dictionary + activation generator (+ optional
+hierarchy and correlation), the toy "language model" of synthetic SAE benchmarks (role of
+sae_lens/synthetic/synthetic_model.py, training.py, initialization.py, stats.py).
+
+Saved layout (directory): `synthetic_model_config.json` (the config), `synthetic_model.safetensors`
+(feature vectors, bias, firing probabilities, magnitudes, low-rank correlation factors) and, with a
+hierarchy, `synthetic_model_hierarchy.json`.
+"""
+
+from __future__ import annotations
+
+import json
+from collections.abc import Iterator
+from dataclasses import asdict, dataclass, field
+from pathlib import Path
+from typing import Any
+
+import torch
+from torch import nn
+
+from saelens_b200.synthetic.distributions import (
+    FiringProbabilityConfig,
+    LowRankCorrelationMatrix,
+    MagnitudeConfig,
+    ZipfianFiringProbabilityConfig,
+    generate_magnitudes,
+    generate_random_low_rank_correlation_matrix,
+)
+from saelens_b200.synthetic.generation import (
+    ActivationGenerator,
+    FeatureDictionary,
+    Hierarchy,
+    HierarchyConfig,
+    generate_hierarchy,
+    orthogonal_initializer,
+)
+from saelens_b200.utils.misc import cosine_similarities
+
+SYNTHETIC_MODEL_CONFIG_FILENAME = "synthetic_model_config.json"
+SYNTHETIC_MODEL_WEIGHTS_FILENAME = "synthetic_model.safetensors"
+SYNTHETIC_MODEL_HIERARCHY_FILENAME = "synthetic_model_hierarchy.json"
+
+
+@dataclass
+class OrthogonalizationConfig:
+    num_steps: int = 200
+    lr: float = 0.01
+    chunk_size: int = 1024
+
+    def to_dict(self) -> dict[str, Any]:
+        return asdict(self)
+
+    @classmethod
+    def from_dict(cls, d: dict[str, Any]) -> "OrthogonalizationConfig":
+        return cls(**d)
+
+
+@dataclass
+class LowRankCorrelationConfig:
+    rank: int = 32
+    correlation_scale: float = 0.075
+
+    def to_dict(self) -> dict[str, Any]:
+        return asdict(self)
+
+    @classmethod
+    def from_dict(cls, d: dict[str, Any]) -> "LowRankCorrelationConfig":
+        return cls(**d)
+
+
+def _mag_to_json(v: float | MagnitudeConfig) -> Any:
+    return v.to_dict() if isinstance(v, MagnitudeConfig) else float(v)
+
+
+def _mag_from_json(v: Any) -> float | MagnitudeConfig:
+    return MagnitudeConfig.from_dict(v) if isinstance(v, dict) else float(v)
+
+
+@dataclass
+class SyntheticModelConfig:
+    num_features: int = 16384
+    hidden_dim: int = 768
+    firing_probability: FiringProbabilityConfig = field(default_factory=ZipfianFiringProbabilityConfig)
+    mean_firing_magnitude: float | MagnitudeConfig = 1.0
+    std_firing_magnitude: float | MagnitudeConfig = 0.0
+    bias: bool | float = False
+    orthogonalization: OrthogonalizationConfig | None = field(default_factory=OrthogonalizationConfig)
+    correlation: LowRankCorrelationConfig | None = None
+    hierarchy: HierarchyConfig | None = None
+    seed: int = 42
+    dtype: str = "float32"
+
+    def __post_init__(self) -> None:
+        if self.num_features < 1 or self.hidden_dim < 1:
+            raise ValueError("num_features and hidden_dim must be positive")
+
+    def to_dict(self) -> dict[str, Any]:
+        return {"num_features": self.num_features, "hidden_dim": self.hidden_dim,
+                "firing_probability": self.firing_probability.to_dict(),
+                "mean_firing_magnitude": _mag_to_json(self.mean_firing_magnitude),
+                "std_firing_magnitude": _mag_to_json(self.std_firing_magnitude), "bias": self.bias,
+                "orthogonalization": self.orthogonalization.to_dict() if self.orthogonalization else None,
+                "correlation": self.correlation.to_dict() if self.correlation else None,
+                "hierarchy": self.hierarchy.to_dict() if self.hierarchy else None, "seed": self.seed,
+                "dtype": self.dtype}
+
+    @classmethod
+    def from_dict(cls, d: dict[str, Any]) -> "SyntheticModelConfig":
+        return cls(num_features=d["num_features"], hidden_dim=d["hidden_dim"],
+                   firing_probability=FiringProbabilityConfig.from_dict(d["firing_probability"]),
+                   mean_firing_magnitude=_mag_from_json(d.get("mean_firing_magnitude", 1.0)),
+                   std_firing_magnitude=_mag_from_json(d.get("std_firing_magnitude", 0.0)),
+                   bias=d.get("bias", False),
+                   orthogonalization=OrthogonalizationConfig.from_dict(d["orthogonalization"])
+                   if d.get("orthogonalization") else None,
+                   correlation=LowRankCorrelationConfig.from_dict(d["correlation"]) if d.get("correlation") else None,
+                   hierarchy=HierarchyConfig.from_dict(d["hierarchy"]) if d.get("hierarchy") else None,
+                   seed=d.get("seed", 42), dtype=d.get("dtype", "float32"))
+
+
+class SyntheticModel(nn.Module):
+    """`sample(batch)` -> hidden activations [batch, hidden_dim]; `sample_with_features(batch)` also
+    returns the ground-truth feature activations."""
+
+    def __init__(self, cfg: SyntheticModelConfig, device: str | torch.device = "cpu",
+                 _tensors: dict[str, torch.Tensor] | None = None, _hierarchy: Hierarchy | None = None):
+        super().__init__()
+        self.cfg = cfg
+        self.device = torch.device(device)
+        t = _tensors or {}
+        init = None
+        if "feature_vectors" not in t and cfg.orthogonalization is not None:
+            o = cfg.orthogonalization
+            init = orthogonal_initializer(o.num_steps, o.lr, o.chunk_size)
+        self.feature_dict = FeatureDictionary(cfg.num_features, cfg.hidden_dim, bias=cfg.bias, initializer=init,
+                                              device=self.device, seed=cfg.seed)
+        if "feature_vectors" in t:
+            with torch.no_grad():
+                self.feature_dict.feature_vectors.copy_(t["feature_vectors"])
+                self.feature_dict.bias.copy_(t["bias"])
+        self.hierarchy = _hierarchy if _hierarchy is not None else (
+            generate_hierarchy(cfg.num_features, cfg.hierarchy, seed=cfg.seed) if cfg.hierarchy else None)
+        probs = t.get("firing_probabilities")
+        if probs is None:
+            probs = cfg.firing_probability.generate(cfg.num_features, seed=cfg.seed)
+            if self.hierarchy is not None and cfg.hierarchy is not None and cfg.hierarchy.compensate_probabilities:
+                probs = (probs * self.hierarchy.compute_probability_correction_factors(probs)).clamp(max=1.0)
+        mean = t.get("mean_firing_magnitudes", generate_magnitudes(cfg.num_features, cfg.mean_firing_magnitude,
+                                                                   seed=cfg.seed + 1))
+        std = t.get("std_firing_magnitudes", generate_magnitudes(cfg.num_features, cfg.std_firing_magnitude,
+                                                                 seed=cfg.seed + 2))
+        corr = None
+        if "correlation_factor" in t:
+            corr = LowRankCorrelationMatrix(t["correlation_factor"], t["correlation_diag"])
+        elif cfg.correlation is not None:
+            corr = generate_random_low_rank_correlation_matrix(cfg.num_features, cfg.correlation.rank,
+                                                               cfg.correlation.correlation_scale, seed=cfg.seed + 3)
+        self.correlation = corr
+        self.activation_generator = ActivationGenerator(
+            cfg.num_features, probs, std_firing_magnitudes=std, mean_firing_magnitudes=mean,
+            modify_activations=self.hierarchy.modifier if self.hierarchy is not None else None,
+            correlation_matrix=corr, device=self.device, dtype=cfg.dtype)
+
+    @property
+    def use_sparse_tensors(self) -> bool:
+        return self.activation_generator.use_sparse_tensors
+
+    @use_sparse_tensors.setter
+    def use_sparse_tensors(self, value: bool) -> None:
+        self.activation_generator.use_sparse_tensors = value
+
+    @torch.no_grad()
+    def sample_with_features(self, batch_size: int) -> tuple[torch.Tensor, torch.Tensor]:
+        f = self.activation_generator.sample(batch_size)
+        return self.feature_dict(f), f
+
+    @torch.no_grad()
+    def sample(self, batch_size: int) -> torch.Tensor:
+        return self.sample_with_features(batch_size)[0]
+
+    def forward(self, batch_size: int) -> torch.Tensor:
+        return self.sample(batch_size)
+
+    # ---------------------------------------------------------------------- persistence
+    def save(self, path: str | Path) -> None:
+        from safetensors.torch import save_file
+
+        p = Path(path)
+        p.mkdir(parents=True, exist_ok=True)
+        (p / SYNTHETIC_MODEL_CONFIG_FILENAME).write_text(json.dumps(self.cfg.to_dict(), indent=2))
+        g = self.activation_generator
+        t = {"feature_vectors": self.feature_dict.feature_vectors.detach(), "bias": self.feature_dict.bias.detach(),
+             "firing_probabilities": g.firing_probabilities, "mean_firing_magnitudes": g.mean_firing_magnitudes,
+             "std_firing_magnitudes": g.std_firing_magnitudes}
+        if self.correlation is not None:
+            t["correlation_factor"] = self.correlation.correlation_factor
+            t["correlation_diag"] = self.correlation.correlation_diag
+        save_file({k: v.contiguous().cpu() for k, v in t.items()}, str(p / SYNTHETIC_MODEL_WEIGHTS_FILENAME))
+        if self.hierarchy is not None:
+            (p / SYNTHETIC_MODEL_HIERARCHY_FILENAME).write_text(json.dumps(self.hierarchy.to_dict()))
+
+    @classmethod
+    def load_from_disk(cls, path: str | Path, device: str | torch.device = "cpu") -> "SyntheticModel":
+        from safetensors.torch import load_file
+
+        p = Path(path)
+        cfg = SyntheticModelConfig.from_dict(json.loads((p / SYNTHETIC_MODEL_CONFIG_FILENAME).read_text()))
+        t = {k: v.to(device) for k, v in load_file(str(p / SYNTHETIC_MODEL_WEIGHTS_FILENAME)).items()}
+        hp = p / SYNTHETIC_MODEL_HIERARCHY_FILENAME
+        h = Hierarchy.from_dict(json.loads(hp.read_text())) if hp.exists() else None
+        return cls(cfg, device=device, _tensors=t, _hierarchy=h)
+
+    @classmethod
+    def from_pretrained(cls, repo_id: str, subfolder: str | None = None, device: str | torch.device = "cpu",
+                        revision: str | None = None) -> "SyntheticModel":
+        from huggingface_hub import snapshot_download
+
+        root = Path(snapshot_download(repo_id, revision=revision,
+                                      allow_patterns=[f"{subfolder}/*"] if subfolder else None))
+        return cls.load_from_disk(root / subfolder if subfolder else root, device=device)
+
+    @classmethod
+    def load_from_source(cls, source: str | Path, device: str | torch.device = "cpu") -> "SyntheticModel":
+        """A local directory, or `repo_id[/subfolder]` on the Hugging Face hub."""
+        if Path(source).exists():
+            return cls.load_from_disk(source, device=device)
+        parts = str(source).split("/")
+        return cls.from_pretrained("/".join(parts[:2]), "/".join(parts[2:]) or None, device=device)
+
+
+# ---------------------------------------------------------------------------- training helpers
+class SyntheticActivationIterator(Iterator[torch.Tensor]):
+    """Endless iterator of hidden-activation batches from a SyntheticModel (a data provider)."""
+
+    def __init__(self, model: SyntheticModel, batch_size: int, dtype: torch.dtype | None = None,
+                 device: str | torch.device | None = None):
+        self.model, self.batch_size, self.dtype = model, batch_size, dtype
+        self.device = torch.device(device) if device is not None else model.device
+
+    def __iter__(self) -> "SyntheticActivationIterator":
+        return self
+
+    def __next__(self) -> torch.Tensor:
+        x = self.model.sample(self.batch_size).to(self.device)
+        return x.to(self.dtype) if self.dtype is not None else x
+
+
+def init_sae_to_match_feature_dict(sae: Any, feature_dict: FeatureDictionary, noise_level: float = 0.0,
+                                   feature_ordering: torch.Tensor | None = None) -> None:
+    """Set the SAE decoder rows to the ground-truth features (optionally permuted / noised), the
+    encoder to the decoder transpose, and zero the biases."""
+    fv = feature_dict.feature_vectors.detach().float()
+    if feature_ordering is not None:
+        fv = fv[feature_ordering]
+    n = min(fv.shape[0], sae.W_dec.shape[0])
+    with torch.no_grad():
+        W = sae.W_dec.detach().float().clone()
+        W[:n] = fv[:n].to(W.device)
+        if noise_level > 0:
+            W += noise_level * torch.randn_like(W)
+        W = W / W.norm(dim=1, keepdim=True).clamp(min=1e-12)
+        sae.W_dec.copy_(W.to(sae.W_dec.dtype))
+        sae.W_enc.copy_(W.T.to(sae.W_enc.dtype))
+        sae.b_enc.zero_()
+        sae.b_dec.zero_()
+
+
+def train_toy_sae(sae: Any, model: SyntheticModel, training_samples: int = 2_000_000, batch_size: int = 1024,
+                  lr: float = 3e-4, device: str | torch.device | None = None) -> list[float]:
+    """Minimal training loop (Adam on the SAE's own training forward pass) for quick experiments;
+    returns the loss history.  Use SyntheticSAERunner for full trainer features."""
+    from saelens_b200.models.sae import TrainStepInput
+
+    dev = torch.device(device) if device is not None else next(iter(sae.parameters())).device
+    opt = torch.optim.Adam(sae.parameters(), lr=lr)
+    it = SyntheticActivationIterator(model, batch_size, device=dev)
+    losses = []
+    for step in range(max(1, training_samples // batch_size)):
+        x = next(it).to(sae.W_enc.dtype)
+        out = sae.training_forward_pass(TrainStepInput(sae_in=x, coefficients={"l1": 1.0}, dead_neuron_mask=None,
+                                                       n_training_steps=step))
+        opt.zero_grad(set_to_none=True)
+        out.loss.backward()
+        opt.step()
+        losses.append(float(out.loss.detach()))
+    return losses
+
+
+# ---------------------------------------------------------------------------- statistics
+@dataclass
+class SuperpositionStats:
+    num_features: int
+    hidden_dim: int
+    superposition_ratio: float
+    mean_abs_cosine: float
+    max_abs_cosine: float
+    mean_max_abs_cosine: float
+
+
+def compute_superposition_stats(feature_vectors: torch.Tensor, chunk_size: int = 4096) -> SuperpositionStats:
+    """Off-diagonal |cos| statistics of the dictionary (computed in row chunks)."""
+    n, d = feature_vectors.shape
+    fv = feature_vectors.float()
+    tot, mx, mean_max = 0.0, 0.0, 0.0
+    for s in range(0, n, chunk_size):
+        c = cosine_similarities(fv[s : s + chunk_size], fv).abs()
+        idx = torch.arange(c.shape[0], device=c.device)
+        c[idx, s + idx] = 0.0
+        tot += float(c.sum())
+        mx = max(mx, float(c.max())) if n > 1 else 0.0
+        mean_max += float(c.max(dim=1).values.sum())
+    pairs = max(n * (n - 1), 1)
+    return SuperpositionStats(n, d, n / d, tot / pairs, mx, mean_max / n)
+
+
+@dataclass
+class CorrelationMatrixStats:
+    num_features: int
+    mean_abs_offdiag: float
+    max_abs_offdiag: float
+    frac_nonzero_offdiag: float
+
+
+def compute_correlation_matrix_stats(m: torch.Tensor, tol: float = 1e-6) -> CorrelationMatrixStats:
+    n = m.shape[0]
+    off = m.float() - torch.diag(m.diagonal().float())
+    a = off.abs()
+    cnt = max(n * (n - 1), 1)
+    return CorrelationMatrixStats(n, float(a.sum()) / cnt, float(a.max()) if n > 1 else 0.0,
+                                  float((a > tol).sum()) / cnt)
+
+
+def compute_low_rank_correlation_matrix_stats(c: LowRankCorrelationMatrix, sample: int = 2048,
+                                              seed: int = 0) -> CorrelationMatrixStats:
+    """Statistics of the implied correlation on a random subset of `sample` features."""
+    n = c.correlation_factor.shape[0]
+    g = torch.Generator().manual_seed(seed)
+    idx = torch.randperm(n, generator=g)[: min(sample, n)].to(c.correlation_factor.device)
+    f = c.correlation_factor[idx].float()
+    m = f @ f.T + torch.diag(c.correlation_diag[idx].float())
+    s = compute_correlation_matrix_stats(m)
+    return CorrelationMatrixStats(n, s.mean_abs_offdiag, s.max_abs_offdiag, s.frac_nonzero_offdiag)

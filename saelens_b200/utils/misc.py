@@ -81,3 +81,10 @@ def extract_stop_at_layer_from_hook_name(hook_name: str) -> int | None:
         if p == "blocks" and i + 1 < len(parts) and parts[i + 1].isdigit():
             return int(parts[i + 1]) + 1
     return None
+
+
+def cosine_similarities(a: torch.Tensor, b: torch.Tensor | None = None) -> torch.Tensor:
+    """Pairwise cosine similarities between the rows of a [n, d] and b [m, d] (b defaults to a)."""
+    a_n = a / a.norm(dim=-1, keepdim=True).clamp(min=1e-12)
+    b_n = a_n if b is None else b / b.norm(dim=-1, keepdim=True).clamp(min=1e-12)
+    return a_n @ b_n.T

@@ -46,13 +46,16 @@ def _worker(rank, world, port, d_in, d_sae, k, B, out_dir, segments):
     rows = x[rank * (B // world) : (rank + 1) * (B // world)].cuda()
     act = torch.zeros(d_sae, device=f"cuda:{rank}")
     since = torch.zeros(d_sae, device=f"cuda:{rank}")
+    eng.step(rows, update=False)  # gradient only: the averaged gradient is compared directly
+    torch.cuda.synchronize()
+    g0 = {"g_dec": eng.g_avg[0].float().cpu(), "g_enc": eng.g_avg[1].float().cpu()}
     losses = []
     for _ in range(4):
         losses.append(float(eng.step(rows, act_freq=act, since_fired=since).loss))
     torch.cuda.synchronize()
     eng.status.check()
     torch.save({"losses": losses, "p_dec": eng.p_dec.cpu(), "p_enc": eng.p_enc.cpu(), "p_bdec": eng.p_bdec.cpu(),
-                "act": act.cpu(), "since": since.cpu()}, os.path.join(out_dir, f"rank{rank}.pt"))
+                "act": act.cpu(), "since": since.cpu(), **g0}, os.path.join(out_dir, f"rank{rank}.pt"))
     eng.close()
     dist.destroy_process_group()
 
@@ -72,8 +75,19 @@ def test_ddp2_matches_single_gpu_full_batch(tmp_path, segments):
     x = torch.randn(B, d_in, generator=g).to(torch.bfloat16).cuda()
     act = torch.zeros(d_sae, device="cuda:0")
     since = torch.zeros(d_sae, device="cuda:0")
+    eng.step(x, update=False)
+    torch.cuda.synchronize()
+    live = (eng.colptr[1:] > eng.colptr[:-1]).cpu()
+    ref_g = {"g_dec": eng.g_dec.float().cpu(), "g_enc": eng.g_enc.float().cpu()}
     ref = [float(eng.step(x, act_freq=act, since_fired=since).loss) for _ in range(4)]
     r = [torch.load(tmp_path / f"rank{i}.pt") for i in range(2)]
+    # the averaged gradient equals the full-batch gradient up to bf16 rounding of the per-rank parts
+    for name in ("g_dec", "g_enc"):
+        got, want = r[0][name], ref_g[name]
+        assert torch.equal(r[0][name], r[1][name])
+        assert got[~live].abs().max().item() == 0.0 if (~live).any() else True
+        rel = ((got[live] - want[live]).norm() / want[live].norm()).item()
+        assert rel < 1e-2, (name, rel)
     for a, b in zip(r[0]["losses"], ref):
         assert abs(a - b) <= 2e-3 * abs(b), (r[0]["losses"], ref)
     assert r[0]["losses"] == r[1]["losses"]
@@ -87,9 +101,11 @@ def test_ddp2_matches_single_gpu_full_batch(tmp_path, segments):
     assert (r[0]["since"] != since.cpu()).float().mean().item() < 1e-2
 
     def close(got, want, name):
+        # Adam normalises each coordinate, so coordinates whose gradient is near zero can move in
+        # opposite directions by up to lr per step between the two runs; the bulk must agree
         d = (got - want).abs()
         frac = (d > (2e-5 + 1e-3 * want.abs())).float().mean().item()
-        assert d.max().item() <= 5e-3 and frac < 5e-3, (name, d.max().item(), frac)
+        assert d.max().item() <= 2 * 4 * 1e-3 and frac < 5e-2, (name, d.max().item(), frac)
 
     close(r[0]["p_dec"], eng.p_dec.cpu(), "p_dec")
     close(r[0]["p_enc"], eng.p_enc.cpu(), "p_enc")
