@@ -158,6 +158,15 @@ class NativeLinear(nn.Module):
         super()._load_from_state_dict(*args, **kwargs)
 
 
+def _native_ok(t: torch.Tensor) -> bool:
+    """Use the framework's CUDA kernels for inference-mode producer ops on a CUDA tensor."""
+    if not (t.is_cuda and not torch.is_grad_enabled()):
+        return False
+    from saelens_b200 import ops
+
+    return ops.available()
+
+
 class Norm(nn.Module):
     def __init__(self, cfg: LMConfig, dtype: torch.dtype):
         super().__init__()
@@ -169,6 +178,15 @@ class Norm(nn.Module):
         self.hook_normalized = HookPoint()
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if (self.rms and x.dtype in (torch.bfloat16, torch.float32) and x.dtype == self.w.dtype
+                and x.shape[-1] % 8 == 0 and _native_ok(x)):
+            from saelens_b200.ops import native
+
+            x2 = x.reshape(-1, x.shape[-1])
+            if not x2.is_contiguous():
+                x2 = x2.contiguous()
+            y = native().rmsnorm(x2, self.w, self.eps, self.one_plus).view(x.shape)
+            return self.hook_normalized(y)
         xf = x.float()
         if self.rms:
             y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
@@ -200,6 +218,12 @@ def rotary_tables(n_pos: int, d: int, base: float, device: Any, dtype: torch.dty
 
 def apply_rotary(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
     """x [B, S, H, d]; rotate-half convention (first half paired with second half)."""
+    if x.dtype == torch.bfloat16 and cos.dtype == torch.float32 and _native_ok(x):
+        from saelens_b200.ops import native
+
+        y = x.contiguous().clone() if x.is_contiguous() else x.contiguous()
+        native().rope_(y, cos.contiguous(), sin.contiguous(), 0)
+        return y
     d2 = x.shape[-1] // 2
     x1, x2 = x[..., :d2].float(), x[..., d2:].float()
     c = cos[None, :, None, :]
@@ -263,7 +287,14 @@ class MLP(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self.gated:
             pre = self.hook_pre(self.gate(x))
-            post = self.hook_post(_act(self.cfg.act_fn, pre) * self.up(x))
+            up = self.up(x)
+            kind = {"silu": 0, "gelu_new": 1, "gelu_pytorch_tanh": 1}.get(self.cfg.act_fn)
+            if kind is not None and pre.dtype == torch.bfloat16 and pre.shape == up.shape and _native_ok(pre):
+                from saelens_b200.ops import native
+
+                post = self.hook_post(native().gated_act(pre.contiguous(), up.contiguous(), kind))
+            else:
+                post = self.hook_post(_act(self.cfg.act_fn, pre) * up)
         else:
             pre = self.hook_pre(self.up(x))
             post = self.hook_post(_act(self.cfg.act_fn, pre))

@@ -28,6 +28,7 @@ SOURCES = [
     "noalloc_csc.cu",
     "p2p.cu",
     "symm.cpp",
+    "lm_kernels.cu",
 ]
 
 NVCC_FLAGS = [

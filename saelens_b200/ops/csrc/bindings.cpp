@@ -78,10 +78,10 @@ void topk_exchange_merge(const torch::Tensor& vals, const torch::Tensor& idx, in
                          const c10::optional<torch::Tensor>& k_dev, const std::vector<int64_t>& peer_bases,
                          int64_t rank, int64_t cv_off, int64_t ci_off, int64_t cnt_off, int64_t epoch,
                          const torch::Tensor& ticket, const torch::Tensor& status);
-std::vector<int64_t> p2p_allreduce_sizes(int64_t n, int64_t elem_bytes, int64_t world);
+std::vector<int64_t> p2p_allreduce_sizes(int64_t n, int64_t elem_bytes, int64_t world, int64_t chunk);
 void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64_t>& peer_bases, int64_t rank,
                    int64_t land_off, int64_t cnt_off, int64_t out_off, int64_t flag_off, int64_t epoch,
-                   const torch::Tensor& ticket, const torch::Tensor& status, int64_t sq_off);
+                   const torch::Tensor& ticket, const torch::Tensor& status, int64_t sq_off, int64_t chunk);
 void p2p_wait_flags(const torch::Tensor& flags, int64_t target, const torch::Tensor& status);
 std::tuple<int64_t, torch::Tensor> symm_alloc(int64_t nbytes);
 int64_t symm_open(const torch::Tensor& handle);
@@ -95,6 +95,9 @@ void p2p_route_rows(const torch::Tensor& src, const torch::Tensor& routes, const
 void p2p_wait_targets(const torch::Tensor& counters, const torch::Tensor& targets, const torch::Tensor& status);
 void p2p_signal(const std::vector<int64_t>& peer_bases, int64_t rank, int64_t off, int64_t index,
                 int64_t rank_mask, int64_t value);
+torch::Tensor rmsnorm(const torch::Tensor& x, const torch::Tensor& w, double eps, bool one_plus);
+void rope_(const torch::Tensor& x, const torch::Tensor& cos, const torch::Tensor& sin, int64_t pos0);
+torch::Tensor gated_act(const torch::Tensor& gate, const torch::Tensor& up, int64_t kind);
 }  // namespace sb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -117,14 +120,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_ag_tn_bf16", &sb::gemm_ag_tn_bf16);
   m.def("decode_rs", &sb::decode_rs);
   m.def("topk_exchange_merge", &sb::topk_exchange_merge);
-  m.def("p2p_allreduce_sizes", &sb::p2p_allreduce_sizes);
+  m.def("p2p_allreduce_sizes", &sb::p2p_allreduce_sizes, py::arg("n"), py::arg("elem_bytes"), py::arg("world"),
+        py::arg("chunk") = 0);
   m.def("p2p_allreduce", &sb::p2p_allreduce, py::arg("x"), py::arg("scale"), py::arg("peer_bases"),
         py::arg("rank"), py::arg("land_off"), py::arg("cnt_off"), py::arg("out_off"), py::arg("flag_off"),
-        py::arg("epoch"), py::arg("ticket"), py::arg("status"), py::arg("sq_off") = -1);
+        py::arg("epoch"), py::arg("ticket"), py::arg("status"), py::arg("sq_off") = -1, py::arg("chunk") = 0);
   m.def("p2p_wait_flags", &sb::p2p_wait_flags);
   m.def("p2p_route_rows", &sb::p2p_route_rows);
   m.def("p2p_wait_targets", &sb::p2p_wait_targets);
   m.def("p2p_signal", &sb::p2p_signal);
+  m.def("rmsnorm", &sb::rmsnorm);
+  m.def("rope_", &sb::rope_);
+  m.def("gated_act", &sb::gated_act);
   m.def("symm_alloc", &sb::symm_alloc);
   m.def("symm_open", &sb::symm_open);
   m.def("symm_close", &sb::symm_close);

@@ -27,7 +27,7 @@ namespace sb {
 namespace p2p {
 
 constexpr int AR_THREADS = 256;
-constexpr int AR_CHUNK = 4096;  // elements per chunk (multiple of 8 * AR_THREADS / 2)
+constexpr int AR_CHUNK_DEFAULT = 4096;  // elements per chunk; any multiple of 8 * AR_THREADS
 
 template <class T>
 struct Elt;
@@ -56,6 +56,7 @@ struct ArArgs {
   int64_t out_off;   // T [nch * CHUNK]
   int64_t flag_off;  // u32 [nch]
   int64_t sq_off;    // fp32 [nch]: per-chunk sum of squares of the result, on every rank (< 0: none)
+  int64_t chunk;     // elements per chunk
   uint32_t epoch;
   int* ticket;
   int* status;
@@ -67,7 +68,8 @@ __global__ void __launch_bounds__(AR_THREADS) allreduce_kernel(const __grid_cons
   __shared__ float s_red[AR_THREADS / 32];
   const int t = threadIdx.x;
   const int S = a.P.world, r = a.P.rank;
-  const int64_t nch = (a.n + AR_CHUNK - 1) / AR_CHUNK;
+  const int64_t CH = a.chunk;
+  const int64_t nch = (a.n + CH - 1) / CH;
   const int64_t per_owner = (nch + S - 1) / S;  // land slots per source
   const int64_t n_own = (nch - r + S - 1) / S;   // chunks r, r+S, ...
   const T* x = reinterpret_cast<const T*>(a.x);
@@ -80,12 +82,12 @@ __global__ void __launch_bounds__(AR_THREADS) allreduce_kernel(const __grid_cons
     if (tk < nch) {
       const int64_t c = (tk + int64_t(r) * per_owner) % nch;  // spread the receivers
       const int o = int(c % S);
-      const int64_t e0 = c * AR_CHUNK;
-      const int64_t len = min(int64_t(AR_CHUNK), a.n - e0);
-      T* dst = at<T>(a.P, o, a.land_off) + (int64_t(r) * per_owner + c / S) * AR_CHUNK;
-      if (len == AR_CHUNK && (reinterpret_cast<uintptr_t>(x + e0) & 15) == 0) {
+      const int64_t e0 = c * CH;
+      const int64_t len = min(CH, a.n - e0);
+      T* dst = at<T>(a.P, o, a.land_off) + (int64_t(r) * per_owner + c / S) * CH;
+      if (len == CH && (reinterpret_cast<uintptr_t>(x + e0) & 15) == 0) {
         constexpr int V = 16 / sizeof(T);
-        for (int v = t; v < AR_CHUNK / V; v += AR_THREADS)
+        for (int v = t; v < CH / V; v += AR_THREADS)
           reinterpret_cast<uint4*>(dst)[v] = __ldg(reinterpret_cast<const uint4*>(x + e0) + v);
       } else {
         for (int64_t e = t; e < len; e += AR_THREADS) dst[e] = x[e0 + e];
@@ -102,19 +104,19 @@ __global__ void __launch_bounds__(AR_THREADS) allreduce_kernel(const __grid_cons
                    : 0;
       __syncthreads();
       if (!s_ok) continue;
-      const int64_t e0 = c * AR_CHUNK;
-      const int64_t len = min(int64_t(AR_CHUNK), a.n - e0);
-      const T* land = at<T>(a.P, r, a.land_off) + (c / S) * AR_CHUNK;
+      const int64_t e0 = c * CH;
+      const int64_t len = min(CH, a.n - e0);
+      const T* land = at<T>(a.P, r, a.land_off) + (c / S) * CH;
       float sq = 0.f;
-      if (len == AR_CHUNK) {
+      if (len == CH) {
         // 16-byte vectors: V elements per thread and step, S loads and S stores of 16 bytes
         constexpr int V = 16 / sizeof(T);
-        for (int v = t; v < AR_CHUNK / V; v += AR_THREADS) {
+        for (int v = t; v < CH / V; v += AR_THREADS) {
           float acc[V];
 #pragma unroll
           for (int i = 0; i < V; ++i) acc[i] = 0.f;
           for (int s = 0; s < S; ++s) {
-            const uint4 q = __ldcg(reinterpret_cast<const uint4*>(land + int64_t(s) * per_owner * AR_CHUNK) + v);
+            const uint4 q = __ldcg(reinterpret_cast<const uint4*>(land + int64_t(s) * per_owner * CH) + v);
             const T* qe = reinterpret_cast<const T*>(&q);
 #pragma unroll
             for (int i = 0; i < V; ++i) acc[i] += Elt<T>::to_f(qe[i]);
@@ -133,7 +135,7 @@ __global__ void __launch_bounds__(AR_THREADS) allreduce_kernel(const __grid_cons
       } else {
         for (int64_t e = t; e < len; e += AR_THREADS) {
           float acc = 0.f;
-          for (int s = 0; s < S; ++s) acc += Elt<T>::ld(land + int64_t(s) * per_owner * AR_CHUNK + e);
+          for (int s = 0; s < S; ++s) acc += Elt<T>::ld(land + int64_t(s) * per_owner * CH + e);
           const T v = Elt<T>::from_f(acc * a.scale);
           const float vr = Elt<T>::to_f(v);
           sq += vr * vr;
@@ -318,10 +320,11 @@ static int p2p_sm_count() {
 
 // Slab bytes the all-reduce needs for n elements of `elem_bytes` on `world` ranks:
 // returns (land, counters, out, flags) sizes; callers place them at 256-byte aligned offsets.
-std::vector<int64_t> p2p_allreduce_sizes(int64_t n, int64_t elem_bytes, int64_t world) {
-  const int64_t nch = (n + p2p::AR_CHUNK - 1) / p2p::AR_CHUNK;
+std::vector<int64_t> p2p_allreduce_sizes(int64_t n, int64_t elem_bytes, int64_t world, int64_t chunk) {
+  if (chunk <= 0) chunk = p2p::AR_CHUNK_DEFAULT;
+  const int64_t nch = (n + chunk - 1) / chunk;
   const int64_t per_owner = (nch + world - 1) / world;
-  return {world * per_owner * p2p::AR_CHUNK * elem_bytes, nch * 4, nch * p2p::AR_CHUNK * elem_bytes, nch * 4};
+  return {world * per_owner * chunk * elem_bytes, nch * 4, nch * chunk * elem_bytes, nch * 4};
 }
 
 // Sum `x` (fp32 or bf16, [n]) over the group, times `scale`; the result lands in the `out` area
@@ -330,7 +333,7 @@ std::vector<int64_t> p2p_allreduce_sizes(int64_t n, int64_t elem_bytes, int64_t 
 // [nch] at sq_off), e.g. for the norm of an averaged gradient.
 void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64_t>& peer_bases, int64_t rank,
                    int64_t land_off, int64_t cnt_off, int64_t out_off, int64_t flag_off, int64_t epoch,
-                   const torch::Tensor& ticket, const torch::Tensor& status, int64_t sq_off) {
+                   const torch::Tensor& ticket, const torch::Tensor& status, int64_t sq_off, int64_t chunk) {
   const int64_t S = int64_t(peer_bases.size());
   TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "p2p_allreduce: bad group");
   TORCH_CHECK(x.is_cuda() && x.is_contiguous() && (x.scalar_type() == at::kFloat || x.scalar_type() == at::kBFloat16),
@@ -338,9 +341,12 @@ void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64
   TORCH_CHECK(land_off % 16 == 0 && out_off % 16 == 0, "p2p_allreduce: offsets must be 16-byte aligned");
   const int64_t n = x.numel();
   if (n == 0) return;
+  if (chunk <= 0) chunk = p2p::AR_CHUNK_DEFAULT;
+  TORCH_CHECK(chunk % (8 * p2p::AR_THREADS) == 0, "p2p_allreduce: chunk must be a multiple of ", 8 * p2p::AR_THREADS);
   const at::cuda::CUDAGuard guard(x.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   p2p::ArArgs a{};
+  a.chunk = chunk;
   a.x = x.data_ptr();
   a.n = n;
   a.scale = float(scale);
@@ -354,7 +360,7 @@ void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64
   a.ticket = ticket.data_ptr<int>();
   a.status = status.data_ptr<int>();
   C10_CUDA_CHECK(cudaMemsetAsync(a.ticket, 0, sizeof(int), stream));
-  const int64_t nch = (n + p2p::AR_CHUNK - 1) / p2p::AR_CHUNK;
+  const int64_t nch = (n + chunk - 1) / chunk;
   const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(2 * nch, int64_t(p2p_sm_count()) * 8));
   if (x.scalar_type() == at::kFloat)
     p2p::allreduce_kernel<float><<<dim3(grid), dim3(p2p::AR_THREADS), 0, stream>>>(a);

@@ -8,6 +8,9 @@
         batch 4096; about 2 GB on the device), the case used for ncu captures of the fused kernels.
     python -m saelens_b200.perf_cases gemm [--pair 0|1]
         Encoder GEMM numerics against fp32 and CUDA-event TFLOP/s on the benchmark shapes.
+    python -m saelens_b200.perf_cases allreduce
+        P2P two-shot all-reduce kernel vs NCCL all_reduce (bf16, sum) over sizes and chunk sizes,
+        under torch.distributed.run; bus bandwidth = 2 (S-1)/S bytes / time, max time over ranks.
     python -m saelens_b200.perf_cases ddp [--d-sae 131072 --k 64 --batch 8192 --steps 10]
         Data-parallel TopK step (replicated SAE, P2P gradient all-reduce) under
         torch.distributed.run: ms/step (max over ranks) and per-phase times.
@@ -172,6 +175,76 @@ def ddp(args: argparse.Namespace) -> None:
     dist.destroy_process_group()
 
 
+def allreduce(args: argparse.Namespace) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from saelens_b200.ops import native
+    from saelens_b200.ops.status import StatusWord
+    from saelens_b200.parallel.symm_heap import SlabBuffer, SymmetricHeap
+
+    world, rank, _ = _init_dist()
+    nat = native()
+    st = StatusWord("cuda")
+    tk = torch.zeros(1, dtype=torch.int32, device="cuda")
+    sizes = [1 << 20, 16 << 20, 256 << 20, 1 << 30]  # bytes
+    chunks = [4096, 16384, 65536]
+    need = max(sum(nat.p2p_allreduce_sizes(n // 2, 2, world, c)) for n in sizes for c in chunks) + (1 << 20)
+    heap = SymmetricHeap(dist.group.WORLD, need)
+
+    def timed(fn, reps: int) -> float:
+        fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / reps], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    rows = []
+    for nbytes in sizes:
+        n = nbytes // 2
+        x = torch.randn(n, device="cuda").to(torch.bfloat16)
+        reps = 20 if nbytes <= (16 << 20) else 5
+        y = x.clone()
+        ms = timed(lambda: dist.all_reduce(y), reps)
+        bus = 2 * (world - 1) / world * nbytes / ms / 1e6
+        rows.append({"bytes": nbytes, "impl": "nccl", "ms": round(ms, 4), "busbw_GBs": round(bus, 1)})
+        for c in chunks:
+            land, cnt, out, flag = nat.p2p_allreduce_sizes(n, 2, world, c)
+            heap._top = 0
+            o_land, o_cnt = heap.alloc_bytes(land), heap.alloc_bytes(cnt)
+            o_out, o_flag = heap.alloc_bytes(out), heap.alloc_bytes(flag)
+            ep = [0]
+
+            def run() -> None:
+                ep[0] += 1
+                nat.p2p_allreduce(x, 1.0, heap.bases, rank, o_land, o_cnt, o_out, o_flag, ep[0], tk, st.tensor,
+                                  -1, c)
+
+            # fresh counters for this layout: zero them on every rank, then agree before use
+            torch.cuda.synchronize()
+            heap.local(SlabBuffer(o_cnt, (cnt // 4,), torch.int32)).zero_()
+            heap.local(SlabBuffer(o_flag, (flag // 4,), torch.int32)).zero_()
+            torch.cuda.synchronize()
+            dist.barrier()
+            ms = timed(run, reps)
+            st.check("allreduce")
+            bus = 2 * (world - 1) / world * nbytes / ms / 1e6
+            rows.append({"bytes": nbytes, "impl": f"p2p chunk {c}", "ms": round(ms, 4), "busbw_GBs": round(bus, 1)})
+        del x, y
+    if rank == 0:
+        for r in rows:
+            print(json.dumps(r), flush=True)
+    heap.close()
+    dist.destroy_process_group()
+
+
 def main() -> None:
     p = argparse.ArgumentParser(prog="python -m saelens_b200.perf_cases")
     sub = p.add_subparsers(dest="cmd", required=True)
@@ -188,8 +261,9 @@ def main() -> None:
     d.add_argument("--batch", type=int, default=8192)
     d.add_argument("--steps", type=int, default=10)
     d.add_argument("--segments", type=int, default=4)
+    sub.add_parser("allreduce")
     args = p.parse_args()
-    {"phases": phases, "fused-case": fused_case, "gemm": gemm, "ddp": ddp}[args.cmd](args)
+    {"phases": phases, "fused-case": fused_case, "gemm": gemm, "ddp": ddp, "allreduce": allreduce}[args.cmd](args)
 
 
 if __name__ == "__main__":
