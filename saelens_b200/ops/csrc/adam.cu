@@ -103,70 +103,83 @@ struct RowArgs {
 };
 
 constexpr int ROW_THREADS = 256;  // 8 warps, one latent row per warp
-constexpr int ROW_UNROLL = 4;
+constexpr int ROW_UNROLL = 2;
 
-// Adam on 4 consecutive elements of one row; streaming (evict-first) loads and stores since
-// every byte of optimizer state is touched exactly once per step.
-__device__ __forceinline__ float4 adam_vec4(float* P, float* Mm, float* V, __nv_bfloat16* W,
-                                            const __nv_bfloat16* G, int64_t off, bool has_g, float c,
-                                            const Hyper& h, int update) {
-  float4 p = __ldcs(reinterpret_cast<const float4*>(P + off));
-  if (update) {
-    float4 m = __ldcs(reinterpret_cast<const float4*>(Mm + off));
-    float4 v = __ldcs(reinterpret_cast<const float4*>(V + off));
-    float g0 = 0.f, g1 = 0.f, g2 = 0.f, g3 = 0.f;
-    if (has_g) {
-      const uint2 gr = __ldcs(reinterpret_cast<const uint2*>(G + off));
-      const __nv_bfloat162* g2p = reinterpret_cast<const __nv_bfloat162*>(&gr);
-      const float2 a = __bfloat1622float2(g2p[0]), b = __bfloat1622float2(g2p[1]);
-      g0 = a.x * c; g1 = a.y * c; g2 = b.x * c; g3 = b.y * c;
-    }
-    adam_update(p.x, m.x, v.x, g0, h);
-    adam_update(p.y, m.y, v.y, g1, h);
-    adam_update(p.z, m.z, v.z, g2, h);
-    adam_update(p.w, m.w, v.w, g3, h);
-    __stcs(reinterpret_cast<float4*>(P + off), p);
-    __stcs(reinterpret_cast<float4*>(Mm + off), m);
-    __stcs(reinterpret_cast<float4*>(V + off), v);
-  }
-  __nv_bfloat162 lo = __floats2bfloat162_rn(p.x, p.y), hi = __floats2bfloat162_rn(p.z, p.w);
-  uint2 o;
-  o.x = *reinterpret_cast<uint32_t*>(&lo);
-  o.y = *reinterpret_cast<uint32_t*>(&hi);
-  *reinterpret_cast<uint2*>(W + off) = o;  // the bf16 copy is read by the next GEMM: keep in L2
-  const float2 a = __bfloat1622float2(lo), b = __bfloat1622float2(hi);
-  return make_float4(a.x, a.y, b.x, b.y);
+__device__ __forceinline__ void unpack_g(const uint2& gr, float c, float* g) {
+  const __nv_bfloat162* g2p = reinterpret_cast<const __nv_bfloat162*>(&gr);
+  const float2 x = __bfloat1622float2(g2p[0]), y = __bfloat1622float2(g2p[1]);
+  g[0] = x.x * c;
+  g[1] = x.y * c;
+  g[2] = y.x * c;
+  g[3] = y.y * c;
 }
 
+// One warp per latent row.  Each iteration first issues every load of ROW_UNROLL 16-byte groups of
+// both matrices (master, m, v, gradient), then does the math and the stores, so a thread keeps
+// 2 * ROW_UNROLL * 56 bytes in flight instead of one group's worth.
 __global__ void __launch_bounds__(ROW_THREADS) rows_kernel(RowArgs a, Hyper h) {
   const float c = (a.update && a.clip) ? *a.clip : 1.f;
   const int nv4 = a.D >> 2;
   const int lane = threadIdx.x & 31;
   const int warps_total = gridDim.x * (ROW_THREADS / 32);
+  float* const Pm[2] = {a.pd, a.pe};
+  float* const Mm[2] = {a.md, a.me};
+  float* const Vm[2] = {a.vd, a.ve};
+  __nv_bfloat16* const Wm[2] = {a.wd, a.we};
+  const __nv_bfloat16* const Gm[2] = {a.gd, a.ge};
   for (int j = blockIdx.x * (ROW_THREADS / 32) + (threadIdx.x >> 5); j < a.N; j += warps_total) {
     const bool has_g = a.update && a.colptr && (a.colptr[j + 1] > a.colptr[j]);
     const int64_t base = int64_t(j) * a.D;
     float nrm = 0.f, dot = 0.f;
     for (int s0 = lane; s0 < nv4; s0 += 32 * ROW_UNROLL) {
-      float4 wd[ROW_UNROLL], we[ROW_UNROLL];
+      float4 P[2][ROW_UNROLL], M[2][ROW_UNROLL], V[2][ROW_UNROLL];
+      uint2 G[2][ROW_UNROLL];
 #pragma unroll
       for (int u = 0; u < ROW_UNROLL; ++u) {
         const int s = s0 + 32 * u;
         if (s < nv4) {
           const int64_t off = base + 4 * int64_t(s);
-          wd[u] = adam_vec4(a.pd, a.md, a.vd, a.wd, a.gd, off, has_g, c, h, a.update);
-          we[u] = adam_vec4(a.pe, a.me, a.ve, a.we, a.ge, off, has_g, c, h, a.update);
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            P[t][u] = __ldcs(reinterpret_cast<const float4*>(Pm[t] + off));
+            if (a.update) {
+              M[t][u] = __ldcs(reinterpret_cast<const float4*>(Mm[t] + off));
+              V[t][u] = __ldcs(reinterpret_cast<const float4*>(Vm[t] + off));
+            }
+            G[t][u] = has_g ? __ldcs(reinterpret_cast<const uint2*>(Gm[t] + off)) : make_uint2(0, 0);
+          }
         }
       }
 #pragma unroll
       for (int u = 0; u < ROW_UNROLL; ++u) {
         const int s = s0 + 32 * u;
-        if (s < nv4) {
-          nrm += wd[u].x * wd[u].x + wd[u].y * wd[u].y + wd[u].z * wd[u].z + wd[u].w * wd[u].w;
-          if (a.b_dec) {
-            const float4 bd = __ldg(reinterpret_cast<const float4*>(a.b_dec) + s);
-            dot += we[u].x * bd.x + we[u].y * bd.y + we[u].z * bd.z + we[u].w * bd.w;
+        if (s >= nv4) continue;
+        const int64_t off = base + 4 * int64_t(s);
+        float4 bd = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (a.b_dec) bd = __ldg(reinterpret_cast<const float4*>(a.b_dec) + s);
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          float4 p = P[t][u];
+          if (a.update) {
+            float4 m = M[t][u], v = V[t][u];
+            float g[4];
+            unpack_g(G[t][u], c, g);
+            adam_update(p.x, m.x, v.x, g[0], h);
+            adam_update(p.y, m.y, v.y, g[1], h);
+            adam_update(p.z, m.z, v.z, g[2], h);
+            adam_update(p.w, m.w, v.w, g[3], h);
+            __stcs(reinterpret_cast<float4*>(Pm[t] + off), p);
+            __stcs(reinterpret_cast<float4*>(Mm[t] + off), m);
+            __stcs(reinterpret_cast<float4*>(Vm[t] + off), v);
           }
+          const __nv_bfloat162 lo = __floats2bfloat162_rn(p.x, p.y), hi = __floats2bfloat162_rn(p.z, p.w);
+          uint2 o;
+          o.x = *reinterpret_cast<const uint32_t*>(&lo);
+          o.y = *reinterpret_cast<const uint32_t*>(&hi);
+          *reinterpret_cast<uint2*>(Wm[t] + off) = o;  // read by the next GEMM: keep in L2
+          const float2 x = __bfloat1622float2(lo), y = __bfloat1622float2(hi);
+          if (t == 0) nrm += x.x * x.x + x.y * x.y + y.x * y.x + y.y * y.y;
+          else dot += x.x * bd.x + x.y * bd.y + y.x * bd.z + y.y * bd.w;
         }
       }
     }

@@ -98,6 +98,8 @@ void p2p_signal(const std::vector<int64_t>& peer_bases, int64_t rank, int64_t of
 torch::Tensor rmsnorm(const torch::Tensor& x, const torch::Tensor& w, double eps, bool one_plus);
 void rope_(const torch::Tensor& x, const torch::Tensor& cos, const torch::Tensor& sin, int64_t pos0);
 torch::Tensor gated_act(const torch::Tensor& gate, const torch::Tensor& up, int64_t kind);
+torch::Tensor batch_topk_select(const torch::Tensor& vals, const torch::Tensor& idx, int64_t K,
+                                const c10::optional<torch::Tensor>& truncated);
 }  // namespace sb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -130,6 +132,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_wait_targets", &sb::p2p_wait_targets);
   m.def("p2p_signal", &sb::p2p_signal);
   m.def("rmsnorm", &sb::rmsnorm);
+  m.def("batch_topk_select", &sb::batch_topk_select);
   m.def("rope_", &sb::rope_);
   m.def("gated_act", &sb::gated_act);
   m.def("symm_alloc", &sb::symm_alloc);

@@ -417,6 +417,125 @@ __global__ void __launch_bounds__(THREADS) topk_exchange_merge_kernel(const __gr
   }
 }
 
+
+// ---------------------------------------------------------------------------------------
+// Batch top-k (BatchTopK SAEs: keep the k*B largest ReLU activations of the whole batch,
+// sae_lens/saes/batchtopk_sae.py:13-33).  Input: per-row candidate lists (the per-row top-k_cap
+// of the row top-k kernel, values exact bf16).  The global threshold comes from a 65536-bin
+// histogram of the candidates' 16-bit keys (positive values only): the largest key whose
+// suffix count reaches K.  Entries above the threshold are kept; ties at it are kept in (row,
+// latent index) order until K entries are selected.  Unselected entries get idx -1.  A row
+// whose k_cap-th candidate is still above the threshold may have lost entries to the per-row
+// cap; those rows are counted in `truncated`.
+// ---------------------------------------------------------------------------------------
+__global__ void batch_hist_kernel(const float* __restrict__ vals, const int* __restrict__ idx, int64_t n,
+                                  uint32_t* __restrict__ hist) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+    const float v = vals[i];
+    if (idx[i] >= 0 && v > 0.f) atomicAdd(hist + bf16_to_key(uint16_t(__float_as_uint(v) >> 16)), 1u);
+  }
+}
+
+// One CTA: find the threshold key and how many ties at it to keep.  sel[0] = key (0 if fewer than
+// K positive candidates: keep every positive one), sel[1] = ties to keep, sel[2] = strictly-above count.
+__global__ void batch_thresh_kernel(const uint32_t* __restrict__ hist, int64_t K, int* __restrict__ sel) {
+  __shared__ uint32_t part[1024];
+  __shared__ int s_found;
+  const int t = threadIdx.x;  // 1024 threads x 64 bins, bins scanned from the top
+  uint32_t sum = 0;
+  for (int b = 0; b < 64; ++b) sum += hist[65535 - (t * 64 + b)];
+  part[t] = sum;
+  if (t == 0) s_found = 0;
+  __syncthreads();
+  if (t == 0) {
+    uint64_t acc = 0;
+    int found = 0;
+    for (int c = 0; c < 1024 && !found; ++c) {
+      if (acc + part[c] >= uint64_t(K)) {
+        for (int b = 0; b < 64; ++b) {
+          const int key = 65535 - (c * 64 + b);
+          const uint32_t h = hist[key];
+          if (acc + h >= uint64_t(K)) {
+            sel[0] = key;
+            sel[1] = int(K - int64_t(acc));
+            sel[2] = int(acc);
+            found = 1;
+            break;
+          }
+          acc += h;
+        }
+      } else {
+        acc += part[c];
+      }
+    }
+    if (!found) {  // fewer than K positive candidates: keep them all
+      sel[0] = 0x8000;  // key of +0.0: every positive value is strictly above it
+      sel[1] = 0;
+      sel[2] = int(acc);
+    }
+    s_found = found;
+  }
+}
+
+// Per row: ties at the threshold key (counted for the prefix over rows).
+__global__ void batch_ties_kernel(const float* __restrict__ vals, const int* __restrict__ idx, int M, int kc,
+                                  const int* __restrict__ sel, int* __restrict__ ties) {
+  const int key = sel[0];
+  for (int row = blockIdx.x * blockDim.y + threadIdx.y; row < M; row += gridDim.x * blockDim.y) {
+    int c = 0;
+    for (int i = threadIdx.x; i < kc; i += 32) {
+      const int64_t o = int64_t(row) * kc + i;
+      const float v = vals[o];
+      c += (idx[o] >= 0 && v > 0.f && int(bf16_to_key(uint16_t(__float_as_uint(v) >> 16))) == key) ? 1 : 0;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+    if (threadIdx.x == 0) ties[row] = c;
+  }
+}
+
+// Per row: keep entries above the key, and ties while the global tie rank (rows before + smaller
+// latent index within the row) is below the tie budget.  tie_prefix = exclusive prefix of ties.
+__global__ void batch_filter_kernel(const float* __restrict__ vals, int* __restrict__ idx, int M, int kc,
+                                    const int* __restrict__ sel, const int64_t* __restrict__ tie_prefix,
+                                    int* __restrict__ truncated) {
+  const int key = sel[0];
+  const int64_t budget = sel[1];
+  for (int row = blockIdx.x * blockDim.y + threadIdx.y; row < M; row += gridDim.x * blockDim.y) {
+    const int64_t before = tie_prefix[row];
+    uint32_t keep_bits = 0;  // bit m: entry lane + 32 m is kept (kc <= 1024)
+    int kept = 0;
+    for (int m = 0, i = threadIdx.x; i < kc; ++m, i += 32) {
+      const int64_t o = int64_t(row) * kc + i;
+      const int j = idx[o];
+      const float v = vals[o];
+      bool keep = false;
+      if (j >= 0 && v > 0.f) {
+        const int kk = int(bf16_to_key(uint16_t(__float_as_uint(v) >> 16)));
+        if (kk > key) {
+          keep = true;
+        } else if (kk == key && budget > before) {
+          int rank = 0;  // ties of this row with a smaller latent index
+          for (int q = 0; q < kc; ++q) {
+            const int64_t oq = int64_t(row) * kc + q;
+            const float vq = vals[oq];
+            rank += (idx[oq] >= 0 && idx[oq] < j && vq > 0.f &&
+                     int(bf16_to_key(uint16_t(__float_as_uint(vq) >> 16))) == key) ? 1 : 0;
+          }
+          keep = before + rank < budget;
+        }
+      }
+      keep_bits |= uint32_t(keep) << m;
+      kept += keep;
+    }
+    __syncwarp();  // every lane has read the row before any slot is cleared
+    for (int m = 0, i = threadIdx.x; i < kc; ++m, i += 32)
+      if (!((keep_bits >> m) & 1u)) idx[int64_t(row) * kc + i] = -1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) kept += __shfl_xor_sync(0xffffffffu, kept, o);
+    if (threadIdx.x == 0 && truncated && kept == kc) atomicAdd(truncated, 1);
+  }
+}
 }  // namespace topk
 
 void topk_merge(const torch::Tensor& cand_val, const torch::Tensor& cand_idx, int64_t n_local, int64_t rank,
@@ -533,6 +652,44 @@ void topk_exchange_merge(const torch::Tensor& vals, const torch::Tensor& idx, in
   const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(2 * B / topk::XM_RB, int64_t(nsm) * std::max(occ, 1)));
   topk::topk_exchange_merge_kernel<<<dim3(grid), dim3(topk::THREADS), smem, stream>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Keep the K = round(k * rows) largest positive candidate values of the whole batch (see
+// batch_hist_kernel).  vals/idx [M, kc] from row_topk; idx is updated in place (-1 = dropped).
+// Returns int32 [3] on the device: threshold key, ties kept, count above the threshold; and
+// counts rows whose whole candidate list was kept into `truncated` (int32 [1], optional).
+torch::Tensor batch_topk_select(const torch::Tensor& vals, const torch::Tensor& idx, int64_t K,
+                                const c10::optional<torch::Tensor>& truncated) {
+  TORCH_CHECK(vals.is_cuda() && vals.is_contiguous() && idx.is_contiguous() && vals.scalar_type() == at::kFloat &&
+                  idx.scalar_type() == at::kInt && vals.sizes() == idx.sizes() && vals.dim() == 2,
+              "batch_topk_select: vals/idx must be contiguous fp32/int32 [M, kc]");
+  const int64_t M = vals.size(0), kc = vals.size(1);
+  TORCH_CHECK(kc <= 1024, "batch_topk_select: at most 1024 candidates per row");
+  const at::cuda::CUDAGuard guard(vals.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto opts = vals.options();
+  auto hist = torch::zeros({65536}, opts.dtype(at::kInt));
+  auto sel = torch::empty({3}, opts.dtype(at::kInt));
+  auto ties = torch::empty({std::max<int64_t>(M, 1)}, opts.dtype(at::kInt));
+  if (M == 0) return sel.zero_();
+  int dev = 0, nsm = 0;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  C10_CUDA_CHECK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t n = M * kc;
+  topk::batch_hist_kernel<<<dim3(int(std::min<int64_t>((n + 255) / 256, int64_t(nsm) * 8))), 256, 0, stream>>>(
+      vals.data_ptr<float>(), idx.data_ptr<int>(), n, reinterpret_cast<uint32_t*>(hist.data_ptr<int>()));
+  topk::batch_thresh_kernel<<<1, 1024, 0, stream>>>(reinterpret_cast<const uint32_t*>(hist.data_ptr<int>()), K,
+                                                    sel.data_ptr<int>());
+  const dim3 blk(32, 8);
+  const int grid = int(std::min<int64_t>((M + 7) / 8, int64_t(nsm) * 16));
+  topk::batch_ties_kernel<<<grid, blk, 0, stream>>>(vals.data_ptr<float>(), idx.data_ptr<int>(), int(M), int(kc),
+                                                    sel.data_ptr<int>(), ties.data_ptr<int>());
+  auto prefix = torch::cumsum(ties.narrow(0, 0, M).to(at::kLong), 0) - ties.narrow(0, 0, M).to(at::kLong);
+  topk::batch_filter_kernel<<<grid, blk, 0, stream>>>(vals.data_ptr<float>(), idx.data_ptr<int>(), int(M), int(kc),
+                                                      sel.data_ptr<int>(), prefix.data_ptr<int64_t>(),
+                                                      truncated ? truncated->data_ptr<int>() : nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return sel;
 }
 
 }  // namespace sb

@@ -114,6 +114,8 @@ class TPTopKEngine(FusedTopKEngine):
         self.input_layout = input_layout
         super().__init__(sae, lr=lr, beta1=beta1, beta2=beta2, eps=eps, max_grad_norm=max_grad_norm,
                          h_buffer_bytes=h_buffer_bytes)
+        if self.batch_topk:
+            raise NotImplementedError("latent-sharded BatchTopK trains on the PyTorch path")
         self.n_local = self.N
         self.collectives = 0
         self.fused = bool(fused) and self.size <= 8

@@ -93,7 +93,16 @@ class FusedTopKEngine:
         self.native = ops.native()
         self.sae = sae
         cfg = sae.cfg
-        self.k = int(cfg.k)
+        # BatchTopK: keep the k * B largest activations of the batch.  Each row contributes its
+        # top `batch_topk_cap` candidates (4k by default) to the batch-wide selection.
+        from saelens_b200.models.batchtopk import BatchTopKTrainingSAE
+
+        self.batch_topk = isinstance(sae, BatchTopKTrainingSAE)
+        self.batch_k = float(cfg.k)
+        if self.batch_topk:
+            self.k = int(min(1024, sae.cfg.d_sae, max(1, round(4 * float(cfg.k)))))
+        else:
+            self.k = int(cfg.k)
         self.rescale = bool(cfg.rescale_acts_by_decoder_norm)
         self.aux_coef = float(getattr(cfg, "aux_loss_coefficient", 1.0))
         self.apply_b_dec = bool(cfg.apply_b_dec_to_input)
@@ -140,6 +149,7 @@ class FusedTopKEngine:
         self.cursor = torch.zeros(self.N, dtype=torch.int32, device=dev)
         self.colptr = torch.zeros(self.N + 1, dtype=torch.int64, device=dev)
         self.status = StatusWord(dev)
+        self.batch_truncated = torch.zeros(1, dtype=torch.int32, device=dev)  # rows whose candidate cap was hit
         self.h_buffer_bytes = h_buffer_bytes
         self.step_count = 0  # Adam steps taken
         self.launches = 0    # native kernel launches issued by step() so far
@@ -289,6 +299,16 @@ class FusedTopKEngine:
                 nat.row_topk(h, c, k_aux, k_aux_dev, mask_words, aux_vals[r0:r1], aux_idx[r0:r1],
                              self.status.tensor)
         del H, cm
+        if self.batch_topk:
+            # batch-wide selection among the per-row candidates (k * B largest ReLU activations)
+            nat.batch_topk_select(vals, idx, int(round(self.batch_k * B)), self.batch_truncated)
+            self.launches += 4
+            kept = torch.where(idx >= 0, vals, torch.full_like(vals, float("inf"))).amin()
+            thr = self.sae.topk_threshold
+            lr_t = float(self.sae.cfg.topk_threshold_lr)
+            new_thr = torch.where(torch.isfinite(kept), (1 - lr_t) * thr + lr_t * kept.to(thr.dtype), thr)
+            thr.copy_(new_thr)
+            self._mark("batch_topk_select")
 
         # 3. decode + MSE + dL/dx_hat (+ sum over rows for the b_dec gradient)
         sae_out = torch.empty(B, D, dtype=torch.bfloat16, device=dev) if (want_sae_out or aux_on) else None
@@ -373,7 +393,9 @@ def engine_supported(sae: Any) -> bool:
 
     if type(sae).__name__ != "TopKTrainingSAE" and not isinstance(sae, TopKTrainingSAE):
         return False
-    if type(sae) is not TopKTrainingSAE:  # BatchTopK / Matryoshka need their own selection
+    from saelens_b200.models.batchtopk import BatchTopKTrainingSAE
+
+    if type(sae) not in (TopKTrainingSAE, BatchTopKTrainingSAE):  # Matryoshka: nested-width losses
         return False
     if not sae.W_dec.is_cuda or not ops.available():
         return False

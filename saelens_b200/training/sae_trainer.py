@@ -164,13 +164,14 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
             from saelens_b200.training.engine import FusedTopKEngine, engine_supported
 
             tp_group = getattr(self._base_sae, "_tp_group", None)
-            if engine_supported(self._base_sae) and tp_group is not None:
+            batch_topk = type(self._base_sae).__name__ == "BatchTopKTrainingSAE"
+            if engine_supported(self._base_sae) and tp_group is not None and not batch_topk:
                 from saelens_b200.parallel.tp_engine import TPTopKEngine
 
                 self.engine = TPTopKEngine(self._base_sae, lr=cfg.lr, group=tp_group, beta1=cfg.adam_beta1,
                                            beta2=cfg.adam_beta2, input_layout=tp_input_layout,
                                            fused=getattr(cfg, "tp_exchange", "p2p") == "p2p")
-            elif engine_supported(self._base_sae):
+            elif engine_supported(self._base_sae) and tp_group is None:
                 self.engine = FusedTopKEngine(self._base_sae, lr=cfg.lr, beta1=cfg.adam_beta1,
                                               beta2=cfg.adam_beta2)
             elif want == "native":

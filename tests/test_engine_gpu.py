@@ -150,3 +150,58 @@ def test_engine_aux_loss_matches_reference():
     ref_aux = out.losses["auxiliary_reconstruction_loss"].item()
     assert ref_aux > 0
     assert abs(res.aux_loss.item() - ref_aux) <= 5e-2 * ref_aux
+
+
+def test_batchtopk_engine_selection_and_gradients():
+    """BatchTopK on the fused engine: exactly k*B activations are kept batch-wide (the largest ReLU
+    values up to bf16 ties), rows keep variable counts, gradients match fp32 autograd on the
+    engine's selection, and the threshold EMA moves toward the smallest kept activation."""
+    from saelens_b200.models.batchtopk import BatchTopKTrainingSAE, BatchTopKTrainingSAEConfig
+    from saelens_b200.training.engine import FusedTopKEngine
+
+    torch.manual_seed(0)
+    sae = BatchTopKTrainingSAE(BatchTopKTrainingSAEConfig(d_in=256, d_sae=2048, k=16, device="cuda"))
+    with torch.no_grad():
+        sae.b_enc.normal_(0, 0.01)
+        sae.b_dec.normal_(0, 0.05)
+    x = torch.randn(512, 256, device="cuda").to(torch.bfloat16)
+    eng = FusedTopKEngine(sae, lr=1e-3)
+    w_enc0, w_dec0 = eng.w_enc.clone(), eng.w_dec.clone()
+    b_enc0, b_dec0 = eng.p_benc.clone(), eng.p_bdec.clone()
+    res = eng.step(x, update=False)
+    torch.cuda.synchronize()
+    eng.status.check()
+    sel = res.topk_idx >= 0
+    K = 16 * 512
+    assert int(sel.sum()) == K
+    per_row = sel.sum(1)
+    assert per_row.max() > per_row.min()  # a batch-wide, not per-row, selection
+    assert int(eng.batch_truncated.item()) == 0
+    # oracle pre-activations (fp32 of the bf16 compute copies)
+    We, Wd = w_enc0.float().T, w_dec0.float()
+    norm = Wd.norm(dim=-1)
+    h = ((x.float() - b_dec0) @ We + b_enc0) * norm
+    kth = torch.topk(h.relu().flatten(), K).values[-1]
+    chosen = torch.gather(h, 1, res.topk_idx.clamp(min=0).long())[sel]
+    assert (chosen >= kth - 0.02 * kth.abs() - 1e-3).all()
+    # gradients against fp32 autograd with the engine's selection as the mask
+    mask = torch.zeros_like(h, dtype=torch.bool)
+    rows = torch.arange(512, device="cuda")[:, None].expand_as(res.topk_idx)
+    mask[rows[sel], res.topk_idx[sel].long()] = True
+    Wd_ = Wd.clone().requires_grad_(True)
+    We_ = We.clone().requires_grad_(True)
+    be = b_enc0.clone().requires_grad_(True)
+    bd = b_dec0.clone().requires_grad_(True)
+    n_ = Wd_.norm(dim=-1)
+    hh = ((x.float() - bd) @ We_ + be) * n_
+    acts = torch.where(mask, hh.relu(), torch.zeros_like(hh))
+    out = (acts / n_) @ Wd_ + bd
+    mse = (out - x.float()).pow(2).sum(-1).mean()
+    mse.backward()
+    assert abs(res.mse_loss.item() - mse.item()) <= 2e-2 * mse.item()
+    live = (eng.colptr[1:] > eng.colptr[:-1])
+    assert _rel(eng.g_dec[live], Wd_.grad[live]) < 2e-2
+    assert _rel(eng.g_enc[live], We_.grad.T[live]) < 2e-2
+    # threshold EMA: 0.99 * 0 + 0.01 * (smallest kept activation)
+    kept_min = res.topk_vals[sel].min().double()
+    assert torch.allclose(sae.topk_threshold, 0.01 * kept_min, rtol=1e-5)
