@@ -8,10 +8,11 @@ namespace sb {
 void gemm_tn_bf16(const torch::Tensor& A, const torch::Tensor& B, const c10::optional<torch::Tensor>& bias,
                   const c10::optional<torch::Tensor>& scale, bool relu,
                   const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& cmax,
-                  const torch::Tensor& status, int64_t max_ctas);
+                  const torch::Tensor& status, int64_t max_ctas, const c10::optional<torch::Tensor>& tmax);
 void row_topk(const torch::Tensor& H, const torch::Tensor& cmax, int64_t k_max,
               const c10::optional<torch::Tensor>& k_dev, const c10::optional<torch::Tensor>& mask,
-              const torch::Tensor& out_val, const torch::Tensor& out_idx, const torch::Tensor& status);
+              const torch::Tensor& out_val, const torch::Tensor& out_idx, const torch::Tensor& status,
+              const c10::optional<torch::Tensor>& tmax);
 void decode_mse(const torch::Tensor& vals, const torch::Tensor& idx, bool relu,
                 const c10::optional<torch::Tensor>& inv_scale, const torch::Tensor& W,
                 const c10::optional<torch::Tensor>& bias, const torch::Tensor& target,
@@ -65,7 +66,7 @@ void gemm_ag_tn_bf16(const torch::Tensor& x_own, const std::vector<int64_t>& pee
                      bool push, int64_t epoch, const torch::Tensor& B, const c10::optional<torch::Tensor>& bias,
                      const c10::optional<torch::Tensor>& scale, bool relu, const c10::optional<torch::Tensor>& out,
                      const c10::optional<torch::Tensor>& cmax, const torch::Tensor& status,
-                     const torch::Tensor& ticket, int64_t max_ctas);
+                     const torch::Tensor& ticket, int64_t max_ctas, const c10::optional<torch::Tensor>& tmax);
 void decode_rs(const torch::Tensor& vals, const torch::Tensor& idx, bool relu,
                const c10::optional<torch::Tensor>& inv_scale, const torch::Tensor& W,
                const std::vector<int64_t>& peer_bases, int64_t rank, int64_t land_off, int64_t lcnt_off,
@@ -104,8 +105,11 @@ torch::Tensor batch_topk_select(const torch::Tensor& vals, const torch::Tensor& 
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "saelens_b200 sm_100a kernels";
-  m.def("gemm_tn_bf16", &sb::gemm_tn_bf16);
-  m.def("row_topk", &sb::row_topk);
+  m.def("gemm_tn_bf16", &sb::gemm_tn_bf16, py::arg("A"), py::arg("B"), py::arg("bias"), py::arg("scale"),
+        py::arg("relu"), py::arg("out"), py::arg("cmax"), py::arg("status"), py::arg("max_ctas"),
+        py::arg("tmax") = py::none());
+  m.def("row_topk", &sb::row_topk, py::arg("H"), py::arg("cmax"), py::arg("k_max"), py::arg("k_dev"),
+        py::arg("mask"), py::arg("out_val"), py::arg("out_idx"), py::arg("status"), py::arg("tmax") = py::none());
   m.def("decode_mse", &sb::decode_mse);
   m.def("csc_count", &sb::csc_count);
   m.def("csc_fill", &sb::csc_fill);
@@ -119,7 +123,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("topk_merge", &sb::topk_merge);
   m.def("decode_partial", &sb::decode_partial);
   m.def("finish_mse", &sb::finish_mse);
-  m.def("gemm_ag_tn_bf16", &sb::gemm_ag_tn_bf16);
+  m.def("gemm_ag_tn_bf16", &sb::gemm_ag_tn_bf16, py::arg("x_own"), py::arg("peer_bases"), py::arg("rank"),
+        py::arg("x_off"), py::arg("flag_off"), py::arg("total_rows"), py::arg("m_base"), py::arg("M"), py::arg("push"),
+        py::arg("epoch"), py::arg("B"), py::arg("bias"), py::arg("scale"), py::arg("relu"), py::arg("out"),
+        py::arg("cmax"), py::arg("status"), py::arg("ticket"), py::arg("max_ctas"), py::arg("tmax") = py::none());
   m.def("decode_rs", &sb::decode_rs);
   m.def("topk_exchange_merge", &sb::topk_exchange_merge);
   m.def("p2p_allreduce_sizes", &sb::p2p_allreduce_sizes, py::arg("n"), py::arg("elem_bytes"), py::arg("world"),

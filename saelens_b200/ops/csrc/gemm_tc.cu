@@ -60,6 +60,8 @@ struct Epi {
   int relu;                // apply max(., 0) after bias/scale
   __nv_bfloat16* cmax;     // [M, ldc] chunk maxima (one per 32 columns) or nullptr
   int64_t ldc;
+  __nv_bfloat16* tmax;     // [M, ldt] tile maxima (one per 256 columns) or nullptr
+  int64_t ldt;
 };
 
 // All-gather fusion parameters (byte offsets inside the symmetric slabs).
@@ -89,6 +91,7 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mt
 // Epilogue of one accumulator tile: this thread's TMEM lane `trow` holds output row `row`
 // (columns nt*BN .. nt*BN+255): bias, per-column scale, ReLU, bf16 store, 32-column maxima.
 __device__ __forceinline__ void epilogue_tile(const Epi& ep, uint32_t trow, int row, int M, int nt) {
+  float tile_max = -INFINITY;
 #pragma unroll 1
   for (int c = 0; c < BN / 32; ++c) {
     uint32_t r[32];
@@ -142,7 +145,9 @@ __device__ __forceinline__ void epilogue_tile(const Epi& ep, uint32_t trow, int 
       }
       if (ep.cmax) ep.cmax[int64_t(row) * ep.ldc + (col0 >> 5)] = __float2bfloat16_rn(cm);
     }
+    tile_max = fmaxf(tile_max, cm);
   }
+  if (ep.tmax && row < M) ep.tmax[int64_t(row) * ep.ldt + nt] = __float2bfloat16_rn(tile_max);
 }
 
 // All-gather pushers (two warps, ct = 0..63): claim (distance d, own m-tile j) items from the
@@ -545,7 +550,8 @@ static int num_sms_cached() {
 
 static gemm::Epi make_epi(int64_t M, int64_t N, const c10::optional<torch::Tensor>& bias,
                           const c10::optional<torch::Tensor>& scale, bool relu,
-                          const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& cmax) {
+                          const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& cmax,
+                          const c10::optional<torch::Tensor>& tmax = c10::nullopt) {
   gemm::Epi ep{};
   if (out) {
     TORCH_CHECK(out->scalar_type() == at::kBFloat16 && out->size(0) == M && out->size(1) == N &&
@@ -570,6 +576,13 @@ static gemm::Epi make_epi(int64_t M, int64_t N, const c10::optional<torch::Tenso
     TORCH_CHECK(scale->scalar_type() == at::kFloat && scale->numel() == N && scale->is_contiguous(),
                 "gemm_tn_bf16: scale must be fp32 [N]");
     ep.scale = scale->data_ptr<float>();
+  }
+  if (tmax) {
+    TORCH_CHECK(tmax->scalar_type() == at::kBFloat16 && tmax->size(0) == M && tmax->size(1) == N / gemm::BN &&
+                    tmax->stride(1) == 1,
+                "gemm_tn_bf16: bad tmax (bf16 [M, N/256])");
+    ep.tmax = reinterpret_cast<__nv_bfloat16*>(tmax->data_ptr());
+    ep.ldt = tmax->stride(0);
   }
   ep.relu = relu ? 1 : 0;
   return ep;
@@ -644,7 +657,7 @@ static void launch_gemm(const void* a_ptr, int64_t lda, int64_t M, const torch::
 void gemm_tn_bf16(const torch::Tensor& A, const torch::Tensor& B, const c10::optional<torch::Tensor>& bias,
                   const c10::optional<torch::Tensor>& scale, bool relu,
                   const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& cmax,
-                  const torch::Tensor& status, int64_t max_ctas) {
+                  const torch::Tensor& status, int64_t max_ctas, const c10::optional<torch::Tensor>& tmax) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda(), "gemm_tn_bf16: CUDA tensors required");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16,
               "gemm_tn_bf16: bf16 operands required");
@@ -655,7 +668,7 @@ void gemm_tn_bf16(const torch::Tensor& A, const torch::Tensor& B, const c10::opt
   TORCH_CHECK(N % gemm::BN == 0, "gemm_tn_bf16: N must be a multiple of 256, got ", N);
   TORCH_CHECK(M >= 1 && M < (1ll << 31) && N < (1ll << 31), "gemm_tn_bf16: size");
   const at::cuda::CUDAGuard guard(A.device());
-  const gemm::Epi ep = make_epi(M, N, bias, scale, relu, out, cmax);
+  const gemm::Epi ep = make_epi(M, N, bias, scale, relu, out, cmax, tmax);
   launch_gemm<false>(A.data_ptr(), A.stride(0), M, B, ep, status, max_ctas, gemm::Ag{}, use_pair(M));
 }
 
@@ -668,7 +681,7 @@ void gemm_ag_tn_bf16(const torch::Tensor& x_own, const std::vector<int64_t>& pee
                      bool push, int64_t epoch, const torch::Tensor& B, const c10::optional<torch::Tensor>& bias,
                      const c10::optional<torch::Tensor>& scale, bool relu, const c10::optional<torch::Tensor>& out,
                      const c10::optional<torch::Tensor>& cmax, const torch::Tensor& status,
-                     const torch::Tensor& ticket, int64_t max_ctas) {
+                     const torch::Tensor& ticket, int64_t max_ctas, const c10::optional<torch::Tensor>& tmax) {
   const int64_t S = int64_t(peer_bases.size());
   TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "gemm_ag: bad group");
   TORCH_CHECK(x_own.is_cuda() && x_own.scalar_type() == at::kBFloat16 && x_own.is_contiguous(),
@@ -684,7 +697,7 @@ void gemm_ag_tn_bf16(const torch::Tensor& x_own, const std::vector<int64_t>& pee
   TORCH_CHECK(K % gemm::BK == 0 && N % gemm::BN == 0, "gemm_ag: K % 64 and N % 256");
   TORCH_CHECK(x_off % 16 == 0 && flag_off % 4 == 0, "gemm_ag: slab offsets must be aligned");
   const at::cuda::CUDAGuard guard(x_own.device());
-  const gemm::Epi ep = make_epi(M, N, bias, scale, relu, out, cmax);
+  const gemm::Epi ep = make_epi(M, N, bias, scale, relu, out, cmax, tmax);
   gemm::Ag ag{};
   ag.P = p2p::make_peers(peer_bases, rank);
   ag.src = reinterpret_cast<const __nv_bfloat16*>(x_own.data_ptr());

@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(THREADS)
                     const __nv_bfloat16* __restrict__ cmax, int64_t ldc, int N, int k_max,
                     const int* __restrict__ k_dev, const uint32_t* __restrict__ mask,
                     float* __restrict__ out_val, int* __restrict__ out_idx, int64_t ldo,
-                    int* status) {
+                    int* status, const __nv_bfloat16* __restrict__ tmax, int64_t ldtm) {
   __shared__ uint32_t hist[256];
   __shared__ uint32_t sh[4];
   __shared__ int n_cand, n_out;
@@ -151,35 +151,74 @@ __global__ void __launch_bounds__(THREADS)
   }
   __syncthreads();
   if (mask == nullptr) {
-  for (int c = tid; c < NC; c += THREADS) ckeys[c] = uint16_t(bf16_to_key(crow[c]));
-  __syncthreads();
-
-  uint32_t klb = 0;
-  if (NC > k) {
-    klb = block_select16(NC, k, [&](int i) { return uint32_t(ckeys[i]); }, hist, sh).key;
-  }
-
-  // collect candidates: warps sweep 32 chunks at a time
-  for (int base = warp * 32; base < NC; base += THREADS) {
-    const int c = base + lane;
-    const bool is_cand = c < NC && uint32_t(ckeys[c]) >= klb;
-    unsigned m = __ballot_sync(0xffffffffu, is_cand);
-    while (m) {
-      const int bit = __ffs(m) - 1;
-      m &= m - 1;
-      const int col = (base + bit) * 32 + lane;
-      const uint32_t key = bf16_to_key(hrow[col]);
-      const bool keep = key >= klb;
-      const unsigned km = __ballot_sync(0xffffffffu, keep);
-      int basepos = 0;
-      if (lane == 0 && km) basepos = atomicAdd(&n_cand, __popc(km));
-      basepos = __shfl_sync(0xffffffffu, basepos, 0);
-      const int pos = basepos + __popc(km & ((1u << lane) - 1u));
-      if (keep && pos < CAP) {
-        cand_key[pos] = key;
-        cand_idx[pos] = col;
+  // Collect every value >= klb from the listed chunks (warps sweep 32 list entries at a time).
+  auto collect = [&](int n_list, auto chunk_key, auto chunk_id, uint32_t klb) {
+    for (int base = warp * 32; base < n_list; base += THREADS) {
+      const int c = base + lane;
+      const bool is_cand = c < n_list && chunk_key(c) >= klb;
+      unsigned m = __ballot_sync(0xffffffffu, is_cand);
+      while (m) {
+        const int bit = __ffs(m) - 1;
+        m &= m - 1;
+        const int col = chunk_id(base + bit) * 32 + lane;
+        const uint32_t key = bf16_to_key(hrow[col]);
+        const bool keep = key >= klb;
+        const unsigned km = __ballot_sync(0xffffffffu, keep);
+        int basepos = 0;
+        if (lane == 0 && km) basepos = atomicAdd(&n_cand, __popc(km));
+        basepos = __shfl_sync(0xffffffffu, basepos, 0);
+        const int pos = basepos + __popc(km & ((1u << lane) - 1u));
+        if (keep && pos < CAP) {
+          cand_key[pos] = key;
+          cand_idx[pos] = col;
+        }
       }
     }
+  };
+  bool collected = false;
+  const int NT = N >> 8;
+  if (tmax != nullptr && NT > k) {
+    // Two levels: the k-th largest 256-column tile maximum bounds the k-th value from below; only
+    // chunks of tiles at or above it can hold a top-k value, and the k-th largest chunk maximum
+    // among them is the (tighter) bound used to collect candidates.
+    const uint16_t* trow = reinterpret_cast<const uint16_t*>(tmax + int64_t(row) * ldtm);
+    uint16_t* tkeys = ckeys;                  // NT tile keys
+    const int lcap = ((NC - NT) / 2) & ~7;    // chunk-list capacity in the rest of ckeys
+    uint16_t* lkey = ckeys + NT;
+    uint16_t* lidx = lkey + lcap;
+    __shared__ int n_list;
+    for (int t = tid; t < NT; t += THREADS) tkeys[t] = uint16_t(bf16_to_key(trow[t]));
+    if (tid == 0) n_list = 0;
+    __syncthreads();
+    const uint32_t klb0 = block_select16(NT, k, [&](int i) { return uint32_t(tkeys[i]); }, hist, sh).key;
+    for (int t = tid; t < NT; t += THREADS) {
+      if (uint32_t(tkeys[t]) >= klb0) {
+        const int pos = atomicAdd(&n_list, 8);
+        if (pos + 8 <= lcap) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            lkey[pos + j] = uint16_t(bf16_to_key(crow[t * 8 + j]));
+            lidx[pos + j] = uint16_t(t * 8 + j);
+          }
+        }
+      }
+    }
+    __syncthreads();
+    const int nl = n_list;
+    if (nl <= lcap) {
+      const uint32_t klb =
+          block_select16(nl, min(k, nl), [&](int i) { return uint32_t(lkey[i]); }, hist, sh).key;
+      collect(nl, [&](int i) { return uint32_t(lkey[i]); }, [&](int i) { return int(lidx[i]); }, klb);
+      collected = true;
+    }
+    __syncthreads();
+  }
+  if (!collected) {
+    for (int c = tid; c < NC; c += THREADS) ckeys[c] = uint16_t(bf16_to_key(crow[c]));
+    __syncthreads();
+    uint32_t klb = 0;
+    if (NC > k) klb = block_select16(NC, k, [&](int i) { return uint32_t(ckeys[i]); }, hist, sh).key;
+    collect(NC, [&](int i) { return uint32_t(ckeys[i]); }, [&](int i) { return i; }, klb);
   }
   __syncthreads();
   const int C = n_cand;
@@ -564,7 +603,8 @@ void topk_merge(const torch::Tensor& cand_val, const torch::Tensor& cand_idx, in
 // [N/32]) optionally restricts the eligible columns.  Unused output slots hold idx -1, val 0.
 void row_topk(const torch::Tensor& H, const torch::Tensor& cmax, int64_t k_max,
               const c10::optional<torch::Tensor>& k_dev, const c10::optional<torch::Tensor>& mask,
-              const torch::Tensor& out_val, const torch::Tensor& out_idx, const torch::Tensor& status) {
+              const torch::Tensor& out_val, const torch::Tensor& out_idx, const torch::Tensor& status,
+              const c10::optional<torch::Tensor>& tmax) {
   TORCH_CHECK(H.is_cuda() && H.scalar_type() == at::kBFloat16 && H.dim() == 2 && H.stride(1) == 1,
               "row_topk: H must be a CUDA bf16 matrix with contiguous rows");
   const int64_t M = H.size(0), N = H.size(1);
@@ -588,6 +628,11 @@ void row_topk(const torch::Tensor& H, const torch::Tensor& cmax, int64_t k_max,
                 "row_topk: mask must be int32 [N/32]");
     mk = reinterpret_cast<const uint32_t*>(mask->data_ptr<int>());
   }
+  if (tmax) {
+    TORCH_CHECK(N % 256 == 0 && tmax->scalar_type() == at::kBFloat16 && tmax->size(0) == M &&
+                    tmax->size(1) == N / 256 && tmax->stride(1) == 1,
+                "row_topk: tmax must be bf16 [M, N/256]");
+  }
   if (M == 0) return;
   const at::cuda::CUDAGuard guard(H.device());
   const int NC = int(N / 32);
@@ -603,7 +648,8 @@ void row_topk(const torch::Tensor& H, const torch::Tensor& cmax, int64_t k_max,
       reinterpret_cast<const __nv_bfloat16*>(H.data_ptr()), H.stride(0),
       reinterpret_cast<const __nv_bfloat16*>(cmax.data_ptr()), cmax.stride(0), int(N), int(k_max),
       kd, mk, out_val.data_ptr<float>(), out_idx.data_ptr<int>(), out_val.stride(0),
-      status.data_ptr<int>());
+      status.data_ptr<int>(), tmax ? reinterpret_cast<const __nv_bfloat16*>(tmax->data_ptr()) : nullptr,
+      tmax ? tmax->stride(0) : 0);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -209,6 +209,7 @@ class TPTopKEngine(FusedTopKEngine):
         R = self._row_chunk(B)
         H = torch.empty(min(R, B), N, dtype=torch.bfloat16, device=dev)
         cm = torch.empty(min(R, B), N // 32, dtype=torch.bfloat16, device=dev)
+        tm = torch.empty(min(R, B), N // 256, dtype=torch.bfloat16, device=dev)  # 256-column tile maxima
         vals = torch.empty(B, k, dtype=torch.float32, device=dev)
         idx = torch.empty(B, k, dtype=torch.int32, device=dev)
         if aux_on:
@@ -226,17 +227,17 @@ class TPTopKEngine(FusedTopKEngine):
             k_loc_dev = torch.tensor([local_dead], dtype=torch.int32, device=dev)
         for r0 in range(0, B, R):
             r1 = min(B, r0 + R)
-            h, c = H[: r1 - r0], cm[: r1 - r0]
+            h, c, t = H[: r1 - r0], cm[: r1 - r0], tm[: r1 - r0]
             nat.gemm_tn_bf16(X[r0:r1], self.w_enc, self.bias_eff, self.scale if self.rescale else None, False,
-                             h, c, self.status.tensor, 0)
+                             h, c, self.status.tensor, 0, tmax=t)
             self._mark("encoder_gemm")
-            nat.row_topk(h, c, k, None, None, vals[r0:r1], idx[r0:r1], self.status.tensor)
+            nat.row_topk(h, c, k, None, None, vals[r0:r1], idx[r0:r1], self.status.tensor, tmax=t)
             self._mark("row_topk")
             self.launches += 2
             if aux_on:
                 nat.row_topk(h, c, k_aux, k_loc_dev, mask_words, aux_vals[r0:r1], aux_idx[r0:r1], self.status.tensor)
                 self.launches += 1
-        del H, cm
+        del H, cm, tm
 
         # 3. global top-k from the shards' candidates
         self._global_topk(vals, idx, k, None)
@@ -362,6 +363,7 @@ class TPTopKEngine(FusedTopKEngine):
         R = self._row_chunk(B)
         H = torch.empty(min(R, B), N, dtype=torch.bfloat16, device=dev)
         cm = torch.empty(min(R, B), N // 32, dtype=torch.bfloat16, device=dev)
+        tm = torch.empty(min(R, B), N // 256, dtype=torch.bfloat16, device=dev)  # 256-column tile maxima
         vals = torch.empty(B, k, dtype=torch.float32, device=dev)
         idx = torch.empty(B, k, dtype=torch.int32, device=dev)
         if aux_on:
@@ -380,18 +382,18 @@ class TPTopKEngine(FusedTopKEngine):
         assert fb.x is not None
         for r0 in range(0, B, R):
             r1 = min(B, r0 + R)
-            h, c = H[: r1 - r0], cm[: r1 - r0]
+            h, c, t = H[: r1 - r0], cm[: r1 - r0], tm[: r1 - r0]
             nat.gemm_ag_tn_bf16(xb_own, bases, r, fb.x.offset, fb.ag_flags.offset, B, r0, r1 - r0, r0 == 0, ep,
                                 self.w_enc, self.bias_eff, self.scale if self.rescale else None, False, h, c, st,
-                                tk, 0)
+                                tk, 0, tmax=t)
             self._mark("ag_encoder_gemm")
-            nat.row_topk(h, c, k, None, None, vals[r0:r1], idx[r0:r1], st)
+            nat.row_topk(h, c, k, None, None, vals[r0:r1], idx[r0:r1], st, tmax=t)
             self._mark("row_topk")
             self.launches += 2
             if aux_on:
                 nat.row_topk(h, c, k_aux, k_loc_dev, mask_words, aux_vals[r0:r1], aux_idx[r0:r1], st)
                 self.launches += 1
-        del H, cm
+        del H, cm, tm
         X = fb.x_local
 
         # 3. candidate all-gather fused with the global merge

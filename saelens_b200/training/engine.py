@@ -267,6 +267,7 @@ class FusedTopKEngine:
         R = self._row_chunk(B)
         H = torch.empty(min(R, B), N, dtype=torch.bfloat16, device=dev)
         cm = torch.empty(min(R, B), N // 32, dtype=torch.bfloat16, device=dev)
+        tm = torch.empty(min(R, B), N // 256, dtype=torch.bfloat16, device=dev)  # 256-column tile maxima
         vals = torch.empty(B, k, dtype=torch.float32, device=dev)
         idx = torch.empty(B, k, dtype=torch.int32, device=dev)
         aux_on = run_aux and dead_mask is not None
@@ -288,17 +289,18 @@ class FusedTopKEngine:
             r1 = min(B, r0 + R)
             h = H[: r1 - r0]
             c = cm[: r1 - r0]
+            t = tm[: r1 - r0]
             nat.gemm_tn_bf16(xb[r0:r1], self.w_enc, self.bias_eff, self.scale if self.rescale else None, False,
-                             h, c, self.status.tensor, 0)
+                             h, c, self.status.tensor, 0, tmax=t)
             self._mark("encoder_gemm")
-            nat.row_topk(h, c, k, None, None, vals[r0:r1], idx[r0:r1], self.status.tensor)
+            nat.row_topk(h, c, k, None, None, vals[r0:r1], idx[r0:r1], self.status.tensor, tmax=t)
             self._mark("row_topk")
             self.launches += 2
             if aux_on:
                 self.launches += 1
                 nat.row_topk(h, c, k_aux, k_aux_dev, mask_words, aux_vals[r0:r1], aux_idx[r0:r1],
                              self.status.tensor)
-        del H, cm
+        del H, cm, tm
         if self.batch_topk:
             # batch-wide selection among the per-row candidates (k * B largest ReLU activations)
             nat.batch_topk_select(vals, idx, int(round(self.batch_k * B)), self.batch_truncated)

@@ -56,7 +56,7 @@ def test_llama_forward_native_matches_torch():
     from saelens_b200.models.lm import HookedLM, preset_config
 
     torch.manual_seed(0)
-    cfg = preset_config("Llama-3-8B", n_layers=2, d_model=256, n_heads=4, n_key_value_heads=2, d_mlp=512,
+    cfg = preset_config("llama-3-8b", n_layers=2, d_model=256, n_heads=4, n_key_value_heads=2, d_mlp=512,
                         d_vocab=1000, n_ctx=64, dtype="bfloat16")
     lm = HookedLM(cfg).cuda()
     toks = torch.randint(0, 1000, (2, 32), device="cuda")
