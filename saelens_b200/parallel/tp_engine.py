@@ -102,10 +102,58 @@ class _FusedBufs:
         self.heap.close()
 
 
+class _DPReducer:
+    """Averages a TP rank's latent-shard gradients over the data-parallel replicas of that shard
+    (the ranks of `group` hold the same latents and see different rows) with the P2P all-reduce
+    kernel, and sums the firing counts.  Gradient rows are dense ([2, N, D] buffer, zero rows for
+    latents no local pair touched) because other replicas may touch them."""
+
+    def __init__(self, eng: "TPTopKEngine", group: dist.ProcessGroup, small_n: int):
+        from saelens_b200.parallel.ddp_engine import _ArArea
+
+        nat, N, D = eng.native, eng.N, eng.D
+        self.size = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        sizes = [2 * N * D * 2]
+        sizes += _ArArea.nbytes(nat, N * D, 2, self.size, False) * 2
+        sizes += _ArArea.nbytes(nat, small_n, 4, self.size, True) + _ArArea.nbytes(nat, N, 4, self.size, True)
+        self.heap = SymmetricHeap(group, slab_bytes_needed(sizes) + 65536)
+        self.gbuf = torch.empty(2, N, D, dtype=torch.bfloat16, device=eng.device)
+        self.gout_buf = self.heap.alloc((2, N, D), torch.bfloat16)
+        self.g_avg = self.heap.local(self.gout_buf)
+        self.a_dec = _ArArea(self.heap, nat, N * D, 2, self.gout_buf.offset)
+        self.a_enc = _ArArea(self.heap, nat, N * D, 2, self.gout_buf.offset + N * D * 2)
+        self.a_small = _ArArea(self.heap, nat, small_n, 4, None)
+        self.a_fire = _ArArea(self.heap, nat, N, 4, None)
+        self.small_out = self.heap.local(SlabBuffer(self.a_small.out, (small_n,), torch.float32))
+        self.fire_out = self.heap.local(SlabBuffer(self.a_fire.out, (N,), torch.float32))
+        self.tickets = torch.zeros(4, dtype=torch.int32, device=eng.device)
+        self.dense_colptr = torch.arange(N + 1, dtype=torch.int64, device=eng.device)
+        self.nat, self.status = nat, eng.status
+
+    def _ar(self, x: torch.Tensor, scale: float, area: Any, t: int, sq: bool) -> None:
+        area.epoch += 1
+        self.nat.p2p_allreduce(x, scale, self.heap.bases, self.rank, area.land, area.cnt, area.out, area.flag,
+                               area.epoch, self.tickets[t : t + 1], self.status.tensor,
+                               area.sq_buf.offset if sq else -1)
+
+    def reduce(self, small: torch.Tensor, fire: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """Returns (averaged small vector, summed fire counts, sum of squares of the averaged W grads)."""
+        inv = 1.0 / self.size
+        self._ar(self.gbuf[0].reshape(-1), inv, self.a_dec, 0, True)
+        self._ar(self.gbuf[1].reshape(-1), inv, self.a_enc, 1, True)
+        self._ar(small, inv, self.a_small, 2, False)
+        self._ar(fire, 1.0, self.a_fire, 3, False)
+        return self.small_out, self.fire_out, self.a_dec.sq.sum() + self.a_enc.sq.sum()
+
+    def close(self) -> None:
+        self.heap.close()
+
+
 class TPTopKEngine(FusedTopKEngine):
     def __init__(self, sae: Any, lr: float, group: dist.ProcessGroup, beta1: float = 0.9, beta2: float = 0.999,
                  eps: float = 1e-8, max_grad_norm: float = 1.0, input_layout: str = "row_sharded",
-                 h_buffer_bytes: int = 8 << 30, fused: bool = True):
+                 h_buffer_bytes: int = 8 << 30, fused: bool = True, dp_group: dist.ProcessGroup | None = None):
         if input_layout not in ("row_sharded", "replicated"):
             raise ValueError("input_layout must be 'row_sharded' or 'replicated'")
         self.group = group
@@ -122,6 +170,13 @@ class TPTopKEngine(FusedTopKEngine):
         self._fb: _FusedBufs | None = None
         self._fb_aux: _FusedBufs | None = None
         self._ticket = torch.zeros(4, dtype=torch.int32, device=self.device)
+        # data parallel over replicas of this latent shard (tensor x data parallel)
+        self._dp: _DPReducer | None = None
+        if dp_group is not None and dist.get_world_size(dp_group) > 1:
+            if not self.fused:
+                raise NotImplementedError("tensor x data parallel needs the fused exchanges (fused=True)")
+            self._dp = _DPReducer(self, dp_group, self.N + 2 * self.D + 2)
+            self.g_dec, self.g_enc = self._dp.gbuf[0], self._dp.gbuf[1]
 
     def close(self) -> None:
         """Release the peer-memory slabs (collective)."""
@@ -129,6 +184,9 @@ class TPTopKEngine(FusedTopKEngine):
             if b is not None:
                 b.close()
         self._fb = self._fb_aux = None
+        if self._dp is not None:
+            self._dp.close()
+            self._dp = None
 
     def _fused_bufs(self, B: int) -> _FusedBufs:
         if self._fb is None or self._fb.B != B:
@@ -448,16 +506,35 @@ class TPTopKEngine(FusedTopKEngine):
                      self.cursor, pairs)
         self._mark("csc_build")
         sumsq = red[2 * D : 2 * D + 1]
+        dp = self._dp
         nat.latent_grad(self.colptr, pairs, vals, aux_vals if aux_on else None,
                         self.inv_scale if self.rescale else None, dX, daux, X,
                         self.p_bdec if self.apply_b_dec else None, self.w_dec, self.w_enc, self.g_dec, self.g_enc,
-                        self.g_benc, bterm if self.apply_b_dec else None, sumsq, self.fire_counts, act_freq,
-                        since_fired, idx, aux_idx if aux_on else None)
+                        self.g_benc, bterm if self.apply_b_dec else None, sumsq if dp is None else None,
+                        self.fire_counts, act_freq if dp is None else None, since_fired if dp is None else None,
+                        idx, aux_idx if aux_on else None, 0, -1, dp is not None)
         self.launches += 3
         self._mark("latent_grad")
+        red[2 * D + 1] = loss_row.sum()
+        g_dec, g_enc, g_benc, colptr = self.g_dec, self.g_enc, self.g_benc, self.colptr
+        if dp is not None:
+            # average this shard's gradients over its data-parallel replicas; the clip norm is taken
+            # from the averaged gradients (then summed over the tensor-parallel shards below)
+            small = torch.cat([self.g_benc, red[: 2 * D], red[2 * D + 1 : 2 * D + 3]])
+            avg, fired, sq_w = dp.reduce(small, self.fire_counts.to(torch.float32))
+            self.launches += 4
+            N = self.N
+            g_benc = avg[:N]
+            red = torch.cat([avg[N : N + 2 * D], (sq_w + g_benc.square().sum()).reshape(1), avg[N + 2 * D :]])
+            g_dec, g_enc, colptr = dp.g_avg[0], dp.g_avg[1], dp.dense_colptr
+            if act_freq is not None:
+                act_freq += fired
+            if since_fired is not None:
+                since_fired.copy_(torch.where(fired > 0, torch.zeros_like(since_fired), since_fired + 1))
+            self.fire_counts.copy_(fired.round().to(torch.int32))
+            self._mark("dp_grad_all_reduce")
 
         # 6. one P2P all-reduce for b_dec grad terms, grad norm and losses
-        red[2 * D + 1] = loss_row.sum()
         nat.p2p_allreduce(red, 1.0, bases, r, fb.red.land, fb.red.cnt, fb.red.out_buf.offset, fb.red.flag, ep,
                           tk, st)
         self.launches += 1
@@ -473,8 +550,8 @@ class TPTopKEngine(FusedTopKEngine):
                           self.p_bdec, self.m_bdec, self.v_bdec, cur_lr, self.beta1, self.beta2, self.eps,
                           self.step_count, self.max_grad_norm, True)
             nat.adam_rows(self.p_dec, self.m_dec, self.v_dec, self.p_enc, self.m_enc, self.v_enc, self.w_dec,
-                          self.w_enc, self.g_dec, self.g_enc, self.p_benc, self.m_benc, self.v_benc, self.g_benc,
-                          self.colptr, self.clip, self.p_bdec if self.apply_b_dec else None, self.scale,
+                          self.w_enc, g_dec, g_enc, self.p_benc, self.m_benc, self.v_benc, g_benc.contiguous(),
+                          colptr, self.clip, self.p_bdec if self.apply_b_dec else None, self.scale,
                           self.inv_scale, self.bias_eff, cur_lr, self.beta1, self.beta2, self.eps, self.step_count,
                           True)
             self.launches += 2

@@ -152,11 +152,20 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
             from saelens_b200.training.engine import engine_supported
 
             group = dp_group if dp_group is not None else getattr(sae, "process_group", None) or dist.group.WORLD
-            if engine_supported(self._base_sae) and getattr(self._base_sae, "_tp_group", None) is None:
+            tp_group = getattr(self._base_sae, "_tp_group", None)
+            batch_topk = type(self._base_sae).__name__ == "BatchTopKTrainingSAE"
+            if engine_supported(self._base_sae) and tp_group is None:
                 from saelens_b200.parallel.ddp_engine import DDPTopKEngine
 
                 self.engine = DDPTopKEngine(self._base_sae, lr=cfg.lr, group=group, beta1=cfg.adam_beta1,
                                             beta2=cfg.adam_beta2)
+                self._engine_stats_global = True
+            elif engine_supported(self._base_sae) and not batch_topk and getattr(cfg, "tp_exchange", "p2p") == "p2p":
+                from saelens_b200.parallel.tp_engine import TPTopKEngine
+
+                self.engine = TPTopKEngine(self._base_sae, lr=cfg.lr, group=tp_group, beta1=cfg.adam_beta1,
+                                           beta2=cfg.adam_beta2, input_layout=tp_input_layout, fused=True,
+                                           dp_group=group)
                 self._engine_stats_global = True
             elif want == "native":
                 raise ValueError("sae_engine='native' requested but this SAE/device is not supported by the fused engine")
@@ -330,7 +339,10 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
         res = self.engine.step(sae_in, lr=self.current_lr(), dead_mask=self.dead_neurons if run_aux else None,
                                want_sae_out=want_out, act_freq=self.act_freq_scores,
                                since_fired=self.n_forward_passes_since_fired, run_aux=run_aux)
-        world = dist.get_world_size(self.engine.group) if self._engine_stats_global else 1
+        world = 1
+        if self._engine_stats_global:
+            dpg = getattr(self.engine, "_dp", None)
+            world = dpg.size if dpg is not None else dist.get_world_size(self.engine.group)
         self.n_frac_active_samples += self.cfg.train_batch_size_samples * world
         self.lr_scheduler.step()
         for s in self.coefficient_schedulers.values():
