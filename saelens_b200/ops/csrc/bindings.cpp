@@ -36,7 +36,12 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
                  const c10::optional<torch::Tensor>& fire_counts,
                  const c10::optional<torch::Tensor>& act_freq,
                  const c10::optional<torch::Tensor>& since_fired, const torch::Tensor& idx,
-                 const c10::optional<torch::Tensor>& aux_idx, int64_t j0, int64_t j1, bool zero_empty);
+                 const c10::optional<torch::Tensor>& aux_idx, int64_t j0, int64_t j1, bool zero_empty,
+                 const c10::optional<torch::Tensor>& jr_thr, const c10::optional<torch::Tensor>& jr_pre,
+                 double jr_bandwidth, double jr_l0c, const c10::optional<torch::Tensor>& jr_gthr);
+void threshold_select(const torch::Tensor& H, const torch::Tensor& cmax, const torch::Tensor& lo,
+                      const torch::Tensor& lo_cmin, const torch::Tensor& out_val, const torch::Tensor& out_idx,
+                      const torch::Tensor& counts, const c10::optional<torch::Tensor>& truncated);
 void adam_bdec(const c10::optional<torch::Tensor>& bsum, const c10::optional<torch::Tensor>& bterm,
                const torch::Tensor& gb_dec, const c10::optional<torch::Tensor>& sumsq,
                const c10::optional<torch::Tensor>& clip_out, const torch::Tensor& p, const torch::Tensor& m,
@@ -117,7 +122,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("inv_scale"), py::arg("dxhat"), py::arg("daux"), py::arg("x"), py::arg("b_dec"), py::arg("W_dec"),
         py::arg("W_enc"), py::arg("gW_dec"), py::arg("gW_enc"), py::arg("gb_enc"), py::arg("bterm"),
         py::arg("sumsq"), py::arg("fire_counts"), py::arg("act_freq"), py::arg("since_fired"), py::arg("idx"),
-        py::arg("aux_idx"), py::arg("j0") = 0, py::arg("j1") = -1, py::arg("zero_empty") = false);
+        py::arg("aux_idx"), py::arg("j0") = 0, py::arg("j1") = -1, py::arg("zero_empty") = false,
+        py::arg("jr_thr") = py::none(), py::arg("jr_pre") = py::none(), py::arg("jr_bandwidth") = 0.0,
+        py::arg("jr_l0c") = 0.0, py::arg("jr_gthr") = py::none());
+  m.def("threshold_select", &sb::threshold_select);
   m.def("adam_bdec", &sb::adam_bdec);
   m.def("adam_rows", &sb::adam_rows);
   m.def("topk_merge", &sb::topk_merge);

@@ -827,6 +827,15 @@ struct PairDzArgs {
   int* prow;      // [P] row | (aux << 31)
   float* pcoef;   // [P]
   float* pdz;     // [P]
+  // JumpReLU mode (jr_thr != nullptr): main pairs are candidate entries with pre-activation
+  // jr_pre[p]; active = pre > threshold; coefficient and gradient flow only through active entries,
+  // and every entry inside the rectangle window |pre - threshold| < bandwidth/2 adds
+  // -(threshold / bandwidth) dz - jr_l0c to jr_gthr[j] (MSE and L0 straight-through terms).
+  const float* jr_thr;
+  const float* jr_pre;
+  float jr_inv_bw;
+  float jr_l0c;
+  float* jr_gthr;
 };
 
 __global__ void __launch_bounds__(LR_THREADS) pair_dz_kernel(const __grid_constant__ PairDzArgs a) {
@@ -841,10 +850,19 @@ __global__ void __launch_bounds__(LR_THREADS) pair_dz_kernel(const __grid_consta
     int64_t b;
     int j, aux;
     float coef;
+    float jr_pre = 0.f, jr_th = 0.f;
+    bool jr_active = true;
     if (p < a.n_main) {
       b = p / a.k;
       j = a.idx[p];
-      coef = fmaxf(a.vals[p], 0.f);
+      if (a.jr_thr) {
+        jr_pre = a.jr_pre[p];
+        jr_th = __ldg(a.jr_thr + j);
+        jr_active = jr_pre > jr_th;
+        coef = jr_active ? jr_pre : 0.f;
+      } else {
+        coef = fmaxf(a.vals[p], 0.f);
+      }
       aux = 0;
     } else {
       const int64_t q = p - a.n_main;
@@ -879,7 +897,9 @@ __global__ void __launch_bounds__(LR_THREADS) pair_dz_kernel(const __grid_consta
     if (lane == 0) {
       a.prow[pos] = int(b) | (aux << 31);
       a.pcoef[pos] = coef;
-      a.pdz[pos] = d;
+      a.pdz[pos] = jr_active ? d : 0.f;
+      if (a.jr_thr && fabsf(jr_pre - jr_th) * a.jr_inv_bw < 0.5f)
+        atomicAdd(a.jr_gthr + j, -(jr_th * a.jr_inv_bw) * d - a.jr_l0c);
     }
   }
 }
@@ -1237,13 +1257,15 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
                  const c10::optional<torch::Tensor>& fire_counts,
                  const c10::optional<torch::Tensor>& act_freq,
                  const c10::optional<torch::Tensor>& since_fired, const torch::Tensor& idx,
-                 const c10::optional<torch::Tensor>& aux_idx, int64_t j0, int64_t j1, bool zero_empty) {
+                 const c10::optional<torch::Tensor>& aux_idx, int64_t j0, int64_t j1, bool zero_empty,
+                 const c10::optional<torch::Tensor>& jr_thr, const c10::optional<torch::Tensor>& jr_pre,
+                 double jr_bandwidth, double jr_l0c, const c10::optional<torch::Tensor>& jr_gthr) {
   static const bool v1 = [] {
     const char* e = std::getenv("SAELENS_B200_LATENT_GRAD");
     return e && std::string(e) == "v1";
   }();
   if (j1 < 0) j1 = W_dec.size(0);
-  if (v1 && j0 == 0 && j1 == W_dec.size(0) && !zero_empty) {
+  if (v1 && j0 == 0 && j1 == W_dec.size(0) && !zero_empty && !jr_thr) {
     latent_grad_v1(colptr, pairs, vals, aux_vals, inv_scale, dxhat, daux, x, b_dec, W_dec, W_enc, gW_dec, gW_enc,
                    gb_enc, bterm, sumsq, fire_counts, act_freq, since_fired);
     return;
@@ -1288,6 +1310,16 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
     pa.prow = prow.data_ptr<int>();
     pa.pcoef = pcoef.data_ptr<float>();
     pa.pdz = pdz.data_ptr<float>();
+    if (jr_thr) {
+      TORCH_CHECK(jr_pre && jr_gthr && jr_pre->sizes() == vals.sizes() && jr_thr->numel() == N &&
+                      jr_gthr->numel() == N && jr_bandwidth > 0,
+                  "latent_grad: JumpReLU mode needs jr_pre [M, k], jr_thr [N], jr_gthr [N], bandwidth > 0");
+      pa.jr_thr = jr_thr->data_ptr<float>();
+      pa.jr_pre = jr_pre->data_ptr<float>();
+      pa.jr_inv_bw = float(1.0 / jr_bandwidth);
+      pa.jr_l0c = float(jr_l0c);
+      pa.jr_gthr = jr_gthr->data_ptr<float>();
+    }
     const int64_t grid = std::min<int64_t>((P + sparse::LR_WARPS - 1) / sparse::LR_WARPS, int64_t(sm_count()) * 8);
     sparse::pair_dz_kernel<<<dim3(grid), dim3(sparse::LR_THREADS), 0, stream>>>(pa);
     C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -575,6 +575,61 @@ __global__ void batch_filter_kernel(const float* __restrict__ vals, int* __restr
     if (threadIdx.x == 0 && truncated && kept == kc) atomicAdd(truncated, 1);
   }
 }
+
+// ---------------------------------------------------------------------------------------
+// JumpReLU candidates (sae_lens/saes/jumprelu_sae.py:19-85): per row, every column whose
+// pre-activation exceeds lo[col] = threshold - bandwidth/2.  That covers the active entries
+// (pre > threshold) and the rectangle window of the threshold's straight-through gradient.  A
+// 32-column chunk can hold a candidate only if its maximum reaches the chunk's smallest lo, so the
+// chunk maxima prune the row.  At most `cap` entries per row are kept (rows over the cap are
+// counted in `truncated`); unused slots get idx -1.
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(THREADS)
+    threshold_select_kernel(const __nv_bfloat16* __restrict__ H, int64_t ldh, const __nv_bfloat16* __restrict__ cmax,
+                            int64_t ldc, int N, const float* __restrict__ lo, const float* __restrict__ lo_cmin,
+                            int cap, float* __restrict__ out_val, int* __restrict__ out_idx, int* __restrict__ counts,
+                            int* __restrict__ truncated) {
+  __shared__ int n_out;
+  const int row = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int NC = N >> 5;
+  const __nv_bfloat16* hrow = H + int64_t(row) * ldh;
+  const __nv_bfloat16* crow = cmax + int64_t(row) * ldc;
+  float* vrow = out_val + int64_t(row) * cap;
+  int* irow = out_idx + int64_t(row) * cap;
+  if (tid == 0) n_out = 0;
+  __syncthreads();
+  for (int base = warp * 32; base < NC; base += THREADS) {
+    const int c = base + lane;
+    const bool is_cand = c < NC && __bfloat162float(crow[c]) >= __ldg(lo_cmin + c);
+    unsigned m = __ballot_sync(0xffffffffu, is_cand);
+    while (m) {
+      const int bit = __ffs(m) - 1;
+      m &= m - 1;
+      const int col = (base + bit) * 32 + lane;
+      const float v = __bfloat162float(hrow[col]);
+      const bool keep = v > __ldg(lo + col);
+      const unsigned km = __ballot_sync(0xffffffffu, keep);
+      int basepos = 0;
+      if (lane == 0 && km) basepos = atomicAdd(&n_out, __popc(km));
+      basepos = __shfl_sync(0xffffffffu, basepos, 0);
+      const int pos = basepos + __popc(km & ((1u << lane) - 1u));
+      if (keep && pos < cap) {
+        vrow[pos] = v;
+        irow[pos] = col;
+      }
+    }
+  }
+  __syncthreads();
+  const int n = n_out;
+  for (int i = n + tid; i < cap; i += THREADS) {
+    vrow[i] = 0.f;
+    irow[i] = -1;
+  }
+  if (tid == 0) {
+    counts[row] = min(n, cap);
+    if (n > cap && truncated) atomicAdd(truncated, 1);
+  }
+}
 }  // namespace topk
 
 void topk_merge(const torch::Tensor& cand_val, const torch::Tensor& cand_idx, int64_t n_local, int64_t rank,
@@ -736,6 +791,32 @@ torch::Tensor batch_topk_select(const torch::Tensor& vals, const torch::Tensor& 
                                                       truncated ? truncated->data_ptr<int>() : nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return sel;
+}
+
+// JumpReLU candidate lists (see threshold_select_kernel).  H [M, N] bf16 pre-activations, cmax
+// [M, N/32], lo [N] fp32 (threshold - bandwidth/2), lo_cmin [N/32] (per-chunk minimum of lo).
+void threshold_select(const torch::Tensor& H, const torch::Tensor& cmax, const torch::Tensor& lo,
+                      const torch::Tensor& lo_cmin, const torch::Tensor& out_val, const torch::Tensor& out_idx,
+                      const torch::Tensor& counts, const c10::optional<torch::Tensor>& truncated) {
+  TORCH_CHECK(H.is_cuda() && H.scalar_type() == at::kBFloat16 && H.dim() == 2 && H.stride(1) == 1,
+              "threshold_select: H must be CUDA bf16 [M, N]");
+  const int64_t M = H.size(0), N = H.size(1);
+  TORCH_CHECK(N % 32 == 0 && cmax.size(0) == M && cmax.size(1) == N / 32 && cmax.stride(1) == 1,
+              "threshold_select: cmax");
+  TORCH_CHECK(lo.numel() == N && lo_cmin.numel() == N / 32 && lo.scalar_type() == at::kFloat &&
+                  lo_cmin.scalar_type() == at::kFloat && lo.is_contiguous() && lo_cmin.is_contiguous(),
+              "threshold_select: lo / lo_cmin");
+  TORCH_CHECK(out_val.is_contiguous() && out_idx.is_contiguous() && out_val.size(0) == M && out_idx.size(0) == M &&
+                  out_val.size(1) == out_idx.size(1) && counts.numel() == M,
+              "threshold_select: outputs");
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(H.device());
+  topk::threshold_select_kernel<<<dim3(M), dim3(topk::THREADS), 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(H.data_ptr()), H.stride(0),
+      reinterpret_cast<const __nv_bfloat16*>(cmax.data_ptr()), cmax.stride(0), int(N), lo.data_ptr<float>(),
+      lo_cmin.data_ptr<float>(), int(out_val.size(1)), out_val.data_ptr<float>(), out_idx.data_ptr<int>(),
+      counts.data_ptr<int>(), truncated ? truncated->data_ptr<int>() : nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 }  // namespace sb

@@ -98,12 +98,14 @@ class FusedTopKEngine:
         from saelens_b200.models.batchtopk import BatchTopKTrainingSAE
 
         self.batch_topk = isinstance(sae, BatchTopKTrainingSAE)
-        self.batch_k = float(cfg.k)
+        self.batch_k = float(getattr(cfg, "k", 0) or 0)
         if self.batch_topk:
             self.k = int(min(1024, sae.cfg.d_sae, max(1, round(4 * float(cfg.k)))))
-        else:
+        elif hasattr(cfg, "k"):
             self.k = int(cfg.k)
-        self.rescale = bool(cfg.rescale_acts_by_decoder_norm)
+        else:  # threshold-sparse SAEs: `k` is the per-row candidate capacity
+            self.k = int(min(1024, sae.cfg.d_sae))
+        self.rescale = bool(getattr(cfg, "rescale_acts_by_decoder_norm", False))
         self.aux_coef = float(getattr(cfg, "aux_loss_coefficient", 1.0))
         self.apply_b_dec = bool(cfg.apply_b_dec_to_input)
         if cfg.normalize_activations in ("constant_norm_rescale", "layer_norm"):

@@ -180,6 +180,13 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
                 self.engine = TPTopKEngine(self._base_sae, lr=cfg.lr, group=tp_group, beta1=cfg.adam_beta1,
                                            beta2=cfg.adam_beta2, input_layout=tp_input_layout,
                                            fused=getattr(cfg, "tp_exchange", "p2p") == "p2p")
+            elif want == "native" and tp_group is None and type(self._base_sae).__name__ == "JumpReLUTrainingSAE":
+                # opt-in: the native JumpReLU step pays off once the SAE is sparse (candidate cap per row)
+                from saelens_b200.training.jumprelu_engine import JumpReLUEngine, jumprelu_engine_supported
+
+                if not jumprelu_engine_supported(self._base_sae):
+                    raise ValueError("sae_engine='native' requested but this JumpReLU SAE/device is not supported")
+                self.engine = JumpReLUEngine(self._base_sae, lr=cfg.lr, beta1=cfg.adam_beta1, beta2=cfg.adam_beta2)
             elif engine_supported(self._base_sae) and tp_group is None:
                 self.engine = FusedTopKEngine(self._base_sae, lr=cfg.lr, beta1=cfg.adam_beta1,
                                               beta2=cfg.adam_beta2)
@@ -336,6 +343,8 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
         self._sparsity_window_tick()
         run_aux = self.n_training_steps >= self.cfg.dead_feature_window and bool(self.dead_neurons.any())
         want_out = self._is_logging_step() or self.mse_history_path is not None
+        if hasattr(self.engine, "set_coefficients"):
+            self.engine.set_coefficients(self.get_coefficients())
         res = self.engine.step(sae_in, lr=self.current_lr(), dead_mask=self.dead_neurons if run_aux else None,
                                want_sae_out=want_out, act_freq=self.act_freq_scores,
                                since_fired=self.n_forward_passes_since_fired, run_aux=run_aux)
@@ -347,7 +356,7 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
         self.lr_scheduler.step()
         for s in self.coefficient_schedulers.values():
             s.step()
-        losses = {"mse_loss": res.mse_loss, "auxiliary_reconstruction_loss": res.aux_loss}
+        losses = {"mse_loss": res.mse_loss, getattr(self.engine, "aux_loss_name", "auxiliary_reconstruction_loss"): res.aux_loss}
         d_sae = self._base_sae.cfg.d_sae
         out = TrainStepOutput(
             sae_in=sae_in, sae_out=res.sae_out if res.sae_out is not None else sae_in.new_empty(0),

@@ -29,7 +29,7 @@ def _build(d_in, d_sae, k, device):
     return sae
 
 
-def _worker(rank, world, port, d_in, d_sae, k, B, out_dir):
+def _worker(rank, world, port, d_in, d_sae, k, B, out_dir, tp_size):
     import torch.distributed as dist
     from datetime import timedelta
 
@@ -37,9 +37,10 @@ def _worker(rank, world, port, d_in, d_sae, k, B, out_dir):
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
                             device_id=torch.device("cuda", rank))
-    tp_groups = [dist.new_group([0, 1]), dist.new_group([2, 3])]
-    dp_groups = [dist.new_group([0, 2]), dist.new_group([1, 3])]
-    tp_rank, dp_rank = rank % 2, rank // 2
+    dp_size = world // tp_size
+    tp_groups = [dist.new_group(list(range(d * tp_size, (d + 1) * tp_size))) for d in range(dp_size)]
+    dp_groups = [dist.new_group(list(range(t, world, tp_size))) for t in range(tp_size)]
+    tp_rank, dp_rank = rank % tp_size, rank // tp_size
     tp, dp = tp_groups[dp_rank], dp_groups[tp_rank]
     from saelens_b200.parallel.tp_engine import TPTopKEngine
 
@@ -48,8 +49,9 @@ def _worker(rank, world, port, d_in, d_sae, k, B, out_dir):
     eng = TPTopKEngine(sae, lr=1e-3, group=tp, fused=True, dp_group=dp)
     g = torch.Generator(device="cpu").manual_seed(11)
     x = torch.randn(B, d_in, generator=g).to(torch.bfloat16)
-    rep = x[dp_rank * (B // 2) : (dp_rank + 1) * (B // 2)]
-    rows = rep[tp_rank * (B // 4) : (tp_rank + 1) * (B // 4)].cuda()
+    per_rep = B // dp_size
+    rep = x[dp_rank * per_rep : (dp_rank + 1) * per_rep]
+    rows = rep[tp_rank * (per_rep // tp_size) : (tp_rank + 1) * (per_rep // tp_size)].cuda()
     losses = [float(eng.step(rows).loss) for _ in range(3)]
     torch.cuda.synchronize()
     eng.status.check()
@@ -59,26 +61,29 @@ def _worker(rank, world, port, d_in, d_sae, k, B, out_dir):
     dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 4, reason="needs 4 GPUs")
-def test_tp2_dp2_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("tp_size,world", [(1, 2), (2, 4)])
+def test_tp_dp_matches_single_gpu(tmp_path, tp_size, world):
     import torch.multiprocessing as mp
 
     from saelens_b200.training.engine import FusedTopKEngine
 
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     d_in, d_sae, k, B = 256, 2048, 32, 1024
-    mp.spawn(_worker, args=(4, _free_port(), d_in, d_sae, k, B, str(tmp_path)), nprocs=4, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), d_in, d_sae, k, B, str(tmp_path), tp_size), nprocs=world, join=True)
     sae = _build(d_in, d_sae, k, "cuda:0")
     eng = FusedTopKEngine(sae, lr=1e-3)
     g = torch.Generator(device="cpu").manual_seed(11)
     x = torch.randn(B, d_in, generator=g).to(torch.bfloat16).cuda()
     ref = [float(eng.step(x).loss) for _ in range(3)]
-    r = [torch.load(tmp_path / f"rank{i}.pt") for i in range(4)]
+    r = [torch.load(tmp_path / f"rank{i}.pt") for i in range(world)]
     for a, b in zip(r[0]["losses"], ref):
         assert abs(a - b) <= 3e-3 * abs(b), (r[0]["losses"], ref)
-    assert r[0]["losses"] == r[1]["losses"] == r[2]["losses"] == r[3]["losses"]
-    assert torch.equal(r[0]["p_dec"], r[2]["p_dec"]) and torch.equal(r[1]["p_dec"], r[3]["p_dec"])
-    n = d_sae // 2
-    for tp_rank in range(2):
+    assert all(ri["losses"] == r[0]["losses"] for ri in r)
+    for i in range(world):  # replicas of a shard stay identical
+        assert torch.equal(r[i]["p_dec"], r[i % tp_size]["p_dec"])
+    n = d_sae // tp_size
+    for tp_rank in range(tp_size):
         got, want = r[tp_rank]["p_dec"], eng.p_dec[tp_rank * n : (tp_rank + 1) * n].cpu()
         d = (got - want).abs()
         frac = (d > (2e-5 + 1e-3 * want.abs())).float().mean().item()
