@@ -368,6 +368,12 @@ NAMED_PRETRAINED_SAE_LOADERS: dict[str, Callable[..., Any]] = {
 }
 
 
+def _register_extra_converters() -> None:
+    from saelens_b200.loading import converters_extra
+
+    NAMED_PRETRAINED_SAE_LOADERS.update(converters_extra.LOADERS)
+
+
 def load_sae_config_from_huggingface(release: str, sae_id: str, device: str = "cpu",
                                      force_download: bool = False) -> dict[str, Any]:
     from saelens_b200.loading.pretrained_saes_directory import (
@@ -379,11 +385,17 @@ def load_sae_config_from_huggingface(release: str, sae_id: str, device: str = "c
     repo_id, folder = get_repo_id_and_folder_name(release, sae_id)
     overrides = get_config_overrides(release, sae_id)
     name = get_conversion_loader_name(release)
+    from saelens_b200.loading import converters_extra
+
     getters: dict[str, Callable[..., dict[str, Any]]] = {
         "sae_lens": get_sae_lens_config_from_hf,
         "gemma_2": get_gemma_2_config_from_hf,
         "llama_scope": get_llama_scope_config_from_hf,
         "dictionary_learning_1": get_dictionary_learning_config_1_from_hf,
+        **converters_extra.CONFIG_GETTERS,
     }
     cfg = getters[name](repo_id, folder, device, force_download, overrides)
     return handle_config_defaulting(cfg)
+
+
+_register_extra_converters()
