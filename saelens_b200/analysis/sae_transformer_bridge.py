@@ -19,12 +19,10 @@ from saelens_b200.analysis.hooked_sae_transformer import HookedSAETransformer
 
 
 def has_transformer_bridge() -> bool:
-    """The bridge needs only `transformers` (no TransformerLens install)."""
-    try:
-        import transformers  # noqa: F401
-    except ImportError:
-        return False
-    return True
+    """The bridge needs only `transformers` (no TransformerLens install); checked without importing it."""
+    import importlib.util
+
+    return importlib.util.find_spec("transformers") is not None
 
 
 class SAETransformerBridge(HookedSAETransformer):

@@ -29,6 +29,11 @@ from saelens_b200.constants import (
 from saelens_b200.registry import get_sae_class
 from saelens_b200.utils.misc import filter_valid_dataclass_fields, str_to_dtype
 
+# Loader signatures (the interface third-party converters implement)
+PretrainedSaeHuggingfaceLoader = Callable[..., "tuple[dict[str, Any], dict[str, torch.Tensor], torch.Tensor | None]"]
+PretrainedSaeDiskLoader = Callable[..., "tuple[dict[str, Any], dict[str, torch.Tensor]]"]
+PretrainedSaeConfigHuggingfaceLoader = Callable[..., dict[str, Any]]
+
 LLM_METADATA_KEYS = {
     "model_name", "hook_name", "model_class_name", "hook_head_index", "model_from_pretrained_kwargs",
     "prepend_bos", "exclude_special_tokens", "neuronpedia_id", "context_size", "seqpos_slice",

@@ -1325,8 +1325,16 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   const int nvec = int(D / 8);
+  // d_in slices per latent (power of two <= 8): each warp owns one slice of every latent it visits.
+  // SAELENS_B200_LR_SLICES caps it (fewer, wider slices: more loads in flight per warp item).
+  static const int max_ns = [] {
+    const char* e = std::getenv("SAELENS_B200_LR_SLICES");
+    const int v = e ? std::atoi(e) : 8;
+    return (v == 1 || v == 2 || v == 4 || v == 8) ? v : 8;
+  }();
   int ns = 1;
-  while (ns < 8 && ns * 64 < nvec) ns *= 2;
+  while (ns < max_ns && ns * 64 < nvec) ns *= 2;
+  TORCH_CHECK((nvec + 32 * ns - 1) / (32 * ns) <= 4, "latent_grad: d_in too wide for ", ns, " slices");
   const int vpl = (nvec + 32 * ns - 1) / (32 * ns);
   const int sw = 32 * vpl * 8;
   const int grid = sm_count() * 2;

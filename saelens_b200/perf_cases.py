@@ -11,6 +11,9 @@
     python -m saelens_b200.perf_cases allreduce
         P2P two-shot all-reduce kernel vs NCCL all_reduce (bf16, sum) over sizes and chunk sizes,
         under torch.distributed.run; bus bandwidth = 2 (S-1)/S bytes / time, max time over ranks.
+    python -m saelens_b200.perf_cases router [--rows 8192 --d 4096]
+        Shard-routing transfer: rank 0 produces fp32 rows, the other ranks consume bf16 unit-norm
+        rows; the fused P2P router vs NCCL send/recv with separate normalise + cast (max over ranks).
     python -m saelens_b200.perf_cases ddp [--d-sae 131072 --k 64 --batch 8192 --steps 10]
         Data-parallel TopK step (replicated SAE, P2P gradient all-reduce) under
         torch.distributed.run: ms/step (max over ranks) and per-phase times.
@@ -245,6 +248,73 @@ def allreduce(args: argparse.Namespace) -> None:
     dist.destroy_process_group()
 
 
+def router(args: argparse.Namespace) -> None:
+    import math
+
+    import torch
+    import torch.distributed as dist
+
+    from saelens_b200.parallel.row_router import P2PRowRouter
+    from saelens_b200.parallel.shard_routing import compute_routing_table
+
+    world, rank, _ = _init_dist()
+    producers, consumers = [0], list(range(1, world)) if world > 1 else [0]
+    rows, d = args.rows, args.d
+    scale = math.sqrt(d)
+    x = torch.randn(rows, d, device="cuda")
+    r = P2PRowRouter(dist.group.WORLD, producers, consumers, rows, d, normalize="unit_norm", scale=scale)
+    routes = compute_routing_table(1, len(consumers), rows)
+
+    def p2p_step() -> None:
+        if rank in producers:
+            r.send(x)
+        if rank in consumers:
+            r.recv()
+            r.release()
+
+    recv_bufs = {c: torch.empty(rt.n_rows, d, dtype=torch.bfloat16, device="cuda")
+                 for c, rt in zip(consumers, routes)}
+
+    def nccl_step() -> None:
+        ops = []
+        if rank in producers:
+            y = (x / x.norm(dim=-1, keepdim=True) * scale).to(torch.bfloat16)
+            for c, rt in zip(consumers, routes):
+                ops.append(dist.P2POp(dist.isend, y[rt.row_start : rt.row_end].contiguous(), c))
+        if rank in consumers:
+            ops.append(dist.P2POp(dist.irecv, recv_bufs[rank], producers[0]))
+        if ops:
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()
+
+    def timed(fn, reps: int = 20) -> float:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / reps], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms_p2p = timed(p2p_step)
+    r.status.check("router")
+    ms_nccl = timed(nccl_step)
+    bytes_out = rows * d * 2
+    if rank == 0:
+        print(json.dumps({"world": world, "rows": rows, "d": d, "p2p_ms": round(ms_p2p, 4),
+                          "nccl_ms": round(ms_nccl, 4), "p2p_GBs": round(bytes_out / ms_p2p / 1e6, 1),
+                          "nccl_GBs": round(bytes_out / ms_nccl / 1e6, 1),
+                          "note": "bytes = bf16 rows leaving the producer; fp32 input read once"}), flush=True)
+    r.close()
+    dist.destroy_process_group()
+
+
 def main() -> None:
     p = argparse.ArgumentParser(prog="python -m saelens_b200.perf_cases")
     sub = p.add_subparsers(dest="cmd", required=True)
@@ -262,8 +332,11 @@ def main() -> None:
     d.add_argument("--steps", type=int, default=10)
     d.add_argument("--segments", type=int, default=4)
     sub.add_parser("allreduce")
+    rt = sub.add_parser("router")
+    rt.add_argument("--rows", type=int, default=8192)
+    rt.add_argument("--d", type=int, default=4096)
     args = p.parse_args()
-    {"phases": phases, "fused-case": fused_case, "gemm": gemm, "ddp": ddp, "allreduce": allreduce}[args.cmd](args)
+    {"phases": phases, "fused-case": fused_case, "gemm": gemm, "ddp": ddp, "allreduce": allreduce, "router": router}[args.cmd](args)
 
 
 if __name__ == "__main__":

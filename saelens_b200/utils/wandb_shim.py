@@ -9,17 +9,28 @@ import os
 import time
 from typing import Any
 
-try:  # pragma: no cover - depends on the environment
-    import wandb as _wandb  # type: ignore[import-not-found]
-except Exception:  # noqa: BLE001
-    _wandb = None
+import importlib.util
 
-AVAILABLE = _wandb is not None
+AVAILABLE = importlib.util.find_spec("wandb") is not None
+_wandb: Any = None  # imported on first use (importing wandb takes seconds)
+
+
+def _module() -> Any:
+    global _wandb
+    if _wandb is None and AVAILABLE:
+        try:  # pragma: no cover - depends on the environment
+            import wandb  # type: ignore[import-not-found]
+
+            _wandb = wandb
+        except Exception:  # noqa: BLE001
+            return None
+    return _wandb
 
 
 def _live() -> bool:
     """True when a real wandb run is active; otherwise calls go to the offline JSONL log."""
-    return _wandb is not None and getattr(_wandb, "run", None) is not None
+    m = _module() if "wandb" in __import__("sys").modules else None
+    return m is not None and getattr(m, "run", None) is not None
 
 
 def _log_path() -> str:
@@ -64,8 +75,9 @@ class Artifact:
 
 
 def init(**kwargs: Any) -> Any:
-    if _wandb is not None:
-        return _wandb.init(**kwargs)
+    m = _module()
+    if m is not None:
+        return m.init(**kwargs)
     with open(_log_path(), "a") as f:
         f.write(json.dumps({"event": "init", "time": time.time(), **{k: _jsonable(v) for k, v in kwargs.items()}}) + "\n")
     return None
