@@ -106,6 +106,13 @@ void rope_(const torch::Tensor& x, const torch::Tensor& cos, const torch::Tensor
 torch::Tensor gated_act(const torch::Tensor& gate, const torch::Tensor& up, int64_t kind);
 torch::Tensor batch_topk_select(const torch::Tensor& vals, const torch::Tensor& idx, int64_t K,
                                 const c10::optional<torch::Tensor>& truncated);
+void batch_hist(const torch::Tensor& vals, const torch::Tensor& idx, const torch::Tensor& hist);
+void batch_thresh(const torch::Tensor& hist, int64_t K, const torch::Tensor& sel);
+void batch_ties(const torch::Tensor& vals, const torch::Tensor& idx, const torch::Tensor& sel,
+                const torch::Tensor& ties);
+void batch_filter(const torch::Tensor& vals, const torch::Tensor& idx, const torch::Tensor& sel,
+                  const torch::Tensor& ties_all, int64_t rank, const torch::Tensor& prefix,
+                  const c10::optional<torch::Tensor>& truncated);
 }  // namespace sb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -148,6 +155,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_signal", &sb::p2p_signal);
   m.def("rmsnorm", &sb::rmsnorm);
   m.def("batch_topk_select", &sb::batch_topk_select);
+  m.def("batch_hist", &sb::batch_hist);
+  m.def("batch_thresh", &sb::batch_thresh);
+  m.def("batch_ties", &sb::batch_ties);
+  m.def("batch_filter", &sb::batch_filter);
   m.def("rope_", &sb::rope_);
   m.def("gated_act", &sb::gated_act);
   m.def("symm_alloc", &sb::symm_alloc);

@@ -28,21 +28,39 @@ namespace p2p {
 
 constexpr int AR_THREADS = 256;
 
+// Element traits: A = accumulator type, to_a/ld widen, fin scales and rounds, sqv is the value's
+// square for the per-chunk sum of squares.  int32 sums are exact (scale and sums of squares do
+// not apply; the host checks).
 template <class T>
 struct Elt;
 template <>
 struct Elt<float> {
+  using A = float;
   static __device__ __forceinline__ float ld(const float* p) { return __ldcg(p); }
-  static __device__ __forceinline__ float to_f(float v) { return v; }
-  static __device__ __forceinline__ float from_f(float v) { return v; }
+  static __device__ __forceinline__ float to_a(float v) { return v; }
+  static __device__ __forceinline__ float fin(float v, float s) { return v * s; }
+  static __device__ __forceinline__ float sqv(float v) { return v * v; }
 };
 template <>
 struct Elt<__nv_bfloat16> {
+  using A = float;
   static __device__ __forceinline__ float ld(const __nv_bfloat16* p) {
     return __bfloat162float(__ushort_as_bfloat16(__ldcg(reinterpret_cast<const unsigned short*>(p))));
   }
-  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
-  static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+  static __device__ __forceinline__ float to_a(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 fin(float v, float s) { return __float2bfloat16_rn(v * s); }
+  static __device__ __forceinline__ float sqv(__nv_bfloat16 v) {
+    const float f = __bfloat162float(v);
+    return f * f;
+  }
+};
+template <>
+struct Elt<int> {
+  using A = int;
+  static __device__ __forceinline__ int ld(const int* p) { return __ldcg(p); }
+  static __device__ __forceinline__ int to_a(int v) { return v; }
+  static __device__ __forceinline__ int fin(int v, float) { return v; }
+  static __device__ __forceinline__ float sqv(int) { return 0.f; }
 };
 
 struct ArArgs {
@@ -111,33 +129,31 @@ __global__ void __launch_bounds__(AR_THREADS) allreduce_kernel(const __grid_cons
         // 16-byte vectors: V elements per thread and step, S loads and S stores of 16 bytes
         constexpr int V = 16 / sizeof(T);
         for (int v = t; v < CH / V; v += AR_THREADS) {
-          float acc[V];
+          typename Elt<T>::A acc[V];
 #pragma unroll
-          for (int i = 0; i < V; ++i) acc[i] = 0.f;
+          for (int i = 0; i < V; ++i) acc[i] = 0;
           for (int s = 0; s < S; ++s) {
             const uint4 q = __ldcg(reinterpret_cast<const uint4*>(land + int64_t(s) * per_owner * CH) + v);
             const T* qe = reinterpret_cast<const T*>(&q);
 #pragma unroll
-            for (int i = 0; i < V; ++i) acc[i] += Elt<T>::to_f(qe[i]);
+            for (int i = 0; i < V; ++i) acc[i] += Elt<T>::to_a(qe[i]);
           }
           uint4 o;
           T* oe = reinterpret_cast<T*>(&o);
 #pragma unroll
           for (int i = 0; i < V; ++i) {
-            oe[i] = Elt<T>::from_f(acc[i] * a.scale);
-            const float vr = Elt<T>::to_f(oe[i]);
-            sq += vr * vr;
+            oe[i] = Elt<T>::fin(acc[i], a.scale);
+            sq += Elt<T>::sqv(oe[i]);
           }
           for (int d = 0; d < S; ++d)
             reinterpret_cast<uint4*>(at<T>(a.P, (r + d) % S, a.out_off) + e0)[v] = o;
         }
       } else {
         for (int64_t e = t; e < len; e += AR_THREADS) {
-          float acc = 0.f;
+          typename Elt<T>::A acc = 0;
           for (int s = 0; s < S; ++s) acc += Elt<T>::ld(land + int64_t(s) * per_owner * CH + e);
-          const T v = Elt<T>::from_f(acc * a.scale);
-          const float vr = Elt<T>::to_f(v);
-          sq += vr * vr;
+          const T v = Elt<T>::fin(acc, a.scale);
+          sq += Elt<T>::sqv(v);
           for (int d = 0; d < S; ++d) at<T>(a.P, (r + d) % S, a.out_off)[e0 + e] = v;
         }
       }
@@ -335,7 +351,7 @@ std::vector<int64_t> p2p_allreduce_sizes(int64_t n, int64_t elem_bytes, int64_t 
   return {world * per_owner * chunk * elem_bytes, nch * 4, nch * chunk * elem_bytes, nch * 4};
 }
 
-// Sum `x` (fp32 or bf16, [n]) over the group, times `scale`; the result lands in the `out` area
+// Sum `x` (fp32, bf16 or int32, [n]) over the group, times `scale`; the result lands in the `out` area
 // of every rank's slab (offset out_off, same dtype).  Offsets are those of p2p_allreduce_sizes.
 // With sq_off >= 0, every rank also receives the sum of squares of each result chunk (fp32
 // [nch] at sq_off), e.g. for the norm of an averaged gradient.
@@ -344,8 +360,11 @@ void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64
                    const torch::Tensor& ticket, const torch::Tensor& status, int64_t sq_off, int64_t chunk) {
   const int64_t S = int64_t(peer_bases.size());
   TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "p2p_allreduce: bad group");
-  TORCH_CHECK(x.is_cuda() && x.is_contiguous() && (x.scalar_type() == at::kFloat || x.scalar_type() == at::kBFloat16),
-              "p2p_allreduce: contiguous fp32/bf16 CUDA tensor required");
+  TORCH_CHECK(x.is_cuda() && x.is_contiguous() &&
+                  (x.scalar_type() == at::kFloat || x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kInt),
+              "p2p_allreduce: contiguous fp32/bf16/int32 CUDA tensor required");
+  TORCH_CHECK(x.scalar_type() != at::kInt || (scale == 1.0 && sq_off < 0),
+              "p2p_allreduce: int32 sums take no scale and no sums of squares");
   TORCH_CHECK(land_off % 16 == 0 && out_off % 16 == 0, "p2p_allreduce: offsets must be 16-byte aligned");
   const int64_t n = x.numel();
   if (n == 0) return;
@@ -372,6 +391,8 @@ void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64
   const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(2 * nch, int64_t(p2p_sm_count()) * 8));
   if (x.scalar_type() == at::kFloat)
     p2p::allreduce_kernel<float><<<dim3(grid), dim3(p2p::AR_THREADS), 0, stream>>>(a);
+  else if (x.scalar_type() == at::kInt)
+    p2p::allreduce_kernel<int><<<dim3(grid), dim3(p2p::AR_THREADS), 0, stream>>>(a);
   else
     p2p::allreduce_kernel<__nv_bfloat16><<<dim3(grid), dim3(p2p::AR_THREADS), 0, stream>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

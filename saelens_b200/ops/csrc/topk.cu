@@ -475,16 +475,23 @@ __global__ void batch_hist_kernel(const float* __restrict__ vals, const int* __r
   }
 }
 
-// One CTA: find the threshold key and how many ties at it to keep.  sel[0] = key (0 if fewer than
-// K positive candidates: keep every positive one), sel[1] = ties to keep, sel[2] = strictly-above count.
+// One CTA: find the threshold key and how many ties at it to keep.  sel[0] = key (0x8000 if fewer
+// than K positive candidates: keep every positive one), sel[1] = ties to keep, sel[2] =
+// strictly-above count, sel[3] = key of the smallest kept value (0 if nothing is kept).  With
+// K >= 1 and the threshold found, at least one tie is kept, so the smallest kept value is the
+// threshold key's; otherwise it is the smallest positive key present.
 __global__ void batch_thresh_kernel(const uint32_t* __restrict__ hist, int64_t K, int* __restrict__ sel) {
   __shared__ uint32_t part[1024];
   __shared__ int s_found;
+  __shared__ uint32_t s_min;
   const int t = threadIdx.x;  // 1024 threads x 64 bins, bins scanned from the top
   uint32_t sum = 0;
   for (int b = 0; b < 64; ++b) sum += hist[65535 - (t * 64 + b)];
   part[t] = sum;
-  if (t == 0) s_found = 0;
+  if (t == 0) {
+    s_found = 0;
+    s_min = 0x10000u;
+  }
   __syncthreads();
   if (t == 0) {
     uint64_t acc = 0;
@@ -498,6 +505,7 @@ __global__ void batch_thresh_kernel(const uint32_t* __restrict__ hist, int64_t K
             sel[0] = key;
             sel[1] = int(K - int64_t(acc));
             sel[2] = int(acc);
+            sel[3] = K - int64_t(acc) > 0 ? key : 0;
             found = 1;
             break;
           }
@@ -513,6 +521,17 @@ __global__ void batch_thresh_kernel(const uint32_t* __restrict__ hist, int64_t K
       sel[2] = int(acc);
     }
     s_found = found;
+  }
+  __syncthreads();
+  if (!s_found) {
+    uint32_t mn = 0x10000u;
+    for (int b = 0; b < 64; ++b) {
+      const uint32_t key = 65535u - uint32_t(t * 64 + b);
+      if (key > 0x8000u && hist[key] > 0) mn = min(mn, key);
+    }
+    if (mn < 0x10000u) atomicMin(&s_min, mn);
+    __syncthreads();
+    if (t == 0) sel[3] = s_min < 0x10000u ? int(s_min) : 0;
   }
 }
 
@@ -530,6 +549,39 @@ __global__ void batch_ties_kernel(const float* __restrict__ vals, const int* __r
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
     if (threadIdx.x == 0) ties[row] = c;
+  }
+}
+
+// One CTA of 1024 threads: prefix[b] = ties of rows < b on every rank + ties of row b on ranks
+// < rank, from the per-rank tie counts ties[S][M] (S = 1 on one GPU).  With latents sharded in
+// contiguous blocks, (row, rank, local index) order is (row, global latent index) order.
+__global__ void __launch_bounds__(1024) tie_prefix_kernel(const int* __restrict__ ties, int S, int M, int rank,
+                                                          int64_t* __restrict__ prefix) {
+  __shared__ int64_t part[1024];
+  const int t = threadIdx.x;
+  const int per = (M + 1023) / 1024;
+  const int r0 = min(M, t * per), r1 = min(M, r0 + per);
+  int64_t sum = 0;
+  for (int b = r0; b < r1; ++b)
+    for (int q = 0; q < S; ++q) sum += ties[int64_t(q) * M + b];
+  part[t] = sum;
+  __syncthreads();
+  for (int o = 1; o < 1024; o <<= 1) {  // inclusive scan
+    const int64_t v = t >= o ? part[t - o] : 0;
+    __syncthreads();
+    part[t] += v;
+    __syncthreads();
+  }
+  int64_t run = t > 0 ? part[t - 1] : 0;
+  for (int b = r0; b < r1; ++b) {
+    int64_t row_all = 0, row_before = 0;
+    for (int q = 0; q < S; ++q) {
+      const int c = ties[int64_t(q) * M + b];
+      row_all += c;
+      if (q < rank) row_before += c;
+    }
+    prefix[b] = run + row_before;
+    run += row_all;
   }
 }
 
@@ -755,41 +807,107 @@ void topk_exchange_merge(const torch::Tensor& vals, const torch::Tensor& idx, in
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-// Keep the K = round(k * rows) largest positive candidate values of the whole batch (see
-// batch_hist_kernel).  vals/idx [M, kc] from row_topk; idx is updated in place (-1 = dropped).
-// Returns int32 [3] on the device: threshold key, ties kept, count above the threshold; and
-// counts rows whose whole candidate list was kept into `truncated` (int32 [1], optional).
-torch::Tensor batch_topk_select(const torch::Tensor& vals, const torch::Tensor& idx, int64_t K,
-                                const c10::optional<torch::Tensor>& truncated) {
+static void check_cands(const torch::Tensor& vals, const torch::Tensor& idx, const char* what) {
   TORCH_CHECK(vals.is_cuda() && vals.is_contiguous() && idx.is_contiguous() && vals.scalar_type() == at::kFloat &&
                   idx.scalar_type() == at::kInt && vals.sizes() == idx.sizes() && vals.dim() == 2,
-              "batch_topk_select: vals/idx must be contiguous fp32/int32 [M, kc]");
-  const int64_t M = vals.size(0), kc = vals.size(1);
-  TORCH_CHECK(kc <= 1024, "batch_topk_select: at most 1024 candidates per row");
-  const at::cuda::CUDAGuard guard(vals.device());
-  auto stream = at::cuda::getCurrentCUDAStream();
-  auto opts = vals.options();
-  auto hist = torch::zeros({65536}, opts.dtype(at::kInt));
-  auto sel = torch::empty({3}, opts.dtype(at::kInt));
-  auto ties = torch::empty({std::max<int64_t>(M, 1)}, opts.dtype(at::kInt));
-  if (M == 0) return sel.zero_();
+              what, ": vals/idx must be contiguous fp32/int32 [M, kc]");
+  TORCH_CHECK(vals.size(1) <= 1024, what, ": at most 1024 candidates per row");
+}
+
+static int sm_count_here() {
   int dev = 0, nsm = 0;
   C10_CUDA_CHECK(cudaGetDevice(&dev));
   C10_CUDA_CHECK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
-  const int64_t n = M * kc;
-  topk::batch_hist_kernel<<<dim3(int(std::min<int64_t>((n + 255) / 256, int64_t(nsm) * 8))), 256, 0, stream>>>(
-      vals.data_ptr<float>(), idx.data_ptr<int>(), n, reinterpret_cast<uint32_t*>(hist.data_ptr<int>()));
-  topk::batch_thresh_kernel<<<1, 1024, 0, stream>>>(reinterpret_cast<const uint32_t*>(hist.data_ptr<int>()), K,
-                                                    sel.data_ptr<int>());
-  const dim3 blk(32, 8);
-  const int grid = int(std::min<int64_t>((M + 7) / 8, int64_t(nsm) * 16));
-  topk::batch_ties_kernel<<<grid, blk, 0, stream>>>(vals.data_ptr<float>(), idx.data_ptr<int>(), int(M), int(kc),
-                                                    sel.data_ptr<int>(), ties.data_ptr<int>());
-  auto prefix = torch::cumsum(ties.narrow(0, 0, M).to(at::kLong), 0) - ties.narrow(0, 0, M).to(at::kLong);
-  topk::batch_filter_kernel<<<grid, blk, 0, stream>>>(vals.data_ptr<float>(), idx.data_ptr<int>(), int(M), int(kc),
-                                                      sel.data_ptr<int>(), prefix.data_ptr<int64_t>(),
-                                                      truncated ? truncated->data_ptr<int>() : nullptr);
+  return nsm;
+}
+
+// 65536-bin histogram (int32, zeroed here) of the positive candidates' bf16 keys.
+void batch_hist(const torch::Tensor& vals, const torch::Tensor& idx, const torch::Tensor& hist) {
+  check_cands(vals, idx, "batch_hist");
+  TORCH_CHECK(hist.is_cuda() && hist.is_contiguous() && hist.scalar_type() == at::kInt && hist.numel() == 65536,
+              "batch_hist: hist must be int32 [65536]");
+  const at::cuda::CUDAGuard guard(vals.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  C10_CUDA_CHECK(cudaMemsetAsync(hist.data_ptr<int>(), 0, 65536 * sizeof(int), stream));
+  const int64_t n = vals.numel();
+  if (n == 0) return;
+  topk::batch_hist_kernel<<<dim3(int(std::min<int64_t>((n + 255) / 256, int64_t(sm_count_here()) * 8))), 256, 0,
+                            stream>>>(vals.data_ptr<float>(), idx.data_ptr<int>(), n,
+                                      reinterpret_cast<uint32_t*>(hist.data_ptr<int>()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Threshold of the K largest from a (possibly group-summed) histogram; sel int32 [4] (see
+// batch_thresh_kernel).
+void batch_thresh(const torch::Tensor& hist, int64_t K, const torch::Tensor& sel) {
+  TORCH_CHECK(hist.is_cuda() && hist.is_contiguous() && hist.scalar_type() == at::kInt && hist.numel() == 65536 &&
+                  sel.is_cuda() && sel.scalar_type() == at::kInt && sel.numel() >= 4,
+              "batch_thresh: hist int32 [65536], sel int32 [4]");
+  const at::cuda::CUDAGuard guard(hist.device());
+  topk::batch_thresh_kernel<<<1, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const uint32_t*>(hist.data_ptr<int>()), K, sel.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Ties at the threshold key per row (int32 [M], contiguous).
+void batch_ties(const torch::Tensor& vals, const torch::Tensor& idx, const torch::Tensor& sel,
+                const torch::Tensor& ties) {
+  check_cands(vals, idx, "batch_ties");
+  const int64_t M = vals.size(0), kc = vals.size(1);
+  TORCH_CHECK(ties.is_cuda() && ties.is_contiguous() && ties.scalar_type() == at::kInt && ties.numel() == M,
+              "batch_ties: ties must be int32 [M]");
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(vals.device());
+  const int grid = int(std::min<int64_t>((M + 7) / 8, int64_t(sm_count_here()) * 16));
+  topk::batch_ties_kernel<<<grid, dim3(32, 8), 0, at::cuda::getCurrentCUDAStream()>>>(
+      vals.data_ptr<float>(), idx.data_ptr<int>(), int(M), int(kc), sel.data_ptr<int>(), ties.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Keep the selected entries (idx -1 elsewhere), with ties ranked in (row, rank, local index)
+// order from every rank's per-row tie counts ties_all [S, M].  prefix: int64 [M] scratch.
+void batch_filter(const torch::Tensor& vals, const torch::Tensor& idx, const torch::Tensor& sel,
+                  const torch::Tensor& ties_all, int64_t rank, const torch::Tensor& prefix,
+                  const c10::optional<torch::Tensor>& truncated) {
+  check_cands(vals, idx, "batch_filter");
+  const int64_t M = vals.size(0), kc = vals.size(1);
+  TORCH_CHECK(ties_all.is_cuda() && ties_all.is_contiguous() && ties_all.scalar_type() == at::kInt &&
+                  ties_all.dim() == 2 && ties_all.size(1) == M && rank >= 0 && rank < ties_all.size(0),
+              "batch_filter: ties_all must be int32 [S, M]");
+  TORCH_CHECK(prefix.is_cuda() && prefix.is_contiguous() && prefix.scalar_type() == at::kLong && prefix.numel() >= M,
+              "batch_filter: prefix must be int64 [M]");
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(vals.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  topk::tie_prefix_kernel<<<1, 1024, 0, stream>>>(ties_all.data_ptr<int>(), int(ties_all.size(0)), int(M), int(rank),
+                                                   prefix.data_ptr<int64_t>());
+  const int grid = int(std::min<int64_t>((M + 7) / 8, int64_t(sm_count_here()) * 16));
+  topk::batch_filter_kernel<<<grid, dim3(32, 8), 0, stream>>>(vals.data_ptr<float>(), idx.data_ptr<int>(), int(M),
+                                                               int(kc), sel.data_ptr<int>(),
+                                                               prefix.data_ptr<int64_t>(),
+                                                               truncated ? truncated->data_ptr<int>() : nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Keep the K = round(k * rows) largest positive candidate values of the whole batch (see
+// batch_hist_kernel).  vals/idx [M, kc] from row_topk; idx is updated in place (-1 = dropped).
+// Returns int32 [4] on the device (see batch_thresh_kernel); counts rows whose whole candidate
+// list was kept into `truncated` (int32 [1], optional).  Five launches, no host sync.
+torch::Tensor batch_topk_select(const torch::Tensor& vals, const torch::Tensor& idx, int64_t K,
+                                const c10::optional<torch::Tensor>& truncated) {
+  check_cands(vals, idx, "batch_topk_select");
+  const int64_t M = vals.size(0);
+  auto opts = vals.options();
+  auto sel = torch::zeros({4}, opts.dtype(at::kInt));
+  if (M == 0) return sel;
+  auto hist = torch::empty({65536}, opts.dtype(at::kInt));
+  auto ties = torch::empty({1, M}, opts.dtype(at::kInt));
+  auto prefix = torch::empty({M}, opts.dtype(at::kLong));
+  batch_hist(vals, idx, hist);
+  batch_thresh(hist, K, sel);
+  auto ties_row = ties.select(0, 0);
+  batch_ties(vals, idx, sel, ties_row);
+  batch_filter(vals, idx, sel, ties, 0, prefix, truncated);
   return sel;
 }
 

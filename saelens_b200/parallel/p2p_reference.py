@@ -15,6 +15,10 @@ testable without GPUs:
 * `route_rows`           - ops/csrc/p2p.cu route_rows_kernel: producer rows to consumers by the
                            shard-routing table, normalised and cast to bf16, assembled in producer
                            order.
+* `sharded_batch_topk`   - the latent-sharded BatchTopK of parallel/tp_engine.py (ops/csrc/topk.cu
+                           batch_* kernels): per-shard row candidates, summed 16-bit key histogram,
+                           threshold, summed [S, B] tie counts, ties kept in (row, global latent)
+                           order.
 """
 
 from __future__ import annotations
@@ -131,4 +135,53 @@ def route_rows(x: torch.Tensor | None, producers: list[int], consumers: list[int
     return torch.cat(parts)
 
 
-__all__ = ["two_shot_allreduce", "decode_reduce_scatter", "candidate_merge", "route_rows"]
+def bf16_keys(v: torch.Tensor) -> torch.Tensor:
+    """Order-preserving 16-bit keys of bf16 values (int64): positive values map above 0x8000."""
+    b = v.to(torch.bfloat16).view(torch.int16).to(torch.int64) & 0xFFFF
+    return torch.where(b >= 0x8000, (~b) & 0xFFFF, b | 0x8000)
+
+
+def sharded_batch_topk(h_local: torch.Tensor, k_batch: float, k_cap: int,
+                       group: dist.ProcessGroup | None = None) -> torch.Tensor:
+    """h_local [B, n_local]: this shard's pre-activations (bf16-exact).  Returns the bool mask of
+    this shard's entries among the round(k_batch * B) largest positive values of the whole
+    [B, S * n_local] batch (only the per-shard per-row top-k_cap are candidates)."""
+    S, r = dist.get_world_size(group), dist.get_rank(group)
+    B, n = h_local.shape
+    K = int(round(k_batch * B))
+    cv, ci = h_local.float().topk(min(k_cap, n), dim=1)
+    keys = bf16_keys(cv)
+    pos = cv > 0
+    hist = torch.bincount(keys[pos], minlength=65536).to(torch.int64)
+    dist.all_reduce(hist, group=group)
+    above_cum = hist.flip(0).cumsum(0).flip(0)  # count of keys >= key
+    hit = (above_cum >= K).nonzero()
+    if K > 0 and len(hit) > 0 and int(hit.max()) > 0x8000:
+        key = int(hit.max())
+        budget = K - int(above_cum[key + 1]) if key < 65535 else K
+    else:
+        key, budget = 0x8000, 0
+    tie = pos & (keys == key)
+    ties = torch.zeros(S, B, dtype=torch.int64)
+    ties[r] = tie.sum(1)
+    dist.all_reduce(ties, group=group)
+    row_tot = ties.sum(0)
+    prefix = row_tot.cumsum(0) - row_tot + ties[:r].sum(0)
+    mask = torch.zeros(B, n, dtype=torch.bool)
+    for b in range(B):
+        order = ci[b].argsort()  # ties ranked by local index inside the row
+        seen = 0
+        for j in order.tolist():
+            if not pos[b, j]:
+                continue
+            if keys[b, j] > key:
+                mask[b, ci[b, j]] = True
+            elif keys[b, j] == key:
+                if prefix[b] + seen < budget:
+                    mask[b, ci[b, j]] = True
+                seen += 1
+    return mask
+
+
+__all__ = ["two_shot_allreduce", "decode_reduce_scatter", "candidate_merge", "route_rows", "bf16_keys",
+           "sharded_batch_topk"]

@@ -24,6 +24,13 @@ Two implementations of the exchanges share the compute kernels:
   dL/dx_hat broadcast), and the statistics all-reduce is a two-shot P2P kernel.  No NCCL call
   runs inside a step.
 * `fused=False`: the same step with NCCL collectives between the kernels (the baseline).
+
+BatchTopK (keep the k*B largest activations of the TP batch, sae_lens/saes/batchtopk_sae.py:13-33;
+the reference's TP path all-gathers the [B, d_sae] pre-activations and selects on every rank)
+replaces step 3: each shard lists its per-row top-k_cap candidates, the 65536-bin histogram of
+their bf16 keys is summed over the shards (exact int32 P2P all-reduce), every rank derives the
+same threshold, and the per-row tie counts [S, B] are summed the same way so that ties at the
+threshold are kept in (row, global latent) order on every shard.
 """
 
 from __future__ import annotations
@@ -35,7 +42,7 @@ import torch.distributed as dist
 
 from saelens_b200.parallel.profiling import nccl_nvtx_range
 from saelens_b200.parallel.symm_heap import SlabBuffer, SymmetricHeap, slab_bytes_needed
-from saelens_b200.training.engine import EngineStepResult, FusedTopKEngine
+from saelens_b200.training.engine import EngineStepResult, FusedTopKEngine, update_topk_threshold_ema
 
 
 class _AllReduceBufs:
@@ -60,7 +67,7 @@ class _FusedBufs:
     """Peer-memory buffers of the fused TP step for one batch size (main or aux exchanges)."""
 
     def __init__(self, group: dist.ProcessGroup, nat: Any, B: int, D: int, k: int, world: int,
-                 with_input: bool):
+                 with_input: bool, batch_topk: bool = False):
         Bo = B // world
         f4, i4, b2 = 4, 4, 2
         sizes = []
@@ -70,6 +77,8 @@ class _FusedBufs:
                   world * Bo * D * f4, (Bo // 16) * 4, B * D * b2, (B // 16) * 4]  # decode
         if with_input:
             sizes += _AllReduceBufs.nbytes(nat, 2 * D + 3, 4, world) + _AllReduceBufs.nbytes(nat, 1, 4, world)
+        if batch_topk:
+            sizes += _AllReduceBufs.nbytes(nat, 65536, 4, world) + _AllReduceBufs.nbytes(nat, world * B, 4, world)
         heap = SymmetricHeap(group, slab_bytes_needed(sizes) + 4096)
         self.heap = heap
         self.B, self.Bo, self.k = B, Bo, k
@@ -91,6 +100,9 @@ class _FusedBufs:
         if with_input:
             self.red = _AllReduceBufs(heap, nat, 2 * D + 3, torch.float32)
             self.dead = _AllReduceBufs(heap, nat, 1, torch.float32)
+        if batch_topk:  # BatchTopK: summed key histogram and per-(rank, row) tie counts
+            self.hist = _AllReduceBufs(heap, nat, 65536, torch.int32)
+            self.ties = _AllReduceBufs(heap, nat, world * B, torch.int32)
         self.epochs: dict[str, int] = {}
 
     def next_epoch(self, name: str) -> int:
@@ -162,8 +174,6 @@ class TPTopKEngine(FusedTopKEngine):
         self.input_layout = input_layout
         super().__init__(sae, lr=lr, beta1=beta1, beta2=beta2, eps=eps, max_grad_norm=max_grad_norm,
                          h_buffer_bytes=h_buffer_bytes)
-        if self.batch_topk:
-            raise NotImplementedError("latent-sharded BatchTopK trains on the PyTorch path")
         self.n_local = self.N
         self.collectives = 0
         self.fused = bool(fused) and self.size <= 8
@@ -192,7 +202,8 @@ class TPTopKEngine(FusedTopKEngine):
         if self._fb is None or self._fb.B != B:
             if self._fb is not None:
                 self._fb.close()
-            self._fb = _FusedBufs(self.group, self.native, B, self.D, self.k, self.size, with_input=True)
+            self._fb = _FusedBufs(self.group, self.native, B, self.D, self.k, self.size, with_input=True,
+                                  batch_topk=self.batch_topk)
         return self._fb
 
     def _fused_aux_bufs(self, B: int, k_aux: int) -> _FusedBufs:
@@ -227,6 +238,40 @@ class TPTopKEngine(FusedTopKEngine):
         self.native.topk_merge(cv.view(self.size, B, k), ci.view(self.size, B, k), self.n_local, self.rank,
                                k_dev, vals, idx)
         self.launches += 1
+
+    def _batch_select(self, vals: torch.Tensor, idx: torch.Tensor, fb: _FusedBufs | None, ep: int) -> None:
+        """BatchTopK over the shards (see the module docstring).  Leaves in (vals, idx) only this
+        rank's entries among the round(k * B) largest of the TP batch."""
+        nat, S, r, B = self.native, self.size, self.rank, vals.shape[0]
+        K = int(round(self.batch_k * B))
+        hist = torch.empty(65536, dtype=torch.int32, device=self.device)
+        sel = torch.empty(4, dtype=torch.int32, device=self.device)
+        ties = torch.zeros(S, B, dtype=torch.int32, device=self.device)
+        prefix = torch.empty(B, dtype=torch.int64, device=self.device)
+        nat.batch_hist(vals, idx, hist)
+        if fb is not None:
+            st, tk = self.status.tensor, self._ticket
+            nat.p2p_allreduce(hist, 1.0, fb.heap.bases, r, fb.hist.land, fb.hist.cnt, fb.hist.out_buf.offset,
+                              fb.hist.flag, ep, tk, st)
+            hist = fb.hist.out
+        else:
+            with nccl_nvtx_range("nccl:tp_batch_hist_all_reduce", self.group):
+                dist.all_reduce(hist, group=self.group)
+            self.collectives += 1
+        nat.batch_thresh(hist, K, sel)
+        nat.batch_ties(vals, idx, sel, ties[r])
+        if fb is not None:
+            nat.p2p_allreduce(ties.view(-1), 1.0, fb.heap.bases, r, fb.ties.land, fb.ties.cnt,
+                              fb.ties.out_buf.offset, fb.ties.flag, ep, tk, st)
+            ties = fb.ties.out.view(S, B)
+            self.launches += 2
+        else:
+            with nccl_nvtx_range("nccl:tp_batch_ties_all_reduce", self.group):
+                dist.all_reduce(ties, group=self.group)
+            self.collectives += 1
+        nat.batch_filter(vals, idx, sel, ties, r, prefix, self.batch_truncated)
+        self.launches += 5
+        update_topk_threshold_ema(self.sae, sel)
 
     # ------------------------------------------------------------------ the step
     @torch.no_grad()
@@ -297,8 +342,11 @@ class TPTopKEngine(FusedTopKEngine):
                 self.launches += 1
         del H, cm, tm
 
-        # 3. global top-k from the shards' candidates
-        self._global_topk(vals, idx, k, None)
+        # 3. global top-k from the shards' candidates (BatchTopK: batch-wide threshold)
+        if self.batch_topk:
+            self._batch_select(vals, idx, None, 0)
+        else:
+            self._global_topk(vals, idx, k, None)
         if aux_on:
             self._global_topk(aux_vals, aux_idx, k_aux, k_aux_dev)
         self._mark("topk_exchange")
@@ -454,10 +502,13 @@ class TPTopKEngine(FusedTopKEngine):
         del H, cm, tm
         X = fb.x_local
 
-        # 3. candidate all-gather fused with the global merge
-        nat.topk_exchange_merge(vals, idx, self.n_local, None, bases, r, fb.cv.offset, fb.ci.offset,
-                                fb.ccnt.offset, ep, tk, st)
-        self.launches += 1
+        # 3. candidate all-gather fused with the global merge (BatchTopK: batch-wide threshold)
+        if self.batch_topk:
+            self._batch_select(vals, idx, fb, ep)
+        else:
+            nat.topk_exchange_merge(vals, idx, self.n_local, None, bases, r, fb.cv.offset, fb.ci.offset,
+                                    fb.ccnt.offset, ep, tk, st)
+            self.launches += 1
         if aux_on:
             fa = self._fused_aux_bufs(B, k_aux)
             ep_aux = fa.next_epoch("aux")

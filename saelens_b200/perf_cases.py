@@ -54,10 +54,10 @@ def phases(args: argparse.Namespace) -> None:
     rank = 0
     if world > 1:
         world, rank, _ = _init_dist()
-    s = BenchSetup(d_in=4096, d_sae=args.d_sae, k=128, batch=16384, world=world, rank=rank,
-                   tp_exchange=args.tp_exchange)
+    s = BenchSetup(d_in=args.d_in, d_sae=args.d_sae, k=args.k, batch=args.batch, world=world, rank=rank,
+                   tp_exchange=args.tp_exchange, arch=args.arch)
     eng = _make_engine(s)
-    x = synthetic_batch(BenchSetup(**{**s.__dict__, "batch": 16384 // world}), 1 + rank, device="cuda")
+    x = synthetic_batch(BenchSetup(**{**s.__dict__, "batch": args.batch // world}), 1 + rank, device="cuda")
     for _ in range(3):
         eng.step(x)
     eng.phase_times_ms()
@@ -67,12 +67,65 @@ def phases(args: argparse.Namespace) -> None:
     t = eng.phase_times_ms()
     print(rank, args.tp_exchange if world > 1 else "single",
           json.dumps({k: round(v / n, 3) for k, v in t.items()}), "total_ms", round(sum(t.values()) / n, 2),
-          flush=True)
+          "tokens_per_s", round(args.batch / (sum(t.values()) / n) * 1e3, 1), flush=True)
+    if args.arch == "batchtopk":
+        print(rank, "truncated_rows", int(eng.batch_truncated.item()), "topk_threshold",
+              float(eng.sae.topk_threshold), flush=True)
     eng.status.check()
     eng.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def tpdp(args: argparse.Namespace) -> None:
+    """Tensor x data parallel step: TP groups of `--tp` consecutive ranks, DP groups across them.
+    Each DP replica trains on `--batch` rows per step (split over its TP ranks); tokens/s counts
+    all replicas.  Device time from CUDA events over the steps, max over ranks."""
+    os.environ["SAELENS_B200_PHASE_TIMING"] = "1"
+    import torch
+    import torch.distributed as dist
+
+    from saelens_b200.parallel.tp_engine import TPTopKEngine
+    from saelens_b200.training.bench_driver import BenchSetup, _build_sae, _materialise_local, synthetic_batch
+
+    world, rank, _ = _init_dist()
+    tp_size = args.tp
+    if world % tp_size:
+        raise SystemExit(f"world {world} is not a multiple of tp {tp_size}")
+    dp_size = world // tp_size
+    tp_groups = [dist.new_group(list(range(d * tp_size, (d + 1) * tp_size))) for d in range(dp_size)]
+    dp_groups = [dist.new_group(list(range(t, world, tp_size))) for t in range(tp_size)]
+    tp_rank, dp_rank = rank % tp_size, rank // tp_size
+    s = BenchSetup(d_in=args.d_in, d_sae=args.d_sae, k=args.k, batch=args.batch, world=tp_size, rank=tp_rank,
+                   arch=args.arch)
+    sae = _materialise_local(_build_sae(s), s)
+    eng = TPTopKEngine(sae, lr=s.lr, group=tp_groups[dp_rank], fused=True, dp_group=dp_groups[tp_rank])
+    x = synthetic_batch(BenchSetup(**{**s.__dict__, "batch": args.batch // tp_size}), 1 + rank, device="cuda")
+    for _ in range(3):
+        eng.step(x)
+    eng.phase_times_ms()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        eng.step(x)
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / args.steps], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ph = eng.phase_times_ms()
+    ms = float(t.item())
+    if rank == 0:
+        print(json.dumps({"tp": tp_size, "dp": dp_size, "arch": args.arch, "d_in": args.d_in, "d_sae": args.d_sae,
+                          "k": args.k, "batch_per_replica": args.batch, "ms_per_step": round(ms, 3),
+                          "tokens_per_s": round(args.batch * dp_size / ms * 1e3, 1),
+                          "phases_ms": {k: round(v / args.steps, 3) for k, v in ph.items()}}), flush=True)
+    eng.status.check()
+    eng.close()
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 def fused_case(args: argparse.Namespace) -> None:
@@ -321,6 +374,10 @@ def main() -> None:
     a = sub.add_parser("phases")
     a.add_argument("--tp-exchange", choices=["p2p", "nccl"], default="p2p")
     a.add_argument("--d-sae", type=int, default=1048576)
+    a.add_argument("--d-in", type=int, default=4096)
+    a.add_argument("--k", type=int, default=128)
+    a.add_argument("--batch", type=int, default=16384, help="rows per step over the whole TP group")
+    a.add_argument("--arch", choices=["topk", "batchtopk"], default="topk")
     b = sub.add_parser("fused-case")
     b.add_argument("--steps", type=int, default=2)
     c = sub.add_parser("gemm")
@@ -331,12 +388,21 @@ def main() -> None:
     d.add_argument("--batch", type=int, default=8192)
     d.add_argument("--steps", type=int, default=10)
     d.add_argument("--segments", type=int, default=4)
+    td = sub.add_parser("tpdp")
+    td.add_argument("--tp", type=int, default=4)
+    td.add_argument("--arch", choices=["topk", "batchtopk"], default="batchtopk")
+    td.add_argument("--d-in", type=int, default=5120)
+    td.add_argument("--d-sae", type=int, default=327680)
+    td.add_argument("--k", type=int, default=64)
+    td.add_argument("--batch", type=int, default=8192, help="rows per step and data-parallel replica")
+    td.add_argument("--steps", type=int, default=10)
     sub.add_parser("allreduce")
     rt = sub.add_parser("router")
     rt.add_argument("--rows", type=int, default=8192)
     rt.add_argument("--d", type=int, default=4096)
     args = p.parse_args()
-    {"phases": phases, "fused-case": fused_case, "gemm": gemm, "ddp": ddp, "allreduce": allreduce, "router": router}[args.cmd](args)
+    {"phases": phases, "fused-case": fused_case, "gemm": gemm, "ddp": ddp, "allreduce": allreduce, "router": router,
+     "tpdp": tpdp}[args.cmd](args)
 
 
 if __name__ == "__main__":

@@ -26,12 +26,17 @@ class BenchSetup:
     rank: int
     lr: float = 5e-5
     tp_exchange: str = "p2p"  # "p2p": fused NVLink kernels; "nccl": NCCL collectives between kernels
+    arch: str = "topk"  # "topk" or "batchtopk" (k = mean active latents per row)
 
 
 def _build_sae(s: BenchSetup) -> Any:
+    from saelens_b200.models.batchtopk import BatchTopKTrainingSAE, BatchTopKTrainingSAEConfig
     from saelens_b200.models.topk import TopKTrainingSAE, TopKTrainingSAEConfig
 
     torch.manual_seed(1234)
+    if s.arch == "batchtopk":
+        return BatchTopKTrainingSAE(BatchTopKTrainingSAEConfig(d_in=s.d_in, d_sae=s.d_sae, k=s.k, dtype="bfloat16",
+                                                               device="meta"))
     cfg = TopKTrainingSAEConfig(d_in=s.d_in, d_sae=s.d_sae, k=s.k, dtype="bfloat16", device="meta")
     sae = TopKTrainingSAE(cfg)
     return sae
@@ -54,6 +59,8 @@ def _materialise_local(sae: Any, s: BenchSetup) -> Any:
     sae.W_enc = nn.Parameter(W_dec.T, requires_grad=False)
     sae.b_enc = nn.Parameter(torch.zeros(n_local, dtype=torch.bfloat16, device=dev), requires_grad=False)
     sae.b_dec = nn.Parameter(torch.zeros(s.d_in, dtype=torch.bfloat16, device=dev), requires_grad=False)
+    if hasattr(sae, "topk_threshold"):
+        sae.topk_threshold = torch.zeros((), dtype=torch.double, device=dev)
     sae.device = dev
     return sae
 

@@ -83,6 +83,17 @@ class _StepState:
     update: bool
 
 
+def update_topk_threshold_ema(sae: Any, sel: torch.Tensor) -> None:
+    """BatchTopK inference threshold: EMA of the smallest kept activation
+    (sae_lens/saes/batchtopk_sae.py:116-125).  sel[3] is that value's 16-bit order key (0 when
+    nothing was kept); kept values are exact bf16, so the key gives the value exactly."""
+    k3 = sel[3]
+    kept = ((k3 & 0x7FFF) << 16).view(torch.float32)
+    thr = sae.topk_threshold
+    lr_t = float(sae.cfg.topk_threshold_lr)
+    thr.copy_(torch.where(k3 > 0x8000, (1 - lr_t) * thr + lr_t * kept.to(thr.dtype), thr))
+
+
 class FusedTopKEngine:
     """Owns the optimizer state of a (possibly latent-sharded) TopK SAE and steps it natively."""
 
@@ -117,6 +128,7 @@ class FusedTopKEngine:
         W_dec = sae.W_dec.detach()
         W_enc = sae.W_enc.detach()
         self.N, self.D = W_dec.shape
+        self.k = min(self.k, self.N)  # a latent shard may be narrower than the candidate cap
         if self.D % 64 != 0 or self.N % 256 != 0:
             raise ValueError(f"fused engine needs d_in % 64 == 0 and local d_sae % 256 == 0, got {self.D}, {self.N}")
         if self.k > self.N:
@@ -305,13 +317,9 @@ class FusedTopKEngine:
         del H, cm, tm
         if self.batch_topk:
             # batch-wide selection among the per-row candidates (k * B largest ReLU activations)
-            nat.batch_topk_select(vals, idx, int(round(self.batch_k * B)), self.batch_truncated)
-            self.launches += 4
-            kept = torch.where(idx >= 0, vals, torch.full_like(vals, float("inf"))).amin()
-            thr = self.sae.topk_threshold
-            lr_t = float(self.sae.cfg.topk_threshold_lr)
-            new_thr = torch.where(torch.isfinite(kept), (1 - lr_t) * thr + lr_t * kept.to(thr.dtype), thr)
-            thr.copy_(new_thr)
+            sel = nat.batch_topk_select(vals, idx, int(round(self.batch_k * B)), self.batch_truncated)
+            self.launches += 5
+            update_topk_threshold_ema(self.sae, sel)
             self._mark("batch_topk_select")
 
         # 3. decode + MSE + dL/dx_hat (+ sum over rows for the b_dec gradient)

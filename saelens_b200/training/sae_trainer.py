@@ -153,14 +153,13 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
 
             group = dp_group if dp_group is not None else getattr(sae, "process_group", None) or dist.group.WORLD
             tp_group = getattr(self._base_sae, "_tp_group", None)
-            batch_topk = type(self._base_sae).__name__ == "BatchTopKTrainingSAE"
             if engine_supported(self._base_sae) and tp_group is None:
                 from saelens_b200.parallel.ddp_engine import DDPTopKEngine
 
                 self.engine = DDPTopKEngine(self._base_sae, lr=cfg.lr, group=group, beta1=cfg.adam_beta1,
                                             beta2=cfg.adam_beta2)
                 self._engine_stats_global = True
-            elif engine_supported(self._base_sae) and not batch_topk and getattr(cfg, "tp_exchange", "p2p") == "p2p":
+            elif engine_supported(self._base_sae) and getattr(cfg, "tp_exchange", "p2p") == "p2p":
                 from saelens_b200.parallel.tp_engine import TPTopKEngine
 
                 self.engine = TPTopKEngine(self._base_sae, lr=cfg.lr, group=tp_group, beta1=cfg.adam_beta1,
@@ -173,8 +172,7 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
             from saelens_b200.training.engine import FusedTopKEngine, engine_supported
 
             tp_group = getattr(self._base_sae, "_tp_group", None)
-            batch_topk = type(self._base_sae).__name__ == "BatchTopKTrainingSAE"
-            if engine_supported(self._base_sae) and tp_group is not None and not batch_topk:
+            if engine_supported(self._base_sae) and tp_group is not None:
                 from saelens_b200.parallel.tp_engine import TPTopKEngine
 
                 self.engine = TPTopKEngine(self._base_sae, lr=cfg.lr, group=tp_group, beta1=cfg.adam_beta1,

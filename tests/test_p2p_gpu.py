@@ -68,6 +68,12 @@ def _ar_worker(rank, world, port, out_dir):
                               tk, st.tensor)
             outs.append(bufs.out.clone().cpu())
         results[name] = outs
+    # exact int32 sums (histograms, counts) above 2^24, where fp32 accumulation would round
+    bufs = _AllReduceBufs(heap, nat, 65536 + 7, torch.int32)
+    xi = (torch.arange(65536 + 7, dtype=torch.int64) * (rank + 3) + (1 << 24) + 1).to(torch.int32).cuda()
+    nat.p2p_allreduce(xi, 1.0, heap.bases, rank, bufs.land, bufs.cnt, bufs.out_buf.offset, bufs.flag, 1, tk,
+                      st.tensor)
+    results["i32"] = bufs.out.clone().cpu()
     torch.cuda.synchronize()
     st.check("allreduce")
     torch.save(results, os.path.join(out_dir, f"ar{rank}.pt"))
@@ -92,3 +98,7 @@ def test_p2p_allreduce_two_ranks(tmp_path):
                 tol = 1e-6 if dtype == torch.float32 else 1e-2
                 assert torch.allclose(got, want.to(dtype).float(), atol=tol, rtol=tol), (name, ep, r)
             assert torch.equal(res[0][name][ep - 1], res[1][name][ep - 1])
+    ar = torch.arange(65536 + 7, dtype=torch.int64)
+    want_i = (ar * 3 + (1 << 24) + 1) + (ar * 4 + (1 << 24) + 1)
+    for r in range(2):
+        assert torch.equal(res[r]["i32"].to(torch.int64), want_i)

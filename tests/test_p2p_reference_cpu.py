@@ -45,6 +45,10 @@ def _worker(rank, world, port, out_dir):
     # row routing: rank 0 produces, the others consume
     xr = torch.randn(12, 4, generator=torch.Generator().manual_seed(5)) if rank == 0 else None
     res["route"] = R.route_rows(xr, [0], list(range(1, world)), 12, "unit_norm", 2.0)
+    # sharded BatchTopK: a coarse value grid makes ties at the threshold certain
+    hg = torch.Generator().manual_seed(3)
+    H = (torch.randint(-6, 10, (16, 12 * world), generator=hg).float() * 0.25)
+    res["btk"] = R.sharded_batch_topk(H[:, rank * 12 : (rank + 1) * 12].contiguous(), 2.5, 8)
     torch.save(res, os.path.join(out_dir, f"r{rank}.pt"))
     dist.destroy_process_group()
 
@@ -87,3 +91,15 @@ def test_reference_algorithms(tmp_path, world):
     got = torch.cat([r[i]["route"] for i in range(1, world)])
     assert torch.equal(got, xn)
     assert r[0]["route"] is None
+    # sharded BatchTopK = the top K of the full batch, ties in (row, latent) order
+    H = (torch.randint(-6, 10, (16, 12 * world), generator=torch.Generator().manual_seed(3)).float() * 0.25)
+    K = round(2.5 * 16)
+    flat = H.reshape(-1)
+    order = sorted(range(flat.numel()), key=lambda i: (-float(flat[i]), i))  # (row, latent) = flat order
+    want = torch.zeros(flat.numel(), dtype=torch.bool)
+    for i in order[:K]:
+        if flat[i] > 0:
+            want[i] = True
+    got = torch.cat([r[i]["btk"] for i in range(world)], dim=1).reshape(-1)
+    assert int(got.sum()) == K
+    assert torch.equal(got, want)

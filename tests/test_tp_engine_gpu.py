@@ -1,5 +1,6 @@
 """Tensor-parallel native step (2 ranks; fused NVLink kernels or NCCL exchanges) against the
-single-GPU native step, with and without the dead-latent aux loss."""
+single-GPU native step, with and without the dead-latent aux loss, for TopK and BatchTopK (the
+batch-wide threshold is taken over the shards)."""
 
 import os
 import socket
@@ -18,11 +19,15 @@ def _free_port() -> int:
     return p
 
 
-def _build(d_in, d_sae, k, device):
+def _build(d_in, d_sae, k, device, kind="topk"):
+    from saelens_b200.models.batchtopk import BatchTopKTrainingSAE, BatchTopKTrainingSAEConfig
     from saelens_b200.models.topk import TopKTrainingSAE, TopKTrainingSAEConfig
 
     torch.manual_seed(7)
-    sae = TopKTrainingSAE(TopKTrainingSAEConfig(d_in=d_in, d_sae=d_sae, k=k, device=device))
+    if kind == "batchtopk":
+        sae = BatchTopKTrainingSAE(BatchTopKTrainingSAEConfig(d_in=d_in, d_sae=d_sae, k=k, device=device))
+    else:
+        sae = TopKTrainingSAE(TopKTrainingSAEConfig(d_in=d_in, d_sae=d_sae, k=k, device=device))
     with torch.no_grad():
         sae.b_enc.normal_(0, 0.01)
         sae.b_dec.normal_(0, 0.05)
@@ -33,7 +38,7 @@ def _dead_mask(d_sae, device):
     return (torch.arange(d_sae, device=device) % 3) == 0
 
 
-def _worker(rank, world, port, d_in, d_sae, k, B, out_dir, exchange):
+def _worker(rank, world, port, d_in, d_sae, k, B, out_dir, exchange, kind):
     import torch.distributed as dist
     from datetime import timedelta
 
@@ -43,7 +48,7 @@ def _worker(rank, world, port, d_in, d_sae, k, B, out_dir, exchange):
                             device_id=torch.device("cuda", rank))
     from saelens_b200.parallel.tp_engine import TPTopKEngine
 
-    sae = _build(d_in, d_sae, k, f"cuda:{rank}")
+    sae = _build(d_in, d_sae, k, f"cuda:{rank}", kind)
     sae.shard_weights(dist.group.WORLD)
     eng = TPTopKEngine(sae, lr=1e-3, group=dist.group.WORLD, fused=exchange == "p2p")
     g = torch.Generator(device="cpu").manual_seed(11)
@@ -58,22 +63,27 @@ def _worker(rank, world, port, d_in, d_sae, k, B, out_dir, exchange):
     torch.cuda.synchronize()
     eng.status.check()
     eng.close()
-    torch.save({"losses": losses, "p_dec": eng.p_dec.cpu(), "p_enc": eng.p_enc.cpu(), "p_bdec": eng.p_bdec.cpu()},
-               os.path.join(out_dir, f"rank{rank}.pt"))
+    out = {"losses": losses, "p_dec": eng.p_dec.cpu(), "p_enc": eng.p_enc.cpu(), "p_bdec": eng.p_bdec.cpu()}
+    if kind == "batchtopk":
+        out["thr"] = float(sae.topk_threshold)
+        out["truncated"] = int(eng.batch_truncated.item())
+    torch.save(out, os.path.join(out_dir, f"rank{rank}.pt"))
     dist.barrier()
     dist.destroy_process_group()
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
-def test_tp2_matches_single_gpu(tmp_path, exchange):
+@pytest.mark.parametrize("exchange,kind", [("p2p", "topk"), ("nccl", "topk"), ("p2p", "batchtopk"),
+                                           ("nccl", "batchtopk")])
+def test_tp2_matches_single_gpu(tmp_path, exchange, kind):
     import torch.multiprocessing as mp
 
     from saelens_b200.training.engine import FusedTopKEngine
 
     d_in, d_sae, k, B = 256, 2048, 32, 512
-    mp.spawn(_worker, args=(2, _free_port(), d_in, d_sae, k, B, str(tmp_path), exchange), nprocs=2, join=True)
-    sae = _build(d_in, d_sae, k, "cuda:0")
+    mp.spawn(_worker, args=(2, _free_port(), d_in, d_sae, k, B, str(tmp_path), exchange, kind), nprocs=2,
+             join=True)
+    sae = _build(d_in, d_sae, k, "cuda:0", kind)
     eng = FusedTopKEngine(sae, lr=1e-3)
     g = torch.Generator(device="cpu").manual_seed(11)
     x = torch.randn(B, d_in, generator=g).to(torch.bfloat16).cuda()
@@ -83,6 +93,13 @@ def test_tp2_matches_single_gpu(tmp_path, exchange):
     for a, b in zip(r[0]["losses"], ref_losses):
         assert abs(a - b) <= 1e-3 * abs(b), (r[0]["losses"], ref_losses)
     assert r[0]["losses"] == r[1]["losses"]
+    if kind == "batchtopk":
+        # no row hit a candidate cap, so both runs select the same k*B entries
+        assert int(eng.batch_truncated.item()) == 0 and r[0]["truncated"] == r[1]["truncated"] == 0
+        want = float(sae.topk_threshold)
+        assert want > 0 and r[0]["thr"] == r[1]["thr"]
+        # the EMA of the smallest kept value; later steps' weights differ in their last bits
+        assert abs(r[0]["thr"] - want) <= 1e-2 * want, (r[0]["thr"], want)
     n = d_sae // 2
 
     def close(got, want, name):
