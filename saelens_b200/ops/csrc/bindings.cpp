@@ -38,7 +38,9 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
                  const c10::optional<torch::Tensor>& since_fired, const torch::Tensor& idx,
                  const c10::optional<torch::Tensor>& aux_idx, int64_t j0, int64_t j1, bool zero_empty,
                  const c10::optional<torch::Tensor>& jr_thr, const c10::optional<torch::Tensor>& jr_pre,
-                 double jr_bandwidth, double jr_l0c, const c10::optional<torch::Tensor>& jr_gthr);
+                 double jr_bandwidth, double jr_l0c, const c10::optional<torch::Tensor>& jr_gthr,
+                 const std::vector<int64_t>& rs_bases, int64_t rs_rank, int64_t rs_dec_off, int64_t rs_enc_off,
+                 int64_t rs_n);
 void threshold_select(const torch::Tensor& H, const torch::Tensor& cmax, const torch::Tensor& lo,
                       const torch::Tensor& lo_cmin, const torch::Tensor& out_val, const torch::Tensor& out_idx,
                       const torch::Tensor& counts, const c10::optional<torch::Tensor>& truncated);
@@ -72,6 +74,13 @@ void gemm_ag_tn_bf16(const torch::Tensor& x_own, const std::vector<int64_t>& pee
                      const c10::optional<torch::Tensor>& scale, bool relu, const c10::optional<torch::Tensor>& out,
                      const c10::optional<torch::Tensor>& cmax, const torch::Tensor& status,
                      const torch::Tensor& ticket, int64_t max_ctas, const c10::optional<torch::Tensor>& tmax);
+void gemm_fsdp_tn_bf16(const torch::Tensor& A, const torch::Tensor& w_own, const std::vector<int64_t>& peer_bases,
+                       int64_t rank, int64_t w_off, int64_t flag_off, bool push, int64_t epoch,
+                       const c10::optional<torch::Tensor>& w2_own, int64_t w2_off, int64_t flag2_off,
+                       const c10::optional<torch::Tensor>& bias, const c10::optional<torch::Tensor>& scale, bool relu,
+                       const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& cmax,
+                       const torch::Tensor& status, const torch::Tensor& ticket, int64_t max_ctas,
+                       const c10::optional<torch::Tensor>& tmax);
 void decode_rs(const torch::Tensor& vals, const torch::Tensor& idx, bool relu,
                const c10::optional<torch::Tensor>& inv_scale, const torch::Tensor& W,
                const std::vector<int64_t>& peer_bases, int64_t rank, int64_t land_off, int64_t lcnt_off,
@@ -88,6 +97,8 @@ std::vector<int64_t> p2p_allreduce_sizes(int64_t n, int64_t elem_bytes, int64_t 
 void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64_t>& peer_bases, int64_t rank,
                    int64_t land_off, int64_t cnt_off, int64_t out_off, int64_t flag_off, int64_t epoch,
                    const torch::Tensor& ticket, const torch::Tensor& status, int64_t sq_off, int64_t chunk);
+void p2p_slot_reduce(const torch::Tensor& land, double scale, const torch::Tensor& out,
+                     const c10::optional<torch::Tensor>& sumsq);
 void p2p_wait_flags(const torch::Tensor& flags, int64_t target, const torch::Tensor& status);
 std::tuple<int64_t, torch::Tensor> symm_alloc(int64_t nbytes);
 int64_t symm_open(const torch::Tensor& handle);
@@ -131,7 +142,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("sumsq"), py::arg("fire_counts"), py::arg("act_freq"), py::arg("since_fired"), py::arg("idx"),
         py::arg("aux_idx"), py::arg("j0") = 0, py::arg("j1") = -1, py::arg("zero_empty") = false,
         py::arg("jr_thr") = py::none(), py::arg("jr_pre") = py::none(), py::arg("jr_bandwidth") = 0.0,
-        py::arg("jr_l0c") = 0.0, py::arg("jr_gthr") = py::none());
+        py::arg("jr_l0c") = 0.0, py::arg("jr_gthr") = py::none(), py::arg("rs_bases") = std::vector<int64_t>{},
+        py::arg("rs_rank") = 0, py::arg("rs_dec_off") = 0, py::arg("rs_enc_off") = 0, py::arg("rs_n") = 0);
   m.def("threshold_select", &sb::threshold_select);
   m.def("adam_bdec", &sb::adam_bdec);
   m.def("adam_rows", &sb::adam_rows);
@@ -142,6 +154,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("x_off"), py::arg("flag_off"), py::arg("total_rows"), py::arg("m_base"), py::arg("M"), py::arg("push"),
         py::arg("epoch"), py::arg("B"), py::arg("bias"), py::arg("scale"), py::arg("relu"), py::arg("out"),
         py::arg("cmax"), py::arg("status"), py::arg("ticket"), py::arg("max_ctas"), py::arg("tmax") = py::none());
+  m.def("gemm_fsdp_tn_bf16", &sb::gemm_fsdp_tn_bf16, py::arg("A"), py::arg("w_own"), py::arg("peer_bases"),
+        py::arg("rank"), py::arg("w_off"), py::arg("flag_off"), py::arg("push"), py::arg("epoch"), py::arg("w2_own"),
+        py::arg("w2_off"), py::arg("flag2_off"), py::arg("bias"), py::arg("scale"), py::arg("relu"), py::arg("out"),
+        py::arg("cmax"), py::arg("status"), py::arg("ticket"), py::arg("max_ctas") = 0, py::arg("tmax") = py::none());
   m.def("decode_rs", &sb::decode_rs);
   m.def("topk_exchange_merge", &sb::topk_exchange_merge);
   m.def("p2p_allreduce_sizes", &sb::p2p_allreduce_sizes, py::arg("n"), py::arg("elem_bytes"), py::arg("world"),
@@ -150,6 +166,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rank"), py::arg("land_off"), py::arg("cnt_off"), py::arg("out_off"), py::arg("flag_off"),
         py::arg("epoch"), py::arg("ticket"), py::arg("status"), py::arg("sq_off") = -1, py::arg("chunk") = 0);
   m.def("p2p_wait_flags", &sb::p2p_wait_flags);
+  m.def("p2p_slot_reduce", &sb::p2p_slot_reduce);
   m.def("p2p_route_rows", &sb::p2p_route_rows);
   m.def("p2p_wait_targets", &sb::p2p_wait_targets);
   m.def("p2p_signal", &sb::p2p_signal);

@@ -23,6 +23,15 @@
 // order starts with the rank's own rows, then the next rank's, so the transfers overlap the
 // tensor-core work instead of preceding it (the reference all-gathers first and multiplies
 // after: sae_lens/distributed.py:404-461 around sae_lens/saes/topk_sae.py:626).
+//
+// Parameter all-gather variant (sharded data parallel / FSDP, operand = B): B is the full
+// encoder weight [N, K] in the slab, of which each rank owns the latents [r*n, (r+1)*n).  The
+// copy warps push the own latent rows, one 256-row n-tile at a time, to every rank; the producer
+// waits for each n-tile's flag, and the tile walk starts at the rank's own latents.  A second
+// operand (the decoder shard) can ride along: its tiles are pushed and flagged after the first
+// operand's, and nothing in this kernel waits for them (the decode does).  Replaces the
+// parameter all-gather that torch FSDP runs before the forward
+// (sae_lens/llm_sae_training_runner.py:449-463).
 #include <ATen/cuda/CUDAContext.h>
 #include <cstdlib>
 #include <string>
@@ -67,18 +76,22 @@ struct Epi {
 // All-gather fusion parameters (byte offsets inside the symmetric slabs).
 struct Ag {
   p2p::Peers P;
-  const __nv_bfloat16* src;  // this rank's rows [Bo, K] (any device memory)
-  int64_t x_off;             // offset of the full input [B, K] bf16 in every slab
-  int64_t flag_off;          // offset of the per-m-tile epoch flags [B / BM] u32
-  int rows_per_rank;         // Bo (multiple of BM)
-  int m_base;                // first global row of this launch's A (multiple of BM)
-  int rot;                   // m-tile rotation so that the tile walk starts at the own rows
+  const __nv_bfloat16* src;  // this rank's rows [rows_per_rank, K] (any device memory)
+  int64_t x_off;             // offset of the full operand [S * rows_per_rank, K] bf16 in every slab
+  int64_t flag_off;          // offset of the per-unit epoch flags u32 (unit = BM rows for A, BN for B)
+  int rows_per_rank;         // multiple of the unit
+  int m_base;                // first global row of this launch's A (multiple of BM; operand A)
+  int rot;                   // tile rotation so that the tile walk starts at the own rows
   int push;                  // 1: this launch pushes the own rows (first launch of a step)
   uint32_t epoch;
   int* ticket;               // push-item counter, zero at launch: items go to whichever CTAs run
+  int operand;               // 0: gather A rows (m-tiles); 1: gather B rows (n-tiles)
+  const __nv_bfloat16* src2;  // optional second operand pushed along (same row split), or nullptr
+  int64_t x2_off, flag2_off;
 };
 
-__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mt, int& nt, int rot = 0) {
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mt, int& nt, int rot = 0,
+                                            int rot_n = 0) {
   const int group = t / (num_m * GROUP_N);
   const int first_n = group * GROUP_N;
   const int gsize = min(GROUP_N, num_n - first_n);
@@ -86,6 +99,7 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mt
   mt = r / gsize;
   if (rot) mt = (mt + rot) % num_m;
   nt = first_n + r % gsize;
+  if (rot_n) nt = (nt + rot_n) % num_n;
 }
 
 // Epilogue of one accumulator tile: this thread's TMEM lane `trow` holds output row `row`
@@ -150,39 +164,50 @@ __device__ __forceinline__ void epilogue_tile(const Epi& ep, uint32_t trow, int 
   if (ep.tmax && row < M) ep.tmax[int64_t(row) * ep.ldt + nt] = __float2bfloat16_rn(tile_max);
 }
 
-// All-gather pushers (two warps, ct = 0..63): claim (distance d, own m-tile j) items from the
-// launch's ticket counter, copy own rows [j*BM, (j+1)*BM) into the slab of rank (r - d) mod S,
-// which consumes them d-th in its rotated tile walk, and publish the tile's epoch flag there.
+// All-gather pushers (two warps, ct = 0..63): claim (operand, distance d, own unit j) items from
+// the launch's ticket counter, copy own rows [j*U, (j+1)*U) (U = BM for A, BN for B) into the
+// slab of rank (r - d) mod S, which consumes them d-th in its rotated tile walk, and publish the
+// unit's epoch flag there.  A copy whose source already is the destination (the own shard kept
+// in place in the slab) only publishes.  Second-operand items come after all first-operand ones.
 __device__ __forceinline__ void ag_push(const Ag& ag, int K, int ct) {
   if (!ag.push) return;
   __shared__ int s_item;
   const int S = ag.P.world, r = ag.P.rank;
-  const int mtpr = ag.rows_per_rank / BM;
-  const int64_t vec_per_tile = int64_t(BM) * K / 8;
+  const int U = ag.operand ? BN : BM;
+  const int upr = ag.rows_per_rank / U;
+  const int64_t vec_per_unit = int64_t(U) * K / 8;
+  const int per_op = S * upr;
+  const int n_items = ag.src2 ? 2 * per_op : per_op;
   while (true) {
     if (ct == 0) s_item = atomicAdd(ag.ticket, 1);
     asm volatile("bar.sync 1, %0;" ::"n"(32 * NUM_COPY_WARPS) : "memory");
-    const int item = s_item;
-    if (item >= S * mtpr) break;
-    const int d = item / mtpr, j = item - d * mtpr;
+    int item = s_item;
+    if (item >= n_items) break;
+    const bool second = item >= per_op;
+    if (second) item -= per_op;
+    const int d = item / upr, j = item - d * upr;
     const int dst = (r - d + S) % S;
-    const uint4* src = reinterpret_cast<const uint4*>(ag.src + int64_t(j) * BM * K);
-    uint4* out = reinterpret_cast<uint4*>(p2p::at<__nv_bfloat16>(ag.P, dst, ag.x_off) +
-                                          (int64_t(r) * ag.rows_per_rank + int64_t(j) * BM) * K);
-    int64_t v = ct;
-    for (; v + 3 * 64 < vec_per_tile; v += 4 * 64) {
-      const uint4 a0 = __ldg(src + v), a1 = __ldg(src + v + 64), a2 = __ldg(src + v + 128),
-                  a3 = __ldg(src + v + 192);
-      out[v] = a0;
-      out[v + 64] = a1;
-      out[v + 128] = a2;
-      out[v + 192] = a3;
+    const __nv_bfloat16* base = second ? ag.src2 : ag.src;
+    const uint4* src = reinterpret_cast<const uint4*>(base + int64_t(j) * U * K);
+    uint4* out = reinterpret_cast<uint4*>(p2p::at<__nv_bfloat16>(ag.P, dst, second ? ag.x2_off : ag.x_off) +
+                                          (int64_t(r) * ag.rows_per_rank + int64_t(j) * U) * K);
+    if (reinterpret_cast<const void*>(out) != reinterpret_cast<const void*>(src)) {
+      int64_t v = ct;
+      for (; v + 3 * 64 < vec_per_unit; v += 4 * 64) {
+        const uint4 a0 = __ldg(src + v), a1 = __ldg(src + v + 64), a2 = __ldg(src + v + 128),
+                    a3 = __ldg(src + v + 192);
+        out[v] = a0;
+        out[v + 64] = a1;
+        out[v + 128] = a2;
+        out[v + 192] = a3;
+      }
+      for (; v < vec_per_unit; v += 64) out[v] = __ldg(src + v);
     }
-    for (; v < vec_per_tile; v += 64) out[v] = __ldg(src + v);
     __threadfence_system();
     asm volatile("bar.sync 1, %0;" ::"n"(32 * NUM_COPY_WARPS) : "memory");
     if (ct == 0)
-      st_release_sys_u32(p2p::at<uint32_t>(ag.P, dst, ag.flag_off) + (r * mtpr + j), ag.epoch);
+      st_release_sys_u32(p2p::at<uint32_t>(ag.P, dst, second ? ag.flag2_off : ag.flag_off) + (r * upr + j),
+                         ag.epoch);
   }
 }
 
@@ -244,9 +269,9 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int mt, nt;
-        tile_coords(t, num_m, num_n, mt, nt, AG ? ag.rot : 0);
+        tile_coords(t, num_m, num_n, mt, nt, AG && !ag.operand ? ag.rot : 0, AG && ag.operand ? ag.rot : 0);
         if (AG) {
-          const int gm = ag.m_base / BM + mt;
+          const int gm = ag.operand ? nt : ag.m_base / BM + mt;
           if (!(ready_bits[gm >> 5] & (1u << (gm & 31)))) {
             const uint32_t* f = p2p::at<uint32_t>(ag.P, ag.P.rank, ag.flag_off) + gm;
             if (!wait_geq_sys(f, ag.epoch, status, kTimeoutPeerFlag)) {
@@ -327,7 +352,7 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
     uint32_t tc = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tc) {
       int mt, nt;
-      tile_coords(t, num_m, num_n, mt, nt, AG ? ag.rot : 0);
+      tile_coords(t, num_m, num_n, mt, nt, AG && !ag.operand ? ag.rot : 0, AG && ag.operand ? ag.rot : 0);
       const int acc = tc & 1;
       const uint32_t aph = (tc >> 1) & 1;
       if (!mbar_wait_bounded(&tfull_bar[acc], aph, abort_flag, status, kTimeoutEpilogue)) break;
@@ -426,9 +451,9 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
       bool ok = true;
       for (int t = pair; t < num_tiles && ok; t += npairs) {
         int mt, nt;
-        tile_coords(t, num_m, num_n, mt, nt, AG ? ag.rot : 0);
+        tile_coords(t, num_m, num_n, mt, nt, AG && !ag.operand ? ag.rot : 0, AG && ag.operand ? ag.rot : 0);
         if (AG) {
-          const int gm = ag.m_base / BM + 2 * mt + int(cta);
+          const int gm = ag.operand ? nt : ag.m_base / BM + 2 * mt + int(cta);
           if (!(ready_bits[gm >> 5] & (1u << (gm & 31)))) {
             const uint32_t* f = p2p::at<uint32_t>(ag.P, ag.P.rank, ag.flag_off) + gm;
             if (!wait_geq_sys(f, ag.epoch, status, kTimeoutPeerFlag)) {
@@ -510,7 +535,7 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
     uint32_t tc = 0;
     for (int t = pair; t < num_tiles; t += npairs, ++tc) {
       int mt, nt;
-      tile_coords(t, num_m, num_n, mt, nt, AG ? ag.rot : 0);
+      tile_coords(t, num_m, num_n, mt, nt, AG && !ag.operand ? ag.rot : 0, AG && ag.operand ? ag.rot : 0);
       const int acc = tc & 1;
       const uint32_t aph = (tc >> 1) & 1;
       if (!mbar_wait_bounded(&tfull_bar[acc], aph, abort_flag, status, kTimeoutEpilogue)) break;
@@ -718,6 +743,60 @@ void gemm_ag_tn_bf16(const torch::Tensor& x_own, const std::vector<int64_t>& pee
   if (push) C10_CUDA_CHECK(cudaMemsetAsync(ag.ticket, 0, sizeof(int), at::cuda::getCurrentCUDAStream()));
   const char* a_ptr = reinterpret_cast<const char*>(peer_bases[rank]) + x_off + m_base * K * 2;
   launch_gemm<true>(a_ptr, K, M, B, ep, status, max_ctas, ag, pair);
+}
+
+// Parameter all-gather fused encoder GEMM (sharded data parallel): out = epilogue(A @ W^T) where
+// W [N, K] is the full encoder weight at byte offset w_off of every rank's slab and this rank
+// owns rows [rank*n, (rank+1)*n) of it (`w_own`, usually that very slab region).  With `push`,
+// the kernel distributes the own rows (and, if given, the rows of `w2_own` into the [N, K] area
+// at w2_off with flags at flag2_off) to every rank; it waits (bounded) for the epoch flag of each
+// 256-row n-tile at flag_off before reading it.  A: [M, K] local rows.
+void gemm_fsdp_tn_bf16(const torch::Tensor& A, const torch::Tensor& w_own, const std::vector<int64_t>& peer_bases,
+                       int64_t rank, int64_t w_off, int64_t flag_off, bool push, int64_t epoch,
+                       const c10::optional<torch::Tensor>& w2_own, int64_t w2_off, int64_t flag2_off,
+                       const c10::optional<torch::Tensor>& bias, const c10::optional<torch::Tensor>& scale, bool relu,
+                       const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& cmax,
+                       const torch::Tensor& status, const torch::Tensor& ticket, int64_t max_ctas,
+                       const c10::optional<torch::Tensor>& tmax) {
+  const int64_t S = int64_t(peer_bases.size());
+  TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "gemm_fsdp: bad group");
+  TORCH_CHECK(A.is_cuda() && A.scalar_type() == at::kBFloat16 && A.dim() == 2 && A.stride(1) == 1,
+              "gemm_fsdp: A must be CUDA bf16 with contiguous rows");
+  TORCH_CHECK(w_own.is_cuda() && w_own.scalar_type() == at::kBFloat16 && w_own.is_contiguous() &&
+                  w_own.size(1) == A.size(1),
+              "gemm_fsdp: w_own must be contiguous bf16 [n, K]");
+  const int64_t M = A.size(0), K = A.size(1), n = w_own.size(0), N = n * S;
+  TORCH_CHECK(n % gemm::BN == 0 && K % gemm::BK == 0, "gemm_fsdp: shard rows % 256 and K % 64");
+  TORCH_CHECK(N / gemm::BN <= gemm::MAX_MTILES && M >= 1 && M < (1ll << 31), "gemm_fsdp: size");
+  TORCH_CHECK(w_off % 16 == 0 && flag_off % 4 == 0 && w2_off % 16 == 0 && flag2_off % 4 == 0,
+              "gemm_fsdp: slab offsets must be aligned");
+  if (w2_own) {
+    TORCH_CHECK(w2_own->is_cuda() && w2_own->scalar_type() == at::kBFloat16 && w2_own->is_contiguous() &&
+                    w2_own->sizes() == w_own.sizes(),
+                "gemm_fsdp: w2_own must be contiguous bf16 like w_own");
+  }
+  const at::cuda::CUDAGuard guard(A.device());
+  const gemm::Epi ep = make_epi(M, N, bias, scale, relu, out, cmax, tmax);
+  gemm::Ag ag{};
+  ag.P = p2p::make_peers(peer_bases, rank);
+  ag.src = reinterpret_cast<const __nv_bfloat16*>(w_own.data_ptr());
+  ag.x_off = w_off;
+  ag.flag_off = flag_off;
+  ag.rows_per_rank = int(n);
+  ag.operand = 1;
+  ag.rot = int((rank * n) / gemm::BN);
+  ag.push = push ? 1 : 0;
+  ag.epoch = uint32_t(epoch);
+  ag.src2 = w2_own ? reinterpret_cast<const __nv_bfloat16*>(w2_own->data_ptr()) : nullptr;
+  ag.x2_off = w2_off;
+  ag.flag2_off = flag2_off;
+  TORCH_CHECK(ticket.is_cuda() && ticket.scalar_type() == at::kInt && ticket.numel() >= 1, "gemm_fsdp: ticket");
+  ag.ticket = ticket.data_ptr<int>();
+  if (push) C10_CUDA_CHECK(cudaMemsetAsync(ag.ticket, 0, sizeof(int), at::cuda::getCurrentCUDAStream()));
+  // the full weight as seen in this rank's slab
+  auto W = torch::from_blob(reinterpret_cast<char*>(peer_bases[rank]) + w_off, {N, K},
+                            A.options().dtype(at::kBFloat16));
+  launch_gemm<true>(A.data_ptr(), A.stride(0), M, W, ep, status, max_ctas, ag, use_pair(M));
 }
 
 }  // namespace sb

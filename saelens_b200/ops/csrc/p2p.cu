@@ -178,6 +178,49 @@ __global__ void __launch_bounds__(AR_THREADS) allreduce_kernel(const __grid_cons
     wait_geq_sys(at<uint32_t>(a.P, r, a.flag_off) + c, a.epoch, a.status, kTimeoutPeerFlag);
 }
 
+// Owner side of the gradient reduce-scatter of sharded data parallel: every rank stored its
+// gradient rows of this rank's latents into slot [src] of land [S, n*D] (bf16); out = scale *
+// sum over src (rank order, fp32), rounded to bf16, and sumsq += the rounded result's squares.
+__global__ void slot_reduce_kernel(const __nv_bfloat16* __restrict__ land, int S, int64_t nvec, float scale,
+                                   __nv_bfloat16* __restrict__ out, float* __restrict__ sumsq) {
+  __shared__ float s_red[AR_THREADS / 32];
+  float sq = 0.f;
+  for (int64_t v = int64_t(blockIdx.x) * AR_THREADS + threadIdx.x; v < nvec; v += int64_t(gridDim.x) * AR_THREADS) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int src = 0; src < S; ++src) {
+      const uint4 q = __ldcg(reinterpret_cast<const uint4*>(land) + int64_t(src) * nvec + v);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&q);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h[e]);
+        acc[2 * e] += f.x;
+        acc[2 * e + 1] += f.y;
+      }
+    }
+    uint4 o;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const __nv_bfloat162 hb = __floats2bfloat162_rn(acc[2 * e] * scale, acc[2 * e + 1] * scale);
+      w[e] = *reinterpret_cast<const uint32_t*>(&hb);
+      const float2 f = __bfloat1622float2(hb);
+      sq += f.x * f.x + f.y * f.y;
+    }
+    reinterpret_cast<uint4*>(out)[v] = o;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  if (threadIdx.x == 0 && sumsq) {
+    float t = 0.f;
+    for (int i = 0; i < AR_THREADS / 32; ++i) t += s_red[i];
+    atomicAdd(sumsq, t);
+  }
+}
+
 __global__ void wait_flags_kernel(const uint32_t* flags, int64_t n, uint32_t target, int* status) {
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
     wait_geq_sys(flags + i, target, status, kTimeoutPeerFlag);
@@ -395,6 +438,28 @@ void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64
     p2p::allreduce_kernel<int><<<dim3(grid), dim3(p2p::AR_THREADS), 0, stream>>>(a);
   else
     p2p::allreduce_kernel<__nv_bfloat16><<<dim3(grid), dim3(p2p::AR_THREADS), 0, stream>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// out [n, D] bf16 = scale * sum over the S slots of land [S, n, D] bf16 (see slot_reduce_kernel);
+// sumsq (fp32 [1], optional) accumulates the squares of the result.
+void p2p_slot_reduce(const torch::Tensor& land, double scale, const torch::Tensor& out,
+                     const c10::optional<torch::Tensor>& sumsq) {
+  TORCH_CHECK(land.is_cuda() && land.scalar_type() == at::kBFloat16 && land.is_contiguous() && land.dim() == 3,
+              "p2p_slot_reduce: land must be contiguous bf16 [S, n, D]");
+  TORCH_CHECK(out.is_contiguous() && out.scalar_type() == at::kBFloat16 && out.numel() == land.size(1) * land.size(2),
+              "p2p_slot_reduce: out must be contiguous bf16 [n, D]");
+  const int64_t n_el = out.numel();
+  TORCH_CHECK(n_el % 8 == 0, "p2p_slot_reduce: n * D must be a multiple of 8");
+  if (sumsq) TORCH_CHECK(sumsq->scalar_type() == at::kFloat && sumsq->is_cuda(), "p2p_slot_reduce: sumsq");
+  if (n_el == 0) return;
+  const at::cuda::CUDAGuard guard(land.device());
+  const int64_t nvec = n_el / 8;
+  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>((nvec + p2p::AR_THREADS - 1) / p2p::AR_THREADS,
+                                                              int64_t(p2p_sm_count()) * 8));
+  p2p::slot_reduce_kernel<<<dim3(grid), dim3(p2p::AR_THREADS), 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(land.data_ptr()), int(land.size(0)), nvec, float(scale),
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), sumsq ? sumsq->data_ptr<float>() : nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -926,7 +926,20 @@ struct LatentRowsArgs {
   int N, D, nslices;
   int j0, j1;      // latent range of this launch
   int zero_empty;  // write zero gradient rows for latents without a live pair (dense consumers)
+  // Reduce-scatter destination (sharded data parallel): with rs_n > 0 the gradient rows of
+  // latent j go to the slab of its owner o = j / rs_n, into slot [this rank][j - o * rs_n] of the
+  // [S, rs_n, D] areas at rs_dec_off / rs_enc_off, instead of gW_dec / gW_enc.
+  p2p::Peers P;
+  int64_t rs_dec_off, rs_enc_off;
+  int rs_n;
 };
+
+__device__ __forceinline__ __nv_bfloat16* grad_row(const LatentRowsArgs& a, __nv_bfloat16* local, int64_t off,
+                                                   int j) {
+  if (a.rs_n == 0) return local + int64_t(j) * a.D;
+  const int o = j / a.rs_n;
+  return p2p::at<__nv_bfloat16>(a.P, o, off) + (int64_t(a.P.rank) * a.rs_n + (j - o * a.rs_n)) * a.D;
+}
 
 template <int VPL>
 __global__ void __launch_bounds__(LR_THREADS, 2) latent_rows_kernel(const __grid_constant__ LatentRowsArgs a) {
@@ -965,8 +978,8 @@ __global__ void __launch_bounds__(LR_THREADS, 2) latent_rows_kernel(const __grid
         for (int u = 0; u < VPL; ++u) {
           const int vi = vbase + 32 * u;
           if (vi < nvec) {
-            reinterpret_cast<uint4*>(a.gW_dec + int64_t(j) * a.D)[vi] = make_uint4(0, 0, 0, 0);
-            reinterpret_cast<uint4*>(a.gW_enc + int64_t(j) * a.D)[vi] = make_uint4(0, 0, 0, 0);
+            reinterpret_cast<uint4*>(grad_row(a, a.gW_dec, a.rs_dec_off, j))[vi] = make_uint4(0, 0, 0, 0);
+            reinterpret_cast<uint4*>(grad_row(a, a.gW_enc, a.rs_enc_off, j))[vi] = make_uint4(0, 0, 0, 0);
           }
         }
       }
@@ -1027,8 +1040,8 @@ __global__ void __launch_bounds__(LR_THREADS, 2) latent_rows_kernel(const __grid
       if (vi < nvec) {
         const uint4 qd = f32_to_bf16x8(gd[u]);
         const uint4 qe = f32_to_bf16x8(ge[u]);
-        reinterpret_cast<uint4*>(a.gW_dec + int64_t(j) * a.D)[vi] = qd;
-        reinterpret_cast<uint4*>(a.gW_enc + int64_t(j) * a.D)[vi] = qe;
+        reinterpret_cast<uint4*>(grad_row(a, a.gW_dec, a.rs_dec_off, j))[vi] = qd;
+        reinterpret_cast<uint4*>(grad_row(a, a.gW_enc, a.rs_enc_off, j))[vi] = qe;
         float rd[8], re[8];
         bf16x8_to_f32(qd, rd);
         bf16x8_to_f32(qe, re);
@@ -1056,6 +1069,9 @@ __global__ void __launch_bounds__(LR_THREADS, 2) latent_rows_kernel(const __grid
       d4[1] = make_float4(bt[u][4], bt[u][5], bt[u][6], bt[u][7]);
     }
   }
+  // peer rows: this thread's stores are performed system-wide before the kernel ends, so a
+  // release published by a later launch on this stream orders after them
+  if (a.rs_n) __threadfence_system();
   const float tot = block_sum(sq, red);
   if (threadIdx.x == 0 && a.sumsq) atomicAdd(a.sumsq, tot);
 }
@@ -1259,13 +1275,15 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
                  const c10::optional<torch::Tensor>& since_fired, const torch::Tensor& idx,
                  const c10::optional<torch::Tensor>& aux_idx, int64_t j0, int64_t j1, bool zero_empty,
                  const c10::optional<torch::Tensor>& jr_thr, const c10::optional<torch::Tensor>& jr_pre,
-                 double jr_bandwidth, double jr_l0c, const c10::optional<torch::Tensor>& jr_gthr) {
+                 double jr_bandwidth, double jr_l0c, const c10::optional<torch::Tensor>& jr_gthr,
+                 const std::vector<int64_t>& rs_bases, int64_t rs_rank, int64_t rs_dec_off, int64_t rs_enc_off,
+                 int64_t rs_n) {
   static const bool v1 = [] {
     const char* e = std::getenv("SAELENS_B200_LATENT_GRAD");
     return e && std::string(e) == "v1";
   }();
   if (j1 < 0) j1 = W_dec.size(0);
-  if (v1 && j0 == 0 && j1 == W_dec.size(0) && !zero_empty && !jr_thr) {
+  if (v1 && j0 == 0 && j1 == W_dec.size(0) && !zero_empty && !jr_thr && rs_n == 0) {
     latent_grad_v1(colptr, pairs, vals, aux_vals, inv_scale, dxhat, daux, x, b_dec, W_dec, W_enc, gW_dec, gW_enc,
                    gb_enc, bterm, sumsq, fire_counts, act_freq, since_fired);
     return;
@@ -1366,6 +1384,14 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
   a.j0 = int(j0);
   a.j1 = int(j1);
   a.zero_empty = zero_empty ? 1 : 0;
+  if (rs_n > 0) {
+    TORCH_CHECK(zero_empty && int64_t(rs_bases.size()) * rs_n == N && rs_dec_off % 16 == 0 && rs_enc_off % 16 == 0,
+                "latent_grad: reduce-scatter destination needs zero_empty, S * rs_n == N and aligned offsets");
+    a.P = p2p::make_peers(rs_bases, rs_rank);
+    a.rs_dec_off = rs_dec_off;
+    a.rs_enc_off = rs_enc_off;
+    a.rs_n = int(rs_n);
+  }
   switch (vpl) {
     case 1: sparse::latent_rows_kernel<1><<<dim3(grid), dim3(sparse::LR_THREADS), 0, stream>>>(a); break;
     case 2: sparse::latent_rows_kernel<2><<<dim3(grid), dim3(sparse::LR_THREADS), 0, stream>>>(a); break;

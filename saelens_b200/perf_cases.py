@@ -202,9 +202,15 @@ def ddp(args: argparse.Namespace) -> None:
 
     world, rank, local = _init_dist()
     torch.manual_seed(1234)
-    sae = TopKTrainingSAE(TopKTrainingSAEConfig(d_in=4096, d_sae=args.d_sae, k=args.k, device=f"cuda:{local}"))
-    eng = DDPTopKEngine(sae, lr=5e-5, group=dist.group.WORLD, segments=args.segments)
-    s = BenchSetup(d_in=4096, d_sae=args.d_sae, k=args.k, batch=args.batch, world=1, rank=rank)
+    d_in = getattr(args, "d_in", 4096)
+    sae = TopKTrainingSAE(TopKTrainingSAEConfig(d_in=d_in, d_sae=args.d_sae, k=args.k, device=f"cuda:{local}"))
+    if getattr(args, "engine", "ddp") == "fsdp":
+        from saelens_b200.parallel.fsdp_engine import FSDPTopKEngine
+
+        eng = FSDPTopKEngine(sae, lr=5e-5, group=dist.group.WORLD)
+    else:
+        eng = DDPTopKEngine(sae, lr=5e-5, group=dist.group.WORLD, segments=args.segments)
+    s = BenchSetup(d_in=d_in, d_sae=args.d_sae, k=args.k, batch=args.batch, world=1, rank=rank)
     xs = [synthetic_batch(s, 10 * i + rank, device="cuda") for i in range(2)]
     for i in range(3):
         eng.step(xs[i % 2])
@@ -222,7 +228,8 @@ def ddp(args: argparse.Namespace) -> None:
     t = eng.phase_times_ms()
     eng.status.check()
     if rank == 0:
-        print(json.dumps({"world": world, "d_sae": args.d_sae, "k": args.k, "batch_per_gpu": args.batch,
+        print(json.dumps({"engine": getattr(args, "engine", "ddp"), "world": world, "d_in": d_in,
+                          "d_sae": args.d_sae, "k": args.k, "batch_per_gpu": args.batch,
                           "ms_per_step": round(float(ms.item()), 3),
                           "tokens_per_s": round(args.batch * world * 1000.0 / float(ms.item()), 1),
                           "phases_ms": {k: round(v / args.steps, 3) for k, v in t.items()}}), flush=True)
@@ -383,11 +390,19 @@ def main() -> None:
     c = sub.add_parser("gemm")
     c.add_argument("--pair", type=int, choices=[0, 1], default=1)
     d = sub.add_parser("ddp")
+    d.add_argument("--d-in", type=int, default=4096)
     d.add_argument("--d-sae", type=int, default=131072)
     d.add_argument("--k", type=int, default=64)
     d.add_argument("--batch", type=int, default=8192)
     d.add_argument("--steps", type=int, default=10)
     d.add_argument("--segments", type=int, default=4)
+    fs = sub.add_parser("fsdp", help="sharded data parallel engine (latent-sharded optimizer state)")
+    fs.add_argument("--d-in", type=int, default=3584)
+    fs.add_argument("--d-sae", type=int, default=131072)
+    fs.add_argument("--k", type=int, default=64)
+    fs.add_argument("--batch", type=int, default=4096)
+    fs.add_argument("--steps", type=int, default=10)
+    fs.set_defaults(engine="fsdp", segments=1)
     td = sub.add_parser("tpdp")
     td.add_argument("--tp", type=int, default=4)
     td.add_argument("--arch", choices=["topk", "batchtopk"], default="batchtopk")
@@ -402,7 +417,7 @@ def main() -> None:
     rt.add_argument("--d", type=int, default=4096)
     args = p.parse_args()
     {"phases": phases, "fused-case": fused_case, "gemm": gemm, "ddp": ddp, "allreduce": allreduce, "router": router,
-     "tpdp": tpdp}[args.cmd](args)
+     "tpdp": tpdp, "fsdp": ddp}[args.cmd](args)
 
 
 if __name__ == "__main__":

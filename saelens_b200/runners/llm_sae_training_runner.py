@@ -26,7 +26,12 @@ import torch.distributed as dist
 
 from saelens_b200 import logger
 from saelens_b200.config import LanguageModelSAERunnerConfig, LoggingConfig
-from saelens_b200.constants import ACTIVATIONS_STORE_STATE_FILENAME, RUNNER_CFG_FILENAME, SPARSITY_FILENAME
+from saelens_b200.constants import (
+    ACTIVATIONS_STORE_STATE_FILENAME,
+    RUNNER_CFG_FILENAME,
+    SAE_WEIGHTS_FILENAME,
+    SPARSITY_FILENAME,
+)
 from saelens_b200.models.sae import TrainingSAE, TrainingSAEConfig
 from saelens_b200.registry import get_sae_training_class
 from saelens_b200.training.activations_store import ActivationsStore
@@ -59,6 +64,8 @@ class LanguageModelSAETrainingRunner:
         self.token_count_weighted_dp = token_count_weighted_dp
         self.tp_group: dist.ProcessGroup | None = None
         self.dp_group: dist.ProcessGroup | None = None
+        self.ddp_hook_state: Any = None  # P2P gradient all-reduce of the DDP wrapper, when used
+        self.native_fsdp = False  # sae_dp_mode="fsdp" on the native sharded engine
         self._init_distributed()
         self.model = override_model if override_model is not None else self._load_model()
         shard, nshard = (self._dp_rank(), self.sae_dp_size) if self.sae_dp_size > 1 else (0, 1)
@@ -107,6 +114,17 @@ class LanguageModelSAETrainingRunner:
             sae = get_sae_training_class(sae_cfg.architecture())[0](sae_cfg)
         return sae
 
+    def _native_fsdp_ok(self, sae: TrainingSAE[Any]) -> bool:
+        """TopK / BatchTopK on CUDA with the native ops, at most 8 NCCL ranks (one NVSwitch
+        domain), d_sae divisible into 256-latent tiles per rank."""
+        if self.cfg.sae_engine == "torch" or not sae.W_dec.is_cuda:
+            return False
+        from saelens_b200.training.engine import engine_supported
+
+        world = dist.get_world_size(self.dp_group)
+        return (engine_supported(sae) and 1 < world <= 8 and dist.get_backend(self.dp_group) == "nccl"
+                and sae.W_dec.shape[0] % (256 * world) == 0)
+
     def _wrap_dp(self, sae: TrainingSAE[Any]) -> Any:
         if self.dp_group is None or self.cfg.sae_dp_mode == "manual":
             return sae
@@ -121,9 +139,18 @@ class LanguageModelSAETrainingRunner:
                     kw[k] = v
             if sae.W_dec.is_cuda:
                 kw["device_ids"] = [sae.W_dec.device.index]
-            return DDP(sae, **kw)
+            ddp = DDP(sae, **kw)
+            if getattr(self.cfg, "ddp_exchange", "p2p") == "p2p":
+                from saelens_b200.parallel.p2p_ddp_hook import p2p_hook_supported, register_p2p_allreduce
+
+                if p2p_hook_supported(sae, self.dp_group):
+                    self.ddp_hook_state = register_p2p_allreduce(ddp, sae, self.dp_group, kw.get("bucket_cap_mb"))
+            return ddp
         if self.tp_group is not None:
             raise ValueError("sae_dp_mode='fsdp' cannot be combined with sae_tp_size > 1")
+        if self._native_fsdp_ok(sae):
+            self.native_fsdp = True  # the trainer's FSDPTopKEngine shards the module itself
+            return sae
         from torch.distributed.fsdp import FullyShardedDataParallel as FSDP
         from torch.distributed.fsdp import ShardingStrategy
 
@@ -141,13 +168,23 @@ class LanguageModelSAETrainingRunner:
         trainer = SAETrainer(
             cfg=cfg.to_sae_trainer_config(), sae=self.wrapped, base_sae=self.sae, data_provider=self.activations_store,
             evaluator=self._evaluator(), save_checkpoint_fn=self._save_checkpoint_extras, dp_group=self.dp_group,
-            token_count_weighted_dp=self.token_count_weighted_dp,
+            token_count_weighted_dp=self.token_count_weighted_dp, native_fsdp=self.native_fsdp,
         )
         self.trainer = trainer
         if self.resume_from_checkpoint is not None:
             ck = Path(self.resume_from_checkpoint)
-            self.sae.load_weights_from_checkpoint(ck)
-            if trainer.engine is not None:
+            if self.native_fsdp:
+                # the module holds one latent shard: the engine takes its part of the full weights
+                from safetensors.torch import load_file
+
+                sd = load_file(ck / SAE_WEIGHTS_FILENAME)
+                self.sae.process_state_dict_for_loading(sd)
+                trainer.engine.load_weights(sd["W_enc"], sd["W_dec"], sd["b_enc"], sd["b_dec"])
+                if "topk_threshold" in sd and hasattr(self.sae, "topk_threshold"):
+                    self.sae.topk_threshold.copy_(sd["topk_threshold"])
+            else:
+                self.sae.load_weights_from_checkpoint(ck)
+            if trainer.engine is not None and not self.native_fsdp:
                 trainer.engine.refresh()
             trainer.load_trainer_state(ck)
             if (ck / ACTIVATIONS_STORE_STATE_FILENAME).exists():
@@ -156,6 +193,8 @@ class LanguageModelSAETrainingRunner:
         old_term = signal.signal(signal.SIGTERM, _interrupt)
         try:
             sae = trainer.fit()
+            if self.ddp_hook_state is not None:
+                self.ddp_hook_state.check()
         except (KeyboardInterrupt, InterruptedException):
             logger.warning("interrupted: saving a checkpoint before exiting")
             trainer.save_checkpoint(checkpoint_name=f"interrupted_{trainer.n_training_samples}")

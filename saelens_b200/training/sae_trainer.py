@@ -15,6 +15,7 @@ from __future__ import annotations
 
 import contextlib
 import json
+import logging
 import math
 import os
 import time
@@ -46,9 +47,12 @@ from saelens_b200.training.optim import CoefficientScheduler, LRSchedule, get_lr
 from saelens_b200.utils import wandb_shim as wandb
 from saelens_b200.utils.misc import path_or_tmp_dir
 
+logger = logging.getLogger(__name__)
+
 T_TRAINING_SAE = TypeVar("T_TRAINING_SAE", bound=TrainingSAE[Any])
 DataProvider = Iterator[torch.Tensor]
 FSDP_OPTIMIZER_STATE_FORMAT = "fsdp_sharded"
+NATIVE_FSDP_OPTIMIZER_STATE_FORMAT = "native_fsdp_latent_sharded"
 
 
 class SaveCheckpointFn(Protocol):
@@ -88,7 +92,7 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
                  evaluator: Evaluator | None = None, save_checkpoint_fn: SaveCheckpointFn | None = None,
                  dp_group: dist.ProcessGroup | None = None, token_count_weighted_dp: bool = False,
                  base_sae: Any = None, append_logs: bool = False,
-                 tp_input_layout: str = "replicated") -> None:
+                 tp_input_layout: str = "replicated", native_fsdp: bool = False) -> None:
         self.sae = sae
         # "replicated": every TP rank receives the same full batch (reference semantics);
         # "row_sharded": each TP rank receives its 1/tp slice of the batch rows.
@@ -96,6 +100,10 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
         self._base_sae = base_sae if base_sae is not None else sae
         self._is_fsdp = _is_fsdp(sae)
         self._is_ddp = _is_ddp(sae)
+        # sharded data parallel on the native engine (latent-sharded optimizer state, fused
+        # parameter all-gather / gradient reduce-scatter); the module is not wrapped
+        self._native_fsdp = bool(native_fsdp)
+        self._warned_fsdp_evals = False
         self.data_provider = data_provider
         self.evaluator = evaluator
         self.activation_scaler = ActivationScaler()
@@ -148,7 +156,13 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
         self.engine: Any = None
         want = getattr(cfg, "sae_engine", "auto")
         self._engine_stats_global = False  # engine firing statistics already cover every DP rank
-        if want != "torch" and not self._is_fsdp and (dp_group is not None or self._is_ddp):
+        if self._native_fsdp:
+            from saelens_b200.parallel.fsdp_engine import FSDPTopKEngine
+
+            self.engine = FSDPTopKEngine(self._base_sae, lr=cfg.lr, group=dp_group, beta1=cfg.adam_beta1,
+                                         beta2=cfg.adam_beta2)
+            self._engine_stats_global = True
+        elif want != "torch" and not self._is_fsdp and (dp_group is not None or self._is_ddp):
             from saelens_b200.training.engine import engine_supported
 
             group = dp_group if dp_group is not None else getattr(sae, "process_group", None) or dist.group.WORLD
@@ -226,7 +240,7 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
 
     @property
     def sae_dp_mode(self) -> str:
-        return "fsdp" if self._is_fsdp else ("ddp" if self._is_ddp else "manual")
+        return "fsdp" if (self._is_fsdp or self._native_fsdp) else ("ddp" if self._is_ddp else "manual")
 
     @property
     def log_feature_sparsity(self) -> torch.Tensor:
@@ -319,6 +333,8 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
             self.activation_scaler.scaling_factor = None
         if self.cfg.save_final_checkpoint:
             self.save_checkpoint(checkpoint_name=f"final_{self.n_training_samples}")
+        if self._native_fsdp:
+            self.engine.restore_full_module()
         return self._base_sae
 
     # ------------------------------------------------------------------ one step
@@ -460,7 +476,7 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
         tp_group = getattr(self._base_sae, "_tp_group", None)
         tp_rank = dist.get_rank(tp_group) if tp_group is not None else 0
         dp_rank = dist.get_rank(self.dp_group) if self.dp_group is not None else 0
-        if dp_rank != 0 and not self._is_fsdp:
+        if dp_rank != 0 and not (self._is_fsdp or self._native_fsdp):
             return
         ckpt: Path | None = None
         if self.cfg.checkpoint_path is not None or self.cfg.logger.log_to_wandb:
@@ -478,6 +494,17 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
             self.save_checkpoint_fn(checkpoint_path=ckpt)
 
     def _save_model(self, path: Path) -> tuple[Path, Path]:
+        if self._native_fsdp:
+            full = self.engine.full_weights()  # collective
+            sd = {k: v.detach().cpu() for k, v in self._base_sae.state_dict().items()}
+            sd.update({k: v.detach().cpu() for k, v in full.items()})
+            self._base_sae.process_state_dict_for_saving(sd)
+            wpath, cpath = path / SAE_WEIGHTS_FILENAME, path / SAE_CFG_FILENAME
+            if dist.get_rank(self.dp_group) == 0:
+                save_file({k: v.contiguous() for k, v in sd.items()}, wpath)
+                with open(cpath, "w") as f:
+                    json.dump(self._base_sae.cfg.to_dict(), f)
+            return wpath, cpath
         if not self._is_fsdp:
             return self._base_sae.save_model(str(path))
         from torch.distributed.fsdp import FullStateDictConfig, StateDictType
@@ -506,12 +533,19 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
         tp_rank = dist.get_rank(tp_group) if tp_group is not None else 0
         dp_rank = dist.get_rank(self.dp_group) if self.dp_group is not None else 0
         dp_size = dist.get_world_size(self.dp_group) if self.dp_group is not None else 1
-        if self._is_fsdp:
+        if self._native_fsdp:
+            shard = {n: {k: (v.detach().cpu() if torch.is_tensor(v) else v) for k, v in s.items()}
+                     for n, s in self.engine.optimizer_state().items()}
+            torch.save(shard, self._fsdp_optimizer_state_path(checkpoint_path))
+            if dp_rank != 0:
+                return
+            opt_state: dict[str, Any] = {"optimizer_state_format": NATIVE_FSDP_OPTIMIZER_STATE_FORMAT,
+                                         "fsdp_dp_size": dp_size}
+        elif self._is_fsdp:
             self._save_fsdp_optimizer_state(checkpoint_path)
             if dp_rank != 0 or tp_rank != 0:
                 return
-            opt_state: dict[str, Any] = {"optimizer_state_format": FSDP_OPTIMIZER_STATE_FORMAT,
-                                         "fsdp_dp_size": dp_size}
+            opt_state = {"optimizer_state_format": FSDP_OPTIMIZER_STATE_FORMAT, "fsdp_dp_size": dp_size}
         else:
             by_name = self._build_named_optimizer_state_for_save()
             if tp_rank != 0:
@@ -546,7 +580,20 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
                     f"Cannot resume: checkpoint was saved with sae_dp_mode='{saved}' but current mode is "
                     f"'{self.sae_dp_mode}'. Cross-mode optimizer resume is not supported."
                 )
-            if self._is_fsdp:
+            if self._native_fsdp:
+                if st.get("optimizer_state_format") != NATIVE_FSDP_OPTIMIZER_STATE_FORMAT:
+                    raise ValueError("Cannot resume: checkpoint was not written by the native sharded engine "
+                                     f"(optimizer_state_format='{st.get('optimizer_state_format')}').")
+                cur = dist.get_world_size(self.dp_group) if self.dp_group is not None else 1
+                if st.get("fsdp_dp_size") != cur:
+                    raise ValueError(
+                        "Cannot resume FSDP checkpoint with a different sae_dp_size: checkpoint has "
+                        f"{st.get('fsdp_dp_size')}, current run has {cur}."
+                    )
+                shard = torch.load(self._fsdp_optimizer_state_path(checkpoint_path), map_location="cpu",
+                                   weights_only=False)
+                self.engine.load_optimizer_state(shard)
+            elif self._is_fsdp:
                 if st.get("optimizer_state_format") != FSDP_OPTIMIZER_STATE_FORMAT:
                     raise ValueError(f"Cannot resume FSDP checkpoint: missing optimizer_state_format='{FSDP_OPTIMIZER_STATE_FORMAT}'.")
                 cur = dist.get_world_size(self.dp_group) if self.dp_group is not None else 1
@@ -730,6 +777,11 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
     def _run_and_log_evals(self) -> None:
         every = self.cfg.logger.wandb_log_frequency * self.cfg.logger.eval_every_n_wandb_logs
         if (self.n_training_steps + 1) % every != 0:
+            return
+        if self._native_fsdp:  # the module holds one latent shard until the end of training
+            if not self._warned_fsdp_evals:
+                logger.warning("evals are skipped during sharded data-parallel training on the native engine")
+                self._warned_fsdp_evals = True
             return
         self.sae.eval()
         metrics = self.evaluator(self._base_sae, self.data_provider, self.activation_scaler) if self.evaluator else {}
