@@ -96,7 +96,8 @@ void topk_exchange_merge(const torch::Tensor& vals, const torch::Tensor& idx, in
 std::vector<int64_t> p2p_allreduce_sizes(int64_t n, int64_t elem_bytes, int64_t world, int64_t chunk);
 void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64_t>& peer_bases, int64_t rank,
                    int64_t land_off, int64_t cnt_off, int64_t out_off, int64_t flag_off, int64_t epoch,
-                   const torch::Tensor& ticket, const torch::Tensor& status, int64_t sq_off, int64_t chunk);
+                   const torch::Tensor& ticket, const torch::Tensor& status, int64_t sq_off, int64_t chunk,
+                   int64_t max_ctas);
 void p2p_slot_reduce(const torch::Tensor& land, double scale, const torch::Tensor& out,
                      const c10::optional<torch::Tensor>& sumsq);
 void p2p_wait_flags(const torch::Tensor& flags, int64_t target, const torch::Tensor& status);
@@ -164,7 +165,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("chunk") = 0);
   m.def("p2p_allreduce", &sb::p2p_allreduce, py::arg("x"), py::arg("scale"), py::arg("peer_bases"),
         py::arg("rank"), py::arg("land_off"), py::arg("cnt_off"), py::arg("out_off"), py::arg("flag_off"),
-        py::arg("epoch"), py::arg("ticket"), py::arg("status"), py::arg("sq_off") = -1, py::arg("chunk") = 0);
+        py::arg("epoch"), py::arg("ticket"), py::arg("status"), py::arg("sq_off") = -1, py::arg("chunk") = 0, py::arg("max_ctas") = 0);
   m.def("p2p_wait_flags", &sb::p2p_wait_flags);
   m.def("p2p_slot_reduce", &sb::p2p_slot_reduce);
   m.def("p2p_route_rows", &sb::p2p_route_rows);

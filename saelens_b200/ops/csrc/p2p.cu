@@ -400,7 +400,8 @@ std::vector<int64_t> p2p_allreduce_sizes(int64_t n, int64_t elem_bytes, int64_t 
 // [nch] at sq_off), e.g. for the norm of an averaged gradient.
 void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64_t>& peer_bases, int64_t rank,
                    int64_t land_off, int64_t cnt_off, int64_t out_off, int64_t flag_off, int64_t epoch,
-                   const torch::Tensor& ticket, const torch::Tensor& status, int64_t sq_off, int64_t chunk) {
+                   const torch::Tensor& ticket, const torch::Tensor& status, int64_t sq_off, int64_t chunk,
+                   int64_t max_ctas) {
   const int64_t S = int64_t(peer_bases.size());
   TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "p2p_allreduce: bad group");
   TORCH_CHECK(x.is_cuda() && x.is_contiguous() &&
@@ -431,7 +432,8 @@ void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64
   a.status = status.data_ptr<int>();
   C10_CUDA_CHECK(cudaMemsetAsync(a.ticket, 0, sizeof(int), stream));
   const int64_t nch = (n + chunk - 1) / chunk;
-  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(2 * nch, int64_t(p2p_sm_count()) * 8));
+  int64_t grid = std::max<int64_t>(1, std::min<int64_t>(2 * nch, int64_t(p2p_sm_count()) * 8));
+  if (max_ctas > 0) grid = std::min(grid, max_ctas);  // leave SMs to overlapping compute
   if (x.scalar_type() == at::kFloat)
     p2p::allreduce_kernel<float><<<dim3(grid), dim3(p2p::AR_THREADS), 0, stream>>>(a);
   else if (x.scalar_type() == at::kInt)

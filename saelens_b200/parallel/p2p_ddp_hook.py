@@ -17,6 +17,7 @@ targets grow by one epoch per use of that shape.
 from __future__ import annotations
 
 import math
+import os
 from typing import Any
 
 import torch
@@ -41,7 +42,7 @@ def max_bucket_bytes(param_bytes: list[int], bucket_cap_mb: float | None) -> int
 
 class P2PAllReduceHookState:
     def __init__(self, module: torch.nn.Module, group: dist.ProcessGroup | None,
-                 bucket_cap_mb: float | None = None, counter_bytes: int = 16 << 20):
+                 bucket_cap_mb: float | None = None, counter_bytes: int = 16 << 20, max_ctas: int | None = None):
         from saelens_b200.ops import native
         from saelens_b200.ops.status import StatusWord
 
@@ -69,6 +70,11 @@ class P2PAllReduceHookState:
         self.status = StatusWord(self.device)
         self.calls = 0
         self.nccl_fallbacks = 0  # buckets larger than the reserved area (averaged by NCCL)
+        # CTAs of the all-reduce kernel: it overlaps the backward, so it may be capped to leave SMs
+        # to the compute (0 = as many as the transfer can use)
+        if max_ctas is None:
+            max_ctas = int(os.environ.get("SAELENS_B200_DDP_HOOK_CTAS", "0"))
+        self.max_ctas = max(0, int(max_ctas))
 
     def _area(self, n: int, dtype: torch.dtype) -> list[int] | None:
         key = (n, dtype)
@@ -97,7 +103,8 @@ class P2PAllReduceHookState:
             a = self._area(n, buf.dtype)
             a[2] += 1
             self.nat.p2p_allreduce(buf, 1.0 / self.world, self.heap.bases, self.rank, self.land_off, a[0],
-                                   self.out_off, a[1], a[2], self.ticket, self.status.tensor)
+                                   self.out_off, a[1], a[2], self.ticket, self.status.tensor,
+                                   max_ctas=self.max_ctas)
             buf.copy_(self.heap.local(SlabBuffer(self.out_off, (n,), buf.dtype)))
             self.calls += 1
             fut: torch.futures.Future = torch.futures.Future(devices=[self.device])

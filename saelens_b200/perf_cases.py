@@ -238,6 +238,74 @@ def ddp(args: argparse.Namespace) -> None:
     dist.destroy_process_group()
 
 
+def ddp_hook(args: argparse.Namespace) -> None:
+    """PyTorch-path SAE under torch DDP (JumpReLU by default, the FSDP JumpReLU config's shape):
+    gradient buckets averaged by the P2P all-reduce hook vs DDP's NCCL all-reduce.  Device time
+    from CUDA events over the steps, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from torch.nn.parallel import DistributedDataParallel as DDP
+
+    from saelens_b200.models.jumprelu import JumpReLUTrainingSAE, JumpReLUTrainingSAEConfig
+    from saelens_b200.models.sae import TrainStepInput
+    from saelens_b200.models.standard import StandardTrainingSAE, StandardTrainingSAEConfig
+    from saelens_b200.parallel.p2p_ddp_hook import register_p2p_allreduce
+    from saelens_b200.training.bench_driver import BenchSetup, synthetic_batch
+
+    world, rank, local = _init_dist()
+    dev = f"cuda:{local}"
+    x = synthetic_batch(BenchSetup(d_in=args.d_in, d_sae=args.d_sae, k=1, batch=args.batch, world=1, rank=rank),
+                        1 + rank, device="cuda").float()
+    res = {}
+    for mode in ("p2p", "nccl"):
+        torch.manual_seed(1234)
+        if args.arch == "jumprelu":
+            sae = JumpReLUTrainingSAE(JumpReLUTrainingSAEConfig(
+                d_in=args.d_in, d_sae=args.d_sae, jumprelu_init_threshold=0.001, jumprelu_bandwidth=0.001,
+                l0_coefficient=1.0, device=dev))
+            coef = {"l0": 1.0}
+        else:
+            sae = StandardTrainingSAE(StandardTrainingSAEConfig(d_in=args.d_in, d_sae=args.d_sae, device=dev))
+            coef = {"l1": 5.0}
+        ddp = DDP(sae, device_ids=[local])
+        state = register_p2p_allreduce(ddp, sae, dist.group.WORLD) if mode == "p2p" else None
+        opt = torch.optim.Adam(sae.parameters(), lr=5e-5)
+
+        def step(i: int) -> None:
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                out = ddp(TrainStepInput(sae_in=x, coefficients=coef, dead_neuron_mask=None, n_training_steps=i))
+            out.loss.backward()
+            opt.step()
+            opt.zero_grad(set_to_none=False)
+
+        for i in range(3):
+            step(i)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.steps):
+            step(i)
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / args.steps], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res[mode] = round(float(t.item()), 3)
+        if state is not None:
+            state.check()
+            res["p2p_nccl_fallbacks"] = state.nccl_fallbacks
+            state.close()
+        del ddp, opt, sae
+        torch.cuda.empty_cache()
+    if rank == 0:
+        print(json.dumps({"world": world, "arch": args.arch, "d_in": args.d_in, "d_sae": args.d_sae,
+                          "batch_per_gpu": args.batch, "ms_per_step": res,
+                          "tokens_per_s": {m: round(args.batch * world / res[m] * 1e3, 1) for m in ("p2p", "nccl")},
+                          "precision": "fp32 params, bf16 autocast"}), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def allreduce(args: argparse.Namespace) -> None:
     import torch
     import torch.distributed as dist
@@ -411,13 +479,19 @@ def main() -> None:
     td.add_argument("--k", type=int, default=64)
     td.add_argument("--batch", type=int, default=8192, help="rows per step and data-parallel replica")
     td.add_argument("--steps", type=int, default=10)
+    dh = sub.add_parser("ddp-hook", help="PyTorch-path SAE under DDP: P2P all-reduce hook vs NCCL")
+    dh.add_argument("--arch", choices=["jumprelu", "standard"], default="jumprelu")
+    dh.add_argument("--d-in", type=int, default=3584)
+    dh.add_argument("--d-sae", type=int, default=131072)
+    dh.add_argument("--batch", type=int, default=4096)
+    dh.add_argument("--steps", type=int, default=10)
     sub.add_parser("allreduce")
     rt = sub.add_parser("router")
     rt.add_argument("--rows", type=int, default=8192)
     rt.add_argument("--d", type=int, default=4096)
     args = p.parse_args()
     {"phases": phases, "fused-case": fused_case, "gemm": gemm, "ddp": ddp, "allreduce": allreduce, "router": router,
-     "tpdp": tpdp, "fsdp": ddp}[args.cmd](args)
+     "tpdp": tpdp, "fsdp": ddp, "ddp-hook": ddp_hook}[args.cmd](args)
 
 
 if __name__ == "__main__":

@@ -492,6 +492,8 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
                     self.cfg.logger.log(self, wpath, cpath, sparsity_path=spath, wandb_aliases=wandb_aliases)
         if self.save_checkpoint_fn is not None and tp_rank == 0:
             self.save_checkpoint_fn(checkpoint_path=ckpt)
+        if self._native_fsdp and self.dp_group is not None:
+            dist.barrier(group=self.dp_group)  # every rank's shard and rank 0's files are written
 
     def _save_model(self, path: Path) -> tuple[Path, Path]:
         if self._native_fsdp:

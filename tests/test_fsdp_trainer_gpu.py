@@ -58,6 +58,7 @@ def _worker(rank, world, port, out_dir):
     assert isinstance(tr.engine, FSDPTopKEngine) and tr.sae_dp_mode == "fsdp"
     out = tr.fit()
     assert out.W_dec.shape == (1024, 128) and out.W_enc.shape == (128, 1024)
+    dist.barrier()
     final = sorted(p for p in os.listdir(ckpt) if p.startswith("final_"))[-1]
     state = torch.load(os.path.join(ckpt, final, "trainer_state.pt"), weights_only=False)
     # resume into a fresh sharded trainer
