@@ -207,6 +207,11 @@ class LanguageModelSAERunnerConfig(Generic[T_TRAINING_SAE_CONFIG]):
     streaming_buffer_name: str = ""
     streaming_shuffle: bool = True
     streaming_random_chunks: bool = True
+    # Transport of streaming mode (no counterpart in the reference): "device" = ring in the
+    # consumer GPU's memory written over NVLink, "host" = the /dev/shm ring, "auto" = device when
+    # on CUDA with SAE TP 1 and one hook.
+    streaming_transport: Literal["auto", "device", "host"] = "auto"
+    streaming_buffer_dir: str = "/dev/shm"
 
     # B200 engine knobs (no counterpart in the reference): use the fused native TopK-family
     # training step on CUDA when available ("auto"), always ("native") or never ("torch").

@@ -97,9 +97,18 @@ std::vector<int64_t> p2p_allreduce_sizes(int64_t n, int64_t elem_bytes, int64_t 
 void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64_t>& peer_bases, int64_t rank,
                    int64_t land_off, int64_t cnt_off, int64_t out_off, int64_t flag_off, int64_t epoch,
                    const torch::Tensor& ticket, const torch::Tensor& status, int64_t sq_off, int64_t chunk,
-                   int64_t max_ctas);
+                   int64_t max_ctas, const c10::optional<torch::Tensor>& x_out);
 void p2p_slot_reduce(const torch::Tensor& land, double scale, const torch::Tensor& out,
                      const c10::optional<torch::Tensor>& sumsq);
+void ring_claim(const std::vector<int64_t>& peer_bases, int64_t rank, int64_t owner, int64_t state_off,
+                int64_t n_slots, int64_t from, int64_t to, int64_t start, double timeout_ms, const torch::Tensor& slot);
+void ring_write(const torch::Tensor& src, const std::vector<int64_t>& peer_bases, int64_t rank, int64_t owner,
+                int64_t data_off, int64_t chunk_rows, const torch::Tensor& slot, int64_t mode, double scale);
+void ring_publish(const std::vector<int64_t>& peer_bases, int64_t rank, int64_t owner, int64_t state_off,
+                  int64_t meta_off, const torch::Tensor& slot, int64_t rows, int64_t producer, int64_t seq,
+                  int64_t value);
+void ring_gather(const torch::Tensor& data, const torch::Tensor& slot, const c10::optional<torch::Tensor>& perm,
+                 const torch::Tensor& out);
 void p2p_wait_flags(const torch::Tensor& flags, int64_t target, const torch::Tensor& status);
 std::tuple<int64_t, torch::Tensor> symm_alloc(int64_t nbytes);
 int64_t symm_open(const torch::Tensor& handle);
@@ -165,9 +174,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("chunk") = 0);
   m.def("p2p_allreduce", &sb::p2p_allreduce, py::arg("x"), py::arg("scale"), py::arg("peer_bases"),
         py::arg("rank"), py::arg("land_off"), py::arg("cnt_off"), py::arg("out_off"), py::arg("flag_off"),
-        py::arg("epoch"), py::arg("ticket"), py::arg("status"), py::arg("sq_off") = -1, py::arg("chunk") = 0, py::arg("max_ctas") = 0);
+        py::arg("epoch"), py::arg("ticket"), py::arg("status"), py::arg("sq_off") = -1, py::arg("chunk") = 0, py::arg("max_ctas") = 0, py::arg("x_out") = py::none());
   m.def("p2p_wait_flags", &sb::p2p_wait_flags);
   m.def("p2p_slot_reduce", &sb::p2p_slot_reduce);
+  m.def("ring_claim", &sb::ring_claim);
+  m.def("ring_write", &sb::ring_write);
+  m.def("ring_publish", &sb::ring_publish);
+  m.def("ring_gather", &sb::ring_gather);
   m.def("p2p_route_rows", &sb::p2p_route_rows);
   m.def("p2p_wait_targets", &sb::p2p_wait_targets);
   m.def("p2p_signal", &sb::p2p_signal);

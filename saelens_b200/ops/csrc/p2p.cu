@@ -8,7 +8,10 @@
 //            fused scale (e.g. 1/world for a gradient mean), rounds to the element type and stores
 //            the result into every rank's `out` area, publishing one epoch flag per chunk;
 //   phase C  after the work counter ran dry, each CTA waits for the flags of a share of the
-//            chunks, so the whole result is in local memory when the kernel ends.
+//            chunks, so the whole result is in local memory when the kernel ends; with an
+//            output tensor (`x_out`, may be `x` itself) each arrived chunk is also copied there.
+//            In place is safe: a chunk's flag comes from its owner after all S arrivals, so this
+//            rank's phase A has finished reading that chunk of `x`.
 // Work items come from one counter (phase A items first), so no wait depends on a CTA that is
 // not running.  NVLink bytes per rank: 2 (S-1)/S n elements, the bandwidth-optimal amount.
 // Replaces the gradient / statistics all-reduces of the reference's DDP and TP paths
@@ -74,6 +77,7 @@ struct ArArgs {
   int64_t flag_off;  // u32 [nch]
   int64_t sq_off;    // fp32 [nch]: per-chunk sum of squares of the result, on every rank (< 0: none)
   int64_t chunk;     // elements per chunk
+  void* x_out;       // optional local copy of the result [n] (may alias x)
   uint32_t epoch;
   int* ticket;
   int* status;
@@ -174,8 +178,29 @@ __global__ void __launch_bounds__(AR_THREADS) allreduce_kernel(const __grid_cons
     }
   }
   // phase C: the result of every chunk is local before the kernel ends
-  for (int64_t c = int64_t(blockIdx.x) * AR_THREADS + t; c < nch; c += int64_t(gridDim.x) * AR_THREADS)
-    wait_geq_sys(at<uint32_t>(a.P, r, a.flag_off) + c, a.epoch, a.status, kTimeoutPeerFlag);
+  if (a.x_out == nullptr) {
+    for (int64_t c = int64_t(blockIdx.x) * AR_THREADS + t; c < nch; c += int64_t(gridDim.x) * AR_THREADS)
+      wait_geq_sys(at<uint32_t>(a.P, r, a.flag_off) + c, a.epoch, a.status, kTimeoutPeerFlag);
+    return;
+  }
+  const T* res = at<T>(a.P, r, a.out_off);
+  T* xo = reinterpret_cast<T*>(a.x_out);
+  for (int64_t c = blockIdx.x; c < nch; c += gridDim.x) {
+    __syncthreads();
+    if (t == 0)
+      s_ok = wait_geq_sys(at<uint32_t>(a.P, r, a.flag_off) + c, a.epoch, a.status, kTimeoutPeerFlag) ? 1 : 0;
+    __syncthreads();
+    if (!s_ok) return;
+    const int64_t e0 = c * CH;
+    const int64_t len = min(CH, a.n - e0);
+    if (len == CH && (reinterpret_cast<uintptr_t>(xo + e0) & 15) == 0) {
+      constexpr int V = 16 / sizeof(T);
+      for (int v = t; v < CH / V; v += AR_THREADS)
+        reinterpret_cast<uint4*>(xo + e0)[v] = __ldcg(reinterpret_cast<const uint4*>(res + e0) + v);
+    } else {
+      for (int64_t e = t; e < len; e += AR_THREADS) xo[e0 + e] = res[e0 + e];
+    }
+  }
 }
 
 // Owner side of the gradient reduce-scatter of sharded data parallel: every rank stored its
@@ -218,6 +243,128 @@ __global__ void slot_reduce_kernel(const __nv_bfloat16* __restrict__ land, int S
     float t = 0.f;
     for (int i = 0; i < AR_THREADS / 32; ++i) t += s_red[i];
     atomicAdd(sumsq, t);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Device activation ring (streaming between disjoint producer and consumer GPUs).  N chunk slots
+// of [chunk_rows, D] bf16 live in the consumer's slab with one state word per slot (FREE ->
+// WRITING -> READY -> CONSUMING -> FREE, the state machine of the reference's /dev/shm ring,
+// sae_lens/training/shared_activation_buffer.py:36-41 and 151-296) and meta [N][4] (rows,
+// producer, sequence, 0).  Claims are system-scope compare-and-swaps on the state words (over
+// NVLink for producers); the rows travel as P2P stores from the producer GPU, normalised and
+// cast to bf16 in the same kernel; READY / FREE are published with release stores.
+// ---------------------------------------------------------------------------------------
+__global__ void ring_claim_kernel(Peers P, int owner, int64_t state_off, int n_slots, uint32_t from, uint32_t to,
+                                  int start, long long timeout_ns, int* out_slot) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  uint32_t* st = at<uint32_t>(P, owner, state_off);
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    for (int i = 0; i < n_slots; ++i) {
+      const int sidx = (start + i) % n_slots;
+      if (atomicCAS_system(st + sidx, from, to) == from) {
+        __threadfence_system();  // later reads of the slot are ordered after the claim
+        *out_slot = sidx;
+        return;
+      }
+    }
+    if ((long long)(globaltimer_ns() - t0) > timeout_ns) {
+      *out_slot = -1;
+      return;
+    }
+    __nanosleep(1000);
+  }
+}
+
+// One warp per row: sum of squares (mode 2), then scale, bf16 cast and 16-byte P2P stores.
+__global__ void ring_write_kernel(const void* __restrict__ src, int64_t ld_src, int src_f32, int rows, int D,
+                                  int mode, float scale, Peers P, int owner, int64_t data_off, int chunk_rows,
+                                  const int* __restrict__ slot_ptr) {
+  const int slot = *slot_ptr;
+  if (slot < 0) return;
+  __nv_bfloat16* dst = at<__nv_bfloat16>(P, owner, data_off) + int64_t(slot) * chunk_rows * D;
+  const int lane = threadIdx.x & 31;
+  const int nvec = D >> 3;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  auto load8 = [&](int64_t row, int v, float* f) {
+    if (src_f32) {
+      const float4* s4 = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + row * ld_src) + 2 * v;
+      const float4 a = __ldg(s4), b = __ldg(s4 + 1);
+      f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    } else {
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(src) + row * ld_src) + v);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&q);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 t = __bfloat1622float2(h[e]);
+        f[2 * e] = t.x;
+        f[2 * e + 1] = t.y;
+      }
+    }
+  };
+  for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows; row += warps) {
+    float mul = mode == 1 ? scale : 1.f;
+    if (mode == 2) {
+      float ss = 0.f;
+      for (int v = lane; v < nvec; v += 32) {
+        float f[8];
+        load8(row, v, f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      mul = ss > 0.f ? scale * rsqrtf(ss) : 0.f;
+    }
+    for (int v = lane; v < nvec; v += 32) {
+      float f[8];
+      load8(row, v, f);
+      uint4 q;
+      uint32_t* w = reinterpret_cast<uint32_t*>(&q);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * e] * mul, f[2 * e + 1] * mul);
+        w[e] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      reinterpret_cast<uint4*>(dst + int64_t(row) * D)[v] = q;
+    }
+  }
+  __threadfence_system();  // the publish launch that follows orders after these stores
+}
+
+// Thread 0: optional meta (rows >= 0), then a release store of `value` into the slot's state.
+__global__ void ring_publish_kernel(Peers P, int owner, int64_t state_off, int64_t meta_off,
+                                    const int* __restrict__ slot_ptr, int rows, int producer, int seq,
+                                    uint32_t value) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const int slot = *slot_ptr;
+  if (slot < 0) return;
+  if (rows >= 0) {
+    int* meta = at<int>(P, owner, meta_off) + 4 * slot;
+    meta[0] = rows;
+    meta[1] = producer;
+    meta[2] = seq;
+  }
+  __threadfence_system();
+  st_release_sys_u32(at<uint32_t>(P, owner, state_off) + slot, value);
+}
+
+// out[i] = slot rows[perm ? perm[i] : i] (local ring data), one warp per output row.
+__global__ void ring_gather_kernel(const __nv_bfloat16* __restrict__ data, int chunk_rows, int D,
+                                   const int* __restrict__ slot_ptr, const int* __restrict__ perm, int rows,
+                                   __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  const int slot = *slot_ptr;
+  if (slot < 0) return;
+  const __nv_bfloat16* base = data + int64_t(slot) * chunk_rows * D;
+  const int lane = threadIdx.x & 31;
+  const int nvec = D >> 3;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < rows; i += warps) {
+    const int r = perm ? perm[i] : i;
+    const uint4* s4 = reinterpret_cast<const uint4*>(base + int64_t(r) * D);
+    uint4* o4 = reinterpret_cast<uint4*>(out + int64_t(i) * ldo);
+    for (int v = lane; v < nvec; v += 32) o4[v] = __ldcg(s4 + v);
   }
 }
 
@@ -401,7 +548,7 @@ std::vector<int64_t> p2p_allreduce_sizes(int64_t n, int64_t elem_bytes, int64_t 
 void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64_t>& peer_bases, int64_t rank,
                    int64_t land_off, int64_t cnt_off, int64_t out_off, int64_t flag_off, int64_t epoch,
                    const torch::Tensor& ticket, const torch::Tensor& status, int64_t sq_off, int64_t chunk,
-                   int64_t max_ctas) {
+                   int64_t max_ctas, const c10::optional<torch::Tensor>& x_out) {
   const int64_t S = int64_t(peer_bases.size());
   TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "p2p_allreduce: bad group");
   TORCH_CHECK(x.is_cuda() && x.is_contiguous() &&
@@ -430,6 +577,12 @@ void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64
   a.epoch = uint32_t(epoch);
   a.ticket = ticket.data_ptr<int>();
   a.status = status.data_ptr<int>();
+  if (x_out) {
+    TORCH_CHECK(x_out->is_cuda() && x_out->is_contiguous() && x_out->scalar_type() == x.scalar_type() &&
+                    x_out->numel() == n,
+                "p2p_allreduce: x_out must be a contiguous tensor like x");
+    a.x_out = x_out->data_ptr();
+  }
   C10_CUDA_CHECK(cudaMemsetAsync(a.ticket, 0, sizeof(int), stream));
   const int64_t nch = (n + chunk - 1) / chunk;
   int64_t grid = std::max<int64_t>(1, std::min<int64_t>(2 * nch, int64_t(p2p_sm_count()) * 8));
@@ -462,6 +615,71 @@ void p2p_slot_reduce(const torch::Tensor& land, double scale, const torch::Tenso
   p2p::slot_reduce_kernel<<<dim3(grid), dim3(p2p::AR_THREADS), 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(land.data_ptr()), int(land.size(0)), nvec, float(scale),
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), sumsq ? sumsq->data_ptr<float>() : nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Device activation ring host entry points (see ring_claim_kernel).  `slot` is an int32 [1]
+// device word: the claimed slot index, or -1 when the bounded claim timed out.
+void ring_claim(const std::vector<int64_t>& peer_bases, int64_t rank, int64_t owner, int64_t state_off,
+                int64_t n_slots, int64_t from, int64_t to, int64_t start, double timeout_ms, const torch::Tensor& slot) {
+  TORCH_CHECK(slot.is_cuda() && slot.scalar_type() == at::kInt && slot.numel() >= 1, "ring_claim: slot");
+  TORCH_CHECK(n_slots >= 1 && owner >= 0 && owner < int64_t(peer_bases.size()) && state_off % 4 == 0,
+              "ring_claim: ring");
+  const at::cuda::CUDAGuard guard(slot.device());
+  p2p::Peers P = p2p::make_peers(peer_bases, rank);
+  p2p::ring_claim_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      P, int(owner), state_off, int(n_slots), uint32_t(from), uint32_t(to), int(start % n_slots),
+      (long long)(timeout_ms * 1e6), slot.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void ring_write(const torch::Tensor& src, const std::vector<int64_t>& peer_bases, int64_t rank, int64_t owner,
+                int64_t data_off, int64_t chunk_rows, const torch::Tensor& slot, int64_t mode, double scale) {
+  TORCH_CHECK(src.is_cuda() && src.dim() == 2 && src.stride(1) == 1 &&
+                  (src.scalar_type() == at::kFloat || src.scalar_type() == at::kBFloat16),
+              "ring_write: src must be a CUDA fp32/bf16 matrix with contiguous rows");
+  const int64_t rows = src.size(0), D = src.size(1);
+  TORCH_CHECK(rows <= chunk_rows && D % 8 == 0 && data_off % 16 == 0, "ring_write: rows <= chunk_rows, D % 8");
+  TORCH_CHECK(src.scalar_type() == at::kBFloat16 ? src.stride(0) % 8 == 0 : src.stride(0) % 4 == 0,
+              "ring_write: row stride alignment");
+  TORCH_CHECK(mode >= 0 && mode <= 2, "ring_write: mode");
+  if (rows == 0) return;
+  const at::cuda::CUDAGuard guard(src.device());
+  p2p::Peers P = p2p::make_peers(peer_bases, rank);
+  const int grid = int(std::min<int64_t>((rows + 7) / 8, int64_t(p2p_sm_count()) * 8));
+  p2p::ring_write_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      src.data_ptr(), src.stride(0), src.scalar_type() == at::kFloat ? 1 : 0, int(rows), int(D), int(mode),
+      float(scale), P, int(owner), data_off, int(chunk_rows), slot.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void ring_publish(const std::vector<int64_t>& peer_bases, int64_t rank, int64_t owner, int64_t state_off,
+                  int64_t meta_off, const torch::Tensor& slot, int64_t rows, int64_t producer, int64_t seq,
+                  int64_t value) {
+  const at::cuda::CUDAGuard guard(slot.device());
+  p2p::Peers P = p2p::make_peers(peer_bases, rank);
+  p2p::ring_publish_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      P, int(owner), state_off, meta_off, slot.data_ptr<int>(), int(rows), int(producer), int(seq), uint32_t(value));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void ring_gather(const torch::Tensor& data, const torch::Tensor& slot, const c10::optional<torch::Tensor>& perm,
+                 const torch::Tensor& out) {
+  TORCH_CHECK(data.is_cuda() && data.scalar_type() == at::kBFloat16 && data.dim() == 3 && data.is_contiguous(),
+              "ring_gather: data must be contiguous bf16 [N, chunk_rows, D]");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.dim() == 2 && out.size(1) == data.size(2) &&
+                  out.stride(1) == 1 && out.stride(0) % 8 == 0 && out.size(0) <= data.size(1),
+              "ring_gather: out must be bf16 [rows <= chunk_rows, D] with contiguous rows");
+  if (perm) TORCH_CHECK(perm->is_cuda() && perm->scalar_type() == at::kInt && perm->numel() >= out.size(0),
+                        "ring_gather: perm must be CUDA int32 [rows]");
+  const int64_t rows = out.size(0);
+  if (rows == 0) return;
+  const at::cuda::CUDAGuard guard(data.device());
+  const int grid = int(std::min<int64_t>((rows + 7) / 8, int64_t(p2p_sm_count()) * 8));
+  p2p::ring_gather_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(data.data_ptr()), int(data.size(1)), int(data.size(2)),
+      slot.data_ptr<int>(), perm ? perm->data_ptr<int>() : nullptr, int(rows),
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -43,8 +43,10 @@ def init_distributed_v2(P: int, Q: int, vllm_tp_size: int, sae_tp_size: int, bat
     roles = lay.roles_of(rank)
     groups: dict[str, object] = {}
     p2p: dict[int, object] = {}
+    on_nccl = dist.get_backend() == "nccl"
     for kind, ranks, backend, i in lay.groups:
-        g = dist.new_group(ranks, backend=backend)
+        # device groups are NCCL on GPUs; a CPU (gloo) world uses its own backend for them
+        g = dist.new_group(ranks, backend=backend if (on_nccl or backend != "nccl") else None)
         if rank not in ranks:
             continue
         if kind == "vllm_tp" and roles["producer_idx"] == i:

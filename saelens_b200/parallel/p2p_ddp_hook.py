@@ -23,7 +23,7 @@ from typing import Any
 import torch
 import torch.distributed as dist
 
-from saelens_b200.parallel.symm_heap import SlabBuffer, SymmetricHeap, slab_bytes_needed
+from saelens_b200.parallel.symm_heap import SymmetricHeap, slab_bytes_needed
 
 _DEFAULT_BUCKET_CAP_MB = 25.0
 
@@ -102,10 +102,10 @@ class P2PAllReduceHookState:
         with torch.cuda.stream(self.stream):
             a = self._area(n, buf.dtype)
             a[2] += 1
+            # the kernel copies each averaged chunk back into the bucket as soon as it arrived
             self.nat.p2p_allreduce(buf, 1.0 / self.world, self.heap.bases, self.rank, self.land_off, a[0],
                                    self.out_off, a[1], a[2], self.ticket, self.status.tensor,
-                                   max_ctas=self.max_ctas)
-            buf.copy_(self.heap.local(SlabBuffer(self.out_off, (n,), buf.dtype)))
+                                   max_ctas=self.max_ctas, x_out=buf)
             self.calls += 1
             fut: torch.futures.Future = torch.futures.Future(devices=[self.device])
             fut.set_result(buf)

@@ -66,17 +66,41 @@ class LanguageModelSAETrainingRunner:
         self.dp_group: dist.ProcessGroup | None = None
         self.ddp_hook_state: Any = None  # P2P gradient all-reduce of the DDP wrapper, when used
         self.native_fsdp = False  # sae_dp_mode="fsdp" on the native sharded engine
-        self._init_distributed()
-        self.model = override_model if override_model is not None else self._load_model()
-        shard, nshard = (self._dp_rank(), self.sae_dp_size) if self.sae_dp_size > 1 else (0, 1)
-        self.activations_store = ActivationsStore.from_config(self.model, cfg, override_dataset=override_dataset,
-                                                              shard_index=shard, num_shards=nshard)
-        self.sae = override_sae if override_sae is not None else self._build_sae()
-        if self.tp_group is not None and hasattr(self.sae, "shard_weights"):
-            self.sae.shard_weights(self.tp_group)
-        self.wrapped = self._wrap_dp(self.sae)
+        self.role: str | None = None  # streaming mode: "producer" (LM) or "consumer" (SAE)
+        if self.streaming_mode:
+            from saelens_b200.runners.streaming import streaming_init
+
+            streaming_init(self)  # groups, roles and the activation ring (collective)
+        else:
+            self._init_distributed()
+        producer_side = self.role in (None, "producer")
+        consumer_side = self.role in (None, "consumer")
+        self.model = None
+        self.activations_store: Any = None
+        if producer_side:
+            self.model = override_model if override_model is not None else self._load_model()
+            if self.streaming_mode:
+                shard, nshard = self._streaming_producer_shard()
+            else:
+                shard, nshard = (self._dp_rank(), self.sae_dp_size) if self.sae_dp_size > 1 else (0, 1)
+            self.activations_store = ActivationsStore.from_config(self.model, cfg, override_dataset=override_dataset,
+                                                                  shard_index=shard, num_shards=nshard)
+        self.sae: Any = None
+        self.wrapped: Any = None
+        if consumer_side:
+            self.sae = override_sae if override_sae is not None else self._build_sae()
+            if self.tp_group is not None and hasattr(self.sae, "shard_weights"):
+                self.sae.shard_weights(self.tp_group)
+            self.wrapped = self._wrap_dp(self.sae)
 
     # ---------------------------------------------------------------- setup
+    def _streaming_producer_shard(self) -> tuple[int, int]:
+        """Each streaming producer reads its own slice of the token dataset."""
+        from saelens_b200.parallel import distributed_streaming as ds
+
+        n = max(self.vllm_dp_size, 1)
+        return (ds.get_producer_idx(), n) if n > 1 else (0, 1)
+
     def _init_distributed(self) -> None:
         world = int(os.environ.get("WORLD_SIZE", "1"))
         if world <= 1 or (self.sae_tp_size == 1 and self.sae_dp_size == 1):
@@ -160,6 +184,10 @@ class LanguageModelSAETrainingRunner:
     # ---------------------------------------------------------------- run
     def run(self) -> TrainingSAE[Any]:
         cfg = self.cfg
+        if self.streaming_mode:
+            from saelens_b200.runners.streaming import run_streaming
+
+            return run_streaming(self)
         if cfg.logger.log_to_wandb and self._is_writer():
             from saelens_b200.utils import wandb_shim as wandb
 

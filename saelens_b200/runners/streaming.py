@@ -1,0 +1,234 @@
+"""Streaming mode of the LM training runner: producer GPUs run the LM and push activation chunks
+into a ring, a disjoint consumer GPU set trains the SAE from it (behaviour of
+sae_lens/llm_sae_training_runner.py:1112-1679 with sae_lens/distributed_streaming.py).
+
+Two transports carry the chunks:
+
+* "device" (default on CUDA with NCCL, SAE TP 1 and one hook): `DeviceActivationRing` in the
+  consumer GPU's symmetric slab.  Producers claim slots over NVLink and store the rows with P2P
+  stores, cast to bf16 in the same kernel; the consumer gathers batches on the device
+  (`DeviceRingProvider`).  No host copy, no H2D.
+* "host": the reference's design, a `/dev/shm` ring (`SharedActivationBuffer`) read by
+  `StreamingActivationProvider` (pinned staging, async H2D, NCCL broadcast to SAE TP ranks).
+
+Producers split the chunk quota statically (producer p writes sequence numbers p, p + P, ...),
+watch the quiesce-request file between chunks (checkpoint their dataset position, then ack) and
+signal "done" at the end.  The consumer trains through `SAETrainer` until the training tokens
+are reached or every producer is done and the ring is empty.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+import time
+from pathlib import Path
+from typing import Any
+
+import torch
+import torch.distributed as dist
+
+from saelens_b200.parallel import distributed_streaming as ds
+
+
+def choose_transport(cfg: Any, sae_tp: int, n_hooks: int) -> str:
+    want = getattr(cfg, "streaming_transport", "auto")
+    if want != "auto":
+        return want
+    on_cuda = str(cfg.device).startswith("cuda") and torch.cuda.is_available()
+    return "device" if (on_cuda and sae_tp == 1 and n_hooks == 1) else "host"
+
+
+def streaming_init(runner: Any) -> None:
+    """Process group, roles, and the ring (collective: every rank calls it)."""
+    cfg = runner.cfg
+    if not dist.is_initialized():
+        backend = "nccl" if str(cfg.device).startswith("cuda") and torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group(backend)
+    vllm_tp, vllm_dp = max(runner.vllm_tp_size, 1), max(runner.vllm_dp_size, 1)
+    sae_tp = max(runner.sae_tp_size, 1)
+    if vllm_tp != 1:
+        raise ValueError("streaming producers run the framework's LM on one GPU each (vllm_tp_size must be 1)")
+    ds.init_distributed_streaming(vllm_tp=vllm_tp, vllm_dp=vllm_dp, sae_tp=sae_tp, sae_dp=1)
+    runner.role = "producer" if ds.is_producer() else "consumer"
+    n_hooks = len(getattr(cfg, "hook_names", None) or [cfg.hook_name])
+    runner.streaming_transport = choose_transport(cfg, sae_tp, n_hooks)
+    runner.n_producers = vllm_dp
+    runner.target_chunks = math.ceil(cfg.training_tokens / cfg.streaming_chunk_size_tokens)
+    runner.ring = None
+    runner.shm_buffer = None
+    if runner.streaming_transport == "device":
+        from saelens_b200.parallel.device_ring import DeviceActivationRing
+
+        producers = [ds.get_producer_tp_root(p) for p in range(vllm_dp)]
+        runner.ring = DeviceActivationRing(dist.group.WORLD, producers, ds.get_consumer_tp_root(0),
+                                           n_slots=cfg.streaming_num_chunks,
+                                           chunk_rows=cfg.streaming_chunk_size_tokens, d=cfg.sae.d_in)
+    else:
+        from saelens_b200.training.shared_activation_buffer import SharedActivationBuffer
+        from saelens_b200.utils.misc import str_to_dtype
+
+        name = cfg.streaming_buffer_name or f"saeb_{os.environ.get('MASTER_PORT', 'run')}_{os.getppid()}"
+        kw = dict(name=name, num_chunks=cfg.streaming_num_chunks, chunk_size_tokens=cfg.streaming_chunk_size_tokens * n_hooks,
+                  d_model=cfg.sae.d_in, num_producers=vllm_dp, target_chunks=runner.target_chunks,
+                  base_dir=getattr(cfg, "streaming_buffer_dir", "/dev/shm"))
+        if dist.get_rank() == 0 and not cfg.streaming_buffer_name:
+            runner.shm_buffer = SharedActivationBuffer(create=True, dtype=str_to_dtype(cfg.dtype)
+                                                       if str_to_dtype(cfg.dtype) in (torch.bfloat16, torch.float32)
+                                                       else torch.bfloat16, **kw)
+        dist.barrier()
+        if runner.shm_buffer is None:
+            runner.shm_buffer = SharedActivationBuffer(create=False, **kw)
+
+
+def _quiesce_paths(runner: Any) -> tuple[Path | None, Path | None, Path | None]:
+    cfg = runner.cfg
+    qdir = Path(cfg.checkpoint_path) if cfg.checkpoint_path is not None else None
+    if qdir is None:
+        return None, None, None
+    pidx = ds.get_producer_idx()
+    return qdir / "quiesce_request", qdir / f"quiesce_ack_producer_{pidx}", qdir / f"producer_dataset_state_{pidx}"
+
+
+def run_producer(runner: Any) -> int:
+    """Write this producer's share of the chunk quota; returns the number of chunks written."""
+    cfg, store = runner.cfg, runner.activations_store
+    pidx, P = ds.get_producer_idx(), runner.n_producers
+    rows_per_chunk = cfg.streaming_chunk_size_tokens
+    req, ack, state_dir = _quiesce_paths(runner)
+    written = 0
+    seq = pidx
+    while seq < runner.target_chunks:
+        if req is not None and req.exists():
+            if state_dir is not None:
+                state_dir.mkdir(parents=True, exist_ok=True)
+                store.save_to_checkpoint(state_dir)
+            if ack is not None:
+                ack.touch()
+            break
+        rows = max(1, min(rows_per_chunk, cfg.training_tokens - seq * rows_per_chunk))
+        acts, valid = store.get_streaming_activations(rows)
+        if runner.ring is not None:
+            runner.ring.write(acts)
+        else:
+            buf = runner.shm_buffer
+            got = buf.allocate_write_chunk()
+            if got is None:
+                break
+            idx, _ = got
+            buf.write_chunk(idx, acts.detach().to("cpu"), valid, producer_id=pidx)
+            buf.mark_ready(idx)
+        written += 1
+        seq += P
+    if runner.ring is not None:
+        runner.ring.producer_done()
+    else:
+        runner.shm_buffer.signal_done()
+    return written
+
+
+class DeviceRingProvider:
+    """Training batches from a `DeviceActivationRing` (consumer side).  Chunks are gathered on
+    the device (rows permuted when `shuffle`), concatenated with the leftover of the previous
+    chunk and cut into `train_batch_size_tokens` rows.  Stops when every producer is done and
+    the ring holds no READY chunk."""
+
+    def __init__(self, ring: Any, train_batch_size_tokens: int, shuffle: bool = True, seed: int = 0,
+                 dtype: torch.dtype = torch.float32, timeout_s: float = 600.0):
+        self.ring = ring
+        self.batch = int(train_batch_size_tokens)
+        self.shuffle = shuffle
+        self.dtype = dtype
+        self.timeout_s = timeout_s
+        dev = ring.heap.device
+        self._gen = torch.Generator(device=dev)
+        self._gen.manual_seed(seed)
+        self._pool: torch.Tensor | None = None
+        self._consumed = 0
+
+    def __iter__(self) -> DeviceRingProvider:
+        return self
+
+    @property
+    def consumed_tokens(self) -> int:
+        return self._consumed
+
+    def _avail(self) -> int:
+        return 0 if self._pool is None else self._pool.shape[0]
+
+    def __next__(self) -> torch.Tensor:
+        ring = self.ring
+        while self._avail() < self.batch:
+            t0 = time.monotonic()
+            chunk = None
+            while chunk is None:
+                # done flags are set after a producer's last READY publish, so "done and nothing
+                # READY" means the stream has ended
+                if ring.producers_done() and ring.ready_chunks() == 0:
+                    break
+                try:
+                    chunk, _ = ring.take(timeout_s=1.0, shuffle=self._gen if self.shuffle else None)
+                except TimeoutError:
+                    if time.monotonic() - t0 > self.timeout_s:
+                        raise
+            if chunk is None:
+                break
+            self._pool = chunk if self._pool is None else torch.cat([self._pool, chunk])
+        if self._avail() == 0:
+            raise StopIteration
+        n = min(self.batch, self._avail())
+        assert self._pool is not None
+        b, self._pool = self._pool[:n], self._pool[n:]
+        self._consumed += n
+        return b.to(self.dtype)
+
+    def consume_last_data_timing(self) -> dict[str, float]:
+        return {"vllm_step_time_s": 0.0, "transfer_time_s": 0.0}
+
+
+def run_consumer(runner: Any) -> Any:
+    """Train the SAE from the ring; returns the trained SAE (on the consumer ranks)."""
+    from saelens_b200.training.sae_trainer import SAETrainer
+    from saelens_b200.training.streaming_activation_provider import StreamingActivationProvider
+    from saelens_b200.utils.misc import str_to_dtype
+
+    cfg = runner.cfg
+    dev = runner.sae.W_dec.device
+    if runner.ring is not None:
+        provider: Any = DeviceRingProvider(runner.ring, cfg.train_batch_size_tokens, shuffle=cfg.streaming_shuffle,
+                                           seed=cfg.seed, dtype=str_to_dtype(cfg.dtype))
+    else:
+        tp = ds.get_sae_tp_group() if ds.get_sae_tp_size() > 1 else None
+        provider = StreamingActivationProvider(
+            runner.shm_buffer, cfg.train_batch_size_tokens, cfg.streaming_prefetch_chunks, dev, sae_tp_group=tp,
+            sae_tp_rank=ds.get_sae_tp_rank(), sae_tp_root_global_rank=ds.get_consumer_tp_root(0),
+            d_model=cfg.sae.d_in, dtype=str_to_dtype(cfg.dtype), shuffle=cfg.streaming_shuffle,
+            random_chunks=cfg.streaming_random_chunks)
+    trainer = SAETrainer(cfg=cfg.to_sae_trainer_config(), sae=runner.sae, base_sae=runner.sae, data_provider=provider,
+                         evaluator=None, save_checkpoint_fn=None)
+    runner.trainer = trainer
+    sae = trainer.fit()
+    if runner.ring is None or ds.get_sae_tp_rank() == 0:
+        runner.save_final_sae(sae, trainer)
+    return sae
+
+
+def run_streaming(runner: Any) -> Any:
+    """Entry point of `LanguageModelSAETrainingRunner.run()` in streaming mode."""
+    result = None
+    if runner.role == "producer":
+        run_producer(runner)
+    else:
+        result = run_consumer(runner)
+    dist.barrier()
+    if runner.ring is not None:
+        runner.ring.close()
+    elif runner.shm_buffer is not None:
+        runner.shm_buffer.close()
+    return result
+
+
+__all__ = ["DeviceRingProvider", "choose_transport", "run_consumer", "run_producer", "run_streaming",
+           "streaming_init"]

@@ -186,6 +186,28 @@ class ActivationsStore:
             return a[keep.to(a.device)] if keep is not None else a
         return {h: flat(v) for h, v in acts.items()} if isinstance(acts, dict) else flat(acts)
 
+    @torch.no_grad()
+    def get_streaming_activations(self, max_tokens: int) -> tuple[torch.Tensor, int]:
+        """Up to `max_tokens` activation rows [n, d_in] for one streaming chunk (producer side of
+        sae_lens/training/activations_store.py:778-915): whole LM batches are run, the rows past
+        `max_tokens` are kept for the next chunk."""
+        parts: list[torch.Tensor] = []
+        have = 0
+        rest = getattr(self, "_stream_residual", None)
+        if rest is not None and rest.shape[0]:
+            parts.append(rest)
+            have = rest.shape[0]
+        while have < max_tokens:
+            a = self.get_filtered_llm_batch()
+            if isinstance(a, dict):
+                a = torch.cat([a[h] for h in self.hook_names], dim=-1)
+            parts.append(a)
+            have += a.shape[0]
+        cat = torch.cat(parts) if len(parts) > 1 else parts[0]
+        self._stream_residual = cat[max_tokens:]
+        out = cat[:max_tokens]
+        return out, int(out.shape[0])
+
     def _cached_batches(self) -> Iterator[torch.Tensor]:
         while True:
             for f in self._cached_files:
