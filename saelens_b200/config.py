@@ -219,9 +219,11 @@ class LanguageModelSAERunnerConfig(Generic[T_TRAINING_SAE_CONFIG]):
     # Tensor-parallel exchanges of the native engine: NVLink peer-memory kernels fused with the
     # compute ("p2p") or NCCL collectives between kernels ("nccl").
     tp_exchange: Literal["p2p", "nccl"] = "p2p"
-    # Gradient all-reduce of `sae_dp_mode="ddp"` on the PyTorch path: a DDP communication hook
-    # running the P2P all-reduce kernel ("p2p") or DDP's own NCCL all-reduce ("nccl").
-    ddp_exchange: Literal["p2p", "nccl"] = "p2p"
+    # Gradient all-reduce of `sae_dp_mode="ddp"` on the PyTorch path (SAEs without a native
+    # engine): DDP's own NCCL all-reduce ("nccl", default: measured faster on the dense
+    # JumpReLU step, where the all-reduce overlaps cuBLAS GEMMs) or a DDP communication hook
+    # running the P2P all-reduce kernel ("p2p").  TopK-family SAEs use the native DDP engine.
+    ddp_exchange: Literal["p2p", "nccl"] = "nccl"
 
     def __post_init__(self) -> None:
         if self.multi_sae_seed_mode not in ("same", "offset"):

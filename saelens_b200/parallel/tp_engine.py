@@ -118,29 +118,37 @@ class _DPReducer:
     """Averages a TP rank's latent-shard gradients over the data-parallel replicas of that shard
     (the ranks of `group` hold the same latents and see different rows) with the P2P all-reduce
     kernel, and sums the firing counts.  Gradient rows are dense ([2, N, D] buffer, zero rows for
-    latents no local pair touched) because other replicas may touch them."""
+    latents no local pair touched) because other replicas may touch them.  The rows are reduced
+    in `segments` latent ranges on a communication stream while the next range's gradients are
+    computed (the overlap of the DDP engine)."""
 
-    def __init__(self, eng: "TPTopKEngine", group: dist.ProcessGroup, small_n: int):
+    def __init__(self, eng: "TPTopKEngine", group: dist.ProcessGroup, small_n: int, segments: int = 4):
         from saelens_b200.parallel.ddp_engine import _ArArea
 
         nat, N, D = eng.native, eng.N, eng.D
         self.size = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        segments = max(1, min(int(segments), N // 256))
+        bounds = [N * i // segments // 256 * 256 for i in range(segments)] + [N]
+        self.ranges = [(bounds[i], bounds[i + 1]) for i in range(segments) if bounds[i + 1] > bounds[i]]
         sizes = [2 * N * D * 2]
-        sizes += _ArArea.nbytes(nat, N * D, 2, self.size, False) * 2
+        for j0, j1 in self.ranges:
+            sizes += _ArArea.nbytes(nat, (j1 - j0) * D, 2, self.size, False) * 2
         sizes += _ArArea.nbytes(nat, small_n, 4, self.size, True) + _ArArea.nbytes(nat, N, 4, self.size, True)
         self.heap = SymmetricHeap(group, slab_bytes_needed(sizes) + 65536)
         self.gbuf = torch.empty(2, N, D, dtype=torch.bfloat16, device=eng.device)
         self.gout_buf = self.heap.alloc((2, N, D), torch.bfloat16)
         self.g_avg = self.heap.local(self.gout_buf)
-        self.a_dec = _ArArea(self.heap, nat, N * D, 2, self.gout_buf.offset)
-        self.a_enc = _ArArea(self.heap, nat, N * D, 2, self.gout_buf.offset + N * D * 2)
+        base = self.gout_buf.offset
+        self.areas = [(j0, j1, _ArArea(self.heap, nat, (j1 - j0) * D, 2, base + j0 * D * 2),
+                       _ArArea(self.heap, nat, (j1 - j0) * D, 2, base + (N + j0) * D * 2)) for j0, j1 in self.ranges]
         self.a_small = _ArArea(self.heap, nat, small_n, 4, None)
         self.a_fire = _ArArea(self.heap, nat, N, 4, None)
         self.small_out = self.heap.local(SlabBuffer(self.a_small.out, (small_n,), torch.float32))
         self.fire_out = self.heap.local(SlabBuffer(self.a_fire.out, (N,), torch.float32))
-        self.tickets = torch.zeros(4, dtype=torch.int32, device=eng.device)
+        self.tickets = torch.zeros(2 * len(self.areas) + 2, dtype=torch.int32, device=eng.device)
         self.dense_colptr = torch.arange(N + 1, dtype=torch.int64, device=eng.device)
+        self.comm = torch.cuda.Stream(device=eng.device)
         self.nat, self.status = nat, eng.status
 
     def _ar(self, x: torch.Tensor, scale: float, area: Any, t: int, sq: bool) -> None:
@@ -149,14 +157,33 @@ class _DPReducer:
                                area.epoch, self.tickets[t : t + 1], self.status.tensor,
                                area.sq_buf.offset if sq else -1)
 
-    def reduce(self, small: torch.Tensor, fire: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-        """Returns (averaged small vector, summed fire counts, sum of squares of the averaged W grads)."""
-        inv = 1.0 / self.size
-        self._ar(self.gbuf[0].reshape(-1), inv, self.a_dec, 0, True)
-        self._ar(self.gbuf[1].reshape(-1), inv, self.a_enc, 1, True)
-        self._ar(small, inv, self.a_small, 2, False)
-        self._ar(fire, 1.0, self.a_fire, 3, False)
-        return self.small_out, self.fire_out, self.a_dec.sq.sum() + self.a_enc.sq.sum()
+    def reduce_segment(self, i: int) -> None:
+        """Average segment i's gradient rows on the communication stream (after the compute
+        stream's work so far)."""
+        j0, j1, a_dec, a_enc = self.areas[i]
+        ready = torch.cuda.Event()
+        ready.record()
+        with torch.cuda.stream(self.comm):
+            self.comm.wait_event(ready)
+            inv = 1.0 / self.size
+            self._ar(self.gbuf[0, j0:j1].reshape(-1), inv, a_dec, 2 * i, True)
+            self._ar(self.gbuf[1, j0:j1].reshape(-1), inv, a_enc, 2 * i + 1, True)
+
+    def finish(self, small: torch.Tensor, fire: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """Returns (averaged small vector, summed fire counts, sum of squares of the averaged W
+        grads); the compute stream waits for every reduction."""
+        nt = 2 * len(self.areas)
+        ready = torch.cuda.Event()
+        ready.record()
+        with torch.cuda.stream(self.comm):
+            self.comm.wait_event(ready)
+            self._ar(small, 1.0 / self.size, self.a_small, nt, False)
+            self._ar(fire, 1.0, self.a_fire, nt + 1, False)
+        done = torch.cuda.Event()
+        done.record(self.comm)
+        torch.cuda.current_stream().wait_event(done)
+        sq = sum(a.sq.sum() + b.sq.sum() for _, _, a, b in self.areas)
+        return self.small_out, self.fire_out, sq
 
     def close(self) -> None:
         self.heap.close()
@@ -558,13 +585,24 @@ class TPTopKEngine(FusedTopKEngine):
         self._mark("csc_build")
         sumsq = red[2 * D : 2 * D + 1]
         dp = self._dp
-        nat.latent_grad(self.colptr, pairs, vals, aux_vals if aux_on else None,
-                        self.inv_scale if self.rescale else None, dX, daux, X,
-                        self.p_bdec if self.apply_b_dec else None, self.w_dec, self.w_enc, self.g_dec, self.g_enc,
-                        self.g_benc, bterm if self.apply_b_dec else None, sumsq if dp is None else None,
-                        self.fire_counts, act_freq if dp is None else None, since_fired if dp is None else None,
-                        idx, aux_idx if aux_on else None, 0, -1, dp is not None)
-        self.launches += 3
+        if dp is None:
+            nat.latent_grad(self.colptr, pairs, vals, aux_vals if aux_on else None,
+                            self.inv_scale if self.rescale else None, dX, daux, X,
+                            self.p_bdec if self.apply_b_dec else None, self.w_dec, self.w_enc, self.g_dec,
+                            self.g_enc, self.g_benc, bterm if self.apply_b_dec else None, sumsq, self.fire_counts,
+                            act_freq, since_fired, idx, aux_idx if aux_on else None, 0, -1, False)
+            self.launches += 3
+        else:
+            # dense rows by latent range; each range is averaged over the replicas on the
+            # communication stream while the next range's gradients are computed
+            for i, (j0, j1, _, _) in enumerate(dp.areas):
+                nat.latent_grad(self.colptr, pairs, vals, aux_vals if aux_on else None,
+                                self.inv_scale if self.rescale else None, dX, daux, X,
+                                self.p_bdec if self.apply_b_dec else None, self.w_dec, self.w_enc, self.g_dec,
+                                self.g_enc, self.g_benc, bterm if self.apply_b_dec else None, None, None, None, None,
+                                idx, aux_idx if aux_on else None, j0, j1, True)
+                dp.reduce_segment(i)
+                self.launches += 5
         self._mark("latent_grad")
         red[2 * D + 1] = loss_row.sum()
         g_dec, g_enc, g_benc, colptr = self.g_dec, self.g_enc, self.g_benc, self.colptr
@@ -572,8 +610,8 @@ class TPTopKEngine(FusedTopKEngine):
             # average this shard's gradients over its data-parallel replicas; the clip norm is taken
             # from the averaged gradients (then summed over the tensor-parallel shards below)
             small = torch.cat([self.g_benc, red[: 2 * D], red[2 * D + 1 : 2 * D + 3]])
-            avg, fired, sq_w = dp.reduce(small, self.fire_counts.to(torch.float32))
-            self.launches += 4
+            avg, fired, sq_w = dp.finish(small, self.fire_counts.to(torch.float32))
+            self.launches += 2
             N = self.N
             g_benc = avg[:N]
             red = torch.cat([avg[N : N + 2 * D], (sq_w + g_benc.square().sum()).reshape(1), avg[N + 2 * D :]])

@@ -18,9 +18,9 @@ def test_hook_unsupported_for_cpu_parameters():
     assert not p2p_hook_supported(torch.nn.Linear(4, 4), None)
 
 
-def test_runner_config_defaults_to_p2p_ddp_exchange():
+def test_runner_config_ddp_exchange_default():
     from saelens_b200.config import LanguageModelSAERunnerConfig
     from saelens_b200.models.standard import StandardTrainingSAEConfig
 
     cfg = LanguageModelSAERunnerConfig(sae=StandardTrainingSAEConfig(d_in=8, d_sae=16), device="cpu")
-    assert cfg.ddp_exchange == "p2p"
+    assert cfg.ddp_exchange == "nccl"
