@@ -35,6 +35,7 @@ threshold are kept in (row, global latent) order on every shard.
 
 from __future__ import annotations
 
+import os
 from typing import Any
 
 import torch
@@ -212,7 +213,8 @@ class TPTopKEngine(FusedTopKEngine):
         if dp_group is not None and dist.get_world_size(dp_group) > 1:
             if not self.fused:
                 raise NotImplementedError("tensor x data parallel needs the fused exchanges (fused=True)")
-            self._dp = _DPReducer(self, dp_group, self.N + 2 * self.D + 2)
+            segments = int(os.environ.get("SAELENS_B200_DP_SEGMENTS", "4"))
+            self._dp = _DPReducer(self, dp_group, self.N + 2 * self.D + 2, segments)
             self.g_dec, self.g_enc = self._dp.gbuf[0], self._dp.gbuf[1]
 
     def close(self) -> None:

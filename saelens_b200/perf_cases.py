@@ -432,7 +432,7 @@ def router(args: argparse.Namespace) -> None:
 
     ms_p2p = timed(p2p_step)
     r.status.check("router")
-    ms_nccl = timed(nccl_step)
+    ms_nccl = float("nan") if args.no_nccl else timed(nccl_step)
     bytes_out = rows * d * 2
     if rank == 0:
         print(json.dumps({"world": world, "rows": rows, "d": d, "p2p_ms": round(ms_p2p, 4),
@@ -489,6 +489,7 @@ def main() -> None:
     rt = sub.add_parser("router")
     rt.add_argument("--rows", type=int, default=8192)
     rt.add_argument("--d", type=int, default=4096)
+    rt.add_argument("--no-nccl", action="store_true", help="skip the NCCL comparison (1-GPU profiling runs)")
     args = p.parse_args()
     {"phases": phases, "fused-case": fused_case, "gemm": gemm, "ddp": ddp, "allreduce": allreduce, "router": router,
      "tpdp": tpdp, "fsdp": ddp, "ddp-hook": ddp_hook}[args.cmd](args)
