@@ -306,6 +306,92 @@ def ddp_hook(args: argparse.Namespace) -> None:
     dist.destroy_process_group()
 
 
+def ring(args: argparse.Namespace) -> None:
+    """Streaming transport throughput, rank 0 producer -> rank 1 consumer: chunks of fp32 rows
+    normalised to norm sqrt(d) and cast to bf16, through the device ring (P2P stores into the
+    consumer GPU) and through the /dev/shm ring (D2H, shared memory, pinned H2D).  Consumer-side
+    CUDA events around the whole stream of chunks; GB/s counts the bf16 rows delivered."""
+    import math
+    import tempfile
+
+    import torch
+    import torch.distributed as dist
+
+    from saelens_b200.parallel.device_ring import DeviceActivationRing
+    from saelens_b200.training.shared_activation_buffer import SharedActivationBuffer
+    from saelens_b200.training.streaming_activation_provider import StreamingActivationProvider
+
+    world, rank, _ = _init_dist()
+    rows, d, n = args.rows, args.d, args.chunks
+    x = torch.randn(rows, d, device="cuda")
+    res = {}
+    # device ring
+    ringd = DeviceActivationRing(dist.group.WORLD, [0], 1, n_slots=4, chunk_rows=rows, d=d, normalize="unit_norm",
+                                 scale=math.sqrt(d))
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if rank == 0:
+        for _ in range(n):
+            ringd.write(x)
+        torch.cuda.synchronize()
+    else:
+        out = torch.empty(rows, d, dtype=torch.bfloat16, device="cuda")
+        ringd.take(out=out)  # first chunk: warm-up
+        e0.record()
+        for _ in range(n - 1):
+            ringd.take(out=out)
+        e1.record()
+        torch.cuda.synchronize()
+        res["device_ms_per_chunk"] = e0.elapsed_time(e1) / (n - 1)
+    dist.barrier()
+    ringd.close()
+    # host ring (/dev/shm): the reference's transport
+    import shutil
+
+    need = 4 * rows * d * 2 + (1 << 20)
+    base = "/dev/shm" if os.path.isdir("/dev/shm") and shutil.disk_usage("/dev/shm").free > need \
+        else tempfile.gettempdir()
+    name_t = torch.tensor([os.getpid()], device="cuda")
+    dist.broadcast(name_t, src=0)
+    name = f"perf_ring_{int(name_t.item())}"
+    if rank == 0:
+        buf = SharedActivationBuffer(name, 4, rows, d, num_producers=1, target_chunks=n, create=True, base_dir=base)
+    dist.barrier()
+    if rank == 1:
+        buf = SharedActivationBuffer(name, 4, rows, d, num_producers=1, target_chunks=n, base_dir=base)
+    dist.barrier()
+    if rank == 0:
+        for _ in range(n):
+            got = buf.allocate_write_chunk()
+            if got is None:
+                break
+            y = (x / x.norm(dim=-1, keepdim=True) * math.sqrt(d)).to(torch.bfloat16).cpu()
+            buf.write_chunk(got[0], y, rows)
+            buf.mark_ready(got[0])
+        buf.signal_done()
+    else:
+        prov = StreamingActivationProvider(buf, rows, 1, "cuda", d_model=d, dtype=torch.bfloat16, shuffle=False,
+                                           random_chunks=False)
+        next(prov)
+        e0.record()
+        for _ in range(n - 1):
+            next(prov)
+        e1.record()
+        torch.cuda.synchronize()
+        res["host_ms_per_chunk"] = e0.elapsed_time(e1) / (n - 1)
+    dist.barrier()
+    buf.close()
+    if rank == 0:
+        buf.unlink()
+    if rank == 1:
+        gb = rows * d * 2 / 1e9
+        print(json.dumps({"rows": rows, "d": d, "chunks": n, **{k: round(v, 3) for k, v in res.items()},
+                          "device_GBs": round(gb / res["device_ms_per_chunk"] * 1e3, 1),
+                          "host_GBs": round(gb / res["host_ms_per_chunk"] * 1e3, 1)}), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def allreduce(args: argparse.Namespace) -> None:
     import torch
     import torch.distributed as dist
@@ -485,6 +571,10 @@ def main() -> None:
     dh.add_argument("--d-sae", type=int, default=131072)
     dh.add_argument("--batch", type=int, default=4096)
     dh.add_argument("--steps", type=int, default=10)
+    rg = sub.add_parser("ring", help="streaming transport throughput: device ring vs /dev/shm ring (2 ranks)")
+    rg.add_argument("--rows", type=int, default=8192)
+    rg.add_argument("--d", type=int, default=4096)
+    rg.add_argument("--chunks", type=int, default=24)
     sub.add_parser("allreduce")
     rt = sub.add_parser("router")
     rt.add_argument("--rows", type=int, default=8192)
@@ -492,7 +582,7 @@ def main() -> None:
     rt.add_argument("--no-nccl", action="store_true", help="skip the NCCL comparison (1-GPU profiling runs)")
     args = p.parse_args()
     {"phases": phases, "fused-case": fused_case, "gemm": gemm, "ddp": ddp, "allreduce": allreduce, "router": router,
-     "tpdp": tpdp, "fsdp": ddp, "ddp-hook": ddp_hook}[args.cmd](args)
+     "tpdp": tpdp, "fsdp": ddp, "ddp-hook": ddp_hook, "ring": ring}[args.cmd](args)
 
 
 if __name__ == "__main__":
