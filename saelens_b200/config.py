@@ -212,6 +212,9 @@ class LanguageModelSAERunnerConfig(Generic[T_TRAINING_SAE_CONFIG]):
     # on CUDA with SAE TP 1 and one hook.
     streaming_transport: Literal["auto", "device", "host"] = "auto"
     streaming_buffer_dir: str = "/dev/shm"
+    # Transport of shard routing (`use_shard_routing`): "p2p" = row-router kernel over NVLink,
+    # "collective" = torch.distributed point-to-point sends; "auto" = p2p on NCCL.
+    routing_transport: Literal["auto", "p2p", "collective"] = "auto"
 
     # B200 engine knobs (no counterpart in the reference): use the fused native TopK-family
     # training step on CUDA when available ("auto"), always ("native") or never ("torch").

@@ -18,6 +18,8 @@ both or neither.
 
 from __future__ import annotations
 
+import time
+
 from typing import Sequence
 
 import torch
@@ -84,22 +86,41 @@ class P2PRowRouter:
         self.send_epoch = 0
         self.recv_epoch = 0
 
-    def send(self, acts: torch.Tensor) -> None:
-        """Producer: route this step's rows (fp32 or bf16 [batch_rows, d]) to the consumers."""
+    @staticmethod
+    def _host_wait(view: torch.Tensor, target: torch.Tensor, timeout_s: float, what: str) -> None:
+        """Poll device words from the host until view >= target (elementwise): long waits (an LM
+        step, a slow consumer) happen here, so the kernels' own bounded waits find the data."""
+        t0 = time.monotonic()
+        while True:
+            if bool((view.to(torch.int64).cpu() >= target).all()):
+                return
+            if time.monotonic() - t0 > timeout_s:
+                raise TimeoutError(f"row router: {what} not reached within {timeout_s:.0f} s")
+            time.sleep(5e-5)
+
+    def send(self, acts: torch.Tensor, host_wait_s: float | None = None) -> None:
+        """Producer: route this step's rows (fp32 or bf16 [batch_rows, d]) to the consumers.
+        With `host_wait_s`, first wait on the host until the destination slots were released."""
         if self.p_idx is None:
             raise RuntimeError(f"rank {self.rank} is not a producer")
+        if host_wait_s is not None and self.send_epoch + 1 >= 3:
+            free = self.heap.local(self.free)[torch.tensor(self.free_slots, device=self.heap.device)]
+            self._host_wait(free, torch.tensor(self.send_epoch + 1 - 2), host_wait_s, "consumer release")
         self.send_epoch += 1
         self.nat.p2p_route_rows(acts, self.table, self.heap.bases, self.rank, self.land.offset, self.rows_cap,
                                 (self.send_epoch - 1) % 2, self.cnt.offset, self.p_idx, self.free.offset,
                                 self.free_slots, self.mode, self.scale, self.send_epoch, self.status.tensor)
 
-    def recv(self) -> torch.Tensor:
+    def recv(self, host_wait_s: float | None = None) -> torch.Tensor:
         """Consumer: wait (on the stream) for this step's rows; returns a view of the landing slot.
-        Call `release()` once the rows have been consumed."""
+        Call `release()` once the rows have been consumed.  With `host_wait_s`, first wait on the
+        host until every producer's rows arrived."""
         if self.c_idx is None:
             raise RuntimeError(f"rank {self.rank} is not a consumer")
         self.recv_epoch += 1
         targets = self._chunks * self.recv_epoch
+        if host_wait_s is not None:
+            self._host_wait(self.cnt_local[: self.P], targets.cpu(), host_wait_s, "producer rows")
         self.nat.p2p_wait_targets(self.cnt_local, targets, self.status.tensor)
         return self.land_local[(self.recv_epoch - 1) % 2, : self.rows_for[self.c_idx]]
 

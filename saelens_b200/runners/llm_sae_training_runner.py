@@ -66,21 +66,35 @@ class LanguageModelSAETrainingRunner:
         self.dp_group: dist.ProcessGroup | None = None
         self.ddp_hook_state: Any = None  # P2P gradient all-reduce of the DDP wrapper, when used
         self.native_fsdp = False  # sae_dp_mode="fsdp" on the native sharded engine
-        self.role: str | None = None  # streaming mode: "producer" (LM) or "consumer" (SAE)
+        self.role: str | None = None  # streaming / routed mode: producer (LM), consumer (SAE) or both
+        self.router: Any = None
+        self.routed = bool(use_shard_routing) and int(os.environ.get("WORLD_SIZE", "1")) > 1 and not self.streaming_mode
         if self.streaming_mode:
             from saelens_b200.runners.streaming import streaming_init
 
             streaming_init(self)  # groups, roles and the activation ring (collective)
+        elif self.routed:
+            from saelens_b200.runners.routing import routing_init
+
+            routing_init(self)  # v2 layout, roles and the row router (collective)
         else:
             self._init_distributed()
-        producer_side = self.role in (None, "producer")
-        consumer_side = self.role in (None, "consumer")
+        if self.routed:
+            producer_side, consumer_side = self.is_route_producer, self.is_route_consumer
+        else:
+            producer_side = self.role in (None, "producer")
+            consumer_side = self.role in (None, "consumer")
         self.model = None
         self.activations_store: Any = None
         if producer_side:
             self.model = override_model if override_model is not None else self._load_model()
             if self.streaming_mode:
                 shard, nshard = self._streaming_producer_shard()
+            elif self.routed:
+                from saelens_b200.parallel import distributed_v2 as v2
+
+                n = max(self.vllm_dp_size, 1)
+                shard, nshard = (v2.get_producer_idx(), n) if n > 1 else (0, 1)
             else:
                 shard, nshard = (self._dp_rank(), self.sae_dp_size) if self.sae_dp_size > 1 else (0, 1)
             self.activations_store = ActivationsStore.from_config(self.model, cfg, override_dataset=override_dataset,
@@ -188,6 +202,8 @@ class LanguageModelSAETrainingRunner:
             from saelens_b200.runners.streaming import run_streaming
 
             return run_streaming(self)
+        if self.routed:
+            return self._run_routed()
         if cfg.logger.log_to_wandb and self._is_writer():
             from saelens_b200.utils import wandb_shim as wandb
 
@@ -235,6 +251,31 @@ class LanguageModelSAETrainingRunner:
             from saelens_b200.utils import wandb_shim as wandb
 
             wandb.finish()
+        return sae
+
+    def _run_routed(self) -> Any:
+        """Shard-routing mode: producers feed the consumers' trainers step by step."""
+        from saelens_b200.runners.routing import RoutedExchange, RoutedProvider, run_producer_only
+
+        cfg = self.cfg
+        n_steps = cfg.total_training_steps
+        sae = None
+        if not self.is_route_consumer:
+            run_producer_only(self, n_steps)
+        else:
+            ex = RoutedExchange(self)
+            trainer = SAETrainer(
+                cfg=cfg.to_sae_trainer_config(), sae=self.wrapped, base_sae=self.sae,
+                data_provider=RoutedProvider(ex, n_steps), evaluator=None,
+                save_checkpoint_fn=self._save_checkpoint_extras if self.activations_store is not None else None,
+                dp_group=self.dp_group, native_fsdp=self.native_fsdp)
+            self.trainer = trainer
+            sae = trainer.fit()
+            ex.finish()
+            self.save_final_sae(sae, trainer)
+        dist.barrier()
+        if self.router is not None:
+            self.router.close()
         return sae
 
     def _evaluator(self) -> Any:
