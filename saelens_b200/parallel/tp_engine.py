@@ -213,7 +213,7 @@ class TPTopKEngine(FusedTopKEngine):
         if dp_group is not None and dist.get_world_size(dp_group) > 1:
             if not self.fused:
                 raise NotImplementedError("tensor x data parallel needs the fused exchanges (fused=True)")
-            segments = int(os.environ.get("SAELENS_B200_DP_SEGMENTS", "4"))
+            segments = int(os.environ.get("SAELENS_B200_DP_SEGMENTS", "1"))
             self._dp = _DPReducer(self, dp_group, self.N + 2 * self.D + 2, segments)
             self.g_dec, self.g_enc = self._dp.gbuf[0], self._dp.gbuf[1]
 
