@@ -147,9 +147,11 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
             stride = math.ceil(cfg.total_training_samples / (cfg.n_checkpoints + 1))
             self.checkpoint_thresholds = list(range(0, cfg.total_training_samples, stride))[1:]
 
-        d_sae_local = self._base_sae.W_dec.shape[0]
-        self.act_freq_scores = torch.zeros(d_sae_local, device=cfg.device)
-        self.n_forward_passes_since_fired = torch.zeros(d_sae_local, device=cfg.device)
+        # firing statistics cover every latent (the PyTorch TP forward gathers the activations to
+        # full width); the native TP engine keeps them per latent shard (resized below)
+        d_stats = int(self._base_sae.cfg.d_sae)
+        self.act_freq_scores = torch.zeros(d_stats, device=cfg.device)
+        self.n_forward_passes_since_fired = torch.zeros(d_stats, device=cfg.device)
         self.n_frac_active_samples = 0
 
         # ---- engine selection
@@ -205,6 +207,12 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
             elif want == "native":
                 raise ValueError("sae_engine='native' requested but this SAE/device is not supported by the fused engine")
 
+        from saelens_b200.parallel.tp_engine import TPTopKEngine
+
+        if isinstance(self.engine, TPTopKEngine):
+            n_local = int(self.engine.N)
+            self.act_freq_scores = torch.zeros(n_local, device=cfg.device)
+            self.n_forward_passes_since_fired = torch.zeros(n_local, device=cfg.device)
         assert cfg.lr_end is not None
         if self.engine is None:
             self.optimizer: torch.optim.Optimizer | None = torch.optim.Adam(

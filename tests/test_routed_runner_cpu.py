@@ -19,7 +19,7 @@ def _port() -> int:
     return p
 
 
-def _worker(rank, world, port, tmp, P, Q):
+def _worker(rank, world, port, tmp, P, Q, tp=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
     import torch.distributed as dist
@@ -28,6 +28,7 @@ def _worker(rank, world, port, tmp, P, Q):
     from saelens_b200.config import LanguageModelSAERunnerConfig, LoggingConfig
     from saelens_b200.models.lm import HookedLM, preset_config
     from saelens_b200.models.standard import StandardTrainingSAEConfig
+    from saelens_b200.models.topk import TopKTrainingSAEConfig
     from saelens_b200.runners.llm_sae_training_runner import LanguageModelSAETrainingRunner
 
     torch.manual_seed(0)
@@ -35,13 +36,14 @@ def _worker(rank, world, port, tmp, P, Q):
                                 dtype="float32"))
     torch.manual_seed(1)
     cfg = LanguageModelSAERunnerConfig(
-        sae=StandardTrainingSAEConfig(d_in=64, d_sae=128, l1_coefficient=1e-3), model_name="gpt2",
+        sae=(StandardTrainingSAEConfig(d_in=64, d_sae=128, l1_coefficient=1e-3) if tp == 1
+             else TopKTrainingSAEConfig(d_in=64, d_sae=128, k=8)), model_name="gpt2",
         hook_name="blocks.1.hook_resid_pre", dataset_path="synthetic:uniform:500:32", context_size=16,
         training_tokens=64 * 8, train_batch_size_tokens=64, store_batch_size_prompts=4, n_batches_in_buffer=2,
         output_path=os.path.join(tmp, "out"), logger=LoggingConfig(log_to_wandb=False), device="cpu",
         save_mse_every_n_steps=1, n_checkpoints=0, verbose=False, routing_transport="collective")
     runner = LanguageModelSAETrainingRunner(cfg, override_model=lm, vllm_dp_size=P, sae_dp_size=Q,
-                                            use_shard_routing=True)
+                                            sae_tp_size=tp, use_shard_routing=True)
     out = runner.run()
     info = {"role": runner.role, "transport": runner.routing_transport}
     if out is not None:
@@ -64,3 +66,12 @@ def test_routed_runner(tmp_path, P, Q):
         assert r[0]["steps"] == r[1]["steps"] == 8
         assert r[0]["W_dec_sum"] == pytest.approx(r[1]["W_dec_sum"], rel=1e-6)  # DP replicas agree
     assert (tmp_path / "out" / "sae_weights.safetensors").exists()
+
+
+def test_routed_runner_to_tensor_parallel_consumer(tmp_path):
+    """One producer feeds an SAE whose latents are sharded over two consumer ranks: the consumer
+    root receives the rows and broadcasts them to its TP member."""
+    mp.spawn(_worker, args=(3, _port(), str(tmp_path), 1, 1, 2), nprocs=3, join=True)
+    r = [json.loads((tmp_path / f"r{i}.json").read_text()) for i in range(3)]
+    assert r[0]["role"] == "producer" and r[1]["role"] == r[2]["role"] == "consumer"
+    assert r[1]["steps"] == r[2]["steps"] == 8
