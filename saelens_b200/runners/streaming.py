@@ -74,18 +74,27 @@ def streaming_init(runner: Any) -> None:
         kw = dict(name=name, num_chunks=cfg.streaming_num_chunks, chunk_size_tokens=cfg.streaming_chunk_size_tokens * n_hooks,
                   d_model=cfg.sae.d_in, num_producers=vllm_dp, target_chunks=runner.target_chunks,
                   base_dir=getattr(cfg, "streaming_buffer_dir", "/dev/shm"))
-        if dist.get_rank() == 0 and not cfg.streaming_buffer_name:
-            runner.shm_buffer = SharedActivationBuffer(create=True, dtype=str_to_dtype(cfg.dtype)
-                                                       if str_to_dtype(cfg.dtype) in (torch.bfloat16, torch.float32)
-                                                       else torch.bfloat16, **kw)
+        exists = Path(kw["base_dir"], f"{name}.ctl").exists()
+        if dist.get_rank() == 0 and not exists:  # fresh run; a restart attaches (READY chunks kept)
+            dt = str_to_dtype(cfg.dtype)
+            runner.shm_buffer = SharedActivationBuffer(
+                create=True, dtype=dt if dt in (torch.bfloat16, torch.float32) else torch.bfloat16, **kw)
         dist.barrier()
         if runner.shm_buffer is None:
             runner.shm_buffer = SharedActivationBuffer(create=False, **kw)
 
 
+def _quiesce_dir(runner: Any) -> Path | None:
+    """Where quiesce requests and acks live: the supervisor's run directory when launched by it,
+    else the checkpoint directory."""
+    qdir = getattr(runner, "quiesce_dir", None)
+    if qdir is None and runner.cfg.checkpoint_path is not None:
+        qdir = runner.cfg.checkpoint_path
+    return Path(qdir) if qdir is not None else None
+
+
 def _quiesce_paths(runner: Any) -> tuple[Path | None, Path | None, Path | None]:
-    cfg = runner.cfg
-    qdir = Path(cfg.checkpoint_path) if cfg.checkpoint_path is not None else None
+    qdir = _quiesce_dir(runner)
     if qdir is None:
         return None, None, None
     pidx = ds.get_producer_idx()
@@ -98,6 +107,8 @@ def run_producer(runner: Any) -> int:
     pidx, P = ds.get_producer_idx(), runner.n_producers
     rows_per_chunk = cfg.streaming_chunk_size_tokens
     req, ack, state_dir = _quiesce_paths(runner)
+    if runner.resume_from_checkpoint is not None and state_dir is not None and state_dir.exists():
+        store.load_from_checkpoint(state_dir)  # continue this producer's dataset where it stopped
     written = 0
     seq = pidx
     while seq < runner.target_chunks:
@@ -209,8 +220,16 @@ def run_consumer(runner: Any) -> Any:
     trainer = SAETrainer(cfg=cfg.to_sae_trainer_config(), sae=runner.sae, base_sae=runner.sae, data_provider=provider,
                          evaluator=None, save_checkpoint_fn=None)
     runner.trainer = trainer
-    sae = trainer.fit()
-    if runner.ring is None or ds.get_sae_tp_rank() == 0:
+    if runner.resume_from_checkpoint is not None:
+        ck = Path(runner.resume_from_checkpoint)
+        runner.sae.load_weights_from_checkpoint(ck)
+        if trainer.engine is not None:
+            trainer.engine.refresh()
+        trainer.load_trainer_state(ck)
+    qdir = _quiesce_dir(runner)
+    sae = trainer.fit(quiesce_request_path=qdir / "quiesce_request" if qdir is not None else None,
+                      quiesce_ack_path=qdir / "quiesce_ack" if qdir is not None else None)
+    if not getattr(trainer, "quiesced", False) and (runner.ring is None or ds.get_sae_tp_rank() == 0):
         runner.save_final_sae(sae, trainer)
     return sae
 

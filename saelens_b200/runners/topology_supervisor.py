@@ -64,10 +64,14 @@ def find_free_port() -> int:
 
 def build_torchrun_cmd(worker_script: str, topo: TopologySpec, run_dir: Path, extra_args: list[str],
                        port: int | None = None) -> list[str]:
+    """torchrun command of one worker group; `worker_script` is a script path or `-m module`."""
+    target = worker_script.split() if worker_script.startswith("-m ") else [worker_script]
     return [
         sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={topo.world_size}",
-        "--master-addr", "127.0.0.1", f"--master-port={port or find_free_port()}", worker_script,
-        "--run-dir", str(run_dir), "--streaming-mode", *extra_args,
+        "--master-addr", "127.0.0.1", f"--master-port={port or find_free_port()}", *target,
+        "--run-dir", str(run_dir), "--streaming-mode", f"--vllm-tp-size={topo.vllm_tp}",
+        f"--vllm-dp-size={topo.vllm_dp}", f"--sae-tp-size={topo.sae_tp}", f"--sae-dp-size={max(topo.sae_dp, 1)}",
+        *extra_args,
     ]
 
 
@@ -257,7 +261,7 @@ def request_topology_switch(run_dir: str | Path, topology: TopologySpec) -> None
 def main(argv: list[str] | None = None) -> int:
     ap = argparse.ArgumentParser(description="Topology supervisor for streaming SAE training")
     ap.add_argument("--run-dir", required=True)
-    ap.add_argument("--worker-script", default="-m saelens_b200.runners.llm_sae_training_runner")
+    ap.add_argument("--worker-script", default="-m saelens_b200.runners.worker")
     ap.add_argument("--vllm-tp", type=int, default=1)
     ap.add_argument("--vllm-dp", type=int, default=1)
     ap.add_argument("--sae-tp", type=int, default=1)

@@ -267,13 +267,22 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
     def fit(self, quiesce_request_path: Path | str | None = None,
             quiesce_ack_path: Path | str | None = None) -> Any:
         self._prepare_fit()
+
+        def quiesce_if_requested() -> bool:
+            if quiesce_request_path is None or not Path(quiesce_request_path).exists():
+                return False
+            self.save_checkpoint(checkpoint_name=f"quiesce_{self.n_training_samples}")
+            if quiesce_ack_path is not None and self._is_metric_writer_rank():
+                Path(quiesce_ack_path).touch()
+            self.quiesced = True  # the run continues after a restart: no final checkpoint
+            return True
+
         while self.n_training_samples < self.cfg.total_training_samples:
             if not self._fit_one_step():
+                # the data can end because the producers quiesced first: quiesce, do not finish
+                quiesce_if_requested()
                 break
-            if quiesce_request_path is not None and Path(quiesce_request_path).exists():
-                self.save_checkpoint(checkpoint_name=f"quiesce_{self.n_training_samples}")
-                if quiesce_ack_path is not None and self._is_metric_writer_rank():
-                    Path(quiesce_ack_path).touch()
+            if quiesce_if_requested():
                 break
         return self._finish_fit()
 
@@ -334,6 +343,8 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
         return out
 
     def _finish_fit(self) -> Any:
+        if getattr(self, "quiesced", False):
+            return self._base_sae
         if self.activation_scaler.scaling_factor is not None:
             self._base_sae.fold_activation_norm_scaling_factor(self.activation_scaler.scaling_factor)
             if self.engine is not None:
