@@ -1,6 +1,6 @@
 """Headline benchmark: SAE-training tokens/s of a tensor-parallel TopK SAE on N B200s.
 
-Workload: TopK SAE, d_in 4096, d_sae 1,048,576 (sharded N-way over latents),
+Workload: the latent-sharded TopK SAE, d_in 4096, d_sae 1,048,576 (sharded N-way over latents),
 k 128, batch 16384 tokens per step, bf16 compute with fp32 master weights and fp32 Adam
 moments.  Inputs are synthetic activations ~N(0, 1) rescaled to norm sqrt(d_in); SAE weights
 are random-init.  Total work is fixed as N grows (strong scaling).
@@ -29,7 +29,7 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 METRIC = "SAE-train tokens/sec (device-timed, max over ranks)"
-BASELINE_VALUE = None  # the reference publishes no throughput number for this config
+PUBLISHED_VALUE = None  # the reference publishes no throughput number for this workload
 
 
 def _parse() -> argparse.Namespace:
@@ -147,7 +147,7 @@ def main() -> None:
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
             "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None if BASELINE_VALUE is None else value / BASELINE_VALUE,
+            "vs_baseline": None if PUBLISHED_VALUE is None else value / PUBLISHED_VALUE,
             "dtype": "bf16", "data": "synthetic: N(0,1) activations scaled to norm sqrt(d_in); random-init SAE",
             "config": {"model": f"TopK SAE d_in {args.d_in} d_sae {args.d_sae} k {args.k} (latent-sharded TP{world})",
                        "global_batch": args.batch, "seq_len": None, "parallelism": f"tp{world}" + (f"-{args.tp_exchange}" if world > 1 else ""),
