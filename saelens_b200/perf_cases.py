@@ -239,7 +239,7 @@ def ddp(args: argparse.Namespace) -> None:
 
 
 def ddp_hook(args: argparse.Namespace) -> None:
-    """PyTorch-path SAE under torch DDP (JumpReLU by default, the FSDP JumpReLU config's shape):
+    """PyTorch-path SAE under torch DDP (by default JumpReLU, d_in 3584, d_sae 131072, 4096 rows per GPU):
     gradient buckets averaged by the P2P all-reduce hook vs DDP's NCCL all-reduce.  Device time
     from CUDA events over the steps, max over ranks."""
     import torch
