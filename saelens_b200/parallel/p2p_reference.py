@@ -15,6 +15,10 @@ testable without GPUs:
 * `route_rows`           - ops/csrc/p2p.cu route_rows_kernel: producer rows to consumers by the
                            shard-routing table, normalised and cast to bf16, assembled in producer
                            order.
+* `fsdp_reduce_scatter`  - the gradient reduce-scatter of parallel/fsdp_engine.py (ops/csrc/sparse.cu
+                           latent_rows_kernel stores + ops/csrc/p2p.cu slot_reduce_kernel): rank r
+                           stores the bf16 row of latent j in slot [r][j - o*n] of owner o = j // n;
+                           the owner sums its S slots in rank order, times 1/S, rounded to bf16.
 * `sharded_batch_topk`   - the latent-sharded BatchTopK of parallel/tp_engine.py (ops/csrc/topk.cu
                            batch_* kernels): per-shard row candidates, summed 16-bit key histogram,
                            threshold, summed [S, B] tie counts, ties kept in (row, global latent)
@@ -135,6 +139,22 @@ def route_rows(x: torch.Tensor | None, producers: list[int], consumers: list[int
     return torch.cat(parts)
 
 
+def fsdp_reduce_scatter(grad_rows: torch.Tensor, group: dist.ProcessGroup | None = None) -> torch.Tensor:
+    """grad_rows [N, D]: this rank's gradient rows of every latent.  Returns this rank's shard
+    [N / S, D] of the rank-mean, with the kernels' rounding (bf16 parts, fp32 sum, bf16 result)."""
+    S, r = dist.get_world_size(group), dist.get_rank(group)
+    N, D = grad_rows.shape
+    n = N // S
+    mine = grad_rows.to(torch.bfloat16)
+    # slots[o][src] on the owner: every rank's rows of owner o's latents (an all-gather moves the
+    # same bytes on CPU ranks as the P2P stores into the owners' landing areas)
+    every = _gather_all(mine, group)
+    acc = torch.zeros(n, D, dtype=torch.float32)
+    for src in range(S):  # rank order, as the owner's slot reduce
+        acc += every[src][r * n : (r + 1) * n].float()
+    return (acc * (1.0 / S)).to(torch.bfloat16)
+
+
 def bf16_keys(v: torch.Tensor) -> torch.Tensor:
     """Order-preserving 16-bit keys of bf16 values (int64): positive values map above 0x8000."""
     b = v.to(torch.bfloat16).view(torch.int16).to(torch.int64) & 0xFFFF
@@ -184,4 +204,4 @@ def sharded_batch_topk(h_local: torch.Tensor, k_batch: float, k_cap: int,
 
 
 __all__ = ["two_shot_allreduce", "decode_reduce_scatter", "candidate_merge", "route_rows", "bf16_keys",
-           "sharded_batch_topk"]
+           "sharded_batch_topk", "fsdp_reduce_scatter"]

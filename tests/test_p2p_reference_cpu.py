@@ -49,6 +49,9 @@ def _worker(rank, world, port, out_dir):
     hg = torch.Generator().manual_seed(3)
     H = (torch.randint(-6, 10, (16, 12 * world), generator=hg).float() * 0.25)
     res["btk"] = R.sharded_batch_topk(H[:, rank * 12 : (rank + 1) * 12].contiguous(), 2.5, 8)
+    # FSDP reduce-scatter: rank-mean of every rank's gradient rows, sharded by latent owner
+    gr = torch.randn(8 * world, 16, generator=torch.Generator().manual_seed(40 + rank))
+    res["fsdp"] = R.fsdp_reduce_scatter(gr)
     torch.save(res, os.path.join(out_dir, f"r{rank}.pt"))
     dist.destroy_process_group()
 
@@ -103,3 +106,9 @@ def test_reference_algorithms(tmp_path, world):
     got = torch.cat([r[i]["btk"] for i in range(world)], dim=1).reshape(-1)
     assert int(got.sum()) == K
     assert torch.equal(got, want)
+    # FSDP reduce-scatter: the shards concatenate to the bf16-rounded mean of the ranks' rows
+    grs = [torch.randn(8 * world, 16, generator=torch.Generator().manual_seed(40 + i)).to(torch.bfloat16).float()
+           for i in range(world)]
+    mean = (sum(grs) / world).to(torch.bfloat16)
+    full = torch.cat([r[i]["fsdp"] for i in range(world)])
+    assert full.shape == (8 * world, 16) and torch.allclose(full.float(), mean.float(), atol=1e-2, rtol=1e-2)
