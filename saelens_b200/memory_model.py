@@ -12,6 +12,13 @@ adds a second gradient buffer plus the all-reduce slab (landing area and result)
 parallelism the exchange slab (full input rows, candidate lists, fp32 partial rows, dL/dx_hat).
 A producer LM adds its weights (split over producer TP ranks) and the activations of one forward.
 
+Sharded data parallel (`fsdp=True`, the FSDP engine over `sae_dp` ranks) keeps masters, moments and
+the reduced gradient rows for n = d_sae / sae_dp latents only, while the slab holds the full bf16
+W_enc and W_dec (gathered inside the encoder GEMM) and S landing slots of n gradient rows per
+matrix; H spans all d_sae latents.  The streaming ring (`ring_slots` x `ring_chunk_rows` bf16 rows)
+and the row router's double-buffered landing slots (`route_rows` per step) are symmetric slabs,
+allocated on every rank of their group.
+
 CLI: `python -m saelens_b200.memory_model --d-in 4096 --d-sae 1048576 --k 128 --batch 16384 --sae-tp 8`.
 """
 
@@ -47,13 +54,21 @@ class MemoryEstimate:
 def estimate(*, d_in: int, d_sae: int, k: int, batch: int, sae_tp: int = 1, sae_dp: int = 1,
              h_buffer_bytes: int = 8 << 30, aux_k: int | None = None, producer_params: int = 0,
              producer_tp: int = 1, producer_dtype_bytes: int = 2, producer_tokens: int = 0,
-             producer_d_model: int = 0, activation_buffer_rows: int = 0,
+             producer_d_model: int = 0, activation_buffer_rows: int = 0, fsdp: bool = False,
+             ring_slots: int = 0, ring_chunk_rows: int = 0, route_rows: int = 0,
              runtime_mb: float = 600.0) -> MemoryEstimate:
     """Memory of one rank.  `batch` is the number of rows this rank's SAE group trains on per step
     (the tensor-parallel group shares it); `aux_k` > 0 includes the dead-latent aux buffers."""
-    N = d_sae // sae_tp
     D = d_in
-    state = 6 * N * D * 4 + 2 * N * D * 2 + 2 * N * D * 2 + 16 * N * 4 + 8 * D * 4
+    if fsdp:
+        if sae_tp != 1:
+            raise ValueError("sharded data parallel does not combine with tensor parallelism")
+        N = d_sae  # the step works on every latent; the state below is per shard
+        n = d_sae // max(sae_dp, 1)
+        state = 6 * n * D * 4 + 2 * n * D * 2 + 16 * n * 4 + 8 * D * 4 + 6 * N * 4
+    else:
+        N = d_sae // sae_tp
+        state = 6 * N * D * 4 + 2 * N * D * 2 + 2 * N * D * 2 + 16 * N * 4 + 8 * D * 4
     rows_h = max(1, min(batch, (h_buffer_bytes // (2 * N)) // 128 * 128 or 128))
     h = rows_h * N * 2 * (1 + 1 / 16 + 1 / 128)
     kk = k
@@ -70,8 +85,12 @@ def estimate(*, d_in: int, d_sae: int, k: int, batch: int, sae_tp: int = 1, sae_
         slabs += batch * D * 2 + S * batch * kk * 8 + S * Bo * D * 4 + batch * D * 2 + batch * 16
         if aux_k:
             slabs += S * batch * aux_k * 8 + S * Bo * D * 4 + batch * D * 2
-    if sae_dp > 1:
+    if fsdp:
+        slabs += 2 * N * D * 2 + 2 * N * D * 2 + 3 * N * 4 * 2  # full bf16 weights, landing slots, vectors
+    elif sae_dp > 1:
         slabs += 2 * N * D * 2 * 3                  # local grads, landing area, averaged result
+    slabs += ring_slots * ring_chunk_rows * D * 2
+    slabs += 2 * route_rows * D * 2
     producer = 0.0
     if producer_params:
         producer += producer_params * producer_dtype_bytes / producer_tp
@@ -94,11 +113,16 @@ def main() -> None:
     p.add_argument("--producer-tokens", type=int, default=0)
     p.add_argument("--producer-d-model", type=int, default=0)
     p.add_argument("--activation-buffer-rows", type=int, default=0)
+    p.add_argument("--fsdp", action="store_true", help="sharded data parallel over --sae-dp ranks")
+    p.add_argument("--ring-slots", type=int, default=0)
+    p.add_argument("--ring-chunk-rows", type=int, default=0)
+    p.add_argument("--route-rows", type=int, default=0)
     a = p.parse_args()
     est = estimate(d_in=a.d_in, d_sae=a.d_sae, k=a.k, batch=a.batch, sae_tp=a.sae_tp, sae_dp=a.sae_dp,
                    aux_k=a.aux_k or None, producer_params=a.producer_params, producer_tp=a.producer_tp,
                    producer_tokens=a.producer_tokens, producer_d_model=a.producer_d_model,
-                   activation_buffer_rows=a.activation_buffer_rows)
+                   activation_buffer_rows=a.activation_buffer_rows, fsdp=a.fsdp, ring_slots=a.ring_slots,
+                   ring_chunk_rows=a.ring_chunk_rows, route_rows=a.route_rows)
     print(json.dumps(est.to_dict(), indent=2))
 
 

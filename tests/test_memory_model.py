@@ -38,3 +38,18 @@ def test_memory_model_matches_measured_step_peak():
     est = estimate(d_in=1024, d_sae=65536, k=64, batch=4096)
     model = (est.sae_state_mb + est.step_buffers_mb) * MB
     assert 0.8 < peak / model < 1.25, (peak / MB, model / MB)
+
+
+def test_memory_model_sharded_data_parallel_and_slabs():
+    kw = dict(d_in=3584, d_sae=131072, k=64, batch=4096)
+    ddp = estimate(sae_dp=8, **kw)
+    fsdp = estimate(sae_dp=8, fsdp=True, **kw)
+    # optimizer state per GPU is an eighth of a replica's; the slab carries the gathered weights
+    assert fsdp.sae_state_mb < ddp.sae_state_mb / 4
+    N, D = 131072, 3584
+    assert fsdp.parallel_slabs_mb * (1 << 20) >= 4 * N * D * 2
+    ring = estimate(ring_slots=32, ring_chunk_rows=4096, **kw)
+    base = estimate(**kw)
+    assert abs((ring.parallel_slabs_mb - base.parallel_slabs_mb) * (1 << 20) - 32 * 4096 * D * 2) < 1
+    routed = estimate(route_rows=4096, **kw)
+    assert abs((routed.parallel_slabs_mb - base.parallel_slabs_mb) * (1 << 20) - 2 * 4096 * D * 2) < 1
