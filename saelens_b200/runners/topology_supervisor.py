@@ -273,6 +273,20 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--exit-timeout-s", type=float, default=60.0)
     args, extra = ap.parse_known_args(argv)
     topo = TopologySpec(args.vllm_tp, args.vllm_dp, args.sae_tp, args.sae_dp)
+    buffer_params, target_chunks = None, 0
+    if extra:
+        # the ring's geometry and quota come from the workers' own config fields
+        import math
+
+        from saelens_b200.runners.worker import parse as parse_worker
+
+        extra = [*extra, "--streaming_buffer_dir", args.buffer_base_dir]
+        _, wcfg = parse_worker(extra)
+        n_hooks = len(wcfg.hook_names) if getattr(wcfg, "hook_names", None) else 1
+        buffer_params = BufferParams(wcfg.streaming_num_chunks, wcfg.streaming_chunk_size_tokens, wcfg.sae.d_in,
+                                     "float32" if wcfg.dtype in ("float32", "torch.float32") else "bfloat16",
+                                     num_hooks=n_hooks)
+        target_chunks = math.ceil(wcfg.training_tokens / wcfg.streaming_chunk_size_tokens)
     if topo.world_size > args.num_gpus:
         raise SystemExit(f"topology needs {topo.world_size} GPUs, only {args.num_gpus} available")
     run_dir = Path(args.run_dir)
@@ -283,7 +297,8 @@ def main(argv: list[str] | None = None) -> int:
             cmd += ["--resume-from-checkpoint", state.checkpoint_path]
         return subprocess.Popen(cmd, start_new_session=True)
 
-    sup = TopologySupervisor(run_dir, topo, launch, buffer_base_dir=args.buffer_base_dir, poll_s=args.poll_s,
+    sup = TopologySupervisor(run_dir, topo, launch, buffer_params=buffer_params, target_chunks=target_chunks,
+                             buffer_base_dir=args.buffer_base_dir, poll_s=args.poll_s,
                              exit_timeout_s=args.exit_timeout_s, resume_from_checkpoint=args.resume_from_checkpoint)
     return sup.run()
 

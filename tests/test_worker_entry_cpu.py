@@ -38,3 +38,25 @@ def test_supervisor_launches_worker_module_with_topology(tmp_path):
     for flag in ("--vllm-tp-size=1", "--vllm-dp-size=2", "--sae-tp-size=2", "--sae-dp-size=1", "--streaming-mode"):
         assert flag in cmd
     assert "--nproc-per-node=4" in cmd and cmd[-2:] == ["--k", "8"]
+
+
+def test_supervisor_main_derives_ring_geometry_from_worker_args(tmp_path, monkeypatch):
+    import saelens_b200.runners.topology_supervisor as ts
+
+    seen = {}
+
+    class FakeSup:
+        def __init__(self, run_dir, topo, launch, **kw):
+            seen.update(kw, topo=topo)
+
+        def run(self):
+            return 0
+
+    monkeypatch.setattr(ts, "TopologySupervisor", FakeSup)
+    rc = ts.main(["--run-dir", str(tmp_path), "--num-gpus", "2", "--buffer-base-dir", str(tmp_path),
+                  *_CFG, "--streaming_num_chunks", "8", "--streaming_chunk_size_tokens", "512",
+                  "--training_tokens", "5000"])
+    assert rc == 0
+    bp = seen["buffer_params"]
+    assert (bp.num_chunks, bp.chunk_size_tokens, bp.d_model) == (8, 512, 64)
+    assert seen["target_chunks"] == 10 and seen["buffer_base_dir"] == str(tmp_path)
