@@ -109,7 +109,6 @@ class FSDPTopKEngine(FusedTopKEngine):
         self.fire_f = torch.zeros(NF, dtype=torch.int32, device=dev)
         self.cursor_f = torch.zeros(NF, dtype=torch.int32, device=dev)
         self.colptr_f = torch.zeros(NF + 1, dtype=torch.int64, device=dev)
-        self.gb_enc_f = torch.zeros(NF, dtype=f32, device=dev)
         self.dense_colptr = torch.arange(n + 1, dtype=torch.int64, device=dev)
         self._ticket = torch.zeros(1, dtype=torch.int32, device=dev)
         self._epochs: dict[str, int] = {}
