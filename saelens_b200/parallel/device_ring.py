@@ -22,6 +22,7 @@ chunks taken, done flag) gives a supervisor a view of the ring without touching 
 from __future__ import annotations
 
 import time
+from collections.abc import Callable
 from pathlib import Path
 
 import numpy as np
@@ -96,7 +97,8 @@ class DeviceActivationRing:
             self.header = HostRingHeader(header_path, self.world, self.rank, create=False)
 
     # ------------------------------------------------------------------ helpers
-    def _claim(self, owner: int, frm: int, to: int, start: int, timeout_s: float, what: str) -> int:
+    def _claim(self, owner: int, frm: int, to: int, start: int, timeout_s: float, what: str,
+               stop_check: Callable[[], bool] | None = None) -> int | None:
         t0 = time.monotonic()
         while True:
             self.nat.ring_claim(self.heap.bases, self.rank, owner, self.state.offset, self.n_slots, frm, to, start,
@@ -104,6 +106,8 @@ class DeviceActivationRing:
             s = int(self.slot.item())
             if s >= 0:
                 return s
+            if stop_check is not None and stop_check():
+                return None
             if time.monotonic() - t0 > timeout_s:
                 raise TimeoutError(f"device ring: no {what} slot within {timeout_s:.1f} s")
 
@@ -115,16 +119,20 @@ class DeviceActivationRing:
         return self.heap.local(self.meta)
 
     # ------------------------------------------------------------------ producer
-    def write(self, x: torch.Tensor, timeout_s: float = 60.0) -> int:
+    def write(self, x: torch.Tensor, timeout_s: float = 60.0,
+              stop_check: Callable[[], bool] | None = None) -> int | None:
         """Store `x` ([rows <= chunk_rows, d], fp32 or bf16, on this GPU) as one READY chunk.
-        Returns the slot used.  Blocks (bounded waits, host retries) while the ring is full."""
+        Returns the slot used.  Blocks (bounded waits, host retries) while the ring is full;
+        returns None without writing when `stop_check()` turns true meanwhile."""
         if self.rank not in self.producers:
             raise RuntimeError(f"rank {self.rank} is not a producer of this ring")
         if x.dim() != 2 or x.shape[1] != self.d or x.shape[0] > self.chunk_rows:
             raise ValueError(f"chunk must be [<= {self.chunk_rows}, {self.d}]")
         p_idx = self.producers.index(self.rank)
         start = (self.seq * len(self.producers) + p_idx) % self.n_slots
-        slot = self._claim(self.consumer, FREE, WRITING, start, timeout_s, "FREE")
+        slot = self._claim(self.consumer, FREE, WRITING, start, timeout_s, "FREE", stop_check)
+        if slot is None:
+            return None
         self.nat.ring_write(x.contiguous(), self.heap.bases, self.rank, self.consumer, self.data.offset,
                             self.chunk_rows, self.slot, self.mode, self.scale)
         self.nat.ring_publish(self.heap.bases, self.rank, self.consumer, self.state.offset, self.meta.offset,
@@ -151,6 +159,7 @@ class DeviceActivationRing:
             raise RuntimeError(f"rank {self.rank} is not the consumer of this ring")
         start = (self.taken * 5 + 3) % self.n_slots
         slot = self._claim(self.rank, READY, CONSUMING, start, timeout_s, "READY")
+        assert slot is not None
         rows = int(self.local_meta()[slot, 0].item())
         if perm is None and shuffle is not None:
             perm = torch.randperm(rows, device=self.heap.device, generator=shuffle, dtype=torch.int32)

@@ -109,24 +109,35 @@ def run_producer(runner: Any) -> int:
     req, ack, state_dir = _quiesce_paths(runner)
     if runner.resume_from_checkpoint is not None and state_dir is not None and state_dir.exists():
         store.load_from_checkpoint(state_dir)  # continue this producer's dataset where it stopped
+    def requested() -> bool:
+        return req is not None and req.exists()
+
+    def quiesce() -> None:
+        if state_dir is not None:
+            state_dir.mkdir(parents=True, exist_ok=True)
+            store.save_to_checkpoint(state_dir)
+        if ack is not None:
+            ack.touch()
+
     written = 0
     seq = pidx
     while seq < runner.target_chunks:
-        if req is not None and req.exists():
-            if state_dir is not None:
-                state_dir.mkdir(parents=True, exist_ok=True)
-                store.save_to_checkpoint(state_dir)
-            if ack is not None:
-                ack.touch()
+        if requested():
+            quiesce()
             break
         rows = max(1, min(rows_per_chunk, cfg.training_tokens - seq * rows_per_chunk))
         acts, valid = store.get_streaming_activations(rows)
+        # a full ring blocks the producer; the quiesce request must still reach it there
         if runner.ring is not None:
-            runner.ring.write(acts)
+            if runner.ring.write(acts, stop_check=requested) is None:
+                quiesce()
+                break
         else:
             buf = runner.shm_buffer
-            got = buf.allocate_write_chunk()
+            got = buf.allocate_write_chunk(stop_check=requested)
             if got is None:
+                if requested():
+                    quiesce()
                 break
             idx, _ = got
             buf.write_chunk(idx, acts.detach().to("cpu"), valid, producer_id=pidx)
