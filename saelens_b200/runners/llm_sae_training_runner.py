@@ -101,7 +101,13 @@ class LanguageModelSAETrainingRunner:
                                                                   shard_index=shard, num_shards=nshard)
         self.sae: Any = None
         self.wrapped: Any = None
-        if consumer_side:
+        self.hook_names = list(cfg.hook_names) if cfg.hook_names else [cfg.hook_name]
+        self.is_multi_sae = len(self.hook_names) > 1
+        self.sae_by_hook: dict[str, Any] = {}
+        self.base_sae_by_hook: dict[str, Any] = {}
+        if consumer_side and self.is_multi_sae:
+            self._init_multi_saes()
+        elif consumer_side:
             self.sae = override_sae if override_sae is not None else self._build_sae()
             if self.tp_group is not None and hasattr(self.sae, "shard_weights"):
                 self.sae.shard_weights(self.tp_group)
@@ -151,6 +157,62 @@ class LanguageModelSAETrainingRunner:
             torch.manual_seed(cfg.seed)
             sae = get_sae_training_class(sae_cfg.architecture())[0](sae_cfg)
         return sae
+
+    def _init_multi_saes(self) -> None:
+        """One SAE per hook, trained from one LM pass (sae_lens/llm_sae_training_runner.py:489-584):
+        the same seed for every hook ("same") or seed + index ("offset"); each SAE records its hook
+        in the metadata, is sharded for TP and wrapped for DDP / FSDP like a single SAE."""
+        cfg = self.cfg
+        if cfg.streaming_mode or self.routed:
+            raise ValueError("multi-hook training runs on the non-routed data path")
+        for idx, hook in enumerate(self.hook_names):
+            seed = cfg.seed if cfg.multi_sae_seed_mode == "same" else cfg.seed + idx
+            sae_cfg = type(cfg.sae).from_sae_runner_config(cfg)
+            sae_cfg.device = cfg.device
+            sae_cfg.dtype = cfg.dtype
+            torch.manual_seed(seed)
+            sae = get_sae_training_class(sae_cfg.architecture())[0](sae_cfg)
+            sae.cfg.metadata.hook_name = hook
+            if self.tp_group is not None and hasattr(sae, "shard_weights"):
+                sae.shard_weights(self.tp_group)
+            self.base_sae_by_hook[hook] = sae
+            if self.dp_group is not None and cfg.sae_dp_mode == "fsdp":
+                from torch.distributed.fsdp import FullyShardedDataParallel as FSDP
+                from torch.distributed.fsdp import ShardingStrategy
+
+                self.sae_by_hook[hook] = FSDP(sae, process_group=self.dp_group,
+                                              sharding_strategy=ShardingStrategy.FULL_SHARD, use_orig_params=True,
+                                              device_id=sae.W_dec.device if sae.W_dec.is_cuda else None)
+            elif self.dp_group is not None and cfg.sae_dp_mode == "ddp":
+                from torch.nn.parallel import DistributedDataParallel as DDP
+
+                kw: dict[str, Any] = {"process_group": self.dp_group}
+                if sae.W_dec.is_cuda:
+                    kw["device_ids"] = [sae.W_dec.device.index]
+                self.sae_by_hook[hook] = DDP(sae, **kw)
+            else:
+                self.sae_by_hook[hook] = sae
+
+    def _run_multi(self) -> dict[str, Any]:
+        from saelens_b200.training.multi_sae_trainer import MultiSAETrainer
+
+        cfg = self.cfg
+        trainer = MultiSAETrainer(
+            hook_names=self.hook_names, sae_by_hook=self.sae_by_hook, base_sae_by_hook=self.base_sae_by_hook,
+            data_provider=self.activations_store, cfg=cfg.to_sae_trainer_config(), dp_group=self.dp_group,
+            token_count_weighted_dp=self.token_count_weighted_dp, sae_dp_mode=cfg.sae_dp_mode,
+            backward_mode=cfg.multi_sae_backward_mode, seed_mode=cfg.multi_sae_seed_mode)
+        self.trainer = trainer
+        if self.resume_from_checkpoint is not None:
+            trainer.load_trainer_state(self.resume_from_checkpoint)
+            if (Path(self.resume_from_checkpoint) / ACTIVATIONS_STORE_STATE_FILENAME).exists():
+                self.activations_store.load_from_checkpoint(self.resume_from_checkpoint)
+        result = trainer.fit()
+        if cfg.output_path is not None and self._is_writer():
+            trainer.save_final(cfg.output_path)
+            with open(Path(cfg.output_path) / RUNNER_CFG_FILENAME, "w") as f:
+                json.dump(cfg.to_dict(), f, default=str)
+        return result
 
     def _native_fsdp_ok(self, sae: TrainingSAE[Any]) -> bool:
         """TopK / BatchTopK on CUDA with the native ops, at most 8 NCCL ranks (one NVSwitch
@@ -204,6 +266,8 @@ class LanguageModelSAETrainingRunner:
             return run_streaming(self)
         if self.routed:
             return self._run_routed()
+        if self.is_multi_sae:
+            return self._run_multi()
         if cfg.logger.log_to_wandb and self._is_writer():
             from saelens_b200.utils import wandb_shim as wandb
 

@@ -107,3 +107,22 @@ def test_run_evals_metrics(tmp_path):
     m2, _ = run_evals(id_sae, store, lm, get_eval_everything_config(4, 1, 1))
     assert m2["model_performance_preservation"]["ce_loss_score"] == pytest.approx(1.0, abs=1e-4)
     assert m2["reconstruction_quality"]["explained_variance"] == pytest.approx(1.0, abs=1e-5)
+
+
+def test_runner_multi_hook_trains_one_sae_per_hook(tmp_path):
+    from saelens_b200.runners.llm_sae_training_runner import LanguageModelSAETrainingRunner
+    from saelens_b200.training.multi_sae_trainer import sanitize_hook_name_for_path
+
+    hooks = ["blocks.0.hook_resid_pre", "blocks.1.hook_resid_pre"]
+    cfg = _cfg(tmp_path, hook_names=hooks, training_tokens=64 * 10, multi_sae_seed_mode="offset")
+    runner = LanguageModelSAETrainingRunner(cfg, override_model=_tiny_lm())
+    out_saes = runner.run()
+    assert set(out_saes) == set(hooks)
+    w = [out_saes[h].W_dec.detach().clone() for h in hooks]
+    assert not torch.equal(w[0], w[1])  # offset seeds and different inputs
+    for h in hooks:
+        d = tmp_path / "out" / sanitize_hook_name_for_path(h)
+        loaded = SAE.load_from_disk(d)
+        assert loaded.cfg.metadata.hook_name == h and loaded.cfg.d_sae == 128
+    assert runner.trainer.n_training_steps == 10
+    assert (tmp_path / "out" / "runner_cfg.json").exists()
