@@ -88,6 +88,8 @@ class LanguageModelSAETrainingRunner:
         self.activations_store: Any = None
         if producer_side:
             self.model = override_model if override_model is not None else self._load_model()
+            if cfg.compile_llm:
+                self.model = torch.compile(self.model, mode=cfg.llm_compilation_mode)
             if self.streaming_mode:
                 shard, nshard = self._streaming_producer_shard()
             elif self.routed:
@@ -111,6 +113,7 @@ class LanguageModelSAETrainingRunner:
             self.sae = override_sae if override_sae is not None else self._build_sae()
             if self.tp_group is not None and hasattr(self.sae, "shard_weights"):
                 self.sae.shard_weights(self.tp_group)
+            self._compile_sae_if_needed(self.sae)
             self.wrapped = self._wrap_dp(self.sae)
 
     # ---------------------------------------------------------------- setup
@@ -158,6 +161,12 @@ class LanguageModelSAETrainingRunner:
             sae = get_sae_training_class(sae_cfg.architecture())[0](sae_cfg)
         return sae
 
+    def _compile_sae_if_needed(self, sae: Any) -> None:
+        """`compile_sae`: compile the SAE's training forward before any DP wrapping (the PyTorch
+        path; the native engines do not run it)."""
+        if self.cfg.compile_sae:
+            sae.training_forward_pass = torch.compile(sae.training_forward_pass, mode=self.cfg.sae_compilation_mode)
+
     def _init_multi_saes(self) -> None:
         """One SAE per hook, trained from one LM pass (sae_lens/llm_sae_training_runner.py:489-584):
         the same seed for every hook ("same") or seed + index ("offset"); each SAE records its hook
@@ -175,6 +184,7 @@ class LanguageModelSAETrainingRunner:
             sae.cfg.metadata.hook_name = hook
             if self.tp_group is not None and hasattr(sae, "shard_weights"):
                 sae.shard_weights(self.tp_group)
+            self._compile_sae_if_needed(sae)
             self.base_sae_by_hook[hook] = sae
             if self.dp_group is not None and cfg.sae_dp_mode == "fsdp":
                 from torch.distributed.fsdp import FullyShardedDataParallel as FSDP

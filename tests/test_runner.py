@@ -126,3 +126,20 @@ def test_runner_multi_hook_trains_one_sae_per_hook(tmp_path):
         assert loaded.cfg.metadata.hook_name == h and loaded.cfg.d_sae == 128
     assert runner.trainer.n_training_steps == 10
     assert (tmp_path / "out" / "runner_cfg.json").exists()
+
+
+def test_runner_compile_flags(tmp_path, monkeypatch):
+    from saelens_b200.runners.llm_sae_training_runner import LanguageModelSAETrainingRunner
+
+    calls = []
+
+    def fake_compile(fn, mode=None, **kw):
+        calls.append((getattr(fn, "__name__", type(fn).__name__), mode))
+        return fn
+
+    monkeypatch.setattr(torch, "compile", fake_compile)
+    cfg = _cfg(tmp_path, compile_llm=True, llm_compilation_mode="max-autotune-no-cudagraphs", compile_sae=True,
+               sae_compilation_mode="max-autotune")
+    LanguageModelSAETrainingRunner(cfg, override_model=_tiny_lm())
+    assert ("HookedLM", "max-autotune-no-cudagraphs") in calls
+    assert ("training_forward_pass", "max-autotune") in calls
