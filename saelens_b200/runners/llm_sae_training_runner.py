@@ -79,6 +79,7 @@ class LanguageModelSAETrainingRunner:
             routing_init(self)  # v2 layout, roles and the row router (collective)
         else:
             self._init_distributed()
+        self._sync_run_paths_across_ranks()
         if self.routed:
             producer_side, consumer_side = self.is_route_producer, self.is_route_consumer
         else:
@@ -160,6 +161,15 @@ class LanguageModelSAETrainingRunner:
             torch.manual_seed(cfg.seed)
             sae = get_sae_training_class(sae_cfg.architecture())[0](sae_cfg)
         return sae
+
+    def _sync_run_paths_across_ranks(self) -> None:
+        """Every rank uses rank 0's output and checkpoint paths (default paths carry a timestamp,
+        which differs between processes started a second apart)."""
+        if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+            return
+        paths = [self.cfg.output_path, self.cfg.checkpoint_path]
+        dist.broadcast_object_list(paths, src=0)
+        self.cfg.output_path, self.cfg.checkpoint_path = paths
 
     def _compile_sae_if_needed(self, sae: Any) -> None:
         """`compile_sae`: compile the SAE's training forward before any DP wrapping (the PyTorch

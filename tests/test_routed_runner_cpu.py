@@ -42,8 +42,11 @@ def _worker(rank, world, port, tmp, P, Q, tp=1):
         training_tokens=64 * 8, train_batch_size_tokens=64, store_batch_size_prompts=4, n_batches_in_buffer=2,
         output_path=os.path.join(tmp, "out"), logger=LoggingConfig(log_to_wandb=False), device="cpu",
         save_mse_every_n_steps=1, n_checkpoints=0, verbose=False, routing_transport="collective")
+    if rank == 1:  # a rank with other paths (e.g. another timestamp) follows rank 0
+        cfg.checkpoint_path = os.path.join(tmp, "elsewhere")
     runner = LanguageModelSAETrainingRunner(cfg, override_model=lm, vllm_dp_size=P, sae_dp_size=Q,
                                             sae_tp_size=tp, use_shard_routing=True)
+    assert cfg.checkpoint_path != os.path.join(tmp, "elsewhere")
     out = runner.run()
     info = {"role": runner.role, "transport": runner.routing_transport}
     if out is not None:
