@@ -80,8 +80,19 @@ class LanguageModelSAETrainingRunner:
         else:
             self._init_distributed()
         self._sync_run_paths_across_ranks()
+        self.fan_in = False
+        if not (self.streaming_mode or self.routed) and dist.is_available() and dist.is_initialized():
+            from saelens_b200.parallel import distributed as D
+
+            if D.get_layout_mode() == "vllm_dp_fan_in":  # legacy m:1 / mn:m producers -> SAE roots
+                if self.sae_tp_size > 1:
+                    raise ValueError("the fan-in data path serves SAE TP 1; use shard routing for TP consumers")
+                self.fan_in = True
+                self.role = "producer+consumer" if D.is_sae_active() else "producer"
         if self.routed:
             producer_side, consumer_side = self.is_route_producer, self.is_route_consumer
+        elif self.fan_in:
+            producer_side, consumer_side = True, self.role == "producer+consumer"
         else:
             producer_side = self.role in (None, "producer")
             consumer_side = self.role in (None, "consumer")
@@ -98,6 +109,10 @@ class LanguageModelSAETrainingRunner:
 
                 n = max(self.vllm_dp_size, 1)
                 shard, nshard = (v2.get_producer_idx(), n) if n > 1 else (0, 1)
+            elif self.fan_in:
+                from saelens_b200.parallel import distributed as D
+
+                shard, nshard = D.get_vllm_dp_rank(), max(self.vllm_dp_size, 1)
             else:
                 shard, nshard = (self._dp_rank(), self.sae_dp_size) if self.sae_dp_size > 1 else (0, 1)
             self.activations_store = ActivationsStore.from_config(self.model, cfg, override_dataset=override_dataset,
@@ -127,7 +142,7 @@ class LanguageModelSAETrainingRunner:
 
     def _init_distributed(self) -> None:
         world = int(os.environ.get("WORLD_SIZE", "1"))
-        if world <= 1 or (self.sae_tp_size == 1 and self.sae_dp_size == 1):
+        if world <= 1 or (self.sae_tp_size == 1 and self.sae_dp_size == 1 and self.vllm_dp_size <= 1):
             return
         if not dist.is_initialized():
             backend = "nccl" if self.cfg.device.startswith("cuda") else "gloo"
@@ -288,6 +303,32 @@ class LanguageModelSAETrainingRunner:
             return self._run_routed()
         if self.is_multi_sae:
             return self._run_multi()
+        if self.fan_in:
+            return self._run_fan_in()
+        return self._run_standard()
+
+    def _run_fan_in(self) -> Any:
+        """Fan-in: helpers serve activation batches to their cluster's SAE root."""
+        from saelens_b200.parallel import distributed as D
+        from saelens_b200.runners.fan_in import FanInRoot, run_helper
+
+        group = D.get_vllm_dp_p2p_group()
+        root = D.get_sae_root_rank()
+        sae = None
+        if self.role == "producer":
+            run_helper(self.activations_store, root, group)
+        else:
+            block = D.get_cluster_block()
+            fan = FanInRoot(self.activations_store, [root + i for i in range(1, block)], group)
+            try:
+                sae = self._run_standard()
+            finally:
+                fan.close()
+        dist.barrier()
+        return sae
+
+    def _run_standard(self) -> Any:
+        cfg = self.cfg
         if cfg.logger.log_to_wandb and self._is_writer():
             from saelens_b200.utils import wandb_shim as wandb
 
