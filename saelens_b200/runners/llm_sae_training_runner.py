@@ -380,7 +380,7 @@ class LanguageModelSAETrainingRunner:
 
     def _run_routed(self) -> Any:
         """Shard-routing mode: producers feed the consumers' trainers step by step."""
-        from saelens_b200.runners.routing import RoutedExchange, RoutedProvider, run_producer_only
+        from saelens_b200.runners.routing import RoutedExchange, RoutedProvider, resume_state, run_producer_only
 
         cfg = self.cfg
         n_steps = cfg.total_training_steps
@@ -389,12 +389,19 @@ class LanguageModelSAETrainingRunner:
             run_producer_only(self, n_steps)
         else:
             ex = RoutedExchange(self)
+            done = resume_state(self, ex)
             trainer = SAETrainer(
                 cfg=cfg.to_sae_trainer_config(), sae=self.wrapped, base_sae=self.sae,
-                data_provider=RoutedProvider(ex, n_steps), evaluator=None,
+                data_provider=RoutedProvider(ex, n_steps - done), evaluator=None,
                 save_checkpoint_fn=self._save_checkpoint_extras if self.activations_store is not None else None,
                 dp_group=self.dp_group, native_fsdp=self.native_fsdp)
             self.trainer = trainer
+            if self.resume_from_checkpoint is not None:
+                ck = Path(self.resume_from_checkpoint)
+                self.sae.load_weights_from_checkpoint(ck)
+                if trainer.engine is not None:
+                    trainer.engine.refresh()
+                trainer.load_trainer_state(ck)
             sae = trainer.fit()
             ex.finish()
             self.save_final_sae(sae, trainer)

@@ -20,7 +20,9 @@ Transports:
 
 from __future__ import annotations
 
+import math
 import os
+from pathlib import Path
 from typing import Any
 
 import torch
@@ -107,12 +109,32 @@ class RoutedExchange:
         self.dev = torch.device(self.cfg.device if str(self.cfg.device) != "cuda" else f"cuda:{torch.cuda.current_device()}")
         self._pending_release = False
         self.rank = dist.get_rank()
+        # producers save their dataset position where the consumers' trainer checkpoints: after
+        # the same steps (same thresholds), into the same directory, so a resume restarts both
+        self.done_steps = 0
+        self.produced = 0
+        self._thresholds: list[int] = []
+        if self.source is not None and self.cfg.n_checkpoints > 0 and self.cfg.checkpoint_path is not None:
+            total = self.cfg.total_training_tokens
+            stride = math.ceil(total / (self.cfg.n_checkpoints + 1))
+            self._thresholds = list(range(0, total, stride))[1:]
+
+    def _after_produce(self) -> None:
+        self.produced += 1
+        n = (self.done_steps + self.produced) * self.cfg.train_batch_size_tokens
+        while self._thresholds and n > self._thresholds[0]:
+            d = Path(self.cfg.checkpoint_path) / str(n) / f"producer_dataset_state_{self.p_idx}"
+            d.mkdir(parents=True, exist_ok=True)
+            self.r.activations_store.save_to_checkpoint(d)
+            self._thresholds.pop(0)
 
     def _produce(self) -> torch.Tensor | None:
         return self.source.take(self.r.route_batch) if self.source is not None else None
 
     def step(self) -> torch.Tensor | None:
         rows = self._produce()
+        if rows is not None:
+            self._after_produce()
         if self.r.router is not None:
             return self._step_p2p(rows)
         return self._step_collective(rows)
@@ -192,11 +214,33 @@ class RoutedProvider:
         return batch
 
 
+def resume_state(runner: Any, ex: RoutedExchange) -> int:
+    """Steps already trained in the resume checkpoint (0 without one); the producer side reloads
+    its dataset position from the checkpoint and skips the checkpoint thresholds already passed."""
+    ck = runner.resume_from_checkpoint
+    if ck is None:
+        return 0
+    from saelens_b200.constants import TRAINER_STATE_FILENAME
+
+    st = torch.load(Path(ck) / TRAINER_STATE_FILENAME, map_location="cpu", weights_only=False)
+    # samples, not the step counter: a checkpoint is written before its step is counted
+    done = int(st.get("n_training_samples", 0)) // runner.cfg.train_batch_size_tokens
+    ex.done_steps = done
+    n_done = done * runner.cfg.train_batch_size_tokens
+    ex._thresholds = [t for t in ex._thresholds if t >= n_done]
+    if ex.source is not None:
+        state = Path(ck) / f"producer_dataset_state_{ex.p_idx}"
+        if state.exists():
+            runner.activations_store.load_from_checkpoint(state)
+    return done
+
+
 def run_producer_only(runner: Any, n_steps: int) -> None:
     ex = RoutedExchange(runner)
-    for _ in range(n_steps):
+    done = resume_state(runner, ex)
+    for _ in range(n_steps - done):
         ex.step()
     ex.finish()
 
 
-__all__ = ["RoutedExchange", "RoutedProvider", "routing_init", "run_producer_only"]
+__all__ = ["RoutedExchange", "RoutedProvider", "resume_state", "routing_init", "run_producer_only"]

@@ -78,3 +78,52 @@ def test_routed_runner_to_tensor_parallel_consumer(tmp_path):
     r = [json.loads((tmp_path / f"r{i}.json").read_text()) for i in range(3)]
     assert r[0]["role"] == "producer" and r[1]["role"] == r[2]["role"] == "consumer"
     assert r[1]["steps"] == r[2]["steps"] == 8
+
+
+def _resume_worker(rank, world, port, tmp, phase):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from saelens_b200.config import LanguageModelSAERunnerConfig, LoggingConfig
+    from saelens_b200.models.lm import HookedLM, preset_config
+    from saelens_b200.models.standard import StandardTrainingSAEConfig
+    from saelens_b200.runners.llm_sae_training_runner import LanguageModelSAETrainingRunner
+
+    torch.manual_seed(0)
+    lm = HookedLM(preset_config("gpt2", n_layers=2, d_model=64, n_heads=4, d_mlp=128, d_vocab=500, n_ctx=64,
+                                dtype="float32"))
+    cfg = LanguageModelSAERunnerConfig(
+        sae=StandardTrainingSAEConfig(d_in=64, d_sae=128, l1_coefficient=1e-3), model_name="gpt2",
+        hook_name="blocks.1.hook_resid_pre", dataset_path="synthetic:uniform:500:32", context_size=16,
+        training_tokens=64 * 8, train_batch_size_tokens=64, store_batch_size_prompts=4, n_batches_in_buffer=2,
+        output_path=os.path.join(tmp, f"out{phase}"), checkpoint_path=os.path.join(tmp, "ckpt"),
+        logger=LoggingConfig(log_to_wandb=False), device="cpu", n_checkpoints=1, save_final_checkpoint=False,
+        verbose=False, routing_transport="collective")
+    resume = None
+    if phase == 2:  # the config adds a run id under checkpoint_path
+        from pathlib import Path
+
+        resume = str(next(Path(tmp, "ckpt").glob("*/320")))
+    runner = LanguageModelSAETrainingRunner(cfg, override_model=lm, vllm_dp_size=1, sae_dp_size=1,
+                                            use_shard_routing=True, resume_from_checkpoint=resume)
+    runner.run()
+    if runner.role == "consumer":
+        with open(os.path.join(tmp, f"steps{phase}.json"), "w") as f:
+            json.dump({"samples": runner.trainer.n_training_samples,
+                       "mse_rows": len(runner.trainer.mse_history_path.read_text().splitlines())
+                       if runner.trainer.mse_history_path else None}, f)
+    dist.destroy_process_group()
+
+
+def test_routed_runner_checkpoint_and_resume(tmp_path):
+    mp.spawn(_resume_worker, args=(2, _port(), str(tmp_path), 1), nprocs=2, join=True)
+    ck = next((tmp_path / "ckpt").glob("*/320"))
+    assert (ck / "trainer_state.pt").exists() and (ck / "producer_dataset_state_0").exists()
+    mp.spawn(_resume_worker, args=(2, _port(), str(tmp_path), 2), nprocs=2, join=True)
+    # the resumed run trains the 3 remaining steps (samples 320 -> 512); the producer sends exactly
+    # those, so nothing waits on a send that is never received
+    st = json.loads((tmp_path / "steps2.json").read_text())
+    assert st["samples"] == 512
+    assert (tmp_path / "out2" / "sae_weights.safetensors").exists()
