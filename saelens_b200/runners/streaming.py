@@ -121,6 +121,16 @@ def run_producer(runner: Any) -> int:
 
     written = 0
     seq = pidx
+    if runner.ring is not None and runner.resume_from_checkpoint is not None:
+        # the device ring starts empty after a restart: skip the chunks the consumer's checkpoint
+        # already trained on (the /dev/shm ring keeps its own claim counter instead)
+        from saelens_b200.constants import TRAINER_STATE_FILENAME
+
+        st_path = Path(runner.resume_from_checkpoint) / TRAINER_STATE_FILENAME
+        if st_path.exists():
+            st = torch.load(st_path, map_location="cpu", weights_only=False)
+            consumed = int(st.get("n_training_samples", 0)) // rows_per_chunk
+            seq = pidx + ((max(consumed - pidx, 0) + P - 1) // P) * P
     while seq < runner.target_chunks:
         if requested():
             quiesce()
