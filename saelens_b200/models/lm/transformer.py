@@ -20,7 +20,7 @@ GEMM (`saelens_b200.ops.gemm_tn`); attention uses `scaled_dot_product_attention`
 from __future__ import annotations
 
 import math
-from dataclasses import asdict, dataclass, field
+from dataclasses import asdict, dataclass
 from typing import Any
 
 import torch
