@@ -204,8 +204,10 @@ class LanguageModelSAETrainingRunner:
             sae_cfg = type(cfg.sae).from_sae_runner_config(cfg)
             sae_cfg.device = cfg.device
             sae_cfg.dtype = cfg.dtype
-            torch.manual_seed(seed)
-            sae = get_sae_training_class(sae_cfg.architecture())[0](sae_cfg)
+            from saelens_b200.utils.misc import temporary_seed
+
+            with temporary_seed(seed):  # the global RNG stream is left as it was
+                sae = get_sae_training_class(sae_cfg.architecture())[0](sae_cfg)
             sae.cfg.metadata.hook_name = hook
             if self.tp_group is not None and hasattr(sae, "shard_weights"):
                 sae.shard_weights(self.tp_group)

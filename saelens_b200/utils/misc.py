@@ -83,6 +83,33 @@ def extract_stop_at_layer_from_hook_name(hook_name: str) -> int | None:
     return None
 
 
+def extract_layer_from_tlens_hook_name(hook_name: str) -> int | None:
+    """The layer index of a TransformerLens-style hook name (`blocks.6.hook_resid_pre` -> 6): the
+    first dot-delimited all-digit component, or None."""
+    for part in hook_name.split(".")[1:-1]:
+        if part.isdigit():
+            return int(part)
+    return None
+
+
+def extract_stop_at_layer_from_tlens_hook_name(hook_name: str) -> int | None:
+    """The `stop_at_layer` that still runs the hook's layer (layer + 1), or None."""
+    layer = extract_layer_from_tlens_hook_name(hook_name)
+    return None if layer is None else layer + 1
+
+
+@contextmanager
+def temporary_seed(seed: int | None) -> Iterator[None]:
+    """Seed torch's global RNG inside the block only (CPU and CUDA states are restored after);
+    `None` leaves the RNG alone."""
+    if seed is None:
+        yield
+        return
+    with torch.random.fork_rng():
+        torch.manual_seed(seed)
+        yield
+
+
 def cosine_similarities(a: torch.Tensor, b: torch.Tensor | None = None) -> torch.Tensor:
     """Pairwise cosine similarities between the rows of a [n, d] and b [m, d] (b defaults to a)."""
     a_n = a / a.norm(dim=-1, keepdim=True).clamp(min=1e-12)

@@ -128,3 +128,24 @@ def test_bridge_boots_hf_model_and_splices_sae():
         spliced = br.run_with_saes(toks, saes=[sae], use_error_term=True)
     assert torch.allclose(spliced, ref, atol=1e-3)  # error term restores the clean activations
     assert br.acts_to_saes == {}
+
+
+def test_hook_name_layer_helpers_and_temporary_seed():
+    from saelens_b200.utils.misc import (
+        extract_layer_from_tlens_hook_name,
+        extract_stop_at_layer_from_tlens_hook_name,
+        temporary_seed,
+    )
+
+    assert extract_layer_from_tlens_hook_name("blocks.12.hook_resid_pre") == 12
+    assert extract_layer_from_tlens_hook_name("blocks.3.attn.hook_z") == 3
+    assert extract_layer_from_tlens_hook_name("hook_embed") is None
+    assert extract_stop_at_layer_from_tlens_hook_name("blocks.12.hook_resid_pre") == 13
+    assert extract_stop_at_layer_from_tlens_hook_name("ln_final.hook_normalized") is None
+    torch.manual_seed(0)
+    before = torch.random.get_rng_state()
+    with temporary_seed(123):
+        a = torch.rand(3)
+    with temporary_seed(123):
+        b = torch.rand(3)
+    assert torch.equal(a, b) and torch.equal(torch.random.get_rng_state(), before)
