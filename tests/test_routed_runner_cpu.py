@@ -127,3 +127,43 @@ def test_routed_runner_checkpoint_and_resume(tmp_path):
     st = json.loads((tmp_path / "steps2.json").read_text())
     assert st["samples"] == 512
     assert (tmp_path / "out2" / "sae_weights.safetensors").exists()
+
+
+def _colocated_tp_worker(rank, world, port, tmp):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from saelens_b200.config import LanguageModelSAERunnerConfig, LoggingConfig
+    from saelens_b200.models.batchtopk import BatchTopKTrainingSAEConfig
+    from saelens_b200.models.lm import HookedLM, preset_config
+    from saelens_b200.runners.llm_sae_training_runner import LanguageModelSAETrainingRunner
+
+    torch.manual_seed(0)
+    lm = HookedLM(preset_config("gpt2", n_layers=2, d_model=64, n_heads=4, d_mlp=128, d_vocab=500, n_ctx=64,
+                                dtype="float32"))
+    cfg = LanguageModelSAERunnerConfig(
+        sae=BatchTopKTrainingSAEConfig(d_in=64, d_sae=128, k=8), model_name="gpt2",
+        hook_name="blocks.1.hook_resid_pre", dataset_path="synthetic:uniform:500:32", context_size=16,
+        training_tokens=64 * 6, train_batch_size_tokens=64, store_batch_size_prompts=4, n_batches_in_buffer=2,
+        output_path=os.path.join(tmp, "out"), logger=LoggingConfig(log_to_wandb=False), device="cpu",
+        n_checkpoints=0, verbose=False, routing_transport="collective", sae_dp_mode="manual")
+    runner = LanguageModelSAETrainingRunner(cfg, override_model=lm, vllm_dp_size=2, sae_dp_size=2, sae_tp_size=2,
+                                            use_shard_routing=True)
+    out = runner.run()
+    info = {"role": runner.role}
+    if out is not None:
+        info["steps"] = runner.trainer.n_training_steps
+        info["W_dec_shard_rows"] = int(out.W_dec.shape[0])
+    with open(os.path.join(tmp, f"r{rank}.json"), "w") as f:
+        json.dump(info, f)
+    dist.destroy_process_group()
+
+
+def test_routed_colocated_producers_with_tp_dp_consumers(tmp_path):
+    """2 producers co-located with the first ranks of two data-parallel SAE replicas of TP 2."""
+    mp.spawn(_colocated_tp_worker, args=(4, _port(), str(tmp_path)), nprocs=4, join=True)
+    r = [json.loads((tmp_path / f"r{i}.json").read_text()) for i in range(4)]
+    assert [x["role"] for x in r] == ["producer+consumer", "producer+consumer", "consumer", "consumer"]
+    assert all(x["steps"] == 6 and x["W_dec_shard_rows"] == 64 for x in r)
