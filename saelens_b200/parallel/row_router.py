@@ -19,7 +19,7 @@ both or neither.
 from __future__ import annotations
 
 import time
-
+from dataclasses import dataclass, field
 from typing import Sequence
 
 import torch
@@ -32,10 +32,72 @@ ROUTE_CHUNK_ROWS = 8  # rows per published chunk; the kernel's RT_RR
 _MODES = {"none": 0, "scale": 1, "unit_norm": 2}
 
 
+@dataclass
+class RoutePlan:
+    """Host-side plan of one rank in the router (no device state)."""
+
+    routes: list
+    rows_for: list[int]
+    members: list[list[int]]
+    member_slot: dict[tuple[int, int], int]  # (consumer, receiving rank) -> release flag index
+    p_idx: int | None
+    c_idx: int | None
+    m_slot: int | None
+    table: list[list[int]] = field(default_factory=list)  # [row_start, n_rows, dst_rank, dst_row]
+    free_slots: list[int] = field(default_factory=list)
+    chunks: list[int] = field(default_factory=list)  # chunks expected from each producer
+
+
+def route_plan(producers: Sequence[int], consumers: Sequence[int], batch_rows: int, rank: int,
+               consumer_members: Sequence[Sequence[int]] | None = None) -> RoutePlan:
+    """Routes, destination rows and release slots for `rank`.  `consumer_members[c]` (first entry
+    `consumers[c]`) lists every rank that receives consumer c's rows; each gets its own copy of the
+    rows and its own release flag."""
+    P, Q = len(producers), len(consumers)
+    routes = compute_routing_table(P, Q, batch_rows)
+    members = [list(m) for m in consumer_members] if consumer_members is not None else [[c] for c in consumers]
+    if len(members) != Q or any(not members[c] or members[c][0] != consumers[c] for c in range(Q)):
+        raise ValueError("consumer_members[c] must start with consumer_ranks[c]")
+    member_slot: dict[tuple[int, int], int] = {}
+    for c, ranks in enumerate(members):
+        for rk in ranks:
+            if any(rk == r for (_, r) in member_slot):
+                raise ValueError(f"rank {rk} receives rows for more than one consumer")
+            member_slot[(c, rk)] = len(member_slot)
+    # destination row of producer p's block inside consumer c's batch: earlier producers first
+    offset: dict[tuple[int, int], int] = {}
+    fill = [0] * Q
+    for r in sorted(routes, key=lambda r: (r.consumer_idx, r.producer_idx)):
+        offset[(r.producer_idx, r.consumer_idx)] = fill[r.consumer_idx]
+        fill[r.consumer_idx] += r.n_rows
+    p_idx = producers.index(rank) if rank in producers else None
+    c_idx = next((c for c, ranks in enumerate(members) if rank in ranks), None)
+    plan = RoutePlan(routes, rows_per_consumer(routes, Q), members, member_slot, p_idx, c_idx,
+                     member_slot[(c_idx, rank)] if c_idx is not None else None)
+    if p_idx is not None:
+        for r in routes:
+            if r.producer_idx != p_idx:
+                continue
+            for rk in members[r.consumer_idx]:
+                plan.table.append([r.row_start, r.n_rows, rk, offset[(r.producer_idx, r.consumer_idx)]])
+                plan.free_slots.append(member_slot[(r.consumer_idx, rk)])
+        if len(plan.table) > 16:  # the kernel's RT_MAX_ROUTES
+            raise ValueError(f"producer {p_idx} has {len(plan.table)} destinations; at most 16 are supported")
+    if c_idx is not None:
+        plan.chunks = [0] * P
+        for r in routes:
+            if r.consumer_idx == c_idx:
+                plan.chunks[r.producer_idx] += (r.n_rows + ROUTE_CHUNK_ROWS - 1) // ROUTE_CHUNK_ROWS
+    return plan
+
+
 class P2PRowRouter:
     def __init__(self, group: dist.ProcessGroup | None, producer_ranks: Sequence[int],
                  consumer_ranks: Sequence[int], batch_rows: int, d: int, normalize: str = "none",
-                 scale: float = 1.0):
+                 scale: float = 1.0, consumer_members: Sequence[Sequence[int]] | None = None):
+        """`consumer_members[c]` lists every rank that receives consumer c's rows (an SAE TP
+        group with replicated input): the producer stores the rows into each member's landing
+        buffer directly, so no broadcast follows.  Default: the consumer rank alone."""
         from saelens_b200.ops import native
         from saelens_b200.ops.status import StatusWord
 
@@ -50,36 +112,24 @@ class P2PRowRouter:
         self.d = int(d)
         self.mode = _MODES[normalize]
         self.scale = float(scale)
-        self.routes = compute_routing_table(self.P, self.Q, batch_rows)
-        self.rows_for = rows_per_consumer(self.routes, self.Q)
+        plan = route_plan(self.producers, self.consumers, batch_rows, self.rank, consumer_members)
+        self.routes, self.rows_for, self.members = plan.routes, plan.rows_for, plan.members
+        self.member_slot, self.p_idx, self.c_idx, self.m_slot = plan.member_slot, plan.p_idx, plan.c_idx, plan.m_slot
         self.rows_cap = max(self.rows_for)
-        sizes = [2 * self.rows_cap * self.d * 2, self.P * 4, self.Q * 4]
+        n_slots = len(self.member_slot)
+        sizes = [2 * self.rows_cap * self.d * 2, self.P * 4, n_slots * 4]
         self.heap = SymmetricHeap(group, slab_bytes_needed(sizes) + 4096)
         self.land = self.heap.alloc((2, self.rows_cap, self.d), torch.bfloat16)
         self.cnt = self.heap.alloc(max(self.P, 1), torch.int32)
-        self.free = self.heap.alloc(max(self.Q, 1), torch.int32)
+        self.free = self.heap.alloc(max(n_slots, 1), torch.int32)
         self.land_local = self.heap.local(self.land)
         self.cnt_local = self.heap.local(self.cnt)
         self.status = StatusWord(self.heap.device)
-        # destination row of producer p's block inside consumer c's batch: earlier producers first
-        offset: dict[tuple[int, int], int] = {}
-        fill = [0] * self.Q
-        for r in sorted(self.routes, key=lambda r: (r.consumer_idx, r.producer_idx)):
-            offset[(r.producer_idx, r.consumer_idx)] = fill[r.consumer_idx]
-            fill[r.consumer_idx] += r.n_rows
-        self.p_idx = self.producers.index(self.rank) if self.rank in self.producers else None
-        self.c_idx = self.consumers.index(self.rank) if self.rank in self.consumers else None
         if self.p_idx is not None:
-            mine = [r for r in self.routes if r.producer_idx == self.p_idx]
-            self.table = torch.tensor([[r.row_start, r.n_rows, self.consumers[r.consumer_idx],
-                                        offset[(r.producer_idx, r.consumer_idx)]] for r in mine], dtype=torch.int64)
-            self.free_slots = [r.consumer_idx for r in mine]
+            self.table = torch.tensor(plan.table, dtype=torch.int64).reshape(-1, 4)
+            self.free_slots = plan.free_slots
         if self.c_idx is not None:
-            chunks = [0] * self.P
-            for r in self.routes:
-                if r.consumer_idx == self.c_idx:
-                    chunks[r.producer_idx] += (r.n_rows + ROUTE_CHUNK_ROWS - 1) // ROUTE_CHUNK_ROWS
-            self._chunks = torch.tensor(chunks, dtype=torch.int64, device=self.heap.device)
+            self._chunks = torch.tensor(plan.chunks, dtype=torch.int64, device=self.heap.device)
             self._producer_mask = 0
             for p in self.producers:
                 self._producer_mask |= 1 << p
@@ -126,7 +176,7 @@ class P2PRowRouter:
 
     def release(self) -> None:
         """Consumer: the last received slot may be overwritten (stream-ordered)."""
-        self.nat.p2p_signal(self.heap.bases, self.rank, self.free.offset, self.c_idx, self._producer_mask,
+        self.nat.p2p_signal(self.heap.bases, self.rank, self.free.offset, self.m_slot, self._producer_mask,
                             self.recv_epoch)
 
     def close(self) -> None:

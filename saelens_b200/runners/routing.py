@@ -5,7 +5,9 @@ P producers (each runs the LM on one GPU) and Q consumers (SAE replicas of `sae_
 lockstep.  Every step each producer makes `Q * train_batch / P` activation rows and the routing
 table (`compute_routing_table`, interval overlap) splits them over the consumers; each consumer
 trains on its assembled rows (earlier producers first).  A rank may be a producer, a consumer or
-both; with SAE TP the consumer root broadcasts the rows to its TP group.
+both.  With SAE TP every member of a consumer's TP group needs the same rows: the p2p transport
+stores them into every member's landing buffer from the producer (no second hop), the collective
+transport sends them to the consumer root, which broadcasts them to its TP group.
 
 Transports:
 
@@ -65,10 +67,17 @@ def routing_init(runner: Any) -> None:
     producers = [v2.get_producer_tp_root(p) for p in range(P)]
     consumers = [v2.get_consumer_tp_root(c) for c in range(Q)]
     runner.route_producers, runner.route_consumers = producers, consumers
+    runner.route_to_members = False
     if runner.routing_transport == "p2p":
         from saelens_b200.parallel.row_router import P2PRowRouter
 
-        runner.router = P2PRowRouter(dist.group.WORLD, producers, consumers, runner.route_batch, cfg.sae.d_in)
+        members = None
+        if stp > 1:
+            layout = v2.get_layout()
+            members = [list(layout.consumer_ranks[c]) for c in range(Q)]
+            runner.route_to_members = True
+        runner.router = P2PRowRouter(dist.group.WORLD, producers, consumers, runner.route_batch, cfg.sae.d_in,
+                                     consumer_members=members)
 
 
 class _RowSource:
@@ -146,6 +155,12 @@ class RoutedExchange:
             self._pending_release = False
         if rows is not None:
             router.send(rows.to(self.dev), host_wait_s=HOST_WAIT_S)
+        if self.r.route_to_members:  # every TP member receives the rows itself
+            if self.c_idx < 0:
+                return None
+            got = router.recv(host_wait_s=HOST_WAIT_S)
+            self._pending_release = True
+            return got.to(self.dtype)
         if self.c_idx < 0 or self.rank != self.r.route_consumers[self.c_idx]:
             return self._bcast_tp(None)
         got = router.recv(host_wait_s=HOST_WAIT_S)
