@@ -27,6 +27,12 @@ def _dl(repo_id: str, filename: str, force_download: bool = False, subfolder: st
     return base._hf_download(repo_id, filename, force_download, subfolder)
 
 
+def _missing() -> tuple[type[BaseException], ...]:
+    from saelens_b200.loading import pretrained_sae_loaders as base
+
+    return base.MISSING_FILE_ERRORS
+
+
 def _load_st(path: str, device: str = "cpu", dtype: Any = None) -> dict[str, torch.Tensor]:
     from saelens_b200.loading import pretrained_sae_loaders as base
 
@@ -266,11 +272,11 @@ def get_mwhanna_transcoder_config_from_hf(repo_id: str, folder_name: str, device
     layer = int(folder_name.replace(".safetensors", "").split("_")[-1])
     try:
         wb = _yaml(_dl(repo_id, "wandb-config.yaml", force_download))
-    except Exception:
+    except _missing():
         wb = _yaml(_dl(repo_id, "wanb-config.yaml", force_download))
     try:
         base_cfg = _yaml(_dl(repo_id, "config.yaml", force_download))
-    except Exception:
+    except _missing():
         m = re.search(r"qwen3-(\d+(?:\.\d+)?)b", repo_id)
         if m is None:
             raise ValueError(f"could not find the Qwen3 size in {repo_id!r}") from None

@@ -17,7 +17,7 @@ from typing import Any
 
 import numpy as np
 import torch
-from packaging.version import Version
+from packaging.version import InvalidVersion, Version
 from safetensors import safe_open
 
 from saelens_b200.constants import (
@@ -40,6 +40,14 @@ LLM_METADATA_KEYS = {
     "dataset_path", "sae_lens_version", "sae_lens_training_version", "hook_name_out",
     "hook_head_index_out", "hf_hook_name", "hf_hook_name_out",
 }
+
+
+try:  # a file missing from a hub repo, or from the local cache when offline
+    from huggingface_hub.errors import EntryNotFoundError as _EntryNotFound
+
+    MISSING_FILE_ERRORS: tuple[type[BaseException], ...] = (OSError, _EntryNotFound)
+except ImportError:
+    MISSING_FILE_ERRORS = (OSError,)
 
 
 def _hf_download(repo_id: str, filename: str, force_download: bool = False, subfolder: str | None = None) -> str:
@@ -112,7 +120,7 @@ def sae_lens_huggingface_loader(repo_id: str, folder_name: str, device: str = "c
     wpath = _hf_download(repo_id, f"{folder_name}/{SAE_WEIGHTS_FILENAME}", force_download)
     try:
         spath: str | None = _hf_download(repo_id, f"{folder_name}/{SPARSITY_FILENAME}", force_download)
-    except Exception:
+    except MISSING_FILE_ERRORS:
         spath = None
     cfg, sd = read_sae_components_from_disk(cfg, wpath, device=device)
     log_sparsity = None
@@ -129,7 +137,7 @@ def handle_config_defaulting(cfg_dict: dict[str, Any]) -> dict[str, Any]:
         version = cfg_dict["metadata"].get("sae_lens_version")
     try:
         old = (not version) or Version(str(version)) < Version("6.0.0-rc.0")
-    except Exception:
+    except InvalidVersion:
         old = False
     if old and "metadata" not in cfg_dict:
         return handle_pre_6_0_config(cfg_dict)

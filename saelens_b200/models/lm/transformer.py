@@ -8,7 +8,7 @@ embedding scale, sandwich norms and logit soft-capping.
 
 Hooks (per block i): `hook_resid_pre`, `ln1.hook_normalized`, `attn.hook_q/k/v` (before RoPE),
 `attn.hook_z` (per-head attention output), `hook_attn_out`, `hook_resid_mid`, `ln2.hook_normalized`,
-`mlp.hook_pre` (gate branch before the activation), `mlp.hook_post`, `hook_mlp_out`,
+`mlp.hook_in` (the MLP's input), `mlp.hook_pre` (gate branch before the activation), `mlp.hook_post`, `hook_mlp_out`,
 `hook_resid_post`; plus `hook_embed`, `hook_pos_embed`, `ln_final.hook_normalized`.
 `run_with_cache(tokens, names_filter, stop_at_layer=n)` runs only blocks [0, n), which is how the
 SAE data pipeline stops right after the hooked layer.
@@ -281,10 +281,12 @@ class MLP(nn.Module):
             self.gate = NativeLinear(cfg.d_model, cfg.d_mlp, cfg.mlp_bias, dtype)
         self.up = NativeLinear(cfg.d_model, cfg.d_mlp, cfg.mlp_bias, dtype)
         self.down = NativeLinear(cfg.d_mlp, cfg.d_model, cfg.mlp_bias, dtype)
+        self.hook_in = HookPoint()  # the MLP's input (after the pre-MLP norm): transcoders read it
         self.hook_pre = HookPoint()
         self.hook_post = HookPoint()
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        x = self.hook_in(x)
         if self.gated:
             pre = self.hook_pre(self.gate(x))
             up = self.up(x)

@@ -24,7 +24,7 @@ def _is_nccl(group: Any) -> bool:
         if not dist.is_available() or not dist.is_initialized():
             return False
         return dist.get_backend(group) == "nccl"
-    except Exception:
+    except (RuntimeError, ValueError):  # a group this process is not part of
         return False
 
 
