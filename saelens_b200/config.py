@@ -259,7 +259,8 @@ class LanguageModelSAERunnerConfig(Generic[T_TRAINING_SAE_CONFIG]):
         if self.sae_dp_mode == "ddp" and self.compile_sae:
             raise ValueError("compile_sae=True is incompatible with sae_dp_mode='ddp'.")
         if self.hook_eval != "NOT_IN_USE":
-            warnings.warn("The 'hook_eval' field is deprecated and is not used.", DeprecationWarning, stacklevel=2)
+            warnings.warn("The 'hook_eval' field is deprecated and will be removed in v7.0.0. It is not used.",
+                          DeprecationWarning, stacklevel=2)
         if self.use_cached_activations and self.cached_activations_path is None:
             if self.hook_names is not None and len(self.hook_names) > 1:
                 raise ValueError("use_cached_activations is not supported with multi-layer hook_names.")

@@ -2,8 +2,10 @@
 (behaviour of sae_lens/training/mixing_buffer.py:35-96).
 
 Batches are concatenated until `buffer_size` rows are held; the buffer is permuted with a
-dedicated generator, `mix_fraction` of it is kept for mixing with the next fill and the rest is
-served in `batch_size` slices.  Dict batches (several hooks at once) are permuted jointly.
+dedicated generator, `mix_fraction * buffer_size` rows are kept for mixing with the next fill and
+the rest is served in `batch_size` slices.  Dict batches (several hooks at once) are permuted
+jointly.  The fill / permute / serve steps match the reference's so that a given generator seed
+yields the same batches.
 """
 
 from __future__ import annotations
@@ -34,36 +36,31 @@ def _take(b: Batch, idx: torch.Tensor | slice) -> Batch:
 @torch.no_grad()
 def mixing_buffer(buffer_size: int, batch_size: int, activations_loader: Iterator[Batch],
                   mix_fraction: float = 0.5, generator: torch.Generator | None = None) -> Iterator[Batch]:
+    """Whenever at least `buffer_size` rows are held: permute them (CPU `randperm` on
+    `generator`, so a seed gives the same stream on any device), serve whole batches from the
+    front and hold the last `int(buffer_size * mix_fraction)` rows (at least one batch is served
+    per fill, so even `mix_fraction=1` keeps the held rows bounded).  With `mix_fraction=0` rows
+    are served in arrival order.  Leftover rows are served unshuffled at the end, whole batches
+    only."""
     if buffer_size < batch_size:
         raise ValueError("Buffer size must be greater than or equal to batch size")
     if not 0 <= mix_fraction <= 1:
         raise ValueError("mix_fraction must be in [0, 1]")
-    held: list[Batch] = []
-    n_held = 0
+    keep = int(buffer_size * mix_fraction)
+    held: Batch | None = None
     for batch in activations_loader:
-        held.append(batch)
-        n_held += _rows(batch)
-        if n_held < buffer_size:
+        held = batch if held is None else _cat([held, batch])
+        n = _rows(held)
+        if n < buffer_size:
             continue
-        buf = _cat(held)
-        n = _rows(buf)
         if mix_fraction > 0:
-            dev = next(iter(buf.values())).device if isinstance(buf, dict) else buf.device
-            perm = torch.randperm(n, generator=generator, device="cpu").to(dev)
-            buf = _take(buf, perm)
-        keep = int(n * mix_fraction)
-        serve = _take(buf, slice(keep, None))
-        held = [_take(buf, slice(0, keep))] if keep > 0 else []
-        n_held = keep
-        n_serve = _rows(serve)
-        for s in range(0, n_serve - batch_size + 1, batch_size):
-            yield _take(serve, slice(s, s + batch_size))
-        rem = n_serve % batch_size
-        if rem:
-            held.append(_take(serve, slice(n_serve - rem, None)))
-            n_held += rem
-    if n_held:
-        buf = _cat(held)
-        n = _rows(buf)
-        for s in range(0, n - batch_size + 1, batch_size):
-            yield _take(buf, slice(s, s + batch_size))
+            dev = next(iter(held.values())).device if isinstance(held, dict) else held.device
+            held = _take(held, torch.randperm(n, generator=generator).to(dev))
+        n_batches = max(1, (n - keep) // batch_size)
+        cut = n_batches * batch_size
+        serve, held = _take(held, slice(0, cut)), _take(held, slice(cut, None))
+        for i in range(n_batches):
+            yield _take(serve, slice(i * batch_size, (i + 1) * batch_size))
+    if held is not None:
+        for i in range(_rows(held) // batch_size):
+            yield _take(held, slice(i * batch_size, (i + 1) * batch_size))
