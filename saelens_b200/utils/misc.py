@@ -32,7 +32,7 @@ def str_to_dtype(dtype: str | torch.dtype) -> torch.dtype:
     try:
         return DTYPE_MAP[dtype]
     except KeyError as e:
-        raise ValueError(f"unknown dtype {dtype!r}; expected one of {sorted(DTYPE_MAP)}") from e
+        raise ValueError(f"Invalid dtype: {dtype!r}; expected one of {sorted(DTYPE_MAP)}") from e
 
 
 def dtype_to_str(dtype: torch.dtype | str) -> str:
@@ -41,15 +41,22 @@ def dtype_to_str(dtype: torch.dtype | str) -> str:
     for name in ("float32", "float64", "float16", "bfloat16"):
         if DTYPE_MAP[name] == dtype:
             return name
-    raise ValueError(f"unsupported dtype {dtype}")
+    raise ValueError(f"Invalid dtype: {dtype}")
 
 
-def filter_valid_dataclass_fields(data: dict[str, Any], cls: Any,
-                                  whitelist: list[str] | None = None) -> dict[str, Any]:
-    """Keep only the keys of `data` that are init fields of dataclass `cls`."""
+def filter_valid_dataclass_fields(data: dict[str, Any] | Any, cls: Any,
+                                  whitelist_fields: list[str] | None = None) -> dict[str, Any]:
+    """The entries of `data` (a dict or a dataclass instance) that are init fields of dataclass
+    `cls`, plus any `whitelist_fields` present in `data`."""
+    if not dataclasses.is_dataclass(cls):
+        raise ValueError(f"{cls} is not a dataclass")
+    if dataclasses.is_dataclass(data) and not isinstance(data, type):
+        data = {f.name: getattr(data, f.name) for f in dataclasses.fields(data)}
+    elif not isinstance(data, dict):
+        raise ValueError(f"{data!r} is not a dict or dataclass")
     names = {f.name for f in dataclasses.fields(cls) if f.init}
-    if whitelist:
-        names |= set(whitelist)
+    if whitelist_fields:
+        names |= set(whitelist_fields)
     return {k: v for k, v in data.items() if k in names}
 
 
