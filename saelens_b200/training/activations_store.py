@@ -263,6 +263,19 @@ class ActivationsStore:
         self._token_iter = None
         self._batch_iter = None
 
+    def reset_input_dataset(self) -> None:
+        """Restart token reading from the first context (same seed), e.g. between eval passes.
+        Activations already in the mixing buffer stay; later batches read the restarted tokens."""
+        self.n_dataset_processed = 0
+        self._token_iter = None
+
+    def token_position(self) -> tuple[int, Any]:
+        """Opaque token-reading position; `restore_token_position` puts it back."""
+        return self.n_dataset_processed, self._token_iter
+
+    def restore_token_position(self, pos: tuple[int, Any]) -> None:
+        self.n_dataset_processed, self._token_iter = pos
+
     @torch.no_grad()
     def estimate_norm_scaling_factor(self, n_batches_for_norm_estimate: int = 100) -> float:
         norms = []
