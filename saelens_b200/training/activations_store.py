@@ -11,6 +11,7 @@ saved in checkpoints so a resumed run continues where it stopped.
 from __future__ import annotations
 
 import json
+import warnings
 from collections.abc import Iterator
 from pathlib import Path
 from typing import Any
@@ -18,7 +19,7 @@ from typing import Any
 import torch
 from safetensors.torch import load_file, save_file
 
-from saelens_b200.training.datasets import open_token_source
+from saelens_b200.training.datasets import first_tokenized_length, open_token_source
 from saelens_b200.training.mixing_buffer import mixing_buffer
 from saelens_b200.training.tokenization_and_batching import concat_and_batch_sequences
 from saelens_b200.utils.misc import extract_stop_at_layer_from_hook_name, get_special_token_ids, str_to_dtype
@@ -90,6 +91,29 @@ class ActivationsStore:
                 raise FileNotFoundError(f"no activation shards in {cached_activations_path}")
         self._token_iter: Iterator[torch.Tensor] | None = None
         self._batch_iter: Iterator[Any] | None = None
+        self._check_pretokenized_length()
+
+    def _check_pretokenized_length(self) -> None:
+        """A pretokenized dataset whose rows are shorter than `context_size` cannot fill a
+        context (error); longer rows are cut (warning)."""
+        if self.cached_activations_path is not None:
+            return
+        if isinstance(self.dataset, str) and self.dataset.startswith("synthetic:"):
+            return
+        if not isinstance(self.dataset, (str, Path, torch.Tensor, list, tuple)):  # one-shot iterables stay unread
+            return
+        try:
+            n = first_tokenized_length(self.dataset)
+        except (FileNotFoundError, ValueError, OSError):
+            return
+        if n is None:
+            return
+        if n < self.context_size:
+            raise ValueError(f"pretokenized dataset has context size {n}, but the provided context_size is "
+                             f"{self.context_size}: the dataset cannot fill a context.")
+        if n > self.context_size:
+            warnings.warn(f"pretokenized dataset has context size {n}, but the provided context_size is "
+                          f"{self.context_size}; each row is split across contexts.", RuntimeWarning, stacklevel=3)
 
     # ---------------------------------------------------------------- construction helpers
     @classmethod
