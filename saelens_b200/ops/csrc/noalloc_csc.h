@@ -1,10 +1,10 @@
 // Allocation-free entry point for building the latent-major (CSC) pair lists of a TopK step.
 //
 // This entry point has no counterpart in the reference (SAELens has no native code); it exists
-// for callers of this library that cannot allocate device memory themselves: code running
-// inside a CUDA-graph capture that must not grow the allocator, embedders whose memory is fully
-// reserved up front by a host framework, and plain C/C++ programs that link this library
-// without PyTorch's caching allocator.  The caller passes inputs and outputs; the working
+// for callers of this library that cannot allocate device memory themselves: embedders whose
+// device memory is fully reserved up front by a host framework (so a cudaMalloc would fail or
+// fight that framework's pool), and plain C/C++ programs that link this library without
+// PyTorch's caching allocator and may not call into it.  The caller passes inputs and outputs; the working
 // memory (per-latent counters, cursors and scan partials) lives in a fixed-size device array
 // inside this library.
 //

@@ -45,6 +45,8 @@ class PretokenizeRunner:
 
     def tokenize(self) -> np.ndarray:
         c = self.cfg
+        if c.streaming and c.num_proc > 1:  # a streamed dataset is read by one process
+            raise ValueError("num_proc must be 1 when streaming is True")
         src = open_token_source(self.dataset, tokenizer=self.tokenizer, column=c.column_name)
         rows = list(concat_and_batch_sequences(
             src, c.context_size, begin_batch_token_id=_special(c.begin_batch_token, self.tokenizer),

@@ -3,6 +3,7 @@
 import json
 
 import numpy as np
+import pytest
 import torch
 
 from saelens_b200.config import CacheActivationsRunnerConfig, LoggingConfig, PretokenizeRunnerConfig, SAETrainerConfig
@@ -87,3 +88,16 @@ def test_multi_sae_trainer_two_hooks(tmp_path):
     tr2 = MultiSAETrainer(hook_names=["a", "b"], sae_by_hook=saes, data_provider=gen(), cfg=cfg)
     tr2.load_trainer_state(tmp_path / "ck")
     assert tr2.n_training_steps == 20
+
+
+def test_pretokenize_shuffle_and_streaming_checks(tmp_path):
+    data = [{"text": "hello world " * 3}, {"text": "sparse autoencoders " * 3}, {"text": "b200 " * 6}]
+    plain = PretokenizeRunner(PretokenizeRunnerConfig(tokenizer_name="char", context_size=8, shuffle=False),
+                              tokenizer=_Tok(), override_dataset=data).tokenize()
+    mixed = PretokenizeRunner(PretokenizeRunnerConfig(tokenizer_name="char", context_size=8, shuffle=True, seed=3),
+                              tokenizer=_Tok(), override_dataset=data).tokenize()
+    # shuffling permutes whole contexts
+    assert sorted(map(tuple, plain.tolist())) == sorted(map(tuple, mixed.tolist()))
+    cfg = PretokenizeRunnerConfig(tokenizer_name="char", context_size=8, num_proc=2, streaming=True)
+    with pytest.raises(ValueError, match="num_proc must be 1"):
+        PretokenizeRunner(cfg, tokenizer=_Tok(), override_dataset=data).tokenize()
