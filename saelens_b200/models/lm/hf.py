@@ -68,12 +68,25 @@ class HookedProxyLM(HookedRootModule):
     def cfg(self) -> Any:
         return self.model.config
 
-    def forward(self, tokens: torch.Tensor, stop_at_layer: int | None = None, **kwargs: Any) -> Any:
+    def forward(self, tokens: torch.Tensor, return_type: str | None = "logits", stop_at_layer: int | None = None,
+                **kwargs: Any) -> Any:
+        """`return_type` "logits" (or None) gives the logits; "both" gives (logits, loss) with the
+        Hugging Face model's own next-token loss and cannot stop early (sae_lens/load_model.py
+        HookedProxyLM.forward)."""
+        if return_type not in ("logits", "both", None):
+            raise NotImplementedError(f"Only return_type supported is 'both', 'logits' or None, got {return_type!r}")
+        if return_type == "both" and stop_at_layer is not None:
+            raise NotImplementedError("stop_at_layer is not supported for return_type='both'")
+        kwargs.pop("_names_filter", None)
         if stop_at_layer is not None and 0 < stop_at_layer <= len(self._layer_names):
             self._stop_after = self._layer_names[stop_at_layer - 1]
+        dev = next(self.model.parameters()).device
         try:
-            out = self.model(input_ids=tokens.to(next(self.model.parameters()).device), **kwargs)
-            return getattr(out, "logits", out)
+            if return_type == "both":
+                ids = tokens.to(dev)
+                out = self.model(input_ids=ids, labels=ids, **kwargs)
+                return _extract_logits_from_output(out), out.loss
+            return _extract_logits_from_output(self.model(input_ids=tokens.to(dev), **kwargs))
         except _StopForward:
             return None
         finally:
@@ -92,9 +105,34 @@ class HookedProxyLM(HookedRootModule):
             out = self(*args, **kwargs)
         return out, cache
 
-    def to_tokens(self, text: str | list[str], prepend_bos: bool = True) -> torch.Tensor:
+    def to_tokens(self, text: str | list[str], prepend_bos: bool | None = False, padding_side: str | None = None,
+                  truncate: bool = False, move_to_device: bool = False) -> torch.Tensor:
+        """Tokenizer ids exactly as the Hugging Face tokenizer makes them: the tokenizer decides
+        about BOS, so the TransformerLens-style options are accepted only at their no-op values."""
+        if prepend_bos is not False:
+            raise ValueError("Only works with prepend_bos=False, to match the Hugging Face tokenizer")
+        if padding_side is not None:
+            raise ValueError("Only works with padding_side=None, to match the Hugging Face tokenizer")
+        if truncate:
+            raise ValueError("Only works with truncate=False, to match the Hugging Face tokenizer")
+        if move_to_device:
+            raise ValueError("Only works with move_to_device=False, to match the Hugging Face tokenizer")
         enc = self.tokenizer(text if isinstance(text, list) else [text], return_tensors="pt", padding=True)
         return enc["input_ids"]
+
+
+def _extract_logits_from_output(out: Any) -> torch.Tensor | None:
+    """Logits from a Hugging Face model output: a tensor, a dict-like or object with `logits`
+    (None when it is None), or a tuple whose first entry is the logits."""
+    if isinstance(out, torch.Tensor):
+        return out
+    if isinstance(out, dict):
+        return out.get("logits")
+    if isinstance(out, tuple):
+        return out[0]
+    if hasattr(out, "logits"):
+        return out.logits
+    raise ValueError(f"Unsupported model output type: {type(out)}")
 
 
 def _cfg_from_hf(hc: Any) -> LMConfig:

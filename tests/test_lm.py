@@ -71,3 +71,52 @@ def test_hooked_proxy_lm_stops_early():
     out, cache = proxy.run_with_cache(toks, names_filter="model.layers.0", stop_at_layer=1)
     assert out is None and cache["model.layers.0"].shape == (1, 5, 64)
     assert "model.layers.1" not in proxy.run_with_cache(toks, names_filter="model.layers.1", stop_at_layer=1)[1]
+
+
+def test_hooked_proxy_lm_return_types_and_option_checks():
+    import pytest
+
+    from saelens_b200.models.lm.hf import _extract_logits_from_output
+
+    hf = _tiny_llama().eval()
+    proxy = HookedProxyLM(hf)
+    toks = torch.randint(0, 300, (2, 6))
+    with torch.no_grad():
+        logits = proxy(toks)
+        both_logits, loss = proxy(toks, return_type="both")
+        torch.testing.assert_close(both_logits, logits)
+        lp = torch.log_softmax(logits[:, :-1].float(), -1)
+        want = -lp.gather(-1, toks[:, 1:].unsqueeze(-1)).mean()
+        torch.testing.assert_close(loss.float(), want, rtol=1e-4, atol=1e-4)
+        for bad in ("loss", "activations"):
+            with pytest.raises(NotImplementedError, match="Only return_type supported is"):
+                proxy(toks, return_type=bad)
+        with pytest.raises(NotImplementedError, match="stop_at_layer is not supported for return_type='both'"):
+            proxy(toks, return_type="both", stop_at_layer=1)
+        out_tuple = hf(input_ids=toks, return_dict=False)
+        torch.testing.assert_close(_extract_logits_from_output(out_tuple), logits)
+    with pytest.raises(ValueError, match="Unsupported model output type"):
+        _extract_logits_from_output("not an output")
+
+    class _Obj:
+        def __init__(self, lg):
+            self.logits = lg
+
+    assert _extract_logits_from_output(_Obj(None)) is None
+    torch.testing.assert_close(_extract_logits_from_output(_Obj(logits)), logits)
+
+
+def test_hooked_proxy_to_tokens_options_and_unknown_model_class():
+    import pytest
+
+    from saelens_b200.models.lm.load_model import load_model
+
+    proxy = HookedProxyLM(_tiny_llama(), tokenizer=lambda t, **kw: {"input_ids": torch.tensor([[5, 6]] * len(t))})
+    assert proxy.to_tokens("hi").tolist() == [[5, 6]]
+    for kw, msg in [({"prepend_bos": True}, "prepend_bos=False"), ({"prepend_bos": None}, "prepend_bos=False"),
+                    ({"padding_side": "left"}, "padding_side=None"), ({"truncate": True}, "truncate=False"),
+                    ({"move_to_device": True}, "move_to_device=False")]:
+        with pytest.raises(ValueError, match=f"Only works with {msg}"):
+            proxy.to_tokens("hi", **kw)
+    with pytest.raises(ValueError, match="Unknown model class: FakeModelClass"):
+        load_model("FakeModelClass", "some-model", device="cpu")
