@@ -55,6 +55,9 @@ class CacheActivationsRunner:
             t = self.store.get_batch_tokens()
             a = self.store.get_activations(t)
             a = next(iter(a.values())) if isinstance(a, dict) else a
+            if a.shape[-1] != self.cfg.d_in:
+                raise RuntimeError(f"The hook {self.cfg.hook_name} has width {a.shape[-1]}, but d_in is "
+                                   f"{self.cfg.d_in}: the cached activations would not match the config.")
             acts.append(a.to("cpu", str_to_dtype(self.cfg.dtype)))
             toks.append(t[:, slice(*self.cfg.seqpos_slice)].to(torch.int32).cpu())
             got += t.shape[0]
@@ -72,6 +75,8 @@ class CacheActivationsRunner:
     def run(self) -> Path:
         c = self.cfg
         out = Path(c.new_cached_activations_path or "activations")
+        if out.exists() and any(out.iterdir()):  # never overwrite a directory the user filled
+            raise FileExistsError(f"{out} is not empty. Please delete it or specify a different path.")
         tmp = out.parent / (out.name + ".tmp_shards")
         if tmp.exists():
             shutil.rmtree(tmp)
@@ -90,8 +95,8 @@ class CacheActivationsRunner:
         info = {"hook_name": c.hook_name, "d_in": c.d_in, "context_size": c.sliced_context_size, "dtype": c.dtype,
                 "n_shards": i, "total_tokens": total_tokens, "model_name": c.model_name, "dataset_path": c.dataset_path}
         (tmp / "cache_info.json").write_text(json.dumps(info, indent=2))
-        if out.exists():
-            shutil.rmtree(out)
+        if out.exists():  # an empty directory
+            out.rmdir()
         tmp.rename(out)
         if c.hf_repo_id:
             self._push_to_hub(out)

@@ -101,3 +101,38 @@ def test_pretokenize_shuffle_and_streaming_checks(tmp_path):
     cfg = PretokenizeRunnerConfig(tokenizer_name="char", context_size=8, num_proc=2, streaming=True)
     with pytest.raises(ValueError, match="num_proc must be 1"):
         PretokenizeRunner(cfg, tokenizer=_Tok(), override_dataset=data).tokenize()
+
+
+def _cache_cfg(tmp_path, **kw):
+    base = dict(dataset_path="synthetic:uniform:500:32", model_name="gpt2", model_batch_size=4,
+                hook_name="blocks.0.hook_resid_post", d_in=64, training_tokens=16 * 8, context_size=16,
+                new_cached_activations_path=str(tmp_path / "cache"), device="cpu",
+                buffer_size_gb=16 * 8 * 64 * 4 / 1e9, shuffle=False)
+    base.update(kw)
+    return CacheActivationsRunnerConfig(**base)
+
+
+def test_cache_runner_refuses_a_nonempty_directory_and_a_wrong_width(tmp_path):
+    (tmp_path / "cache").mkdir()
+    (tmp_path / "cache" / "some_file.txt").write_text("keep me")
+    with pytest.raises(FileExistsError, match="is not empty. Please delete it or specify a different path."):
+        CacheActivationsRunner(_cache_cfg(tmp_path), override_model=_lm()).run()
+    assert (tmp_path / "cache" / "some_file.txt").read_text() == "keep me"
+    with pytest.raises(RuntimeError, match="has width 64, but d_in is 65"):
+        CacheActivationsRunner(_cache_cfg(tmp_path, d_in=65, new_cached_activations_path=str(tmp_path / "c2")),
+                               override_model=_lm()).run()
+
+
+def test_cache_runner_seqpos_and_shuffle_keep_token_alignment(tmp_path):
+    lm = _lm()
+    out = CacheActivationsRunner(_cache_cfg(tmp_path, seqpos_slice=(2, 10), shuffle=True), override_model=lm).run()
+    from safetensors.torch import load_file
+
+    sd = load_file(str(sorted(out.glob("*.safetensors"))[0]))
+    assert sd["activations"].shape[1] == 8 and sd["token_ids"].shape[1] == 8
+    # shuffled positions still carry their own token id: same multiset as an unshuffled run
+    plain = CacheActivationsRunner(_cache_cfg(tmp_path, seqpos_slice=(2, 10), shuffle=False,
+                                              new_cached_activations_path=str(tmp_path / "plain")),
+                                   override_model=lm).run()
+    sp = load_file(str(sorted(plain.glob("*.safetensors"))[0]))
+    assert sorted(sd["token_ids"].flatten().tolist()) == sorted(sp["token_ids"].flatten().tolist())
