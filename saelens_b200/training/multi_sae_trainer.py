@@ -244,6 +244,13 @@ class MultiSAETrainer:
         (base / MULTI_SAE_MANIFEST_FILENAME).write_text(json.dumps(self._manifest(), indent=2))
 
     def load_trainer_state(self, checkpoint_path: str | Path) -> None:
+        """Restore counters, statistics and optimizer state; the checkpoint must hold the same
+        hooks (multi_sae_trainer.py resume in the reference raises on a mismatch too)."""
+        man = Path(checkpoint_path) / MULTI_SAE_MANIFEST_FILENAME
+        if man.exists():
+            saved = json.loads(man.read_text()).get("hook_names")
+            if saved is not None and list(saved) != list(self.hook_names):
+                raise ValueError(f"checkpoint hooks {saved} do not match this trainer's hooks {self.hook_names}")
         st = torch.load(Path(checkpoint_path) / TRAINER_STATE_FILENAME, map_location="cpu", weights_only=False)
         self.n_training_steps = st["n_training_steps"]
         self.n_training_samples = st["n_training_samples"]

@@ -136,3 +136,36 @@ def test_cache_runner_seqpos_and_shuffle_keep_token_alignment(tmp_path):
                                    override_model=lm).run()
     sp = load_file(str(sorted(plain.glob("*.safetensors"))[0]))
     assert sorted(sd["token_ids"].flatten().tolist()) == sorted(sp["token_ids"].flatten().tolist())
+
+
+def test_multi_sae_checkpoint_restores_state_and_rejects_other_hooks(tmp_path):
+    cfg = SAETrainerConfig(
+        n_checkpoints=0, checkpoint_path=None, save_final_checkpoint=False, output_path=None, save_mse_every_n_steps=0,
+        save_timing_every_n_steps=0, save_memory_every_n_steps=0, synchronize_timing=False,
+        multi_sae_backward_order="forward", multi_sae_stats_sync_mode="immediate", multi_sae_stats_sync_interval=1,
+        total_training_samples=32 * 6, device="cpu", autocast=False, lr=1e-3, lr_end=1e-4,
+        lr_scheduler_name="constant", lr_warm_up_steps=0, adam_beta1=0.9, adam_beta2=0.999, lr_decay_steps=0,
+        n_restart_cycles=1, train_batch_size_samples=32, dead_feature_window=5, feature_sampling_window=10,
+        logger=LoggingConfig(log_to_wandb=False))
+    g = torch.Generator().manual_seed(0)
+
+    def gen():
+        while True:
+            yield {"a": torch.randn(32, 16, generator=g), "b": torch.randn(32, 16, generator=g)}
+
+    saes = {"a": StandardTrainingSAE(StandardTrainingSAEConfig(d_in=16, d_sae=32)),
+            "b": StandardTrainingSAE(StandardTrainingSAEConfig(d_in=16, d_sae=32))}
+    tr = MultiSAETrainer(hook_names=["a", "b"], sae_by_hook=saes, data_provider=gen(), cfg=cfg)
+    tr.fit()
+    tr.save_checkpoint(tmp_path / "ck")
+    tr2 = MultiSAETrainer(hook_names=["a", "b"], sae_by_hook=saes, data_provider=gen(), cfg=cfg)
+    tr2.load_trainer_state(tmp_path / "ck")
+    assert tr2.n_training_samples == tr.n_training_samples
+    for h in ("a", "b"):
+        torch.testing.assert_close(tr2.act_freq_scores[h], tr.act_freq_scores[h])
+    s1, s2 = tr.optimizer.state_dict()["state"], tr2.optimizer.state_dict()["state"]
+    assert s1.keys() == s2.keys() and all(torch.equal(s1[k]["exp_avg"], s2[k]["exp_avg"]) for k in s1)
+    other = {"a": saes["a"], "c": StandardTrainingSAE(StandardTrainingSAEConfig(d_in=16, d_sae=32))}
+    tr3 = MultiSAETrainer(hook_names=["a", "c"], sae_by_hook=other, data_provider=gen(), cfg=cfg)
+    with pytest.raises(ValueError, match="do not match"):
+        tr3.load_trainer_state(tmp_path / "ck")
