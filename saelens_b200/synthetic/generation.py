@@ -317,7 +317,8 @@ class HierarchyConfig:
         lo, hi = (self.branching_factor, self.branching_factor) if isinstance(self.branching_factor, int) \
             else tuple(self.branching_factor)
         if lo < 2:
-            raise ValueError("branching_factor must be at least 2")
+            raise ValueError("branching_factor must be at least 2" if isinstance(self.branching_factor, int)
+                             else "branching_factor minimum must be at least 2")
         if lo > hi:
             raise ValueError("branching_factor[0] must be <= branching_factor[1]")
         if self.max_depth < 1:
