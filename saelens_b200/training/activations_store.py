@@ -95,7 +95,7 @@ class ActivationsStore:
 
     def _check_pretokenized_length(self) -> None:
         """A pretokenized dataset whose rows are shorter than `context_size` cannot fill a
-        context (error); longer rows are cut (warning)."""
+        context (error); longer rows are cut to `context_size` (warning)."""
         if self.cached_activations_path is not None:
             return
         if isinstance(self.dataset, str) and self.dataset.startswith("synthetic:"):
@@ -113,7 +113,7 @@ class ActivationsStore:
                              f"{self.context_size}: the dataset cannot fill a context.")
         if n > self.context_size:
             warnings.warn(f"pretokenized dataset has context size {n}, but the provided context_size is "
-                          f"{self.context_size}; each row is split across contexts.", RuntimeWarning, stacklevel=3)
+                          f"{self.context_size}; each row is cut to its first {self.context_size} tokens.", RuntimeWarning, stacklevel=3)
 
     # ---------------------------------------------------------------- construction helpers
     @classmethod
@@ -150,15 +150,28 @@ class ActivationsStore:
 
     # ---------------------------------------------------------------- tokens
     def _tokens(self) -> Iterator[torch.Tensor]:
+        """Context-length token rows.  Pretokenized records are used as they are, each cut to
+        `context_size` (their BOS / separator tokens were added when they were tokenized);
+        text records are tokenized and packed with the BOS / separator rules
+        (sae_lens/training/activations_store.py:499-530)."""
         src = open_token_source(self.dataset, tokenizer=self.tokenizer, column=self.text_column,
                                 shard_index=self.shard_index, num_shards=self.num_shards,
-                                skip=self.n_dataset_processed, seed=self.seed, default_len=self.context_size)
+                                skip=self.n_dataset_processed, seed=self.seed, default_len=self.context_size,
+                                with_kind=True)
+        try:
+            first = next(src)
+        except StopIteration:
+            return iter(())
 
         def counted() -> Iterator[torch.Tensor]:
-            for t in src:
+            self.n_dataset_processed += 1
+            yield first[0]
+            for t, _ in src:
                 self.n_dataset_processed += 1
                 yield t
 
+        if first[1]:
+            return (t[: self.context_size] for t in counted())
         return concat_and_batch_sequences(counted(), self.context_size, begin_batch_token_id=self._begin_batch,
                                           begin_sequence_token_id=None, sequence_separator_token_id=self._sep,
                                           disable_concat_sequences=self.disable_concat_sequences)

@@ -24,6 +24,18 @@ import torch
 TOKEN_KEYS = ("tokens", "input_ids")
 
 
+def record_is_pretokenized(rec: Any) -> bool:
+    """True when a dataset record already holds token ids (a tensor, an array, a list of ints or
+    a dict with a "tokens" / "input_ids" field); False for text records."""
+    if isinstance(rec, (torch.Tensor, np.ndarray)):
+        return True
+    if isinstance(rec, (list, tuple)):
+        return not rec or isinstance(rec[0], (int, np.integer))
+    if isinstance(rec, dict):
+        return any(k in rec for k in TOKEN_KEYS)
+    return False
+
+
 def _record_tokens(rec: Any, tokenizer: Any, column: str = "text") -> torch.Tensor | None:
     if isinstance(rec, torch.Tensor):
         return rec.long().flatten()
@@ -111,7 +123,10 @@ def synthetic_uniform(vocab: int, length: int, seed: int = 0) -> Iterator[torch.
 
 
 def open_token_source(src: Any, tokenizer: Any = None, column: str = "text", shard_index: int = 0,
-                      num_shards: int = 1, skip: int = 0, seed: int = 0, default_len: int = 1024) -> Iterator[torch.Tensor]:
+                      num_shards: int = 1, skip: int = 0, seed: int = 0, default_len: int = 1024,
+                      with_kind: bool = False) -> Iterator[Any]:
+    """Token sequences of `src`; with `with_kind`, (tokens, pretokenized) pairs, where
+    `pretokenized` says whether the record already held token ids (synthetic sources do)."""
     if isinstance(src, str) and src.startswith("synthetic:"):
         parts = src.split(":")
         vocab = int(parts[2]) if len(parts) > 2 else 50257
@@ -119,7 +134,7 @@ def open_token_source(src: Any, tokenizer: Any = None, column: str = "text", sha
         it: Iterable[torch.Tensor] = synthetic_uniform(vocab, length, seed=seed + 7919 * shard_index)
         for i, t in enumerate(it):
             if i >= skip:
-                yield t
+                yield (t, True) if with_kind else t
         return
     for i, rec in enumerate(_iter_records(src)):
         if i % num_shards != shard_index:
@@ -128,7 +143,7 @@ def open_token_source(src: Any, tokenizer: Any = None, column: str = "text", sha
             continue
         t = _record_tokens(rec, tokenizer, column)
         if t is not None and t.numel() > 0:
-            yield t
+            yield (t, record_is_pretokenized(rec)) if with_kind else t
 
 
 def first_tokenized_length(src: Any) -> int | None:

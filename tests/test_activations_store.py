@@ -115,3 +115,32 @@ def test_from_sae_takes_hook_and_context_from_metadata(lm):
     assert s.hook_name == HOOK and s.context_size == 16
     s = ActivationsStore.from_sae(lm, sae, "synthetic:uniform:200:16", context_size=8)
     assert s.context_size == 8
+
+
+class _Tok:
+    bos_token_id = 1
+    eos_token_id = 2
+    sep_token_id = None
+
+    def encode(self, text):
+        return [int(t) for t in text.split()]
+
+
+@pytest.mark.parametrize("rows, expected", [
+    # BOS-led rows longer than the context: each row is cut, nothing spills into the next context
+    ([[1, 5, 6, 7, 8], [1, 9, 9, 9, 9]], [[1, 5, 6, 7], [1, 9, 9, 9]]),
+    # rows pretokenized without BOS stay without it
+    ([[5, 6, 7, 8, 3], [9, 4, 4, 4, 4]], [[5, 6, 7, 8], [9, 4, 4, 4]]),
+])
+def test_pretokenized_rows_are_cut_to_the_context(lm, rows, expected):
+    with pytest.warns(RuntimeWarning, match="cut to its first 4 tokens"):
+        s = _store(lm, dataset=[{"input_ids": r} for r in rows], context_size=4, store_batch_size_prompts=2,
+                   prepend_bos=True, tokenizer=_Tok())
+    assert s.get_batch_tokens().tolist() == expected
+    assert s.n_dataset_processed == 2
+
+
+def test_text_rows_are_packed_with_bos(lm):
+    s = _store(lm, dataset=[{"text": "5 6 7"}, {"text": "8 9"}], context_size=4, store_batch_size_prompts=1,
+               prepend_bos=True, tokenizer=_Tok(), sequence_separator_token=None)
+    assert s.get_batch_tokens().tolist() == [[1, 5, 6, 7]]
