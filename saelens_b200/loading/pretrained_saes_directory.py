@@ -3,8 +3,13 @@
 Same YAML schema as the reference's directory (sae_lens/loading/pretrained_saes_directory.py:
 release keys with `repo_id`, `model`, `conversion_func`, `saes: [{id, path, l0,
 variance_explained, neuronpedia, norm_scaling_factor}]`, `config_overrides`).  The package ships a
-small directory; point `SAELENS_B200_PRETRAINED_YAML` at a larger file (for example the
-reference's full directory) to extend it, or call `register_release`.
+small directory.  The full directory is found, in this order of precedence (later entries
+override earlier ones):
+1. the shipped `pretrained_saes.yaml`;
+2. the `pretrained_saes.yaml` of an installed `sae_lens` package, located on `sys.path` without
+   importing it (the reference's 156-release directory, same schema);
+3. every file named in `SAELENS_B200_PRETRAINED_YAML` (`os.pathsep`-separated);
+4. releases added at runtime with `register_release`.
 """
 
 from __future__ import annotations
@@ -58,14 +63,40 @@ def _parse(data: dict[str, Any]) -> dict[str, PretrainedSAELookup]:
     return out
 
 
+def installed_sae_lens_directory() -> str | None:
+    """Path of an installed `sae_lens` package's pretrained_saes.yaml, found without importing it."""
+    import importlib.util
+
+    try:
+        spec = importlib.util.find_spec("sae_lens")
+    except (ImportError, ValueError):
+        return None
+    if spec is None or not spec.submodule_search_locations:
+        return None
+    for root in spec.submodule_search_locations:
+        path = os.path.join(root, "pretrained_saes.yaml")
+        if os.path.isfile(path):
+            return path
+    return None
+
+
+def directory_files() -> list[str]:
+    """The YAML files the directory is read from, lowest precedence first."""
+    out = [str(files("saelens_b200.loading").joinpath("pretrained_saes.yaml"))]
+    ref = installed_sae_lens_directory()
+    if ref:
+        out.append(ref)
+    for extra in os.environ.get("SAELENS_B200_PRETRAINED_YAML", "").split(os.pathsep):
+        if extra and os.path.exists(extra):
+            out.append(extra)
+    return out
+
+
 @cache
 def _load_files() -> dict[str, PretrainedSAELookup]:
     directory: dict[str, PretrainedSAELookup] = {}
-    with files("saelens_b200.loading").joinpath("pretrained_saes.yaml").open("r") as f:
-        directory.update(_parse(yaml.safe_load(f)))
-    extra = os.environ.get("SAELENS_B200_PRETRAINED_YAML")
-    if extra and os.path.exists(extra):
-        with open(extra) as f:
+    for path in directory_files():
+        with open(path) as f:
             directory.update(_parse(yaml.safe_load(f)))
     return directory
 

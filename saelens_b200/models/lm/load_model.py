@@ -3,6 +3,13 @@
 * "HookedTransformer" / "HookedLM" / "HookedSAETransformer": this package's `HookedLM`; a preset
   name (e.g. "gpt2", "meta-llama/Meta-Llama-3-8B") gives a random-init model of that shape, a local
   Hugging Face checkpoint directory is converted weight for weight.
+* "VLLMModel": the reference's vLLM activation producer (sae_lens/vllm_model.py:548).  Here it is
+  this package's producer, `HookedLM`, resolved like "HookedTransformer": it runs to the hooked
+  layer on the framework's own kernels (tcgen05 GEMMs and attention).  vLLM engine options
+  (`gpu_memory_utilization`, `max_model_len`, `enforce_eager`, `tensor_parallel_size`, ...) have no
+  meaning for it and are dropped; producer tensor parallelism is set by the runner's
+  `vllm_tp_size`.
+* "HookedMamba": needs the `mamba_lens` package, as in the reference.
 * "AutoModelForCausalLM": a `transformers` model (local path, or `from_config` when
   `model_from_pretrained_kwargs={"random_init": True, ...config fields}`) wrapped in
   `HookedProxyLM`.
@@ -27,9 +34,27 @@ def _tokenizer(name: str) -> Any:
         return None
 
 
+# vLLM engine arguments a "VLLMModel" config may carry (sae_lens/vllm_model.py:548-625)
+_VLLM_ENGINE_KWARGS = ("gpu_memory_utilization", "max_model_len", "enforce_eager", "tensor_parallel_size",
+                       "pipeline_parallel_size", "distributed_executor_backend", "max_num_seqs",
+                       "max_num_batched_tokens", "enable_chunked_prefill", "enable_prefix_caching", "seed_vllm",
+                       "trust_remote_code", "swap_space", "kv_cache_dtype", "quantization", "n_devices")
+
+
 def load_model(model_class_name: str, model_name: str, device: str | torch.device | None = None,
                model_from_pretrained_kwargs: dict[str, Any] | None = None) -> Any:
     kw = dict(model_from_pretrained_kwargs or {})
+    if model_class_name == "VLLMModel":
+        for k in _VLLM_ENGINE_KWARGS:
+            kw.pop(k, None)
+        model_class_name = "HookedTransformer"
+    if model_class_name == "HookedMamba":
+        try:
+            from mamba_lens import HookedMamba  # type: ignore[import-not-found]
+        except ImportError as e:
+            raise ValueError("mamba-lens must be installed to load HookedMamba models") from e
+        return HookedMamba.from_pretrained(model_name, device=device, **kw)
+    kw.pop("n_devices", None)
     dtype = kw.pop("dtype", None)
     for ignored in ("center_writing_weights", "fold_ln", "center_unembed", "refactor_factored_attn_matrices"):
         kw.pop(ignored, None)

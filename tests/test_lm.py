@@ -120,3 +120,22 @@ def test_hooked_proxy_to_tokens_options_and_unknown_model_class():
             proxy.to_tokens("hi", **kw)
     with pytest.raises(ValueError, match="Unknown model class: FakeModelClass"):
         load_model("FakeModelClass", "some-model", device="cpu")
+
+
+def test_load_model_vllm_class_name_gives_the_native_producer():
+    from saelens_b200.models.lm.load_model import load_model
+    from saelens_b200.models.lm.transformer import HookedLM
+
+    lm = load_model("VLLMModel", "gpt2", device="cpu",
+                    model_from_pretrained_kwargs={"gpu_memory_utilization": 0.5, "max_model_len": 128,
+                                                  "enforce_eager": True, "n_layers": 1, "dtype": "float32"})
+    assert isinstance(lm, HookedLM) and lm.cfg.n_layers == 1
+
+
+def test_load_model_hooked_mamba_needs_mamba_lens():
+    import pytest
+
+    from saelens_b200.models.lm.load_model import load_model
+
+    with pytest.raises(ValueError, match="mamba-lens"):
+        load_model("HookedMamba", "state-spaces/mamba-130m")

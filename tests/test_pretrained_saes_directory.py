@@ -70,3 +70,26 @@ def test_norm_scaling_factor_and_loader_name():
     assert get_conversion_loader_name("gpt2-small-res-jb") == "sae_lens"
     info = get_pretrained_saes_directory()["test-scaled-release"]
     assert info.expected_var_explained["l0"] == 0.8 and info.expected_l0["l0"] == 30.0
+
+
+def test_installed_reference_directory_is_found_without_import(tmp_path, monkeypatch):
+    import sys
+
+    from saelens_b200.loading import pretrained_saes_directory as d
+
+    pkg = tmp_path / "sae_lens"
+    pkg.mkdir()
+    (pkg / "__init__.py").write_text("raise ImportError('must not be imported')\n")
+    (pkg / "pretrained_saes.yaml").write_text(
+        "ref-release:\n  repo_id: someone/saes\n  model: gpt2\n  conversion_func: null\n"
+        "  saes:\n  - id: blocks.0.hook_resid_pre\n    path: blocks.0\n    l0: 12.5\n")
+    monkeypatch.syspath_prepend(str(tmp_path))
+    monkeypatch.delitem(sys.modules, "sae_lens", raising=False)
+    d._load_files.cache_clear()
+    try:
+        assert d.installed_sae_lens_directory() == str(pkg / "pretrained_saes.yaml")
+        got = d.get_pretrained_saes_directory()["ref-release"]
+        assert got.repo_id == "someone/saes" and got.expected_l0["blocks.0.hook_resid_pre"] == 12.5
+        assert "sae_lens" not in sys.modules
+    finally:
+        d._load_files.cache_clear()
