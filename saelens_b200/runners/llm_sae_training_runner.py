@@ -89,8 +89,19 @@ class LanguageModelSAETrainingRunner:
                     raise ValueError("the fan-in data path serves SAE TP 1; use shard routing for TP consumers")
                 self.fan_in = True
                 self.role = "producer+consumer" if D.is_sae_active() else "producer"
+        # split roles (local overlap / matched DP with SAE TP): only the replica's LM root runs the LM
+        # and broadcasts each batch to its SAE TP group (sae_lens/training/activations_store.py:617-738)
+        self.split_role = False
+        if not (self.streaming_mode or self.routed or self.fan_in) and self.tp_group is not None:
+            from saelens_b200.parallel import distributed as D
+
+            if D.get_layout_mode() in ("local_overlap", "matched_dp"):
+                self.split_role = True
+                self.role = "producer+consumer" if D.get_worker_rank() == 0 else "consumer"
         if self.routed:
             producer_side, consumer_side = self.is_route_producer, self.is_route_consumer
+        elif self.split_role:
+            producer_side, consumer_side = self.role == "producer+consumer", True
         elif self.fan_in:
             producer_side, consumer_side = True, self.role == "producer+consumer"
         else:
@@ -336,9 +347,18 @@ class LanguageModelSAETrainingRunner:
 
             wandb.init(project=cfg.logger.wandb_project, entity=cfg.logger.wandb_entity, name=cfg.logger.run_name,
                        id=cfg.logger.wandb_id, config=cfg.to_dict())
+        data: Any = self.activations_store
+        if self.split_role:
+            from saelens_b200.parallel import distributed as D
+            from saelens_b200.training.replica_broadcast import ReplicaBroadcastProvider
+            from saelens_b200.utils.misc import str_to_dtype
+
+            data = ReplicaBroadcastProvider(self.activations_store, self.tp_group, D.get_sae_root_rank(),
+                                            self.sae.cfg.d_in, str_to_dtype(cfg.dtype), cfg.act_store_device)
         trainer = SAETrainer(
-            cfg=cfg.to_sae_trainer_config(), sae=self.wrapped, base_sae=self.sae, data_provider=self.activations_store,
-            evaluator=self._evaluator(), save_checkpoint_fn=self._save_checkpoint_extras, dp_group=self.dp_group,
+            cfg=cfg.to_sae_trainer_config(), sae=self.wrapped, base_sae=self.sae, data_provider=data,
+            evaluator=self._evaluator() if self.activations_store is not None else None,
+            save_checkpoint_fn=self._save_checkpoint_extras, dp_group=self.dp_group,
             token_count_weighted_dp=self.token_count_weighted_dp, native_fsdp=self.native_fsdp,
         )
         self.trainer = trainer
@@ -358,7 +378,7 @@ class LanguageModelSAETrainingRunner:
             if trainer.engine is not None and not self.native_fsdp:
                 trainer.engine.refresh()
             trainer.load_trainer_state(ck)
-            if (ck / ACTIVATIONS_STORE_STATE_FILENAME).exists():
+            if (ck / ACTIVATIONS_STORE_STATE_FILENAME).exists() and self.activations_store is not None:
                 self.activations_store.load_from_checkpoint(ck)
         old_int = signal.signal(signal.SIGINT, _interrupt)
         old_term = signal.signal(signal.SIGTERM, _interrupt)
@@ -424,7 +444,7 @@ class LanguageModelSAETrainingRunner:
         return tp == 0 and dp == 0
 
     def _save_checkpoint_extras(self, checkpoint_path: Path | None) -> None:
-        if checkpoint_path is None:
+        if checkpoint_path is None or self.activations_store is None:
             return
         self.activations_store.save_to_checkpoint(checkpoint_path)
         with open(Path(checkpoint_path) / RUNNER_CFG_FILENAME, "w") as f:
