@@ -13,8 +13,12 @@ Hooks (per block i): `hook_resid_pre`, `ln1.hook_normalized`, `attn.hook_q/k/v` 
 `run_with_cache(tokens, names_filter, stop_at_layer=n)` runs only blocks [0, n), which is how the
 SAE data pipeline stops right after the hooked layer.
 
-On CUDA with bf16 weights, the q/k/v, output and MLP projections run on this package's tcgen05
-GEMM (`saelens_b200.ops.gemm_tn`); attention uses `scaled_dot_product_attention`.
+On CUDA with bf16 weights and no autograd, the forward runs on this package's kernels: the
+q/k/v, output, MLP and unembedding projections on the tcgen05 GEMM (`saelens_b200.ops.gemm_tn`),
+causal grouped-query attention (with Gemma-2's soft-cap) on the tcgen05 attention kernel
+(`saelens_b200.ops.attention`), RMSNorm / LayerNorm, rotary embeddings, the gated activation and
+the embedding gather on the elementwise kernels.  On CPU, or with autograd, the same math runs in
+PyTorch (the CPU oracle of the tests).
 """
 
 from __future__ import annotations
@@ -124,19 +128,20 @@ def preset_config(name: str, **overrides: Any) -> LMConfig:
 
 # ------------------------------------------------------------------------------ layers
 class NativeLinear(nn.Module):
-    """y = x W^T + b with W [out, in]; the tcgen05 GEMM on CUDA bf16 when the shape allows."""
+    """y = x W^T + b with W [out, in]; the tcgen05 GEMM on CUDA bf16 (any width; the input width a
+    multiple of 8 elements, i.e. 16-byte rows)."""
 
     def __init__(self, d_in: int, d_out: int, bias: bool, dtype: torch.dtype, device: Any = None):
         super().__init__()
         self.weight = nn.Parameter(torch.empty(d_out, d_in, dtype=dtype, device=device))
         self.bias = nn.Parameter(torch.zeros(d_out, dtype=dtype, device=device)) if bias else None
-        self._native_ok = d_out % 256 == 0 and d_in % 64 == 0
+        self._native_ok = d_in % 8 == 0
         self._bias_f32: torch.Tensor | None = None
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         w = self.weight
         if (self._native_ok and x.is_cuda and w.dtype == torch.bfloat16 and x.dtype == torch.bfloat16
-                and not torch.is_grad_enabled()):
+                and not torch.is_grad_enabled() and not FORCE_TORCH):
             from saelens_b200 import ops
 
             if ops.available():
@@ -150,6 +155,8 @@ class NativeLinear(nn.Module):
                         self._bias_f32 = self.bias.detach().float().contiguous()
                     b = self._bias_f32
                 out, _ = ops.gemm_tn(x2, w, bias=b)
+                if not out.is_contiguous():  # a width that is not a multiple of 8
+                    out = out.contiguous()
                 return out.view(*shp[:-1], w.shape[0])
         return F.linear(x, w, self.bias)
 
@@ -158,9 +165,59 @@ class NativeLinear(nn.Module):
         super()._load_from_state_dict(*args, **kwargs)
 
 
+class _FusedWeights:
+    """Row-concatenation of several projections' weights (and fp32 biases), rebuilt whenever one of
+    them changes (storage or in-place version), so one tcgen05 GEMM computes all of them."""
+
+    def __init__(self) -> None:
+        self._key: tuple | None = None
+        self.w: torch.Tensor | None = None
+        self.b: torch.Tensor | None = None
+
+    def get(self, layers: list[NativeLinear]) -> tuple[torch.Tensor, torch.Tensor | None]:
+        params = [p for m in layers for p in ((m.weight,) if m.bias is None else (m.weight, m.bias))]
+        key = tuple((p.data_ptr(), p._version) for p in params)
+        if key != self._key:
+            self.w = torch.cat([m.weight.detach() for m in layers]).contiguous()
+            has_b = any(m.bias is not None for m in layers)
+            self.b = torch.cat([m.bias.detach().float() if m.bias is not None else
+                                torch.zeros(m.weight.shape[0], device=m.weight.device) for m in layers]) if has_b else None
+            self._key = key
+        assert self.w is not None
+        return self.w, self.b
+
+
+def _fused_linear(x: torch.Tensor, cache: _FusedWeights, layers: list[NativeLinear]) -> torch.Tensor:
+    """[..., sum of the layers' widths] output of one tcgen05 GEMM over the concatenated weights."""
+    from saelens_b200 import ops
+
+    w, b = cache.get(layers)
+    x2 = x.reshape(-1, x.shape[-1])
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    out, _ = ops.gemm_tn(x2, w, bias=b)
+    return out.view(*x.shape[:-1], w.shape[0]) if out.is_contiguous() else out.reshape(*x.shape[:-1], w.shape[0])
+
+
+def _tied_unembed(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """x @ w.T with the embedding matrix (tied unembedding) on the tcgen05 GEMM when possible."""
+    if x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.shape[-1] % 8 == 0 and _native_ok(x):
+        from saelens_b200 import ops
+
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        out, _ = ops.gemm_tn(x2, w)
+        return out.contiguous().view(*x.shape[:-1], w.shape[0])
+    return x @ w.T
+
+
+# Set to True to run the producer on PyTorch ops even on CUDA (the comparison arm of the
+# producer timing case); never needed otherwise.
+FORCE_TORCH = False
+
+
 def _native_ok(t: torch.Tensor) -> bool:
     """Use the framework's CUDA kernels for inference-mode producer ops on a CUDA tensor."""
-    if not (t.is_cuda and not torch.is_grad_enabled()):
+    if FORCE_TORCH or not (t.is_cuda and not torch.is_grad_enabled()):
         return False
     from saelens_b200 import ops
 
@@ -186,6 +243,15 @@ class Norm(nn.Module):
             if not x2.is_contiguous():
                 x2 = x2.contiguous()
             y = native().rmsnorm(x2, self.w, self.eps, self.one_plus).view(x.shape)
+            return self.hook_normalized(y)
+        if (not self.rms and x.dtype in (torch.bfloat16, torch.float32) and x.dtype == self.w.dtype
+                and x.shape[-1] % 8 == 0 and _native_ok(x)):
+            from saelens_b200.ops import native
+
+            x2 = x.reshape(-1, x.shape[-1])
+            if not x2.is_contiguous():
+                x2 = x2.contiguous()
+            y = native().layernorm(x2, self.w, self.b, self.eps).view(x.shape)
             return self.hook_normalized(y)
         xf = x.float()
         if self.rms:
@@ -245,16 +311,45 @@ class Attention(nn.Module):
         self.hook_z = HookPoint()
         self.hook_rot_q, self.hook_rot_k = HookPoint(), HookPoint()
         self.scale = 1.0 / math.sqrt(cfg.query_pre_attn_scalar if cfg.query_pre_attn_scalar else dh)
+        self._qkv = _FusedWeights()
 
     def forward(self, x: torch.Tensor, rot: tuple[torch.Tensor, torch.Tensor] | None) -> torch.Tensor:
         B, S, _ = x.shape
         H, KV, dh = self.cfg.n_heads, self.cfg.n_key_value_heads, self.cfg.d_head
-        q = self.hook_q(self.q(x).view(B, S, H, dh))
-        k = self.hook_k(self.k(x).view(B, S, KV, dh))
-        v = self.hook_v(self.v(x).view(B, S, KV, dh))
+        fused = (x.dtype == torch.bfloat16 and self.q.weight.dtype == torch.bfloat16 and x.shape[-1] % 8 == 0
+                 and _native_ok(x))
+        if fused:
+            # one GEMM for q, k and v; the heads are strided views of its output
+            qkv = _fused_linear(x, self._qkv, [self.q, self.k, self.v])
+            q = self.hook_q(qkv[..., : H * dh].view(B, S, H, dh))
+            k = self.hook_k(qkv[..., H * dh : (H + KV) * dh].view(B, S, KV, dh))
+            v = self.hook_v(qkv[..., (H + KV) * dh :].view(B, S, KV, dh))
+        else:
+            q = self.hook_q(self.q(x).view(B, S, H, dh))
+            k = self.hook_k(self.k(x).view(B, S, KV, dh))
+            v = self.hook_v(self.v(x).view(B, S, KV, dh))
         if rot is not None:
-            q = self.hook_rot_q(apply_rotary(q, *rot))
-            k = self.hook_rot_k(apply_rotary(k, *rot))
+            in_place = (fused and rot[0].dtype == torch.float32 and not (self.hook_q.has_hooks or self.hook_k.has_hooks)
+                        and q.stride(-1) == 1 and k.stride(-1) == 1)
+            if in_place:
+                # nothing holds the pre-rotation values: rotate q and k where they are
+                from saelens_b200.ops import native
+
+                cos, sin = rot[0].contiguous(), rot[1].contiguous()
+                native().rope_(q, cos, sin, 0)
+                native().rope_(k, cos, sin, 0)
+                q, k = self.hook_rot_q(q), self.hook_rot_k(k)
+            else:
+                q = self.hook_rot_q(apply_rotary(q, *rot))
+                k = self.hook_rot_k(apply_rotary(k, *rot))
+        if q.dtype == torch.bfloat16 and dh in (64, 128, 256) and _native_ok(q):
+            from saelens_b200 import ops
+
+            # tcgen05 prefill attention: K/V heads are read in place by their query-head group,
+            # the soft-cap (Gemma-2) is applied to the logits inside the kernel
+            z = ops.attention(q, k, v, self.scale, softcap=self.cfg.attn_softcap, causal=True)
+            z = self.hook_z(z)
+            return self.o(z.reshape(B, S, H * dh))
         qh, kh, vh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
         if KV != H:
             rep = H // KV
@@ -284,13 +379,28 @@ class MLP(nn.Module):
         self.hook_in = HookPoint()  # the MLP's input (after the pre-MLP norm): transcoders read it
         self.hook_pre = HookPoint()
         self.hook_post = HookPoint()
+        self._gate_up = _FusedWeights()
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         x = self.hook_in(x)
         if self.gated:
+            kind = {"silu": 0, "gelu_new": 1, "gelu_pytorch_tanh": 1}.get(self.cfg.act_fn)
+            d = self.cfg.d_mlp
+            if (kind is not None and x.dtype == torch.bfloat16 and self.gate.weight.dtype == torch.bfloat16
+                    and x.shape[-1] % 8 == 0 and d % 8 == 0 and _native_ok(x)):
+                # one GEMM for the gate and up projections; the activation reads both halves in place
+                from saelens_b200.ops import native
+
+                gu = _fused_linear(x, self._gate_up, [self.gate, self.up])
+                pre = self.hook_pre(gu[..., :d])
+                up = gu[..., d:]
+                if pre.shape == up.shape and pre.stride(-1) == 1:
+                    post = self.hook_post(native().gated_act(pre, up, kind))
+                else:
+                    post = self.hook_post(_act(self.cfg.act_fn, pre) * up)
+                return self.down(post)
             pre = self.hook_pre(self.gate(x))
             up = self.up(x)
-            kind = {"silu": 0, "gelu_new": 1, "gelu_pytorch_tanh": 1}.get(self.cfg.act_fn)
             if kind is not None and pre.dtype == torch.bfloat16 and pre.shape == up.shape and _native_ok(pre):
                 from saelens_b200.ops import native
 
@@ -392,6 +502,32 @@ class HookedLM(HookedRootModule):
             self._rot = rotary_tables(max(S, self.cfg.n_ctx), self.cfg.d_head or 0, self.cfg.rotary_base, dev)
         return self._rot[0][:S], self._rot[1][:S]
 
+    def _embed(self, tokens: torch.Tensor) -> torch.Tensor:
+        """Token embedding (times sqrt(d_model) for Gemma) plus learned positions when present.
+        With no hooks on `hook_embed` / `hook_pos_embed` the gather, scale and position add are one
+        kernel on CUDA."""
+        S = tokens.shape[1]
+        w = self.embed.weight
+        hooked = self.hook_embed.has_hooks or (self.cfg.positional == "standard" and self.hook_pos_embed.has_hooks)
+        if (not hooked and w.dtype in (torch.bfloat16, torch.float32) and w.shape[1] % 8 == 0 and _native_ok(w)):
+            from saelens_b200.ops import native
+
+            scale = math.sqrt(self.cfg.d_model) if self.cfg.embed_scale else 1.0
+            if scale != 1.0 and w.dtype == torch.bfloat16:
+                scale = float(torch.tensor(scale, dtype=torch.bfloat16))  # the eager path's bf16 constant
+            pos = self.pos_embed.weight if self.cfg.positional == "standard" else None
+            bad = torch.zeros(1, dtype=torch.int32, device=w.device)
+            x = native().embed(tokens.contiguous(), w, scale, pos, bad)
+            self._bad_tokens = bad
+            return x
+        x = self.hook_embed(self.embed(tokens))
+        if self.cfg.embed_scale:
+            x = x * torch.tensor(math.sqrt(self.cfg.d_model), dtype=x.dtype, device=x.device)
+        if self.cfg.positional == "standard":
+            pos = torch.arange(S, device=tokens.device)
+            x = x + self.hook_pos_embed(self.pos_embed(pos))[None]
+        return x
+
     def forward(self, tokens: torch.Tensor, return_type: str | None = "logits",
                 stop_at_layer: int | None = None, start_at_layer: int | None = None,
                 residual: torch.Tensor | None = None) -> torch.Tensor | None:
@@ -402,12 +538,7 @@ class HookedLM(HookedRootModule):
             if tokens.dim() == 1:
                 tokens = tokens.unsqueeze(0)
             S = tokens.shape[1]
-            x = self.hook_embed(self.embed(tokens))
-            if self.cfg.embed_scale:
-                x = x * torch.tensor(math.sqrt(self.cfg.d_model), dtype=x.dtype, device=x.device)
-            if self.cfg.positional == "standard":
-                pos = torch.arange(S, device=tokens.device)
-                x = x + self.hook_pos_embed(self.pos_embed(pos))[None]
+            x = self._embed(tokens)
             start = 0
         else:
             assert residual is not None
@@ -423,7 +554,7 @@ class HookedLM(HookedRootModule):
         x = self.ln_final(x)
         if return_type == "residual":
             return x
-        logits = x @ self.W_U.T if self.unembed is None else self.unembed(x)
+        logits = _tied_unembed(x, self.W_U) if self.unembed is None else self.unembed(x)
         if self.cfg.final_softcap:
             logits = self.cfg.final_softcap * torch.tanh(logits.float() / self.cfg.final_softcap)
         if return_type == "logits":

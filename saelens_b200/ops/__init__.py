@@ -19,6 +19,7 @@ __all__ = [
     "gemm_tn",
     "row_topk",
     "decode_mse",
+    "attention",
     "StatusWord",
 ]
 
@@ -51,13 +52,15 @@ def gemm_tn(
 ) -> tuple[torch.Tensor | None, torch.Tensor | None]:
     """`epilogue(a @ b.T)` on the tcgen05 tensor cores.
 
-    a: [M, K] bf16, b: [N, K] bf16 (K contiguous, K % 64 == 0, N % 256 == 0).
-    Epilogue: `(acc + bias) * scale`, optional ReLU, rounded to bf16.  With `chunk_max` it also
-    returns the max of every 32-column chunk ([M, N/32] bf16).
+    a: [M, K] bf16, b: [N, K] bf16 (K contiguous, K % 8 == 0; any N, with N % 256 == 0 when
+    `chunk_max` is set).  Epilogue: `(acc + bias) * scale`, optional ReLU, rounded to bf16.  With
+    `chunk_max` it also returns the max of every 32-column chunk ([M, N/32] bf16).  When N is not
+    a multiple of 8 the result is a view of rows padded to a multiple of 8 (16-byte rows).
     """
     M, N = a.shape[0], b.shape[0]
     if out is None:
-        out = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
+        n_alloc = (N + 7) // 8 * 8
+        out = torch.empty(M, n_alloc, dtype=torch.bfloat16, device=a.device)[:, :N]
     cmax = torch.empty(M, N // 32, dtype=torch.bfloat16, device=a.device) if chunk_max else None
     st = status or StatusWord(a.device)
     native().gemm_tn_bf16(a, b, bias, scale, relu, out, cmax, st.tensor, max_ctas)
@@ -126,3 +129,64 @@ def decode_mse(
     if bsum is not None:
         res["bsum"] = bsum
     return res
+
+
+def attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    scale: float,
+    softcap: float | None = None,
+    causal: bool = True,
+    out: torch.Tensor | None = None,
+    status: StatusWord | None = None,
+) -> torch.Tensor:
+    """Prefill attention on the tcgen05 tensor cores.
+
+    q: [B, S, H, D], k / v: [B, S, KV, D] bf16 (head dim contiguous, heads adjacent within a
+    token; H a multiple of KV, query head h reads K/V head h // (H / KV)).  Returns
+    softmax(cap(q k^T * scale)) v as [B, S, H, D] bf16, causal unless `causal=False`, with
+    cap(x) = softcap * tanh(x / softcap) when `softcap` is given.  D in {64, 128, 256}.
+    """
+    if q.dim() != 4 or q.shape[-1] not in (64, 128, 256):
+        raise ValueError(f"attention: head dim must be 64, 128 or 256, got shape {tuple(q.shape)}")
+    if k.shape[2] < 1 or q.shape[2] % k.shape[2]:
+        raise ValueError("attention: query heads must be a multiple of the K/V heads")
+    if out is None:
+        out = torch.empty(q.shape, dtype=torch.bfloat16, device=q.device)
+    st = status or StatusWord(q.device)
+    native().attention_fwd(q, k, v, out, float(scale), float(softcap or 0.0), bool(causal), st.tensor)
+    if status is None:
+        st.check("attention")
+    return out
+
+
+def gemm_dense(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    a_mn: bool = False,
+    b_mn: bool = False,
+    out: torch.Tensor | None = None,
+    want_out: bool = True,
+    status: StatusWord | None = None,
+    **epi: object,
+) -> torch.Tensor | None:
+    """Dense GEMM of the dense SAE steps on tcgen05: `epilogue(A @ B^T)` with A given as [M, K]
+    (or [K, M] when `a_mn`) and B as [N, K] (or [K, N] when `b_mn`), bf16.
+
+    Epilogue keywords (all optional, see `gemm_dense_bf16`): out2, bias, r1_row / r1_col, thr,
+    relu, hin / bandwidth / l0c / gthr (JumpReLU backward), target / res_coef / loss (residual),
+    colsum, colcnt, nnz, sumsq, gate_bias / mag_scale (gated SAE), rs_bases / rs_rank / rs_off / rs_n
+    (reduce-scatter: rows stored into their owners' landing slots over NVLink, with
+    `want_out=False`).  Returns `out` ([M, N] bf16), or None with `want_out=False`.
+    """
+    M = a.shape[1] if a_mn else a.shape[0]
+    N = b.shape[1] if b_mn else b.shape[0]
+    if out is None and want_out:
+        n_alloc = (N + 7) // 8 * 8
+        out = torch.empty(M, n_alloc, dtype=torch.bfloat16, device=a.device)[:, :N]
+    st = status or StatusWord(a.device)
+    native().gemm_dense_bf16(a, a_mn, b, b_mn, out=out if want_out else None, status=st.tensor, **epi)
+    if status is None:
+        st.check("gemm_dense")
+    return out

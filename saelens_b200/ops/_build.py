@@ -29,6 +29,7 @@ SOURCES = [
     "p2p.cu",
     "symm.cpp",
     "lm_kernels.cu",
+    "attention.cu",
 ]
 
 NVCC_FLAGS = [

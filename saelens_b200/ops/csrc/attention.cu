@@ -1,0 +1,371 @@
+// Prefill attention for the activation-producing LM on tcgen05 (causal or full, grouped-query,
+// optional logit soft-capping):
+//
+//   z[b, s, h, :] = sum_t softmax_t( cap(q[b,s,h] . k[b,t,h/g] * scale) ) v[b,t,h/g]      (t <= s if causal)
+//
+// q is [B, S, H, D] and k, v are [B, S, KV, D] (bf16, head dim contiguous, any token stride, so
+// views into a fused QKV projection work); g = H / KV query heads share one K/V head, which is
+// read from its own rows (no repeat of K/V).  `cap` is the identity or x -> c * tanh(x / c)
+// (Gemma-2's attention soft-capping).  Replaces `F.scaled_dot_product_attention` and the eager
+// soft-capped path of the producer (the reference runs its producer in HookedTransformer or in
+// vLLM's kernels: sae_lens/vllm_model.py:626-743, sae_lens/load_model.py:17-67).
+//
+// One CTA computes 128 query rows of one head (the heaviest causal tiles are scheduled first):
+//   warp 0      TMA: the Q tile once, then K and V tiles of BN rows through 2 stages (SWIZZLE_128B)
+//   warp 1      MMA: S_j = Q K_j^T into one of two TMEM buffers (M=128, N=BN), and after the
+//               softmax has produced P_j, O += P_j V_j (M=128, N=D, V read MN-major) in TMEM
+//   warps 2..5  softmax, one query row per thread: tcgen05.ld of S_j, scale / soft-cap / causal
+//               mask, running max and sum (online softmax), P_j as bf16 into shared memory in the
+//               K-major SWIZZLE_128B layout the MMA reads; O is rescaled in TMEM only when the row
+//               max grew by more than 2^8 since the last rescale (exact: the stale max only bounds
+//               P by 256), and at the end O / l is written out as bf16.
+// S_{j+1} is computed while the softmax works on S_j.  Every wait is bounded (status word).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "tmap.h"
+
+namespace sb {
+namespace attn {
+
+constexpr int BM = 128;
+constexpr int NUM_SOFTMAX_WARPS = 4;
+constexpr int NUM_THREADS = 64 + 32 * NUM_SOFTMAX_WARPS;
+constexpr int KV_STAGES = 2;
+constexpr int TMEM_COLS = 512;
+constexpr float kRescaleThreshold = 8.f;  // log2 units: rescale O once the max grew by 2^8
+
+template <int D, int BN>
+struct Cfg {
+  static_assert(D % 64 == 0 && BN % 64 == 0, "tiles are made of 64-element swizzle rows");
+  static_assert(2 * BN + D <= TMEM_COLS, "two S buffers and O must fit in TMEM");
+  static constexpr int Q_BYTES = BM * D * 2;
+  static constexpr int KV_BYTES = BN * D * 2;  // one K or one V tile
+  static constexpr int P_BYTES = BM * BN * 2;
+  static constexpr int NUM_BARS = 10;
+  static constexpr int SMEM = Q_BYTES + 2 * KV_STAGES * KV_BYTES + P_BYTES + 1024 + 8 * NUM_BARS + 16;
+};
+
+struct Params {
+  int B, S, H, KV;
+  int causal;
+  float scale_log2;      // softmax scale * log2(e) (no soft-cap)
+  float cap_log2;        // soft-cap c * log2(e), 0 = no soft-cap
+  float scale_over_cap;  // softmax scale / c
+  __nv_bfloat16* out;    // [B, S, H, D] contiguous
+  int* status;
+};
+
+template <int D, int BN>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using C = Cfg<D, BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                                // D/64 chunks of [BM rows x 128 B]
+  uint8_t* sK = sQ + C::Q_BYTES;                     // stage s: D/64 chunks of [BN rows x 128 B]
+  uint8_t* sV = sK + KV_STAGES * C::KV_BYTES;
+  uint8_t* sP = sV + KV_STAGES * C::KV_BYTES;        // BN/64 chunks of [BM rows x 128 B]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + C::P_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* p_full = bars + 7;
+  uint64_t* o_done = bars + 8;
+  uint64_t* drain = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqt = (p.S + BM - 1) / BM;
+  const int qt = nqt - 1 - int(blockIdx.x);  // heaviest causal tiles first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (p.H / p.KV);
+  const int q0 = qt * BM;
+  const int kv_tiles_all = (p.S + BN - 1) / BN;
+  const int n_kv = p.causal ? min((q0 + BM + BN - 1) / BN, kv_tiles_all) : kv_tiles_all;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < KV_STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+    }
+    mbar_init(p_full, NUM_SOFTMAX_WARPS * 32);
+    mbar_init(o_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tO = tmem_base + 2 * BN;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (elect_one()) {
+      mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+      for (int c = 0; c < D / 64; ++c) tma_load_3d(sQ + c * BM * 128, &tmQ, q_full, h * D + c * 64, q0, b);
+      int issued = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait_bounded(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.status, kTimeoutTmaProducer)) break;
+        mbar_arrive_expect_tx(&kv_full[s], 2 * C::KV_BYTES);
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_3d(sK + s * C::KV_BYTES + c * BN * 128, &tmK, &kv_full[s], kvh * D + c * 64, j * BN, b);
+          tma_load_3d(sV + s * C::KV_BYTES + c * BN * 128, &tmV, &kv_full[s], kvh * D + c * 64, j * BN, b);
+        }
+        issued = j + 1;
+      }
+      // every copy issued lands before the CTA leaves (bounded, also after an abort; in a normal
+      // run these phases completed long ago)
+      volatile int keep_waiting = 0;
+      mbar_wait_bounded(q_full, 0, &keep_waiting, nullptr, 0);
+      for (int j = max(0, issued - KV_STAGES); j < issued; ++j)
+        mbar_wait_bounded(&kv_full[j & 1], (j >> 1) & 1, &keep_waiting, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      const uint32_t idesc_qk = make_idesc_bf16_f32(BM, BN);
+      const uint32_t idesc_pv = make_idesc_bf16_f32(BM, D) | (1u << 16);  // B (= V) MN-major
+      bool ok = mbar_wait_bounded(q_full, 0, abort_flag, p.status, kTimeoutMmaFull);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait_bounded(&kv_full[s], (j >> 1) & 1, abort_flag, p.status, kTimeoutMmaFull)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int chunk = kk >> 2, within = kk & 3;
+          const uint64_t a = make_sdesc_sw128_kmajor(smem_u32(sQ + chunk * BM * 128 + within * 32));
+          const uint64_t bd = make_sdesc_sw128_kmajor(smem_u32(sK + s * C::KV_BYTES + chunk * BN * 128 + within * 32));
+          umma_bf16_ss(tmem_base + s * BN, a, bd, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[s]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && n_kv > 1) ok = issue_s(1);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        if (!mbar_wait_bounded(p_full, j & 1, abort_flag, p.status, kTimeoutMmaFull)) break;
+        tc_fence_after();
+        const int s = j & 1;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const int chunk = kk >> 2, within = kk & 3;
+          const uint64_t a = make_sdesc_sw128_kmajor(smem_u32(sP + chunk * BM * 128 + within * 32));
+          const uint64_t bd = make_sdesc_sw128_mnmajor(smem_u32(sV + s * C::KV_BYTES + kk * 16 * 128), BN * 128);
+          umma_bf16_ss(tO, a, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&kv_empty[s]);
+        umma_commit(o_done);
+        if (j + 2 < n_kv) ok = issue_s(j + 2);
+      }
+      // every MMA issued above completes before TMEM is released
+      umma_commit(drain);
+      volatile int keep_waiting = 0;
+      mbar_wait_bounded(drain, 0, &keep_waiting, nullptr, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax (one row per thread)
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const int q_idx = q0 + row;
+    const uint32_t lane_base = uint32_t(quad * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int s = j & 1;
+      // warp-uniform outcome: the tcgen05.ld below is a whole-warp instruction
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&s_full[s], (j >> 1) & 1, abort_flag, p.status, kTimeoutEpilogue))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float v[BN];
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + lane_base + s * BN + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float x = __uint_as_float(r[e]);
+          float t = p.cap_log2 > 0.f ? p.cap_log2 * tanhf(x * p.scale_over_cap) : x * p.scale_log2;
+          const int kv_idx = j * BN + c * 32 + e;
+          if ((p.causal && kv_idx > q_idx) || kv_idx >= p.S) t = -INFINITY;
+          v[c * 32 + e] = t;
+          tmax = fmaxf(tmax, t);
+        }
+      }
+      bool need = false;
+      float m_new = m_run;
+      if (tmax > m_run + kRescaleThreshold) {
+        m_new = tmax;
+        need = true;
+      }
+      const float alpha = need ? exp2f(m_run - m_new) : 1.f;  // m_run = -inf -> 0 (l_run is 0 then)
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      if (j > 0) {
+        // P_{j-1} V_{j-1} has finished: the P buffer is free and O holds every earlier tile
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(o_done, (j - 1) & 1, abort_flag, p.status, kTimeoutEpilogue))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tO + lane_base + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+            tmem_st_32x32b_x32(tO + lane_base + c * 32, r);
+          }
+          tmem_st_wait();
+        }
+      }
+      l_run *= alpha;
+      m_run = m_new;
+      float rowsum = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < BN / 64; ++cc) {
+        uint8_t* prow = sP + cc * BM * 128 + row * 128;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          uint32_t packed[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float e0 = exp2f(v[cc * 64 + g * 8 + 2 * i] - m_use);
+            const float e1 = exp2f(v[cc * 64 + g * 8 + 2 * i + 1] - m_use);
+            const __nv_bfloat162 h2 = __floats2bfloat162_rn(e0, e1);
+            rowsum += __low2float(h2) + __high2float(h2);
+            packed[i] = *reinterpret_cast<const uint32_t*>(&h2);
+          }
+          *reinterpret_cast<uint4*>(prow + ((g ^ (row & 7)) << 4)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        }
+      }
+      l_run += rowsum;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && n_kv > 0 &&
+        __all_sync(0xffffffffu, mbar_wait_bounded(o_done, (n_kv - 1) & 1, abort_flag, p.status, kTimeoutEpilogue))) {
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      __nv_bfloat16* dst = p.out + ((int64_t(b) * p.S + q_idx) * p.H + h) * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tO + lane_base + c * 32, r);
+        tmem_ld_wait();
+        uint32_t packed[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const __nv_bfloat162 h2 =
+              __floats2bfloat162_rn(__uint_as_float(r[2 * e]) * inv, __uint_as_float(r[2 * e + 1]) * inv);
+          packed[e] = *reinterpret_cast<const uint32_t*>(&h2);
+        }
+        if (q_idx < p.S) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) d4[e] = make_uint4(packed[4 * e], packed[4 * e + 1], packed[4 * e + 2], packed[4 * e + 3]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+template <int D, int BN>
+void launch(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const Params& prm) {
+  using C = Cfg<D, BN>;
+  const int B = prm.B, S = prm.S, H = prm.H, KV = prm.KV;
+  const auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap tq = make_tmap_3d(q.data_ptr(), bf, 2, uint64_t(H) * D, S, B, q.stride(1) * 2, q.stride(0) * 2, 64, BM, 1,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tk = make_tmap_3d(k.data_ptr(), bf, 2, uint64_t(KV) * D, S, B, k.stride(1) * 2, k.stride(0) * 2, 64, BN,
+                                1, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tv = make_tmap_3d(v.data_ptr(), bf, 2, uint64_t(KV) * D, S, B, v.stride(1) * 2, v.stride(0) * 2, 64, BN,
+                                1, CU_TENSOR_MAP_SWIZZLE_128B);
+  auto kern = attn_fwd_kernel<D, BN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    attr_set = true;
+  }
+  const dim3 grid((S + BM - 1) / BM, H, B);
+  kern<<<grid, NUM_THREADS, C::SMEM, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, prm);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace attn
+
+// q [B, S, H, D], k / v [B, S, KV, D] bf16 (head dim contiguous, heads adjacent within a token,
+// token and batch strides multiples of 8 elements); out [B, S, H, D] contiguous bf16.
+// softcap <= 0 disables soft-capping.  D must be 64, 128 or 256.
+void attention_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& out,
+                   double scale, double softcap, bool causal, const torch::Tensor& status) {
+  TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda() && out.is_cuda(), "attention_fwd: CUDA tensors required");
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16 &&
+                  out.scalar_type() == at::kBFloat16,
+              "attention_fwd: bf16 tensors required");
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "attention_fwd: q, k, v must be [B, S, heads, D]");
+  const int64_t B = q.size(0), S = q.size(1), H = q.size(2), D = q.size(3), KV = k.size(2);
+  TORCH_CHECK(D == 64 || D == 128 || D == 256, "attention_fwd: head dim must be 64, 128 or 256, got ", D);
+  TORCH_CHECK(k.size(0) == B && k.size(1) == S && k.size(3) == D && v.sizes() == k.sizes(), "attention_fwd: k/v shape");
+  TORCH_CHECK(KV >= 1 && H % KV == 0, "attention_fwd: query heads must be a multiple of the K/V heads");
+  for (const auto* t : {&q, &k, &v}) {
+    TORCH_CHECK(t->stride(3) == 1 && t->stride(2) == D && t->stride(1) % 8 == 0 && t->stride(0) % 8 == 0,
+                "attention_fwd: head dim contiguous, heads adjacent, token/batch strides multiples of 8");
+  }
+  TORCH_CHECK(out.is_contiguous() && out.sizes() == q.sizes(), "attention_fwd: out must be contiguous [B, S, H, D]");
+  TORCH_CHECK(status.is_cuda() && status.scalar_type() == at::kInt, "attention_fwd: status");
+  TORCH_CHECK(B <= 65535 && H <= 65535 && S < (1 << 30), "attention_fwd: size");
+  if (B == 0 || S == 0 || H == 0) return;
+  const at::cuda::CUDAGuard guard(q.device());
+  attn::Params prm{};
+  prm.B = int(B);
+  prm.S = int(S);
+  prm.H = int(H);
+  prm.KV = int(KV);
+  prm.causal = causal ? 1 : 0;
+  const float log2e = 1.4426950408889634f;
+  prm.scale_log2 = float(scale) * log2e;
+  prm.cap_log2 = softcap > 0 ? float(softcap) * log2e : 0.f;
+  prm.scale_over_cap = softcap > 0 ? float(scale / softcap) : 0.f;
+  prm.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  prm.status = status.data_ptr<int>();
+  switch (D) {
+    case 64: attn::launch<64, 128>(q, k, v, prm); break;
+    case 128: attn::launch<128, 128>(q, k, v, prm); break;
+    default: attn::launch<256, 64>(q, k, v, prm); break;  // D == 256 (checked above)
+  }
+}
+
+}  // namespace sb

@@ -125,6 +125,31 @@ void p2p_signal(const std::vector<int64_t>& peer_bases, int64_t rank, int64_t of
 torch::Tensor rmsnorm(const torch::Tensor& x, const torch::Tensor& w, double eps, bool one_plus);
 void rope_(const torch::Tensor& x, const torch::Tensor& cos, const torch::Tensor& sin, int64_t pos0);
 torch::Tensor gated_act(const torch::Tensor& gate, const torch::Tensor& up, int64_t kind);
+torch::Tensor layernorm(const torch::Tensor& x, const torch::Tensor& w, const c10::optional<torch::Tensor>& b,
+                        double eps);
+torch::Tensor embed(const torch::Tensor& tokens, const torch::Tensor& table, double scale,
+                    const c10::optional<torch::Tensor>& pos, const torch::Tensor& bad);
+void gemm_dense_bf16(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn,
+                     const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& out2,
+                     const c10::optional<torch::Tensor>& bias, const c10::optional<torch::Tensor>& r1_row,
+                     const c10::optional<torch::Tensor>& r1_col, const c10::optional<torch::Tensor>& thr, bool relu,
+                     const c10::optional<torch::Tensor>& hin, double bandwidth, double l0c,
+                     const c10::optional<torch::Tensor>& gthr, const c10::optional<torch::Tensor>& target,
+                     double res_coef, const c10::optional<torch::Tensor>& loss,
+                     const c10::optional<torch::Tensor>& colsum, const c10::optional<torch::Tensor>& colcnt,
+                     const c10::optional<torch::Tensor>& nnz, const c10::optional<torch::Tensor>& sumsq,
+                     const c10::optional<torch::Tensor>& gate_bias, const c10::optional<torch::Tensor>& mag_scale,
+                     const torch::Tensor& status, int64_t max_ctas, const std::vector<int64_t>& rs_bases,
+                     int64_t rs_rank, int64_t rs_off, int64_t rs_n);
+void gemm_fsdp_dense_bf16(const torch::Tensor& A, const torch::Tensor& w_own, const std::vector<int64_t>& peer_bases,
+                          int64_t rank, int64_t w_off, int64_t flag_off, bool push, int64_t epoch,
+                          const c10::optional<torch::Tensor>& w2_own, int64_t w2_off, int64_t flag2_off,
+                          const torch::Tensor& out, const c10::optional<torch::Tensor>& out2,
+                          const c10::optional<torch::Tensor>& bias, const c10::optional<torch::Tensor>& thr,
+                          const c10::optional<torch::Tensor>& colcnt, const c10::optional<torch::Tensor>& nnz,
+                          const torch::Tensor& status, const torch::Tensor& ticket);
+void attention_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& out,
+                   double scale, double softcap, bool causal, const torch::Tensor& status);
 torch::Tensor batch_topk_select(const torch::Tensor& vals, const torch::Tensor& idx, int64_t K,
                                 const c10::optional<torch::Tensor>& truncated);
 void batch_hist(const torch::Tensor& vals, const torch::Tensor& idx, const torch::Tensor& hist);
@@ -192,6 +217,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("batch_filter", &sb::batch_filter);
   m.def("rope_", &sb::rope_);
   m.def("gated_act", &sb::gated_act);
+  m.def("layernorm", &sb::layernorm);
+  m.def("embed", &sb::embed);
+  m.def("gemm_dense_bf16", &sb::gemm_dense_bf16, py::arg("A"), py::arg("a_mn"), py::arg("B"), py::arg("b_mn"),
+        py::arg("out") = py::none(), py::arg("out2") = py::none(), py::arg("bias") = py::none(),
+        py::arg("r1_row") = py::none(), py::arg("r1_col") = py::none(), py::arg("thr") = py::none(),
+        py::arg("relu") = false, py::arg("hin") = py::none(), py::arg("bandwidth") = 0.0, py::arg("l0c") = 0.0,
+        py::arg("gthr") = py::none(), py::arg("target") = py::none(), py::arg("res_coef") = 1.0,
+        py::arg("loss") = py::none(), py::arg("colsum") = py::none(), py::arg("colcnt") = py::none(),
+        py::arg("nnz") = py::none(), py::arg("sumsq") = py::none(), py::arg("gate_bias") = py::none(),
+        py::arg("mag_scale") = py::none(), py::arg("status"), py::arg("max_ctas") = 0,
+        py::arg("rs_bases") = std::vector<int64_t>{}, py::arg("rs_rank") = 0, py::arg("rs_off") = 0,
+        py::arg("rs_n") = 0);
+  m.def("gemm_fsdp_dense_bf16", &sb::gemm_fsdp_dense_bf16);
+  m.def("attention_fwd", &sb::attention_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"),
+        py::arg("scale"), py::arg("softcap"), py::arg("causal"), py::arg("status"));
   m.def("symm_alloc", &sb::symm_alloc);
   m.def("symm_open", &sb::symm_open);
   m.def("symm_close", &sb::symm_close);

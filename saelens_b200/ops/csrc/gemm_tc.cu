@@ -73,6 +73,244 @@ struct Epi {
   int64_t ldt;
 };
 
+// Epilogue of the dense SAE steps (every field optional; order of application below).
+//   v = acc - r1_row[row] * r1_col[col] + bias[col]                      (rank-1 correction, bias)
+//   residual mode (target):  out2 = v (reconstruction), loss += (v - t)^2, v = res_coef * (v - t)
+//   JumpReLU backward (hin): gthr[col] += rect((h - thr) / bw) * (-(thr / bw) * v - l0c),
+//                            v = v * 1[h > thr]
+//   JumpReLU forward (thr, no hin): out2 = v (pre-activation), v = v * 1[v > thr]
+//   gated (gate_bias):       out2 = relu(acc + gate_bias) (gate path), v = 1[acc + gate_bias > 0] *
+//                            relu(acc * mag_scale + bias)        (magnitude path: x (W * e^r) + b_mag)
+//   relu;  out = bf16(v);  then over the stored values: colsum[col] += v, colcnt[col] += 1[v != 0],
+//   nnz += 1[v != 0], sumsq += v^2 (rows >= M and columns >= N contribute nothing).
+struct EpiD {
+  __nv_bfloat16* out;
+  int64_t ldo;
+  __nv_bfloat16* out2;
+  int64_t ldo2;
+  const float* bias;
+  const float* r1_row;
+  const float* r1_col;
+  const float* thr;
+  int relu;
+  const __nv_bfloat16* hin;
+  int64_t ldh;
+  float inv_bw, l0c;
+  float* gthr;
+  const __nv_bfloat16* target;
+  int64_t ldtg;
+  float res_coef;
+  float* loss;
+  float* colsum;
+  float* colcnt;
+  unsigned long long* nnz;
+  float* sumsq;
+  const float* gate_bias;
+  const float* mag_scale;
+  // reduce-scatter mode (rs_n > 0): output row `row` belongs to owner o = row / rs_n and is stored
+  // over NVLink into o's slab at rs_off, slot [P.rank], row (row - o * rs_n) (ldo apart); the
+  // stores are made visible system-wide before the kernel ends
+  p2p::Peers P;
+  int64_t rs_off;
+  int rs_n;
+};
+
+// Sum over the 32 lanes of v[c] for every c; lane L returns the sum for column L.  Butterfly
+// transpose-reduce: 16 + 8 + 4 + 2 + 1 shuffles; `v` is destroyed.
+__device__ __forceinline__ float warp_colsum32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const bool upper = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < o; ++i) {
+      const float send = upper ? v[i] : v[i + o];
+      const float keep = upper ? v[i + o] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  return v[0];
+}
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* p, float (&f)[32]) {
+  const uint4* p4 = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 u = p4[q];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 t = __bfloat1622float2(h[j]);
+      f[8 * q + 2 * j] = t.x;
+      f[8 * q + 2 * j + 1] = t.y;
+    }
+  }
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* p, const float (&f)[32], int n_valid) {
+  if (n_valid >= 32) {
+    uint4* p4 = reinterpret_cast<uint4*>(p);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(f[8 * q + 2 * j], f[8 * q + 2 * j + 1]);
+        w[j] = *reinterpret_cast<uint32_t*>(&h2);
+      }
+      p4[q] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < n_valid) p[j] = __float2bfloat16_rn(f[j]);
+  }
+}
+
+// Dense epilogue of one accumulator tile (see EpiD); `lane` is the thread's lane.
+__device__ __forceinline__ void epilogue_tile_dense(const EpiD& e, uint32_t trow, int row, int M, int N, int nt,
+                                                    int lane) {
+  const bool rowok = row < M;
+  float s_loss = 0.f, s_sq = 0.f, s_nnz = 0.f;
+  const float rr = (e.r1_row && rowok) ? e.r1_row[row] : 0.f;
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(trow + c * 32, r);
+    tmem_ld_wait();
+    const int col0 = nt * BN + c * 32;
+    if (col0 >= N) continue;  // warp-uniform
+    const int nv = min(32, N - col0);
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    if (e.r1_row) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nv) v[j] -= rr * __ldg(e.r1_col + col0 + j);
+    }
+    if (e.gate_bias) {
+      float gate[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const bool ok = j < nv;
+        const float pg = v[j] + (ok ? __ldg(e.gate_bias + col0 + j) : 0.f);
+        const float pm = v[j] * (ok ? __ldg(e.mag_scale + col0 + j) : 0.f) + (ok && e.bias ? __ldg(e.bias + col0 + j) : 0.f);
+        gate[j] = fmaxf(pg, 0.f);
+        v[j] = pg > 0.f ? fmaxf(pm, 0.f) : 0.f;
+      }
+      if (e.out2 && rowok) store_bf16x32(e.out2 + int64_t(row) * e.ldo2 + col0, gate, nv);
+    } else if (e.bias) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nv) v[j] += __ldg(e.bias + col0 + j);
+    }
+    if (e.target) {
+      float t[32];
+      if (rowok && nv == 32) {
+        load_bf16x32(e.target + int64_t(row) * e.ldtg + col0, t);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          t[j] = (rowok && j < nv) ? __bfloat162float(e.target[int64_t(row) * e.ldtg + col0 + j]) : 0.f;
+      }
+      if (e.out2 && rowok) store_bf16x32(e.out2 + int64_t(row) * e.ldo2 + col0, v, nv);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        // the loss uses the bf16-rounded reconstruction the model outputs
+        const float xh = __bfloat162float(__float2bfloat16_rn(v[j]));
+        const float d = xh - t[j];
+        if (rowok && j < nv) s_loss += d * d;
+        v[j] = e.res_coef * d;
+      }
+    }
+    if (e.hin) {
+      float h[32], g[32];
+      if (rowok && nv == 32) {
+        load_bf16x32(e.hin + int64_t(row) * e.ldh + col0, h);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          h[j] = (rowok && j < nv) ? __bfloat162float(e.hin[int64_t(row) * e.ldh + col0 + j]) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const bool ok = rowok && j < nv;
+        const float th = j < nv ? __ldg(e.thr + col0 + j) : 0.f;
+        const float x = (h[j] - th) * e.inv_bw;
+        const bool inwin = ok && x > -0.5f && x < 0.5f;
+        g[j] = inwin ? (-(th * e.inv_bw) * v[j] - e.l0c) : 0.f;
+        v[j] = (ok && h[j] > th) ? v[j] : 0.f;
+      }
+      if (e.gthr) {
+        const float gs = warp_colsum32(g, lane);
+        if (lane < nv && gs != 0.f) atomicAdd(e.gthr + col0 + lane, gs);
+      }
+    } else if (e.thr) {
+      // the gate compares the stored (bf16) pre-activation, as the backward does
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
+      if (e.out2 && rowok) store_bf16x32(e.out2 + int64_t(row) * e.ldo2 + col0, v, nv);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float th = j < nv ? __ldg(e.thr + col0 + j) : 0.f;
+        v[j] = v[j] > th ? v[j] : 0.f;
+      }
+    }
+    if (e.relu) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
+    }
+    // round to what is stored; statistics are taken over the stored values
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = (rowok && j < nv) ? __bfloat162float(__float2bfloat16_rn(v[j])) : 0.f;
+    if (e.rs_n > 0) {
+      if (rowok) {
+        const int o = row / e.rs_n;
+        __nv_bfloat16* orow = p2p::at<__nv_bfloat16>(e.P, o, e.rs_off) +
+                              (int64_t(e.P.rank) * e.rs_n + (row - o * e.rs_n)) * e.ldo;
+        store_bf16x32(orow + col0, v, nv);
+      }
+    } else if (e.out && rowok) {
+      store_bf16x32(e.out + int64_t(row) * e.ldo + col0, v, nv);
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      s_sq += v[j] * v[j];
+      s_nnz += v[j] != 0.f ? 1.f : 0.f;
+    }
+    if (e.colcnt) {
+      float cnt[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) cnt[j] = v[j] != 0.f ? 1.f : 0.f;
+      const float cs = warp_colsum32(cnt, lane);
+      if (lane < nv && cs != 0.f) atomicAdd(e.colcnt + col0 + lane, cs);
+    }
+    if (e.colsum) {
+      const float cs = warp_colsum32(v, lane);  // v is not used after this
+      if (lane < nv && cs != 0.f) atomicAdd(e.colsum + col0 + lane, cs);
+    }
+  }
+  if (e.rs_n > 0) __threadfence_system();  // peer rows visible before a later launch's release flag
+  if (e.loss) {
+    const float t = warp_sum(s_loss);
+    if (lane == 0 && t != 0.f) atomicAdd(e.loss, t);
+  }
+  if (e.sumsq) {
+    const float t = warp_sum(s_sq);
+    if (lane == 0 && t != 0.f) atomicAdd(e.sumsq, t);
+  }
+  if (e.nnz) {
+    const float t = warp_sum(s_nnz);
+    if (lane == 0 && t != 0.f) atomicAdd(e.nnz, (unsigned long long)(t + 0.5f));
+  }
+}
+
 // All-gather fusion parameters (byte offsets inside the symmetric slabs).
 struct Ag {
   p2p::Peers P;
@@ -104,7 +342,8 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mt
 
 // Epilogue of one accumulator tile: this thread's TMEM lane `trow` holds output row `row`
 // (columns nt*BN .. nt*BN+255): bias, per-column scale, ReLU, bf16 store, 32-column maxima.
-__device__ __forceinline__ void epilogue_tile(const Epi& ep, uint32_t trow, int row, int M, int nt) {
+// Columns >= N (a partial last tile) are neither read from bias/scale nor stored.
+__device__ __forceinline__ void epilogue_tile(const Epi& ep, uint32_t trow, int row, int M, int N, int nt) {
   float tile_max = -INFINITY;
 #pragma unroll 1
   for (int c = 0; c < BN / 32; ++c) {
@@ -112,29 +351,43 @@ __device__ __forceinline__ void epilogue_tile(const Epi& ep, uint32_t trow, int 
     tmem_ld_32x32b_x32(trow + c * 32, r);
     tmem_ld_wait();
     const int col0 = nt * BN + c * 32;
+    if (col0 >= N) continue;  // after the (warp-collective) load
+    const bool full = col0 + 32 <= N;
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
     if (ep.bias) {
-      const float4* b4 = reinterpret_cast<const float4*>(ep.bias + col0);
+      if (full) {
+        const float4* b4 = reinterpret_cast<const float4*>(ep.bias + col0);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float4 b = __ldg(b4 + j);
-        v[4 * j] += b.x;
-        v[4 * j + 1] += b.y;
-        v[4 * j + 2] += b.z;
-        v[4 * j + 3] += b.w;
+        for (int j = 0; j < 8; ++j) {
+          const float4 b = __ldg(b4 + j);
+          v[4 * j] += b.x;
+          v[4 * j + 1] += b.y;
+          v[4 * j + 2] += b.z;
+          v[4 * j + 3] += b.w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < N) v[j] += __ldg(ep.bias + col0 + j);
       }
     }
     if (ep.scale) {
-      const float4* s4 = reinterpret_cast<const float4*>(ep.scale + col0);
+      if (full) {
+        const float4* s4 = reinterpret_cast<const float4*>(ep.scale + col0);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float4 s = __ldg(s4 + j);
-        v[4 * j] *= s.x;
-        v[4 * j + 1] *= s.y;
-        v[4 * j + 2] *= s.z;
-        v[4 * j + 3] *= s.w;
+        for (int j = 0; j < 8; ++j) {
+          const float4 s = __ldg(s4 + j);
+          v[4 * j] *= s.x;
+          v[4 * j + 1] *= s.y;
+          v[4 * j + 2] *= s.z;
+          v[4 * j + 3] *= s.w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < N) v[j] *= __ldg(ep.scale + col0 + j);
       }
     }
     if (ep.relu) {
@@ -147,15 +400,22 @@ __device__ __forceinline__ void epilogue_tile(const Epi& ep, uint32_t trow, int 
     for (int j = 0; j < 16; ++j) {
       __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
       packed[j] = *reinterpret_cast<uint32_t*>(&h2);
-      cm = fmaxf(cm, fmaxf(__low2float(h2), __high2float(h2)));
+      if (full || col0 + 2 * j < N) cm = fmaxf(cm, __low2float(h2));
+      if (full || col0 + 2 * j + 1 < N) cm = fmaxf(cm, __high2float(h2));
     }
     if (row < M) {
       if (ep.out) {
-        uint4* dst = reinterpret_cast<uint4*>(ep.out + int64_t(row) * ep.ldo + col0);
+        if (full) {
+          uint4* dst = reinterpret_cast<uint4*>(ep.out + int64_t(row) * ep.ldo + col0);
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
-                              packed[4 * j + 3]);
+          for (int j = 0; j < 4; ++j)
+            dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+        } else {
+          __nv_bfloat16* dst = ep.out + int64_t(row) * ep.ldo + col0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < N) dst[j] = __float2bfloat16_rn(v[j]);
+        }
       }
       if (ep.cmax) ep.cmax[int64_t(row) * ep.ldc + (col0 >> 5)] = __float2bfloat16_rn(cm);
     }
@@ -211,10 +471,14 @@ __device__ __forceinline__ void ag_push(const Ag& ag, int K, int ct) {
   }
 }
 
-template <bool AG>
+// A_MN / B_MN: the operand is stored MN-major ([K, M] / [K, N], M / N contiguous) and is loaded as
+// 64 x 64 TMA boxes (64 MN elements by 64 k-rows, 8 KB each, LBO = 8 KB between MN chunks).
+// DENSE: the epilogue is `epilogue_tile_dense` (EpiD) instead of the encoder epilogue (Epi).
+template <bool AG, bool A_MN = false, bool B_MN = false, bool DENSE = false>
 __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   int M, int N, int K, Epi ep, int* status, const __grid_constant__ Ag ag) {
+                   int M, int N, int K, Epi ep, int* status, const __grid_constant__ Ag ag,
+                   const __grid_constant__ EpiD ed) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -231,9 +495,9 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_m = (M + BM - 1) / BM;
-  const int num_n = N / BN;
+  const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
-  const int num_kb = K / BK;
+  const int num_kb = (K + BK - 1) / BK;  // a ragged last k-block reads zeros past K
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -291,8 +555,20 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
             break;
           }
           mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
-          tma_load_2d(sA + s * A_TILE_BYTES, &tmA, &full_bar[s], kb * BK, mt * BM);
-          tma_load_2d(sB + s * B_TILE_BYTES, &tmB, &full_bar[s], kb * BK, nt * BN);
+          if (A_MN) {
+#pragma unroll
+            for (int c = 0; c < BM / 64; ++c)
+              tma_load_2d(sA + s * A_TILE_BYTES + c * 8192, &tmA, &full_bar[s], mt * BM + c * 64, kb * BK);
+          } else {
+            tma_load_2d(sA + s * A_TILE_BYTES, &tmA, &full_bar[s], kb * BK, mt * BM);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c)
+              tma_load_2d(sB + s * B_TILE_BYTES + c * 8192, &tmB, &full_bar[s], nt * BN + c * 64, kb * BK);
+          } else {
+            tma_load_2d(sB + s * B_TILE_BYTES, &tmB, &full_bar[s], kb * BK, nt * BN);
+          }
         }
       }
       if (!ok) {
@@ -307,7 +583,7 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------ MMA issuer --------------------------------
     if (elect_one()) {
-      const uint32_t idesc = make_idesc_bf16_f32(BM, BN);
+      const uint32_t idesc = make_idesc_bf16_f32(BM, BN) | (A_MN ? (1u << 15) : 0u) | (B_MN ? (1u << 16) : 0u);
       uint32_t it = 0, tc = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++tc) {
@@ -332,9 +608,11 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
           const uint32_t b_addr = smem_u32(sB + s * B_TILE_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            umma_bf16_ss(d_tmem, make_sdesc_sw128_kmajor(a_addr + k * 32),
-                         make_sdesc_sw128_kmajor(b_addr + k * 32), idesc,
-                         (kb > 0 || k > 0) ? 1u : 0u);
+            const uint64_t ad = A_MN ? make_sdesc_sw128_mnmajor(a_addr + k * 2048, 8192)
+                                     : make_sdesc_sw128_kmajor(a_addr + k * 32);
+            const uint64_t bd = B_MN ? make_sdesc_sw128_mnmajor(b_addr + k * 2048, 8192)
+                                     : make_sdesc_sw128_kmajor(b_addr + k * 32);
+            umma_bf16_ss(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty_bar[s]);
         }
@@ -359,7 +637,10 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
       tc_fence_after();
       const int row = mt * BM + q * 32 + lane;
       const uint32_t trow = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
-      epilogue_tile(ep, trow, row, M, nt);
+      if (DENSE)
+        epilogue_tile_dense(ed, trow, row, M, N, nt, lane);
+      else
+        epilogue_tile(ep, trow, row, M, N, nt);
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
     }
@@ -412,9 +693,9 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
   const bool leader = cta == 0;
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int num_m = (M + 2 * BM - 1) / (2 * BM);
-  const int num_n = N / BN;
+  const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
-  const int num_kb = K / BK;
+  const int num_kb = (K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < PSTAGES; ++s) {
@@ -542,7 +823,7 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
       tc_fence_after();
       const int row = mt * 2 * BM + int(cta) * BM + q * 32 + lane;
       const uint32_t trow = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
-      epilogue_tile(ep, trow, row, M, nt);
+      epilogue_tile(ep, trow, row, M, N, nt);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
@@ -613,12 +894,11 @@ static gemm::Epi make_epi(int64_t M, int64_t N, const c10::optional<torch::Tenso
   return ep;
 }
 
-// CTA-pair kernel unless disabled (SAELENS_B200_GEMM_PAIR=0) or M is too small to fill pairs.
+// CTA-pair kernel unless disabled (SAELENS_B200_GEMM_PAIR=0, read at every call) or M is too small
+// to fill pairs.
 static bool use_pair(int64_t M) {
-  static const bool off = [] {
-    const char* e = std::getenv("SAELENS_B200_GEMM_PAIR");
-    return e && std::string(e) == "0";
-  }();
+  const char* e = std::getenv("SAELENS_B200_GEMM_PAIR");
+  const bool off = e && e[0] == '0' && e[1] == 0;
   return !off && M >= 2 * gemm::BM;
 }
 
@@ -642,11 +922,11 @@ static void launch_gemm(const void* a_ptr, int64_t lda, int64_t M, const torch::
                                           gemm::SMEM_BYTES));
       attr_set = true;
     }
-    const int64_t tiles = ((M + gemm::BM - 1) / gemm::BM) * (N / gemm::BN);
+    const int64_t tiles = ((M + gemm::BM - 1) / gemm::BM) * ((N + gemm::BN - 1) / gemm::BN);
     int64_t grid = std::min<int64_t>(tiles, num_sms_cached());
     if (max_ctas > 0) grid = std::min<int64_t>(grid, max_ctas);
     gemm::gemm_tn_kernel<AG><<<dim3(grid), dim3(threads), gemm::SMEM_BYTES, stream>>>(tA, tB, iM, iN, iK, ep, st,
-                                                                                         ag);
+                                                                                         ag, gemm::EpiD{});
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     return;
   }
@@ -670,7 +950,7 @@ static void launch_gemm(const void* a_ptr, int64_t lda, int64_t M, const torch::
     C10_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
     max_pairs = std::max(1, n);
   }
-  const int64_t tiles = ((M + 2 * gemm::BM - 1) / (2 * gemm::BM)) * (N / gemm::BN);
+  const int64_t tiles = ((M + 2 * gemm::BM - 1) / (2 * gemm::BM)) * ((N + gemm::BN - 1) / gemm::BN);
   int64_t pairs = std::min<int64_t>(tiles, max_pairs);
   if (max_ctas > 0) pairs = std::max<int64_t>(1, std::min<int64_t>(pairs, max_ctas / 2));
   cfg.gridDim = dim3(unsigned(2 * pairs));
@@ -689,8 +969,9 @@ void gemm_tn_bf16(const torch::Tensor& A, const torch::Tensor& B, const c10::opt
   TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm_tn_bf16: shape");
   TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1, "gemm_tn_bf16: K must be contiguous");
   const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
-  TORCH_CHECK(K % gemm::BK == 0, "gemm_tn_bf16: K must be a multiple of 64, got ", K);
-  TORCH_CHECK(N % gemm::BN == 0, "gemm_tn_bf16: N must be a multiple of 256, got ", N);
+  TORCH_CHECK(K % 8 == 0, "gemm_tn_bf16: K must be a multiple of 8 (16-byte rows), got ", K);
+  TORCH_CHECK(N >= 1 && ((!cmax && !tmax) || N % gemm::BN == 0),
+              "gemm_tn_bf16: chunk / tile maxima need N to be a multiple of 256, got ", N);
   TORCH_CHECK(M >= 1 && M < (1ll << 31) && N < (1ll << 31), "gemm_tn_bf16: size");
   const at::cuda::CUDAGuard guard(A.device());
   const gemm::Epi ep = make_epi(M, N, bias, scale, relu, out, cmax, tmax);
@@ -797,6 +1078,201 @@ void gemm_fsdp_tn_bf16(const torch::Tensor& A, const torch::Tensor& w_own, const
   auto W = torch::from_blob(reinterpret_cast<char*>(peer_bases[rank]) + w_off, {N, K},
                             A.options().dtype(at::kBFloat16));
   launch_gemm<true>(A.data_ptr(), A.stride(0), M, W, ep, status, max_ctas, ag, use_pair(M));
+}
+
+}  // namespace sb
+
+namespace sb {
+
+template <bool A_MN, bool B_MN>
+static void launch_dense(const CUtensorMap& tA, const CUtensorMap& tB, int M, int N, int K, const gemm::EpiD& ed,
+                         int* st, int64_t max_ctas) {
+  auto kern = gemm::gemm_tn_kernel<false, A_MN, B_MN, true>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::SMEM_BYTES));
+    attr_set = true;
+  }
+  const int64_t tiles = int64_t((M + gemm::BM - 1) / gemm::BM) * ((N + gemm::BN - 1) / gemm::BN);
+  int64_t grid = std::min<int64_t>(tiles, num_sms_cached());
+  if (max_ctas > 0) grid = std::min<int64_t>(grid, max_ctas);
+  kern<<<dim3(unsigned(grid)), dim3(gemm::NUM_THREADS), gemm::SMEM_BYTES, at::cuda::getCurrentCUDAStream()>>>(
+      tA, tB, M, N, K, gemm::Epi{}, st, gemm::Ag{}, ed);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+static const float* opt_f32(const c10::optional<torch::Tensor>& t, int64_t n, const char* what) {
+  if (!t) return nullptr;
+  TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == n,
+              "gemm_dense_bf16: ", what, " must be a contiguous CUDA fp32 tensor of ", n, " elements");
+  return t->data_ptr<float>();
+}
+
+static __nv_bfloat16* opt_bf16_mat(const c10::optional<torch::Tensor>& t, int64_t M, int64_t N, int64_t* ld,
+                                   const char* what) {
+  if (!t) return nullptr;
+  TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 2 && t->size(0) == M &&
+                  t->size(1) == N && t->stride(1) == 1 && t->stride(0) % 8 == 0 &&
+                  reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
+              "gemm_dense_bf16: ", what, " must be bf16 [M, N] with 16-byte aligned rows");
+  *ld = t->stride(0);
+  return reinterpret_cast<__nv_bfloat16*>(t->data_ptr());
+}
+
+// Dense GEMM of the dense SAE steps: C[M, N] = epilogue(sum_k A[m, k] B[n, k]) on tcgen05, with each
+// operand either K-major (A [M, K], B [N, K]) or MN-major (A [K, M], B [K, N]; `a_mn` / `b_mn`),
+// bf16 with contiguous inner dimension and 16-byte row strides.  The epilogue (EpiD) is assembled
+// from the optional tensors; `nnz` is an int64 scalar, the other accumulators fp32.
+void gemm_dense_bf16(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, bool b_mn,
+                     const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& out2,
+                     const c10::optional<torch::Tensor>& bias, const c10::optional<torch::Tensor>& r1_row,
+                     const c10::optional<torch::Tensor>& r1_col, const c10::optional<torch::Tensor>& thr, bool relu,
+                     const c10::optional<torch::Tensor>& hin, double bandwidth, double l0c,
+                     const c10::optional<torch::Tensor>& gthr, const c10::optional<torch::Tensor>& target,
+                     double res_coef, const c10::optional<torch::Tensor>& loss,
+                     const c10::optional<torch::Tensor>& colsum, const c10::optional<torch::Tensor>& colcnt,
+                     const c10::optional<torch::Tensor>& nnz, const c10::optional<torch::Tensor>& sumsq,
+                     const c10::optional<torch::Tensor>& gate_bias, const c10::optional<torch::Tensor>& mag_scale,
+                     const torch::Tensor& status, int64_t max_ctas, const std::vector<int64_t>& rs_bases,
+                     int64_t rs_rank, int64_t rs_off, int64_t rs_n) {
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 &&
+                  A.dim() == 2 && B.dim() == 2 && A.stride(1) == 1 && B.stride(1) == 1,
+              "gemm_dense_bf16: A and B must be 2-D CUDA bf16 with a contiguous inner dimension");
+  const int64_t M = a_mn ? A.size(1) : A.size(0), K = a_mn ? A.size(0) : A.size(1);
+  const int64_t N = b_mn ? B.size(1) : B.size(0), Kb = b_mn ? B.size(0) : B.size(1);
+  TORCH_CHECK(K == Kb && K >= 1 && M >= 1 && N >= 1, "gemm_dense_bf16: inner dimensions differ (", K, " vs ", Kb, ")");
+  TORCH_CHECK(A.stride(0) % 8 == 0 && B.stride(0) % 8 == 0, "gemm_dense_bf16: row strides must be multiples of 8");
+  TORCH_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm_dense_bf16: size");
+  gemm::EpiD ed{};
+  if (rs_n > 0) {
+    const int64_t S = int64_t(rs_bases.size());
+    TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rs_rank >= 0 && rs_rank < S && rs_n % gemm::BM == 0 &&
+                    S * rs_n == M && rs_off % 16 == 0 && N % 8 == 0 && !out,
+                "gemm_dense_bf16: reduce-scatter mode needs M = world * rs_n, rs_n % 128 == 0, N % 8 == 0, an "
+                "aligned landing offset and no local out");
+    ed.P = p2p::make_peers(rs_bases, rs_rank);
+    ed.rs_off = rs_off;
+    ed.rs_n = int(rs_n);
+    ed.ldo = N;
+  }
+  ed.out = opt_bf16_mat(out, M, N, &ed.ldo, "out");
+  ed.out2 = opt_bf16_mat(out2, M, N, &ed.ldo2, "out2");
+  ed.bias = opt_f32(bias, N, "bias");
+  ed.r1_row = opt_f32(r1_row, M, "r1_row");
+  ed.r1_col = opt_f32(r1_col, N, "r1_col");
+  TORCH_CHECK(!ed.r1_row == !ed.r1_col, "gemm_dense_bf16: r1_row and r1_col go together");
+  ed.thr = opt_f32(thr, N, "thr");
+  ed.relu = relu ? 1 : 0;
+  ed.hin = opt_bf16_mat(hin, M, N, &ed.ldh, "hin");
+  TORCH_CHECK(!ed.hin || (ed.thr && bandwidth > 0), "gemm_dense_bf16: hin needs thr and a positive bandwidth");
+  ed.inv_bw = bandwidth > 0 ? float(1.0 / bandwidth) : 0.f;
+  ed.l0c = float(l0c);
+  ed.gthr = const_cast<float*>(opt_f32(gthr, N, "gthr"));
+  ed.target = opt_bf16_mat(target, M, N, &ed.ldtg, "target");
+  ed.res_coef = float(res_coef);
+  ed.loss = const_cast<float*>(opt_f32(loss, 1, "loss"));
+  ed.colsum = const_cast<float*>(opt_f32(colsum, N, "colsum"));
+  ed.colcnt = const_cast<float*>(opt_f32(colcnt, N, "colcnt"));
+  if (nnz) {
+    TORCH_CHECK(nnz->is_cuda() && nnz->scalar_type() == at::kLong && nnz->numel() == 1, "gemm_dense_bf16: nnz int64[1]");
+    ed.nnz = reinterpret_cast<unsigned long long*>(nnz->data_ptr<int64_t>());
+  }
+  ed.sumsq = const_cast<float*>(opt_f32(sumsq, 1, "sumsq"));
+  ed.gate_bias = opt_f32(gate_bias, N, "gate_bias");
+  ed.mag_scale = opt_f32(mag_scale, N, "mag_scale");
+  TORCH_CHECK(!ed.gate_bias == !ed.mag_scale, "gemm_dense_bf16: gate_bias and mag_scale go together");
+  const auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  CUtensorMap tA = a_mn ? make_tmap_2d(A.data_ptr(), bf, 2, K, M, A.stride(0) * 2, 64, 64, sw)
+                        : make_tmap_2d(A.data_ptr(), bf, 2, M, K, A.stride(0) * 2, gemm::BM, gemm::BK, sw);
+  CUtensorMap tB = b_mn ? make_tmap_2d(B.data_ptr(), bf, 2, K, N, B.stride(0) * 2, 64, 64, sw)
+                        : make_tmap_2d(B.data_ptr(), bf, 2, N, K, B.stride(0) * 2, gemm::BN, gemm::BK, sw);
+  TORCH_CHECK(status.is_cuda() && status.scalar_type() == at::kInt, "gemm_dense_bf16: status");
+  const at::cuda::CUDAGuard guard(A.device());
+  int* st = status.data_ptr<int>();
+  const int iM = int(M), iN = int(N), iK = int(K);
+  if (a_mn && b_mn)
+    launch_dense<true, true>(tA, tB, iM, iN, iK, ed, st, max_ctas);
+  else if (a_mn)
+    launch_dense<true, false>(tA, tB, iM, iN, iK, ed, st, max_ctas);
+  else if (b_mn)
+    launch_dense<false, true>(tA, tB, iM, iN, iK, ed, st, max_ctas);
+  else
+    launch_dense<false, false>(tA, tB, iM, iN, iK, ed, st, max_ctas);
+}
+
+// Sharded data-parallel encoder GEMM with the dense (JumpReLU / gated) epilogue: the parameter
+// all-gather of `gemm_fsdp_tn_bf16` (own W_enc / W_dec latent tiles pushed to every rank, the
+// TMA producer waiting per 256-latent tile) with the EpiD epilogue of the dense steps.
+void gemm_fsdp_dense_bf16(const torch::Tensor& A, const torch::Tensor& w_own, const std::vector<int64_t>& peer_bases,
+                          int64_t rank, int64_t w_off, int64_t flag_off, bool push, int64_t epoch,
+                          const c10::optional<torch::Tensor>& w2_own, int64_t w2_off, int64_t flag2_off,
+                          const torch::Tensor& out, const c10::optional<torch::Tensor>& out2,
+                          const c10::optional<torch::Tensor>& bias, const c10::optional<torch::Tensor>& thr,
+                          const c10::optional<torch::Tensor>& colcnt, const c10::optional<torch::Tensor>& nnz,
+                          const torch::Tensor& status, const torch::Tensor& ticket) {
+  const int64_t S = int64_t(peer_bases.size());
+  TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "gemm_fsdp_dense: bad group");
+  TORCH_CHECK(A.is_cuda() && A.scalar_type() == at::kBFloat16 && A.dim() == 2 && A.stride(1) == 1 &&
+                  A.stride(0) % 8 == 0,
+              "gemm_fsdp_dense: A must be CUDA bf16 [M, K] with 16-byte rows");
+  TORCH_CHECK(w_own.is_cuda() && w_own.scalar_type() == at::kBFloat16 && w_own.is_contiguous() &&
+                  w_own.size(1) == A.size(1),
+              "gemm_fsdp_dense: w_own must be contiguous bf16 [n, K]");
+  const int64_t M = A.size(0), K = A.size(1), n = w_own.size(0), N = n * S;
+  TORCH_CHECK(n % gemm::BN == 0 && K % gemm::BK == 0, "gemm_fsdp_dense: shard rows % 256 and K % 64");
+  TORCH_CHECK(N / gemm::BN <= gemm::MAX_MTILES && M >= 1 && M < (1ll << 31), "gemm_fsdp_dense: size");
+  TORCH_CHECK(w_off % 16 == 0 && flag_off % 4 == 0 && w2_off % 16 == 0 && flag2_off % 4 == 0,
+              "gemm_fsdp_dense: slab offsets must be aligned");
+  if (w2_own)
+    TORCH_CHECK(w2_own->is_cuda() && w2_own->scalar_type() == at::kBFloat16 && w2_own->is_contiguous() &&
+                    w2_own->sizes() == w_own.sizes(),
+                "gemm_fsdp_dense: w2_own must be contiguous bf16 like w_own");
+  gemm::EpiD ed{};
+  ed.out = opt_bf16_mat(out, M, N, &ed.ldo, "out");
+  ed.out2 = opt_bf16_mat(out2, M, N, &ed.ldo2, "out2");
+  ed.bias = opt_f32(bias, N, "bias");
+  ed.thr = opt_f32(thr, N, "thr");
+  ed.colcnt = const_cast<float*>(opt_f32(colcnt, N, "colcnt"));
+  if (nnz) {
+    TORCH_CHECK(nnz->is_cuda() && nnz->scalar_type() == at::kLong && nnz->numel() == 1, "gemm_fsdp_dense: nnz");
+    ed.nnz = reinterpret_cast<unsigned long long*>(nnz->data_ptr<int64_t>());
+  }
+  TORCH_CHECK(ticket.is_cuda() && ticket.scalar_type() == at::kInt && ticket.numel() >= 1, "gemm_fsdp_dense: ticket");
+  TORCH_CHECK(status.is_cuda() && status.scalar_type() == at::kInt, "gemm_fsdp_dense: status");
+  const at::cuda::CUDAGuard guard(A.device());
+  gemm::Ag ag{};
+  ag.P = p2p::make_peers(peer_bases, rank);
+  ag.src = reinterpret_cast<const __nv_bfloat16*>(w_own.data_ptr());
+  ag.x_off = w_off;
+  ag.flag_off = flag_off;
+  ag.rows_per_rank = int(n);
+  ag.operand = 1;
+  ag.rot = int((rank * n) / gemm::BN);
+  ag.push = push ? 1 : 0;
+  ag.epoch = uint32_t(epoch);
+  ag.src2 = w2_own ? reinterpret_cast<const __nv_bfloat16*>(w2_own->data_ptr()) : nullptr;
+  ag.x2_off = w2_off;
+  ag.flag2_off = flag2_off;
+  ag.ticket = ticket.data_ptr<int>();
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (push) C10_CUDA_CHECK(cudaMemsetAsync(ag.ticket, 0, sizeof(int), stream));
+  const char* wbase = reinterpret_cast<const char*>(peer_bases[rank]) + w_off;
+  const auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  CUtensorMap tA = make_tmap_2d(A.data_ptr(), bf, 2, M, K, A.stride(0) * 2, gemm::BM, gemm::BK, sw);
+  CUtensorMap tB = make_tmap_2d(wbase, bf, 2, N, K, K * 2, gemm::BN, gemm::BK, sw);
+  auto kern = gemm::gemm_tn_kernel<true, false, false, true>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::SMEM_BYTES));
+    attr_set = true;
+  }
+  const int64_t tiles = ((M + gemm::BM - 1) / gemm::BM) * (N / gemm::BN);
+  const int64_t grid = std::min<int64_t>(tiles, num_sms_cached());
+  kern<<<dim3(unsigned(grid)), dim3(gemm::NUM_THREADS_AG), gemm::SMEM_BYTES, stream>>>(
+      tA, tB, int(M), int(N), int(K), gemm::Epi{}, status.data_ptr<int>(), ag, ed);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 }  // namespace sb

@@ -5,6 +5,7 @@
 //   [0, MAX)               per-latent counts
 //   [MAX, 2*MAX)           per-latent fill cursors
 //   [2*MAX, 2*MAX + MAX/1024)  per-block partial sums of the scan
+//   [2*MAX + MAX/1024]     number of pairs skipped for a latent index >= n_latents
 #include <mutex>
 
 #include "noalloc_csc.h"
@@ -17,18 +18,26 @@ constexpr int kScanBlocksMax = kMax / kScanBlock;
 constexpr int kMaxDevices = 64;
 
 // 8 MiB + 4 KiB per device that loads the library, held until exit.
-static __device__ __align__(256) int32_t g_csc_scratch[2 * kMax + kScanBlocksMax];
+static __device__ __align__(256) int32_t g_csc_scratch[2 * kMax + kScanBlocksMax + 1];
 
 __global__ void zero_kernel(int32_t* p, int n) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = 0;
 }
 
+// Counts kept pairs per latent; an index >= n_latents is skipped and counted in *bad.
 __global__ void count_kernel(const float* __restrict__ vals, const int32_t* __restrict__ idx, int64_t n_pairs,
-                             int32_t* __restrict__ counts) {
+                             int32_t n_latents, int32_t* __restrict__ counts, int32_t* __restrict__ bad) {
+  int32_t nbad = 0;
   for (int64_t p = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; p < n_pairs; p += int64_t(gridDim.x) * blockDim.x) {
     const int32_t j = idx[p];
-    if (j >= 0 && vals[p] > 0.f) atomicAdd(counts + j, 1);
+    if (j < 0 || !(vals[p] > 0.f)) continue;
+    if (j >= n_latents) {
+      ++nbad;
+      continue;
+    }
+    atomicAdd(counts + j, 1);
   }
+  if (nbad) atomicAdd(bad, nbad);
 }
 
 // inclusive warp scan helper
@@ -61,6 +70,8 @@ __device__ __forceinline__ int32_t block_excl(int32_t v, int32_t* total) {
   return out;
 }
 
+__global__ void copy_count_kernel(const int32_t* __restrict__ src, int32_t* __restrict__ dst) { *dst = *src; }
+
 __global__ void __launch_bounds__(kScanBlock) block_sum_kernel(const int32_t* __restrict__ counts, int n,
                                                                int32_t* __restrict__ block_sums) {
   __shared__ int32_t tot;
@@ -89,11 +100,11 @@ __global__ void __launch_bounds__(kScanBlock) colptr_kernel(const int32_t* __res
 }
 
 __global__ void fill_kernel(const float* __restrict__ vals, const int32_t* __restrict__ idx, int64_t n_pairs,
-                            const int64_t* __restrict__ colptr, int32_t* __restrict__ cursor,
+                            int32_t n_latents, const int64_t* __restrict__ colptr, int32_t* __restrict__ cursor,
                             int64_t* __restrict__ pairs) {
   for (int64_t p = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; p < n_pairs; p += int64_t(gridDim.x) * blockDim.x) {
     const int32_t j = idx[p];
-    if (j >= 0 && vals[p] > 0.f) {
+    if (j >= 0 && j < n_latents && vals[p] > 0.f) {
       const int32_t pos = atomicAdd(cursor + j, 1);
       pairs[colptr[j] + pos] = p;
     }
@@ -121,33 +132,53 @@ int scratch_for_current_device(int32_t** out) {
 }  // namespace
 
 extern "C" int sb_csc_build_noalloc(const float* vals, const int32_t* idx, int64_t n_pairs, int32_t n_latents,
-                                    int64_t* colptr, int64_t* pairs, cudaStream_t stream) {
+                                    int64_t* colptr, int64_t* pairs, int32_t* bad_pairs, cudaStream_t stream) {
   if (n_latents < 1 || n_latents > kMax) return SB_NOALLOC_ERR_TOO_MANY_LATENTS;
+  if (n_pairs > SB_NOALLOC_CSC_MAX_PAIRS) return SB_NOALLOC_ERR_TOO_MANY_PAIRS;
   if (n_pairs < 0 || colptr == nullptr || (n_pairs > 0 && (vals == nullptr || idx == nullptr || pairs == nullptr)))
     return SB_NOALLOC_ERR_BAD_ARGUMENT;
+  if (cudaGetLastError() != cudaSuccess) return SB_NOALLOC_ERR_PENDING;
   int32_t* scratch = nullptr;
   const int rc = scratch_for_current_device(&scratch);
   if (rc != SB_NOALLOC_OK) return rc;
   int32_t* counts = scratch;
   int32_t* cursor = scratch + kMax;
   int32_t* block_sums = scratch + 2 * kMax;
+  int32_t* bad = scratch + 2 * kMax + kScanBlocksMax;
   const int n = n_latents;
   const int nb = (n + kScanBlock - 1) / kScanBlock;
-  const int zb = (2 * n + 255) / 256;
-  zero_kernel<<<zb < 1024 ? zb : 1024, 256, 0, stream>>>(counts, n);
-  zero_kernel<<<zb < 1024 ? zb : 1024, 256, 0, stream>>>(cursor, n);
+  const int zb = (n + 255) / 256;
+  const int zgrid = zb < 1024 ? zb : 1024;
+  const int64_t g = (n_pairs + 255) / 256;
+  const int pgrid = int(g < 4096 ? g : 4096);
+#define SB_NOALLOC_CHECK_LAUNCH() \
+  if (cudaGetLastError() != cudaSuccess) return SB_NOALLOC_ERR_LAUNCH
+  zero_kernel<<<zgrid, 256, 0, stream>>>(counts, n);
+  SB_NOALLOC_CHECK_LAUNCH();
+  zero_kernel<<<zgrid, 256, 0, stream>>>(cursor, n);
+  SB_NOALLOC_CHECK_LAUNCH();
+  zero_kernel<<<1, 32, 0, stream>>>(bad, 1);
+  SB_NOALLOC_CHECK_LAUNCH();
   if (n_pairs > 0) {
-    const int64_t g = (n_pairs + 255) / 256;
-    count_kernel<<<int(g < 4096 ? g : 4096), 256, 0, stream>>>(vals, idx, n_pairs, counts);
+    count_kernel<<<pgrid, 256, 0, stream>>>(vals, idx, n_pairs, n, counts, bad);
+    SB_NOALLOC_CHECK_LAUNCH();
   }
   block_sum_kernel<<<nb, kScanBlock, 0, stream>>>(counts, n, block_sums);
+  SB_NOALLOC_CHECK_LAUNCH();
   scan_block_sums_kernel<<<1, kScanBlock, 0, stream>>>(block_sums, nb);
+  SB_NOALLOC_CHECK_LAUNCH();
   colptr_kernel<<<nb, kScanBlock, 0, stream>>>(counts, n, block_sums, colptr);
+  SB_NOALLOC_CHECK_LAUNCH();
   if (n_pairs > 0) {
-    const int64_t g = (n_pairs + 255) / 256;
-    fill_kernel<<<int(g < 4096 ? g : 4096), 256, 0, stream>>>(vals, idx, n_pairs, colptr, cursor, pairs);
+    fill_kernel<<<pgrid, 256, 0, stream>>>(vals, idx, n_pairs, n, colptr, cursor, pairs);
+    SB_NOALLOC_CHECK_LAUNCH();
   }
-  return cudaPeekAtLastError() == cudaSuccess ? SB_NOALLOC_OK : SB_NOALLOC_ERR_LAUNCH;
+  if (bad_pairs != nullptr) {
+    copy_count_kernel<<<1, 1, 0, stream>>>(bad, bad_pairs);
+    SB_NOALLOC_CHECK_LAUNCH();
+  }
+#undef SB_NOALLOC_CHECK_LAUNCH
+  return SB_NOALLOC_OK;
 }
 
 extern "C" const char* sb_noalloc_strerror(int code) {
@@ -162,6 +193,10 @@ extern "C" const char* sb_noalloc_strerror(int code) {
       return "could not look up the device address of the scratch array (cudaGetSymbolAddress)";
     case SB_NOALLOC_ERR_LAUNCH:
       return "kernel launch failed";
+    case SB_NOALLOC_ERR_TOO_MANY_PAIRS:
+      return "n_pairs must be at most SB_NOALLOC_CSC_MAX_PAIRS (2147483647)";
+    case SB_NOALLOC_ERR_PENDING:
+      return "a CUDA error was already pending when the call started (taken with cudaGetLastError); nothing was launched";
     default:
       return "unknown error";
   }

@@ -43,4 +43,24 @@ inline CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dtype, int
   return m;
 }
 
+// 3-D tensor [d2][d1][d0] (d0 contiguous) with byte strides s1 (between d1 rows) and s2 (between
+// d2 planes); the box is [b2][b1][b0] elements.  Out-of-range rows of a box read as zero.
+inline CUtensorMap make_tmap_3d(const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t d0,
+                                uint64_t d1, uint64_t d2, uint64_t s1_bytes, uint64_t s2_bytes, uint32_t b0,
+                                uint32_t b1, uint32_t b2, CUtensorMapSwizzle swizzle) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK(s1_bytes % 16 == 0 && s2_bytes % 16 == 0, "TMA strides must be multiples of 16 bytes");
+  TORCH_CHECK((uint64_t(b0) * elem_bytes) % 16 == 0, "TMA box inner extent");
+  CUtensorMap m;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1_bytes, s2_bytes};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = get_encode_tiled()(&m, dtype, 3, const_cast<void*>(base), dims, strides, box, estr,
+                                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (3-D) failed with code ", int(r));
+  return m;
+}
+
 }  // namespace sb

@@ -62,6 +62,13 @@ def _shard_module(sae: Any, rank: int, world: int) -> int:
 
 
 class FSDPTopKEngine(FusedTopKEngine):
+    # per-latent vectors replicated after each step: folded bias, ||W_dec||, 1 / ||W_dec|| (a subclass
+    # may add more, filled by `_vector_parts`); extra fp32 slots at the end of the averaged small vector
+    N_VECS = 3
+
+    def _extra_small(self) -> int:
+        return 0
+
     def __init__(self, sae: Any, lr: float, group: dist.ProcessGroup | None, beta1: float = 0.9,
                  beta2: float = 0.999, eps: float = 1e-8, max_grad_norm: float = 1.0,
                  h_buffer_bytes: int = 8 << 30):
@@ -77,10 +84,11 @@ class FSDPTopKEngine(FusedTopKEngine):
         n, D, NF = self.N, self.D, self.N_full
         self.k = min(self.k_request(), NF)
         bf, f32 = torch.bfloat16, torch.float32
-        self._small_n = NF + 2 * D + 3  # [gb_enc | bsum | bterm | mse | aux | norm part]
+        # [gb_enc | bsum | bterm | mse | aux | norm part | subclass extras]
+        self._small_n = NF + 2 * D + 3 + self._extra_small()
         sizes = [NF * D * 2, NF * D * 2, (NF // 256) * 4, (NF // 256) * 4, S * n * D * 2, S * n * D * 2, S * 4]
         sizes += _AllReduceBufs.nbytes(nat, self._small_n, 4, S) + _AllReduceBufs.nbytes(nat, NF, 4, S)
-        sizes += _AllReduceBufs.nbytes(nat, 3 * NF, 4, S)
+        sizes += _AllReduceBufs.nbytes(nat, self.N_VECS * NF, 4, S)
         self.heap = SymmetricHeap(group, slab_bytes_needed(sizes) + 65536, dev)
         h = self.heap
         self.wenc_buf = h.alloc((NF, D), bf)
@@ -92,7 +100,7 @@ class FSDPTopKEngine(FusedTopKEngine):
         self.gflags = h.alloc(S, torch.int32)
         self.small = _AllReduceBufs(h, nat, self._small_n, f32)
         self.fire = _AllReduceBufs(h, nat, NF, f32)
-        self.vecs = _AllReduceBufs(h, nat, 3 * NF, f32)
+        self.vecs = _AllReduceBufs(h, nat, self.N_VECS * NF, f32)
         self.wenc_full = h.local(self.wenc_buf)
         self.wdec_full = h.local(self.wdec_buf)
         self.wdec_flags_local = h.local(self.wdec_flags)
@@ -134,15 +142,18 @@ class FSDPTopKEngine(FusedTopKEngine):
         self.collectives += 1
         return area.out
 
+    def _vector_parts(self) -> list[torch.Tensor]:
+        return [self.bias_eff, self.scale, self.inv_scale]
+
     def _gather_vectors(self) -> None:
         """Full replicas of the per-latent epilogue vectors (disjoint shards summed exactly)."""
         NF, n, r = self.N_full, self.N, self.rank
-        v = torch.zeros(3 * NF, dtype=torch.float32, device=self.device)
-        v[r * n : (r + 1) * n] = self.bias_eff
-        v[NF + r * n : NF + (r + 1) * n] = self.scale
-        v[2 * NF + r * n : 2 * NF + (r + 1) * n] = self.inv_scale
+        v = torch.zeros(self.N_VECS * NF, dtype=torch.float32, device=self.device)
+        for i, part in enumerate(self._vector_parts()):
+            v[i * NF + r * n : i * NF + (r + 1) * n] = part
         out = self._ar(v, self.vecs, "vecs", 1.0)
-        self.bias_full, self.scale_full, self.inv_scale_full = out[:NF], out[NF : 2 * NF], out[2 * NF :]
+        self.vec_full = [out[i * NF : (i + 1) * NF] for i in range(self.N_VECS)]
+        self.bias_full, self.scale_full, self.inv_scale_full = self.vec_full[:3]
 
     def refresh(self) -> None:
         super().refresh()

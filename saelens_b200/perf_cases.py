@@ -14,6 +14,8 @@
     python -m saelens_b200.perf_cases router [--rows 8192 --d 4096]
         Shard-routing transfer: rank 0 produces fp32 rows, the other ranks consume bf16 unit-norm
         rows; the fused P2P router vs NCCL send/recv with separate normalise + cast (max over ranks).
+    python -m saelens_b200.perf_cases lm [--model llama-3-8b --stop 17 --batch 8 --ctx 1024]
+        Producer LM forward up to the hooked layer on this package's kernels vs PyTorch ops.
     python -m saelens_b200.perf_cases ddp [--d-sae 131072 --k 64 --batch 8192 --steps 10]
         Data-parallel TopK step (replicated SAE, P2P gradient all-reduce) under
         torch.distributed.run: ms/step (max over ranks) and per-phase times.
@@ -189,6 +191,68 @@ def gemm(args: argparse.Namespace) -> None:
             line += f" ms={ms:.3f} TFLOPs={2 * M * N * K / ms / 1e9:.1f}"
         print(line, flush=True)
         st.check("gemm")
+
+
+def gemm_step(args: argparse.Namespace) -> None:
+    """Encoder GEMM of the headline step (one 4096-row chunk: 4096 x d_sae x 4096) under the power
+    cap: the CTA-pair and single-CTA tcgen05 kernels with the full epilogue (bias, ||W_dec|| scale,
+    bf16 store, 32-column and tile maxima) and without stores, against cuBLAS (torch.matmul, bf16
+    output).  CUDA-event ms over `reps` back-to-back launches, TFLOP/s and the median SM clock."""
+    import subprocess
+    import tempfile
+
+    import torch
+
+    from saelens_b200.ops import native
+    from saelens_b200.ops.status import StatusWord
+
+    nat = native()
+    st = StatusWord("cuda")
+    M, N, K = args.m, args.n, args.k
+    torch.manual_seed(0)
+    A = (torch.randn(M, K, device="cuda") * 0.5).to(torch.bfloat16)
+    B = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+    bias = torch.randn(N, device="cuda")
+    scale = torch.rand(N, device="cuda") + 0.5
+    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    cm = torch.empty(M, N // 32, dtype=torch.bfloat16, device="cuda")
+    tm = torch.empty(M, N // 256, dtype=torch.bfloat16, device="cuda")
+
+    def ours(full: bool):
+        return lambda: nat.gemm_tn_bf16(A, B, bias if full else None, scale if full else None, False,
+                                        out if full else None, cm if full else None, st.tensor, 0,
+                                        tmax=tm if full else None)
+
+    def cublas():
+        torch.matmul(A, B.T, out=out)
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        log = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        smi = subprocess.Popen(["nvidia-smi", "-i", str(torch.cuda.current_device()), "--query-gpu=clocks.sm,power.draw",
+                                "--format=csv,noheader,nounits", "-lms", "100"], stdout=log, stderr=subprocess.DEVNULL)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        smi.terminate()
+        smi.wait()
+        log.seek(0)
+        mhz = sorted(float(x.split(",")[0]) for x in log.read().splitlines() if x.strip() and float(x.split(",")[1]) > 300)
+        return e0.elapsed_time(e1) / args.reps, (mhz[len(mhz) // 2] if mhz else None)
+
+    res = {}
+    for name, pair, fn in (("pair_full", "1", ours(True)), ("pair_nostore", "1", ours(False)),
+                           ("single_full", "0", ours(True)), ("cublas", "1", cublas)):
+        os.environ["SAELENS_B200_GEMM_PAIR"] = pair
+        ms, mhz = timed(fn)
+        st.check(name)
+        res[name] = {"ms": round(ms, 3), "tflops": round(2 * M * N * K / ms / 1e9, 1), "sm_mhz": mhz}
+    print(json.dumps({"M": M, "N": N, "K": K, **res}), flush=True)
 
 
 def ddp(args: argparse.Namespace) -> None:
@@ -529,6 +593,45 @@ def router(args: argparse.Namespace) -> None:
     dist.destroy_process_group()
 
 
+def lm(args: argparse.Namespace) -> None:
+    """Producer LM forward up to the hooked layer (activation capture), one GPU: CUDA-event ms per
+    forward on this package's kernels against the same model on PyTorch ops (F.linear / cuBLAS,
+    scaled_dot_product_attention / cuDNN or flash, torch norms), plus achieved TFLOP/s."""
+    import torch
+
+    from saelens_b200.models.lm import transformer as T
+    from saelens_b200.models.lm.transformer import HookedLM, preset_config
+
+    torch.cuda.set_device(0)
+    cfg = preset_config(args.model, n_layers=args.stop, dtype="bfloat16")
+    torch.manual_seed(0)
+    model = HookedLM(cfg, device="cuda")
+    tokens = torch.randint(0, cfg.d_vocab, (args.batch, args.ctx), device="cuda")
+    H, KV, dh, d = cfg.n_heads, cfg.n_key_value_heads, cfg.d_head, cfg.d_model
+    per_tok = 2 * (d * H * dh + 2 * d * KV * dh + H * dh * d + (3 if cfg.gated_mlp else 2) * d * cfg.d_mlp)
+    attn = 2 * 2 * (args.ctx + 1) / 2 * H * dh  # causal QK^T and PV per token (mean over positions)
+    flops = args.batch * args.ctx * args.stop * (per_tok + attn)
+    res = {"model": args.model, "layers_run": args.stop, "batch": args.batch, "ctx": args.ctx}
+    for name, native in (("native", True), ("torch", False)):
+        T.FORCE_TORCH = not native
+        with torch.no_grad():
+            for _ in range(2):
+                model(tokens, stop_at_layer=args.stop)
+            torch.cuda.synchronize()
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record()
+            for _ in range(args.reps):
+                out = model(tokens, stop_at_layer=args.stop)
+            t1.record()
+            torch.cuda.synchronize()
+        ms = t0.elapsed_time(t1) / args.reps
+        res[name] = {"ms": round(ms, 3), "tokens_per_s": round(args.batch * args.ctx / ms * 1e3, 1),
+                     "tflops": round(flops / ms / 1e9, 1)}
+        res[name + "_out_norm"] = float(out.float().norm())
+    T.FORCE_TORCH = False
+    print(json.dumps(res), flush=True)
+
+
 def main() -> None:
     p = argparse.ArgumentParser(prog="python -m saelens_b200.perf_cases")
     sub = p.add_subparsers(dest="cmd", required=True)
@@ -580,8 +683,20 @@ def main() -> None:
     rt.add_argument("--rows", type=int, default=8192)
     rt.add_argument("--d", type=int, default=4096)
     rt.add_argument("--no-nccl", action="store_true", help="skip the NCCL comparison (1-GPU profiling runs)")
+    gs = sub.add_parser("gemm-step", help="headline encoder GEMM chunk: ours (pair / single, with / without "
+                                         "stores) vs cuBLAS under the power cap")
+    gs.add_argument("--m", type=int, default=4096)
+    gs.add_argument("--n", type=int, default=1048576)
+    gs.add_argument("--k", type=int, default=4096)
+    gs.add_argument("--reps", type=int, default=10)
+    lmp = sub.add_parser("lm", help="producer LM forward to the hooked layer: native kernels vs PyTorch ops")
+    lmp.add_argument("--model", default="llama-3-8b")
+    lmp.add_argument("--stop", type=int, default=17, help="blocks run (hook layer + 1)")
+    lmp.add_argument("--batch", type=int, default=8)
+    lmp.add_argument("--ctx", type=int, default=1024)
+    lmp.add_argument("--reps", type=int, default=5)
     args = p.parse_args()
-    {"phases": phases, "fused-case": fused_case, "gemm": gemm, "ddp": ddp, "allreduce": allreduce, "router": router,
+    {"gemm-step": gemm_step, "lm": lm, "phases": phases, "fused-case": fused_case, "gemm": gemm, "ddp": ddp, "allreduce": allreduce, "router": router,
      "tpdp": tpdp, "fsdp": ddp, "ddp-hook": ddp_hook, "ring": ring}[args.cmd](args)
 
 

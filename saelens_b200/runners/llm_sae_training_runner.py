@@ -263,15 +263,18 @@ class LanguageModelSAETrainingRunner:
         return result
 
     def _native_fsdp_ok(self, sae: TrainingSAE[Any]) -> bool:
-        """TopK / BatchTopK on CUDA with the native ops, at most 8 NCCL ranks (one NVSwitch
-        domain), d_sae divisible into 256-latent tiles per rank."""
+        """TopK / BatchTopK / JumpReLU on CUDA with the native ops, at most 8 NCCL ranks (one
+        NVSwitch domain), d_sae divisible into 256-latent tiles per rank."""
         if self.cfg.sae_engine == "torch" or not sae.W_dec.is_cuda:
             return False
+        from saelens_b200.parallel.fsdp_jumprelu_engine import fsdp_jumprelu_supported
         from saelens_b200.training.engine import engine_supported
 
         world = dist.get_world_size(self.dp_group)
-        return (engine_supported(sae) and 1 < world <= 8 and dist.get_backend(self.dp_group) == "nccl"
-                and sae.W_dec.shape[0] % (256 * world) == 0)
+        if not (1 < world <= 8 and dist.get_backend(self.dp_group) == "nccl"):
+            return False
+        return ((engine_supported(sae) and sae.W_dec.shape[0] % (256 * world) == 0)
+                or fsdp_jumprelu_supported(sae, world))
 
     def _wrap_dp(self, sae: TrainingSAE[Any]) -> Any:
         if self.dp_group is None or self.cfg.sae_dp_mode == "manual":

@@ -65,13 +65,13 @@ def _materialise_local(sae: Any, s: BenchSetup) -> Any:
     return sae
 
 
-def synthetic_batch(s: BenchSetup, seed: int, device: Any = "cpu") -> torch.Tensor:
-    """N(0,1) activations rescaled to norm sqrt(d_in) (bf16)."""
+def synthetic_batch(s: BenchSetup, seed: int, device: Any = "cpu", dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """N(0,1) activations rescaled to norm sqrt(d_in) (bf16 unless `dtype` says otherwise)."""
     g = torch.Generator(device=device)
     g.manual_seed(seed)
     x = torch.randn(s.batch, s.d_in, generator=g, device=device)
     x = x / x.norm(dim=-1, keepdim=True) * math.sqrt(s.d_in)
-    return x.to(torch.bfloat16)
+    return x.to(dtype)
 
 
 def _make_engine(s: BenchSetup) -> Any:
@@ -143,11 +143,14 @@ def run_device_timed(s: BenchSetup, steps: int, warmup: int, sampler: Any = None
 
 
 class PinnedBatches:
-    """Data provider serving pre-generated pinned host batches (the H2D copy happens in the
-    trainer's `.to(device, non_blocking=True)`)."""
+    """Data provider serving pre-generated fp32 activation batches from pinned host memory, the
+    dtype an activation store yields; the engine casts to bf16 on the device.  `n` distinct
+    batches are served in turn."""
 
-    def __init__(self, s: BenchSetup, n: int = 3):
-        self.bufs = [synthetic_batch(s, seed=500 + i).pin_memory() for i in range(n)]
+    N_DISTINCT = 8
+
+    def __init__(self, s: BenchSetup, n: int = N_DISTINCT):
+        self.bufs = [synthetic_batch(s, seed=500 + i, dtype=torch.float32).pin_memory() for i in range(n)]
         self.i = 0
 
     def __iter__(self) -> "PinnedBatches":
@@ -179,7 +182,9 @@ def run_e2e(s: BenchSetup, steps: int, warmup: int) -> dict[str, Any]:
         feature_sampling_window=2000, logger=LoggingConfig(log_to_wandb=False), sae_engine="native",
         tp_exchange=s.tp_exchange,
     )
-    data = PinnedBatches(local)
+    from saelens_b200.training.prefetch import DevicePrefetcher
+
+    data = DevicePrefetcher(PinnedBatches(local), device=cfg.device)
     trainer = SAETrainer(cfg, sae, data, tp_input_layout="row_sharded")
     trainer.fit_steps(warmup)
     torch.cuda.synchronize()
@@ -192,9 +197,67 @@ def run_e2e(s: BenchSetup, steps: int, warmup: int) -> dict[str, Any]:
     torch.cuda.synchronize()
     _barrier(s.world)
     ms = _max_over_ranks(t0.elapsed_time(t1) / steps, s.world)
-    h2d = rows_local * s.d_in * 2
+    h2d = rows_local * s.d_in * 4  # fp32 rows from pinned host memory
     if hasattr(trainer.engine, "close"):
         trainer.engine.close()
     del trainer, sae, data
     _free()
     return {"ms_per_step": ms, "h2d_bytes": h2d, "d2h_bytes": 4}
+
+
+def parity_check(world: int, rank: int, d_in: int = 4096, d_sae: int = 16384, k: int = 128, batch: int = 2048,
+                 steps: int = 3, lr: float = 1e-3, tp_exchange: str = "p2p") -> dict[str, Any]:
+    """Tensor-parallel step against the single-GPU step on a small SAE, run before the timed region.
+
+    Every rank builds the same full SAE (same seed) twice: one copy is latent-sharded and trained
+    by the TP engine on this rank's rows of the batch, the other is trained whole by the single-GPU
+    engine on the whole batch, on this rank's GPU.  Returns the largest relative loss difference
+    and the largest difference of this rank's parameter shard (max over ranks), plus `ok`.  The
+    dead-latent auxiliary loss runs on the second step."""
+    from saelens_b200.models.topk import TopKTrainingSAE, TopKTrainingSAEConfig
+    from saelens_b200.parallel.tp_engine import TPTopKEngine
+    from saelens_b200.training.engine import FusedTopKEngine
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+
+    def build() -> Any:
+        torch.manual_seed(4321)
+        sae = TopKTrainingSAE(TopKTrainingSAEConfig(d_in=d_in, d_sae=d_sae, k=k, device=str(dev)))
+        with torch.no_grad():
+            sae.b_enc.normal_(0, 0.01)
+            sae.b_dec.normal_(0, 0.05)
+        return sae
+
+    g = torch.Generator(device="cpu").manual_seed(99)
+    x = torch.randn(batch, d_in, generator=g)
+    x = (x / x.norm(dim=-1, keepdim=True) * math.sqrt(d_in)).to(torch.bfloat16).to(dev)
+    dead = (torch.arange(d_sae, device=dev) % 5) == 0
+    n = d_sae // world
+    rows = batch // world
+
+    sae_tp = build()
+    sae_tp.shard_weights(dist.group.WORLD)
+    tp = TPTopKEngine(sae_tp, lr=lr, group=dist.group.WORLD, fused=tp_exchange == "p2p")
+    tp_losses = [float(tp.step(x[rank * rows:(rank + 1) * rows].contiguous(), dead_mask=dead[rank * n:(rank + 1) * n],
+                               run_aux=(i == 1)).loss) for i in range(steps)]
+    torch.cuda.synchronize()
+    tp.status.check("parity (tensor parallel)")
+    one = FusedTopKEngine(build(), lr=lr)
+    ref_losses = [float(one.step(x, dead_mask=dead, run_aux=(i == 1)).loss) for i in range(steps)]
+    torch.cuda.synchronize()
+    one.status.check("parity (single GPU)")
+    loss_err = max(abs(a - b) / max(abs(b), 1e-12) for a, b in zip(tp_losses, ref_losses))
+    sl = slice(rank * n, (rank + 1) * n)
+    param_err = max((tp.p_dec - one.p_dec[sl]).abs().max().item(), (tp.p_enc - one.p_enc[sl]).abs().max().item(),
+                    (tp.p_bdec - one.p_bdec).abs().max().item())
+    if hasattr(tp, "close"):
+        tp.close()
+    del tp, one, sae_tp
+    _free()
+    loss_err = _max_over_ranks(loss_err, world)
+    param_err = _max_over_ranks(param_err, world)
+    # Adam moves every coordinate by at most lr per step, so parameters that differ by more
+    # than a few lr after `steps` steps point at a wrong gradient, not at summation order.
+    ok = loss_err <= 1e-3 and param_err <= 3 * steps * lr
+    return {"max_rel_loss_err": loss_err, "max_param_err": param_err, "ok": bool(ok), "d_sae": d_sae,
+            "batch": batch, "steps": steps}

@@ -44,9 +44,12 @@ class EngineStepResult:
     topk_vals: torch.Tensor     # [B, k] fp32 pre-activations of the selected latents (pre-ReLU)
     topk_idx: torch.Tensor      # [B, k] int32 selected latent indices (-1 = none)
     fire_counts: torch.Tensor   # [d_sae] int32 rows in which each latent fired this step
+    l0: torch.Tensor | None = None  # mean active latents per row, when the step keeps no per-row lists
 
     def feature_acts_sparse(self, d_sae: int) -> torch.Tensor:
         """Sparse COO [B, d_sae] of ReLU'd activations (what the reference's TopK emits)."""
+        if self.topk_idx is None:
+            raise RuntimeError("this native step (dense form) keeps no per-row activation lists")
         B, k = self.topk_idx.shape
         live = (self.topk_idx >= 0) & (self.topk_vals > 0)
         rows = torch.arange(B, device=self.topk_idx.device).unsqueeze(1).expand(B, k)[live]

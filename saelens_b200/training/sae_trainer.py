@@ -161,8 +161,13 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
         if self._native_fsdp:
             from saelens_b200.parallel.fsdp_engine import FSDPTopKEngine
 
-            self.engine = FSDPTopKEngine(self._base_sae, lr=cfg.lr, group=dp_group, beta1=cfg.adam_beta1,
-                                         beta2=cfg.adam_beta2)
+            fsdp_cls: Any = FSDPTopKEngine
+            if type(self._base_sae).__name__ == "JumpReLUTrainingSAE":
+                from saelens_b200.parallel.fsdp_jumprelu_engine import FSDPJumpReLUEngine
+
+                fsdp_cls = FSDPJumpReLUEngine
+            self.engine = fsdp_cls(self._base_sae, lr=cfg.lr, group=dp_group, beta1=cfg.adam_beta1,
+                                   beta2=cfg.adam_beta2)
             self._engine_stats_global = True
         elif want != "torch" and not self._is_fsdp and (dp_group is not None or self._is_ddp):
             from saelens_b200.training.engine import engine_supported
@@ -194,12 +199,11 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
                 self.engine = TPTopKEngine(self._base_sae, lr=cfg.lr, group=tp_group, beta1=cfg.adam_beta1,
                                            beta2=cfg.adam_beta2, input_layout=tp_input_layout,
                                            fused=getattr(cfg, "tp_exchange", "p2p") == "p2p")
-            elif want == "native" and tp_group is None and type(self._base_sae).__name__ == "JumpReLUTrainingSAE":
-                # opt-in: the native JumpReLU step pays off once the SAE is sparse (candidate cap per row)
-                from saelens_b200.training.jumprelu_engine import JumpReLUEngine, jumprelu_engine_supported
+            elif tp_group is None and type(self._base_sae).__name__ == "JumpReLUTrainingSAE" and \
+                    self._jumprelu_native_ok(want == "native"):
+                # dense tcgen05 step while many latents are active, the sparse step once rows are sparse
+                from saelens_b200.training.jumprelu_engine import JumpReLUEngine
 
-                if not jumprelu_engine_supported(self._base_sae):
-                    raise ValueError("sae_engine='native' requested but this JumpReLU SAE/device is not supported")
                 self.engine = JumpReLUEngine(self._base_sae, lr=cfg.lr, beta1=cfg.adam_beta1, beta2=cfg.adam_beta2)
             elif engine_supported(self._base_sae) and tp_group is None:
                 self.engine = FusedTopKEngine(self._base_sae, lr=cfg.lr, beta1=cfg.adam_beta1,
@@ -285,6 +289,14 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
             if quiesce_if_requested():
                 break
         return self._finish_fit()
+
+    def _jumprelu_native_ok(self, required: bool) -> bool:
+        from saelens_b200.training.jumprelu_engine import jumprelu_engine_supported
+
+        ok = jumprelu_engine_supported(self._base_sae)
+        if required and not ok:
+            raise ValueError("sae_engine='native' requested but this JumpReLU SAE/device is not supported")
+        return ok
 
     def fit_steps(self, n_steps: int, read_loss: bool = True) -> list[float]:
         """Run `n_steps` iterations of the training loop (same body as `fit`).
@@ -839,6 +851,8 @@ class _LazySparse:
 
     def l0(self) -> float:
         r = self._res
+        if r.topk_idx is None:
+            return float(r.l0)
         return float(((r.topk_idx >= 0) & (r.topk_vals > 0)).sum(-1).float().mean())
 
     def to_sparse(self) -> torch.Tensor:

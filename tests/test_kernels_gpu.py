@@ -29,6 +29,26 @@ def test_gemm_tn_matches_fp32(M, N, K):
     assert err <= tol, f"max err {err} > {tol}"
 
 
+@pytest.mark.parametrize("M,N,K", [(300, 1000, 1000), (513, 50257, 64), (128, 40, 24), (1024, 2003, 776)])
+def test_gemm_ragged_width_and_depth(M, N, K):
+    """Any N (partial last 256-column tile, masked epilogue) and K a multiple of 8 (the ragged last
+    k-block reads zeros past K), with a bias, on both the single-CTA and the CTA-pair kernel."""
+    ops = _ops()
+    a = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    b = torch.randn(N, K, device="cuda").to(torch.bfloat16)
+    bias = torch.randn(N, device="cuda")
+    guard = 7.0
+    buf = torch.full((M, (N + 7) // 8 * 8 + 8), guard, dtype=torch.bfloat16, device="cuda")
+    out = buf[:, :N]
+    ops.gemm_tn(a, b, bias=bias, out=out)
+    ref = a.float() @ b.float().T + bias
+    torch.cuda.synchronize()
+    assert (out.float() - ref).abs().max().item() <= 1e-2 * ref.abs().max().item() + 1e-3
+    assert (buf[:, N:] == guard).all(), "columns past N were written"
+    auto, _ = ops.gemm_tn(a, b, bias=bias)
+    assert auto.shape == (M, N) and torch.equal(auto, out)
+
+
 def test_gemm_epilogue_bias_scale_relu_chunkmax():
     ops = _ops()
     M, N, K = 384, 768, 512

@@ -20,7 +20,7 @@ def _lib():
     fn = lib.sb_csc_build_noalloc
     fn.restype = ctypes.c_int
     fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p,
-                   ctypes.c_void_p, ctypes.c_void_p]
+                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     lib.sb_noalloc_strerror.restype = ctypes.c_char_p
     lib.sb_noalloc_strerror.argtypes = [ctypes.c_int]
     return lib, fn
@@ -56,25 +56,72 @@ def _canonical(colptr, pairs):
     return torch.sort(key).values
 
 
-def test_noalloc_csc_matches_allocating_path_twice():
+def _call(fn, vals, idx, N, bad=None):
+    M = vals.numel()
+    colptr = torch.full((N + 1,), -5, dtype=torch.int64, device="cuda")
+    pairs = torch.full((max(M, 1),), -5, dtype=torch.int64, device="cuda")
+    rc = fn(vals.data_ptr() if M else 0, idx.data_ptr() if M else 0, M, N, colptr.data_ptr(), pairs.data_ptr(),
+            bad.data_ptr() if bad is not None else 0, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    return rc, colptr, pairs
+
+
+@pytest.mark.parametrize("M, k, N", [
+    (1024, 32, 8192),      # whole scan blocks
+    (512, 16, 1000),       # a partial last scan block
+    (256, 64, 1 << 20),    # the maximum: the single-block scan of 1024 block sums is full
+])
+def test_noalloc_csc_matches_allocating_path_twice(M, k, N):
     lib, fn = _lib()
-    M, k, N = 1024, 32, 8192
+    bad = torch.full((1,), -7, dtype=torch.int32, device="cuda")
     for call, seed in enumerate((1, 2)):  # two calls in a row: the shared scratch is reused
         vals, idx = _random_selection(M, k, N, seed)
         ref_colptr, ref_pairs = _reference(vals, idx, N)
-        colptr = torch.full((N + 1,), -5, dtype=torch.int64, device="cuda")
-        pairs = torch.full((M * k,), -5, dtype=torch.int64, device="cuda")
-        rc = fn(vals.data_ptr(), idx.data_ptr(), M * k, N, colptr.data_ptr(), pairs.data_ptr(),
-                torch.cuda.current_stream().cuda_stream)
-        torch.cuda.synchronize()
+        rc, colptr, pairs = _call(fn, vals, idx, N, bad)
         assert rc == 0, lib.sb_noalloc_strerror(rc)
         assert torch.equal(colptr, ref_colptr), f"call {call}: colptr differs"
         assert torch.equal(_canonical(colptr, pairs), _canonical(ref_colptr, ref_pairs)), f"call {call}: pairs differ"
+        assert int(bad) == 0
 
 
-def test_noalloc_csc_rejects_oversized_latent_count():
+def test_noalloc_csc_with_no_pairs_gives_zero_offsets():
+    lib, fn = _lib()
+    # a previous call leaves counts in the shared scratch; this call must not see them
+    vals, idx = _random_selection(64, 8, 4096, 3)
+    assert _call(fn, vals, idx, 4096)[0] == 0
+    empty_v = torch.empty(0, device="cuda")
+    empty_i = torch.empty(0, dtype=torch.int32, device="cuda")
+    rc, colptr, _ = _call(fn, empty_v, empty_i, 4096)
+    assert rc == 0, lib.sb_noalloc_strerror(rc)
+    assert torch.equal(colptr, torch.zeros_like(colptr))
+
+
+def test_noalloc_csc_skips_and_counts_out_of_range_indices():
+    lib, fn = _lib()
+    M, k, N = 128, 8, 2048
+    vals, idx = _random_selection(M, k, N, 4)
+    vals = vals.abs() + 0.1  # every in-range pair is kept
+    idx[5, 0] = N
+    idx[9, 2] = N + 1000
+    bad = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rc, colptr, pairs = _call(fn, vals, idx, N, bad)
+    assert rc == 0, lib.sb_noalloc_strerror(rc)
+    assert int(bad) == 2
+    ok = idx.clone()
+    ok[5, 0] = -1
+    ok[9, 2] = -1
+    ref_colptr, ref_pairs = _reference(vals, ok, N)
+    assert torch.equal(colptr, ref_colptr)
+    assert torch.equal(_canonical(colptr, pairs), _canonical(ref_colptr, ref_pairs))
+
+
+def test_noalloc_csc_rejects_oversized_arguments():
     lib, fn = _lib()
     colptr = torch.zeros(4, dtype=torch.int64, device="cuda")
-    rc = fn(0, 0, 0, (1 << 20) + 1, colptr.data_ptr(), 0, torch.cuda.current_stream().cuda_stream)
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = fn(0, 0, 0, (1 << 20) + 1, colptr.data_ptr(), 0, 0, stream)
     assert rc == 1
     assert b"1048576" in lib.sb_noalloc_strerror(rc)
+    rc = fn(1, 1, 1 << 31, 3, colptr.data_ptr(), 1, 0, stream)  # never dereferenced: rejected first
+    assert rc == 5
+    assert b"2147483647" in lib.sb_noalloc_strerror(rc)
