@@ -17,6 +17,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "check.h"
 
 namespace sb {
 namespace adam {
@@ -259,10 +260,10 @@ void adam_rows(const torch::Tensor& pd, const torch::Tensor& md, const torch::Te
                const c10::optional<torch::Tensor>& bias_eff, double lr, double beta1, double beta2,
                double eps, int64_t step, bool update) {
   const at::cuda::CUDAGuard guard(pd.device());
-  TORCH_CHECK(pd.is_contiguous() && pe.is_contiguous() && wd.is_contiguous() && we.is_contiguous(),
+  SB_CHECK(pd.is_contiguous() && pe.is_contiguous() && wd.is_contiguous() && we.is_contiguous(),
               "adam_rows: contiguous params required");
   const int64_t N = pd.size(0), D = pd.size(1);
-  TORCH_CHECK(D % 4 == 0, "adam_rows: d_in must be a multiple of 4");
+  SB_CHECK(D % 4 == 0, "adam_rows: d_in must be a multiple of 4");
   adam::RowArgs a{};
   a.pd = pd.data_ptr<float>(); a.md = md.data_ptr<float>(); a.vd = vd.data_ptr<float>();
   a.pe = pe.data_ptr<float>(); a.me = me.data_ptr<float>(); a.ve = ve.data_ptr<float>();
@@ -281,7 +282,7 @@ void adam_rows(const torch::Tensor& pd, const torch::Tensor& md, const torch::Te
   a.N = int(N);
   a.D = int(D);
   a.update = update ? 1 : 0;
-  TORCH_CHECK(!update || (a.gd && a.ge && a.gb && a.colptr), "adam_rows: gradients required for update");
+  SB_CHECK(!update || (a.gd && a.ge && a.gb && a.colptr), "adam_rows: gradients required for update");
   if (N == 0) return;
   const int64_t grid = std::min<int64_t>((N + 7) / 8, int64_t(sm_count_adam()) * 8);
   adam::rows_kernel<<<dim3(grid), dim3(adam::ROW_THREADS), 0, at::cuda::getCurrentCUDAStream()>>>(

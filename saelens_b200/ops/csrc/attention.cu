@@ -26,6 +26,7 @@
 
 #include "common.cuh"
 #include "tmap.h"
+#include "check.h"
 
 namespace sb {
 namespace attn {
@@ -331,22 +332,22 @@ void launch(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor&
 // softcap <= 0 disables soft-capping.  D must be 64, 128 or 256.
 void attention_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& out,
                    double scale, double softcap, bool causal, const torch::Tensor& status) {
-  TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda() && out.is_cuda(), "attention_fwd: CUDA tensors required");
-  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16 &&
+  SB_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda() && out.is_cuda(), "attention_fwd: CUDA tensors required");
+  SB_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16 &&
                   out.scalar_type() == at::kBFloat16,
               "attention_fwd: bf16 tensors required");
-  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "attention_fwd: q, k, v must be [B, S, heads, D]");
+  SB_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "attention_fwd: q, k, v must be [B, S, heads, D]");
   const int64_t B = q.size(0), S = q.size(1), H = q.size(2), D = q.size(3), KV = k.size(2);
-  TORCH_CHECK(D == 64 || D == 128 || D == 256, "attention_fwd: head dim must be 64, 128 or 256, got ", D);
-  TORCH_CHECK(k.size(0) == B && k.size(1) == S && k.size(3) == D && v.sizes() == k.sizes(), "attention_fwd: k/v shape");
-  TORCH_CHECK(KV >= 1 && H % KV == 0, "attention_fwd: query heads must be a multiple of the K/V heads");
+  SB_CHECK(D == 64 || D == 128 || D == 256, "attention_fwd: head dim must be 64, 128 or 256, got ", D);
+  SB_CHECK(k.size(0) == B && k.size(1) == S && k.size(3) == D && v.sizes() == k.sizes(), "attention_fwd: k/v shape");
+  SB_CHECK(KV >= 1 && H % KV == 0, "attention_fwd: query heads must be a multiple of the K/V heads");
   for (const auto* t : {&q, &k, &v}) {
-    TORCH_CHECK(t->stride(3) == 1 && t->stride(2) == D && t->stride(1) % 8 == 0 && t->stride(0) % 8 == 0,
+    SB_CHECK(t->stride(3) == 1 && t->stride(2) == D && t->stride(1) % 8 == 0 && t->stride(0) % 8 == 0,
                 "attention_fwd: head dim contiguous, heads adjacent, token/batch strides multiples of 8");
   }
-  TORCH_CHECK(out.is_contiguous() && out.sizes() == q.sizes(), "attention_fwd: out must be contiguous [B, S, H, D]");
-  TORCH_CHECK(status.is_cuda() && status.scalar_type() == at::kInt, "attention_fwd: status");
-  TORCH_CHECK(B <= 65535 && H <= 65535 && S < (1 << 30), "attention_fwd: size");
+  SB_CHECK(out.is_contiguous() && out.sizes() == q.sizes(), "attention_fwd: out must be contiguous [B, S, H, D]");
+  SB_CHECK(status.is_cuda() && status.scalar_type() == at::kInt, "attention_fwd: status");
+  SB_CHECK(B <= 65535 && H <= 65535 && S < (1 << 30), "attention_fwd: size");
   if (B == 0 || S == 0 || H == 0) return;
   const at::cuda::CUDAGuard guard(q.device());
   attn::Params prm{};

@@ -140,7 +140,9 @@ void gemm_dense_bf16(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, 
                      const c10::optional<torch::Tensor>& nnz, const c10::optional<torch::Tensor>& sumsq,
                      const c10::optional<torch::Tensor>& gate_bias, const c10::optional<torch::Tensor>& mag_scale,
                      const torch::Tensor& status, int64_t max_ctas, const std::vector<int64_t>& rs_bases,
-                     int64_t rs_rank, int64_t rs_off, int64_t rs_n);
+                     int64_t rs_rank, int64_t rs_off, int64_t rs_n, const c10::optional<torch::Tensor>& hsum,
+                     const c10::optional<torch::Tensor>& hoff, const c10::optional<torch::Tensor>& colsum2,
+                     const c10::optional<torch::Tensor>& addend, const c10::optional<torch::Tensor>& oscale);
 void gemm_fsdp_dense_bf16(const torch::Tensor& A, const torch::Tensor& w_own, const std::vector<int64_t>& peer_bases,
                           int64_t rank, int64_t w_off, int64_t flag_off, bool push, int64_t epoch,
                           const c10::optional<torch::Tensor>& w2_own, int64_t w2_off, int64_t flag2_off,
@@ -228,7 +230,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("nnz") = py::none(), py::arg("sumsq") = py::none(), py::arg("gate_bias") = py::none(),
         py::arg("mag_scale") = py::none(), py::arg("status"), py::arg("max_ctas") = 0,
         py::arg("rs_bases") = std::vector<int64_t>{}, py::arg("rs_rank") = 0, py::arg("rs_off") = 0,
-        py::arg("rs_n") = 0);
+        py::arg("rs_n") = 0, py::arg("hsum") = py::none(), py::arg("hoff") = py::none(),
+        py::arg("colsum2") = py::none(), py::arg("addend") = py::none(), py::arg("oscale") = py::none());
   m.def("gemm_fsdp_dense_bf16", &sb::gemm_fsdp_dense_bf16);
   m.def("attention_fwd", &sb::attention_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"),
         py::arg("scale"), py::arg("softcap"), py::arg("causal"), py::arg("status"));

@@ -41,6 +41,7 @@
 #include "common.cuh"
 #include "p2p.cuh"
 #include "tmap.h"
+#include "check.h"
 
 namespace sb {
 namespace gemm {
@@ -81,8 +82,11 @@ struct Epi {
 //   JumpReLU forward (thr, no hin): out2 = v (pre-activation), v = v * 1[v > thr]
 //   gated (gate_bias):       out2 = relu(acc + gate_bias) (gate path), v = 1[acc + gate_bias > 0] *
 //                            relu(acc * mag_scale + bias)        (magnitude path: x (W * e^r) + b_mag)
-//   relu;  out = bf16(v);  then over the stored values: colsum[col] += v, colcnt[col] += 1[v != 0],
-//   nnz += 1[v != 0], sumsq += v^2 (rows >= M and columns >= N contribute nothing).
+//   relu;  colsum[col] += v;  hsum[col] += v * (h - hoff[col]) (backward mode);
+//   colsum2[col] += out2 (gated: the gate activations);
+//   combine (addend): v = v * oscale[col] + addend[row, col];
+//   out = bf16(v);  then over the stored values: colcnt[col] += 1[v != 0], nnz += 1[v != 0],
+//   sumsq += v^2 (rows >= M and columns >= N contribute nothing).
 struct EpiD {
   __nv_bfloat16* out;
   int64_t ldo;
@@ -113,6 +117,12 @@ struct EpiD {
   p2p::Peers P;
   int64_t rs_off;
   int rs_n;
+  float* hsum;
+  const float* hoff;
+  float* colsum2;
+  const __nv_bfloat16* addend;
+  int64_t ldad;
+  const float* oscale;
 };
 
 // Sum over the 32 lanes of v[c] for every c; lane L returns the sum for column L.  Butterfly
@@ -201,10 +211,14 @@ __device__ __forceinline__ void epilogue_tile_dense(const EpiD& e, uint32_t trow
         const bool ok = j < nv;
         const float pg = v[j] + (ok ? __ldg(e.gate_bias + col0 + j) : 0.f);
         const float pm = v[j] * (ok ? __ldg(e.mag_scale + col0 + j) : 0.f) + (ok && e.bias ? __ldg(e.bias + col0 + j) : 0.f);
-        gate[j] = fmaxf(pg, 0.f);
+        gate[j] = (rowok && ok) ? __bfloat162float(__float2bfloat16_rn(fmaxf(pg, 0.f))) : 0.f;
         v[j] = pg > 0.f ? fmaxf(pm, 0.f) : 0.f;
       }
       if (e.out2 && rowok) store_bf16x32(e.out2 + int64_t(row) * e.ldo2 + col0, gate, nv);
+      if (e.colsum2) {
+        const float cs = warp_colsum32(gate, lane);
+        if (lane < nv && cs != 0.f) atomicAdd(e.colsum2 + col0 + lane, cs);
+      }
     } else if (e.bias) {
 #pragma unroll
       for (int j = 0; j < 32; ++j)
@@ -229,8 +243,9 @@ __device__ __forceinline__ void epilogue_tile_dense(const EpiD& e, uint32_t trow
         v[j] = e.res_coef * d;
       }
     }
+    float h[32];
     if (e.hin) {
-      float h[32], g[32];
+      float g[32];
       if (rowok && nv == 32) {
         load_bf16x32(e.hin + int64_t(row) * e.ldh + col0, h);
       } else {
@@ -266,7 +281,36 @@ __device__ __forceinline__ void epilogue_tile_dense(const EpiD& e, uint32_t trow
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
     }
-    // round to what is stored; statistics are taken over the stored values
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = (rowok && j < nv) ? v[j] : 0.f;
+    if (e.colsum) {
+      float t[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) t[j] = v[j];
+      const float cs = warp_colsum32(t, lane);
+      if (lane < nv && cs != 0.f) atomicAdd(e.colsum + col0 + lane, cs);
+    }
+    if (e.hsum && e.hin) {
+      float t[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) t[j] = v[j] * (h[j] - (j < nv ? __ldg(e.hoff + col0 + j) : 0.f));
+      const float cs = warp_colsum32(t, lane);
+      if (lane < nv && cs != 0.f) atomicAdd(e.hsum + col0 + lane, cs);
+    }
+    if (e.addend) {
+      float ad[32];
+      if (rowok && nv == 32) {
+        load_bf16x32(e.addend + int64_t(row) * e.ldad + col0, ad);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          ad[j] = (rowok && j < nv) ? __bfloat162float(e.addend[int64_t(row) * e.ldad + col0 + j]) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        v[j] = (rowok && j < nv) ? v[j] * (e.oscale ? __ldg(e.oscale + col0 + j) : 1.f) + ad[j] : 0.f;
+    }
+    // round to what is stored; the remaining statistics are taken over the stored values
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = (rowok && j < nv) ? __bfloat162float(__float2bfloat16_rn(v[j])) : 0.f;
     if (e.rs_n > 0) {
@@ -290,10 +334,6 @@ __device__ __forceinline__ void epilogue_tile_dense(const EpiD& e, uint32_t trow
       for (int j = 0; j < 32; ++j) cnt[j] = v[j] != 0.f ? 1.f : 0.f;
       const float cs = warp_colsum32(cnt, lane);
       if (lane < nv && cs != 0.f) atomicAdd(e.colcnt + col0 + lane, cs);
-    }
-    if (e.colsum) {
-      const float cs = warp_colsum32(v, lane);  // v is not used after this
-      if (lane < nv && cs != 0.f) atomicAdd(e.colsum + col0 + lane, cs);
     }
   }
   if (e.rs_n > 0) __threadfence_system();  // peer rows visible before a later launch's release flag
@@ -860,31 +900,31 @@ static gemm::Epi make_epi(int64_t M, int64_t N, const c10::optional<torch::Tenso
                           const c10::optional<torch::Tensor>& tmax = c10::nullopt) {
   gemm::Epi ep{};
   if (out) {
-    TORCH_CHECK(out->scalar_type() == at::kBFloat16 && out->size(0) == M && out->size(1) == N &&
+    SB_CHECK(out->scalar_type() == at::kBFloat16 && out->size(0) == M && out->size(1) == N &&
                     out->stride(1) == 1 && out->stride(0) % 8 == 0,
                 "gemm_tn_bf16: bad out");
     ep.out = reinterpret_cast<__nv_bfloat16*>(out->data_ptr());
     ep.ldo = out->stride(0);
   }
   if (cmax) {
-    TORCH_CHECK(cmax->scalar_type() == at::kBFloat16 && cmax->size(0) == M &&
+    SB_CHECK(cmax->scalar_type() == at::kBFloat16 && cmax->size(0) == M &&
                     cmax->size(1) == N / 32 && cmax->stride(1) == 1,
                 "gemm_tn_bf16: bad cmax");
     ep.cmax = reinterpret_cast<__nv_bfloat16*>(cmax->data_ptr());
     ep.ldc = cmax->stride(0);
   }
   if (bias) {
-    TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->numel() == N && bias->is_contiguous(),
+    SB_CHECK(bias->scalar_type() == at::kFloat && bias->numel() == N && bias->is_contiguous(),
                 "gemm_tn_bf16: bias must be fp32 [N]");
     ep.bias = bias->data_ptr<float>();
   }
   if (scale) {
-    TORCH_CHECK(scale->scalar_type() == at::kFloat && scale->numel() == N && scale->is_contiguous(),
+    SB_CHECK(scale->scalar_type() == at::kFloat && scale->numel() == N && scale->is_contiguous(),
                 "gemm_tn_bf16: scale must be fp32 [N]");
     ep.scale = scale->data_ptr<float>();
   }
   if (tmax) {
-    TORCH_CHECK(tmax->scalar_type() == at::kBFloat16 && tmax->size(0) == M && tmax->size(1) == N / gemm::BN &&
+    SB_CHECK(tmax->scalar_type() == at::kBFloat16 && tmax->size(0) == M && tmax->size(1) == N / gemm::BN &&
                     tmax->stride(1) == 1,
                 "gemm_tn_bf16: bad tmax (bf16 [M, N/256])");
     ep.tmax = reinterpret_cast<__nv_bfloat16*>(tmax->data_ptr());
@@ -963,16 +1003,16 @@ void gemm_tn_bf16(const torch::Tensor& A, const torch::Tensor& B, const c10::opt
                   const c10::optional<torch::Tensor>& scale, bool relu,
                   const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& cmax,
                   const torch::Tensor& status, int64_t max_ctas, const c10::optional<torch::Tensor>& tmax) {
-  TORCH_CHECK(A.is_cuda() && B.is_cuda(), "gemm_tn_bf16: CUDA tensors required");
-  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16,
+  SB_CHECK(A.is_cuda() && B.is_cuda(), "gemm_tn_bf16: CUDA tensors required");
+  SB_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16,
               "gemm_tn_bf16: bf16 operands required");
-  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm_tn_bf16: shape");
-  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1, "gemm_tn_bf16: K must be contiguous");
+  SB_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm_tn_bf16: shape");
+  SB_CHECK(A.stride(1) == 1 && B.stride(1) == 1, "gemm_tn_bf16: K must be contiguous");
   const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
-  TORCH_CHECK(K % 8 == 0, "gemm_tn_bf16: K must be a multiple of 8 (16-byte rows), got ", K);
-  TORCH_CHECK(N >= 1 && ((!cmax && !tmax) || N % gemm::BN == 0),
+  SB_CHECK(K % 8 == 0, "gemm_tn_bf16: K must be a multiple of 8 (16-byte rows), got ", K);
+  SB_CHECK(N >= 1 && ((!cmax && !tmax) || N % gemm::BN == 0),
               "gemm_tn_bf16: chunk / tile maxima need N to be a multiple of 256, got ", N);
-  TORCH_CHECK(M >= 1 && M < (1ll << 31) && N < (1ll << 31), "gemm_tn_bf16: size");
+  SB_CHECK(M >= 1 && M < (1ll << 31) && N < (1ll << 31), "gemm_tn_bf16: size");
   const at::cuda::CUDAGuard guard(A.device());
   const gemm::Epi ep = make_epi(M, N, bias, scale, relu, out, cmax, tmax);
   launch_gemm<false>(A.data_ptr(), A.stride(0), M, B, ep, status, max_ctas, gemm::Ag{}, use_pair(M));
@@ -989,19 +1029,19 @@ void gemm_ag_tn_bf16(const torch::Tensor& x_own, const std::vector<int64_t>& pee
                      const c10::optional<torch::Tensor>& cmax, const torch::Tensor& status,
                      const torch::Tensor& ticket, int64_t max_ctas, const c10::optional<torch::Tensor>& tmax) {
   const int64_t S = int64_t(peer_bases.size());
-  TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "gemm_ag: bad group");
-  TORCH_CHECK(x_own.is_cuda() && x_own.scalar_type() == at::kBFloat16 && x_own.is_contiguous(),
+  SB_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "gemm_ag: bad group");
+  SB_CHECK(x_own.is_cuda() && x_own.scalar_type() == at::kBFloat16 && x_own.is_contiguous(),
               "gemm_ag: x_own must be contiguous CUDA bf16");
-  TORCH_CHECK(B.scalar_type() == at::kBFloat16 && B.stride(1) == 1 && B.size(1) == x_own.size(1),
+  SB_CHECK(B.scalar_type() == at::kBFloat16 && B.stride(1) == 1 && B.size(1) == x_own.size(1),
               "gemm_ag: weight");
   const int64_t Bo = x_own.size(0), K = x_own.size(1), N = B.size(0);
-  TORCH_CHECK(Bo * S == total_rows, "gemm_ag: total_rows must be world * own rows");
-  TORCH_CHECK(Bo % gemm::BM == 0 && m_base % gemm::BM == 0 && M % gemm::BM == 0 && M >= gemm::BM &&
+  SB_CHECK(Bo * S == total_rows, "gemm_ag: total_rows must be world * own rows");
+  SB_CHECK(Bo % gemm::BM == 0 && m_base % gemm::BM == 0 && M % gemm::BM == 0 && M >= gemm::BM &&
                   m_base + M <= total_rows,
               "gemm_ag: rows must be multiples of 128");
-  TORCH_CHECK(total_rows / gemm::BM <= gemm::MAX_MTILES, "gemm_ag: too many rows");
-  TORCH_CHECK(K % gemm::BK == 0 && N % gemm::BN == 0, "gemm_ag: K % 64 and N % 256");
-  TORCH_CHECK(x_off % 16 == 0 && flag_off % 4 == 0, "gemm_ag: slab offsets must be aligned");
+  SB_CHECK(total_rows / gemm::BM <= gemm::MAX_MTILES, "gemm_ag: too many rows");
+  SB_CHECK(K % gemm::BK == 0 && N % gemm::BN == 0, "gemm_ag: K % 64 and N % 256");
+  SB_CHECK(x_off % 16 == 0 && flag_off % 4 == 0, "gemm_ag: slab offsets must be aligned");
   const at::cuda::CUDAGuard guard(x_own.device());
   const gemm::Epi ep = make_epi(M, N, bias, scale, relu, out, cmax, tmax);
   gemm::Ag ag{};
@@ -1019,7 +1059,7 @@ void gemm_ag_tn_bf16(const torch::Tensor& x_own, const std::vector<int64_t>& pee
   ag.rot = (own0 >= m_base && own0 < m_base + M) ? int((own0 - m_base) / tile_rows) % num_m : 0;
   ag.push = push ? 1 : 0;
   ag.epoch = uint32_t(epoch);
-  TORCH_CHECK(ticket.is_cuda() && ticket.scalar_type() == at::kInt && ticket.numel() >= 1, "gemm_ag: ticket");
+  SB_CHECK(ticket.is_cuda() && ticket.scalar_type() == at::kInt && ticket.numel() >= 1, "gemm_ag: ticket");
   ag.ticket = ticket.data_ptr<int>();
   if (push) C10_CUDA_CHECK(cudaMemsetAsync(ag.ticket, 0, sizeof(int), at::cuda::getCurrentCUDAStream()));
   const char* a_ptr = reinterpret_cast<const char*>(peer_bases[rank]) + x_off + m_base * K * 2;
@@ -1040,19 +1080,19 @@ void gemm_fsdp_tn_bf16(const torch::Tensor& A, const torch::Tensor& w_own, const
                        const torch::Tensor& status, const torch::Tensor& ticket, int64_t max_ctas,
                        const c10::optional<torch::Tensor>& tmax) {
   const int64_t S = int64_t(peer_bases.size());
-  TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "gemm_fsdp: bad group");
-  TORCH_CHECK(A.is_cuda() && A.scalar_type() == at::kBFloat16 && A.dim() == 2 && A.stride(1) == 1,
+  SB_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "gemm_fsdp: bad group");
+  SB_CHECK(A.is_cuda() && A.scalar_type() == at::kBFloat16 && A.dim() == 2 && A.stride(1) == 1,
               "gemm_fsdp: A must be CUDA bf16 with contiguous rows");
-  TORCH_CHECK(w_own.is_cuda() && w_own.scalar_type() == at::kBFloat16 && w_own.is_contiguous() &&
+  SB_CHECK(w_own.is_cuda() && w_own.scalar_type() == at::kBFloat16 && w_own.is_contiguous() &&
                   w_own.size(1) == A.size(1),
               "gemm_fsdp: w_own must be contiguous bf16 [n, K]");
   const int64_t M = A.size(0), K = A.size(1), n = w_own.size(0), N = n * S;
-  TORCH_CHECK(n % gemm::BN == 0 && K % gemm::BK == 0, "gemm_fsdp: shard rows % 256 and K % 64");
-  TORCH_CHECK(N / gemm::BN <= gemm::MAX_MTILES && M >= 1 && M < (1ll << 31), "gemm_fsdp: size");
-  TORCH_CHECK(w_off % 16 == 0 && flag_off % 4 == 0 && w2_off % 16 == 0 && flag2_off % 4 == 0,
+  SB_CHECK(n % gemm::BN == 0 && K % gemm::BK == 0, "gemm_fsdp: shard rows % 256 and K % 64");
+  SB_CHECK(N / gemm::BN <= gemm::MAX_MTILES && M >= 1 && M < (1ll << 31), "gemm_fsdp: size");
+  SB_CHECK(w_off % 16 == 0 && flag_off % 4 == 0 && w2_off % 16 == 0 && flag2_off % 4 == 0,
               "gemm_fsdp: slab offsets must be aligned");
   if (w2_own) {
-    TORCH_CHECK(w2_own->is_cuda() && w2_own->scalar_type() == at::kBFloat16 && w2_own->is_contiguous() &&
+    SB_CHECK(w2_own->is_cuda() && w2_own->scalar_type() == at::kBFloat16 && w2_own->is_contiguous() &&
                     w2_own->sizes() == w_own.sizes(),
                 "gemm_fsdp: w2_own must be contiguous bf16 like w_own");
   }
@@ -1071,7 +1111,7 @@ void gemm_fsdp_tn_bf16(const torch::Tensor& A, const torch::Tensor& w_own, const
   ag.src2 = w2_own ? reinterpret_cast<const __nv_bfloat16*>(w2_own->data_ptr()) : nullptr;
   ag.x2_off = w2_off;
   ag.flag2_off = flag2_off;
-  TORCH_CHECK(ticket.is_cuda() && ticket.scalar_type() == at::kInt && ticket.numel() >= 1, "gemm_fsdp: ticket");
+  SB_CHECK(ticket.is_cuda() && ticket.scalar_type() == at::kInt && ticket.numel() >= 1, "gemm_fsdp: ticket");
   ag.ticket = ticket.data_ptr<int>();
   if (push) C10_CUDA_CHECK(cudaMemsetAsync(ag.ticket, 0, sizeof(int), at::cuda::getCurrentCUDAStream()));
   // the full weight as seen in this rank's slab
@@ -1103,7 +1143,7 @@ static void launch_dense(const CUtensorMap& tA, const CUtensorMap& tB, int M, in
 
 static const float* opt_f32(const c10::optional<torch::Tensor>& t, int64_t n, const char* what) {
   if (!t) return nullptr;
-  TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == n,
+  SB_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == n,
               "gemm_dense_bf16: ", what, " must be a contiguous CUDA fp32 tensor of ", n, " elements");
   return t->data_ptr<float>();
 }
@@ -1111,7 +1151,7 @@ static const float* opt_f32(const c10::optional<torch::Tensor>& t, int64_t n, co
 static __nv_bfloat16* opt_bf16_mat(const c10::optional<torch::Tensor>& t, int64_t M, int64_t N, int64_t* ld,
                                    const char* what) {
   if (!t) return nullptr;
-  TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 2 && t->size(0) == M &&
+  SB_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 2 && t->size(0) == M &&
                   t->size(1) == N && t->stride(1) == 1 && t->stride(0) % 8 == 0 &&
                   reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
               "gemm_dense_bf16: ", what, " must be bf16 [M, N] with 16-byte aligned rows");
@@ -1134,19 +1174,21 @@ void gemm_dense_bf16(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, 
                      const c10::optional<torch::Tensor>& nnz, const c10::optional<torch::Tensor>& sumsq,
                      const c10::optional<torch::Tensor>& gate_bias, const c10::optional<torch::Tensor>& mag_scale,
                      const torch::Tensor& status, int64_t max_ctas, const std::vector<int64_t>& rs_bases,
-                     int64_t rs_rank, int64_t rs_off, int64_t rs_n) {
-  TORCH_CHECK(A.is_cuda() && B.is_cuda() && A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 &&
+                     int64_t rs_rank, int64_t rs_off, int64_t rs_n, const c10::optional<torch::Tensor>& hsum,
+                     const c10::optional<torch::Tensor>& hoff, const c10::optional<torch::Tensor>& colsum2,
+                     const c10::optional<torch::Tensor>& addend, const c10::optional<torch::Tensor>& oscale) {
+  SB_CHECK(A.is_cuda() && B.is_cuda() && A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 &&
                   A.dim() == 2 && B.dim() == 2 && A.stride(1) == 1 && B.stride(1) == 1,
               "gemm_dense_bf16: A and B must be 2-D CUDA bf16 with a contiguous inner dimension");
   const int64_t M = a_mn ? A.size(1) : A.size(0), K = a_mn ? A.size(0) : A.size(1);
   const int64_t N = b_mn ? B.size(1) : B.size(0), Kb = b_mn ? B.size(0) : B.size(1);
-  TORCH_CHECK(K == Kb && K >= 1 && M >= 1 && N >= 1, "gemm_dense_bf16: inner dimensions differ (", K, " vs ", Kb, ")");
-  TORCH_CHECK(A.stride(0) % 8 == 0 && B.stride(0) % 8 == 0, "gemm_dense_bf16: row strides must be multiples of 8");
-  TORCH_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm_dense_bf16: size");
+  SB_CHECK(K == Kb && K >= 1 && M >= 1 && N >= 1, "gemm_dense_bf16: inner dimensions differ (", K, " vs ", Kb, ")");
+  SB_CHECK(A.stride(0) % 8 == 0 && B.stride(0) % 8 == 0, "gemm_dense_bf16: row strides must be multiples of 8");
+  SB_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm_dense_bf16: size");
   gemm::EpiD ed{};
   if (rs_n > 0) {
     const int64_t S = int64_t(rs_bases.size());
-    TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rs_rank >= 0 && rs_rank < S && rs_n % gemm::BM == 0 &&
+    SB_CHECK(S >= 1 && S <= p2p::kMaxRanks && rs_rank >= 0 && rs_rank < S && rs_n % gemm::BM == 0 &&
                     S * rs_n == M && rs_off % 16 == 0 && N % 8 == 0 && !out,
                 "gemm_dense_bf16: reduce-scatter mode needs M = world * rs_n, rs_n % 128 == 0, N % 8 == 0, an "
                 "aligned landing offset and no local out");
@@ -1160,11 +1202,11 @@ void gemm_dense_bf16(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, 
   ed.bias = opt_f32(bias, N, "bias");
   ed.r1_row = opt_f32(r1_row, M, "r1_row");
   ed.r1_col = opt_f32(r1_col, N, "r1_col");
-  TORCH_CHECK(!ed.r1_row == !ed.r1_col, "gemm_dense_bf16: r1_row and r1_col go together");
+  SB_CHECK(!ed.r1_row == !ed.r1_col, "gemm_dense_bf16: r1_row and r1_col go together");
   ed.thr = opt_f32(thr, N, "thr");
   ed.relu = relu ? 1 : 0;
   ed.hin = opt_bf16_mat(hin, M, N, &ed.ldh, "hin");
-  TORCH_CHECK(!ed.hin || (ed.thr && bandwidth > 0), "gemm_dense_bf16: hin needs thr and a positive bandwidth");
+  SB_CHECK(!ed.hin || (ed.thr && bandwidth > 0), "gemm_dense_bf16: hin needs thr and a positive bandwidth");
   ed.inv_bw = bandwidth > 0 ? float(1.0 / bandwidth) : 0.f;
   ed.l0c = float(l0c);
   ed.gthr = const_cast<float*>(opt_f32(gthr, N, "gthr"));
@@ -1174,20 +1216,30 @@ void gemm_dense_bf16(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, 
   ed.colsum = const_cast<float*>(opt_f32(colsum, N, "colsum"));
   ed.colcnt = const_cast<float*>(opt_f32(colcnt, N, "colcnt"));
   if (nnz) {
-    TORCH_CHECK(nnz->is_cuda() && nnz->scalar_type() == at::kLong && nnz->numel() == 1, "gemm_dense_bf16: nnz int64[1]");
+    SB_CHECK(nnz->is_cuda() && nnz->scalar_type() == at::kLong && nnz->numel() == 1, "gemm_dense_bf16: nnz int64[1]");
     ed.nnz = reinterpret_cast<unsigned long long*>(nnz->data_ptr<int64_t>());
   }
   ed.sumsq = const_cast<float*>(opt_f32(sumsq, 1, "sumsq"));
   ed.gate_bias = opt_f32(gate_bias, N, "gate_bias");
   ed.mag_scale = opt_f32(mag_scale, N, "mag_scale");
-  TORCH_CHECK(!ed.gate_bias == !ed.mag_scale, "gemm_dense_bf16: gate_bias and mag_scale go together");
+  SB_CHECK(!ed.gate_bias == !ed.mag_scale, "gemm_dense_bf16: gate_bias and mag_scale go together");
+  ed.hsum = const_cast<float*>(opt_f32(hsum, N, "hsum"));
+  ed.hoff = opt_f32(hoff, N, "hoff");
+  SB_CHECK(!ed.hsum || (ed.hoff && ed.hin), "gemm_dense_bf16: hsum needs hoff and hin");
+  ed.colsum2 = const_cast<float*>(opt_f32(colsum2, N, "colsum2"));
+  SB_CHECK(!ed.colsum2 || ed.gate_bias, "gemm_dense_bf16: colsum2 is the gated epilogue's gate sum");
+  int64_t ldad = 0;
+  ed.addend = opt_bf16_mat(addend, M, N, &ldad, "addend");
+  ed.ldad = ldad;
+  ed.oscale = opt_f32(oscale, N, "oscale");
+  SB_CHECK(!ed.oscale || ed.addend, "gemm_dense_bf16: oscale is applied with an addend");
   const auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
   CUtensorMap tA = a_mn ? make_tmap_2d(A.data_ptr(), bf, 2, K, M, A.stride(0) * 2, 64, 64, sw)
                         : make_tmap_2d(A.data_ptr(), bf, 2, M, K, A.stride(0) * 2, gemm::BM, gemm::BK, sw);
   CUtensorMap tB = b_mn ? make_tmap_2d(B.data_ptr(), bf, 2, K, N, B.stride(0) * 2, 64, 64, sw)
                         : make_tmap_2d(B.data_ptr(), bf, 2, N, K, B.stride(0) * 2, gemm::BN, gemm::BK, sw);
-  TORCH_CHECK(status.is_cuda() && status.scalar_type() == at::kInt, "gemm_dense_bf16: status");
+  SB_CHECK(status.is_cuda() && status.scalar_type() == at::kInt, "gemm_dense_bf16: status");
   const at::cuda::CUDAGuard guard(A.device());
   int* st = status.data_ptr<int>();
   const int iM = int(M), iN = int(N), iK = int(K);
@@ -1212,20 +1264,20 @@ void gemm_fsdp_dense_bf16(const torch::Tensor& A, const torch::Tensor& w_own, co
                           const c10::optional<torch::Tensor>& colcnt, const c10::optional<torch::Tensor>& nnz,
                           const torch::Tensor& status, const torch::Tensor& ticket) {
   const int64_t S = int64_t(peer_bases.size());
-  TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "gemm_fsdp_dense: bad group");
-  TORCH_CHECK(A.is_cuda() && A.scalar_type() == at::kBFloat16 && A.dim() == 2 && A.stride(1) == 1 &&
+  SB_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "gemm_fsdp_dense: bad group");
+  SB_CHECK(A.is_cuda() && A.scalar_type() == at::kBFloat16 && A.dim() == 2 && A.stride(1) == 1 &&
                   A.stride(0) % 8 == 0,
               "gemm_fsdp_dense: A must be CUDA bf16 [M, K] with 16-byte rows");
-  TORCH_CHECK(w_own.is_cuda() && w_own.scalar_type() == at::kBFloat16 && w_own.is_contiguous() &&
+  SB_CHECK(w_own.is_cuda() && w_own.scalar_type() == at::kBFloat16 && w_own.is_contiguous() &&
                   w_own.size(1) == A.size(1),
               "gemm_fsdp_dense: w_own must be contiguous bf16 [n, K]");
   const int64_t M = A.size(0), K = A.size(1), n = w_own.size(0), N = n * S;
-  TORCH_CHECK(n % gemm::BN == 0 && K % gemm::BK == 0, "gemm_fsdp_dense: shard rows % 256 and K % 64");
-  TORCH_CHECK(N / gemm::BN <= gemm::MAX_MTILES && M >= 1 && M < (1ll << 31), "gemm_fsdp_dense: size");
-  TORCH_CHECK(w_off % 16 == 0 && flag_off % 4 == 0 && w2_off % 16 == 0 && flag2_off % 4 == 0,
+  SB_CHECK(n % gemm::BN == 0 && K % gemm::BK == 0, "gemm_fsdp_dense: shard rows % 256 and K % 64");
+  SB_CHECK(N / gemm::BN <= gemm::MAX_MTILES && M >= 1 && M < (1ll << 31), "gemm_fsdp_dense: size");
+  SB_CHECK(w_off % 16 == 0 && flag_off % 4 == 0 && w2_off % 16 == 0 && flag2_off % 4 == 0,
               "gemm_fsdp_dense: slab offsets must be aligned");
   if (w2_own)
-    TORCH_CHECK(w2_own->is_cuda() && w2_own->scalar_type() == at::kBFloat16 && w2_own->is_contiguous() &&
+    SB_CHECK(w2_own->is_cuda() && w2_own->scalar_type() == at::kBFloat16 && w2_own->is_contiguous() &&
                     w2_own->sizes() == w_own.sizes(),
                 "gemm_fsdp_dense: w2_own must be contiguous bf16 like w_own");
   gemm::EpiD ed{};
@@ -1235,11 +1287,11 @@ void gemm_fsdp_dense_bf16(const torch::Tensor& A, const torch::Tensor& w_own, co
   ed.thr = opt_f32(thr, N, "thr");
   ed.colcnt = const_cast<float*>(opt_f32(colcnt, N, "colcnt"));
   if (nnz) {
-    TORCH_CHECK(nnz->is_cuda() && nnz->scalar_type() == at::kLong && nnz->numel() == 1, "gemm_fsdp_dense: nnz");
+    SB_CHECK(nnz->is_cuda() && nnz->scalar_type() == at::kLong && nnz->numel() == 1, "gemm_fsdp_dense: nnz");
     ed.nnz = reinterpret_cast<unsigned long long*>(nnz->data_ptr<int64_t>());
   }
-  TORCH_CHECK(ticket.is_cuda() && ticket.scalar_type() == at::kInt && ticket.numel() >= 1, "gemm_fsdp_dense: ticket");
-  TORCH_CHECK(status.is_cuda() && status.scalar_type() == at::kInt, "gemm_fsdp_dense: status");
+  SB_CHECK(ticket.is_cuda() && ticket.scalar_type() == at::kInt && ticket.numel() >= 1, "gemm_fsdp_dense: ticket");
+  SB_CHECK(status.is_cuda() && status.scalar_type() == at::kInt, "gemm_fsdp_dense: status");
   const at::cuda::CUDAGuard guard(A.device());
   gemm::Ag ag{};
   ag.P = p2p::make_peers(peer_bases, rank);

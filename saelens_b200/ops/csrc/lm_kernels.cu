@@ -17,6 +17,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <cuda_bf16.h>
 #include <torch/extension.h>
+#include "check.h"
 
 namespace sb {
 namespace lm {
@@ -220,12 +221,12 @@ static int lm_sm_count() {
 
 // y = rmsnorm(x) * (w or 1 + w); x [M, D] (bf16 or fp32, contiguous rows), returns a new tensor.
 torch::Tensor rmsnorm(const torch::Tensor& x, const torch::Tensor& w, double eps, bool one_plus) {
-  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.stride(1) == 1, "rmsnorm: CUDA [M, D] with contiguous rows");
-  TORCH_CHECK(x.scalar_type() == w.scalar_type() && (x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kFloat),
+  SB_CHECK(x.is_cuda() && x.dim() == 2 && x.stride(1) == 1, "rmsnorm: CUDA [M, D] with contiguous rows");
+  SB_CHECK(x.scalar_type() == w.scalar_type() && (x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kFloat),
               "rmsnorm: x and w must both be bf16 or fp32");
   const int64_t M = x.size(0), D = x.size(1);
-  TORCH_CHECK(D % 8 == 0 && w.numel() == D && w.is_contiguous(), "rmsnorm: D % 8 and w [D]");
-  TORCH_CHECK(x.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0, "rmsnorm: alignment");
+  SB_CHECK(D % 8 == 0 && w.numel() == D && w.is_contiguous(), "rmsnorm: D % 8 and w [D]");
+  SB_CHECK(x.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0, "rmsnorm: alignment");
   const at::cuda::CUDAGuard guard(x.device());
   auto y = torch::empty({M, D}, x.options());
   if (M == 0) return y;
@@ -246,13 +247,13 @@ torch::Tensor rmsnorm(const torch::Tensor& x, const torch::Tensor& w, double eps
 // y = layernorm(x) * w + b; x [M, D] (bf16 or fp32, contiguous rows), w / b [D] of x's dtype.
 torch::Tensor layernorm(const torch::Tensor& x, const torch::Tensor& w, const c10::optional<torch::Tensor>& b,
                         double eps) {
-  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.stride(1) == 1, "layernorm: CUDA [M, D] with contiguous rows");
-  TORCH_CHECK(x.scalar_type() == w.scalar_type() && (x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kFloat),
+  SB_CHECK(x.is_cuda() && x.dim() == 2 && x.stride(1) == 1, "layernorm: CUDA [M, D] with contiguous rows");
+  SB_CHECK(x.scalar_type() == w.scalar_type() && (x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kFloat),
               "layernorm: x and w must both be bf16 or fp32");
   const int64_t M = x.size(0), D = x.size(1);
-  TORCH_CHECK(D % 8 == 0 && w.numel() == D && w.is_contiguous(), "layernorm: D % 8 and w [D]");
-  if (b) TORCH_CHECK(b->scalar_type() == x.scalar_type() && b->numel() == D && b->is_contiguous(), "layernorm: b [D]");
-  TORCH_CHECK(x.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0, "layernorm: alignment");
+  SB_CHECK(D % 8 == 0 && w.numel() == D && w.is_contiguous(), "layernorm: D % 8 and w [D]");
+  if (b) SB_CHECK(b->scalar_type() == x.scalar_type() && b->numel() == D && b->is_contiguous(), "layernorm: b [D]");
+  SB_CHECK(x.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0, "layernorm: alignment");
   const at::cuda::CUDAGuard guard(x.device());
   auto y = torch::empty({M, D}, x.options());
   if (M == 0) return y;
@@ -276,17 +277,17 @@ torch::Tensor layernorm(const torch::Tensor& x, const torch::Tensor& w, const c1
 // `bad` (int32 on the device) to 1.
 torch::Tensor embed(const torch::Tensor& tokens, const torch::Tensor& table, double scale,
                     const c10::optional<torch::Tensor>& pos, const torch::Tensor& bad) {
-  TORCH_CHECK(tokens.is_cuda() && tokens.scalar_type() == at::kLong && tokens.dim() == 2 && tokens.is_contiguous(),
+  SB_CHECK(tokens.is_cuda() && tokens.scalar_type() == at::kLong && tokens.dim() == 2 && tokens.is_contiguous(),
               "embed: tokens must be contiguous CUDA int64 [B, S]");
-  TORCH_CHECK(table.dim() == 2 && table.is_contiguous() && table.size(1) % 8 == 0 &&
+  SB_CHECK(table.dim() == 2 && table.is_contiguous() && table.size(1) % 8 == 0 &&
                   (table.scalar_type() == at::kBFloat16 || table.scalar_type() == at::kFloat),
               "embed: table must be contiguous bf16/fp32 [vocab, D] with D % 8 == 0");
   const int64_t B = tokens.size(0), S = tokens.size(1), D = table.size(1);
   if (pos)
-    TORCH_CHECK(pos->scalar_type() == table.scalar_type() && pos->is_contiguous() && pos->size(1) == D &&
+    SB_CHECK(pos->scalar_type() == table.scalar_type() && pos->is_contiguous() && pos->size(1) == D &&
                     pos->size(0) >= S,
                 "embed: pos must be [>= S, D] like the table");
-  TORCH_CHECK(bad.is_cuda() && bad.scalar_type() == at::kInt && bad.numel() >= 1, "embed: bad flag");
+  SB_CHECK(bad.is_cuda() && bad.scalar_type() == at::kInt && bad.numel() >= 1, "embed: bad flag");
   const at::cuda::CUDAGuard guard(tokens.device());
   auto y = torch::empty({B, S, D}, table.options());
   if (B * S == 0) return y;
@@ -306,10 +307,10 @@ torch::Tensor embed(const torch::Tensor& tokens, const torch::Tensor& table, dou
 
 // In-place rotary embedding on x [B, S, H, d] bf16 (last dim contiguous) with tables [>= pos0+S, d/2].
 void rope_(const torch::Tensor& x, const torch::Tensor& cos, const torch::Tensor& sin, int64_t pos0) {
-  TORCH_CHECK(x.is_cuda() && x.dim() == 4 && x.stride(3) == 1 && x.scalar_type() == at::kBFloat16,
+  SB_CHECK(x.is_cuda() && x.dim() == 4 && x.stride(3) == 1 && x.scalar_type() == at::kBFloat16,
               "rope_: x must be CUDA bf16 [B, S, H, d] with a contiguous last dim");
   const int64_t B = x.size(0), S = x.size(1), H = x.size(2), d = x.size(3);
-  TORCH_CHECK(d % 2 == 0 && cos.scalar_type() == at::kFloat && sin.scalar_type() == at::kFloat &&
+  SB_CHECK(d % 2 == 0 && cos.scalar_type() == at::kFloat && sin.scalar_type() == at::kFloat &&
                   cos.is_contiguous() && sin.is_contiguous() && cos.size(-1) == d / 2 && cos.size(0) >= pos0 + S &&
                   sin.sizes() == cos.sizes(),
               "rope_: tables must be fp32 [positions, d/2]");
@@ -327,15 +328,15 @@ void rope_(const torch::Tensor& x, const torch::Tensor& cos, const torch::Tensor
 // themselves may be strided, e.g. halves of a fused gate/up projection); kind 0 = SiLU,
 // 1 = tanh-GELU.  Returns a contiguous tensor.
 torch::Tensor gated_act(const torch::Tensor& gate, const torch::Tensor& up, int64_t kind) {
-  TORCH_CHECK(gate.is_cuda() && gate.scalar_type() == at::kBFloat16 && up.scalar_type() == at::kBFloat16 &&
+  SB_CHECK(gate.is_cuda() && gate.scalar_type() == at::kBFloat16 && up.scalar_type() == at::kBFloat16 &&
                   gate.sizes() == up.sizes() && gate.dim() >= 1,
               "gated_act: bf16 CUDA tensors of equal shape");
-  TORCH_CHECK(kind == 0 || kind == 1, "gated_act: kind 0 (SiLU) or 1 (tanh-GELU)");
+  SB_CHECK(kind == 0 || kind == 1, "gated_act: kind 0 (SiLU) or 1 (tanh-GELU)");
   const int64_t width = gate.size(-1);
   const int64_t rows = width ? gate.numel() / width : 0;
   auto g2 = gate.reshape({rows, width});
   auto u2 = up.reshape({rows, width});
-  TORCH_CHECK(width % 8 == 0 && g2.stride(1) == 1 && u2.stride(1) == 1 && g2.stride(0) % 8 == 0 &&
+  SB_CHECK(width % 8 == 0 && g2.stride(1) == 1 && u2.stride(1) == 1 && g2.stride(0) % 8 == 0 &&
                   u2.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(g2.data_ptr()) % 16 == 0 &&
                   reinterpret_cast<uintptr_t>(u2.data_ptr()) % 16 == 0,
               "gated_act: rows must be contiguous, 16-byte aligned, width % 8 == 0");

@@ -25,6 +25,7 @@
 
 #include "common.cuh"
 #include "p2p.cuh"
+#include "check.h"
 
 namespace sb {
 namespace p2p {
@@ -550,17 +551,17 @@ void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64
                    const torch::Tensor& ticket, const torch::Tensor& status, int64_t sq_off, int64_t chunk,
                    int64_t max_ctas, const c10::optional<torch::Tensor>& x_out) {
   const int64_t S = int64_t(peer_bases.size());
-  TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "p2p_allreduce: bad group");
-  TORCH_CHECK(x.is_cuda() && x.is_contiguous() &&
+  SB_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "p2p_allreduce: bad group");
+  SB_CHECK(x.is_cuda() && x.is_contiguous() &&
                   (x.scalar_type() == at::kFloat || x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kInt),
               "p2p_allreduce: contiguous fp32/bf16/int32 CUDA tensor required");
-  TORCH_CHECK(x.scalar_type() != at::kInt || (scale == 1.0 && sq_off < 0),
+  SB_CHECK(x.scalar_type() != at::kInt || (scale == 1.0 && sq_off < 0),
               "p2p_allreduce: int32 sums take no scale and no sums of squares");
-  TORCH_CHECK(land_off % 16 == 0 && out_off % 16 == 0, "p2p_allreduce: offsets must be 16-byte aligned");
+  SB_CHECK(land_off % 16 == 0 && out_off % 16 == 0, "p2p_allreduce: offsets must be 16-byte aligned");
   const int64_t n = x.numel();
   if (n == 0) return;
   if (chunk <= 0) chunk = auto_chunk(n);
-  TORCH_CHECK(chunk % (8 * p2p::AR_THREADS) == 0, "p2p_allreduce: chunk must be a multiple of ", 8 * p2p::AR_THREADS);
+  SB_CHECK(chunk % (8 * p2p::AR_THREADS) == 0, "p2p_allreduce: chunk must be a multiple of ", 8 * p2p::AR_THREADS);
   const at::cuda::CUDAGuard guard(x.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   p2p::ArArgs a{};
@@ -578,7 +579,7 @@ void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64
   a.ticket = ticket.data_ptr<int>();
   a.status = status.data_ptr<int>();
   if (x_out) {
-    TORCH_CHECK(x_out->is_cuda() && x_out->is_contiguous() && x_out->scalar_type() == x.scalar_type() &&
+    SB_CHECK(x_out->is_cuda() && x_out->is_contiguous() && x_out->scalar_type() == x.scalar_type() &&
                     x_out->numel() == n,
                 "p2p_allreduce: x_out must be a contiguous tensor like x");
     a.x_out = x_out->data_ptr();
@@ -600,13 +601,13 @@ void p2p_allreduce(const torch::Tensor& x, double scale, const std::vector<int64
 // sumsq (fp32 [1], optional) accumulates the squares of the result.
 void p2p_slot_reduce(const torch::Tensor& land, double scale, const torch::Tensor& out,
                      const c10::optional<torch::Tensor>& sumsq) {
-  TORCH_CHECK(land.is_cuda() && land.scalar_type() == at::kBFloat16 && land.is_contiguous() && land.dim() == 3,
+  SB_CHECK(land.is_cuda() && land.scalar_type() == at::kBFloat16 && land.is_contiguous() && land.dim() == 3,
               "p2p_slot_reduce: land must be contiguous bf16 [S, n, D]");
-  TORCH_CHECK(out.is_contiguous() && out.scalar_type() == at::kBFloat16 && out.numel() == land.size(1) * land.size(2),
+  SB_CHECK(out.is_contiguous() && out.scalar_type() == at::kBFloat16 && out.numel() == land.size(1) * land.size(2),
               "p2p_slot_reduce: out must be contiguous bf16 [n, D]");
   const int64_t n_el = out.numel();
-  TORCH_CHECK(n_el % 8 == 0, "p2p_slot_reduce: n * D must be a multiple of 8");
-  if (sumsq) TORCH_CHECK(sumsq->scalar_type() == at::kFloat && sumsq->is_cuda(), "p2p_slot_reduce: sumsq");
+  SB_CHECK(n_el % 8 == 0, "p2p_slot_reduce: n * D must be a multiple of 8");
+  if (sumsq) SB_CHECK(sumsq->scalar_type() == at::kFloat && sumsq->is_cuda(), "p2p_slot_reduce: sumsq");
   if (n_el == 0) return;
   const at::cuda::CUDAGuard guard(land.device());
   const int64_t nvec = n_el / 8;
@@ -622,8 +623,8 @@ void p2p_slot_reduce(const torch::Tensor& land, double scale, const torch::Tenso
 // device word: the claimed slot index, or -1 when the bounded claim timed out.
 void ring_claim(const std::vector<int64_t>& peer_bases, int64_t rank, int64_t owner, int64_t state_off,
                 int64_t n_slots, int64_t from, int64_t to, int64_t start, double timeout_ms, const torch::Tensor& slot) {
-  TORCH_CHECK(slot.is_cuda() && slot.scalar_type() == at::kInt && slot.numel() >= 1, "ring_claim: slot");
-  TORCH_CHECK(n_slots >= 1 && owner >= 0 && owner < int64_t(peer_bases.size()) && state_off % 4 == 0,
+  SB_CHECK(slot.is_cuda() && slot.scalar_type() == at::kInt && slot.numel() >= 1, "ring_claim: slot");
+  SB_CHECK(n_slots >= 1 && owner >= 0 && owner < int64_t(peer_bases.size()) && state_off % 4 == 0,
               "ring_claim: ring");
   const at::cuda::CUDAGuard guard(slot.device());
   p2p::Peers P = p2p::make_peers(peer_bases, rank);
@@ -635,14 +636,14 @@ void ring_claim(const std::vector<int64_t>& peer_bases, int64_t rank, int64_t ow
 
 void ring_write(const torch::Tensor& src, const std::vector<int64_t>& peer_bases, int64_t rank, int64_t owner,
                 int64_t data_off, int64_t chunk_rows, const torch::Tensor& slot, int64_t mode, double scale) {
-  TORCH_CHECK(src.is_cuda() && src.dim() == 2 && src.stride(1) == 1 &&
+  SB_CHECK(src.is_cuda() && src.dim() == 2 && src.stride(1) == 1 &&
                   (src.scalar_type() == at::kFloat || src.scalar_type() == at::kBFloat16),
               "ring_write: src must be a CUDA fp32/bf16 matrix with contiguous rows");
   const int64_t rows = src.size(0), D = src.size(1);
-  TORCH_CHECK(rows <= chunk_rows && D % 8 == 0 && data_off % 16 == 0, "ring_write: rows <= chunk_rows, D % 8");
-  TORCH_CHECK(src.scalar_type() == at::kBFloat16 ? src.stride(0) % 8 == 0 : src.stride(0) % 4 == 0,
+  SB_CHECK(rows <= chunk_rows && D % 8 == 0 && data_off % 16 == 0, "ring_write: rows <= chunk_rows, D % 8");
+  SB_CHECK(src.scalar_type() == at::kBFloat16 ? src.stride(0) % 8 == 0 : src.stride(0) % 4 == 0,
               "ring_write: row stride alignment");
-  TORCH_CHECK(mode >= 0 && mode <= 2, "ring_write: mode");
+  SB_CHECK(mode >= 0 && mode <= 2, "ring_write: mode");
   if (rows == 0) return;
   const at::cuda::CUDAGuard guard(src.device());
   p2p::Peers P = p2p::make_peers(peer_bases, rank);
@@ -665,12 +666,12 @@ void ring_publish(const std::vector<int64_t>& peer_bases, int64_t rank, int64_t 
 
 void ring_gather(const torch::Tensor& data, const torch::Tensor& slot, const c10::optional<torch::Tensor>& perm,
                  const torch::Tensor& out) {
-  TORCH_CHECK(data.is_cuda() && data.scalar_type() == at::kBFloat16 && data.dim() == 3 && data.is_contiguous(),
+  SB_CHECK(data.is_cuda() && data.scalar_type() == at::kBFloat16 && data.dim() == 3 && data.is_contiguous(),
               "ring_gather: data must be contiguous bf16 [N, chunk_rows, D]");
-  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.dim() == 2 && out.size(1) == data.size(2) &&
+  SB_CHECK(out.scalar_type() == at::kBFloat16 && out.dim() == 2 && out.size(1) == data.size(2) &&
                   out.stride(1) == 1 && out.stride(0) % 8 == 0 && out.size(0) <= data.size(1),
               "ring_gather: out must be bf16 [rows <= chunk_rows, D] with contiguous rows");
-  if (perm) TORCH_CHECK(perm->is_cuda() && perm->scalar_type() == at::kInt && perm->numel() >= out.size(0),
+  if (perm) SB_CHECK(perm->is_cuda() && perm->scalar_type() == at::kInt && perm->numel() >= out.size(0),
                         "ring_gather: perm must be CUDA int32 [rows]");
   const int64_t rows = out.size(0);
   if (rows == 0) return;
@@ -685,7 +686,7 @@ void ring_gather(const torch::Tensor& data, const torch::Tensor& slot, const c10
 
 // Stream-ordered wait until `n` u32 epoch flags at `flags` (local memory) reach `target`.
 void p2p_wait_flags(const torch::Tensor& flags, int64_t target, const torch::Tensor& status) {
-  TORCH_CHECK(flags.is_cuda() && flags.scalar_type() == at::kInt && flags.is_contiguous(), "p2p_wait_flags");
+  SB_CHECK(flags.is_cuda() && flags.scalar_type() == at::kInt && flags.is_contiguous(), "p2p_wait_flags");
   const int64_t n = flags.numel();
   if (n == 0) return;
   const at::cuda::CUDAGuard guard(flags.device());
@@ -704,17 +705,17 @@ void p2p_route_rows(const torch::Tensor& src, const torch::Tensor& routes, const
                     int64_t rank, int64_t land_off, int64_t rows_cap, int64_t slot, int64_t cnt_off,
                     int64_t cnt_slot, int64_t free_off, const std::vector<int64_t>& free_slots, int64_t mode,
                     double scale, int64_t epoch, const torch::Tensor& status) {
-  TORCH_CHECK(src.is_cuda() && src.dim() == 2 && src.stride(1) == 1 &&
+  SB_CHECK(src.is_cuda() && src.dim() == 2 && src.stride(1) == 1 &&
                   (src.scalar_type() == at::kFloat || src.scalar_type() == at::kBFloat16),
               "p2p_route_rows: src must be a CUDA fp32/bf16 matrix with contiguous rows");
-  TORCH_CHECK(routes.device().is_cpu() && routes.scalar_type() == at::kLong && routes.dim() == 2 &&
+  SB_CHECK(routes.device().is_cpu() && routes.scalar_type() == at::kLong && routes.dim() == 2 &&
                   routes.size(1) == 4 && routes.size(0) <= p2p::RT_MAX_ROUTES,
               "p2p_route_rows: routes must be a CPU int64 [n <= 16, 4] table");
   const int64_t D = src.size(1);
-  TORCH_CHECK(D % 8 == 0 && D <= p2p::RT_U * 8 * p2p::RT_THREADS,
+  SB_CHECK(D % 8 == 0 && D <= p2p::RT_U * 8 * p2p::RT_THREADS,
               "p2p_route_rows: d must be a multiple of 8 and <= 8192");
-  TORCH_CHECK(mode >= 0 && mode <= 2, "p2p_route_rows: mode");
-  TORCH_CHECK(int64_t(free_slots.size()) == routes.size(0), "p2p_route_rows: free_slots");
+  SB_CHECK(mode >= 0 && mode <= 2, "p2p_route_rows: mode");
+  SB_CHECK(int64_t(free_slots.size()) == routes.size(0), "p2p_route_rows: free_slots");
   const at::cuda::CUDAGuard guard(src.device());
   p2p::RouteArgs a{};
   a.src = src.data_ptr();
@@ -729,7 +730,7 @@ void p2p_route_rows(const torch::Tensor& src, const torch::Tensor& routes, const
     a.r_rows[i] = int(R[i][1]);
     a.r_rank[i] = int(R[i][2]);
     a.r_dst[i] = int(R[i][3]);
-    TORCH_CHECK(R[i][0] >= 0 && R[i][0] + R[i][1] <= src.size(0) && R[i][3] >= 0 && R[i][3] + R[i][1] <= rows_cap &&
+    SB_CHECK(R[i][0] >= 0 && R[i][0] + R[i][1] <= src.size(0) && R[i][3] >= 0 && R[i][3] + R[i][1] <= rows_cap &&
                     R[i][2] >= 0 && R[i][2] < int64_t(peer_bases.size()),
                 "p2p_route_rows: route ", i, " out of range");
     a.r_chunk0[i] = chunks;
@@ -756,7 +757,7 @@ void p2p_route_rows(const torch::Tensor& src, const torch::Tensor& routes, const
 
 // Wait (bounded, stream-ordered) until counters[i] >= targets[i] (targets: CUDA int64).
 void p2p_wait_targets(const torch::Tensor& counters, const torch::Tensor& targets, const torch::Tensor& status) {
-  TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && targets.is_cuda() &&
+  SB_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && targets.is_cuda() &&
                   targets.scalar_type() == at::kLong && targets.numel() <= counters.numel(),
               "p2p_wait_targets");
   const at::cuda::CUDAGuard guard(counters.device());

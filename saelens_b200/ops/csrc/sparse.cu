@@ -23,6 +23,7 @@
 
 #include "common.cuh"
 #include "p2p.cuh"
+#include "check.h"
 
 namespace sb {
 namespace sparse {
@@ -1108,7 +1109,7 @@ static inline int pick_vpt(int64_t D, int threads) {
   if (need <= 1) return 1;
   if (need <= 2) return 2;
   if (need <= 4) return 4;
-  TORCH_CHECK(need <= 8, "d_in too large for the sparse kernels (max 8192)");
+  SB_CHECK(need <= 8, "d_in too large for the sparse kernels (max 8192)");
   return 8;
 }
 
@@ -1126,18 +1127,18 @@ void decode_mse(const torch::Tensor& vals, const torch::Tensor& idx, bool relu,
                 const c10::optional<torch::Tensor>& dxhat, const c10::optional<torch::Tensor>& grad_coef_dev,
                 double grad_coef, const c10::optional<torch::Tensor>& loss_row,
                 const c10::optional<torch::Tensor>& bsum) {
-  TORCH_CHECK(vals.scalar_type() == at::kFloat && idx.scalar_type() == at::kInt && vals.dim() == 2 &&
+  SB_CHECK(vals.scalar_type() == at::kFloat && idx.scalar_type() == at::kInt && vals.dim() == 2 &&
                   vals.sizes() == idx.sizes() && vals.is_contiguous() && idx.is_contiguous(),
               "decode_mse: vals fp32 / idx int32 [M, k]");
-  TORCH_CHECK(W.scalar_type() == at::kBFloat16 && W.dim() == 2 && W.stride(1) == 1, "decode_mse: W");
+  SB_CHECK(W.scalar_type() == at::kBFloat16 && W.dim() == 2 && W.stride(1) == 1, "decode_mse: W");
   const int64_t M = vals.size(0), k = vals.size(1), D = W.size(1);
-  TORCH_CHECK(D % 8 == 0 && W.stride(0) % 8 == 0, "decode_mse: d_in must be a multiple of 8");
-  TORCH_CHECK(target.scalar_type() == at::kBFloat16 && target.size(0) == M && target.size(1) == D &&
+  SB_CHECK(D % 8 == 0 && W.stride(0) % 8 == 0, "decode_mse: d_in must be a multiple of 8");
+  SB_CHECK(target.scalar_type() == at::kBFloat16 && target.size(0) == M && target.size(1) == D &&
                   target.stride(1) == 1 && target.stride(0) % 8 == 0,
               "decode_mse: target bf16 [M, D]");
   auto chk_out = [&](const c10::optional<torch::Tensor>& o, const char* name) -> __nv_bfloat16* {
     if (!o) return nullptr;
-    TORCH_CHECK(o->scalar_type() == at::kBFloat16 && o->size(0) == M && o->size(1) == D &&
+    SB_CHECK(o->scalar_type() == at::kBFloat16 && o->size(0) == M && o->size(1) == D &&
                     o->stride(1) == 1 && o->stride(0) % 8 == 0,
                 "decode_mse: bad ", name);
     return reinterpret_cast<__nv_bfloat16*>(o->data_ptr());
@@ -1147,12 +1148,12 @@ void decode_mse(const torch::Tensor& vals, const torch::Tensor& idx, bool relu,
   __nv_bfloat16* pd = chk_out(dxhat, "dxhat");
   const float* pinv = nullptr;
   if (inv_scale) {
-    TORCH_CHECK(inv_scale->scalar_type() == at::kFloat && inv_scale->numel() == W.size(0), "decode_mse: inv_scale");
+    SB_CHECK(inv_scale->scalar_type() == at::kFloat && inv_scale->numel() == W.size(0), "decode_mse: inv_scale");
     pinv = inv_scale->data_ptr<float>();
   }
   const float* pb = nullptr;
   if (bias) {
-    TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->numel() == D, "decode_mse: bias");
+    SB_CHECK(bias->scalar_type() == at::kFloat && bias->numel() == D, "decode_mse: bias");
     pb = bias->data_ptr<float>();
   }
   const float* pgc = nullptr;
@@ -1208,7 +1209,7 @@ void csc_fill(const torch::Tensor& vals, const torch::Tensor& idx,
   const int64_t n_aux = aux_vals ? aux_vals->numel() : 0;
   const int64_t total = n_main + n_aux;
   if (total == 0) return;
-  TORCH_CHECK(colptr.scalar_type() == at::kLong && pairs.scalar_type() == at::kLong &&
+  SB_CHECK(colptr.scalar_type() == at::kLong && pairs.scalar_type() == at::kLong &&
                   cursor.scalar_type() == at::kInt,
               "csc_fill: dtypes");
   const int64_t grid = std::min<int64_t>((total + 255) / 256, int64_t(sm_count()) * 16);
@@ -1231,12 +1232,12 @@ static void latent_grad_v1(const torch::Tensor& colptr, const torch::Tensor& pai
                  const c10::optional<torch::Tensor>& since_fired) {
   const at::cuda::CUDAGuard guard(vals.device());
   const int64_t N = W_dec.size(0), D = W_dec.size(1);
-  TORCH_CHECK(W_dec.is_contiguous() && W_enc.is_contiguous() && gW_dec.is_contiguous() &&
+  SB_CHECK(W_dec.is_contiguous() && W_enc.is_contiguous() && gW_dec.is_contiguous() &&
                   gW_enc.is_contiguous() && W_enc.size(0) == N && W_enc.size(1) == D,
               "latent_grad: weights must be contiguous [N, D]");
-  TORCH_CHECK(dxhat.is_contiguous() && dxhat.size(1) == D && x.stride(1) == 1 && x.stride(0) % 8 == 0,
+  SB_CHECK(dxhat.is_contiguous() && dxhat.size(1) == D && x.stride(1) == 1 && x.stride(0) % 8 == 0,
               "latent_grad: dxhat / x layout");
-  TORCH_CHECK(D % 8 == 0, "latent_grad: d_in must be a multiple of 8");
+  SB_CHECK(D % 8 == 0, "latent_grad: d_in must be a multiple of 8");
   sparse::LatentGradArgs a{};
   a.colptr = colptr.data_ptr<int64_t>();
   a.pairs = pairs.data_ptr<int64_t>();
@@ -1305,14 +1306,14 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
   }
   const at::cuda::CUDAGuard guard(vals.device());
   const int64_t N = W_dec.size(0), D = W_dec.size(1);
-  TORCH_CHECK(W_dec.is_contiguous() && W_enc.is_contiguous() && gW_dec.is_contiguous() &&
+  SB_CHECK(W_dec.is_contiguous() && W_enc.is_contiguous() && gW_dec.is_contiguous() &&
                   gW_enc.is_contiguous() && W_enc.size(0) == N && W_enc.size(1) == D,
               "latent_grad: weights must be contiguous [N, D]");
-  TORCH_CHECK(dxhat.is_contiguous() && dxhat.size(1) == D && x.stride(1) == 1 && x.stride(0) % 8 == 0,
+  SB_CHECK(dxhat.is_contiguous() && dxhat.size(1) == D && x.stride(1) == 1 && x.stride(0) % 8 == 0,
               "latent_grad: dxhat / x layout");
-  TORCH_CHECK(D % 8 == 0 && D <= 8192, "latent_grad: d_in must be a multiple of 8 and at most 8192");
-  TORCH_CHECK(idx.is_contiguous() && idx.scalar_type() == at::kInt && idx.sizes() == vals.sizes(), "latent_grad: idx");
-  TORCH_CHECK(x.size(0) < (int64_t(1) << 31), "latent_grad: too many rows");
+  SB_CHECK(D % 8 == 0 && D <= 8192, "latent_grad: d_in must be a multiple of 8 and at most 8192");
+  SB_CHECK(idx.is_contiguous() && idx.scalar_type() == at::kInt && idx.sizes() == vals.sizes(), "latent_grad: idx");
+  SB_CHECK(x.size(0) < (int64_t(1) << 31), "latent_grad: too many rows");
   if (N == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
   const int64_t P = pairs.numel();
@@ -1323,8 +1324,8 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
   if (P > 0) {
     sparse::PairDzArgs pa{};
     pa.pairs = pairs.data_ptr<int64_t>();
-    TORCH_CHECK(colptr.numel() == N + 1 && colptr.scalar_type() == at::kLong, "latent_grad: colptr");
-    TORCH_CHECK(j0 >= 0 && j0 <= j1 && j1 <= N, "latent_grad: latent range");
+    SB_CHECK(colptr.numel() == N + 1 && colptr.scalar_type() == at::kLong, "latent_grad: colptr");
+    SB_CHECK(j0 >= 0 && j0 <= j1 && j1 <= N, "latent_grad: latent range");
     pa.pos_begin = colptr.data_ptr<int64_t>() + j0;
     pa.pos_end = colptr.data_ptr<int64_t>() + j1;
     pa.P = P;
@@ -1344,7 +1345,7 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
     pa.pcoef = pcoef.data_ptr<float>();
     pa.pdz = pdz.data_ptr<float>();
     if (jr_thr) {
-      TORCH_CHECK(jr_pre && jr_gthr && jr_pre->sizes() == vals.sizes() && jr_thr->numel() == N &&
+      SB_CHECK(jr_pre && jr_gthr && jr_pre->sizes() == vals.sizes() && jr_thr->numel() == N &&
                       jr_gthr->numel() == N && jr_bandwidth > 0,
                   "latent_grad: JumpReLU mode needs jr_pre [M, k], jr_thr [N], jr_gthr [N], bandwidth > 0");
       pa.jr_thr = jr_thr->data_ptr<float>();
@@ -1367,7 +1368,7 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
   }();
   int ns = 1;
   while (ns < max_ns && ns * 64 < nvec) ns *= 2;
-  TORCH_CHECK((nvec + 32 * ns - 1) / (32 * ns) <= 4, "latent_grad: d_in too wide for ", ns, " slices");
+  SB_CHECK((nvec + 32 * ns - 1) / (32 * ns) <= 4, "latent_grad: d_in too wide for ", ns, " slices");
   const int vpl = (nvec + 32 * ns - 1) / (32 * ns);
   const int sw = 32 * vpl * 8;
   const int grid = sm_count() * 2;
@@ -1400,7 +1401,7 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
   a.j1 = int(j1);
   a.zero_empty = zero_empty ? 1 : 0;
   if (rs_n > 0) {
-    TORCH_CHECK(zero_empty && int64_t(rs_bases.size()) * rs_n == N && rs_dec_off % 16 == 0 && rs_enc_off % 16 == 0,
+    SB_CHECK(zero_empty && int64_t(rs_bases.size()) * rs_n == N && rs_dec_off % 16 == 0 && rs_enc_off % 16 == 0,
                 "latent_grad: reduce-scatter destination needs zero_empty, S * rs_n == N and aligned offsets");
     a.P = p2p::make_peers(rs_bases, rs_rank);
     a.rs_dec_off = rs_dec_off;
@@ -1415,7 +1416,7 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   if (bterm) {
-    TORCH_CHECK(bterm->numel() == D && bterm->scalar_type() == at::kFloat, "latent_grad: bterm");
+    SB_CHECK(bterm->numel() == D && bterm->scalar_type() == at::kFloat, "latent_grad: bterm");
     sparse::col_reduce_kernel<<<dim3(int((D + 31) / 32)), dim3(32, sparse::CR_ROWS), 0, stream>>>(
         bpart.data_ptr<float>(), tw, ns, sw, int(D), bterm->data_ptr<float>());
     C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -1424,11 +1425,11 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
 
 void decode_partial(const torch::Tensor& vals, const torch::Tensor& idx, bool relu,
                     const c10::optional<torch::Tensor>& inv_scale, const torch::Tensor& W, const torch::Tensor& out) {
-  TORCH_CHECK(vals.is_contiguous() && idx.is_contiguous() && vals.scalar_type() == at::kFloat &&
+  SB_CHECK(vals.is_contiguous() && idx.is_contiguous() && vals.scalar_type() == at::kFloat &&
                   idx.scalar_type() == at::kInt, "decode_partial: vals/idx");
-  TORCH_CHECK(out.scalar_type() == at::kFloat && out.is_contiguous() && out.size(1) == W.size(1), "decode_partial: out");
+  SB_CHECK(out.scalar_type() == at::kFloat && out.is_contiguous() && out.size(1) == W.size(1), "decode_partial: out");
   const int64_t M = vals.size(0), k = vals.size(1), D = W.size(1);
-  TORCH_CHECK(D % 8 == 0 && W.stride(1) == 1, "decode_partial: W");
+  SB_CHECK(D % 8 == 0 && W.stride(1) == 1, "decode_partial: W");
   if (M == 0) return;
   const at::cuda::CUDAGuard guard(vals.device());
   const int vpt = pick_vpt(D, sparse::DEC_THREADS);
@@ -1454,11 +1455,11 @@ void finish_mse(const torch::Tensor& xsum, const c10::optional<torch::Tensor>& b
                 const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& resid,
                 const c10::optional<torch::Tensor>& dxhat, const c10::optional<torch::Tensor>& grad_coef_dev,
                 double grad_coef, const torch::Tensor& loss_row, const c10::optional<torch::Tensor>& bsum) {
-  TORCH_CHECK(xsum.scalar_type() == at::kFloat && xsum.stride(1) == 1 && xsum.stride(0) % 8 == 0, "finish_mse: xsum");
+  SB_CHECK(xsum.scalar_type() == at::kFloat && xsum.stride(1) == 1 && xsum.stride(0) % 8 == 0, "finish_mse: xsum");
   const int64_t M = xsum.size(0), D = xsum.size(1);
-  TORCH_CHECK(target.size(0) == M && target.size(1) == D && target.stride(1) == 1, "finish_mse: target");
+  SB_CHECK(target.size(0) == M && target.size(1) == D && target.stride(1) == 1, "finish_mse: target");
   for (const auto* o : {&out, &resid, &dxhat})
-    if (*o) TORCH_CHECK((*o)->is_contiguous() && (*o)->size(0) == M && (*o)->size(1) == D, "finish_mse: outputs");
+    if (*o) SB_CHECK((*o)->is_contiguous() && (*o)->size(0) == M && (*o)->size(1) == D, "finish_mse: outputs");
   if (M == 0) return;
   const at::cuda::CUDAGuard guard(xsum.device());
   const int64_t grid = std::min<int64_t>(M, int64_t(sm_count()) * 8);
@@ -1486,24 +1487,24 @@ void decode_rs(const torch::Tensor& vals, const torch::Tensor& idx, bool relu,
                double grad_coef, const torch::Tensor& loss_row, const c10::optional<torch::Tensor>& bsum,
                const torch::Tensor& ticket, const torch::Tensor& status) {
   const int64_t S = int64_t(peer_bases.size());
-  TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "decode_rs: bad group");
-  TORCH_CHECK(vals.is_contiguous() && idx.is_contiguous() && vals.scalar_type() == at::kFloat &&
+  SB_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "decode_rs: bad group");
+  SB_CHECK(vals.is_contiguous() && idx.is_contiguous() && vals.scalar_type() == at::kFloat &&
                   idx.scalar_type() == at::kInt && vals.sizes() == idx.sizes(),
               "decode_rs: vals/idx");
   const int64_t B = vals.size(0), k = vals.size(1), D = W.size(1);
-  TORCH_CHECK(W.scalar_type() == at::kBFloat16 && W.stride(1) == 1 && D % 8 == 0 && D <= 8 * 8 * sparse::DEC_THREADS,
+  SB_CHECK(W.scalar_type() == at::kBFloat16 && W.stride(1) == 1 && D % 8 == 0 && D <= 8 * 8 * sparse::DEC_THREADS,
               "decode_rs: W");
-  TORCH_CHECK(B % (S * sparse::RS_RB) == 0, "decode_rs: batch must be a multiple of 16 * world");
+  SB_CHECK(B % (S * sparse::RS_RB) == 0, "decode_rs: batch must be a multiple of 16 * world");
   const int64_t Bo = B / S;
-  TORCH_CHECK(target.scalar_type() == at::kBFloat16 && target.size(0) == Bo && target.size(1) == D &&
+  SB_CHECK(target.scalar_type() == at::kBFloat16 && target.size(0) == Bo && target.size(1) == D &&
                   target.stride(1) == 1,
               "decode_rs: target");
   for (const auto* o : {&out, &resid})
-    if (*o) TORCH_CHECK((*o)->is_contiguous() && (*o)->size(0) == Bo && (*o)->size(1) == D, "decode_rs: outputs");
-  TORCH_CHECK(loss_row.numel() == Bo && loss_row.scalar_type() == at::kFloat, "decode_rs: loss_row");
-  if (bias) TORCH_CHECK(bias->numel() == D && bias->scalar_type() == at::kFloat, "decode_rs: bias");
-  if (bsum) TORCH_CHECK(bsum->numel() == D && bsum->scalar_type() == at::kFloat, "decode_rs: bsum");
-  TORCH_CHECK(land_off % 16 == 0 && (dx_off < 0 || dx_off % 16 == 0), "decode_rs: offsets");
+    if (*o) SB_CHECK((*o)->is_contiguous() && (*o)->size(0) == Bo && (*o)->size(1) == D, "decode_rs: outputs");
+  SB_CHECK(loss_row.numel() == Bo && loss_row.scalar_type() == at::kFloat, "decode_rs: loss_row");
+  if (bias) SB_CHECK(bias->numel() == D && bias->scalar_type() == at::kFloat, "decode_rs: bias");
+  if (bsum) SB_CHECK(bsum->numel() == D && bsum->scalar_type() == at::kFloat, "decode_rs: bsum");
+  SB_CHECK(land_off % 16 == 0 && (dx_off < 0 || dx_off % 16 == 0), "decode_rs: offsets");
   const at::cuda::CUDAGuard guard(vals.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   sparse::DecodeRsArgs a{};

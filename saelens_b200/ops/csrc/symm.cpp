@@ -7,13 +7,14 @@
 #include <torch/extension.h>
 
 #include <cstring>
+#include "check.h"
 
 namespace sb {
 
 // Allocates `nbytes` of zeroed device memory on the current device.  Returns (address, handle)
 // where handle is a CPU uint8 tensor holding the cudaIpcMemHandle_t.
 std::tuple<int64_t, torch::Tensor> symm_alloc(int64_t nbytes) {
-  TORCH_CHECK(nbytes > 0, "symm_alloc: size must be positive");
+  SB_CHECK(nbytes > 0, "symm_alloc: size must be positive");
   void* p = nullptr;
   C10_CUDA_CHECK(cudaMalloc(&p, size_t(nbytes)));
   C10_CUDA_CHECK(cudaMemset(p, 0, size_t(nbytes)));
@@ -27,7 +28,7 @@ std::tuple<int64_t, torch::Tensor> symm_alloc(int64_t nbytes) {
 
 // Maps a peer's slab into this process (peer access is enabled lazily by the driver).
 int64_t symm_open(const torch::Tensor& handle) {
-  TORCH_CHECK(handle.numel() == int64_t(sizeof(cudaIpcMemHandle_t)) && handle.scalar_type() == torch::kUInt8,
+  SB_CHECK(handle.numel() == int64_t(sizeof(cudaIpcMemHandle_t)) && handle.scalar_type() == torch::kUInt8,
               "symm_open: expected a 64-byte uint8 handle");
   cudaIpcMemHandle_t h;
   std::memcpy(&h, handle.contiguous().data_ptr(), sizeof(h));

@@ -5,6 +5,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include "check.h"
 
 namespace sb {
 
@@ -14,7 +15,7 @@ inline PFN_cuTensorMapEncodeTiled_v12000 get_encode_tiled() {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
-    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p != nullptr,
+    SB_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p != nullptr,
                 "cuTensorMapEncodeTiled entry point not available");
     fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
   }
@@ -27,9 +28,9 @@ inline CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dtype, int
                                 uint64_t rows, uint64_t cols, uint64_t row_stride_bytes,
                                 uint32_t box_rows, uint32_t box_cols,
                                 CUtensorMapSwizzle swizzle) {
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
-  TORCH_CHECK(row_stride_bytes % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
-  TORCH_CHECK((uint64_t(box_cols) * elem_bytes) % 16 == 0, "TMA box inner extent");
+  SB_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+  SB_CHECK(row_stride_bytes % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  SB_CHECK((uint64_t(box_cols) * elem_bytes) % 16 == 0, "TMA box inner extent");
   CUtensorMap m;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {row_stride_bytes};
@@ -39,7 +40,7 @@ inline CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dtype, int
                                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", int(r));
+  SB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", int(r));
   return m;
 }
 
@@ -48,9 +49,9 @@ inline CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dtype, int
 inline CUtensorMap make_tmap_3d(const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t d0,
                                 uint64_t d1, uint64_t d2, uint64_t s1_bytes, uint64_t s2_bytes, uint32_t b0,
                                 uint32_t b1, uint32_t b2, CUtensorMapSwizzle swizzle) {
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
-  TORCH_CHECK(s1_bytes % 16 == 0 && s2_bytes % 16 == 0, "TMA strides must be multiples of 16 bytes");
-  TORCH_CHECK((uint64_t(b0) * elem_bytes) % 16 == 0, "TMA box inner extent");
+  SB_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+  SB_CHECK(s1_bytes % 16 == 0 && s2_bytes % 16 == 0, "TMA strides must be multiples of 16 bytes");
+  SB_CHECK((uint64_t(b0) * elem_bytes) % 16 == 0, "TMA box inner extent");
   CUtensorMap m;
   cuuint64_t dims[3] = {d0, d1, d2};
   cuuint64_t strides[2] = {s1_bytes, s2_bytes};
@@ -59,7 +60,7 @@ inline CUtensorMap make_tmap_3d(const void* base, CUtensorMapDataType dtype, int
   CUresult r = get_encode_tiled()(&m, dtype, 3, const_cast<void*>(base), dims, strides, box, estr,
                                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (3-D) failed with code ", int(r));
+  SB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (3-D) failed with code ", int(r));
   return m;
 }
 

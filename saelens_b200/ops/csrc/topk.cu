@@ -25,6 +25,7 @@
 
 #include "common.cuh"
 #include "p2p.cuh"
+#include "check.h"
 
 namespace sb {
 namespace topk {
@@ -687,16 +688,16 @@ __global__ void __launch_bounds__(THREADS)
 void topk_merge(const torch::Tensor& cand_val, const torch::Tensor& cand_idx, int64_t n_local, int64_t rank,
                 const c10::optional<torch::Tensor>& k_dev, const torch::Tensor& out_val,
                 const torch::Tensor& out_idx) {
-  TORCH_CHECK(cand_val.dim() == 3 && cand_val.sizes() == cand_idx.sizes() && cand_val.is_contiguous() &&
+  SB_CHECK(cand_val.dim() == 3 && cand_val.sizes() == cand_idx.sizes() && cand_val.is_contiguous() &&
                   cand_idx.is_contiguous() && cand_val.scalar_type() == at::kFloat &&
                   cand_idx.scalar_type() == at::kInt,
               "topk_merge: candidates must be contiguous fp32/int32 [S, M, k]");
   const int64_t S = cand_val.size(0), M = cand_val.size(1), k = cand_val.size(2);
-  TORCH_CHECK(out_val.size(0) == M && out_val.size(1) == k && out_idx.is_contiguous(), "topk_merge: outputs");
+  SB_CHECK(out_val.size(0) == M && out_val.size(1) == k && out_idx.is_contiguous(), "topk_merge: outputs");
   if (M == 0) return;
   const at::cuda::CUDAGuard guard(cand_val.device());
   const size_t smem = ((size_t(S * k) * 4 + 15) & ~size_t(15)) + size_t(S * k) * 8;
-  TORCH_CHECK(smem <= 227 * 1024, "topk_merge: S*k too large for one CTA");
+  SB_CHECK(smem <= 227 * 1024, "topk_merge: S*k too large for one CTA");
   C10_CUDA_CHECK(cudaFuncSetAttribute(topk::topk_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       int(smem)));
   topk::topk_merge_kernel<<<dim3(M), dim3(topk::THREADS), smem, at::cuda::getCurrentCUDAStream()>>>(
@@ -712,31 +713,31 @@ void row_topk(const torch::Tensor& H, const torch::Tensor& cmax, int64_t k_max,
               const c10::optional<torch::Tensor>& k_dev, const c10::optional<torch::Tensor>& mask,
               const torch::Tensor& out_val, const torch::Tensor& out_idx, const torch::Tensor& status,
               const c10::optional<torch::Tensor>& tmax) {
-  TORCH_CHECK(H.is_cuda() && H.scalar_type() == at::kBFloat16 && H.dim() == 2 && H.stride(1) == 1,
+  SB_CHECK(H.is_cuda() && H.scalar_type() == at::kBFloat16 && H.dim() == 2 && H.stride(1) == 1,
               "row_topk: H must be a CUDA bf16 matrix with contiguous rows");
   const int64_t M = H.size(0), N = H.size(1);
-  TORCH_CHECK(N % 32 == 0 && N / 32 <= topk::MAX_NC, "row_topk: N must be a multiple of 32 and <= 2^20");
-  TORCH_CHECK(cmax.scalar_type() == at::kBFloat16 && cmax.size(0) == M && cmax.size(1) == N / 32 &&
+  SB_CHECK(N % 32 == 0 && N / 32 <= topk::MAX_NC, "row_topk: N must be a multiple of 32 and <= 2^20");
+  SB_CHECK(cmax.scalar_type() == at::kBFloat16 && cmax.size(0) == M && cmax.size(1) == N / 32 &&
                   cmax.stride(1) == 1,
               "row_topk: bad cmax");
-  TORCH_CHECK(k_max >= 1 && k_max <= N, "row_topk: k out of range");
-  TORCH_CHECK(out_val.scalar_type() == at::kFloat && out_idx.scalar_type() == at::kInt &&
+  SB_CHECK(k_max >= 1 && k_max <= N, "row_topk: k out of range");
+  SB_CHECK(out_val.scalar_type() == at::kFloat && out_idx.scalar_type() == at::kInt &&
                   out_val.size(0) == M && out_val.size(1) == k_max && out_idx.size(0) == M &&
                   out_idx.size(1) == k_max && out_val.is_contiguous() && out_idx.is_contiguous(),
               "row_topk: bad outputs");
   const int* kd = nullptr;
   if (k_dev) {
-    TORCH_CHECK(k_dev->scalar_type() == at::kInt && k_dev->numel() == 1, "row_topk: k_dev");
+    SB_CHECK(k_dev->scalar_type() == at::kInt && k_dev->numel() == 1, "row_topk: k_dev");
     kd = k_dev->data_ptr<int>();
   }
   const uint32_t* mk = nullptr;
   if (mask) {
-    TORCH_CHECK(mask->scalar_type() == at::kInt && mask->numel() == N / 32 && mask->is_contiguous(),
+    SB_CHECK(mask->scalar_type() == at::kInt && mask->numel() == N / 32 && mask->is_contiguous(),
                 "row_topk: mask must be int32 [N/32]");
     mk = reinterpret_cast<const uint32_t*>(mask->data_ptr<int>());
   }
   if (tmax) {
-    TORCH_CHECK(N % 256 == 0 && tmax->scalar_type() == at::kBFloat16 && tmax->size(0) == M &&
+    SB_CHECK(N % 256 == 0 && tmax->scalar_type() == at::kBFloat16 && tmax->size(0) == M &&
                     tmax->size(1) == N / 256 && tmax->stride(1) == 1,
                 "row_topk: tmax must be bf16 [M, N/256]");
   }
@@ -768,15 +769,15 @@ void topk_exchange_merge(const torch::Tensor& vals, const torch::Tensor& idx, in
                          int64_t rank, int64_t cv_off, int64_t ci_off, int64_t cnt_off, int64_t epoch,
                          const torch::Tensor& ticket, const torch::Tensor& status) {
   const int64_t S = int64_t(peer_bases.size());
-  TORCH_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "topk_exchange_merge: bad group");
-  TORCH_CHECK(vals.is_contiguous() && idx.is_contiguous() && vals.scalar_type() == at::kFloat &&
+  SB_CHECK(S >= 1 && S <= p2p::kMaxRanks && rank >= 0 && rank < S, "topk_exchange_merge: bad group");
+  SB_CHECK(vals.is_contiguous() && idx.is_contiguous() && vals.scalar_type() == at::kFloat &&
                   idx.scalar_type() == at::kInt && vals.sizes() == idx.sizes(),
               "topk_exchange_merge: vals/idx");
   const int64_t B = vals.size(0), k = vals.size(1);
-  TORCH_CHECK(B % topk::XM_RB == 0, "topk_exchange_merge: batch must be a multiple of 16");
-  TORCH_CHECK(cv_off % 16 == 0 && ci_off % 16 == 0, "topk_exchange_merge: offsets");
+  SB_CHECK(B % topk::XM_RB == 0, "topk_exchange_merge: batch must be a multiple of 16");
+  SB_CHECK(cv_off % 16 == 0 && ci_off % 16 == 0, "topk_exchange_merge: offsets");
   const size_t smem = ((size_t(S * k) * 4 + 15) & ~size_t(15)) + size_t(S * k) * 8;
-  TORCH_CHECK(smem <= 200 * 1024, "topk_exchange_merge: S*k too large for one CTA");
+  SB_CHECK(smem <= 200 * 1024, "topk_exchange_merge: S*k too large for one CTA");
   const at::cuda::CUDAGuard guard(vals.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   topk::XMergeArgs a{};
@@ -808,10 +809,10 @@ void topk_exchange_merge(const torch::Tensor& vals, const torch::Tensor& idx, in
 }
 
 static void check_cands(const torch::Tensor& vals, const torch::Tensor& idx, const char* what) {
-  TORCH_CHECK(vals.is_cuda() && vals.is_contiguous() && idx.is_contiguous() && vals.scalar_type() == at::kFloat &&
+  SB_CHECK(vals.is_cuda() && vals.is_contiguous() && idx.is_contiguous() && vals.scalar_type() == at::kFloat &&
                   idx.scalar_type() == at::kInt && vals.sizes() == idx.sizes() && vals.dim() == 2,
               what, ": vals/idx must be contiguous fp32/int32 [M, kc]");
-  TORCH_CHECK(vals.size(1) <= 1024, what, ": at most 1024 candidates per row");
+  SB_CHECK(vals.size(1) <= 1024, what, ": at most 1024 candidates per row");
 }
 
 static int sm_count_here() {
@@ -824,7 +825,7 @@ static int sm_count_here() {
 // 65536-bin histogram (int32, zeroed here) of the positive candidates' bf16 keys.
 void batch_hist(const torch::Tensor& vals, const torch::Tensor& idx, const torch::Tensor& hist) {
   check_cands(vals, idx, "batch_hist");
-  TORCH_CHECK(hist.is_cuda() && hist.is_contiguous() && hist.scalar_type() == at::kInt && hist.numel() == 65536,
+  SB_CHECK(hist.is_cuda() && hist.is_contiguous() && hist.scalar_type() == at::kInt && hist.numel() == 65536,
               "batch_hist: hist must be int32 [65536]");
   const at::cuda::CUDAGuard guard(vals.device());
   auto stream = at::cuda::getCurrentCUDAStream();
@@ -840,7 +841,7 @@ void batch_hist(const torch::Tensor& vals, const torch::Tensor& idx, const torch
 // Threshold of the K largest from a (possibly group-summed) histogram; sel int32 [4] (see
 // batch_thresh_kernel).
 void batch_thresh(const torch::Tensor& hist, int64_t K, const torch::Tensor& sel) {
-  TORCH_CHECK(hist.is_cuda() && hist.is_contiguous() && hist.scalar_type() == at::kInt && hist.numel() == 65536 &&
+  SB_CHECK(hist.is_cuda() && hist.is_contiguous() && hist.scalar_type() == at::kInt && hist.numel() == 65536 &&
                   sel.is_cuda() && sel.scalar_type() == at::kInt && sel.numel() >= 4,
               "batch_thresh: hist int32 [65536], sel int32 [4]");
   const at::cuda::CUDAGuard guard(hist.device());
@@ -854,7 +855,7 @@ void batch_ties(const torch::Tensor& vals, const torch::Tensor& idx, const torch
                 const torch::Tensor& ties) {
   check_cands(vals, idx, "batch_ties");
   const int64_t M = vals.size(0), kc = vals.size(1);
-  TORCH_CHECK(ties.is_cuda() && ties.is_contiguous() && ties.scalar_type() == at::kInt && ties.numel() == M,
+  SB_CHECK(ties.is_cuda() && ties.is_contiguous() && ties.scalar_type() == at::kInt && ties.numel() == M,
               "batch_ties: ties must be int32 [M]");
   if (M == 0) return;
   const at::cuda::CUDAGuard guard(vals.device());
@@ -871,10 +872,10 @@ void batch_filter(const torch::Tensor& vals, const torch::Tensor& idx, const tor
                   const c10::optional<torch::Tensor>& truncated) {
   check_cands(vals, idx, "batch_filter");
   const int64_t M = vals.size(0), kc = vals.size(1);
-  TORCH_CHECK(ties_all.is_cuda() && ties_all.is_contiguous() && ties_all.scalar_type() == at::kInt &&
+  SB_CHECK(ties_all.is_cuda() && ties_all.is_contiguous() && ties_all.scalar_type() == at::kInt &&
                   ties_all.dim() == 2 && ties_all.size(1) == M && rank >= 0 && rank < ties_all.size(0),
               "batch_filter: ties_all must be int32 [S, M]");
-  TORCH_CHECK(prefix.is_cuda() && prefix.is_contiguous() && prefix.scalar_type() == at::kLong && prefix.numel() >= M,
+  SB_CHECK(prefix.is_cuda() && prefix.is_contiguous() && prefix.scalar_type() == at::kLong && prefix.numel() >= M,
               "batch_filter: prefix must be int64 [M]");
   if (M == 0) return;
   const at::cuda::CUDAGuard guard(vals.device());
@@ -916,15 +917,15 @@ torch::Tensor batch_topk_select(const torch::Tensor& vals, const torch::Tensor& 
 void threshold_select(const torch::Tensor& H, const torch::Tensor& cmax, const torch::Tensor& lo,
                       const torch::Tensor& lo_cmin, const torch::Tensor& out_val, const torch::Tensor& out_idx,
                       const torch::Tensor& counts, const c10::optional<torch::Tensor>& truncated) {
-  TORCH_CHECK(H.is_cuda() && H.scalar_type() == at::kBFloat16 && H.dim() == 2 && H.stride(1) == 1,
+  SB_CHECK(H.is_cuda() && H.scalar_type() == at::kBFloat16 && H.dim() == 2 && H.stride(1) == 1,
               "threshold_select: H must be CUDA bf16 [M, N]");
   const int64_t M = H.size(0), N = H.size(1);
-  TORCH_CHECK(N % 32 == 0 && cmax.size(0) == M && cmax.size(1) == N / 32 && cmax.stride(1) == 1,
+  SB_CHECK(N % 32 == 0 && cmax.size(0) == M && cmax.size(1) == N / 32 && cmax.stride(1) == 1,
               "threshold_select: cmax");
-  TORCH_CHECK(lo.numel() == N && lo_cmin.numel() == N / 32 && lo.scalar_type() == at::kFloat &&
+  SB_CHECK(lo.numel() == N && lo_cmin.numel() == N / 32 && lo.scalar_type() == at::kFloat &&
                   lo_cmin.scalar_type() == at::kFloat && lo.is_contiguous() && lo_cmin.is_contiguous(),
               "threshold_select: lo / lo_cmin");
-  TORCH_CHECK(out_val.is_contiguous() && out_idx.is_contiguous() && out_val.size(0) == M && out_idx.size(0) == M &&
+  SB_CHECK(out_val.is_contiguous() && out_idx.is_contiguous() && out_val.size(0) == M && out_idx.size(0) == M &&
                   out_val.size(1) == out_idx.size(1) && counts.numel() == M,
               "threshold_select: outputs");
   if (M == 0) return;

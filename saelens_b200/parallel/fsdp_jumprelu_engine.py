@@ -61,6 +61,9 @@ class FSDPJumpReLUEngine(FSDPTopKEngine):
         self.m_lthr, self.v_lthr = torch.zeros_like(self.p_lthr), torch.zeros_like(self.p_lthr)
         self.last_l0 = torch.zeros((), device=self.device)
 
+    def k_request(self) -> int:
+        return 1  # no per-row selection: the dense form keeps no candidate lists
+
     def _vector_parts(self) -> list[torch.Tensor]:
         return [self.bias_eff, self.scale, self.inv_scale, self.p_lthr.exp()]
 

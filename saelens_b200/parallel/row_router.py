@@ -20,7 +20,7 @@ from __future__ import annotations
 
 import time
 from dataclasses import dataclass, field
-from typing import Sequence
+from typing import Callable, Sequence
 
 import torch
 import torch.distributed as dist
@@ -137,12 +137,13 @@ class P2PRowRouter:
         self.recv_epoch = 0
 
     @staticmethod
-    def _host_wait(view: torch.Tensor, target: torch.Tensor, timeout_s: float, what: str) -> None:
-        """Poll device words from the host until view >= target (elementwise): long waits (an LM
-        step, a slow consumer) happen here, so the kernels' own bounded waits find the data."""
+    def _host_wait(read: Callable[[], torch.Tensor], target: torch.Tensor, timeout_s: float, what: str) -> None:
+        """Poll device words from the host until read() >= target (elementwise): long waits (an LM
+        step, a slow consumer) happen here, so the kernels' own bounded waits find the data.
+        `read` reads the words afresh at every poll."""
         t0 = time.monotonic()
         while True:
-            if bool((view.to(torch.int64).cpu() >= target).all()):
+            if bool((read().to(torch.int64).cpu() >= target).all()):
                 return
             if time.monotonic() - t0 > timeout_s:
                 raise TimeoutError(f"row router: {what} not reached within {timeout_s:.0f} s")
@@ -154,8 +155,11 @@ class P2PRowRouter:
         if self.p_idx is None:
             raise RuntimeError(f"rank {self.rank} is not a producer")
         if host_wait_s is not None and self.send_epoch + 1 >= 3:
-            free = self.heap.local(self.free)[torch.tensor(self.free_slots, device=self.heap.device)]
-            self._host_wait(free, torch.tensor(self.send_epoch + 1 - 2), host_wait_s, "consumer release")
+            free = self.heap.local(self.free)
+            slots = torch.tensor(self.free_slots, device=self.heap.device)
+            # index inside the poll: advanced indexing copies, and a copy would never change
+            self._host_wait(lambda: free[slots], torch.tensor(self.send_epoch + 1 - 2), host_wait_s,
+                            "consumer release")
         self.send_epoch += 1
         self.nat.p2p_route_rows(acts, self.table, self.heap.bases, self.rank, self.land.offset, self.rows_cap,
                                 (self.send_epoch - 1) % 2, self.cnt.offset, self.p_idx, self.free.offset,
@@ -170,7 +174,7 @@ class P2PRowRouter:
         self.recv_epoch += 1
         targets = self._chunks * self.recv_epoch
         if host_wait_s is not None:
-            self._host_wait(self.cnt_local[: self.P], targets.cpu(), host_wait_s, "producer rows")
+            self._host_wait(lambda: self.cnt_local[: self.P], targets.cpu(), host_wait_s, "producer rows")
         self.nat.p2p_wait_targets(self.cnt_local, targets, self.status.tensor)
         return self.land_local[(self.recv_epoch - 1) % 2, : self.rows_for[self.c_idx]]
 

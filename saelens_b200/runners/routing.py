@@ -32,7 +32,8 @@ import torch.distributed as dist
 
 from saelens_b200.parallel import distributed_v2 as v2
 
-HOST_WAIT_S = 600.0
+# host-side bound on one routed wait (an LM step, a slow consumer); SAELENS_B200_ROUTE_WAIT_S overrides
+HOST_WAIT_S = float(os.environ.get("SAELENS_B200_ROUTE_WAIT_S", "600"))
 
 
 def routing_init(runner: Any) -> None:

@@ -45,6 +45,7 @@ class EngineStepResult:
     topk_idx: torch.Tensor      # [B, k] int32 selected latent indices (-1 = none)
     fire_counts: torch.Tensor   # [d_sae] int32 rows in which each latent fired this step
     l0: torch.Tensor | None = None  # mean active latents per row, when the step keeps no per-row lists
+    extra_losses: dict[str, torch.Tensor] | None = None  # further named loss terms (already in `loss`)
 
     def feature_acts_sparse(self, d_sae: int) -> torch.Tensor:
         """Sparse COO [B, d_sae] of ReLU'd activations (what the reference's TopK emits)."""
@@ -273,6 +274,64 @@ class FusedTopKEngine:
         statistics (`+= fired rows` and `0 if fired else +1`).  With `run_aux` the dead-latent
         aux-k loss is computed for latents where `dead_mask` is true.
         """
+        fw = self._encode_select(x, dead_mask, run_aux)
+        nat, dev = self.native, self.device
+        B, D, k = fw["B"], self.D, self.k
+        xb, vals, idx, aux_on = fw["xb"], fw["vals"], fw["idx"], fw["aux_on"]
+        aux_vals, aux_idx, aux_scale = fw.get("aux_vals"), fw.get("aux_idx"), fw.get("aux_scale")
+        k_aux = D // 2
+
+        # 3. decode + MSE + dL/dx_hat (+ sum over rows for the b_dec gradient)
+        sae_out = torch.empty(B, D, dtype=torch.bfloat16, device=dev) if (want_sae_out or aux_on) else None
+        dxhat = torch.empty(B, D, dtype=torch.bfloat16, device=dev)
+        loss_row = torch.empty(B, dtype=torch.float32, device=dev)
+        bsum = torch.zeros(D, dtype=torch.float32, device=dev)
+        resid = torch.empty(B, D, dtype=torch.bfloat16, device=dev) if aux_on else None
+        nat.decode_mse(vals, idx, True, self.inv_scale if self.rescale else None, self.w_dec, self.p_bdec, xb,
+                       sae_out, resid, dxhat, None, 2.0 / B, loss_row, bsum)
+        mse = loss_row.sum() / B
+        self.launches += 1
+        self._mark("decode_mse")
+        daux, aux_loss = self._aux_decode(fw, resid)
+        pairs = self._build_csc(fw)
+        return self._grads_and_update(_StepState(
+            B=B, xb=xb, vals=vals, idx=idx, aux_on=aux_on, aux_vals=aux_vals if aux_on else None,
+            aux_idx=aux_idx if aux_on else None, dxhat=dxhat, daux=daux, bsum=bsum, pairs=pairs, mse=mse,
+            aux_loss=aux_loss, sae_out=sae_out, act_freq=act_freq, since_fired=since_fired, lr=lr, update=update))
+
+    def _aux_decode(self, fw: dict[str, Any], resid: torch.Tensor | None) -> tuple[torch.Tensor | None, torch.Tensor]:
+        """Aux-k loss on dead latents against the residual `resid` (step 4); (dL/dx_aux, loss)."""
+        nat, dev, B, D = self.native, self.device, fw["B"], self.D
+        aux_loss = torch.zeros((), dtype=torch.float32, device=dev)
+        if not fw["aux_on"]:
+            return None, aux_loss
+        daux = torch.empty(B, D, dtype=torch.bfloat16, device=dev)
+        aux_row = torch.empty(B, dtype=torch.float32, device=dev)
+        gcoef = (fw["aux_scale"] * (2.0 * self.aux_coef / B)).reshape(1).contiguous()
+        nat.decode_mse(fw["aux_vals"], fw["aux_idx"], False, self.inv_scale if self.rescale else None, self.w_dec,
+                       None, resid, None, None, daux, gcoef, 1.0, aux_row, None)
+        aux_loss = self.aux_coef * fw["aux_scale"] * aux_row.sum() / B
+        self.launches += 1
+        return daux, aux_loss
+
+    def _build_csc(self, fw: dict[str, Any]) -> torch.Tensor:
+        """CSC pair lists of the main (and aux) selections (step 5)."""
+        nat, dev, B, k = self.native, self.device, fw["B"], self.k
+        aux_on = fw["aux_on"]
+        self.counts.zero_()
+        self.fire_counts.zero_()
+        self.cursor.zero_()
+        nat.csc_count(fw["vals"], fw["idx"], fw.get("aux_vals"), fw.get("aux_idx"), self.counts, self.fire_counts)
+        torch.cumsum(self.counts, 0, out=self.colptr[1:])
+        n_pairs = B * k + (B * (self.D // 2) if aux_on else 0)
+        pairs = torch.empty(n_pairs, dtype=torch.int64, device=dev)
+        nat.csc_fill(fw["vals"], fw["idx"], fw.get("aux_vals"), fw.get("aux_idx"), self.colptr, self.cursor, pairs)
+        self._mark("csc_build")
+        return pairs
+
+    def _encode_select(self, x: torch.Tensor, dead_mask: torch.Tensor | None, run_aux: bool) -> dict[str, Any]:
+        """Steps 1-2: encoder GEMM with chunk maxima, row top-k (and the masked aux-k top-k), and
+        the batch-wide selection for BatchTopK."""
         nat = self.native
         dev = self.device
         B = x.shape[0]
@@ -324,48 +383,10 @@ class FusedTopKEngine:
             self.launches += 5
             update_topk_threshold_ema(self.sae, sel)
             self._mark("batch_topk_select")
-
-        # 3. decode + MSE + dL/dx_hat (+ sum over rows for the b_dec gradient)
-        sae_out = torch.empty(B, D, dtype=torch.bfloat16, device=dev) if (want_sae_out or aux_on) else None
-        dxhat = torch.empty(B, D, dtype=torch.bfloat16, device=dev)
-        loss_row = torch.empty(B, dtype=torch.float32, device=dev)
-        bsum = torch.zeros(D, dtype=torch.float32, device=dev)
-        resid = torch.empty(B, D, dtype=torch.bfloat16, device=dev) if aux_on else None
-        nat.decode_mse(vals, idx, True, self.inv_scale if self.rescale else None, self.w_dec, self.p_bdec, xb,
-                       sae_out, resid, dxhat, None, 2.0 / B, loss_row, bsum)
-        mse = loss_row.sum() / B
-        self.launches += 1
-        self._mark("decode_mse")
-
-        # 4. aux-k loss on dead latents
-        daux = None
-        aux_loss = torch.zeros((), dtype=torch.float32, device=dev)
+        fw: dict[str, Any] = {"B": B, "xb": xb, "vals": vals, "idx": idx, "aux_on": aux_on}
         if aux_on:
-            daux = torch.empty(B, D, dtype=torch.bfloat16, device=dev)
-            aux_row = torch.empty(B, dtype=torch.float32, device=dev)
-            gcoef = (aux_scale * (2.0 * self.aux_coef / B)).reshape(1).contiguous()
-            nat.decode_mse(aux_vals, aux_idx, False, self.inv_scale if self.rescale else None, self.w_dec, None,
-                           resid, None, None, daux, gcoef, 1.0, aux_row, None)
-            aux_loss = self.aux_coef * aux_scale * aux_row.sum() / B
-            self.launches += 1
-
-        # 5. CSC pair lists
-        self.counts.zero_()
-        self.fire_counts.zero_()
-        self.cursor.zero_()
-        nat.csc_count(vals, idx, aux_vals if aux_on else None, aux_idx if aux_on else None, self.counts,
-                      self.fire_counts)
-        torch.cumsum(self.counts, 0, out=self.colptr[1:])
-        n_pairs = B * k + (B * k_aux if aux_on else 0)
-        pairs = torch.empty(n_pairs, dtype=torch.int64, device=dev)
-        nat.csc_fill(vals, idx, aux_vals if aux_on else None, aux_idx if aux_on else None, self.colptr,
-                     self.cursor, pairs)
-        self._mark("csc_build")
-
-        return self._grads_and_update(_StepState(
-            B=B, xb=xb, vals=vals, idx=idx, aux_on=aux_on, aux_vals=aux_vals if aux_on else None,
-            aux_idx=aux_idx if aux_on else None, dxhat=dxhat, daux=daux, bsum=bsum, pairs=pairs, mse=mse,
-            aux_loss=aux_loss, sae_out=sae_out, act_freq=act_freq, since_fired=since_fired, lr=lr, update=update))
+            fw.update(aux_vals=aux_vals, aux_idx=aux_idx, aux_scale=aux_scale)
+        return fw
 
     def _grads_and_update(self, st: "_StepState") -> EngineStepResult:
         """Latent gradients, firing statistics, clip and Adam (steps 6-8 of the step)."""
@@ -379,24 +400,29 @@ class FusedTopKEngine:
         self.launches += 3
         self._mark("latent_grad")
         if st.update:
-            self.step_count += 1
-            cur_lr = self.lr if st.lr is None else st.lr
-            nat.adam_bdec(st.bsum, bterm if self.apply_b_dec else None, self.g_bdec, self.sumsq, self.clip,
-                          self.p_bdec, self.m_bdec, self.v_bdec, cur_lr, self.beta1, self.beta2, self.eps,
-                          self.step_count, self.max_grad_norm, True)
-            nat.adam_rows(self.p_dec, self.m_dec, self.v_dec, self.p_enc, self.m_enc, self.v_enc, self.w_dec,
-                          self.w_enc, self.g_dec, self.g_enc, self.p_benc, self.m_benc, self.v_benc, self.g_benc,
-                          self.colptr, self.clip, self.p_bdec if self.apply_b_dec else None, self.scale,
-                          self.inv_scale, self.bias_eff, cur_lr, self.beta1, self.beta2, self.eps,
-                          self.step_count, True)
-            self.launches += 2
-            self._mark("adam")
+            self._update(st, bterm)
         self.last_loss = st.mse + st.aux_loss
         if self._phase_timing and len(self._phase_events) > 64:
             self._flush_phases()
         return EngineStepResult(loss=st.mse + st.aux_loss, mse_loss=st.mse, aux_loss=st.aux_loss,
                                 sae_out=st.sae_out, topk_vals=st.vals, topk_idx=st.idx,
                                 fire_counts=self.fire_counts)
+
+    def _update(self, st: "_StepState", bterm: torch.Tensor) -> None:
+        """Clip + Adam on b_dec and on the latent rows (step 8)."""
+        nat = self.native
+        self.step_count += 1
+        cur_lr = self.lr if st.lr is None else st.lr
+        nat.adam_bdec(st.bsum, bterm if self.apply_b_dec else None, self.g_bdec, self.sumsq, self.clip,
+                      self.p_bdec, self.m_bdec, self.v_bdec, cur_lr, self.beta1, self.beta2, self.eps,
+                      self.step_count, self.max_grad_norm, True)
+        nat.adam_rows(self.p_dec, self.m_dec, self.v_dec, self.p_enc, self.m_enc, self.v_enc, self.w_dec,
+                      self.w_enc, self.g_dec, self.g_enc, self.p_benc, self.m_benc, self.v_benc, self.g_benc,
+                      self.colptr, self.clip, self.p_bdec if self.apply_b_dec else None, self.scale,
+                      self.inv_scale, self.bias_eff, cur_lr, self.beta1, self.beta2, self.eps,
+                      self.step_count, True)
+        self.launches += 2
+        self._mark("adam")
 
     def grad_norm(self) -> torch.Tensor:
         return self.sumsq.sqrt()

@@ -208,6 +208,14 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
             elif engine_supported(self._base_sae) and tp_group is None:
                 self.engine = FusedTopKEngine(self._base_sae, lr=cfg.lr, beta1=cfg.adam_beta1,
                                               beta2=cfg.adam_beta2)
+            elif tp_group is None and self._matryoshka_native_ok():
+                from saelens_b200.training.matryoshka_engine import MatryoshkaEngine
+
+                self.engine = MatryoshkaEngine(self._base_sae, lr=cfg.lr, beta1=cfg.adam_beta1, beta2=cfg.adam_beta2)
+            elif tp_group is None and self._dense_engine_class() is not None:
+                # Standard (L1) / Gated: the dense step on the tcgen05 GEMM family
+                self.engine = self._dense_engine_class()(self._base_sae, lr=cfg.lr, beta1=cfg.adam_beta1,
+                                                         beta2=cfg.adam_beta2)
             elif want == "native":
                 raise ValueError("sae_engine='native' requested but this SAE/device is not supported by the fused engine")
 
@@ -289,6 +297,16 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
             if quiesce_if_requested():
                 break
         return self._finish_fit()
+
+    def _matryoshka_native_ok(self) -> bool:
+        from saelens_b200.training.matryoshka_engine import matryoshka_engine_supported
+
+        return matryoshka_engine_supported(self._base_sae)
+
+    def _dense_engine_class(self) -> Any:
+        from saelens_b200.training.dense_engine import dense_engine_class
+
+        return dense_engine_class(self._base_sae)
 
     def _jumprelu_native_ok(self, required: bool) -> bool:
         from saelens_b200.training.jumprelu_engine import jumprelu_engine_supported
@@ -402,6 +420,8 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
         for s in self.coefficient_schedulers.values():
             s.step()
         losses = {"mse_loss": res.mse_loss, getattr(self.engine, "aux_loss_name", "auxiliary_reconstruction_loss"): res.aux_loss}
+        if res.extra_losses:
+            losses.update(res.extra_losses)
         d_sae = self._base_sae.cfg.d_sae
         out = TrainStepOutput(
             sae_in=sae_in, sae_out=res.sae_out if res.sae_out is not None else sae_in.new_empty(0),

@@ -205,3 +205,59 @@ def test_batchtopk_engine_selection_and_gradients():
     # threshold EMA: 0.99 * 0 + 0.01 * (smallest kept activation)
     kept_min = res.topk_vals[sel].min().double()
     assert torch.allclose(sae.topk_threshold, 0.01 * kept_min, rtol=1e-5)
+
+
+def test_matryoshka_engine_nested_losses_and_gradients():
+    """Matryoshka BatchTopK on the native engine: the nested prefix MSEs and every gradient against
+    fp32 autograd of sum_l MSE(prefix_l reconstruction) with the engine's selection as the mask."""
+    from saelens_b200.models.batchtopk import MatryoshkaBatchTopKTrainingSAE, MatryoshkaBatchTopKTrainingSAEConfig
+    from saelens_b200.training.matryoshka_engine import MatryoshkaEngine, matryoshka_engine_supported
+
+    torch.manual_seed(0)
+    widths = [256, 768, 2048]
+    sae = MatryoshkaBatchTopKTrainingSAE(MatryoshkaBatchTopKTrainingSAEConfig(
+        d_in=256, d_sae=2048, k=16, matryoshka_widths=list(widths), device="cuda"))
+    with torch.no_grad():
+        sae.b_enc.normal_(0, 0.01)
+        sae.b_dec.normal_(0, 0.05)
+    assert matryoshka_engine_supported(sae)
+    x = torch.randn(512, 256, device="cuda").to(torch.bfloat16)
+    eng = MatryoshkaEngine(sae, lr=1e-3)
+    w_enc0, w_dec0 = eng.w_enc.clone(), eng.w_dec.clone()
+    b_enc0, b_dec0 = eng.p_benc.clone(), eng.p_bdec.clone()
+    res = eng.step(x, update=False)
+    torch.cuda.synchronize()
+    eng.status.check()
+    sel = res.topk_idx >= 0
+    mask = torch.zeros(512, 2048, dtype=torch.bool, device="cuda")
+    rows = torch.arange(512, device="cuda")[:, None].expand_as(res.topk_idx)
+    mask[rows[sel], res.topk_idx[sel].long()] = True
+    We = w_enc0.float().T.clone().requires_grad_(True)
+    Wd = w_dec0.float().clone().requires_grad_(True)
+    be = b_enc0.clone().requires_grad_(True)
+    bd = b_dec0.clone().requires_grad_(True)
+    n_ = Wd.norm(dim=-1)
+    hh = ((x.float() - bd) @ We + be) * n_
+    acts = torch.where(mask, hh.relu(), torch.zeros_like(hh)) / n_
+    total = 0.0
+    mses = []
+    for w in widths:
+        rec = acts[:, :w] @ Wd[:w] + bd
+        m = (rec - x.float()).pow(2).sum(-1).mean()
+        mses.append(m)
+        total = total + m
+    total.backward()
+    assert abs(res.mse_loss.item() - mses[-1].item()) <= 1e-2 * mses[-1].item()
+    for w, m in zip(widths[:-1], mses[:-1]):
+        got = res.extra_losses[f"inner_mse_loss_{w}"].item()
+        assert abs(got - m.item()) <= 1e-2 * m.item(), (w, got, m.item())
+    live = eng.colptr[1:] > eng.colptr[:-1]
+
+    def rel(a, b):
+        return ((a.float() - b.float()).norm() / b.float().norm()).item()
+
+    assert rel(eng.g_dec[live], Wd.grad[live]) < 3e-2
+    assert rel(eng.g_enc[live], We.grad.T[live]) < 3e-2
+    assert rel(eng.g_benc[live], be.grad[live]) < 3e-2
+    losses = [float(eng.step(x).loss) for _ in range(5)]
+    assert losses[-1] < losses[0]

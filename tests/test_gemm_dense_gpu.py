@@ -20,7 +20,7 @@ def _close(got, ref, rel=1e-2):
 
 
 @pytest.mark.parametrize("a_mn, b_mn", [(False, False), (False, True), (True, False), (True, True)])
-@pytest.mark.parametrize("M, N, K", [(256, 512, 256), (300, 1000, 200), (1024, 2048, 1024)])
+@pytest.mark.parametrize("M, N, K", [(256, 512, 256), (304, 1000, 200), (1024, 2048, 1024)])
 def test_layouts_and_ragged_sizes(a_mn, b_mn, M, N, K):
     from saelens_b200 import ops
 

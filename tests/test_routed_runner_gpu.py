@@ -21,7 +21,7 @@ def _port() -> int:
 
 def _worker(rank, world, port, tmp, P, Q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
-                      LOCAL_RANK=str(rank))
+                      LOCAL_RANK=str(rank), SAELENS_B200_ROUTE_WAIT_S="90")
     import torch.distributed as dist
     from datetime import timedelta
 
