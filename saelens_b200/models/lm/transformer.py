@@ -312,22 +312,34 @@ class Attention(nn.Module):
         self.hook_rot_q, self.hook_rot_k = HookPoint(), HookPoint()
         self.scale = 1.0 / math.sqrt(cfg.query_pre_attn_scalar if cfg.query_pre_attn_scalar else dh)
         self._qkv = _FusedWeights()
+        # tensor parallelism (models/lm/tp.py): this rank's heads and the group
+        self.n_heads_local, self.n_kv_local = H, KV
+        self.tp: Any = None
+        self.o_bias_after: torch.Tensor | None = None
+
+    def _hook(self, hp: HookPoint, t: torch.Tensor, dim: int) -> torch.Tensor:
+        """Run a hook point on a head-sharded tensor: under tensor parallelism, a hook that is
+        attached sees the full width (all-gathered along `dim`) and the rank keeps its shard of
+        the result."""
+        if self.tp is None or not hp.has_hooks:
+            return hp(t)
+        return self.tp.hooked(hp, t, dim)
 
     def forward(self, x: torch.Tensor, rot: tuple[torch.Tensor, torch.Tensor] | None) -> torch.Tensor:
         B, S, _ = x.shape
-        H, KV, dh = self.cfg.n_heads, self.cfg.n_key_value_heads, self.cfg.d_head
+        H, KV, dh = self.n_heads_local, self.n_kv_local, self.cfg.d_head
         fused = (x.dtype == torch.bfloat16 and self.q.weight.dtype == torch.bfloat16 and x.shape[-1] % 8 == 0
                  and _native_ok(x))
         if fused:
             # one GEMM for q, k and v; the heads are strided views of its output
             qkv = _fused_linear(x, self._qkv, [self.q, self.k, self.v])
-            q = self.hook_q(qkv[..., : H * dh].view(B, S, H, dh))
-            k = self.hook_k(qkv[..., H * dh : (H + KV) * dh].view(B, S, KV, dh))
-            v = self.hook_v(qkv[..., (H + KV) * dh :].view(B, S, KV, dh))
+            q = self._hook(self.hook_q, qkv[..., : H * dh].view(B, S, H, dh), 2)
+            k = self._hook(self.hook_k, qkv[..., H * dh : (H + KV) * dh].view(B, S, KV, dh), 2)
+            v = self._hook(self.hook_v, qkv[..., (H + KV) * dh :].view(B, S, KV, dh), 2)
         else:
-            q = self.hook_q(self.q(x).view(B, S, H, dh))
-            k = self.hook_k(self.k(x).view(B, S, KV, dh))
-            v = self.hook_v(self.v(x).view(B, S, KV, dh))
+            q = self._hook(self.hook_q, self.q(x).view(B, S, H, dh), 2)
+            k = self._hook(self.hook_k, self.k(x).view(B, S, KV, dh), 2)
+            v = self._hook(self.hook_v, self.v(x).view(B, S, KV, dh), 2)
         if rot is not None:
             in_place = (fused and rot[0].dtype == torch.float32 and not (self.hook_q.has_hooks or self.hook_k.has_hooks)
                         and q.stride(-1) == 1 and k.stride(-1) == 1)
@@ -338,18 +350,18 @@ class Attention(nn.Module):
                 cos, sin = rot[0].contiguous(), rot[1].contiguous()
                 native().rope_(q, cos, sin, 0)
                 native().rope_(k, cos, sin, 0)
-                q, k = self.hook_rot_q(q), self.hook_rot_k(k)
+                q, k = self._hook(self.hook_rot_q, q, 2), self._hook(self.hook_rot_k, k, 2)
             else:
-                q = self.hook_rot_q(apply_rotary(q, *rot))
-                k = self.hook_rot_k(apply_rotary(k, *rot))
+                q = self._hook(self.hook_rot_q, apply_rotary(q, *rot), 2)
+                k = self._hook(self.hook_rot_k, apply_rotary(k, *rot), 2)
         if q.dtype == torch.bfloat16 and dh in (64, 128, 256) and _native_ok(q):
             from saelens_b200 import ops
 
             # tcgen05 prefill attention: K/V heads are read in place by their query-head group,
             # the soft-cap (Gemma-2) is applied to the logits inside the kernel
             z = ops.attention(q, k, v, self.scale, softcap=self.cfg.attn_softcap, causal=True)
-            z = self.hook_z(z)
-            return self.o(z.reshape(B, S, H * dh))
+            z = self._hook(self.hook_z, z, 2)
+            return self._out(z.reshape(B, S, H * dh))
         qh, kh, vh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
         if KV != H:
             rep = H // KV
@@ -363,8 +375,18 @@ class Attention(nn.Module):
             z = (torch.softmax(sc, dim=-1) @ vh.float()).to(x.dtype)
         else:
             z = F.scaled_dot_product_attention(qh, kh, vh, is_causal=True, scale=self.scale)
-        z = self.hook_z(z.transpose(1, 2))  # [B, S, H, dh]
-        return self.o(z.reshape(B, S, H * dh))
+        z = self._hook(self.hook_z, z.transpose(1, 2), 2)  # [B, S, H, dh]
+        return self._out(z.reshape(B, S, H * dh))
+
+    def _out(self, z: torch.Tensor) -> torch.Tensor:
+        """Output projection; under tensor parallelism the partial sums of the ranks' heads are
+        all-reduced and the bias is added once, after the sum."""
+        y = self.o(z)
+        if self.tp is not None:
+            y = self.tp.all_reduce(y)
+            if self.o_bias_after is not None:
+                y = y + self.o_bias_after
+        return y
 
 
 class MLP(nn.Module):
@@ -380,37 +402,53 @@ class MLP(nn.Module):
         self.hook_pre = HookPoint()
         self.hook_post = HookPoint()
         self._gate_up = _FusedWeights()
+        self.d_mlp_local = cfg.d_mlp
+        self.tp: Any = None
+        self.down_bias_after: torch.Tensor | None = None
+
+    def _hook(self, hp: HookPoint, t: torch.Tensor) -> torch.Tensor:
+        if self.tp is None or not hp.has_hooks:
+            return hp(t)
+        return self.tp.hooked(hp, t, t.dim() - 1)
+
+    def _down(self, post: torch.Tensor) -> torch.Tensor:
+        y = self.down(post)
+        if self.tp is not None:
+            y = self.tp.all_reduce(y)
+            if self.down_bias_after is not None:
+                y = y + self.down_bias_after
+        return y
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         x = self.hook_in(x)
         if self.gated:
             kind = {"silu": 0, "gelu_new": 1, "gelu_pytorch_tanh": 1}.get(self.cfg.act_fn)
-            d = self.cfg.d_mlp
+            d = self.d_mlp_local
             if (kind is not None and x.dtype == torch.bfloat16 and self.gate.weight.dtype == torch.bfloat16
                     and x.shape[-1] % 8 == 0 and d % 8 == 0 and _native_ok(x)):
                 # one GEMM for the gate and up projections; the activation reads both halves in place
                 from saelens_b200.ops import native
 
                 gu = _fused_linear(x, self._gate_up, [self.gate, self.up])
-                pre = self.hook_pre(gu[..., :d])
+                pre = self._hook(self.hook_pre, gu[..., :d])
                 up = gu[..., d:]
                 if pre.shape == up.shape and pre.stride(-1) == 1:
-                    post = self.hook_post(native().gated_act(pre, up, kind))
+                    post = self._hook(self.hook_post, native().gated_act(pre, up, kind))
                 else:
-                    post = self.hook_post(_act(self.cfg.act_fn, pre) * up)
-                return self.down(post)
-            pre = self.hook_pre(self.gate(x))
+                    post = self._hook(self.hook_post, _act(self.cfg.act_fn, pre) * up)
+                return self._down(post)
+            pre = self._hook(self.hook_pre, self.gate(x))
             up = self.up(x)
             if kind is not None and pre.dtype == torch.bfloat16 and pre.shape == up.shape and _native_ok(pre):
                 from saelens_b200.ops import native
 
-                post = self.hook_post(native().gated_act(pre.contiguous(), up.contiguous(), kind))
+                post = self._hook(self.hook_post, native().gated_act(pre.contiguous(), up.contiguous(), kind))
             else:
-                post = self.hook_post(_act(self.cfg.act_fn, pre) * up)
+                post = self._hook(self.hook_post, _act(self.cfg.act_fn, pre) * up)
         else:
-            pre = self.hook_pre(self.up(x))
-            post = self.hook_post(_act(self.cfg.act_fn, pre))
-        return self.down(post)
+            pre = self._hook(self.hook_pre, self.up(x))
+            post = self._hook(self.hook_post, _act(self.cfg.act_fn, pre))
+        return self._down(post)
 
 
 class Block(nn.Module):

@@ -111,6 +111,10 @@ class LanguageModelSAETrainingRunner:
         self.activations_store: Any = None
         if producer_side:
             self.model = override_model if override_model is not None else self._load_model()
+            if getattr(self, "producer_tp_group", None) is not None:
+                from saelens_b200.models.lm.tp import shard_lm_tensor_parallel
+
+                shard_lm_tensor_parallel(self.model, self.producer_tp_group)  # Megatron split of the producer
             if cfg.compile_llm:
                 self.model = torch.compile(self.model, mode=cfg.llm_compilation_mode)
             if self.streaming_mode:

@@ -9,6 +9,10 @@ both.  With SAE TP every member of a consumer's TP group needs the same rows: th
 stores them into every member's landing buffer from the producer (no second hop), the collective
 transport sends them to the consumer root, which broadcasts them to its TP group.
 
+Producer tensor parallelism (`vllm_tp_size` > 1): every member of a producer's TP group runs the
+Megatron-split LM (`models/lm/tp.py`) on the same tokens in lockstep; the group's first rank holds
+the full activations after the layer's all-reduces and is the one that sends.
+
 Transports:
 
 * "p2p" (CUDA + NCCL): `P2PRowRouter`, one kernel per producer step that stores every route's rows
@@ -46,8 +50,6 @@ def routing_init(runner: Any) -> None:
         dist.init_process_group(backend)
     P, Q = max(runner.vllm_dp_size, 1), max(runner.sae_dp_size, 1)
     vtp, stp = max(runner.vllm_tp_size, 1), max(runner.sae_tp_size, 1)
-    if vtp != 1:
-        raise ValueError("routed producers run the framework's LM on one GPU each (vllm_tp_size must be 1)")
     if (Q * cfg.train_batch_size_tokens) % P:
         raise ValueError("sae_dp_size * train_batch_size_tokens must be divisible by vllm_dp_size")
     runner.route_batch = Q * cfg.train_batch_size_tokens // P
@@ -55,7 +57,10 @@ def routing_init(runner: Any) -> None:
     disjoint = world == P * vtp + Q * stp and world != max(P * vtp, Q * stp)
     v2.init_distributed_v2(P=P, Q=Q, vllm_tp_size=vtp, sae_tp_size=stp, batch_size=runner.route_batch,
                            disjoint=disjoint)
-    runner.is_route_producer = v2.is_producer() and v2.get_vllm_tp_rank() == 0
+    # every member of a producer's TP group runs the (sharded) LM; its first rank sends the rows
+    runner.is_route_producer = v2.is_producer()
+    runner.is_route_sender = v2.is_producer() and v2.get_vllm_tp_rank() == 0
+    runner.producer_tp_group = v2.get_vllm_tp_group() if vtp > 1 and v2.is_producer() else None
     runner.is_route_consumer = v2.is_consumer()
     runner.role = ("producer+consumer" if runner.is_route_producer and runner.is_route_consumer
                    else "producer" if runner.is_route_producer else "consumer" if runner.is_route_consumer else "idle")
@@ -143,6 +148,8 @@ class RoutedExchange:
 
     def step(self) -> torch.Tensor | None:
         rows = self._produce()
+        if rows is not None and not self.r.is_route_sender:
+            rows = None  # a producer TP member: the group's first rank sends
         if rows is not None:
             self._after_produce()
         if self.r.router is not None:

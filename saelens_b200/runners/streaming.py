@@ -49,10 +49,11 @@ def streaming_init(runner: Any) -> None:
         dist.init_process_group(backend)
     vllm_tp, vllm_dp = max(runner.vllm_tp_size, 1), max(runner.vllm_dp_size, 1)
     sae_tp = max(runner.sae_tp_size, 1)
-    if vllm_tp != 1:
-        raise ValueError("streaming producers run the framework's LM on one GPU each (vllm_tp_size must be 1)")
     ds.init_distributed_streaming(vllm_tp=vllm_tp, vllm_dp=vllm_dp, sae_tp=sae_tp, sae_dp=1)
     runner.role = "producer" if ds.is_producer() else "consumer"
+    # producer tensor parallelism: every member runs the split LM, the group's first rank writes
+    runner.producer_tp_group = ds.get_vllm_tp_group() if vllm_tp > 1 and ds.is_producer() else None
+    runner.is_stream_writer = ds.is_producer() and ds.get_vllm_tp_rank() == 0
     n_hooks = len(getattr(cfg, "hook_names", None) or [cfg.hook_name])
     runner.streaming_transport = choose_transport(cfg, sae_tp, n_hooks)
     runner.n_producers = vllm_dp
@@ -119,6 +120,8 @@ def run_producer(runner: Any) -> int:
         if ack is not None:
             ack.touch()
 
+    writer = getattr(runner, "is_stream_writer", True)
+    tp = getattr(runner, "producer_tp_group", None)
     written = 0
     seq = pidx
     if runner.ring is not None and runner.resume_from_checkpoint is not None:
@@ -131,33 +134,43 @@ def run_producer(runner: Any) -> int:
             st = torch.load(st_path, map_location="cpu", weights_only=False)
             consumed = int(st.get("n_training_samples", 0)) // rows_per_chunk
             seq = pidx + ((max(consumed - pidx, 0) + P - 1) // P) * P
-    while seq < runner.target_chunks:
-        if requested():
-            quiesce()
+    stop = None  # None: go on; "quiesce": quiesce and stop; "end": the ring was closed
+    while True:
+        # the writer decides for its whole TP group (the members' LM forwards run in lockstep)
+        go = seq < runner.target_chunks and stop is None and not (writer and requested())
+        if tp is not None:
+            flag = torch.tensor([1 if go else 0], dtype=torch.int32,
+                                device="cuda" if dist.get_backend(tp) == "nccl" else "cpu")
+            dist.broadcast(flag, src=dist.get_global_rank(tp, 0), group=tp)
+            go = bool(flag.item())
+        if not go:
+            if writer and (stop == "quiesce" or (stop is None and seq < runner.target_chunks and requested())):
+                quiesce()
             break
         rows = max(1, min(rows_per_chunk, cfg.training_tokens - seq * rows_per_chunk))
         acts, valid = store.get_streaming_activations(rows)
-        # a full ring blocks the producer; the quiesce request must still reach it there
-        if runner.ring is not None:
-            if runner.ring.write(acts, stop_check=requested) is None:
-                quiesce()
-                break
-        else:
-            buf = runner.shm_buffer
-            got = buf.allocate_write_chunk(stop_check=requested)
-            if got is None:
-                if requested():
-                    quiesce()
-                break
-            idx, _ = got
-            buf.write_chunk(idx, acts.detach().to("cpu"), valid, producer_id=pidx)
-            buf.mark_ready(idx)
-        written += 1
+        if writer:
+            # a full ring blocks the producer; the quiesce request must still reach it there
+            if runner.ring is not None:
+                if runner.ring.write(acts, stop_check=requested) is None:
+                    stop = "quiesce"
+                    continue
+            else:
+                buf = runner.shm_buffer
+                got = buf.allocate_write_chunk(stop_check=requested)
+                if got is None:
+                    stop = "quiesce" if requested() else "end"
+                    continue
+                idx, _ = got
+                buf.write_chunk(idx, acts.detach().to("cpu"), valid, producer_id=pidx)
+                buf.mark_ready(idx)
+            written += 1
         seq += P
-    if runner.ring is not None:
-        runner.ring.producer_done()
-    else:
-        runner.shm_buffer.signal_done()
+    if writer:
+        if runner.ring is not None:
+            runner.ring.producer_done()
+        else:
+            runner.shm_buffer.signal_done()
     return written
 
 

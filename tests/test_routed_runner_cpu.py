@@ -19,7 +19,7 @@ def _port() -> int:
     return p
 
 
-def _worker(rank, world, port, tmp, P, Q, tp=1):
+def _worker(rank, world, port, tmp, P, Q, tp=1, vtp=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
     import torch.distributed as dist
@@ -45,10 +45,11 @@ def _worker(rank, world, port, tmp, P, Q, tp=1):
     if rank == 1:  # a rank with other paths (e.g. another timestamp) follows rank 0
         cfg.checkpoint_path = os.path.join(tmp, "elsewhere")
     runner = LanguageModelSAETrainingRunner(cfg, override_model=lm, vllm_dp_size=P, sae_dp_size=Q,
-                                            sae_tp_size=tp, use_shard_routing=True)
+                                            sae_tp_size=tp, vllm_tp_size=vtp, use_shard_routing=True)
     assert cfg.checkpoint_path != os.path.join(tmp, "elsewhere")
     out = runner.run()
-    info = {"role": runner.role, "transport": runner.routing_transport}
+    info = {"role": runner.role, "transport": runner.routing_transport,
+            "lm_sharded": getattr(runner.model, "tp", None) is not None}
     if out is not None:
         info["steps"] = runner.trainer.n_training_steps
         info["W_dec_sum"] = float(out.W_dec.detach().sum())
@@ -78,6 +79,18 @@ def test_routed_runner_to_tensor_parallel_consumer(tmp_path):
     r = [json.loads((tmp_path / f"r{i}.json").read_text()) for i in range(3)]
     assert r[0]["role"] == "producer" and r[1]["role"] == r[2]["role"] == "consumer"
     assert r[1]["steps"] == r[2]["steps"] == 8
+
+
+def test_routed_runner_with_tensor_parallel_producer(tmp_path):
+    """A producer whose LM is split over two ranks (Megatron TP, every member runs its shard, the
+    first rank sends) trains the consumer's SAE exactly as a one-rank producer does."""
+    mp.spawn(_worker, args=(3, _port(), str(tmp_path / "tp"), 1, 1, 1, 2), nprocs=3, join=True)
+    r = [json.loads((tmp_path / "tp" / f"r{i}.json").read_text()) for i in range(3)]
+    assert r[0]["role"] == r[1]["role"] == "producer" and r[2]["role"] == "consumer"
+    assert r[0]["lm_sharded"] and r[1]["lm_sharded"] and r[2]["steps"] == 8
+    mp.spawn(_worker, args=(2, _port(), str(tmp_path / "one"), 1, 1), nprocs=2, join=True)
+    one = json.loads((tmp_path / "one" / "r1.json").read_text())
+    assert r[2]["W_dec_sum"] == pytest.approx(one["W_dec_sum"], rel=1e-4, abs=1e-4)
 
 
 def _resume_worker(rank, world, port, tmp, phase):

@@ -17,7 +17,7 @@ def _port() -> int:
     return p
 
 
-def _worker(rank, world, port, tmp):
+def _worker(rank, world, port, tmp, vtp=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
     import torch.distributed as dist
@@ -45,9 +45,10 @@ def _worker(rank, world, port, tmp):
         SharedActivationBuffer(f"ring_{port}", 4, 128, 64, num_producers=1, target_chunks=6, create=True,
                                base_dir=tmp, dtype=torch.float32).close()
     dist.barrier()
-    runner = LanguageModelSAETrainingRunner(cfg, override_model=lm, vllm_dp_size=1)
+    runner = LanguageModelSAETrainingRunner(cfg, override_model=lm, vllm_dp_size=1, vllm_tp_size=vtp)
     out = runner.run()
-    info = {"role": runner.role, "transport": runner.streaming_transport}
+    info = {"role": runner.role, "transport": runner.streaming_transport,
+            "lm_sharded": getattr(runner.model, "tp", None) is not None}
     if runner.role == "consumer":
         info["steps"] = runner.trainer.n_training_steps
         info["d_sae"] = int(out.W_dec.shape[0])
@@ -66,3 +67,12 @@ def test_streaming_host_ring_producer_to_consumer(tmp_path):
     assert (out / "cfg.json").exists() and (out / "sae_weights.safetensors").exists()
     rows = [json.loads(x) for x in (out / "mse_history.jsonl").read_text().splitlines()]
     assert len(rows) == 12
+
+
+def test_streaming_with_tensor_parallel_producer(tmp_path):
+    """The producer's LM split over two ranks (Megatron TP): both run every forward, the first rank
+    writes the chunks; the consumer trains the same number of steps."""
+    mp.spawn(_worker, args=(3, _port(), str(tmp_path), 2), nprocs=3, join=True)
+    r = [json.loads((tmp_path / f"r{i}.json").read_text()) for i in range(3)]
+    assert r[0]["role"] == r[1]["role"] == "producer" and r[0]["lm_sharded"] and r[1]["lm_sharded"]
+    assert r[2]["role"] == "consumer" and r[2]["steps"] == 12
