@@ -23,6 +23,8 @@ PyTorch (the CPU oracle of the tests).
 
 from __future__ import annotations
 
+import contextlib
+
 import math
 from dataclasses import asdict, dataclass
 from typing import Any
@@ -489,18 +491,21 @@ class HookedLM(HookedRootModule):
         super().__init__()
         self.cfg = cfg
         dtype = getattr(torch, cfg.dtype)
-        self.embed = nn.Embedding(cfg.d_vocab, cfg.d_model, dtype=dtype)
-        self.hook_embed = HookPoint()
-        if cfg.positional == "standard":
-            self.pos_embed = nn.Embedding(cfg.n_ctx, cfg.d_model, dtype=dtype)
-            self.hook_pos_embed = HookPoint()
-        self.blocks = nn.ModuleList([Block(cfg, dtype) for _ in range(cfg.n_layers)])
-        self.ln_final = Norm(cfg, dtype)
-        self.unembed = None if cfg.tie_embeddings else NativeLinear(cfg.d_model, cfg.d_vocab, False, dtype)
-        self.tokenizer = tokenizer
-        self._rot: tuple[torch.Tensor, torch.Tensor] | None = None
-        if init:
-            self.init_weights()
+        # parameters are allocated and initialised on `device` directly (an 8B-parameter model
+        # built on the host first would spend minutes in host RNG and copies)
+        with torch.device(device) if device is not None else contextlib.nullcontext():
+            self.embed = nn.Embedding(cfg.d_vocab, cfg.d_model, dtype=dtype)
+            self.hook_embed = HookPoint()
+            if cfg.positional == "standard":
+                self.pos_embed = nn.Embedding(cfg.n_ctx, cfg.d_model, dtype=dtype)
+                self.hook_pos_embed = HookPoint()
+            self.blocks = nn.ModuleList([Block(cfg, dtype) for _ in range(cfg.n_layers)])
+            self.ln_final = Norm(cfg, dtype)
+            self.unembed = None if cfg.tie_embeddings else NativeLinear(cfg.d_model, cfg.d_vocab, False, dtype)
+            self.tokenizer = tokenizer
+            self._rot: tuple[torch.Tensor, torch.Tensor] | None = None
+            if init:
+                self.init_weights()
         if device is not None:
             self.to(device)
         self.setup()

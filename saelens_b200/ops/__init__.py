@@ -8,6 +8,8 @@ the CPU oracle in tests.
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from saelens_b200.ops._build import load as _load
@@ -16,6 +18,8 @@ from saelens_b200.ops.status import StatusWord
 __all__ = [
     "native",
     "available",
+    "bounds_violations",
+    "debug_bounds_enabled",
     "gemm_tn",
     "row_topk",
     "decode_mse",
@@ -24,8 +28,51 @@ __all__ = [
 ]
 
 
+class _DebugBoundsNative:
+    """The extension with its index-dereferencing kernels taken from the debug-bounds module
+    (`_C_debug`: every data-dependent index checked before use, violations skipped and recorded;
+    read them with `bounds_violations()`), everything else from the main module."""
+
+    def __init__(self) -> None:
+        from saelens_b200.ops._build import load_debug
+
+        self._main = _load()
+        self._debug = load_debug()
+
+    def __getattr__(self, name: str):
+        return getattr(self._debug, name) if hasattr(self._debug, name) else getattr(self._main, name)
+
+
+_DEBUG_NATIVE: _DebugBoundsNative | None = None
+
+
+def debug_bounds_enabled() -> bool:
+    return os.environ.get("SAELENS_B200_DEBUG_BOUNDS", "0") not in ("", "0")
+
+
 def native():
+    """The compiled extension; with SAELENS_B200_DEBUG_BOUNDS=1 its index-dereferencing kernels
+    come from the bounds-checked debug module."""
+    global _DEBUG_NATIVE
+    if debug_bounds_enabled():
+        if _DEBUG_NATIVE is None:
+            _DEBUG_NATIVE = _DebugBoundsNative()
+        return _DEBUG_NATIVE
     return _load()
+
+
+def bounds_violations(reset: bool = True) -> dict[str, dict[str, int]]:
+    """Bounds violations recorded by the debug-bounds module since the last reset, per source
+    file: {file: {line, value, bound, count}} of the first violation (empty when none)."""
+    from saelens_b200.ops._build import load_debug
+
+    dbg = load_debug()
+    out: dict[str, dict[str, int]] = {}
+    for unit in ("sparse", "topk", "p2p"):
+        line, value, bound, count = getattr(dbg, f"{unit}_bounds_info")(reset)
+        if count:
+            out[f"{unit}.cu"] = {"line": line, "value": value, "bound": bound, "count": count}
+    return out
 
 
 def available() -> bool:

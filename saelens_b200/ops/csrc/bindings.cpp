@@ -1,6 +1,11 @@
 // Python bindings of the saelens_b200 native kernels (module `saelens_b200.ops._C`).
 #include <torch/extension.h>
 
+// SB_DEBUG_BOUNDS=1 builds the debug-bounds module: only the index-dereferencing kernels, checked
+#ifndef SB_DEBUG_BOUNDS
+#define SB_DEBUG_BOUNDS 0
+#endif
+
 #include <tuple>
 #include <vector>
 
@@ -161,13 +166,16 @@ void batch_ties(const torch::Tensor& vals, const torch::Tensor& idx, const torch
 void batch_filter(const torch::Tensor& vals, const torch::Tensor& idx, const torch::Tensor& sel,
                   const torch::Tensor& ties_all, int64_t rank, const torch::Tensor& prefix,
                   const c10::optional<torch::Tensor>& truncated);
+#if SB_DEBUG_BOUNDS
+std::vector<int64_t> sparse_bounds_info(bool reset);
+std::vector<int64_t> topk_bounds_info(bool reset);
+std::vector<int64_t> p2p_bounds_info(bool reset);
+#endif
 }  // namespace sb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "saelens_b200 sm_100a kernels";
-  m.def("gemm_tn_bf16", &sb::gemm_tn_bf16, py::arg("A"), py::arg("B"), py::arg("bias"), py::arg("scale"),
-        py::arg("relu"), py::arg("out"), py::arg("cmax"), py::arg("status"), py::arg("max_ctas"),
-        py::arg("tmax") = py::none());
+  // kernels that dereference data-dependent indices (also built into the debug-bounds module)
   m.def("row_topk", &sb::row_topk, py::arg("H"), py::arg("cmax"), py::arg("k_max"), py::arg("k_dev"),
         py::arg("mask"), py::arg("out_val"), py::arg("out_idx"), py::arg("status"), py::arg("tmax") = py::none());
   m.def("decode_mse", &sb::decode_mse);
@@ -182,19 +190,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("jr_l0c") = 0.0, py::arg("jr_gthr") = py::none(), py::arg("rs_bases") = std::vector<int64_t>{},
         py::arg("rs_rank") = 0, py::arg("rs_dec_off") = 0, py::arg("rs_enc_off") = 0, py::arg("rs_n") = 0);
   m.def("threshold_select", &sb::threshold_select);
-  m.def("adam_bdec", &sb::adam_bdec);
-  m.def("adam_rows", &sb::adam_rows);
   m.def("topk_merge", &sb::topk_merge);
   m.def("decode_partial", &sb::decode_partial);
   m.def("finish_mse", &sb::finish_mse);
-  m.def("gemm_ag_tn_bf16", &sb::gemm_ag_tn_bf16, py::arg("x_own"), py::arg("peer_bases"), py::arg("rank"),
-        py::arg("x_off"), py::arg("flag_off"), py::arg("total_rows"), py::arg("m_base"), py::arg("M"), py::arg("push"),
-        py::arg("epoch"), py::arg("B"), py::arg("bias"), py::arg("scale"), py::arg("relu"), py::arg("out"),
-        py::arg("cmax"), py::arg("status"), py::arg("ticket"), py::arg("max_ctas"), py::arg("tmax") = py::none());
-  m.def("gemm_fsdp_tn_bf16", &sb::gemm_fsdp_tn_bf16, py::arg("A"), py::arg("w_own"), py::arg("peer_bases"),
-        py::arg("rank"), py::arg("w_off"), py::arg("flag_off"), py::arg("push"), py::arg("epoch"), py::arg("w2_own"),
-        py::arg("w2_off"), py::arg("flag2_off"), py::arg("bias"), py::arg("scale"), py::arg("relu"), py::arg("out"),
-        py::arg("cmax"), py::arg("status"), py::arg("ticket"), py::arg("max_ctas") = 0, py::arg("tmax") = py::none());
   m.def("decode_rs", &sb::decode_rs);
   m.def("topk_exchange_merge", &sb::topk_exchange_merge);
   m.def("p2p_allreduce_sizes", &sb::p2p_allreduce_sizes, py::arg("n"), py::arg("elem_bytes"), py::arg("world"),
@@ -211,12 +209,32 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_route_rows", &sb::p2p_route_rows);
   m.def("p2p_wait_targets", &sb::p2p_wait_targets);
   m.def("p2p_signal", &sb::p2p_signal);
-  m.def("rmsnorm", &sb::rmsnorm);
   m.def("batch_topk_select", &sb::batch_topk_select);
   m.def("batch_hist", &sb::batch_hist);
   m.def("batch_thresh", &sb::batch_thresh);
   m.def("batch_ties", &sb::batch_ties);
   m.def("batch_filter", &sb::batch_filter);
+#if SB_DEBUG_BOUNDS
+  m.attr("debug_bounds") = true;
+  m.def("sparse_bounds_info", &sb::sparse_bounds_info, py::arg("reset") = true);
+  m.def("topk_bounds_info", &sb::topk_bounds_info, py::arg("reset") = true);
+  m.def("p2p_bounds_info", &sb::p2p_bounds_info, py::arg("reset") = true);
+#else
+  m.attr("debug_bounds") = false;
+  m.def("gemm_tn_bf16", &sb::gemm_tn_bf16, py::arg("A"), py::arg("B"), py::arg("bias"), py::arg("scale"),
+        py::arg("relu"), py::arg("out"), py::arg("cmax"), py::arg("status"), py::arg("max_ctas"),
+        py::arg("tmax") = py::none());
+  m.def("adam_bdec", &sb::adam_bdec);
+  m.def("adam_rows", &sb::adam_rows);
+  m.def("gemm_ag_tn_bf16", &sb::gemm_ag_tn_bf16, py::arg("x_own"), py::arg("peer_bases"), py::arg("rank"),
+        py::arg("x_off"), py::arg("flag_off"), py::arg("total_rows"), py::arg("m_base"), py::arg("M"), py::arg("push"),
+        py::arg("epoch"), py::arg("B"), py::arg("bias"), py::arg("scale"), py::arg("relu"), py::arg("out"),
+        py::arg("cmax"), py::arg("status"), py::arg("ticket"), py::arg("max_ctas"), py::arg("tmax") = py::none());
+  m.def("gemm_fsdp_tn_bf16", &sb::gemm_fsdp_tn_bf16, py::arg("A"), py::arg("w_own"), py::arg("peer_bases"),
+        py::arg("rank"), py::arg("w_off"), py::arg("flag_off"), py::arg("push"), py::arg("epoch"), py::arg("w2_own"),
+        py::arg("w2_off"), py::arg("flag2_off"), py::arg("bias"), py::arg("scale"), py::arg("relu"), py::arg("out"),
+        py::arg("cmax"), py::arg("status"), py::arg("ticket"), py::arg("max_ctas") = 0, py::arg("tmax") = py::none());
+  m.def("rmsnorm", &sb::rmsnorm);
   m.def("rope_", &sb::rope_);
   m.def("gated_act", &sb::gated_act);
   m.def("layernorm", &sb::layernorm);
@@ -240,4 +258,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_close", &sb::symm_close);
   m.def("symm_free", &sb::symm_free);
   m.def("tensor_at", &sb::tensor_at);
+#endif
 }

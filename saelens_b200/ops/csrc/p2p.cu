@@ -26,6 +26,7 @@
 #include "common.cuh"
 #include "p2p.cuh"
 #include "check.h"
+#include "bounds.cuh"
 
 namespace sb {
 namespace p2p {
@@ -363,6 +364,7 @@ __global__ void ring_gather_kernel(const __nv_bfloat16* __restrict__ data, int c
   const int warps = (gridDim.x * blockDim.x) >> 5;
   for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < rows; i += warps) {
     const int r = perm ? perm[i] : i;
+    if (!SB_IN_RANGE(r, chunk_rows)) continue;  // debug builds: a permutation entry past the chunk
     const uint4* s4 = reinterpret_cast<const uint4*>(base + int64_t(r) * D);
     uint4* o4 = reinterpret_cast<uint4*>(out + int64_t(i) * ldo);
     for (int v = lane; v < nvec; v += 32) o4[v] = __ldcg(s4 + v);
@@ -387,15 +389,15 @@ __global__ void wait_flags_kernel(const uint32_t* flags, int64_t n, uint32_t tar
 // Reference path replaced: NCCL batch_isend_irecv per route + cast/normalise passes
 // (sae_lens/training/activations_store.py:1482-1606, 1063; activation_scaler.py:16-23).
 // ---------------------------------------------------------------------------------------
-constexpr int RT_THREADS = 128;
-constexpr int RT_RR = 8;
+constexpr int RT_RR = 8;                 // rows per published chunk
+constexpr int RT_THREADS = 32 * RT_RR;   // one warp per row of a chunk
 constexpr int RT_MAX_ROUTES = 16;
-constexpr int RT_U = 8;  // vectors of 8 per thread: rows up to 8 * 8 * RT_THREADS = 8192 wide
 
 struct RouteArgs {
   const void* src;
   int src_f32;
   int64_t ld_src;
+  int64_t src_rows;  // rows of `src` (source row bound)
   int D;
   int n_routes;
   int r_src[RT_MAX_ROUTES];    // first source row
@@ -417,10 +419,13 @@ struct RouteArgs {
   int* status;
 };
 
+// One warp per row: the CTA's RT_RR warps each own one row of the chunk.  Pass 1 reads the row
+// (16-byte vectors) for its sum of squares, pass 2 re-reads it (from L1 / L2), scales, casts to
+// bf16 and stores it into the destination's landing slot over NVLink.  Then one system-scope fence
+// per thread, one barrier and one release per chunk.
 __global__ void __launch_bounds__(RT_THREADS) route_rows_kernel(const __grid_constant__ RouteArgs a) {
-  __shared__ float s_red[RT_THREADS / 32];
   __shared__ int s_ok;
-  const int t = threadIdx.x;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int nvec = a.D >> 3;
   if (a.epoch >= 3) {
     if (t == 0) {
@@ -441,60 +446,56 @@ __global__ void __launch_bounds__(RT_THREADS) route_rows_kernel(const __grid_con
     const int nr = min(RT_RR, a.r_rows[ri] - row0);
     const int dst_rank = a.r_rank[ri];
     __nv_bfloat16* land = at<__nv_bfloat16>(a.P, dst_rank, a.land_off) + (int64_t(a.slot) * a.rows_cap) * a.D;
-    for (int rr = 0; rr < nr; ++rr) {
-      const int64_t srow = a.r_src[ri] + row0 + rr;
-      const int64_t drow = a.r_dst[ri] + row0 + rr;
-      float v[8 * RT_U];  // the row, 8 elements per vector, RT_U vectors per thread
-      float ss = 0.f;
-#pragma unroll
-      for (int u = 0; u < RT_U; ++u) {
-        const int vi = u * RT_THREADS + t;
-        if (vi < nvec) {
-          if (a.src_f32) {
-            const float4* s4 =
-                reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.src) + srow * a.ld_src) + 2 * vi;
-            const float4 x0 = __ldg(s4), x1 = __ldg(s4 + 1);
-            v[8 * u + 0] = x0.x; v[8 * u + 1] = x0.y; v[8 * u + 2] = x0.z; v[8 * u + 3] = x0.w;
-            v[8 * u + 4] = x1.x; v[8 * u + 5] = x1.y; v[8 * u + 6] = x1.z; v[8 * u + 7] = x1.w;
-          } else {
-            const uint4 q = __ldg(
-                reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.src) + srow * a.ld_src) + vi);
-            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&q);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = __bfloat1622float2(h[e]);
-              v[8 * u + 2 * e] = f.x;
-              v[8 * u + 2 * e + 1] = f.y;
-            }
-          }
-#pragma unroll
-          for (int e = 0; e < 8; ++e) ss += v[8 * u + e] * v[8 * u + e];
-        }
-      }
-      float mul = a.mode == 1 ? a.scale : 1.f;
-      if (a.mode == 2) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if ((t & 31) == 0) s_red[t >> 5] = ss;
-        __syncthreads();
-        float tot = 0.f;
-        for (int w = 0; w < RT_THREADS / 32; ++w) tot += s_red[w];
-        __syncthreads();
-        mul = tot > 0.f ? a.scale * rsqrtf(tot) : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < RT_U; ++u) {
-        const int vi = u * RT_THREADS + t;
-        if (vi < nvec) {
-          uint4 q;
-          uint32_t* w = reinterpret_cast<uint32_t*>(&q);
+    if (warp < nr && SB_IN_RANGE(a.r_src[ri] + row0 + warp, a.src_rows) &&
+        SB_IN_RANGE(a.r_dst[ri] + row0 + warp, a.rows_cap)) {
+      const int64_t srow = a.r_src[ri] + row0 + warp;
+      const int64_t drow = a.r_dst[ri] + row0 + warp;
+      const float* sf = reinterpret_cast<const float*>(a.src) + srow * a.ld_src;
+      const __nv_bfloat16* sb = reinterpret_cast<const __nv_bfloat16*>(a.src) + srow * a.ld_src;
+      auto load8 = [&](int vi, float (&v)[8]) {
+        if (a.src_f32) {
+          const float4* s4 = reinterpret_cast<const float4*>(sf) + 2 * vi;
+          const float4 x0 = __ldg(s4), x1 = __ldg(s4 + 1);
+          v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
+          v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+        } else {
+          const uint4 q = __ldg(reinterpret_cast<const uint4*>(sb) + vi);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&q);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * u + 2 * e] * mul, v[8 * u + 2 * e + 1] * mul);
-            w[e] = *reinterpret_cast<uint32_t*>(&h);
+            const float2 f = __bfloat1622float2(h[e]);
+            v[2 * e] = f.x;
+            v[2 * e + 1] = f.y;
           }
-          reinterpret_cast<uint4*>(land + drow * a.D)[vi] = q;
         }
+      };
+      float mul = a.mode == 1 ? a.scale : 1.f;
+      if (a.mode == 2) {
+        float ss = 0.f;
+#pragma unroll 4
+        for (int vi = lane; vi < nvec; vi += 32) {
+          float v[8];
+          load8(vi, v);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        mul = ss > 0.f ? a.scale * rsqrtf(ss) : 0.f;
+      }
+      uint4* dst = reinterpret_cast<uint4*>(land + drow * a.D);
+#pragma unroll 4
+      for (int vi = lane; vi < nvec; vi += 32) {
+        float v[8];
+        load8(vi, v);
+        uint4 q;
+        uint32_t* w = reinterpret_cast<uint32_t*>(&q);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * e] * mul, v[2 * e + 1] * mul);
+          w[e] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        dst[vi] = q;
       }
     }
     __threadfence_system();
@@ -712,8 +713,7 @@ void p2p_route_rows(const torch::Tensor& src, const torch::Tensor& routes, const
                   routes.size(1) == 4 && routes.size(0) <= p2p::RT_MAX_ROUTES,
               "p2p_route_rows: routes must be a CPU int64 [n <= 16, 4] table");
   const int64_t D = src.size(1);
-  SB_CHECK(D % 8 == 0 && D <= p2p::RT_U * 8 * p2p::RT_THREADS,
-              "p2p_route_rows: d must be a multiple of 8 and <= 8192");
+  SB_CHECK(D % 8 == 0, "p2p_route_rows: d must be a multiple of 8");
   SB_CHECK(mode >= 0 && mode <= 2, "p2p_route_rows: mode");
   SB_CHECK(int64_t(free_slots.size()) == routes.size(0), "p2p_route_rows: free_slots");
   const at::cuda::CUDAGuard guard(src.device());
@@ -721,6 +721,7 @@ void p2p_route_rows(const torch::Tensor& src, const torch::Tensor& routes, const
   a.src = src.data_ptr();
   a.src_f32 = src.scalar_type() == at::kFloat ? 1 : 0;
   a.ld_src = src.stride(0);
+  a.src_rows = src.size(0);
   a.D = int(D);
   a.n_routes = int(routes.size(0));
   auto R = routes.accessor<int64_t, 2>();
@@ -750,7 +751,7 @@ void p2p_route_rows(const torch::Tensor& src, const torch::Tensor& routes, const
   a.epoch = uint32_t(epoch);
   a.status = status.data_ptr<int>();
   if (chunks == 0) return;
-  const int grid = std::min(chunks, p2p_sm_count() * 4);
+  const int grid = std::min(chunks, p2p_sm_count() * 8);
   p2p::route_rows_kernel<<<dim3(grid), dim3(p2p::RT_THREADS), 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -777,3 +778,10 @@ void p2p_signal(const std::vector<int64_t>& peer_bases, int64_t rank, int64_t of
 }
 
 }  // namespace sb
+
+#if SB_DEBUG_BOUNDS
+namespace sb {
+// {line, value, bound, violations} of this file's first bounds violation (debug module only).
+std::vector<int64_t> p2p_bounds_info(bool reset) { return bounds_read(reset); }
+}  // namespace sb
+#endif

@@ -24,6 +24,7 @@
 #include "common.cuh"
 #include "p2p.cuh"
 #include "check.h"
+#include "bounds.cuh"
 
 namespace sb {
 namespace sparse {
@@ -78,7 +79,7 @@ __global__ void __launch_bounds__(DEC_THREADS)
                       __nv_bfloat16* __restrict__ resid, int64_t ldr,
                       __nv_bfloat16* __restrict__ dxhat, int64_t ldd, const float* grad_coef_dev,
                       float grad_coef, float* __restrict__ loss_row, float* __restrict__ bsum,
-                      int M, int D) {
+                      int M, int D, int n_lat) {
   extern __shared__ float dsm[];
   float* s_a = dsm;                                  // k
   int* s_i = reinterpret_cast<int*>(dsm + k);        // k
@@ -97,7 +98,7 @@ __global__ void __launch_bounds__(DEC_THREADS)
     for (int i = t; i < k; i += DEC_THREADS) {
       const int j = idx[int64_t(row) * ldk + i];
       float a = 0.f;
-      if (j >= 0) {
+      if (j >= 0 && SB_IN_RANGE(j, n_lat)) {
         const float v = vals[int64_t(row) * ldk + i];
         a = (relu ? fmaxf(v, 0.f) : v) * (inv_scale ? __ldg(inv_scale + j) : 1.f);
       }
@@ -218,14 +219,14 @@ template <int VPT>
 __device__ __forceinline__ void decode_row_partial(int row, const float* __restrict__ vals,
                                                    const int* __restrict__ idx, int k, int64_t ldk, int relu,
                                                    const float* __restrict__ inv_scale,
-                                                   const __nv_bfloat16* __restrict__ W, int64_t ldw, int nvec,
-                                                   float* s_a, int* s_i, float (&acc)[VPT][8]) {
+                                                   const __nv_bfloat16* __restrict__ W, int64_t ldw, int n_lat,
+                                                   int nvec, float* s_a, int* s_i, float (&acc)[VPT][8]) {
   const int t = threadIdx.x;
   __syncthreads();
   for (int i = t; i < k; i += DEC_THREADS) {
     const int j = idx[int64_t(row) * ldk + i];
     float a = 0.f;
-    if (j >= 0) {
+    if (j >= 0 && SB_IN_RANGE(j, n_lat)) {
       const float v = vals[int64_t(row) * ldk + i];
       a = (relu ? fmaxf(v, 0.f) : v) * (inv_scale ? __ldg(inv_scale + j) : 1.f);
     }
@@ -284,7 +285,7 @@ template <int VPT>
 __global__ void __launch_bounds__(DEC_THREADS)
     decode_partial_kernel(const float* __restrict__ vals, const int* __restrict__ idx, int k, int64_t ldk,
                           int relu, const float* __restrict__ inv_scale, const __nv_bfloat16* __restrict__ W,
-                          int64_t ldw, float* __restrict__ out, int64_t ldo, int M, int D) {
+                          int64_t ldw, float* __restrict__ out, int64_t ldo, int M, int D, int n_lat) {
   extern __shared__ float dsm[];
   float* s_a = dsm;
   int* s_i = reinterpret_cast<int*>(dsm + k);
@@ -292,7 +293,7 @@ __global__ void __launch_bounds__(DEC_THREADS)
   const int t = threadIdx.x;
   for (int row = blockIdx.x; row < M; row += gridDim.x) {
     float acc[VPT][8];
-    decode_row_partial<VPT>(row, vals, idx, k, ldk, relu, inv_scale, W, ldw, nvec, s_a, s_i, acc);
+    decode_row_partial<VPT>(row, vals, idx, k, ldk, relu, inv_scale, W, ldw, n_lat, nvec, s_a, s_i, acc);
 #pragma unroll
     for (int v = 0; v < VPT; ++v) {
       const int vi = t + v * DEC_THREADS;
@@ -357,9 +358,9 @@ __global__ void __launch_bounds__(DEC_THREADS)
 // kept when its coefficient is non-zero.
 // ---------------------------------------------------------------------------------------
 __device__ __forceinline__ bool pair_live(const float* vals, const int* idx, int64_t p, int relu,
-                                          int& j) {
+                                          int n_lat, int& j) {
   j = idx[p];
-  if (j < 0) return false;
+  if (j < 0 || !SB_IN_RANGE(j, n_lat)) return false;
   const float v = vals[p];
   return relu ? (v > 0.f) : (v != 0.f);
 }
@@ -367,13 +368,14 @@ __device__ __forceinline__ bool pair_live(const float* vals, const int* idx, int
 __global__ void csc_count_kernel(const float* __restrict__ vals, const int* __restrict__ idx,
                                  int64_t n_main, const float* __restrict__ aux_vals,
                                  const int* __restrict__ aux_idx, int64_t n_aux,
-                                 int* __restrict__ counts, int* __restrict__ fire_counts) {
+                                 int* __restrict__ counts, int* __restrict__ fire_counts, int n_lat) {
   const int64_t total = n_main + n_aux;
   for (int64_t p = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; p < total;
        p += int64_t(gridDim.x) * blockDim.x) {
     int j;
     const bool main = p < n_main;
-    const bool live = main ? pair_live(vals, idx, p, 1, j) : pair_live(aux_vals, aux_idx, p - n_main, 0, j);
+    const bool live = main ? pair_live(vals, idx, p, 1, n_lat, j)
+                           : pair_live(aux_vals, aux_idx, p - n_main, 0, n_lat, j);
     if (live) {
       atomicAdd(counts + j, 1);
       if (main && fire_counts) atomicAdd(fire_counts + j, 1);
@@ -385,16 +387,18 @@ __global__ void csc_fill_kernel(const float* __restrict__ vals, const int* __res
                                 int64_t n_main, const float* __restrict__ aux_vals,
                                 const int* __restrict__ aux_idx, int64_t n_aux,
                                 const int64_t* __restrict__ colptr, int* __restrict__ cursor,
-                                int64_t* __restrict__ pairs) {
+                                int64_t* __restrict__ pairs, int n_lat, int64_t pairs_cap) {
   const int64_t total = n_main + n_aux;
   for (int64_t p = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; p < total;
        p += int64_t(gridDim.x) * blockDim.x) {
     int j;
     const bool main = p < n_main;
-    const bool live = main ? pair_live(vals, idx, p, 1, j) : pair_live(aux_vals, aux_idx, p - n_main, 0, j);
+    const bool live = main ? pair_live(vals, idx, p, 1, n_lat, j)
+                           : pair_live(aux_vals, aux_idx, p - n_main, 0, n_lat, j);
     if (live) {
       const int pos = atomicAdd(cursor + j, 1);
-      pairs[colptr[j] + pos] = p;
+      const int64_t dst = colptr[j] + pos;
+      if (SB_IN_RANGE(dst, pairs_cap)) pairs[dst] = p;
     }
   }
 }
@@ -411,6 +415,7 @@ constexpr int LG_GROUP = 4;
 struct LatentGradArgs {
   const int64_t* colptr;
   const int64_t* pairs;
+  int64_t P;  // entries of `pairs`
   int64_t n_main;
   int k, k_aux;
   const float* vals;       // [M, k]
@@ -450,8 +455,10 @@ __global__ void __launch_bounds__(LG_THREADS, 2) latent_grad_kernel(LatentGradAr
     for (int e = 0; e < 8; ++e) bt[v][e] = 0.f;
   float sq = 0.f;
 
+  const int64_t n_pair_ids = a.n_main + (a.aux_vals ? (a.n_main / a.k) * a.k_aux : 0);
   for (int j = blockIdx.x; j < a.N; j += gridDim.x) {
-    const int64_t beg = a.colptr[j], end = a.colptr[j + 1];
+    int64_t beg = a.colptr[j], end = a.colptr[j + 1];
+    if (!(SB_IN_RANGE(beg, a.P + 1) && SB_IN_RANGE(end, a.P + 1) && SB_IN_RANGE(end - beg, a.P + 1))) end = beg = 0;
     if (t == 0 && a.fire_counts) {
       const int fc = a.fire_counts[j];
       if (a.act_freq) a.act_freq[j] += float(fc);
@@ -480,10 +487,12 @@ __global__ void __launch_bounds__(LG_THREADS, 2) latent_grad_kernel(LatentGradAr
       const int cn = int((end - c0) < int64_t(LG_GROUP) ? (end - c0) : int64_t(LG_GROUP));
       __syncthreads();  // previous group's s_* reads are done
       if (t < cn) {
-        const int64_t p = a.pairs[c0 + t];
+        int64_t p = a.pairs[c0 + t];
+        const bool p_ok = SB_IN_RANGE(p, n_pair_ids);
+        if (!p_ok) p = 0;  // debug builds: stand-in pair with a zero coefficient
         if (p < a.n_main) {
           s_row[t] = p / a.k;
-          s_coef[t] = fmaxf(a.vals[p], 0.f) * isc;
+          s_coef[t] = p_ok ? fmaxf(a.vals[p], 0.f) * isc : 0.f;
           s_aux[t] = 0;
         } else {
           const int64_t q = p - a.n_main;
@@ -626,20 +635,19 @@ __global__ void __launch_bounds__(LG_THREADS, 2) latent_grad_kernel(LatentGradAr
 
 
 // ---------------------------------------------------------------------------------------
-// Fused tensor-parallel decode: one launch per rank, all ranks running concurrently.
-//   phase A (tickets [0, B/RB)): this rank's partial reconstruction of RB consecutive rows
-//           (from its own winners), stored straight into the row owner's landing area
-//           land[src = this rank][row - owner*Bo] with NVLink P2P stores, then one release-add
-//           on the owner's arrival counter of that row block.
-//   phase B (tickets [B/RB, B/RB + Bo/RB)): for a row block this rank owns, wait until all S
-//           sources arrived, reduce the S partials in rank order, add b_dec, and produce
-//           loss_row, sae_out, the residual, dL/dx_hat and its column sum; dL/dx_hat rows are
-//           stored into EVERY rank's dx buffer and published with one epoch flag per block.
-// Tickets come from one counter, so a phase-B block is claimed only after every phase-A block
-// has been claimed by a CTA that is running: no wait depends on a CTA that is not resident.
-// Phase A walks the owners starting at rank+1, so at any moment the ranks push to different
-// receivers.  Replaces the reference's dense decode + reduce-scatter + loss
-// (sae_lens/distributed.py:404-461, sae_lens/saes/topk_sae.py:645-674).
+// Tensor-parallel decode -> reduce-scatter, two launches per rank, all ranks running concurrently.
+//   phase A (its own launch, full occupancy, no waits): this rank's partial reconstruction of RB
+//           consecutive rows (from its own winners), stored straight into the row owner's landing
+//           area land[src = this rank][row - owner*Bo] with NVLink P2P stores, then one
+//           release-add on the owner's arrival counter of that row block.
+//   phase B (the next launch): for a row block this rank owns, wait until all S sources arrived,
+//           reduce the S partials in rank order, add b_dec, and produce loss_row, sae_out, the
+//           residual, dL/dx_hat and its column sum; dL/dx_hat rows are stored into EVERY rank's dx
+//           buffer and published with one epoch flag per block.
+// A phase-B wait depends only on the phase-A launches of the other GPUs (each GPU runs its own),
+// never on a CTA of the same launch.  Phase A walks the owners starting at rank+1, so at any
+// moment the ranks push to different receivers.  Replaces the reference's dense decode +
+// reduce-scatter + loss (sae_lens/distributed.py:404-461, sae_lens/saes/topk_sae.py:645-674).
 // ---------------------------------------------------------------------------------------
 constexpr int RS_RB = 16;
 
@@ -653,6 +661,7 @@ struct DecodeRsArgs {
   const __nv_bfloat16* W;
   int64_t ldw;
   int B, Bo, D;
+  int n_lat;  // rows of W (latent id bound)
   p2p::Peers P;
   int64_t land_off, lcnt_off, dx_off, dcnt_off;  // slab byte offsets; dx_off < 0: no broadcast
   uint32_t epoch;
@@ -669,7 +678,10 @@ struct DecodeRsArgs {
   int* status;
 };
 
-template <int VPT>
+// PHASE 0: one launch, both phases, work items from one ticket counter (phase-A tickets first, so a
+//          phase-B item is claimed only after every phase-A item has been claimed by a resident CTA);
+// PHASE 1: phase A only (static strided items); PHASE 2: phase B only (the following launch).
+template <int VPT, int PHASE>
 __global__ void __launch_bounds__(DEC_THREADS) decode_rs_kernel(const __grid_constant__ DecodeRsArgs a) {
   extern __shared__ float dsm[];
   float* s_a = dsm;
@@ -687,13 +699,18 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_rs_kernel(const __grid_con
 #pragma unroll
     for (int e = 0; e < 8; ++e) bacc[v][e] = 0.f;
 
-  while (true) {
+  for (int it = blockIdx.x;; it += gridDim.x) {
     __syncthreads();
-    if (t == 0) s_tk = atomicAdd(a.ticket, 1);
-    __syncthreads();
-    const int tk = s_tk;
-    if (tk >= nT) break;
-    if (tk < nA) {
+    int tk;
+    if (PHASE == 0) {
+      if (t == 0) s_tk = atomicAdd(a.ticket, 1);
+      __syncthreads();
+      tk = s_tk;
+    } else {
+      tk = PHASE == 1 ? it : nA + it;
+    }
+    if (tk >= (PHASE == 1 ? nA : nT)) break;
+    if (PHASE == 1 || (PHASE == 0 && tk < nA)) {  // compile-time split for PHASE 1 / 2
       // ---------------- phase A: partial rows -> owner ----------------
       const int blk = (tk + (r + 1) * nbo) % nA;
       const int o = blk / nbo, lb = blk - o * nbo;
@@ -701,7 +718,7 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_rs_kernel(const __grid_con
       for (int rr = 0; rr < RS_RB; ++rr) {
         float acc[VPT][8];
         decode_row_partial<VPT>(blk * RS_RB + rr, a.vals, a.idx, a.k, a.ldk, a.relu, a.inv_scale, a.W, a.ldw,
-                                nvec, s_a, s_i, acc);
+                                a.n_lat, nvec, s_a, s_i, acc);
 #pragma unroll
         for (int v = 0; v < VPT; ++v) {
           const int vi = t + v * DEC_THREADS;
@@ -784,7 +801,7 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_rs_kernel(const __grid_con
       }
     }
   }
-  if (a.bsum) {
+  if (PHASE != 1 && a.bsum) {
 #pragma unroll
     for (int v = 0; v < VPT; ++v) {
       const int vi = t + v * DEC_THREADS;
@@ -825,6 +842,7 @@ struct PairDzArgs {
   const __nv_bfloat16* daux;
   const __nv_bfloat16* W_dec;
   int D;
+  int N;          // latent id bound
   int* prow;      // [P] row | (aux << 31)
   float* pcoef;   // [P]
   float* pdz;     // [P]
@@ -845,9 +863,21 @@ __global__ void __launch_bounds__(LR_THREADS) pair_dz_kernel(const __grid_consta
   const int nvec = a.D >> 3;
   const int64_t nw = int64_t(gridDim.x) * LR_WARPS;
   const int64_t pend = min(*a.pos_end, a.P);
+  const int64_t n_pair_ids = a.n_main + (a.aux_vals ? (a.n_main / a.k) * a.k_aux : 0);
   for (int64_t pos = *a.pos_begin + ((int64_t(blockIdx.x) * LR_THREADS + threadIdx.x) >> 5); pos < pend;
        pos += nw) {
+    if (!SB_IN_RANGE(pos, a.P)) break;  // debug builds: a negative range start
     const int64_t p = a.pairs[pos];
+    if (!SB_IN_RANGE(p, n_pair_ids) ||
+        !SB_IN_RANGE(p < a.n_main ? a.idx[p] : a.aux_idx[p - a.n_main], a.N)) {
+      // debug builds: an entry that cannot be resolved contributes nothing (row 0, zero weights)
+      if ((threadIdx.x & 31) == 0) {
+        a.prow[pos] = 0;
+        a.pcoef[pos] = 0.f;
+        a.pdz[pos] = 0.f;
+      }
+      continue;
+    }
     int64_t b;
     int j, aux;
     float coef;
@@ -925,6 +955,8 @@ struct LatentRowsArgs {
   float* act_freq;
   float* since_fired;
   int N, D, nslices;
+  int M;           // rows of dxhat / daux / x (pair row bound)
+  int64_t n_pairs; // pair-list length (CSC offset bound)
   int j0, j1;      // latent range of this launch
   int zero_empty;  // write zero gradient rows for latents without a live pair (dense consumers)
   // Reduce-scatter destination (sharded data parallel): with rs_n > 0 the gradient rows of
@@ -966,7 +998,8 @@ __global__ void __launch_bounds__(LR_THREADS, 2) latent_rows_kernel(const __grid
   }
   float sq = 0.f;
   for (int j = a.j0 + gw / a.nslices; j < a.j1; j += tw / a.nslices) {
-    const int64_t beg = a.colptr[j], end = a.colptr[j + 1];
+    int64_t beg = a.colptr[j], end = a.colptr[j + 1];
+    if (!(SB_IN_RANGE(beg, a.n_pairs + 1) && SB_IN_RANGE(end, a.n_pairs + 1) && SB_IN_RANGE(end - beg, a.n_pairs + 1))) end = beg = 0;
     if (sl == 0 && lane == 0 && a.fire_counts) {
       const int fc = a.fire_counts[j];
       if (a.act_freq) a.act_freq[j] += float(fc);
@@ -994,9 +1027,11 @@ __global__ void __launch_bounds__(LR_THREADS, 2) latent_rows_kernel(const __grid
     float gbe = 0.f;
     for (int64_t pos = beg; pos < end; pos += 2) {
       const bool two = pos + 1 < end;
-      const int r0 = a.prow[pos], r1 = two ? a.prow[pos + 1] : r0;
-      const float c0 = a.pcoef[pos], c1 = two ? a.pcoef[pos + 1] : 0.f;
-      const float z0 = a.pdz[pos], z1 = two ? a.pdz[pos + 1] : 0.f;
+      int r0 = a.prow[pos], r1 = two ? a.prow[pos + 1] : r0;
+      float c0 = a.pcoef[pos], c1 = two ? a.pcoef[pos + 1] : 0.f;
+      float z0 = a.pdz[pos], z1 = two ? a.pdz[pos + 1] : 0.f;
+      if (!SB_IN_RANGE(r0 & 0x7fffffff, a.M)) r0 = 0, c0 = z0 = 0.f;  // debug builds: drop the entry
+      if (!SB_IN_RANGE(r1 & 0x7fffffff, a.M)) r1 = 0, c1 = z1 = 0.f;
       const __nv_bfloat16* g0 = ((r0 < 0) ? a.daux : a.dxhat) + int64_t(r0 & 0x7fffffff) * a.D;
       const __nv_bfloat16* g1 = ((r1 < 0) ? a.daux : a.dxhat) + int64_t(r1 & 0x7fffffff) * a.D;
       const __nv_bfloat16* x0 = a.x + int64_t(r0 & 0x7fffffff) * a.ldx;
@@ -1172,7 +1207,7 @@ void decode_mse(const torch::Tensor& vals, const torch::Tensor& idx, bool relu,
       reinterpret_cast<const __nv_bfloat16*>(W.data_ptr()), W.stride(0), pb,                      \
       reinterpret_cast<const __nv_bfloat16*>(target.data_ptr()), target.stride(0), po,             \
       out ? out->stride(0) : 0, pr, resid ? resid->stride(0) : 0, pd, dxhat ? dxhat->stride(0) : 0, \
-      pgc, float(grad_coef), pl, pbs, int(M), int(D))
+      pgc, float(grad_coef), pl, pbs, int(M), int(D), int(W.size(0)))
   switch (vpt) {
     case 1: SB_DEC(1); break;
     case 2: SB_DEC(2); break;
@@ -1197,7 +1232,7 @@ void csc_count(const torch::Tensor& vals, const torch::Tensor& idx,
   sparse::csc_count_kernel<<<dim3(grid), dim3(256), 0, at::cuda::getCurrentCUDAStream()>>>(
       vals.data_ptr<float>(), idx.data_ptr<int>(), n_main,
       aux_vals ? aux_vals->data_ptr<float>() : nullptr, aux_idx ? aux_idx->data_ptr<int>() : nullptr,
-      n_aux, counts.data_ptr<int>(), fire_counts ? fire_counts->data_ptr<int>() : nullptr);
+      n_aux, counts.data_ptr<int>(), fire_counts ? fire_counts->data_ptr<int>() : nullptr, int(counts.numel()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -1216,7 +1251,8 @@ void csc_fill(const torch::Tensor& vals, const torch::Tensor& idx,
   sparse::csc_fill_kernel<<<dim3(grid), dim3(256), 0, at::cuda::getCurrentCUDAStream()>>>(
       vals.data_ptr<float>(), idx.data_ptr<int>(), n_main,
       aux_vals ? aux_vals->data_ptr<float>() : nullptr, aux_idx ? aux_idx->data_ptr<int>() : nullptr,
-      n_aux, colptr.data_ptr<int64_t>(), cursor.data_ptr<int>(), pairs.data_ptr<int64_t>());
+      n_aux, colptr.data_ptr<int64_t>(), cursor.data_ptr<int>(), pairs.data_ptr<int64_t>(),
+      int(colptr.numel() - 1), pairs.numel());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -1241,6 +1277,7 @@ static void latent_grad_v1(const torch::Tensor& colptr, const torch::Tensor& pai
   sparse::LatentGradArgs a{};
   a.colptr = colptr.data_ptr<int64_t>();
   a.pairs = pairs.data_ptr<int64_t>();
+  a.P = pairs.numel();
   a.n_main = vals.numel();
   a.k = int(vals.size(1));
   a.k_aux = aux_vals ? int(aux_vals->size(1)) : 1;
@@ -1341,6 +1378,7 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
     pa.daux = daux ? reinterpret_cast<const __nv_bfloat16*>(daux->data_ptr()) : nullptr;
     pa.W_dec = reinterpret_cast<const __nv_bfloat16*>(W_dec.data_ptr());
     pa.D = int(D);
+    pa.N = int(N);
     pa.prow = prow.data_ptr<int>();
     pa.pcoef = pcoef.data_ptr<float>();
     pa.pdz = pdz.data_ptr<float>();
@@ -1397,6 +1435,8 @@ void latent_grad(const torch::Tensor& colptr, const torch::Tensor& pairs, const 
   a.N = int(N);
   a.D = int(D);
   a.nslices = ns;
+  a.M = int(x.size(0));
+  a.n_pairs = P;
   a.j0 = int(j0);
   a.j1 = int(j1);
   a.zero_empty = zero_empty ? 1 : 0;
@@ -1440,7 +1480,7 @@ void decode_partial(const torch::Tensor& vals, const torch::Tensor& idx, bool re
 #define SB_DP(V) sparse::decode_partial_kernel<V><<<dim3(grid), dim3(sparse::DEC_THREADS), smem, stream>>>( \
       vals.data_ptr<float>(), idx.data_ptr<int>(), int(k), vals.stride(0), relu ? 1 : 0, pinv,                  \
       reinterpret_cast<const __nv_bfloat16*>(W.data_ptr()), W.stride(0), out.data_ptr<float>(), out.stride(0),  \
-      int(M), int(D))
+      int(M), int(D), int(W.size(0)))
   switch (vpt) {
     case 1: SB_DP(1); break;
     case 2: SB_DP(2); break;
@@ -1516,6 +1556,7 @@ void decode_rs(const torch::Tensor& vals, const torch::Tensor& idx, bool relu,
   a.inv_scale = inv_scale ? inv_scale->data_ptr<float>() : nullptr;
   a.W = reinterpret_cast<const __nv_bfloat16*>(W.data_ptr());
   a.ldw = W.stride(0);
+  a.n_lat = int(W.size(0));
   a.B = int(B);
   a.Bo = int(Bo);
   a.D = int(D);
@@ -1536,21 +1577,48 @@ void decode_rs(const torch::Tensor& vals, const torch::Tensor& idx, bool relu,
   a.bsum = bsum ? bsum->data_ptr<float>() : nullptr;
   a.ticket = ticket.data_ptr<int>();
   a.status = status.data_ptr<int>();
-  C10_CUDA_CHECK(cudaMemsetAsync(a.ticket, 0, sizeof(int), stream));
   const size_t smem = size_t(2 * k + 32) * 4;
-  const int64_t tickets = B / sparse::RS_RB + Bo / sparse::RS_RB;
   const int nvec = int(D / 8);
-  auto launch = [&](auto kern) {
+  auto launch = [&](auto kern, int64_t work) {
     int occ = 0;
     C10_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, sparse::DEC_THREADS, smem));
-    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(tickets, int64_t(sm_count()) * std::max(occ, 1)));
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(work, int64_t(sm_count()) * std::max(occ, 1)));
     kern<<<dim3(grid), dim3(sparse::DEC_THREADS), smem, stream>>>(a);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
   };
-  if (nvec <= sparse::DEC_THREADS) launch(sparse::decode_rs_kernel<1>);
-  else if (nvec <= 2 * sparse::DEC_THREADS) launch(sparse::decode_rs_kernel<2>);
-  else if (nvec <= 4 * sparse::DEC_THREADS) launch(sparse::decode_rs_kernel<4>);
-  else launch(sparse::decode_rs_kernel<8>);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const int64_t nA = B / sparse::RS_RB, nB = Bo / sparse::RS_RB;
+  // SAELENS_B200_DECODE_RS=split: phase A and phase B as two launches (phase A at the occupancy of
+  // its own register count); default: one ticketed launch.
+  static const bool split = [] {
+    const char* e = std::getenv("SAELENS_B200_DECODE_RS");
+    return e && std::string(e) == "split";
+  }();
+  if (!split) C10_CUDA_CHECK(cudaMemsetAsync(a.ticket, 0, sizeof(int), stream));
+  auto run = [&](auto k0, auto k1, auto k2) {
+    if (split) {
+      launch(k1, nA);
+      launch(k2, nB);
+    } else {
+      launch(k0, nA + nB);
+    }
+  };
+  if (nvec <= sparse::DEC_THREADS) {
+    run(sparse::decode_rs_kernel<1, 0>, sparse::decode_rs_kernel<1, 1>, sparse::decode_rs_kernel<1, 2>);
+  } else if (nvec <= 2 * sparse::DEC_THREADS) {
+    run(sparse::decode_rs_kernel<2, 0>, sparse::decode_rs_kernel<2, 1>, sparse::decode_rs_kernel<2, 2>);
+  } else if (nvec <= 4 * sparse::DEC_THREADS) {
+    run(sparse::decode_rs_kernel<4, 0>, sparse::decode_rs_kernel<4, 1>, sparse::decode_rs_kernel<4, 2>);
+  } else {
+    run(sparse::decode_rs_kernel<8, 0>, sparse::decode_rs_kernel<8, 1>, sparse::decode_rs_kernel<8, 2>);
+  }
 }
 
+
 }  // namespace sb
+
+#if SB_DEBUG_BOUNDS
+namespace sb {
+// {line, value, bound, violations} of this file's first bounds violation (debug module only).
+std::vector<int64_t> sparse_bounds_info(bool reset) { return bounds_read(reset); }
+}  // namespace sb
+#endif

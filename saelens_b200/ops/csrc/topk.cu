@@ -26,6 +26,7 @@
 #include "common.cuh"
 #include "p2p.cuh"
 #include "check.h"
+#include "bounds.cuh"
 
 namespace sb {
 namespace topk {
@@ -324,7 +325,7 @@ __device__ __forceinline__ void merge_row(const float* cv, const int* ci, int64_
     const int s = c / k, i = c - s * k;
     const int64_t off = int64_t(s) * s_stride + i;
     const int li = __ldcg(ci + off);
-    if (li >= 0) {
+    if (li >= 0 && SB_IN_RANGE(li, n_local)) {  // debug builds: a peer id past its shard is dropped
       const uint32_t bits = __float_as_uint(__ldcg(cv + off)) >> 16;  // values are exact bf16
       key[c] = bf16_to_key(uint16_t(bits));
       gidx[c] = int64_t(s) * n_local + li;
@@ -939,3 +940,10 @@ void threshold_select(const torch::Tensor& H, const torch::Tensor& cmax, const t
 }
 
 }  // namespace sb
+
+#if SB_DEBUG_BOUNDS
+namespace sb {
+// {line, value, bound, violations} of this file's first bounds violation (debug module only).
+std::vector<int64_t> topk_bounds_info(bool reset) { return bounds_read(reset); }
+}  // namespace sb
+#endif

@@ -46,6 +46,9 @@ from saelens_b200.parallel.symm_heap import SlabBuffer, SymmetricHeap, slab_byte
 from saelens_b200.training.engine import EngineStepResult, FusedTopKEngine, update_topk_threshold_ema
 
 
+# decode -> reduce-scatter: one ticketed launch, or two with SAELENS_B200_DECODE_RS=split
+_DECODE_RS_LAUNCHES = 2 if os.environ.get("SAELENS_B200_DECODE_RS") == "split" else 1
+
 class _AllReduceBufs:
     """Slab areas of one two-shot P2P all-reduce of `n` elements."""
 
@@ -555,7 +558,7 @@ class TPTopKEngine(FusedTopKEngine):
         nat.decode_rs(vals, idx, True, self.inv_scale if self.rescale else None, self.w_dec, bases, r,
                       fb.land.offset, fb.lcnt.offset, fb.dx.offset, fb.dcnt.offset, ep, self.p_bdec, xb_own,
                       sae_out, resid, None, 2.0 / B, loss_row, bsum, tk, st)
-        self.launches += 1
+        self.launches += _DECODE_RS_LAUNCHES
         daux = None
         if aux_on:
             assert resid is not None
@@ -563,7 +566,7 @@ class TPTopKEngine(FusedTopKEngine):
             nat.decode_rs(aux_vals, aux_idx, False, self.inv_scale if self.rescale else None, self.w_dec,
                           fa.heap.bases, r, fa.land.offset, fa.lcnt.offset, fa.dx.offset, fa.dcnt.offset, ep_aux,
                           None, resid, None, None, None, 2.0 * self.aux_coef * aux_scale / B, aux_row, None, tk, st)
-            self.launches += 1
+            self.launches += _DECODE_RS_LAUNCHES
             red[2 * D + 2] = aux_row.sum()
             daux = fa.dx_local
         self._mark("decode_reduce_scatter_mse")

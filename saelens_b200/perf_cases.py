@@ -19,6 +19,12 @@
     python -m saelens_b200.perf_cases ddp [--d-sae 131072 --k 64 --batch 8192 --steps 10]
         Data-parallel TopK step (replicated SAE, P2P gradient all-reduce) under
         torch.distributed.run: ms/step (max over ranks) and per-phase times.
+    python -m saelens_b200.perf_cases fsdp-jumprelu [--d-in 3584 --d-sae 131072 --batch 4096]
+        Sharded data-parallel JumpReLU at its dense init: native engine vs torch FSDP(FULL_SHARD).
+    python -m saelens_b200.perf_cases attention [--batch 4 --ctx 2048 --heads 32 --kv-heads 8]
+        Causal GQA prefill attention: tcgen05 kernel vs PyTorch SDPA, ms and TFLOP/s.
+    python -m saelens_b200.perf_cases topology-switch --run-dir DIR --from-topo 1,2,4,1 --to-topo 1,4,4,1 ...
+        Streaming run under the topology supervisor with one switch: timeline, downtime, tokens/s.
 """
 
 from __future__ import annotations
@@ -27,6 +33,7 @@ import argparse
 import json
 import os
 from datetime import timedelta
+from typing import Any
 
 
 def _init_dist() -> tuple[int, int, int]:
@@ -632,6 +639,245 @@ def lm(args: argparse.Namespace) -> None:
     print(json.dumps(res), flush=True)
 
 
+def fsdp_jumprelu(args: argparse.Namespace) -> None:
+    """Sharded data-parallel JumpReLU at the dense init (threshold 0.001, bandwidth 0.001, L0
+    coefficient 1; default d_in 3584, d_sae 131072, 4096 rows per GPU): the native engine
+    (parameter all-gather fused into the encoder GEMM, reduce-scatter fused into the gradient GEMMs,
+    sharded Adam) against torch FSDP(FULL_SHARD) over NCCL with bf16 autocast and torch Adam, the
+    reference's wrapping (sae_lens/llm_sae_training_runner.py:449-463).  Device time from CUDA events
+    over the steps, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from saelens_b200.models.jumprelu import JumpReLUTrainingSAE, JumpReLUTrainingSAEConfig
+    from saelens_b200.models.sae import TrainStepInput
+    from saelens_b200.parallel.fsdp_jumprelu_engine import FSDPJumpReLUEngine
+    from saelens_b200.training.bench_driver import BenchSetup, synthetic_batch
+
+    world, rank, local = _init_dist()
+    dev = f"cuda:{local}"
+    x = synthetic_batch(BenchSetup(d_in=args.d_in, d_sae=args.d_sae, k=1, batch=args.batch, world=1, rank=rank),
+                        1 + rank, device="cuda")
+
+    def build() -> JumpReLUTrainingSAE:
+        torch.manual_seed(1234)
+        return JumpReLUTrainingSAE(JumpReLUTrainingSAEConfig(
+            d_in=args.d_in, d_sae=args.d_sae, jumprelu_init_threshold=0.001, jumprelu_bandwidth=0.001,
+            l0_coefficient=1.0, device=dev))
+
+    def timed(step) -> float:
+        for i in range(3):
+            step(i)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.steps):
+            step(i)
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / args.steps], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return round(float(t.item()), 3)
+
+    res: dict[str, float] = {}
+    eng = FSDPJumpReLUEngine(build(), lr=5e-5, group=dist.group.WORLD)
+    res["native"] = timed(lambda i: eng.step(x))
+    eng.status.check()
+    eng.close()
+    del eng
+    torch.cuda.empty_cache()
+    if not args.no_torch:
+        from torch.distributed.fsdp import FullyShardedDataParallel as FSDP
+        from torch.distributed.fsdp import ShardingStrategy
+
+        sae = build()
+        fs = FSDP(sae, sharding_strategy=ShardingStrategy.FULL_SHARD, device_id=torch.device(dev),
+                  use_orig_params=True)
+        opt = torch.optim.Adam(fs.parameters(), lr=5e-5)
+        xf = x.float()
+
+        def step(i: int) -> None:
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                out = fs(TrainStepInput(sae_in=xf, coefficients={"l0": 1.0}, dead_neuron_mask=None,
+                                        n_training_steps=i))
+            out.loss.backward()
+            fs.clip_grad_norm_(1.0)
+            opt.step()
+            opt.zero_grad(set_to_none=False)
+
+        res["torch_fsdp"] = timed(step)
+        del fs, opt, sae
+        torch.cuda.empty_cache()
+    if rank == 0:
+        print(json.dumps({"world": world, "arch": "jumprelu", "d_in": args.d_in, "d_sae": args.d_sae,
+                          "batch_per_gpu": args.batch, "ms_per_step": res,
+                          "tokens_per_s": {m: round(args.batch * world / v * 1e3, 1) for m, v in res.items()},
+                          "native": "bf16 compute, fp32 master + Adam state, sharded",
+                          "torch_fsdp": "fp32 params, bf16 autocast, FULL_SHARD over NCCL"}), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def attention_case(args: argparse.Namespace) -> None:
+    """Causal GQA prefill attention, one GPU: the tcgen05 kernel (`ops.attention`) against PyTorch
+    scaled_dot_product_attention (flash / cuDNN) on the same bf16 [B, S, H, D] inputs.  CUDA-event
+    ms per call after warm-up; TFLOP/s counts the causal half of QK^T and PV (2 B H S^2 D)."""
+    import torch
+    import torch.nn.functional as F
+
+    from saelens_b200 import ops
+
+    B, S, H, KV, D = args.batch, args.ctx, args.heads, args.kv_heads, args.head_dim
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randn(B, S, H, D, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(B, S, KV, D, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(B, S, KV, D, device="cuda", generator=g).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    st = ops.StatusWord("cuda")
+    scale = D ** -0.5
+
+    def ours() -> None:
+        ops.attention(q, k, v, scale, out=out, status=st)
+
+    qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+
+    def sdpa() -> None:
+        F.scaled_dot_product_attention(qt, kt, vt, is_causal=True, scale=scale, enable_gqa=True)
+
+    def timed(fn) -> float:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.reps
+
+    flops = 2.0 * B * H * S * S * D  # causal: half of 4 B H S^2 D
+    res = {"ours_ms": round(timed(ours), 4)}
+    st.check("attention")
+    if not args.no_sdpa:
+        res["sdpa_ms"] = round(timed(sdpa), 4)
+    res.update({k2.replace("_ms", "_tflops"): round(flops / v2 / 1e9, 1) for k2, v2 in list(res.items())})
+    ref = F.scaled_dot_product_attention(qt.float(), kt.float(), vt.float(), is_causal=True, scale=scale,
+                                         enable_gqa=True).transpose(1, 2)
+    ours()
+    res["max_abs_err_vs_fp32"] = float((out.float() - ref).abs().max())
+    print(json.dumps({"batch": B, "ctx": S, "heads": H, "kv_heads": KV, "head_dim": D, **res}), flush=True)
+
+
+def topology_switch(args: argparse.Namespace) -> None:
+    """Topology switch of a streaming run under the supervisor (scripts/topology_supervisor.py:366-517
+    in the reference): the worker group starts with `--from-topo`, a switch to `--to-topo` is
+    requested after `--steps-before` trainer steps, the supervisor quiesces (producer dataset
+    positions, SAE checkpoint, acks), relaunches from the quiesce checkpoint and the run completes.
+    Prints the supervisor's event timeline, the switch downtime (arrival time of the first trainer
+    step after the relaunch minus that of the last one before the quiesce) and the trainer's tokens/s
+    before and after (its own elapsed-time records).  Topologies are vllm_tp,vllm_dp,sae_tp,sae_dp;
+    every other `--field value` goes to the workers."""
+    import math
+    import signal
+    import subprocess
+    import threading
+    import time
+    from pathlib import Path
+
+    from saelens_b200.runners.topology_supervisor import (
+        TopologySupervisor,
+        build_torchrun_cmd,
+        request_topology_switch,
+    )
+    from saelens_b200.runners.worker import parse as parse_worker
+    from saelens_b200.topology_control import BufferParams, TopologySpec
+
+    def topo(spec: str) -> TopologySpec:
+        a = [int(v) for v in spec.split(",")]
+        return TopologySpec(*a)
+
+    run_dir = Path(args.run_dir)
+    ring_dir = Path(args.ring_dir)
+    run_dir.mkdir(parents=True, exist_ok=True)
+    ring_dir.mkdir(parents=True, exist_ok=True)
+    worker_cfg = list(args.worker_args)
+    if not any(a in ("--output_path", "--output-path") for a in worker_cfg):
+        worker_cfg += ["--output_path", str(run_dir / "out")]
+    worker_cfg += ["--streaming_buffer_dir", str(ring_dir)]
+    _, wcfg = parse_worker(worker_cfg)
+    out = Path(wcfg.output_path)
+    params = BufferParams(wcfg.streaming_num_chunks, wcfg.streaming_chunk_size_tokens, wcfg.sae.d_in,
+                          "float32" if wcfg.dtype in ("float32", "torch.float32") else "bfloat16")
+    target = math.ceil(wcfg.training_tokens / wcfg.streaming_chunk_size_tokens)
+    procs: list[subprocess.Popen] = []
+
+    def launch(state: Any) -> subprocess.Popen:
+        cmd = build_torchrun_cmd("-m saelens_b200.runners.worker", state.topology, run_dir, worker_cfg)
+        if state.checkpoint_path:
+            cmd += ["--resume-from-checkpoint", state.checkpoint_path]
+        log = open(run_dir / f"workers_{state.epoch}.log", "w")
+        p = subprocess.Popen(cmd, stdout=log, stderr=subprocess.STDOUT, start_new_session=True)
+        procs.append(p)
+        return p
+
+    sup = TopologySupervisor(run_dir, topo(args.from_topo), launch, buffer_name=f"sb_switch_{os.getpid()}",
+                             buffer_params=params, target_chunks=target, buffer_base_dir=str(ring_dir), poll_s=0.5,
+                             exit_timeout_s=120.0, ack_timeout_s=300.0)
+    result: dict[str, int] = {}
+    th = threading.Thread(target=lambda: result.setdefault("rc", sup.run()), daemon=True)
+    th.start()
+    hist = out / "timing_history.jsonl"
+    seen: list[tuple[float, dict]] = []  # (arrival wall time, record)
+
+    def poll() -> None:
+        if hist.exists():
+            for ln in hist.read_text().splitlines()[len(seen):]:
+                if ln.strip():
+                    seen.append((time.time(), json.loads(ln)))
+
+    t0, requested, n_before = time.time(), None, 0
+    try:
+        while th.is_alive():
+            poll()
+            if requested is None and len(seen) >= args.steps_before:
+                request_topology_switch(run_dir, topo(args.to_topo))
+                requested = time.time()
+            if time.time() - t0 > args.max_s:
+                raise SystemExit(f"topology switch run exceeded {args.max_s} s")
+            time.sleep(0.1)
+    finally:
+        for p in procs:  # the worker groups this case started, by their own process-group ids
+            if p.poll() is None:
+                os.killpg(p.pid, signal.SIGTERM)
+    poll()
+    events = [json.loads(x) for x in (run_dir / "topology_switch_log.jsonl").read_text().splitlines()]
+    t_quiesce = next((e["time"] for e in events if e["event"] == "quiesce_signaled"), None)
+    relaunch = [e["time"] for e in events if e["event"] == "workers_launched"][1:2]
+    before = [(w, r) for w, r in seen if t_quiesce is None or w < t_quiesce]
+    after = [(w, r) for w, r in seen if relaunch and w > relaunch[0]]
+    n_before = len(before)
+
+    def rate(recs: list[tuple[float, dict]]) -> float | None:
+        recs = recs[3:]  # skip the warm-up steps of a (re)launch
+        if len(recs) < 2:
+            return None
+        (_, a), (_, b) = recs[0], recs[-1]
+        dt = b["elapsed_s"] - a["elapsed_s"]
+        return round((b["n_training_samples"] - a["n_training_samples"]) / dt, 1) if dt > 0 else None
+
+    last_before = max((w for w, _ in seen if t_quiesce is not None and w < t_quiesce), default=None)
+    first_after = after[0][0] if after else None
+    print(json.dumps({
+        "from": args.from_topo, "to": args.to_topo, "rc": result.get("rc"),
+        "events": [{"event": e["event"], "t_s": round(e["time"] - events[0]["time"], 2)} for e in events],
+        "steps_before_switch": n_before, "steps_after_switch": len(after),
+        "downtime_s": round(first_after - last_before, 2) if (first_after and last_before) else None,
+        "tokens_per_s_before": rate(before), "tokens_per_s_after": rate(after),
+    }), flush=True)
+
+
 def main() -> None:
     p = argparse.ArgumentParser(prog="python -m saelens_b200.perf_cases")
     sub = p.add_subparsers(dest="cmd", required=True)
@@ -679,6 +925,27 @@ def main() -> None:
     rg.add_argument("--d", type=int, default=4096)
     rg.add_argument("--chunks", type=int, default=24)
     sub.add_parser("allreduce")
+    fj = sub.add_parser("fsdp-jumprelu", help="sharded data-parallel JumpReLU: native engine vs torch FSDP")
+    fj.add_argument("--d-in", type=int, default=3584)
+    fj.add_argument("--d-sae", type=int, default=131072)
+    fj.add_argument("--batch", type=int, default=4096)
+    fj.add_argument("--steps", type=int, default=10)
+    fj.add_argument("--no-torch", action="store_true", help="skip the torch FSDP comparison")
+    at = sub.add_parser("attention", help="causal GQA prefill attention: tcgen05 kernel vs PyTorch SDPA")
+    at.add_argument("--batch", type=int, default=4)
+    at.add_argument("--ctx", type=int, default=2048)
+    at.add_argument("--heads", type=int, default=32)
+    at.add_argument("--kv-heads", type=int, default=8)
+    at.add_argument("--head-dim", type=int, default=128)
+    at.add_argument("--reps", type=int, default=10)
+    at.add_argument("--no-sdpa", action="store_true", help="time only the tcgen05 kernel (profiling runs)")
+    ts = sub.add_parser("topology-switch", help="streaming run under the supervisor with one topology switch")
+    ts.add_argument("--run-dir", required=True)
+    ts.add_argument("--ring-dir", default="/dev/shm")
+    ts.add_argument("--from-topo", default="1,1,1,1", help="vllm_tp,vllm_dp,sae_tp,sae_dp")
+    ts.add_argument("--to-topo", default="1,2,1,1")
+    ts.add_argument("--steps-before", type=int, default=20)
+    ts.add_argument("--max-s", type=float, default=900.0)
     rt = sub.add_parser("router")
     rt.add_argument("--rows", type=int, default=8192)
     rt.add_argument("--d", type=int, default=4096)
@@ -695,9 +962,14 @@ def main() -> None:
     lmp.add_argument("--batch", type=int, default=8)
     lmp.add_argument("--ctx", type=int, default=1024)
     lmp.add_argument("--reps", type=int, default=5)
-    args = p.parse_args()
+    args, rest = p.parse_known_args()
+    if args.cmd == "topology-switch":
+        args.worker_args = rest
+    elif rest:
+        p.error(f"unrecognized arguments: {' '.join(rest)}")
     {"gemm-step": gemm_step, "lm": lm, "phases": phases, "fused-case": fused_case, "gemm": gemm, "ddp": ddp, "allreduce": allreduce, "router": router,
-     "tpdp": tpdp, "fsdp": ddp, "ddp-hook": ddp_hook, "ring": ring}[args.cmd](args)
+     "tpdp": tpdp, "fsdp": ddp, "ddp-hook": ddp_hook, "ring": ring, "fsdp-jumprelu": fsdp_jumprelu,
+     "attention": attention_case, "topology-switch": topology_switch}[args.cmd](args)
 
 
 if __name__ == "__main__":

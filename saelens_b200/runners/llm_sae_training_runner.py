@@ -15,6 +15,7 @@ from __future__ import annotations
 
 import json
 import os
+from datetime import timedelta
 import signal
 import sys
 from dataclasses import fields
@@ -157,13 +158,20 @@ class LanguageModelSAETrainingRunner:
 
     def _init_distributed(self) -> None:
         world = int(os.environ.get("WORLD_SIZE", "1"))
-        if world <= 1 or (self.sae_tp_size == 1 and self.sae_dp_size == 1 and self.vllm_dp_size <= 1):
+        single_layout = (self.sae_tp_size == 1 and self.sae_dp_size == 1 and self.vllm_dp_size <= 1
+                         and self.vllm_tp_size <= 1)
+        if world <= 1 or (single_layout and not self.use_shard_routing and not self.streaming_mode):
             return
         if not dist.is_initialized():
             backend = "nccl" if self.cfg.device.startswith("cuda") else "gloo"
+            kw: dict[str, Any] = {}
             if backend == "nccl":
-                torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-            dist.init_process_group(backend)
+                local = int(os.environ.get("LOCAL_RANK", "0"))
+                torch.cuda.set_device(local)
+                kw["device_id"] = torch.device("cuda", local)
+            # a short collective timeout: ranks left waiting on a rank that failed end with an error
+            kw["timeout"] = timedelta(seconds=float(os.environ.get("SAELENS_B200_PG_TIMEOUT_S", "300")))
+            dist.init_process_group(backend, **kw)
         from saelens_b200.parallel import distributed as D
 
         D.init_distributed(sae_tp_size=self.sae_tp_size, sae_dp_size=self.sae_dp_size,
@@ -367,6 +375,7 @@ class LanguageModelSAETrainingRunner:
             evaluator=self._evaluator() if self.activations_store is not None else None,
             save_checkpoint_fn=self._save_checkpoint_extras, dp_group=self.dp_group,
             token_count_weighted_dp=self.token_count_weighted_dp, native_fsdp=self.native_fsdp,
+            append_logs=self.resume_from_checkpoint is not None,  # a resumed run continues its histories
         )
         self.trainer = trainer
         if self.resume_from_checkpoint is not None:
@@ -423,7 +432,8 @@ class LanguageModelSAETrainingRunner:
                 cfg=cfg.to_sae_trainer_config(), sae=self.wrapped, base_sae=self.sae,
                 data_provider=RoutedProvider(ex, n_steps - done), evaluator=None,
                 save_checkpoint_fn=self._save_checkpoint_extras if self.activations_store is not None else None,
-                dp_group=self.dp_group, native_fsdp=self.native_fsdp)
+                dp_group=self.dp_group, native_fsdp=self.native_fsdp,
+                append_logs=self.resume_from_checkpoint is not None)
             self.trainer = trainer
             if self.resume_from_checkpoint is not None:
                 ck = Path(self.resume_from_checkpoint)

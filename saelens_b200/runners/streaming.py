@@ -22,6 +22,7 @@ from __future__ import annotations
 import math
 import os
 import time
+from datetime import timedelta
 from pathlib import Path
 from typing import Any
 
@@ -44,13 +45,20 @@ def streaming_init(runner: Any) -> None:
     cfg = runner.cfg
     if not dist.is_initialized():
         backend = "nccl" if str(cfg.device).startswith("cuda") and torch.cuda.is_available() else "gloo"
+        kw: dict[str, Any] = {}
         if backend == "nccl":
-            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-        dist.init_process_group(backend)
+            local = int(os.environ.get("LOCAL_RANK", "0"))
+            torch.cuda.set_device(local)
+            kw["device_id"] = torch.device("cuda", local)
+        # a short collective timeout: ranks left waiting on a rank that failed end with an error
+        kw["timeout"] = timedelta(seconds=float(os.environ.get("SAELENS_B200_PG_TIMEOUT_S", "300")))
+        dist.init_process_group(backend, **kw)
     vllm_tp, vllm_dp = max(runner.vllm_tp_size, 1), max(runner.vllm_dp_size, 1)
     sae_tp = max(runner.sae_tp_size, 1)
     ds.init_distributed_streaming(vllm_tp=vllm_tp, vllm_dp=vllm_dp, sae_tp=sae_tp, sae_dp=1)
     runner.role = "producer" if ds.is_producer() else "consumer"
+    # the consumer ranks form one SAE tensor-parallel group: the runner shards the SAE over it
+    runner.tp_group = ds.get_sae_tp_group() if sae_tp > 1 and not ds.is_producer() else None
     # producer tensor parallelism: every member runs the split LM, the group's first rank writes
     runner.producer_tp_group = ds.get_vllm_tp_group() if vllm_tp > 1 and ds.is_producer() else None
     runner.is_stream_writer = ds.is_producer() and ds.get_vllm_tp_rank() == 0
@@ -252,7 +260,8 @@ def run_consumer(runner: Any) -> Any:
             d_model=cfg.sae.d_in, dtype=str_to_dtype(cfg.dtype), shuffle=cfg.streaming_shuffle,
             random_chunks=cfg.streaming_random_chunks)
     trainer = SAETrainer(cfg=cfg.to_sae_trainer_config(), sae=runner.sae, base_sae=runner.sae, data_provider=provider,
-                         evaluator=None, save_checkpoint_fn=None)
+                         evaluator=None, save_checkpoint_fn=None,
+                         append_logs=runner.resume_from_checkpoint is not None)
     runner.trainer = trainer
     if runner.resume_from_checkpoint is not None:
         ck = Path(runner.resume_from_checkpoint)

@@ -17,7 +17,7 @@ def _port() -> int:
     return p
 
 
-def _worker(rank, world, port, tmp, vtp=1):
+def _worker(rank, world, port, tmp, vtp=1, stp=1):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
     import torch.distributed as dist
@@ -45,13 +45,14 @@ def _worker(rank, world, port, tmp, vtp=1):
         SharedActivationBuffer(f"ring_{port}", 4, 128, 64, num_producers=1, target_chunks=6, create=True,
                                base_dir=tmp, dtype=torch.float32).close()
     dist.barrier()
-    runner = LanguageModelSAETrainingRunner(cfg, override_model=lm, vllm_dp_size=1, vllm_tp_size=vtp)
+    runner = LanguageModelSAETrainingRunner(cfg, override_model=lm, vllm_dp_size=1, vllm_tp_size=vtp, sae_tp_size=stp)
     out = runner.run()
     info = {"role": runner.role, "transport": runner.streaming_transport,
             "lm_sharded": getattr(runner.model, "tp", None) is not None}
     if runner.role == "consumer":
         info["steps"] = runner.trainer.n_training_steps
         info["d_sae"] = int(out.W_dec.shape[0])
+        info["d_sae_local"] = int(runner.sae.W_dec.shape[0])
     with open(os.path.join(tmp, f"r{rank}.json"), "w") as f:
         json.dump(info, f)
     dist.destroy_process_group()
@@ -76,3 +77,15 @@ def test_streaming_with_tensor_parallel_producer(tmp_path):
     r = [json.loads((tmp_path / f"r{i}.json").read_text()) for i in range(3)]
     assert r[0]["role"] == r[1]["role"] == "producer" and r[0]["lm_sharded"] and r[1]["lm_sharded"]
     assert r[2]["role"] == "consumer" and r[2]["steps"] == 12
+
+
+def test_streaming_consumer_is_sae_tensor_parallel(tmp_path):
+    """Two consumer ranks form the SAE TP group: each trains its latent shard of the SAE, both train
+    every step, and the saved SAE is the gathered full dictionary (one timing / MSE writer)."""
+    mp.spawn(_worker, args=(3, _port(), str(tmp_path), 1, 2), nprocs=3, join=True)
+    r = [json.loads((tmp_path / f"r{i}.json").read_text()) for i in range(3)]
+    assert r[0]["role"] == "producer" and r[1]["role"] == r[2]["role"] == "consumer"
+    assert r[1]["d_sae_local"] == r[2]["d_sae_local"] == 64 and r[1]["steps"] == r[2]["steps"] == 12
+    out = tmp_path / "out"
+    rows = [json.loads(x) for x in (out / "mse_history.jsonl").read_text().splitlines()]
+    assert len(rows) == 12
