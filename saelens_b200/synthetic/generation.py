@@ -238,9 +238,7 @@ class HierarchyNode:
         return out
 
     def validate(self) -> None:
-        idx = self.get_all_feature_indices()
-        if len(idx) != len(set(idx)):
-            raise ValueError("a feature index appears more than once in the hierarchy")
+        validate_hierarchy([self])
 
     def __eq__(self, other: object) -> bool:
         return isinstance(other, HierarchyNode) and self.to_dict() == other.to_dict()
@@ -250,47 +248,131 @@ class HierarchyNode:
         return "\n".join([s] + [c.__repr__(indent + 2) for c in self.children])
 
 
-def hierarchy_modifier(roots: HierarchyNode | Sequence[HierarchyNode]) -> ActivationsModifier:
-    """Activations modifier enforcing the trees top-down, level by level (vectorised per parent group)."""
-    roots = [roots] if isinstance(roots, HierarchyNode) else list(roots)
-    for r in roots:
-        r.validate()
-    groups: list[tuple[int, HierarchyNode]] = []  # (depth, parent) in breadth-first order
+def validate_hierarchy(roots: Sequence[HierarchyNode]) -> None:
+    """A forest is valid when no node is its own ancestor, no node object sits in two children
+    lists (one parent per node), no feature index appears twice and every mutually exclusive node
+    has at least two children (sae_lens/synthetic/hierarchy/validation.py)."""
+    seen_nodes: set[int] = set()
+    seen_feats: set[int] = set()
 
-    def walk(n: HierarchyNode, depth: int) -> None:
-        if n.children:
-            groups.append((depth, n))
+    def visit(n: HierarchyNode, path: set[int]) -> None:
+        if id(n) in path:
+            raise ValueError(f"hierarchy has a loop through feature {n.feature_index}")
+        if id(n) in seen_nodes:
+            raise ValueError(f"hierarchy node for feature {n.feature_index} has more than one parent")
+        seen_nodes.add(id(n))
+        if n.feature_index is not None:
+            if n.feature_index in seen_feats:
+                raise ValueError(f"feature index {n.feature_index} appears more than once in the hierarchy")
+            seen_feats.add(n.feature_index)
+        if n.mutually_exclusive_children and len(n.children) < 2:
+            raise ValueError("mutual exclusion needs at least 2 children")
         for c in n.children:
-            walk(c, depth + 1)
+            visit(c, path | {id(n)})
 
     for r in roots:
-        walk(r, 0)
-    groups.sort(key=lambda g: g[0])
+        visit(r, set())
+
+
+class _HierarchyPlan:
+    """Index tensors of a validated forest, level by level (breadth-first depth of each node).
+
+    Every feature node gets an effective parent: the nearest ancestor that has a feature index
+    (-1 under a root or a chain of organisational nodes).  Its activation is gated by that parent
+    (x *= [parent > 0]), or rescaled (x *= parent / mean(parent)) when its immediate parent node has
+    scale_children_by_parent.  A mutually exclusive node's feature children form one group, applied
+    right after the gating of the node's own level: where more than one member is active (and the
+    group's effective parent is active) a uniformly random active member is kept."""
+
+    def __init__(self, roots: Sequence[HierarchyNode]):
+        feats: dict[int, list[tuple[int, int, bool]]] = {}
+        groups: dict[int, list[tuple[int, list[int]]]] = {}
+        queue: list[tuple[HierarchyNode, int, int]] = [(r, -1, 0) for r in roots]
+        head = 0
+        while head < len(queue):
+            node, eff_parent, level = queue[head]
+            head += 1
+            own = node.feature_index if node.feature_index is not None else eff_parent
+            for c in node.children:
+                if c.feature_index is not None:
+                    feats.setdefault(level + 1, []).append((c.feature_index, own, node.scale_children_by_parent))
+                queue.append((c, own, level + 1))
+            kids = [c.feature_index for c in node.children if c.feature_index is not None]
+            if node.mutually_exclusive_children and len(kids) >= 2:
+                groups.setdefault(level, []).append((own, kids))
+        self.levels = sorted(set(feats) | set(groups))
+        self.gate: dict[int, tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = {}
+        for lv, rows in feats.items():
+            rows = [r for r in rows if r[1] >= 0]
+            if rows:
+                self.gate[lv] = (torch.tensor([r[0] for r in rows]), torch.tensor([r[1] for r in rows]),
+                                 torch.tensor([r[2] for r in rows]))
+        self.me: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
+        for lv, gs in groups.items():
+            width = max(len(k) for _, k in gs)
+            sib = torch.full((len(gs), width), -1, dtype=torch.long)
+            for g, (_, kids) in enumerate(gs):
+                sib[g, : len(kids)] = torch.tensor(kids)
+            self.me[lv] = (sib, torch.tensor([p for p, _ in gs]))
+        self.any_rescale = any(bool(t[2].any()) for t in self.gate.values())
+        self._dev: Any = None
+
+    def to(self, device: Any) -> "_HierarchyPlan":
+        if self._dev != device:
+            self.gate = {k: tuple(t.to(device) for t in v) for k, v in self.gate.items()}  # type: ignore[misc]
+            self.me = {k: tuple(t.to(device) for t in v) for k, v in self.me.items()}  # type: ignore[misc]
+            self._dev = device
+        return self
+
+    def apply(self, x: torch.Tensor, means: torch.Tensor | None) -> None:
+        """Enforce the forest on dense activations `x` [batch, features] in place."""
+        if self.any_rescale and means is None:
+            raise ValueError("scale_children_by_parent needs the generator's mean firing magnitudes")
+        for lv in self.levels:
+            if lv in self.gate:
+                f, par, resc = self.gate[lv]
+                pa = x[:, par]
+                factor = (pa > 0).to(x.dtype)
+                if self.any_rescale:
+                    m = means.to(device=x.device, dtype=x.dtype)[par].clamp(min=1e-12)  # type: ignore[union-attr]
+                    factor = torch.where(resc, pa / m, factor)
+                x[:, f] = x[:, f] * factor
+            if lv in self.me:
+                self._exclude(x, *self.me[lv])
+
+    @staticmethod
+    def _exclude(x: torch.Tensor, sib: torch.Tensor, parents: torch.Tensor) -> None:
+        B = x.shape[0]
+        G, W = sib.shape
+        valid = sib >= 0
+        vals = x[:, sib.clamp(min=0).view(-1)].view(B, G, W)
+        active = (vals > 0) & valid
+        has_p = parents >= 0
+        if bool(has_p.any()):
+            p_on = (x[:, parents.clamp(min=0)] > 0) | ~has_p
+            active &= p_on.unsqueeze(2)
+        conflict = active.sum(2) > 1  # [B, G]
+        if not bool(conflict.any()):
+            return
+        score = torch.rand(B, G, W, device=x.device).masked_fill(~active, -1.0)
+        keep = torch.zeros_like(active).scatter_(2, score.argmax(2, keepdim=True), True)
+        drop = active & ~keep & conflict.unsqueeze(2)
+        b, g, w = drop.nonzero(as_tuple=True)
+        x[b, sib[g, w]] = 0
+
+
+def hierarchy_modifier(roots: HierarchyNode | Sequence[HierarchyNode]) -> ActivationsModifier:
+    """Activations modifier enforcing the trees (gating by effective parents, parent rescaling and
+    mutual exclusion, level by level); sparse COO input is densified and returned as COO
+    (sae_lens/synthetic/hierarchy/modifier.py)."""
+    roots = [roots] if isinstance(roots, HierarchyNode) else list(roots)
+    validate_hierarchy(roots)
+    plan = _HierarchyPlan(roots)
 
     def modifier(acts: torch.Tensor, gen: Any = None) -> torch.Tensor:
         sparse = acts.is_sparse
         x = acts.to_dense() if sparse else acts.clone()
-        means = getattr(gen, "mean_firing_magnitudes", None)
-        for _, parent in groups:
-            kids = [c.feature_index for c in parent.children if c.feature_index is not None]
-            if not kids:
-                continue
-            kid_idx = torch.tensor(kids, device=x.device)
-            if parent.feature_index is not None:
-                pa = x[:, parent.feature_index]
-                if parent.scale_children_by_parent:
-                    pm = float(means[parent.feature_index]) if means is not None else 1.0
-                    x[:, kid_idx] = x[:, kid_idx] * (pa / max(pm, 1e-12)).unsqueeze(1)
-                else:
-                    x[:, kid_idx] = x[:, kid_idx] * (pa > 0).to(x.dtype).unsqueeze(1)
-            if parent.mutually_exclusive_children and len(kids) > 1:
-                sub = x[:, kid_idx]
-                active = sub > 0
-                noise = torch.rand(sub.shape, device=x.device).masked_fill(~active, -1.0)
-                keep = noise.argmax(dim=1)
-                mask = torch.zeros_like(active)
-                mask[torch.arange(sub.shape[0], device=x.device), keep] = True
-                x[:, kid_idx] = sub * (mask & active).to(x.dtype)
+        plan.to(x.device).apply(x, getattr(gen, "mean_firing_magnitudes", None))
         return x.to_sparse() if sparse else x
 
     return modifier
