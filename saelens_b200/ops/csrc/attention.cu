@@ -18,9 +18,15 @@
 //               mask, running max and sum (online softmax), P_j as bf16 into shared memory in the
 //               K-major SWIZZLE_128B layout the MMA reads; O is rescaled in TMEM only when the row
 //               max grew by more than 2^8 since the last rescale (exact: the stale max only bounds
-//               P by 256), and at the end O / l is written out as bf16.
+//               P by 256), and at the end O / l is written out as bf16.  Only the tiles that cross
+//               the diagonal or the sequence end are masked; the row max and sum run as four
+//               independent chains.  (With SAELENS_B200_ATTN_WARPS=8, warps 2..9 take half a row
+//               each and exchange the row maxima and sums through shared memory on a bounded
+//               mbarrier; measured slightly slower, so four warps are the default.)
 // S_{j+1} is computed while the softmax works on S_j.  Every wait is bounded (status word).
 #include <ATen/cuda/CUDAContext.h>
+#include <cstdlib>
+#include <string>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
@@ -32,21 +38,28 @@ namespace sb {
 namespace attn {
 
 constexpr int BM = 128;
-constexpr int NUM_SOFTMAX_WARPS = 4;
-constexpr int NUM_THREADS = 64 + 32 * NUM_SOFTMAX_WARPS;
+// softmax warps: 4 (one per TMEM lane quadrant, whole rows) or 8 (two per quadrant, each with half
+// of the columns; the halves exchange row maxima and sums through shared memory)
+constexpr int threads_for(int smw) { return 64 + 32 * smw; }
 constexpr int KV_STAGES = 2;
 constexpr int TMEM_COLS = 512;
 constexpr float kRescaleThreshold = 8.f;  // log2 units: rescale O once the max grew by 2^8
 
-template <int D, int BN>
+template <int D, int BN, int SMW = 4>
 struct Cfg {
   static_assert(D % 64 == 0 && BN % 64 == 0, "tiles are made of 64-element swizzle rows");
   static_assert(2 * BN + D <= TMEM_COLS, "two S buffers and O must fit in TMEM");
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;  // one K or one V tile
   static constexpr int P_BYTES = BM * BN * 2;
-  static constexpr int NUM_BARS = 10;
-  static constexpr int SMEM = Q_BYTES + 2 * KV_STAGES * KV_BYTES + P_BYTES + 1024 + 8 * NUM_BARS + 16;
+  static constexpr int NUM_BARS = 11;
+  static constexpr int XBUF_FLOATS = 6 * BM;  // max exchange [2 tiles][2 halves][BM] + sums [2][BM]
+  static constexpr int SMEM = Q_BYTES + 2 * KV_STAGES * KV_BYTES + P_BYTES + 4 * XBUF_FLOATS + 1024 + 8 * NUM_BARS + 16;
+  static constexpr int HALVES = SMW / 4;
+  static constexpr int CW = BN / HALVES;  // S / P columns per softmax thread
+  static constexpr int DW = D / HALVES;   // O columns per softmax thread
+  static_assert(SMW == 4 || SMW == 8, "4 or 8 softmax warps");
+  static_assert(CW % 32 == 0 && DW % 32 == 0, "32-column TMEM loads");
 };
 
 struct Params {
@@ -59,18 +72,28 @@ struct Params {
   int* status;
 };
 
-template <int D, int BN>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+// 2^x with the hardware's approximate base-2 exponential (PTX ex2.approx.ftz.f32): P is rounded
+// to bf16 right after, far coarser than the instruction's error.
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// SOFTCAP is a template flag so the plain kernel carries no tanh code in its unrolled loops.
+template <int D, int BN, bool SOFTCAP, int SMW>
+__global__ void __launch_bounds__(threads_for(SMW), 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const Params p) {
-  using C = Cfg<D, BN>;
+  using C = Cfg<D, BN, SMW>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                // D/64 chunks of [BM rows x 128 B]
   uint8_t* sK = sQ + C::Q_BYTES;                     // stage s: D/64 chunks of [BN rows x 128 B]
   uint8_t* sV = sK + KV_STAGES * C::KV_BYTES;
   uint8_t* sP = sV + KV_STAGES * C::KV_BYTES;        // BN/64 chunks of [BM rows x 128 B]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + C::P_BYTES);
+  float* xbuf = reinterpret_cast<float*>(sP + C::P_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xbuf + C::XBUF_FLOATS);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;   // [2]
   uint64_t* kv_empty = bars + 3;  // [2]
@@ -78,6 +101,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* p_full = bars + 7;
   uint64_t* o_done = bars + 8;
   uint64_t* drain = bars + 9;
+  uint64_t* xchg = bars + 10;  // the softmax halves' exchange (8 softmax warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -97,7 +121,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
     }
-    mbar_init(p_full, NUM_SOFTMAX_WARPS * 32);
+    mbar_init(p_full, SMW * 32);
+    mbar_init(xchg, SMW * 32);
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -184,13 +209,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_wait_bounded(drain, 0, &keep_waiting, nullptr, 0);
     }
   } else {
-    // ------------------------------------------------------------ softmax (one row per thread)
+    // ------------------------------------------------------------ softmax
+    // warp w handles TMEM lane quadrant w % 4 (rows 32 (w % 4) ..), columns of its half
+    constexpr int HALVES = C::HALVES, CW = C::CW, DW = C::DW;
     const int quad = warp & 3;
+    const int half = (warp - 2) / 4;
     const int row = quad * 32 + lane;
     const int q_idx = q0 + row;
     const uint32_t lane_base = uint32_t(quad * 32) << 16;
+    const int col0 = half * CW;  // first S / P column of this thread
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
+    // the halves of a row meet once per tile (and once at the end) on the exchange barrier;
+    // a half that gave up stops arriving and the other's bounded wait ends too
+    auto exchange = [&](int phase) -> bool {
+      mbar_arrive(xchg);
+      return __all_sync(0xffffffffu, mbar_wait_bounded(xchg, phase & 1, abort_flag, p.status, kTimeoutEpilogue));
+    };
     for (int j = 0; j < n_kv; ++j) {
       const int s = j & 1;
       // warp-uniform outcome: the tcgen05.ld below is a whole-warp instruction
@@ -199,23 +234,51 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       tc_fence_after();
-      float v[BN];
-      float tmax = -INFINITY;
+      float v[CW];
+      // two 32-column loads in flight per wait; scale (or soft-cap) in place
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + lane_base + s * BN + c * 32, r);
+      for (int c = 0; c < CW / 32; c += 2) {
+        uint32_t r0[32], r1[32];
+        tmem_ld_32x32b_x32(tmem_base + lane_base + s * BN + col0 + c * 32, r0);
+        if (c + 1 < CW / 32) tmem_ld_32x32b_x32(tmem_base + lane_base + s * BN + col0 + (c + 1) * 32, r1);
         tmem_ld_wait();
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          const float x = __uint_as_float(r[e]);
-          float t = p.cap_log2 > 0.f ? p.cap_log2 * tanhf(x * p.scale_over_cap) : x * p.scale_log2;
-          const int kv_idx = j * BN + c * 32 + e;
-          if ((p.causal && kv_idx > q_idx) || kv_idx >= p.S) t = -INFINITY;
-          v[c * 32 + e] = t;
-          tmax = fmaxf(tmax, t);
+          if constexpr (SOFTCAP) {
+            v[c * 32 + e] = p.cap_log2 * tanhf(__uint_as_float(r0[e]) * p.scale_over_cap);
+            if (c + 1 < CW / 32) v[(c + 1) * 32 + e] = p.cap_log2 * tanhf(__uint_as_float(r1[e]) * p.scale_over_cap);
+          } else {
+            v[c * 32 + e] = __uint_as_float(r0[e]) * p.scale_log2;
+            if (c + 1 < CW / 32) v[(c + 1) * 32 + e] = __uint_as_float(r1[e]) * p.scale_log2;
+          }
         }
       }
+      // only tiles that cross the diagonal or the sequence end need the mask (warp-uniform test)
+      if ((p.causal && (j + 1) * BN - 1 > q0) || (j + 1) * BN > p.S) {
+        const int lim = min(p.causal ? q_idx : p.S - 1, p.S - 1) - j * BN - col0;  // last visible column
+#pragma unroll
+        for (int e = 0; e < CW; ++e)
+          if (e > lim) v[e] = -INFINITY;
+      }
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent chains
+#pragma unroll
+      for (int e = 0; e < CW; e += 4) {
+        mx[0] = fmaxf(mx[0], v[e]);
+        mx[1] = fmaxf(mx[1], v[e + 1]);
+        mx[2] = fmaxf(mx[2], v[e + 2]);
+        mx[3] = fmaxf(mx[3], v[e + 3]);
+      }
+      float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      if constexpr (HALVES == 2) {
+        float* xb = xbuf + (j & 1) * 2 * BM;  // alternate buffers: a half is at most one tile ahead
+        xb[half * BM + row] = tmax;
+        if (!exchange(j)) {
+          ok = false;
+          break;
+        }
+        tmax = fmaxf(tmax, xb[(half ^ 1) * BM + row]);
+      }
+      // both halves take the same decisions from the same row maximum
       bool need = false;
       float m_new = m_run;
       if (tmax > m_run + kRescaleThreshold) {
@@ -233,51 +296,58 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < DW / 32; ++c) {
             uint32_t r[32];
-            tmem_ld_32x32b_x32(tO + lane_base + c * 32, r);
+            tmem_ld_32x32b_x32(tO + lane_base + half * DW + c * 32, r);
             tmem_ld_wait();
 #pragma unroll
             for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-            tmem_st_32x32b_x32(tO + lane_base + c * 32, r);
+            tmem_st_32x32b_x32(tO + lane_base + half * DW + c * 32, r);
           }
           tmem_st_wait();
         }
       }
       l_run *= alpha;
       m_run = m_new;
-      float rowsum = 0.f;
+      float rs[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
 #pragma unroll
-      for (int cc = 0; cc < BN / 64; ++cc) {
-        uint8_t* prow = sP + cc * BM * 128 + row * 128;
+      for (int g8 = 0; g8 < CW / 8; ++g8) {  // one 16-byte granule (8 columns) per step
+        const int col = col0 + g8 * 8;
+        uint8_t* prow = sP + (col / 64) * BM * 128 + row * 128;
+        uint32_t packed[4];
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          uint32_t packed[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float e0 = exp2f(v[cc * 64 + g * 8 + 2 * i] - m_use);
-            const float e1 = exp2f(v[cc * 64 + g * 8 + 2 * i + 1] - m_use);
-            const __nv_bfloat162 h2 = __floats2bfloat162_rn(e0, e1);
-            rowsum += __low2float(h2) + __high2float(h2);
-            packed[i] = *reinterpret_cast<const uint32_t*>(&h2);
-          }
-          *reinterpret_cast<uint4*>(prow + ((g ^ (row & 7)) << 4)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        for (int i = 0; i < 4; ++i) {
+          const float e0 = ex2_fast(v[g8 * 8 + 2 * i] - m_use);
+          const float e1 = ex2_fast(v[g8 * 8 + 2 * i + 1] - m_use);
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(e0, e1);
+          rs[i] += __low2float(h2) + __high2float(h2);
+          packed[i] = *reinterpret_cast<const uint32_t*>(&h2);
         }
+        *reinterpret_cast<uint4*>(prow + ((((col % 64) / 8) ^ (row & 7)) << 4)) =
+            make_uint4(packed[0], packed[1], packed[2], packed[3]);
       }
-      l_run += rowsum;
+      l_run += (rs[0] + rs[1]) + (rs[2] + rs[3]);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
+    }
+    if constexpr (HALVES == 2) {
+      // the row sum is the sum of the halves' sums (both halves are here only if neither gave up)
+      if (ok) {
+        xbuf[4 * BM + half * BM + row] = l_run;
+        ok = exchange(n_kv);
+        if (ok) l_run += xbuf[4 * BM + (half ^ 1) * BM + row];
+      }
     }
     if (ok && n_kv > 0 &&
         __all_sync(0xffffffffu, mbar_wait_bounded(o_done, (n_kv - 1) & 1, abort_flag, p.status, kTimeoutEpilogue))) {
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      __nv_bfloat16* dst = p.out + ((int64_t(b) * p.S + q_idx) * p.H + h) * D;
+      __nv_bfloat16* dst = p.out + ((int64_t(b) * p.S + q_idx) * p.H + h) * D + half * DW;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < DW / 32; ++c) {
         uint32_t r[32];
-        tmem_ld_32x32b_x32(tO + lane_base + c * 32, r);
+        tmem_ld_32x32b_x32(tO + lane_base + half * DW + c * 32, r);
         tmem_ld_wait();
         uint32_t packed[16];
 #pragma unroll
@@ -303,9 +373,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
-template <int D, int BN>
+template <int D, int BN, bool SOFTCAP, int SMW>
 void launch(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const Params& prm) {
-  using C = Cfg<D, BN>;
+  using C = Cfg<D, BN, SMW>;
   const int B = prm.B, S = prm.S, H = prm.H, KV = prm.KV;
   const auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap tq = make_tmap_3d(q.data_ptr(), bf, 2, uint64_t(H) * D, S, B, q.stride(1) * 2, q.stride(0) * 2, 64, BM, 1,
@@ -314,14 +384,14 @@ void launch(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor&
                                 1, CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap tv = make_tmap_3d(v.data_ptr(), bf, 2, uint64_t(KV) * D, S, B, v.stride(1) * 2, v.stride(0) * 2, 64, BN,
                                 1, CU_TENSOR_MAP_SWIZZLE_128B);
-  auto kern = attn_fwd_kernel<D, BN>;
+  auto kern = attn_fwd_kernel<D, BN, SOFTCAP, SMW>;
   static bool attr_set = false;
   if (!attr_set) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_set = true;
   }
   const dim3 grid((S + BM - 1) / BM, H, B);
-  kern<<<grid, NUM_THREADS, C::SMEM, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, prm);
+  kern<<<grid, threads_for(SMW), C::SMEM, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, prm);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -362,11 +432,20 @@ void attention_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::
   prm.scale_over_cap = softcap > 0 ? float(scale / softcap) : 0.f;
   prm.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   prm.status = status.data_ptr<int>();
+  const bool cap = softcap > 0;
+  // default four softmax warps (whole rows: measured faster); SAELENS_B200_ATTN_WARPS=8 takes
+  // eight (half rows with exchanged row maxima and sums)
+  const char* w = std::getenv("SAELENS_B200_ATTN_WARPS");
+  const bool four = !(w && std::string(w) == "8");
+#define SB_ATTN(DD, BB)                                                                              \
+  (four ? (cap ? attn::launch<DD, BB, true, 4>(q, k, v, prm) : attn::launch<DD, BB, false, 4>(q, k, v, prm)) \
+        : (cap ? attn::launch<DD, BB, true, 8>(q, k, v, prm) : attn::launch<DD, BB, false, 8>(q, k, v, prm)))
   switch (D) {
-    case 64: attn::launch<64, 128>(q, k, v, prm); break;
-    case 128: attn::launch<128, 128>(q, k, v, prm); break;
-    default: attn::launch<256, 64>(q, k, v, prm); break;  // D == 256 (checked above)
+    case 64: SB_ATTN(64, 128); break;
+    case 128: SB_ATTN(128, 128); break;
+    default: SB_ATTN(256, 64); break;  // D == 256 (checked above)
   }
+#undef SB_ATTN
 }
 
 }  // namespace sb

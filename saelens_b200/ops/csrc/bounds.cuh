@@ -24,11 +24,17 @@
 namespace sb {
 
 #if SB_DEBUG_BOUNDS
-// [0] first violating source line + 1 (0: none), [1] its value, [2] its bound, [3] violations.
+// [0] first violating source line + 1 (0: none), [1] its value, [2] its bound, [3] violations
+// (distinct (line, value) per warp).
 // `static`: one record per translation unit (the module is built without relocatable device code).
 static __device__ unsigned long long g_bounds_rec[4];
 
+// Lanes of a warp that report the same (line, value) together (a warp checking one shared index)
+// count as one violation: the lowest such lane records it.
 static __device__ __noinline__ void bounds_record(long long v, long long n, int line) {
+  const unsigned long long key = (static_cast<unsigned long long>(line) << 44) ^ static_cast<unsigned long long>(v);
+  const unsigned same = __match_any_sync(__activemask(), key);
+  if ((threadIdx.x & 31) != __ffs(same) - 1) return;
   atomicAdd(&g_bounds_rec[3], 1ull);
   if (atomicCAS(&g_bounds_rec[0], 0ull, static_cast<unsigned long long>(line) + 1ull) == 0ull) {
     g_bounds_rec[1] = static_cast<unsigned long long>(v);

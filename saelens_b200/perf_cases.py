@@ -758,8 +758,11 @@ def attention_case(args: argparse.Namespace) -> None:
         return e0.elapsed_time(e1) / args.reps
 
     flops = 2.0 * B * H * S * S * D  # causal: half of 4 B H S^2 D
-    res = {"ours_ms": round(timed(ours), 4)}
-    st.check("attention")
+    res = {}
+    for w in ("8", "4"):  # softmax warps: half rows / whole rows (the default, timed last)
+        os.environ["SAELENS_B200_ATTN_WARPS"] = w
+        res[f"ours{w}_ms"] = round(timed(ours), 4)
+        st.check("attention")
     if not args.no_sdpa:
         res["sdpa_ms"] = round(timed(sdpa), 4)
     res.update({k2.replace("_ms", "_tflops"): round(flops / v2 / 1e9, 1) for k2, v2 in list(res.items())})

@@ -60,7 +60,13 @@ def main(argv: list[str] | None = None) -> Any:
         use_shard_routing=known.use_shard_routing, streaming_mode=True if known.streaming_mode else None)
     if known.run_dir is not None:
         runner.quiesce_dir = known.run_dir
-    return runner.run()
+    out = runner.run()
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized():  # every rank leaves together
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
 
 
 if __name__ == "__main__":

@@ -102,3 +102,20 @@ def test_rejects_unsupported_head_dim():
     q, k, v = _inputs(1, 128, 2, 2, 96, seed=1)
     with pytest.raises(ValueError, match="head dim must be 64, 128 or 256"):
         ops.attention(q, k, v, 0.1)
+
+
+@pytest.mark.parametrize("D, softcap", [(64, None), (128, None), (256, 30.0)])
+def test_four_and_eight_softmax_warps_agree(monkeypatch, D, softcap):
+    """The whole-row (4 softmax warps) and half-row (8 warps, exchanged row maxima and sums)
+    kernels both match the fp32 oracle, on a length with a partial last tile."""
+    from saelens_b200 import ops
+
+    q, k, v = _inputs(2, 333, 8, 4, D, seed=D)
+    scale = 1 / math.sqrt(D)
+    ref = _oracle(q, k, v, scale, softcap=softcap)
+    outs = {}
+    for w in ("4", "8"):
+        monkeypatch.setenv("SAELENS_B200_ATTN_WARPS", w)
+        outs[w] = ops.attention(q, k, v, scale, softcap=softcap)
+        _check(outs[w], ref)
+    assert (outs["4"].float() - outs["8"].float()).abs().max().item() <= 2e-2
