@@ -322,7 +322,9 @@ def main() -> None:
                        tp_exchange=args.tp_exchange)
     sampler = ClockSampler(list(range(torch.cuda.device_count()))[:world] if world > 1 else [local]) if rank == 0 else None
     dev = run_device_timed(setup, args.steps, args.warmup, sampler)
-    e2e = None if args.no_e2e else run_e2e(setup, args.steps, args.warmup)
+    e2e_sampler = ClockSampler(list(range(torch.cuda.device_count()))[:world] if world > 1 else [local]) \
+        if rank == 0 else None
+    e2e = None if args.no_e2e else run_e2e(setup, args.steps, args.warmup, e2e_sampler)
     if rank == 0:
         ms = dev["ms_per_step"]
         value = args.batch * 1000.0 / ms
@@ -346,7 +348,8 @@ def main() -> None:
                            "ms_per_step": round(e2e["ms_per_step"], 3),
                            "h2d_bytes_per_step": e2e["h2d_bytes"], "d2h_bytes_per_step": e2e["d2h_bytes"],
                            "input": "fp32 rows from pinned host memory, 8 distinct batches, copied on a side stream "
-                                    "(DevicePrefetcher) overlapping the previous step; loss read back every step"}
+                                    "(DevicePrefetcher) overlapping the previous step; loss read back every step",
+                           "clocks": e2e.get("clocks")}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -117,6 +117,8 @@ void ring_gather(const torch::Tensor& data, const torch::Tensor& slot, const c10
 void p2p_wait_flags(const torch::Tensor& flags, int64_t target, const torch::Tensor& status);
 std::tuple<int64_t, torch::Tensor> symm_alloc(int64_t nbytes);
 int64_t symm_open(const torch::Tensor& handle);
+int64_t host_register(int64_t ptr, int64_t bytes);
+int64_t host_unregister(int64_t ptr);
 void symm_close(int64_t addr);
 void symm_free(int64_t addr);
 torch::Tensor tensor_at(int64_t addr, std::vector<int64_t> sizes, torch::ScalarType dtype, int64_t device);
@@ -255,6 +257,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale"), py::arg("softcap"), py::arg("causal"), py::arg("status"));
   m.def("symm_alloc", &sb::symm_alloc);
   m.def("symm_open", &sb::symm_open);
+  m.def("host_register", &sb::host_register, py::arg("ptr"), py::arg("bytes"));
+  m.def("host_unregister", &sb::host_unregister, py::arg("ptr"));
   m.def("symm_close", &sb::symm_close);
   m.def("symm_free", &sb::symm_free);
   m.def("tensor_at", &sb::tensor_at);

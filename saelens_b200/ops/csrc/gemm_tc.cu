@@ -72,6 +72,7 @@ struct Epi {
   int64_t ldc;
   __nv_bfloat16* tmax;     // [M, ldt] tile maxima (one per 256 columns) or nullptr
   int64_t ldt;
+  int tma_out;             // 1: `out` is written by TMA tile stores from a per-warp staging tile
 };
 
 // Epilogue of the dense SAE steps (every field optional; order of application below).
@@ -383,10 +384,24 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mt
 // Epilogue of one accumulator tile: this thread's TMEM lane `trow` holds output row `row`
 // (columns nt*BN .. nt*BN+255): bias, per-column scale, ReLU, bf16 store, 32-column maxima.
 // Columns >= N (a partial last tile) are neither read from bias/scale nor stored.
-__device__ __forceinline__ void epilogue_tile(const Epi& ep, uint32_t trow, int row, int M, int N, int nt) {
+//
+// With `tmO` (CTA-pair kernel, ep.tma_out) the bf16 row chunk is not stored by the thread: the warp
+// writes its 32 rows x 64 columns into `stage` (4 KB, 1024-aligned, 128-byte swizzle: 16-byte
+// granule g of row r at granule g ^ (r % 8)) and one lane issues a TMA store of that box at
+// (column nt*BN + 64 g, row row0); the tensor map clips rows >= M and columns >= N (the host takes
+// this path only when N % 8 == 0, so every row ends on a 16-byte granule).  The staging
+// tile is reused once the previous box's shared-memory read has completed.
+__device__ __forceinline__ void epilogue_tile(const Epi& ep, uint32_t trow, int row, int M, int N, int nt,
+                                              const CUtensorMap* tmO = nullptr, uint8_t* stage = nullptr,
+                                              int row0 = 0, int lane = 0) {
   float tile_max = -INFINITY;
+  const bool tma = tmO != nullptr && ep.out != nullptr;
 #pragma unroll 1
   for (int c = 0; c < BN / 32; ++c) {
+    if (tma && (c & 1) == 0) {
+      if (lane == 0) bulk_wait_read_all();  // the staging tile is free again
+      __syncwarp();
+    }
     uint32_t r[32];
     tmem_ld_32x32b_x32(trow + c * 32, r);
     tmem_ld_wait();
@@ -443,8 +458,24 @@ __device__ __forceinline__ void epilogue_tile(const Epi& ep, uint32_t trow, int 
       if (full || col0 + 2 * j < N) cm = fmaxf(cm, __low2float(h2));
       if (full || col0 + 2 * j + 1 < N) cm = fmaxf(cm, __high2float(h2));
     }
+    if (tma) {
+      uint8_t* srow = stage + lane * 128;
+      const int g0 = (c & 1) * 4;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<uint4*>(srow + (((g0 + j) ^ (lane & 7)) << 4)) =
+            make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+      if ((c & 1) == 1 || col0 + 32 >= N) {  // the 64-column box is complete (or ends at N)
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(tmO, stage, nt * BN + (c & ~1) * 32, row0);
+          bulk_commit_group();
+        }
+      }
+    }
     if (row < M) {
-      if (ep.out) {
+      if (ep.out && !tma) {
         if (full) {
           uint4* dst = reinterpret_cast<uint4*>(ep.out + int64_t(row) * ep.ldo + col0);
 #pragma unroll
@@ -708,18 +739,21 @@ constexpr int PSTAGES = 6;
 constexpr int PA_BYTES = 128 * BK * 2;
 constexpr int PB_BYTES = 128 * BK * 2;
 constexpr int PSTAGE_BYTES = PA_BYTES + PB_BYTES;
-constexpr int PSMEM_BYTES = PSTAGES * PSTAGE_BYTES + 1024 + 256;
+constexpr int POUT_BYTES = 32 * 128;  // one epilogue warp's staging tile (32 rows x 64 bf16)
+constexpr int PSMEM_BYTES = PSTAGES * PSTAGE_BYTES + NUM_EPI_WARPS * POUT_BYTES + 1024 + 256;
 
 template <bool AG>
 __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
-                     int N, int K, Epi ep, int* status, const __grid_constant__ Ag ag) {
+                     int N, int K, Epi ep, int* status, const __grid_constant__ Ag ag,
+                     const __grid_constant__ CUtensorMap tmO) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + PSTAGES * PA_BYTES;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + PSTAGES * PB_BYTES);
+  uint8_t* sOut = sB + PSTAGES * PB_BYTES;  // NUM_EPI_WARPS staging tiles of 32 rows x 128 B (TMA stores)
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sOut + NUM_EPI_WARPS * POUT_BYTES);
   uint64_t* empty_bar = full_bar + PSTAGES;
   uint64_t* tfull_bar = empty_bar + PSTAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -861,13 +895,16 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
       const uint32_t aph = (tc >> 1) & 1;
       if (!mbar_wait_bounded(&tfull_bar[acc], aph, abort_flag, status, kTimeoutEpilogue)) break;
       tc_fence_after();
-      const int row = mt * 2 * BM + int(cta) * BM + q * 32 + lane;
+      const int row0 = mt * 2 * BM + int(cta) * BM + q * 32;
+      const int row = row0 + lane;
       const uint32_t trow = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
-      epilogue_tile(ep, trow, row, M, N, nt);
+      epilogue_tile(ep, trow, row, M, N, nt, ep.tma_out ? &tmO : nullptr, sOut + (warp - 2) * POUT_BYTES, row0,
+                    lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
     }
+    if (ep.tma_out && lane == 0) bulk_wait_all();  // the tile stores have landed before the CTA ends
   }
 
   tc_fence_before();
@@ -994,7 +1031,20 @@ static void launch_gemm(const void* a_ptr, int64_t lda, int64_t M, const torch::
   int64_t pairs = std::min<int64_t>(tiles, max_pairs);
   if (max_ctas > 0) pairs = std::max<int64_t>(1, std::min<int64_t>(pairs, max_ctas / 2));
   cfg.gridDim = dim3(unsigned(2 * pairs));
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tA, tB, iM, iN, iK, ep, st, ag));
+  // TMA tile stores of `out` (SAELENS_B200_GEMM_TMA_STORE=0 keeps the per-thread row stores)
+  gemm::Epi epp = ep;
+  CUtensorMap tO = tA;  // unused unless epp.tma_out
+  const char* ts = std::getenv("SAELENS_B200_GEMM_TMA_STORE");
+  // rows must end on a 16-byte boundary (N % 8 == 0): the store writes whole 16-byte granules, so a
+  // ragged row end would also write the padding past N
+  const bool tma_ok = !(ts && ts[0] == '0' && ts[1] == 0) && ep.out != nullptr && (ep.ldo * 2) % 16 == 0 &&
+                      reinterpret_cast<uintptr_t>(ep.out) % 16 == 0 && N % 8 == 0;
+  if (tma_ok) {
+    tO = make_tmap_2d(ep.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, N, ep.ldo * 2, 32, 64,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    epp.tma_out = 1;
+  }
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tA, tB, iM, iN, iK, epp, st, ag, tO));
 }
 
 // out = epilogue(A @ B^T).  A: [M, K] bf16 (row stride lda), B: [N, K] bf16.  Optional

@@ -26,6 +26,22 @@ std::tuple<int64_t, torch::Tensor> symm_alloc(int64_t nbytes) {
   return {reinterpret_cast<int64_t>(p), t};
 }
 
+// Page-locks [ptr, ptr + bytes) of host memory (for example a shared-memory activation ring mapped
+// by several processes) for the copy engines of every device (cudaHostRegisterPortable).  Returns
+// the cudaError_t code; a refusal (a mapping the driver cannot pin) leaves no error pending for the
+// next CUDA call.
+int64_t host_register(int64_t ptr, int64_t bytes) {
+  const cudaError_t e = cudaHostRegister(reinterpret_cast<void*>(ptr), size_t(bytes), cudaHostRegisterPortable);
+  if (e != cudaSuccess) (void)cudaGetLastError();
+  return int64_t(e);
+}
+
+int64_t host_unregister(int64_t ptr) {
+  const cudaError_t e = cudaHostUnregister(reinterpret_cast<void*>(ptr));
+  if (e != cudaSuccess) (void)cudaGetLastError();
+  return int64_t(e);
+}
+
 // Maps a peer's slab into this process (peer access is enabled lazily by the driver).
 int64_t symm_open(const torch::Tensor& handle) {
   SB_CHECK(handle.numel() == int64_t(sizeof(cudaIpcMemHandle_t)) && handle.scalar_type() == torch::kUInt8,

@@ -25,6 +25,8 @@
         Causal GQA prefill attention: tcgen05 kernel vs PyTorch SDPA, ms and TFLOP/s.
     python -m saelens_b200.perf_cases topology-switch --run-dir DIR --from-topo 1,2,4,1 --to-topo 1,4,4,1 ...
         Streaming run under the topology supervisor with one switch: timeline, downtime, tokens/s.
+    python -m saelens_b200.perf_cases dense-step [--d-in 2304 --d-sae 65536 --batch 4096]
+        Standard and Gated training steps: native dense engines vs the PyTorch (cuBLAS) path.
 """
 
 from __future__ import annotations
@@ -253,9 +255,13 @@ def gemm_step(args: argparse.Namespace) -> None:
         return e0.elapsed_time(e1) / args.reps, (mhz[len(mhz) // 2] if mhz else None)
 
     res = {}
-    for name, pair, fn in (("pair_full", "1", ours(True)), ("pair_nostore", "1", ours(False)),
-                           ("single_full", "0", ours(True)), ("cublas", "1", cublas)):
+    # pair_full stores H with TMA tile stores from a staging tile; pair_full_rowstores with the
+    # per-thread row stores (SAELENS_B200_GEMM_TMA_STORE=0)
+    for name, pair, tma, fn in (("pair_full", "1", "1", ours(True)), ("pair_full_rowstores", "1", "0", ours(True)),
+                                ("pair_nostore", "1", "1", ours(False)), ("single_full", "0", "1", ours(True)),
+                                ("cublas", "1", "1", cublas)):
         os.environ["SAELENS_B200_GEMM_PAIR"] = pair
+        os.environ["SAELENS_B200_GEMM_TMA_STORE"] = tma
         ms, mhz = timed(fn)
         st.check(name)
         res[name] = {"ms": round(ms, 3), "tflops": round(2 * M * N * K / ms / 1e9, 1), "sm_mhz": mhz}
@@ -881,6 +887,66 @@ def topology_switch(args: argparse.Namespace) -> None:
     }), flush=True)
 
 
+def dense_step(args: argparse.Namespace) -> None:
+    """Standard (ReLU + L1) and Gated SAE training steps, one GPU: the native dense engines
+    (tcgen05 GEMMs with fused epilogues, row-fused Adam) against the PyTorch path on the same
+    shapes (fp32 parameters, bf16 autocast, cuBLAS GEMMs through autograd, torch Adam, clip 1.0).
+    CUDA-event ms per step after 3 warm-up steps."""
+    import torch
+
+    from saelens_b200.models.gated import GatedTrainingSAE, GatedTrainingSAEConfig
+    from saelens_b200.models.sae import TrainStepInput
+    from saelens_b200.models.standard import StandardTrainingSAE, StandardTrainingSAEConfig
+    from saelens_b200.training.bench_driver import BenchSetup, synthetic_batch
+    from saelens_b200.training.dense_engine import GatedEngine, StandardEngine
+
+    x = synthetic_batch(BenchSetup(d_in=args.d_in, d_sae=args.d_sae, k=1, batch=args.batch, world=1, rank=0), 1,
+                        device="cuda")
+    xf = x.float()
+
+    def timed(step) -> float:
+        for i in range(3):
+            step(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.steps):
+            step(i)
+        e1.record()
+        torch.cuda.synchronize()
+        return round(e0.elapsed_time(e1) / args.steps, 3)
+
+    res: dict[str, dict[str, float]] = {}
+    for arch, cls, cfg_cls, eng_cls, coef in (
+            ("standard", StandardTrainingSAE, StandardTrainingSAEConfig, StandardEngine, {"l1": 5.0}),
+            ("gated", GatedTrainingSAE, GatedTrainingSAEConfig, GatedEngine, {"l1": 5.0})):
+        torch.manual_seed(0)
+        eng = eng_cls(cls(cfg_cls(d_in=args.d_in, d_sae=args.d_sae, l1_coefficient=5.0, device="cuda")), lr=5e-5)
+        native = timed(lambda i: eng.step(x))
+        eng.status.check(arch)
+        del eng
+        torch.cuda.empty_cache()
+        torch.manual_seed(0)
+        sae = cls(cfg_cls(d_in=args.d_in, d_sae=args.d_sae, l1_coefficient=5.0, device="cuda"))
+        opt = torch.optim.Adam(sae.parameters(), lr=5e-5)
+
+        def step(i: int) -> None:
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                out = sae.training_forward_pass(TrainStepInput(sae_in=xf, coefficients=coef, dead_neuron_mask=None,
+                                                               n_training_steps=i))
+            out.loss.backward()
+            sae.clip_grad_norm_(1.0)
+            opt.step()
+            opt.zero_grad(set_to_none=False)
+
+        torch_ms = timed(step)
+        del sae, opt
+        torch.cuda.empty_cache()
+        res[arch] = {"native_ms": native, "torch_ms": torch_ms, "speedup": round(torch_ms / native, 2),
+                     "native_tokens_per_s": round(args.batch / native * 1e3, 1)}
+    print(json.dumps({"d_in": args.d_in, "d_sae": args.d_sae, "batch": args.batch, **res}), flush=True)
+
+
 def main() -> None:
     p = argparse.ArgumentParser(prog="python -m saelens_b200.perf_cases")
     sub = p.add_subparsers(dest="cmd", required=True)
@@ -949,6 +1015,11 @@ def main() -> None:
     ts.add_argument("--to-topo", default="1,2,1,1")
     ts.add_argument("--steps-before", type=int, default=20)
     ts.add_argument("--max-s", type=float, default=900.0)
+    dsp = sub.add_parser("dense-step", help="Standard / Gated steps: native dense engines vs the PyTorch path")
+    dsp.add_argument("--d-in", type=int, default=2304)
+    dsp.add_argument("--d-sae", type=int, default=65536)
+    dsp.add_argument("--batch", type=int, default=4096)
+    dsp.add_argument("--steps", type=int, default=10)
     rt = sub.add_parser("router")
     rt.add_argument("--rows", type=int, default=8192)
     rt.add_argument("--d", type=int, default=4096)
@@ -972,7 +1043,7 @@ def main() -> None:
         p.error(f"unrecognized arguments: {' '.join(rest)}")
     {"gemm-step": gemm_step, "lm": lm, "phases": phases, "fused-case": fused_case, "gemm": gemm, "ddp": ddp, "allreduce": allreduce, "router": router,
      "tpdp": tpdp, "fsdp": ddp, "ddp-hook": ddp_hook, "ring": ring, "fsdp-jumprelu": fsdp_jumprelu,
-     "attention": attention_case, "topology-switch": topology_switch}[args.cmd](args)
+     "attention": attention_case, "topology-switch": topology_switch, "dense-step": dense_step}[args.cmd](args)
 
 
 if __name__ == "__main__":

@@ -91,6 +91,10 @@ def streaming_init(runner: Any) -> None:
         dist.barrier()
         if runner.shm_buffer is None:
             runner.shm_buffer = SharedActivationBuffer(create=False, **kw)
+        if str(cfg.device).startswith("cuda") and torch.cuda.is_available():
+            # page-locked ring: producers copy device rows straight into their slot, the trainer
+            # copies claimed slots straight to its GPU (no pageable host copy in between)
+            runner.shm_buffer.register_for_device_copies()
 
 
 def _quiesce_dir(runner: Any) -> Path | None:
@@ -170,7 +174,8 @@ def run_producer(runner: Any) -> int:
                     stop = "quiesce" if requested() else "end"
                     continue
                 idx, _ = got
-                buf.write_chunk(idx, acts.detach().to("cpu"), valid, producer_id=pidx)
+                buf.write_chunk(idx, acts.detach() if buf.registered else acts.detach().to("cpu"), valid,
+                                producer_id=pidx)
                 buf.mark_ready(idx)
             written += 1
         seq += P

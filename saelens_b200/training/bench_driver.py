@@ -162,7 +162,7 @@ class PinnedBatches:
         return b
 
 
-def run_e2e(s: BenchSetup, steps: int, warmup: int) -> dict[str, Any]:
+def run_e2e(s: BenchSetup, steps: int, warmup: int, sampler: Any = None) -> dict[str, Any]:
     from saelens_b200.config import LoggingConfig, SAETrainerConfig
     from saelens_b200.training.sae_trainer import SAETrainer
 
@@ -189,6 +189,8 @@ def run_e2e(s: BenchSetup, steps: int, warmup: int) -> dict[str, Any]:
     trainer.fit_steps(warmup)
     torch.cuda.synchronize()
     _barrier(s.world)
+    if sampler is not None:
+        sampler.start()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
@@ -196,13 +198,14 @@ def run_e2e(s: BenchSetup, steps: int, warmup: int) -> dict[str, Any]:
     t1.record()
     torch.cuda.synchronize()
     _barrier(s.world)
+    clocks = sampler.stop() if sampler is not None else None
     ms = _max_over_ranks(t0.elapsed_time(t1) / steps, s.world)
     h2d = rows_local * s.d_in * 4  # fp32 rows from pinned host memory
     if hasattr(trainer.engine, "close"):
         trainer.engine.close()
     del trainer, sae, data
     _free()
-    return {"ms_per_step": ms, "h2d_bytes": h2d, "d2h_bytes": 4}
+    return {"ms_per_step": ms, "h2d_bytes": h2d, "d2h_bytes": 4, "clocks": clocks}
 
 
 def parity_check(world: int, rank: int, d_in: int = 4096, d_sae: int = 16384, k: int = 128, batch: int = 2048,

@@ -13,6 +13,12 @@ Layout (this package's own, two memory-mapped files plus a lock file in `base_di
   {name}.dat   raw rows [num_slots, chunk_tokens, d_model] (bf16 bit patterns or fp32)
   {name}.lock  empty file for fcntl.flock
 `reset_for_restart` lets a supervisor recycle abandoned WRITING slots between worker launches.
+
+On a CUDA process `register_for_device_copies()` page-locks the data mapping for the copy engines
+(cudaHostRegister): a producer then copies device activations straight into its slot and a trainer
+copies claimed slots straight to the device, with no pageable host copy in between.  The mapping
+is MAP_SHARED, so the processes see each other's rows without an msync; the data file is flushed
+only on close.
 """
 
 from __future__ import annotations
@@ -88,6 +94,7 @@ class SharedActivationBuffer:
                                shape=(num_chunks, chunk_size_tokens, d_model))
         self._lock_fd = open(str(lock), "rb")
         self._backoff_n = 0
+        self._registered = False
 
     # ------------------------------------------------------------------ properties
     @property
@@ -155,14 +162,16 @@ class SharedActivationBuffer:
         a = activations[:rows].detach()
         if a.dtype != self._dtype:
             a = a.to(self._dtype)
-        a = a.cpu().contiguous()
-        view = a.view(torch.int16).numpy().view(np.uint16) if self._code == 0 else a.numpy()
-        self._data[chunk_idx, :rows] = view
+        if self._registered and a.is_cuda:
+            self._slot_tensor(chunk_idx, rows).copy_(a)  # device -> page-locked slot (copy engine)
+        else:
+            a = a.cpu().contiguous()
+            view = a.view(torch.int16).numpy().view(np.uint16) if self._code == 0 else a.numpy()
+            self._data[chunk_idx, :rows] = view
         if rows < self._T:
             self._data[chunk_idx, rows:] = 0
         self._slots[chunk_idx, 1] = rows
         self._slots[chunk_idx, 2] = producer_id
-        self._data.flush()
         self._ctl.flush()
 
     def mark_ready(self, chunk_idx: int) -> None:
@@ -218,6 +227,35 @@ class SharedActivationBuffer:
             np.copyto(dst.numpy(), src)
         return valid
 
+    def _slot_tensor(self, chunk_idx: int, rows: int) -> torch.Tensor:
+        """Zero-copy tensor over the first `rows` rows of a slot (the ring's own memory)."""
+        arr = np.asarray(self._data[chunk_idx, :rows])
+        return torch.from_numpy(arr.view(np.int16)).view(torch.bfloat16) if self._code == 0 else torch.from_numpy(arr)
+
+    def chunk_view(self, chunk_idx: int) -> tuple[torch.Tensor, int]:
+        """Zero-copy tensor of a CONSUMING slot's valid rows, valid only until the slot is
+        released (with `register_for_device_copies()` a non-blocking copy to the device reads it
+        directly; release the slot only after that copy completed)."""
+        valid = int(self._slots[chunk_idx, 1])
+        return self._slot_tensor(chunk_idx, valid), valid
+
+    @property
+    def registered(self) -> bool:
+        return self._registered
+
+    def register_for_device_copies(self) -> bool:
+        """Page-lock the data mapping for the CUDA copy engines of every device of this process
+        (cudaHostRegister, portable).  Returns False, leaving the pageable path, if it is refused."""
+        if self._registered:
+            return True
+        from saelens_b200 import ops
+
+        if not ops.available():
+            return False
+        # a refusal (e.g. a mapping of a file on a disk filesystem) keeps the staging-copy path
+        self._registered = ops.native().host_register(self._data.ctypes.data, self._data.nbytes) == 0
+        return self._registered
+
     def release_chunk(self, chunk_idx: int) -> None:
         with self._locked():
             if int(self._slots[chunk_idx, 0]) != ChunkState.CONSUMING:
@@ -246,6 +284,12 @@ class SharedActivationBuffer:
             self._ctl.flush()
 
     def close(self) -> None:
+        if self._registered:
+            from saelens_b200 import ops
+
+            torch.cuda.synchronize()
+            ops.native().host_unregister(self._data.ctypes.data)
+            self._registered = False
         self._ctl.flush()
         self._data.flush()
         self._lock_fd.close()

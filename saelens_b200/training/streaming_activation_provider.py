@@ -1,10 +1,13 @@
 """Trainer-side data provider over the shared activation ring
 (behaviour of sae_lens/training/streaming_activation_provider.py).
 
-The SAE-TP root claims up to `prefetch_chunks` READY slots, copies them through one pinned
-staging buffer to the device, releases the slots and broadcasts the rows to its TP followers
+The SAE-TP root claims up to `prefetch_chunks` READY slots, copies them to the device, releases
+the slots and broadcasts the rows to its TP followers
 (`[n_rows]` first, 0 meaning end of stream); every rank shuffles, keeps the remainder of the
-previous refill and serves `train_batch_size_tokens` rows per step.  Multi-hook streams store
+previous refill and serves `train_batch_size_tokens` rows per step.  When the ring is page-locked
+(`SharedActivationBuffer.register_for_device_copies`) the copy engine reads the slots directly, on
+a side stream that runs beside the previous step's kernels; otherwise the rows go through one
+pinned staging buffer.  Multi-hook streams store
 `num_hooks` interleaved batches and are served as `{hook_name: rows}` dicts.
 """
 
@@ -49,6 +52,8 @@ class StreamingActivationProvider:
         self._transfer_s = 0.0
         self._t0 = time.time()
         self._staging: torch.Tensor | None = None
+        self._direct = bool(getattr(buffer, "registered", False)) and self._device.type == "cuda" and sae_tp_rank == 0
+        self._copy_stream = torch.cuda.Stream(self._device) if self._direct else None
         self._staging_free: torch.cuda.Event | None = None  # set after the last H2D from staging
         self._log_path = shm_log_path if sae_tp_rank == 0 else None
         self._mon_path = buffer_monitor_path if sae_tp_rank == 0 else None
@@ -117,21 +122,11 @@ class StreamingActivationProvider:
             t1 = time.perf_counter()
             rows_max = len(idx) * self._buffer.chunk_size_tokens
             D = self._d_model or self._buffer._D
-            if self._staging_free is not None:
-                self._staging_free.synchronize()  # the previous async copy out of staging is done
-            if self._staging is None or self._staging.shape[0] < rows_max:
-                self._staging = torch.empty(rows_max, D, dtype=self._buffer.dtype,
-                                            pin_memory=self._device.type == "cuda")
-            n = 0
-            for i in idx:
-                n += self._buffer.read_chunk_into(i, self._staging[n:])
-                self._buffer.release_chunk(i)
-            if self._device.type == "cuda":
-                new = self._staging[:n].to(self._device, non_blocking=True).to(self._dtype)
-                self._staging_free = torch.cuda.Event()
-                self._staging_free.record()
+            if self._direct:
+                new = self._copy_direct(idx, D)
             else:
-                new = self._staging[:n].to(self._dtype, copy=True)
+                new = self._copy_staged(idx, D, rows_max)
+            n = new.shape[0]
             if self._group is not None:
                 self._bcast_count(n)
                 dist.broadcast(new, src=self._root, group=self._group)
@@ -154,6 +149,48 @@ class StreamingActivationProvider:
             assert self._pool is not None
             new = torch.cat([self._pool[self._start :], new])
         self._pool, self._start = new, 0
+
+    def _copy_direct(self, idx: list[int], D: int) -> torch.Tensor:
+        """Claimed page-locked slots -> device on the copy stream; the slots are released once the
+        copies completed, and the compute stream waits for them before it reads the rows."""
+        assert self._copy_stream is not None
+        views = [self._buffer.chunk_view(i) for i in idx]
+        n = sum(v for _, v in views)
+        cur = torch.cuda.current_stream(self._device)
+        with torch.cuda.stream(self._copy_stream):
+            raw = torch.empty(n, D, dtype=self._buffer.dtype, device=self._device)
+            o = 0
+            for t, v in views:
+                raw[o : o + v].copy_(t, non_blocking=True)
+                o += v
+            done = torch.cuda.Event()
+            done.record(self._copy_stream)
+        done.synchronize()  # the slots have been read
+        for i in idx:
+            self._buffer.release_chunk(i)
+        cur.wait_event(done)
+        raw.record_stream(cur)
+        return raw.to(self._dtype)
+
+    def _copy_staged(self, idx: list[int], D: int, rows_max: int) -> torch.Tensor:
+        """Claimed slots -> one pinned staging buffer (host copy) -> device; the slots are free as
+        soon as the host copy is done."""
+        if self._staging_free is not None:
+            self._staging_free.synchronize()  # the previous async copy out of staging is done
+        if self._staging is None or self._staging.shape[0] < rows_max:
+            self._staging = torch.empty(rows_max, D, dtype=self._buffer.dtype,
+                                        pin_memory=self._device.type == "cuda")
+        n = 0
+        for i in idx:
+            n += self._buffer.read_chunk_into(i, self._staging[n:])
+            self._buffer.release_chunk(i)
+        if self._device.type == "cuda":
+            new = self._staging[:n].to(self._device, non_blocking=True).to(self._dtype)
+            self._staging_free = torch.cuda.Event()
+            self._staging_free.record()
+        else:
+            new = self._staging[:n].to(self._dtype, copy=True)
+        return new
 
     def _regroup_hooks(self, new: torch.Tensor) -> torch.Tensor:
         """Rows arrive as [hook0 block, hook1 block, ...] per producer step of `batch` tokens;

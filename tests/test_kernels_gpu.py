@@ -78,6 +78,28 @@ def test_gemm_many_tiles_persistent():
     assert torch.equal(out, out2)
 
 
+@pytest.mark.parametrize("M,N,K", [(512, 1024, 256), (300, 50257, 64), (1000, 2003, 776)])
+def test_pair_gemm_tma_stores_equal_row_stores(monkeypatch, M, N, K):
+    """The CTA-pair kernel's TMA tile stores (staging tile, 128-byte swizzle, clipped at M and N)
+    write exactly what the per-thread row stores write, and nothing past column N."""
+    ops = _ops()
+    a = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    b = torch.randn(N, K, device="cuda").to(torch.bfloat16)
+    bias = torch.randn(N, device="cuda")
+    outs = {}
+    for tma in ("1", "0"):
+        monkeypatch.setenv("SAELENS_B200_GEMM_TMA_STORE", tma)
+        buf = torch.full((M, (N + 7) // 8 * 8 + 8), 7.0, dtype=torch.bfloat16, device="cuda")
+        cm = torch.empty(M, N // 32, dtype=torch.bfloat16, device="cuda") if N % 32 == 0 else None
+        ops.native().gemm_tn_bf16(a, b, bias, None, True, buf[:, :N], cm, ops.StatusWord("cuda").tensor, 0)
+        torch.cuda.synchronize()
+        assert (buf[:, N:] == 7.0).all(), "columns past N were written"
+        outs[tma] = (buf.clone(), cm)
+    assert torch.equal(outs["1"][0], outs["0"][0])
+    if outs["1"][1] is not None:
+        assert torch.equal(outs["1"][1], outs["0"][1])
+
+
 def _check_topk(h, vals, idx, k):
     M, N = h.shape
     hf = h.float()
