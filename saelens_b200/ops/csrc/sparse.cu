@@ -997,8 +997,19 @@ __global__ void __launch_bounds__(LR_THREADS, 2) latent_rows_kernel(const __grid
     }
   }
   float sq = 0.f;
-  for (int j = a.j0 + gw / a.nslices; j < a.j1; j += tw / a.nslices) {
-    int64_t beg = a.colptr[j], end = a.colptr[j + 1];
+  const int jstep = tw / a.nslices;
+  int j = a.j0 + gw / a.nslices;
+  int64_t nbeg = 0, nend = 0;
+  if (j < a.j1) {
+    nbeg = a.colptr[j];
+    nend = a.colptr[j + 1];
+  }
+  for (; j < a.j1; j += jstep) {
+    int64_t beg = nbeg, end = nend;
+    if (j + jstep < a.j1) {  // the next item's offsets load while this item runs
+      nbeg = __ldg(a.colptr + j + jstep);
+      nend = __ldg(a.colptr + j + jstep + 1);
+    }
     if (!(SB_IN_RANGE(beg, a.n_pairs + 1) && SB_IN_RANGE(end, a.n_pairs + 1) && SB_IN_RANGE(end - beg, a.n_pairs + 1))) end = beg = 0;
     if (sl == 0 && lane == 0 && a.fire_counts) {
       const int fc = a.fire_counts[j];

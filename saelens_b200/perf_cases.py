@@ -687,9 +687,12 @@ def fsdp_jumprelu(args: argparse.Namespace) -> None:
         return round(float(t.item()), 3)
 
     res: dict[str, float] = {}
+    os.environ["SAELENS_B200_PHASE_TIMING"] = "1"  # per-phase CUDA events of the native engine
     eng = FSDPJumpReLUEngine(build(), lr=5e-5, group=dist.group.WORLD)
     res["native"] = timed(lambda i: eng.step(x))
     eng.status.check()
+    # the events also ran during the warm-up steps: phase means over warm-up + timed steps
+    phases = {k: round(v / (3 + args.steps), 3) for k, v in eng.phase_times_ms().items()}
     eng.close()
     del eng
     torch.cuda.empty_cache()
@@ -719,6 +722,7 @@ def fsdp_jumprelu(args: argparse.Namespace) -> None:
         print(json.dumps({"world": world, "arch": "jumprelu", "d_in": args.d_in, "d_sae": args.d_sae,
                           "batch_per_gpu": args.batch, "ms_per_step": res,
                           "tokens_per_s": {m: round(args.batch * world / v * 1e3, 1) for m, v in res.items()},
+                          "native_phases_ms": phases,
                           "native": "bf16 compute, fp32 master + Adam state, sharded",
                           "torch_fsdp": "fp32 params, bf16 autocast, FULL_SHARD over NCCL"}), flush=True)
     dist.barrier()
