@@ -39,8 +39,8 @@ def compute_routing_table(P: int, Q: int, batch_size: int) -> list[ShardRoute]:
             n = (ov * batch_size) // Q if i < len(edges) - 1 else batch_size - start
             if n == 0:
                 raise ValueError(
-                    f"batch_size={batch_size} too small: edge (p={p}, c={c}) has positive overlap "
-                    f"(ov_len={ov}) but would receive 0 rows. Increase batch_size or reduce P/Q."
+                    f"routing {batch_size} rows per producer is too small for {P} producers and {Q} consumers: "
+                    f"producer {p} shares {ov} / {Q} of its rows with consumer {c}, which rounds to no rows"
                 )
             out.append(ShardRoute(p, c, start, start + n))
             start += n
