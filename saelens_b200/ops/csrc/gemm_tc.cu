@@ -60,7 +60,8 @@ constexpr int NUM_THREADS_AG = NUM_THREADS + 32 * NUM_COPY_WARPS;
 constexpr int MAX_MTILES = 4096;   // ready bitmap capacity of the AG producer (524288 rows)
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int GROUP_N = 16;  // n-tiles per raster group (L2 reuse of A and B)
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int STAGE_OUT_BYTES = 32 * 64;  // one epilogue warp's 32 x 32 bf16 staging tile (dense stores)
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + NUM_EPI_WARPS * STAGE_OUT_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 
 struct Epi {
   __nv_bfloat16* out;      // [M, ldo] or nullptr
@@ -124,6 +125,7 @@ struct EpiD {
   const __nv_bfloat16* addend;
   int64_t ldad;
   const float* oscale;
+  int staged;  // 1: full 32-column chunks are stored through the warp's staging tile
 };
 
 // Sum over the 32 lanes of v[c] for every c; lane L returns the sum for column L.  Butterfly
@@ -184,9 +186,51 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* p, const float (&f)
 }
 
 // Dense epilogue of one accumulator tile (see EpiD); `lane` is the thread's lane.
+// A warp's 32 rows x 32 columns of bf16 (this lane holds row `lane` in `f`) stored row-contiguously
+// through `stage` (2 KB): each lane writes its row's four 16-byte granules (XOR-swizzled so the
+// 32 lanes spread over the banks), then every store instruction writes 8 rows x 64 contiguous
+// bytes instead of 32 rows x 16 bytes.  `row_ptr` (16-byte aligned) and `rowok` are this lane's;
+// the other lanes' are shuffled in.  Used for full 32-column chunks only.
+__device__ __forceinline__ int stage_off(int r, int q) {
+  return (r >> 1) * 128 + ((((r & 1) << 2) + (q ^ ((r >> 1) & 3))) << 4);
+}
+__device__ __forceinline__ void warp_store_rows_bf16x32(uint8_t* stage, const float (&f)[32],
+                                                        __nv_bfloat16* row_ptr, bool rowok, int lane) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __nv_bfloat162 h2 = __floats2bfloat162_rn(f[8 * q + 2 * j], f[8 * q + 2 * j + 1]);
+      w[j] = *reinterpret_cast<uint32_t*>(&h2);
+    }
+    *reinterpret_cast<uint4*>(stage + stage_off(lane, q)) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  __syncwarp();
+  const unsigned long long mine = reinterpret_cast<unsigned long long>(row_ptr);
+  const int ok_mine = rowok ? 1 : 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = i * 8 + (lane >> 2), q = lane & 3;
+    const unsigned long long p = __shfl_sync(0xffffffffu, mine, r);
+    const int ok = __shfl_sync(0xffffffffu, ok_mine, r);
+    if (ok) reinterpret_cast<uint4*>(p)[q] = *reinterpret_cast<const uint4*>(stage + stage_off(r, q));
+  }
+  __syncwarp();  // the staging tile is free again
+}
+
 __device__ __forceinline__ void epilogue_tile_dense(const EpiD& e, uint32_t trow, int row, int M, int N, int nt,
-                                                    int lane) {
+                                                    int lane, uint8_t* stage = nullptr) {
   const bool rowok = row < M;
+  // row stores: through the warp's staging tile for full 32-column chunks (`stage` given and every
+  // lane calling), per thread otherwise; `p` points at this lane's row and column col0
+  auto put = [&](__nv_bfloat16* p, const float (&f)[32], int nv, bool ok) {
+    if (stage != nullptr && nv == 32) {
+      warp_store_rows_bf16x32(stage, f, p, ok, lane);
+    } else if (ok) {
+      store_bf16x32(p, f, nv);
+    }
+  };
   float s_loss = 0.f, s_sq = 0.f, s_nnz = 0.f;
   const float rr = (e.r1_row && rowok) ? e.r1_row[row] : 0.f;
 #pragma unroll 1
@@ -215,7 +259,7 @@ __device__ __forceinline__ void epilogue_tile_dense(const EpiD& e, uint32_t trow
         gate[j] = (rowok && ok) ? __bfloat162float(__float2bfloat16_rn(fmaxf(pg, 0.f))) : 0.f;
         v[j] = pg > 0.f ? fmaxf(pm, 0.f) : 0.f;
       }
-      if (e.out2 && rowok) store_bf16x32(e.out2 + int64_t(row) * e.ldo2 + col0, gate, nv);
+      if (e.out2) put(e.out2 + int64_t(row) * e.ldo2 + col0, gate, nv, rowok);
       if (e.colsum2) {
         const float cs = warp_colsum32(gate, lane);
         if (lane < nv && cs != 0.f) atomicAdd(e.colsum2 + col0 + lane, cs);
@@ -234,7 +278,7 @@ __device__ __forceinline__ void epilogue_tile_dense(const EpiD& e, uint32_t trow
         for (int j = 0; j < 32; ++j)
           t[j] = (rowok && j < nv) ? __bfloat162float(e.target[int64_t(row) * e.ldtg + col0 + j]) : 0.f;
       }
-      if (e.out2 && rowok) store_bf16x32(e.out2 + int64_t(row) * e.ldo2 + col0, v, nv);
+      if (e.out2) put(e.out2 + int64_t(row) * e.ldo2 + col0, v, nv, rowok);
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         // the loss uses the bf16-rounded reconstruction the model outputs
@@ -271,7 +315,7 @@ __device__ __forceinline__ void epilogue_tile_dense(const EpiD& e, uint32_t trow
       // the gate compares the stored (bf16) pre-activation, as the backward does
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
-      if (e.out2 && rowok) store_bf16x32(e.out2 + int64_t(row) * e.ldo2 + col0, v, nv);
+      if (e.out2) put(e.out2 + int64_t(row) * e.ldo2 + col0, v, nv, rowok);
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const float th = j < nv ? __ldg(e.thr + col0 + j) : 0.f;
@@ -315,14 +359,12 @@ __device__ __forceinline__ void epilogue_tile_dense(const EpiD& e, uint32_t trow
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = (rowok && j < nv) ? __bfloat162float(__float2bfloat16_rn(v[j])) : 0.f;
     if (e.rs_n > 0) {
-      if (rowok) {
-        const int o = row / e.rs_n;
-        __nv_bfloat16* orow = p2p::at<__nv_bfloat16>(e.P, o, e.rs_off) +
-                              (int64_t(e.P.rank) * e.rs_n + (row - o * e.rs_n)) * e.ldo;
-        store_bf16x32(orow + col0, v, nv);
-      }
-    } else if (e.out && rowok) {
-      store_bf16x32(e.out + int64_t(row) * e.ldo + col0, v, nv);
+      const int o = rowok ? row / e.rs_n : 0;  // rows past M name no owner (and store nothing)
+      __nv_bfloat16* orow = p2p::at<__nv_bfloat16>(e.P, o, e.rs_off) +
+                            (int64_t(e.P.rank) * e.rs_n + (rowok ? row - o * e.rs_n : 0)) * e.ldo;
+      put(orow + col0, v, nv, rowok);
+    } else if (e.out) {
+      put(e.out + int64_t(row) * e.ldo + col0, v, nv, rowok);
     }
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
@@ -555,7 +597,8 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
                                              ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_TILE_BYTES;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * B_TILE_BYTES);
+  uint8_t* sStage = sB + STAGES * B_TILE_BYTES;  // dense epilogue staging tiles, one per epilogue warp
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sStage + NUM_EPI_WARPS * STAGE_OUT_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -709,7 +752,7 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
       const int row = mt * BM + q * 32 + lane;
       const uint32_t trow = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
       if (DENSE)
-        epilogue_tile_dense(ed, trow, row, M, N, nt, lane);
+        epilogue_tile_dense(ed, trow, row, M, N, nt, lane, ed.staged ? sStage + (warp - 2) * STAGE_OUT_BYTES : nullptr);
       else
         epilogue_tile(ep, trow, row, M, N, nt);
       tc_fence_before();
@@ -979,6 +1022,13 @@ static bool use_pair(int64_t M) {
   return !off && M >= 2 * gemm::BM;
 }
 
+// SAELENS_B200_GEMM_STAGED_STORE=1 stores the dense epilogue's full 32-column chunks through the
+// warp's staging tile; otherwise per-thread row stores
+static bool staged_stores_enabled() {
+  const char* e = std::getenv("SAELENS_B200_GEMM_STAGED_STORE");
+  return e && e[0] == '1' && e[1] == 0;
+}
+
 template <bool AG>
 static void launch_gemm(const void* a_ptr, int64_t lda, int64_t M, const torch::Tensor& B, const gemm::Epi& ep,
                         const torch::Tensor& status, int64_t max_ctas, const gemm::Ag& ag, bool pair) {
@@ -1236,6 +1286,7 @@ void gemm_dense_bf16(const torch::Tensor& A, bool a_mn, const torch::Tensor& B, 
   SB_CHECK(A.stride(0) % 8 == 0 && B.stride(0) % 8 == 0, "gemm_dense_bf16: row strides must be multiples of 8");
   SB_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm_dense_bf16: size");
   gemm::EpiD ed{};
+  ed.staged = staged_stores_enabled() ? 1 : 0;
   if (rs_n > 0) {
     const int64_t S = int64_t(rs_bases.size());
     SB_CHECK(S >= 1 && S <= p2p::kMaxRanks && rs_rank >= 0 && rs_rank < S && rs_n % gemm::BM == 0 &&
@@ -1331,6 +1382,7 @@ void gemm_fsdp_dense_bf16(const torch::Tensor& A, const torch::Tensor& w_own, co
                     w2_own->sizes() == w_own.sizes(),
                 "gemm_fsdp_dense: w2_own must be contiguous bf16 like w_own");
   gemm::EpiD ed{};
+  ed.staged = staged_stores_enabled() ? 1 : 0;
   ed.out = opt_bf16_mat(out, M, N, &ed.ldo, "out");
   ed.out2 = opt_bf16_mat(out2, M, N, &ed.ldo2, "out2");
   ed.bias = opt_f32(bias, N, "bias");

@@ -128,3 +128,26 @@ def test_gated_dual_path_epilogue():
     pm = acc * r_mag.exp() + b_mag
     _close(gate, torch.relu(pg))
     _close(f, torch.where(pg > 0, torch.relu(pm), torch.zeros_like(pm)))
+
+
+@pytest.mark.parametrize("M, N, K", [(256, 512, 256), (300, 1000, 200), (1024, 2056, 512)])
+def test_staged_row_stores_equal_per_thread_stores(monkeypatch, M, N, K):
+    """The epilogue's warp-staged row stores (full 32-column chunks through a shared-memory tile)
+    write exactly what per-thread stores write, for `out` and `out2`, ragged rows and columns
+    included, and nothing past column N."""
+    from saelens_b200 import ops
+
+    a, b = _bf(M, K, seed=11), _bf(N, K, seed=12)
+    bias = torch.randn(N, device="cuda")
+    thr = torch.rand(N, device="cuda") * 0.5
+    res = {}
+    for staged in ("1", "0"):
+        monkeypatch.setenv("SAELENS_B200_GEMM_STAGED_STORE", staged)
+        n8 = (N + 7) // 8 * 8 + 8
+        buf = torch.full((M, n8), 7.0, dtype=torch.bfloat16, device="cuda")
+        buf2 = torch.full((M, n8), 7.0, dtype=torch.bfloat16, device="cuda")
+        ops.gemm_dense(a, b, out=buf[:, :N], out2=buf2[:, :N], bias=bias, thr=thr)
+        torch.cuda.synchronize()
+        assert (buf[:, N:] == 7.0).all() and (buf2[:, N:] == 7.0).all(), "columns past N were written"
+        res[staged] = (buf, buf2)
+    assert torch.equal(res["1"][0], res["0"][0]) and torch.equal(res["1"][1], res["0"][1])
