@@ -220,8 +220,8 @@ class LanguageModelSAETrainingRunner:
         the same seed for every hook ("same") or seed + index ("offset"); each SAE records its hook
         in the metadata, is sharded for TP and wrapped for DDP / FSDP like a single SAE."""
         cfg = self.cfg
-        if cfg.streaming_mode or self.routed:
-            raise ValueError("multi-hook training runs on the non-routed data path")
+        if self.routed:
+            raise ValueError("multi-hook training runs on the streaming or the non-routed data path")
         for idx, hook in enumerate(self.hook_names):
             seed = cfg.seed if cfg.multi_sae_seed_mode == "same" else cfg.seed + idx
             sae_cfg = type(cfg.sae).from_sae_runner_config(cfg)
@@ -268,10 +268,11 @@ class LanguageModelSAETrainingRunner:
             if (Path(self.resume_from_checkpoint) / ACTIVATIONS_STORE_STATE_FILENAME).exists():
                 self.activations_store.load_from_checkpoint(self.resume_from_checkpoint)
         result = trainer.fit()
-        if cfg.output_path is not None and self._is_writer():
-            trainer.save_final(cfg.output_path)
-            with open(Path(cfg.output_path) / RUNNER_CFG_FILENAME, "w") as f:
-                json.dump(cfg.to_dict(), f, default=str)
+        if cfg.output_path is not None:
+            trainer.save_final(cfg.output_path)  # every rank (TP gathers are collective); one writes
+            if self._is_writer():
+                with open(Path(cfg.output_path) / RUNNER_CFG_FILENAME, "w") as f:
+                    json.dump(cfg.to_dict(), f, default=str)
         return result
 
     def _native_fsdp_ok(self, sae: TrainingSAE[Any]) -> bool:

@@ -63,6 +63,9 @@ def streaming_init(runner: Any) -> None:
     runner.producer_tp_group = ds.get_vllm_tp_group() if vllm_tp > 1 and ds.is_producer() else None
     runner.is_stream_writer = ds.is_producer() and ds.get_vllm_tp_rank() == 0
     n_hooks = len(getattr(cfg, "hook_names", None) or [cfg.hook_name])
+    if n_hooks > 1 and cfg.streaming_chunk_size_tokens % cfg.train_batch_size_tokens:
+        raise ValueError("multi-hook streaming needs streaming_chunk_size_tokens to be a multiple of "
+                         "train_batch_size_tokens (chunks hold whole per-hook training batches)")
     runner.streaming_transport = choose_transport(cfg, sae_tp, n_hooks)
     runner.n_producers = vllm_dp
     runner.target_chunks = math.ceil(cfg.training_tokens / cfg.streaming_chunk_size_tokens)
@@ -114,9 +117,20 @@ def _quiesce_paths(runner: Any) -> tuple[Path | None, Path | None, Path | None]:
     return qdir / "quiesce_request", qdir / f"quiesce_ack_producer_{pidx}", qdir / f"producer_dataset_state_{pidx}"
 
 
+def _hook_blocks(acts: torch.Tensor, n_hooks: int, batch: int) -> tuple[torch.Tensor, int]:
+    """Multi-hook rows [n, H * d] (hooks side by side) as the ring's layout: per training step of
+    `batch` tokens one block of `batch` rows per hook, [(n / batch) * H * batch, d]; a tail shorter
+    than `batch` is dropped."""
+    n = (acts.shape[0] // batch) * batch
+    d = acts.shape[1] // n_hooks
+    out = acts[:n].reshape(n // batch, batch, n_hooks, d).permute(0, 2, 1, 3).reshape(-1, d).contiguous()
+    return out, int(out.shape[0])
+
+
 def run_producer(runner: Any) -> int:
     """Write this producer's share of the chunk quota; returns the number of chunks written."""
     cfg, store = runner.cfg, runner.activations_store
+    n_hooks = len(getattr(cfg, "hook_names", None) or [cfg.hook_name])
     pidx, P = ds.get_producer_idx(), runner.n_producers
     rows_per_chunk = cfg.streaming_chunk_size_tokens
     req, ack, state_dir = _quiesce_paths(runner)
@@ -161,6 +175,8 @@ def run_producer(runner: Any) -> int:
             break
         rows = max(1, min(rows_per_chunk, cfg.training_tokens - seq * rows_per_chunk))
         acts, valid = store.get_streaming_activations(rows)
+        if n_hooks > 1:
+            acts, valid = _hook_blocks(acts, n_hooks, cfg.train_batch_size_tokens)
         if writer:
             # a full ring blocks the producer; the quiesce request must still reach it there
             if runner.ring is not None:
@@ -253,7 +269,9 @@ def run_consumer(runner: Any) -> Any:
     from saelens_b200.utils.misc import str_to_dtype
 
     cfg = runner.cfg
-    dev = runner.sae.W_dec.device
+    multi = bool(getattr(runner, "is_multi_sae", False))
+    first = runner.base_sae_by_hook[runner.hook_names[0]] if multi else runner.sae
+    dev = first.W_dec.device
     if runner.ring is not None:
         provider: Any = DeviceRingProvider(runner.ring, cfg.train_batch_size_tokens, shuffle=cfg.streaming_shuffle,
                                            seed=cfg.seed, dtype=str_to_dtype(cfg.dtype))
@@ -263,7 +281,10 @@ def run_consumer(runner: Any) -> Any:
             runner.shm_buffer, cfg.train_batch_size_tokens, cfg.streaming_prefetch_chunks, dev, sae_tp_group=tp,
             sae_tp_rank=ds.get_sae_tp_rank(), sae_tp_root_global_rank=ds.get_consumer_tp_root(0),
             d_model=cfg.sae.d_in, dtype=str_to_dtype(cfg.dtype), shuffle=cfg.streaming_shuffle,
-            random_chunks=cfg.streaming_random_chunks)
+            random_chunks=cfg.streaming_random_chunks, hook_names=runner.hook_names if multi else None)
+    qdir = _quiesce_dir(runner)
+    if multi:
+        return _run_multi_consumer(runner, provider, qdir)
     trainer = SAETrainer(cfg=cfg.to_sae_trainer_config(), sae=runner.sae, base_sae=runner.sae, data_provider=provider,
                          evaluator=None, save_checkpoint_fn=None,
                          append_logs=runner.resume_from_checkpoint is not None)
@@ -274,12 +295,31 @@ def run_consumer(runner: Any) -> Any:
         if trainer.engine is not None:
             trainer.engine.refresh()
         trainer.load_trainer_state(ck)
-    qdir = _quiesce_dir(runner)
     sae = trainer.fit(quiesce_request_path=qdir / "quiesce_request" if qdir is not None else None,
                       quiesce_ack_path=qdir / "quiesce_ack" if qdir is not None else None)
     if not getattr(trainer, "quiesced", False) and (runner.ring is None or ds.get_sae_tp_rank() == 0):
         runner.save_final_sae(sae, trainer)
     return sae
+
+
+def _run_multi_consumer(runner: Any, provider: Any, qdir: Path | None) -> Any:
+    """One SAE per hook from the ring's per-hook blocks (`MultiSAETrainer`); quiesce and resume as
+    the single-hook consumer."""
+    from saelens_b200.training.multi_sae_trainer import MultiSAETrainer
+
+    cfg = runner.cfg
+    trainer = MultiSAETrainer(
+        hook_names=runner.hook_names, sae_by_hook=runner.sae_by_hook, base_sae_by_hook=runner.base_sae_by_hook,
+        data_provider=provider, cfg=cfg.to_sae_trainer_config(), dp_group=None, sae_dp_mode=cfg.sae_dp_mode,
+        backward_mode=cfg.multi_sae_backward_mode, seed_mode=cfg.multi_sae_seed_mode)
+    runner.trainer = trainer
+    if runner.resume_from_checkpoint is not None:
+        trainer.load_trainer_state(runner.resume_from_checkpoint)
+    result = trainer.fit(quiesce_request_path=qdir / "quiesce_request" if qdir is not None else None,
+                         quiesce_ack_path=qdir / "quiesce_ack" if qdir is not None else None)
+    if not trainer.quiesced and cfg.output_path is not None:
+        trainer.save_final(cfg.output_path)  # every consumer rank (TP gathers), the first writes
+    return result
 
 
 def run_streaming(runner: Any) -> Any:

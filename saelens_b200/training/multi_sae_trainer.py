@@ -272,11 +272,34 @@ class MultiSAETrainer:
                 s.step()
         return {h: float(v) for h, v in losses.items()}
 
-    def fit(self) -> dict[str, Any]:
+    def fit(self, quiesce_request_path: str | Path | None = None,
+            quiesce_ack_path: str | Path | None = None) -> dict[str, Any]:
+        """Train until the sample budget or the data ends.  With `quiesce_request_path` (a
+        topology supervisor's request file) every step checks for it; on a request all ranks write
+        a `quiesce_*` checkpoint, the writer acknowledges, and the run stops without a final
+        checkpoint (`self.quiesced`)."""
+        from saelens_b200.training.sae_trainer import agree_any
+
+        self.quiesced = False
+        first = self.base_sae_by_hook[self.hook_names[0]]
+        groups = [g for g in (_tp_group_of(first), self.dp_group) if g is not None]
+
+        def quiesce_if_requested() -> bool:
+            if quiesce_request_path is None:
+                return False
+            if not agree_any(Path(quiesce_request_path).exists(), groups, first.W_dec.device):
+                return False
+            self.save_checkpoint(checkpoint_name=f"quiesce_{self.n_training_samples}")
+            if quiesce_ack_path is not None and self._is_writer():
+                Path(quiesce_ack_path).touch()
+            self.quiesced = True
+            return True
+
         while self.n_training_samples < self.cfg.total_training_samples:
             try:
                 batch = next(self.data_provider)
             except StopIteration:
+                quiesce_if_requested()  # the data can end because the producers quiesced first
                 break
             if (self.n_training_steps + 1) % self.cfg.feature_sampling_window == 0:
                 for h in self.hook_names:
@@ -290,7 +313,9 @@ class MultiSAETrainer:
             if self.checkpoint_thresholds and self.n_training_samples > self.checkpoint_thresholds[0]:
                 self.save_checkpoint(checkpoint_name=str(self.n_training_samples))
                 self.checkpoint_thresholds.pop(0)
-        if getattr(self.cfg, "save_final_checkpoint", False):
+            if quiesce_if_requested():
+                return self.base_sae_by_hook
+        if getattr(self.cfg, "save_final_checkpoint", False) and not self.quiesced:
             self.save_checkpoint(checkpoint_name=f"final_{self.n_training_samples}")
         return self.base_sae_by_hook
 
@@ -301,13 +326,25 @@ class MultiSAETrainer:
                 "n_training_steps": self.n_training_steps, "n_training_samples": self.n_training_samples}
 
     def save_final(self, output_path: str | Path) -> None:
+        """The inference SAEs, one sub-directory per hook, plus the manifest.  Every rank of the
+        first data-parallel replica calls it (the TP gathers are collective); the first writes."""
+        if self._dp_rank() != 0:
+            return
         base = Path(output_path)
-        base.mkdir(parents=True, exist_ok=True)
+        writer = self._is_writer()
+        sparsity = self.log_feature_sparsity_by_hook()
         for h in self.hook_names:
-            d = base / sanitize_hook_name_for_path(h)
-            self.base_sae_by_hook[h].save_inference_model(d)
-            save_file({"sparsity": self.log_feature_sparsity_by_hook()[h]}, d / SPARSITY_FILENAME)
-        (base / MULTI_SAE_MANIFEST_FILENAME).write_text(json.dumps(self._manifest(), indent=2))
+            sae = self.base_sae_by_hook[h]
+            sd = {k: v.detach().contiguous() for k, v in sae.state_dict().items()}
+            sae.process_state_dict_for_saving_inference(sd)  # gathers the TP shards (collective)
+            if writer:
+                d = base / sanitize_hook_name_for_path(h)
+                d.mkdir(parents=True, exist_ok=True)
+                save_file({k: v.contiguous() for k, v in sd.items()}, d / SAE_WEIGHTS_FILENAME)
+                (d / SAE_CFG_FILENAME).write_text(json.dumps(sae.cfg.get_inference_sae_cfg_dict()))
+                save_file({"sparsity": sparsity[h]}, d / SPARSITY_FILENAME)
+        if writer:
+            (base / MULTI_SAE_MANIFEST_FILENAME).write_text(json.dumps(self._manifest(), indent=2))
 
     def save_checkpoint(self, checkpoint_path: str | Path | None = None, checkpoint_name: str | None = None,
                         ) -> Path | None:

@@ -87,6 +87,20 @@ def _is_ddp(m: Any) -> bool:
     return isinstance(m, DDP)
 
 
+def agree_any(flag: bool, groups: list[Any], device: torch.device) -> bool:
+    """`flag` OR-ed over every rank of `groups` (each in turn), so that ranks which check a file at
+    slightly different moments still act at the same step."""
+    if not groups or not (dist.is_available() and dist.is_initialized()):
+        return flag
+    out = bool(flag)
+    for g in groups:
+        dev = device if dist.get_backend(g) == "nccl" else torch.device("cpu")
+        t = torch.tensor([1 if out else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=g)
+        out = bool(t.item())
+    return out
+
+
 class SAETrainer(Generic[T_TRAINING_SAE]):
     def __init__(self, cfg: SAETrainerConfig, sae: Any, data_provider: DataProvider,
                  evaluator: Evaluator | None = None, save_checkpoint_fn: SaveCheckpointFn | None = None,
@@ -281,7 +295,11 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
         self._prepare_fit()
 
         def quiesce_if_requested() -> bool:
-            if quiesce_request_path is None or not Path(quiesce_request_path).exists():
+            if quiesce_request_path is None:
+                return False
+            # every rank of the trainer takes the same decision at the same step (the checkpoint
+            # gathers are collective): a request seen by any rank counts for all
+            if not agree_any(Path(quiesce_request_path).exists(), self._trainer_groups(), self._base_sae.W_dec.device):
                 return False
             self.save_checkpoint(checkpoint_name=f"quiesce_{self.n_training_samples}")
             if quiesce_ack_path is not None and self._is_metric_writer_rank():
@@ -297,6 +315,9 @@ class SAETrainer(Generic[T_TRAINING_SAE]):
             if quiesce_if_requested():
                 break
         return self._finish_fit()
+
+    def _trainer_groups(self) -> list[Any]:
+        return [g for g in (getattr(self._base_sae, "_tp_group", None), self.dp_group) if g is not None]
 
     def _matryoshka_native_ok(self) -> bool:
         from saelens_b200.training.matryoshka_engine import matryoshka_engine_supported

@@ -17,7 +17,7 @@ def _port() -> int:
     return p
 
 
-def _worker(rank, world, port, tmp, vtp=1, stp=1):
+def _worker(rank, world, port, tmp, vtp=1, stp=1, hooks=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
     import torch.distributed as dist
@@ -33,6 +33,7 @@ def _worker(rank, world, port, tmp, vtp=1, stp=1):
                                 dtype="float32"))
     cfg = LanguageModelSAERunnerConfig(
         sae=TopKTrainingSAEConfig(d_in=64, d_sae=128, k=8), model_name="gpt2", hook_name="blocks.1.hook_resid_pre",
+        hook_names=hooks,
         dataset_path="synthetic:uniform:500:32", context_size=16, training_tokens=64 * 12,
         train_batch_size_tokens=64, store_batch_size_prompts=4, n_batches_in_buffer=2,
         output_path=os.path.join(tmp, "out"), logger=LoggingConfig(log_to_wandb=False), device="cpu",
@@ -42,14 +43,17 @@ def _worker(rank, world, port, tmp, vtp=1, stp=1):
     if rank == 0:  # the ring's files are created before the runners attach
         from saelens_b200.training.shared_activation_buffer import SharedActivationBuffer
 
-        SharedActivationBuffer(f"ring_{port}", 4, 128, 64, num_producers=1, target_chunks=6, create=True,
-                               base_dir=tmp, dtype=torch.float32).close()
+        SharedActivationBuffer(f"ring_{port}", 4, 128 * (len(hooks) if hooks else 1), 64, num_producers=1,
+                               target_chunks=6, create=True, base_dir=tmp, dtype=torch.float32).close()
     dist.barrier()
     runner = LanguageModelSAETrainingRunner(cfg, override_model=lm, vllm_dp_size=1, vllm_tp_size=vtp, sae_tp_size=stp)
     out = runner.run()
     info = {"role": runner.role, "transport": runner.streaming_transport,
             "lm_sharded": getattr(runner.model, "tp", None) is not None}
-    if runner.role == "consumer":
+    if runner.role == "consumer" and hooks:
+        info["steps"] = runner.trainer.n_training_steps
+        info["hooks"] = sorted(out.keys())
+    elif runner.role == "consumer":
         info["steps"] = runner.trainer.n_training_steps
         info["d_sae"] = int(out.W_dec.shape[0])
         info["d_sae_local"] = int(runner.sae.W_dec.shape[0])
@@ -89,3 +93,16 @@ def test_streaming_consumer_is_sae_tensor_parallel(tmp_path):
     out = tmp_path / "out"
     rows = [json.loads(x) for x in (out / "mse_history.jsonl").read_text().splitlines()]
     assert len(rows) == 12
+
+
+def test_streaming_multi_hook_trains_one_sae_per_hook(tmp_path):
+    """Two hooks through the ring (per training step one block of rows per hook): the consumer
+    trains one SAE per hook for every step and writes both SAEs and the manifest."""
+    hooks = ["blocks.0.hook_resid_post", "blocks.1.hook_resid_pre"]
+    mp.spawn(_worker, args=(2, _port(), str(tmp_path), 1, 1, hooks), nprocs=2, join=True)
+    c = json.loads((tmp_path / "r1.json").read_text())
+    assert c["role"] == "consumer" and c["steps"] == 12 and c["hooks"] == sorted(hooks)
+    out = tmp_path / "out"
+    assert (out / "multi_sae_manifest.json").exists()
+    for h in hooks:
+        assert (out / h / "sae_weights.safetensors").exists() and (out / h / "cfg.json").exists()
