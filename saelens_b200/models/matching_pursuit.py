@@ -1,5 +1,9 @@
 """Matching-pursuit SAEs (sae_lens/saes/matching_pursuit_sae.py): greedy encode that repeatedly
-picks the decoder row best aligned with the residual; the encoder is tied to W_dec^T."""
+picks the decoder row best aligned with the residual; the encoder is tied to W_dec^T.
+
+On CUDA the encode runs natively (`saelens_b200.ops.mp`: the tcgen05 score GEMM with a fused row
+argmax, a fused per-row update, and a replaying backward); the loop below is the CPU path and the
+test oracle."""
 
 from __future__ import annotations
 
@@ -22,6 +26,20 @@ from saelens_b200.models.sae import (
 
 def _encode_matching_pursuit(sae_in_centered: torch.Tensor, W_dec: torch.Tensor, residual_threshold: float,
                              max_iterations: int | None, stop_on_duplicate_support: bool) -> torch.Tensor:
+    from saelens_b200.ops import mp
+
+    if mp.native_supported(sae_in_centered, W_dec):
+        return mp.encode_matching_pursuit(sae_in_centered, W_dec, residual_threshold, max_iterations,
+                                          stop_on_duplicate_support)
+    return _encode_matching_pursuit_torch(sae_in_centered, W_dec, residual_threshold, max_iterations,
+                                          stop_on_duplicate_support)
+
+
+def _encode_matching_pursuit_torch(sae_in_centered: torch.Tensor, W_dec: torch.Tensor, residual_threshold: float,
+                                   max_iterations: int | None, stop_on_duplicate_support: bool,
+                                   picks: list[torch.Tensor] | None = None) -> torch.Tensor:
+    """PyTorch loop of the reference's iteration.  `picks`, when given, replaces the argmax of
+    iteration t by `picks[t]` (a test replays the native kernels' selections this way)."""
     resid = sae_in_centered.clone()
     shape = resid.shape
     if resid.ndim > 2:
@@ -33,9 +51,14 @@ def _encode_matching_pursuit(sae_in_centered: torch.Tensor, W_dec: torch.Tensor,
     acts = torch.zeros(n, d_sae, device=W_dec.device, dtype=resid.dtype)
     prev = torch.zeros(n, d_sae, dtype=torch.bool, device=W_dec.device)
     done = torch.zeros(n, dtype=torch.bool, device=W_dec.device)
-    for _ in range(iters):
+    for it in range(iters):
+        if picks is not None and it >= len(picks):
+            break
         with torch.no_grad():
-            pick = (resid @ W_dec.T).relu().argmax(dim=1, keepdim=True)
+            if picks is not None:
+                pick = picks[it].to(device=W_dec.device, dtype=torch.int64).clamp_min(0).unsqueeze(1)
+            else:
+                pick = (resid @ W_dec.T).relu().argmax(dim=1, keepdim=True)
         sel = W_dec[pick.squeeze(1)]
         val = (resid * sel).sum(dim=-1, keepdim=True).relu()
         val = (val * (~done).unsqueeze(1).to(val.dtype)).to(acts.dtype)

@@ -39,6 +39,7 @@ SOURCES = [
     "symm.cpp",
     "lm_kernels.cu",
     "attention.cu",
+    "mp.cu",
 ]
 
 NVCC_FLAGS = [

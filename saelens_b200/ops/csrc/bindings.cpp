@@ -13,7 +13,8 @@ namespace sb {
 void gemm_tn_bf16(const torch::Tensor& A, const torch::Tensor& B, const c10::optional<torch::Tensor>& bias,
                   const c10::optional<torch::Tensor>& scale, bool relu,
                   const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& cmax,
-                  const torch::Tensor& status, int64_t max_ctas, const c10::optional<torch::Tensor>& tmax);
+                  const torch::Tensor& status, int64_t max_ctas, const c10::optional<torch::Tensor>& tmax,
+                  const c10::optional<torch::Tensor>& amax);
 void row_topk(const torch::Tensor& H, const torch::Tensor& cmax, int64_t k_max,
               const c10::optional<torch::Tensor>& k_dev, const c10::optional<torch::Tensor>& mask,
               const torch::Tensor& out_val, const torch::Tensor& out_idx, const torch::Tensor& status,
@@ -157,6 +158,13 @@ void gemm_fsdp_dense_bf16(const torch::Tensor& A, const torch::Tensor& w_own, co
                           const c10::optional<torch::Tensor>& bias, const c10::optional<torch::Tensor>& thr,
                           const c10::optional<torch::Tensor>& colcnt, const c10::optional<torch::Tensor>& nnz,
                           const torch::Tensor& status, const torch::Tensor& ticket);
+void mp_step(const torch::Tensor& resid, const torch::Tensor& resid_bf, const torch::Tensor& key,
+             const torch::Tensor& acts, const torch::Tensor& done, const c10::optional<torch::Tensor>& idx_out,
+             const c10::optional<torch::Tensor>& val_out, const torch::Tensor& n_active, const torch::Tensor& W,
+             double thresh, bool stop_dup);
+void mp_backward(const torch::Tensor& resid, const torch::Tensor& g_resid, const torch::Tensor& g_acts,
+                 const torch::Tensor& idx, const torch::Tensor& val, const c10::optional<torch::Tensor>& g_W,
+                 const torch::Tensor& W);
 void attention_fwd(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, const torch::Tensor& out,
                    double scale, double softcap, bool causal, const torch::Tensor& status);
 torch::Tensor batch_topk_select(const torch::Tensor& vals, const torch::Tensor& idx, int64_t K,
@@ -225,7 +233,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.attr("debug_bounds") = false;
   m.def("gemm_tn_bf16", &sb::gemm_tn_bf16, py::arg("A"), py::arg("B"), py::arg("bias"), py::arg("scale"),
         py::arg("relu"), py::arg("out"), py::arg("cmax"), py::arg("status"), py::arg("max_ctas"),
-        py::arg("tmax") = py::none());
+        py::arg("tmax") = py::none(), py::arg("amax") = py::none());
   m.def("adam_bdec", &sb::adam_bdec);
   m.def("adam_rows", &sb::adam_rows);
   m.def("gemm_ag_tn_bf16", &sb::gemm_ag_tn_bf16, py::arg("x_own"), py::arg("peer_bases"), py::arg("rank"),
@@ -253,6 +261,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rs_n") = 0, py::arg("hsum") = py::none(), py::arg("hoff") = py::none(),
         py::arg("colsum2") = py::none(), py::arg("addend") = py::none(), py::arg("oscale") = py::none());
   m.def("gemm_fsdp_dense_bf16", &sb::gemm_fsdp_dense_bf16);
+  m.def("mp_step", &sb::mp_step, py::arg("resid"), py::arg("resid_bf"), py::arg("key"), py::arg("acts"),
+        py::arg("done"), py::arg("idx_out"), py::arg("val_out"), py::arg("n_active"), py::arg("W"), py::arg("thresh"),
+        py::arg("stop_dup"));
+  m.def("mp_backward", &sb::mp_backward, py::arg("resid"), py::arg("g_resid"), py::arg("g_acts"), py::arg("idx"),
+        py::arg("val"), py::arg("g_W"), py::arg("W"));
   m.def("attention_fwd", &sb::attention_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"),
         py::arg("scale"), py::arg("softcap"), py::arg("causal"), py::arg("status"));
   m.def("symm_alloc", &sb::symm_alloc);

@@ -74,7 +74,18 @@ struct Epi {
   __nv_bfloat16* tmax;     // [M, ldt] tile maxima (one per 256 columns) or nullptr
   int64_t ldt;
   int tma_out;             // 1: `out` is written by TMA tile stores from a per-warp staging tile
+  unsigned long long* amax;  // [M] row argmax keys (atomicMax; see argmax_key) or nullptr
 };
+
+// Order-preserving 64-bit key of (value, column) for a row argmax by atomicMax: the high word maps
+// the fp32 value to an unsigned integer with the same order (sign bit flipped for values >= 0,
+// all bits flipped for negatives; -0 is taken as +0), the low word is 0xFFFFFFFF - column so that
+// of equal values the smallest column wins.  A key of 0 means no column was seen.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int col) {
+  uint32_t b = v == 0.f ? 0u : __float_as_uint(v);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return (static_cast<unsigned long long>(b) << 32) | static_cast<unsigned long long>(0xFFFFFFFFu - uint32_t(col));
+}
 
 // Epilogue of the dense SAE steps (every field optional; order of application below).
 //   v = acc - r1_row[row] * r1_col[col] + bias[col]                      (rank-1 correction, bias)
@@ -437,6 +448,8 @@ __device__ __forceinline__ void epilogue_tile(const Epi& ep, uint32_t trow, int 
                                               const CUtensorMap* tmO = nullptr, uint8_t* stage = nullptr,
                                               int row0 = 0, int lane = 0) {
   float tile_max = -INFINITY;
+  float best_v = -INFINITY;  // row argmax over this tile (ep.amax): first column of the largest value
+  int best_c = -1;
   const bool tma = tmO != nullptr && ep.out != nullptr;
 #pragma unroll 1
   for (int c = 0; c < BN / 32; ++c) {
@@ -491,6 +504,14 @@ __device__ __forceinline__ void epilogue_tile(const Epi& ep, uint32_t trow, int 
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
     }
+    if (ep.amax) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if ((full || col0 + j < N) && v[j] > best_v) {
+          best_v = v[j];
+          best_c = col0 + j;
+        }
+    }
     uint32_t packed[16];
     float cm = -INFINITY;
 #pragma unroll
@@ -535,6 +556,7 @@ __device__ __forceinline__ void epilogue_tile(const Epi& ep, uint32_t trow, int 
     tile_max = fmaxf(tile_max, cm);
   }
   if (ep.tmax && row < M) ep.tmax[int64_t(row) * ep.ldt + nt] = __float2bfloat16_rn(tile_max);
+  if (ep.amax && row < M && best_c >= 0) atomicMax(ep.amax + row, argmax_key(best_v, best_c));
 }
 
 // All-gather pushers (two warps, ct = 0..63): claim (operand, distance d, own unit j) items from
@@ -977,8 +999,14 @@ static int num_sms_cached() {
 static gemm::Epi make_epi(int64_t M, int64_t N, const c10::optional<torch::Tensor>& bias,
                           const c10::optional<torch::Tensor>& scale, bool relu,
                           const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& cmax,
-                          const c10::optional<torch::Tensor>& tmax = c10::nullopt) {
+                          const c10::optional<torch::Tensor>& tmax = c10::nullopt,
+                          const c10::optional<torch::Tensor>& amax = c10::nullopt) {
   gemm::Epi ep{};
+  if (amax) {
+    SB_CHECK(amax->scalar_type() == at::kLong && amax->numel() == M && amax->is_contiguous(),
+             "gemm_tn_bf16: amax must be int64 [M] (row argmax keys)");
+    ep.amax = reinterpret_cast<unsigned long long*>(amax->data_ptr());
+  }
   if (out) {
     SB_CHECK(out->scalar_type() == at::kBFloat16 && out->size(0) == M && out->size(1) == N &&
                     out->stride(1) == 1 && out->stride(0) % 8 == 0,
@@ -1098,11 +1126,15 @@ static void launch_gemm(const void* a_ptr, int64_t lda, int64_t M, const torch::
 }
 
 // out = epilogue(A @ B^T).  A: [M, K] bf16 (row stride lda), B: [N, K] bf16.  Optional
-// bias/scale fp32 [N].  Returns nothing; writes `out` [M, N] bf16 and/or `cmax` [M, N/32] bf16.
+// bias/scale fp32 [N].  Returns nothing; writes `out` [M, N] bf16 and/or `cmax` [M, N/32] bf16,
+// and with `amax` (int64 [M], zeroed by the caller) folds each row's argmax of the fp32 epilogue
+// values into an order-preserving key by atomicMax (value in the high word, 0xFFFFFFFF - column in
+// the low word).
 void gemm_tn_bf16(const torch::Tensor& A, const torch::Tensor& B, const c10::optional<torch::Tensor>& bias,
                   const c10::optional<torch::Tensor>& scale, bool relu,
                   const c10::optional<torch::Tensor>& out, const c10::optional<torch::Tensor>& cmax,
-                  const torch::Tensor& status, int64_t max_ctas, const c10::optional<torch::Tensor>& tmax) {
+                  const torch::Tensor& status, int64_t max_ctas, const c10::optional<torch::Tensor>& tmax,
+                  const c10::optional<torch::Tensor>& amax) {
   SB_CHECK(A.is_cuda() && B.is_cuda(), "gemm_tn_bf16: CUDA tensors required");
   SB_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16,
               "gemm_tn_bf16: bf16 operands required");
@@ -1114,7 +1146,7 @@ void gemm_tn_bf16(const torch::Tensor& A, const torch::Tensor& B, const c10::opt
               "gemm_tn_bf16: chunk / tile maxima need N to be a multiple of 256, got ", N);
   SB_CHECK(M >= 1 && M < (1ll << 31) && N < (1ll << 31), "gemm_tn_bf16: size");
   const at::cuda::CUDAGuard guard(A.device());
-  const gemm::Epi ep = make_epi(M, N, bias, scale, relu, out, cmax, tmax);
+  const gemm::Epi ep = make_epi(M, N, bias, scale, relu, out, cmax, tmax, amax);
   launch_gemm<false>(A.data_ptr(), A.stride(0), M, B, ep, status, max_ctas, gemm::Ag{}, use_pair(M));
 }
 

@@ -27,6 +27,8 @@
         Streaming run under the topology supervisor with one switch: timeline, downtime, tokens/s.
     python -m saelens_b200.perf_cases dense-step [--d-in 2304 --d-sae 65536 --batch 4096]
         Standard and Gated training steps: native dense engines vs the PyTorch (cuBLAS) path.
+    python -m saelens_b200.perf_cases mp [--batch 4096 --d-in 768 --d-sae 24576 --iters 64]
+        Matching-pursuit encode (forward, forward + backward): native kernels vs the PyTorch loop.
 """
 
 from __future__ import annotations
@@ -951,6 +953,74 @@ def dense_step(args: argparse.Namespace) -> None:
     print(json.dumps({"d_in": args.d_in, "d_sae": args.d_sae, "batch": args.batch, **res}), flush=True)
 
 
+def mp_case(args: argparse.Namespace) -> None:
+    """Matching-pursuit encode, one GPU: the native path (tcgen05 score GEMM with fused row argmax
+    + fused per-row update; `ops.mp`) against the PyTorch loop of the reference's iteration, on
+    the same fp32 inputs, for a forward alone and a forward + backward of sum(codes * g).  Inputs
+    are sparse combinations of a random unit-norm dictionary plus noise; the run stops by the
+    reference's rules (duplicate support, residual threshold) or at --iters.  CUDA-event ms per
+    call after one warm-up call; also the iterations run and the mean L0."""
+    import torch
+
+    from saelens_b200.models.matching_pursuit import _encode_matching_pursuit_torch
+    from saelens_b200.ops import mp
+
+    B, D, N = args.batch, args.d_in, args.d_sae
+    g = torch.Generator(device="cuda").manual_seed(0)
+    W = torch.randn(N, D, device="cuda", generator=g)
+    W = W / W.norm(dim=1, keepdim=True)
+    cols = torch.randint(0, N, (B, args.active), device="cuda", generator=g)
+    codes = torch.zeros(B, N, device="cuda").scatter_(1, cols, torch.rand(B, args.active, device="cuda",
+                                                                         generator=g) + 0.5)
+    x = codes @ W + args.noise * torch.randn(B, D, device="cuda", generator=g)
+    del codes
+    g_out = torch.randn(B, N, device="cuda", generator=g)
+    it = args.iters
+
+    def native_fwd():
+        with torch.no_grad():
+            return mp.encode_matching_pursuit(x, W, args.thresh, it, True)
+
+    def torch_fwd():
+        with torch.no_grad():
+            return _encode_matching_pursuit_torch(x, W, args.thresh, it, True)
+
+    def native_fb():
+        xr, Wr = x.detach().requires_grad_(True), W.detach().requires_grad_(True)
+        (mp.encode_matching_pursuit(xr, Wr, args.thresh, it, True) * g_out).sum().backward()
+
+    def torch_fb():
+        xr, Wr = x.detach().requires_grad_(True), W.detach().requires_grad_(True)
+        (_encode_matching_pursuit_torch(xr, Wr, args.thresh, it, True) * g_out).sum().backward()
+
+    def timed(fn) -> float:
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.reps
+
+    _, _, idx, _ = mp.trace_matching_pursuit(x, W, args.thresh, it, True)
+    acts = native_fwd()
+    res = {"iterations": int(idx.shape[0]), "mean_l0": round(float((acts != 0).sum(1).float().mean()), 2),
+           "rel_residual": round(float(((x - acts @ W).norm(dim=1) / x.norm(dim=1)).mean()), 4)}
+    del acts
+    res["native_fwd_ms"] = round(timed(native_fwd), 3)
+    res["native_fwd_bwd_ms"] = round(timed(native_fb), 3)
+    if not args.no_torch:
+        res["torch_fwd_ms"] = round(timed(torch_fwd), 3)
+        res["torch_fwd_bwd_ms"] = round(timed(torch_fb), 3)
+        res["speedup_fwd"] = round(res["torch_fwd_ms"] / res["native_fwd_ms"], 2)
+        res["speedup_fwd_bwd"] = round(res["torch_fwd_bwd_ms"] / res["native_fwd_bwd_ms"], 2)
+    gemm_flops = 2.0 * B * D * N * res["iterations"]
+    res["score_gemm_tflops_equiv"] = round(gemm_flops / res["native_fwd_ms"] / 1e9, 1)
+    print(json.dumps({"batch": B, "d_in": D, "d_sae": N, **res}), flush=True)
+
+
 def main() -> None:
     p = argparse.ArgumentParser(prog="python -m saelens_b200.perf_cases")
     sub = p.add_subparsers(dest="cmd", required=True)
@@ -1040,6 +1110,16 @@ def main() -> None:
     lmp.add_argument("--batch", type=int, default=8)
     lmp.add_argument("--ctx", type=int, default=1024)
     lmp.add_argument("--reps", type=int, default=5)
+    mpc = sub.add_parser("mp", help="matching-pursuit encode: native kernels vs the PyTorch loop")
+    mpc.add_argument("--batch", type=int, default=4096)
+    mpc.add_argument("--d-in", type=int, default=768)
+    mpc.add_argument("--d-sae", type=int, default=24576)
+    mpc.add_argument("--active", type=int, default=16, help="dictionary atoms per synthetic row")
+    mpc.add_argument("--noise", type=float, default=0.02)
+    mpc.add_argument("--thresh", type=float, default=0.01)
+    mpc.add_argument("--iters", type=int, default=64)
+    mpc.add_argument("--reps", type=int, default=3)
+    mpc.add_argument("--no-torch", action="store_true")
     args, rest = p.parse_known_args()
     if args.cmd == "topology-switch":
         args.worker_args = rest
@@ -1047,7 +1127,8 @@ def main() -> None:
         p.error(f"unrecognized arguments: {' '.join(rest)}")
     {"gemm-step": gemm_step, "lm": lm, "phases": phases, "fused-case": fused_case, "gemm": gemm, "ddp": ddp, "allreduce": allreduce, "router": router,
      "tpdp": tpdp, "fsdp": ddp, "ddp-hook": ddp_hook, "ring": ring, "fsdp-jumprelu": fsdp_jumprelu,
-     "attention": attention_case, "topology-switch": topology_switch, "dense-step": dense_step}[args.cmd](args)
+     "attention": attention_case, "topology-switch": topology_switch, "dense-step": dense_step,
+     "mp": mp_case}[args.cmd](args)
 
 
 if __name__ == "__main__":
