@@ -24,6 +24,7 @@ __all__ = [
     "row_topk",
     "decode_mse",
     "attention",
+    "gather_rows",
     "StatusWord",
 ]
 
@@ -236,4 +237,16 @@ def gemm_dense(
     native().gemm_dense_bf16(a, a_mn, b, b_mn, out=out if want_out else None, status=st.tensor, **epi)
     if status is None:
         st.check("gemm_dense")
+    return out
+
+
+def gather_rows(a: torch.Tensor, b: torch.Tensor | None = None, perm: torch.Tensor | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """`torch.cat([a, b])[perm]` in one pass on the device (rows moved as raw bytes, warp per
+    row).  `perm` is int64 on the device; without it the first `len(out)` rows are copied.
+    Indices outside the two sources leave their output row untouched."""
+    n = (a.shape[0] + (0 if b is None else b.shape[0])) if perm is None else perm.shape[0]
+    if out is None:
+        out = torch.empty((n, *a.shape[1:]), dtype=a.dtype, device=a.device)
+    native().gather_rows(a, b, perm, out)
     return out

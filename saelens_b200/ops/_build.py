@@ -40,6 +40,7 @@ SOURCES = [
     "lm_kernels.cu",
     "attention.cu",
     "mp.cu",
+    "rows.cu",
 ]
 
 NVCC_FLAGS = [

@@ -158,6 +158,8 @@ void gemm_fsdp_dense_bf16(const torch::Tensor& A, const torch::Tensor& w_own, co
                           const c10::optional<torch::Tensor>& bias, const c10::optional<torch::Tensor>& thr,
                           const c10::optional<torch::Tensor>& colcnt, const c10::optional<torch::Tensor>& nnz,
                           const torch::Tensor& status, const torch::Tensor& ticket);
+void gather_rows(const torch::Tensor& a, const c10::optional<torch::Tensor>& b, const c10::optional<torch::Tensor>& perm,
+                 const torch::Tensor& out, const c10::optional<torch::Tensor>& bad);
 void mp_step(const torch::Tensor& resid, const torch::Tensor& resid_bf, const torch::Tensor& key,
              const torch::Tensor& acts, const torch::Tensor& done, const c10::optional<torch::Tensor>& idx_out,
              const c10::optional<torch::Tensor>& val_out, const torch::Tensor& n_active, const torch::Tensor& W,
@@ -261,6 +263,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rs_n") = 0, py::arg("hsum") = py::none(), py::arg("hoff") = py::none(),
         py::arg("colsum2") = py::none(), py::arg("addend") = py::none(), py::arg("oscale") = py::none());
   m.def("gemm_fsdp_dense_bf16", &sb::gemm_fsdp_dense_bf16);
+  m.def("gather_rows", &sb::gather_rows, py::arg("a"), py::arg("b"), py::arg("perm"), py::arg("out"),
+        py::arg("bad") = py::none());
   m.def("mp_step", &sb::mp_step, py::arg("resid"), py::arg("resid_bf"), py::arg("key"), py::arg("acts"),
         py::arg("done"), py::arg("idx_out"), py::arg("val_out"), py::arg("n_active"), py::arg("W"), py::arg("thresh"),
         py::arg("stop_dup"));

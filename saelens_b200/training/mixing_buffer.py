@@ -33,6 +33,23 @@ def _take(b: Batch, idx: torch.Tensor | slice) -> Batch:
     return b[idx]
 
 
+def _permute(parts: list[Batch], perm: torch.Tensor) -> Batch:
+    """`cat(parts)[perm]`.  On CUDA one native pass gathers from the last part and the rows
+    before it (`ops.gather_rows`), so the concatenated buffer is never written first."""
+    first = parts[0]
+    t0 = next(iter(first.values())) if isinstance(first, dict) else first
+    if not t0.is_cuda:
+        return _take(_cat(parts), perm)
+    from saelens_b200 import ops
+
+    head = parts[0] if len(parts) <= 2 else _cat(parts[:-1])
+    tail = parts[-1] if len(parts) >= 2 else None
+    if isinstance(head, dict):
+        return {k: ops.gather_rows(v, None if tail is None else tail[k], perm)  # type: ignore[index]
+                for k, v in head.items()}
+    return ops.gather_rows(head, tail, perm)  # type: ignore[arg-type]
+
+
 @torch.no_grad()
 def mixing_buffer(buffer_size: int, batch_size: int, activations_loader: Iterator[Batch],
                   mix_fraction: float = 0.5, generator: torch.Generator | None = None) -> Iterator[Batch]:
@@ -47,20 +64,25 @@ def mixing_buffer(buffer_size: int, batch_size: int, activations_loader: Iterato
     if not 0 <= mix_fraction <= 1:
         raise ValueError("mix_fraction must be in [0, 1]")
     keep = int(buffer_size * mix_fraction)
-    held: Batch | None = None
+    parts: list[Batch] = []  # held rows first, then the batches received since the last fill
+    n = 0
     for batch in activations_loader:
-        held = batch if held is None else _cat([held, batch])
-        n = _rows(held)
+        parts.append(batch)
+        n += _rows(batch)
         if n < buffer_size:
             continue
         if mix_fraction > 0:
-            dev = next(iter(held.values())).device if isinstance(held, dict) else held.device
-            held = _take(held, torch.randperm(n, generator=generator).to(dev))
+            dev = next(iter(batch.values())).device if isinstance(batch, dict) else batch.device
+            held = _permute(parts, torch.randperm(n, generator=generator).to(dev))
+        else:
+            held = parts[0] if len(parts) == 1 else _cat(parts)
         n_batches = max(1, (n - keep) // batch_size)
         cut = n_batches * batch_size
-        serve, held = _take(held, slice(0, cut)), _take(held, slice(cut, None))
+        serve, rest = _take(held, slice(0, cut)), _take(held, slice(cut, None))
+        parts, n = ([rest] if n > cut else []), n - cut
         for i in range(n_batches):
             yield _take(serve, slice(i * batch_size, (i + 1) * batch_size))
-    if held is not None:
+    if parts:
+        held = parts[0] if len(parts) == 1 else _cat(parts)
         for i in range(_rows(held) // batch_size):
             yield _take(held, slice(i * batch_size, (i + 1) * batch_size))
