@@ -2,8 +2,8 @@
 
 `native()` returns the compiled extension; every wrapper here calls it directly, so a missing
 build fails loudly on a CUDA machine instead of silently running a PyTorch fallback.  The
-pure-PyTorch restatements of the same ops live in `saelens_b200.ops.reference` and serve as
-the CPU oracle in tests.
+PyTorch paths of the models (`saelens_b200.models`) compute the same quantities on any device
+and serve as the oracle of the GPU tests.
 """
 
 from __future__ import annotations

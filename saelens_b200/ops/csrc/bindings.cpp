@@ -163,7 +163,7 @@ void gather_rows(const torch::Tensor& a, const c10::optional<torch::Tensor>& b, 
 void mp_step(const torch::Tensor& resid, const torch::Tensor& resid_bf, const torch::Tensor& key,
              const torch::Tensor& acts, const torch::Tensor& done, const c10::optional<torch::Tensor>& idx_out,
              const c10::optional<torch::Tensor>& val_out, const torch::Tensor& n_active, const torch::Tensor& W,
-             double thresh, bool stop_dup);
+             double thresh, bool stop_dup, const c10::optional<torch::Tensor>& rows);
 void mp_backward(const torch::Tensor& resid, const torch::Tensor& g_resid, const torch::Tensor& g_acts,
                  const torch::Tensor& idx, const torch::Tensor& val, const c10::optional<torch::Tensor>& g_W,
                  const torch::Tensor& W);
@@ -267,7 +267,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("bad") = py::none());
   m.def("mp_step", &sb::mp_step, py::arg("resid"), py::arg("resid_bf"), py::arg("key"), py::arg("acts"),
         py::arg("done"), py::arg("idx_out"), py::arg("val_out"), py::arg("n_active"), py::arg("W"), py::arg("thresh"),
-        py::arg("stop_dup"));
+        py::arg("stop_dup"), py::arg("rows") = py::none());
   m.def("mp_backward", &sb::mp_backward, py::arg("resid"), py::arg("g_resid"), py::arg("g_acts"), py::arg("idx"),
         py::arg("val"), py::arg("g_W"), py::arg("W"));
   m.def("attention_fwd", &sb::attention_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"),

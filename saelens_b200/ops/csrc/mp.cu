@@ -63,6 +63,8 @@ struct StepArgs {
   int32_t* idx_out;           // [B] latent picked this iteration (-1 for stopped rows) or nullptr
   float* val_out;             // [B] value added this iteration (0 for stopped rows) or nullptr
   int32_t* n_active;          // += rows still running after this iteration
+  const int32_t* rows;        // [B] row of `acts` / idx_out / val_out for each residual row, or nullptr
+  int64_t n_out;              // rows of acts / idx_out / val_out (row-id bound)
   float thresh;               // residual-norm stop (<= 0: off)
   int stop_dup;               // stop when no new latent was added
   int B, D, N;
@@ -73,7 +75,9 @@ __global__ void __launch_bounds__(32 * WARPS) step_kernel(StepArgs a, const T* _
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * WARPS + (threadIdx.x >> 5);
   bool running = false;
-  if (row < a.B) {
+  // with `rows` the residual rows are a compacted subset: codes and the trace use the original row
+  const int64_t orow = row < a.B ? (a.rows ? int64_t(a.rows[row]) : int64_t(row)) : -1;
+  if (row < a.B && orow >= 0 && orow < a.n_out) {
     const unsigned long long k = a.key[row];
     __syncwarp();
     if (lane == 0) a.key[row] = 0ull;
@@ -124,7 +128,7 @@ __global__ void __launch_bounds__(32 * WARPS) step_kernel(StepArgs a, const T* _
       if (lane == 0) {
         bool added = false;
         if (i >= 0) {
-          float* c = a.acts + int64_t(row) * a.lda + i;
+          float* c = a.acts + orow * a.lda + i;
           const float old = *c, now = old + v;
           *c = now;
           added = old == 0.f && now != 0.f;
@@ -135,8 +139,8 @@ __global__ void __launch_bounds__(32 * WARPS) step_kernel(StepArgs a, const T* _
       }
     }
     if (lane == 0) {
-      if (a.idx_out) a.idx_out[row] = i;
-      if (a.val_out) a.val_out[row] = v;
+      if (a.idx_out) a.idx_out[orow] = i;
+      if (a.val_out) a.val_out[orow] = v;
     }
   }
   const int n = __syncthreads_count(running);
@@ -209,23 +213,26 @@ static void check_rows(const torch::Tensor& t, at::ScalarType dt, int64_t B, int
 void mp_step(const torch::Tensor& resid, const torch::Tensor& resid_bf, const torch::Tensor& key,
              const torch::Tensor& acts, const torch::Tensor& done, const c10::optional<torch::Tensor>& idx_out,
              const c10::optional<torch::Tensor>& val_out, const torch::Tensor& n_active, const torch::Tensor& W,
-             double thresh, bool stop_dup) {
+             double thresh, bool stop_dup, const c10::optional<torch::Tensor>& rows) {
   const int64_t B = resid.size(0), D = resid.size(1), N = W.size(0);
+  const int64_t n_out = acts.size(0);
   SB_CHECK(D % 8 == 0 && W.dim() == 2 && W.size(1) == D, "mp_step: D must be a multiple of 8 and W [N, D]");
   check_rows(resid, at::kFloat, B, D, "resid");
   check_rows(resid_bf, at::kBFloat16, B, D, "resid_bf");
   SB_CHECK(W.is_contiguous() && (W.scalar_type() == at::kFloat || W.scalar_type() == at::kBFloat16),
            "mp_step: W must be contiguous fp32 or bf16");
   SB_CHECK(key.scalar_type() == at::kLong && key.numel() == B && key.is_contiguous(), "mp_step: key int64 [B]");
-  SB_CHECK(acts.scalar_type() == at::kFloat && acts.dim() == 2 && acts.size(0) == B && acts.size(1) == N &&
-               acts.stride(1) == 1,
-           "mp_step: acts fp32 [B, N]");
+  SB_CHECK(acts.scalar_type() == at::kFloat && acts.dim() == 2 && acts.size(1) == N && acts.stride(1) == 1 &&
+               (rows ? n_out >= B : n_out == B),
+           "mp_step: acts fp32 [rows, N] (as many rows as resid without `rows`)");
+  if (rows) SB_CHECK(rows->is_cuda() && rows->scalar_type() == at::kInt && rows->numel() == B && rows->is_contiguous(),
+                     "mp_step: rows int32 [B]");
   SB_CHECK(done.scalar_type() == at::kByte && done.numel() == B && done.is_contiguous(), "mp_step: done uint8 [B]");
   SB_CHECK(n_active.scalar_type() == at::kInt && n_active.numel() >= 1, "mp_step: n_active int32");
-  if (idx_out) SB_CHECK(idx_out->scalar_type() == at::kInt && idx_out->numel() == B && idx_out->is_contiguous(),
-                        "mp_step: idx_out int32 [B]");
-  if (val_out) SB_CHECK(val_out->scalar_type() == at::kFloat && val_out->numel() == B && val_out->is_contiguous(),
-                        "mp_step: val_out fp32 [B]");
+  if (idx_out) SB_CHECK(idx_out->scalar_type() == at::kInt && idx_out->numel() == n_out && idx_out->is_contiguous(),
+                        "mp_step: idx_out int32 [acts rows]");
+  if (val_out) SB_CHECK(val_out->scalar_type() == at::kFloat && val_out->numel() == n_out && val_out->is_contiguous(),
+                        "mp_step: val_out fp32 [acts rows]");
   SB_CHECK(B < (1ll << 31) && N < (1ll << 31), "mp_step: size");
   const at::cuda::CUDAGuard guard(resid.device());
   mp::StepArgs a{};
@@ -238,6 +245,8 @@ void mp_step(const torch::Tensor& resid, const torch::Tensor& resid_bf, const to
   a.idx_out = idx_out ? idx_out->data_ptr<int32_t>() : nullptr;
   a.val_out = val_out ? val_out->data_ptr<float>() : nullptr;
   a.n_active = n_active.data_ptr<int32_t>();
+  a.rows = rows ? rows->data_ptr<int32_t>() : nullptr;
+  a.n_out = n_out;
   a.thresh = float(thresh);
   a.stop_dup = stop_dup ? 1 : 0;
   a.B = int(B);

@@ -35,29 +35,44 @@ def native_supported(sae_in_centered: torch.Tensor, W_dec: torch.Tensor) -> bool
             and W_dec.dtype in (torch.float32, torch.bfloat16))
 
 
+_COMPACT_MIN_ROWS = 256  # no compaction below one CTA-pair tile of rows
+
+
+def _compaction_enabled() -> bool:
+    return os.environ.get("SAELENS_B200_MP_COMPACT", "1") != "0"
+
+
 def _run(resid0: torch.Tensor, W_dec: torch.Tensor, residual_threshold: float, max_iterations: int,
          stop_on_duplicate_support: bool, record: bool):
     """The forward iterations.  Returns (codes fp32 [B, N], final residual fp32 [B, D], picks
-    int32 [T, B] or None, values fp32 [T, B] or None)."""
+    int32 [T, B] or None, values fp32 [T, B] or None).
+
+    Once at most half of the rows still run (and at least `_COMPACT_MIN_ROWS` would remain), the
+    running rows are gathered into smaller residual buffers, so later score GEMMs multiply only
+    those; `rows` maps them back to their rows of the codes and of the trace.  Stopped rows are
+    skipped by every later iteration anyway, so this changes no result."""
     from saelens_b200.ops import native
 
     nat = native()
     B, D = resid0.shape
     N = W_dec.shape[0]
     dev = resid0.device
-    resid = resid0.detach().to(torch.float32).contiguous().clone()
+    resid_full = resid0.detach().to(torch.float32).contiguous().clone()
     acts = torch.zeros(B, N, dtype=torch.float32, device=dev)
     if B == 0 or max_iterations <= 0:
-        return acts, resid, None, None
+        return acts, resid_full, None, None
     W = W_dec.detach().contiguous()
     W_bf = W if W.dtype == torch.bfloat16 else W.to(torch.bfloat16)
+    resid = resid_full  # the running rows' residuals (all rows until the first compaction)
     resid_bf = resid.to(torch.bfloat16)
+    rows: torch.Tensor | None = None  # int32 original row of each running row (None: identity)
     key = torch.zeros(B, dtype=torch.int64, device=dev)
     done = torch.zeros(B, dtype=torch.uint8, device=dev)
     counts = torch.zeros(max_iterations, dtype=torch.int32, device=dev)
-    idx = torch.empty(max_iterations, B, dtype=torch.int32, device=dev) if record else None
-    val = torch.empty(max_iterations, B, dtype=torch.float32, device=dev) if record else None
+    idx = torch.full((max_iterations, B), -1, dtype=torch.int32, device=dev) if record else None
+    val = torch.zeros(max_iterations, B, dtype=torch.float32, device=dev) if record else None
     stops = stop_on_duplicate_support or residual_threshold > 0
+    compact = stops and _compaction_enabled()
     host = torch.empty(max_iterations, dtype=torch.int32, pin_memory=True) if stops else None
     events: list[torch.cuda.Event] = []
     st = StatusWord(dev)
@@ -65,7 +80,7 @@ def _run(resid0: torch.Tensor, W_dec: torch.Tensor, residual_threshold: float, m
     for t in range(max_iterations):
         nat.gemm_tn_bf16(resid_bf, W_bf, None, None, True, None, None, st.tensor, 0, None, key)
         nat.mp_step(resid, resid_bf, key, acts, done, idx[t] if record else None, val[t] if record else None,
-                    counts[t:t + 1], W, float(residual_threshold), bool(stop_on_duplicate_support))
+                    counts[t:t + 1], W, float(residual_threshold), bool(stop_on_duplicate_support), rows)
         T = t + 1
         if not stops:
             continue
@@ -73,18 +88,32 @@ def _run(resid0: torch.Tensor, W_dec: torch.Tensor, residual_threshold: float, m
         ev = torch.cuda.Event()
         ev.record()
         events.append(ev)
-        if t >= 1:
-            events[t - 1].synchronize()
-            if int(host[t - 1]) == 0:
-                T = t  # iteration t ran with every row stopped: it added nothing
-                break
-    else:
-        if stops and events:
-            events[-1].synchronize()
+        if t == 0:
+            continue
+        events[t - 1].synchronize()
+        running = int(host[t - 1])
+        if running == 0:
+            T = t  # iteration t ran with every row stopped: it added nothing
+            break
+        M = resid.shape[0]
+        if compact and t + 1 < max_iterations and running <= M // 2 and running >= _COMPACT_MIN_ROWS:
+            keep = torch.nonzero(done == 0).squeeze(1)  # rows still running after iteration t
+            if keep.numel() == 0:
+                continue
+            if rows is not None:  # the rows that leave keep their final residual in resid_full
+                resid_full.index_copy_(0, rows.long(), resid)
+            new_rows = keep.to(torch.int32) if rows is None else rows.index_select(0, keep)
+            resid = resid.index_select(0, keep)
+            resid_bf = resid_bf.index_select(0, keep)
+            rows = new_rows.contiguous()
+            key = torch.zeros(rows.numel(), dtype=torch.int64, device=dev)
+            done = torch.zeros(rows.numel(), dtype=torch.uint8, device=dev)
+    if rows is not None:
+        resid_full.index_copy_(0, rows.long(), resid)
     st.check("matching pursuit score GEMM")
     if record:
-        return acts, resid, idx[:T], val[:T]
-    return acts, resid, None, None
+        return acts, resid_full, idx[:T], val[:T]
+    return acts, resid_full, None, None
 
 
 class _MatchingPursuitEncode(torch.autograd.Function):
