@@ -1050,11 +1050,12 @@ static bool use_pair(int64_t M) {
   return !off && M >= 2 * gemm::BM;
 }
 
-// SAELENS_B200_GEMM_STAGED_STORE=1 stores the dense epilogue's full 32-column chunks through the
-// warp's staging tile; otherwise per-thread row stores
+// The dense epilogue stores its full 32-column chunks through the warp's staging tile (8 rows x 64
+// contiguous bytes per store instruction, also into a peer's landing slot in reduce-scatter mode);
+// SAELENS_B200_GEMM_STAGED_STORE=0 selects per-thread row stores
 static bool staged_stores_enabled() {
   const char* e = std::getenv("SAELENS_B200_GEMM_STAGED_STORE");
-  return e && e[0] == '1' && e[1] == 0;
+  return !(e && e[0] == '0' && e[1] == 0);
 }
 
 template <bool AG>

@@ -983,19 +983,11 @@ __global__ void __launch_bounds__(LR_THREADS, 2) latent_rows_kernel(const __grid
   const int tw = gridDim.x * LR_WARPS;
   const int sl = gw % a.nslices;
   const int vbase = sl * 32 * VPL + lane;
-  float bd[VPL][8], bt[VPL][8];
+  float bt[VPL][8];
 #pragma unroll
-  for (int u = 0; u < VPL; ++u) {
-    const int vi = vbase + 32 * u;
+  for (int u = 0; u < VPL; ++u)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) bd[u][e] = bt[u][e] = 0.f;
-    if (a.b_dec && vi < nvec) {
-      const float4 b0 = __ldg(reinterpret_cast<const float4*>(a.b_dec) + 2 * vi);
-      const float4 b1 = __ldg(reinterpret_cast<const float4*>(a.b_dec) + 2 * vi + 1);
-      bd[u][0] = b0.x; bd[u][1] = b0.y; bd[u][2] = b0.z; bd[u][3] = b0.w;
-      bd[u][4] = b1.x; bd[u][5] = b1.y; bd[u][6] = b1.z; bd[u][7] = b1.w;
-    }
-  }
+    for (int e = 0; e < 8; ++e) bt[u][e] = 0.f;
   float sq = 0.f;
   const int jstep = tw / a.nslices;
   int j = a.j0 + gw / a.nslices;
@@ -1030,48 +1022,7 @@ __global__ void __launch_bounds__(LR_THREADS, 2) latent_rows_kernel(const __grid
       }
       continue;
     }
-    float gd[VPL][8], ge[VPL][8];
-#pragma unroll
-    for (int u = 0; u < VPL; ++u)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) gd[u][e] = ge[u][e] = 0.f;
-    float gbe = 0.f;
-    for (int64_t pos = beg; pos < end; pos += 2) {
-      const bool two = pos + 1 < end;
-      int r0 = a.prow[pos], r1 = two ? a.prow[pos + 1] : r0;
-      float c0 = a.pcoef[pos], c1 = two ? a.pcoef[pos + 1] : 0.f;
-      float z0 = a.pdz[pos], z1 = two ? a.pdz[pos + 1] : 0.f;
-      if (!SB_IN_RANGE(r0 & 0x7fffffff, a.M)) r0 = 0, c0 = z0 = 0.f;  // debug builds: drop the entry
-      if (!SB_IN_RANGE(r1 & 0x7fffffff, a.M)) r1 = 0, c1 = z1 = 0.f;
-      const __nv_bfloat16* g0 = ((r0 < 0) ? a.daux : a.dxhat) + int64_t(r0 & 0x7fffffff) * a.D;
-      const __nv_bfloat16* g1 = ((r1 < 0) ? a.daux : a.dxhat) + int64_t(r1 & 0x7fffffff) * a.D;
-      const __nv_bfloat16* x0 = a.x + int64_t(r0 & 0x7fffffff) * a.ldx;
-      const __nv_bfloat16* x1 = a.x + int64_t(r1 & 0x7fffffff) * a.ldx;
-      uint4 G0[VPL], G1[VPL], X0[VPL], X1[VPL];
-#pragma unroll
-      for (int u = 0; u < VPL; ++u) {
-        const int vi = vbase + 32 * u;
-        const bool ok = vi < nvec;
-        G0[u] = ok ? __ldg(reinterpret_cast<const uint4*>(g0) + vi) : make_uint4(0, 0, 0, 0);
-        X0[u] = ok ? __ldg(reinterpret_cast<const uint4*>(x0) + vi) : make_uint4(0, 0, 0, 0);
-        G1[u] = (ok && two) ? __ldg(reinterpret_cast<const uint4*>(g1) + vi) : make_uint4(0, 0, 0, 0);
-        X1[u] = (ok && two) ? __ldg(reinterpret_cast<const uint4*>(x1) + vi) : make_uint4(0, 0, 0, 0);
-      }
-#pragma unroll
-      for (int u = 0; u < VPL; ++u) {
-        float f0[8], f1[8], y0[8], y1[8];
-        bf16x8_to_f32(G0[u], f0);
-        bf16x8_to_f32(G1[u], f1);
-        bf16x8_to_f32(X0[u], y0);
-        bf16x8_to_f32(X1[u], y1);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          gd[u][e] += c0 * f0[e] + c1 * f1[e];
-          ge[u][e] += z0 * (y0[e] - bd[u][e]) + z1 * (y1[e] - bd[u][e]);
-        }
-      }
-      gbe += z0 + z1;
-    }
+    // the W_enc slice of the b_dec term does not depend on the pairs: issue it first
     uint4 WE[VPL];
     if (a.bpart) {
 #pragma unroll
@@ -1079,6 +1030,83 @@ __global__ void __launch_bounds__(LR_THREADS, 2) latent_rows_kernel(const __grid
         const int vi = vbase + 32 * u;
         WE[u] = vi < nvec ? __ldg(reinterpret_cast<const uint4*>(a.W_enc + int64_t(j) * a.D) + vi)
                           : make_uint4(0, 0, 0, 0);
+      }
+    }
+    float gd[VPL][8], ge[VPL][8];
+#pragma unroll
+    for (int u = 0; u < VPL; ++u)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) gd[u][e] = ge[u][e] = 0.f;
+    float gbe = 0.f;
+    // pair entries 32 at a time: lane l loads entry cb + l in one round trip, and each pair's row,
+    // coefficient and dz reach the warp by shuffles (the pairs of a latent are few, so one round
+    // trip usually covers them all)
+    for (int64_t cb = beg; cb < end; cb += 32) {
+      const int nc = end - cb < 32 ? int(end - cb) : 32;
+      int mr = 0;
+      float mc = 0.f, mz = 0.f;
+      if (lane < nc) {
+        mr = a.prow[cb + lane];
+        mc = a.pcoef[cb + lane];
+        mz = a.pdz[cb + lane];
+        if (!SB_IN_RANGE(mr & 0x7fffffff, a.M)) mr = 0, mc = mz = 0.f;  // debug builds: drop the entry
+      }
+      for (int q = 0; q < nc; q += 2) {
+        const bool two = q + 1 < nc;
+        const int r0 = __shfl_sync(0xffffffffu, mr, q);
+        const float c0 = __shfl_sync(0xffffffffu, mc, q);
+        const float z0 = __shfl_sync(0xffffffffu, mz, q);
+        const int q1 = two ? q + 1 : q;
+        const int r1 = __shfl_sync(0xffffffffu, mr, q1);
+        const float c1 = two ? __shfl_sync(0xffffffffu, mc, q1) : 0.f;
+        const float z1 = two ? __shfl_sync(0xffffffffu, mz, q1) : 0.f;
+        const __nv_bfloat16* g0 = ((r0 < 0) ? a.daux : a.dxhat) + int64_t(r0 & 0x7fffffff) * a.D;
+        const __nv_bfloat16* g1 = ((r1 < 0) ? a.daux : a.dxhat) + int64_t(r1 & 0x7fffffff) * a.D;
+        const __nv_bfloat16* x0 = a.x + int64_t(r0 & 0x7fffffff) * a.ldx;
+        const __nv_bfloat16* x1 = a.x + int64_t(r1 & 0x7fffffff) * a.ldx;
+        uint4 G0[VPL], G1[VPL], X0[VPL], X1[VPL];
+#pragma unroll
+        for (int u = 0; u < VPL; ++u) {
+          const int vi = vbase + 32 * u;
+          const bool ok = vi < nvec;
+          G0[u] = ok ? __ldg(reinterpret_cast<const uint4*>(g0) + vi) : make_uint4(0, 0, 0, 0);
+          X0[u] = ok ? __ldg(reinterpret_cast<const uint4*>(x0) + vi) : make_uint4(0, 0, 0, 0);
+          G1[u] = (ok && two) ? __ldg(reinterpret_cast<const uint4*>(g1) + vi) : make_uint4(0, 0, 0, 0);
+          X1[u] = (ok && two) ? __ldg(reinterpret_cast<const uint4*>(x1) + vi) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < VPL; ++u) {
+          float f0[8], f1[8], y0[8], y1[8];
+          bf16x8_to_f32(G0[u], f0);
+          bf16x8_to_f32(G1[u], f1);
+          bf16x8_to_f32(X0[u], y0);
+          bf16x8_to_f32(X1[u], y1);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            gd[u][e] += c0 * f0[e] + c1 * f1[e];
+            ge[u][e] += z0 * y0[e] + z1 * y1[e];
+          }
+        }
+        gbe += z0 + z1;
+      }
+    }
+    // sum dz (x - b_dec) = sum dz x - (sum dz) b_dec
+    if (a.b_dec) {
+#pragma unroll
+      for (int u = 0; u < VPL; ++u) {
+        const int vi = vbase + 32 * u;
+        if (vi < nvec) {
+          const float4 b0 = __ldg(reinterpret_cast<const float4*>(a.b_dec) + 2 * vi);
+          const float4 b1 = __ldg(reinterpret_cast<const float4*>(a.b_dec) + 2 * vi + 1);
+          ge[u][0] -= gbe * b0.x;
+          ge[u][1] -= gbe * b0.y;
+          ge[u][2] -= gbe * b0.z;
+          ge[u][3] -= gbe * b0.w;
+          ge[u][4] -= gbe * b1.x;
+          ge[u][5] -= gbe * b1.y;
+          ge[u][6] -= gbe * b1.z;
+          ge[u][7] -= gbe * b1.w;
+        }
       }
     }
 #pragma unroll
