@@ -156,7 +156,7 @@ class NativeLinear(nn.Module):
                     if self._bias_f32 is None or self._bias_f32.device != w.device:
                         self._bias_f32 = self.bias.detach().float().contiguous()
                     b = self._bias_f32
-                out, _ = ops.gemm_tn(x2, w, bias=b)
+                out, _ = ops.gemm_tn(x2, w, bias=b, status=_status_for(x2))
                 if not out.is_contiguous():  # a width that is not a multiple of 8
                     out = out.contiguous()
                 return out.view(*shp[:-1], w.shape[0])
@@ -197,7 +197,7 @@ def _fused_linear(x: torch.Tensor, cache: _FusedWeights, layers: list[NativeLine
     x2 = x.reshape(-1, x.shape[-1])
     if not x2.is_contiguous():
         x2 = x2.contiguous()
-    out, _ = ops.gemm_tn(x2, w, bias=b)
+    out, _ = ops.gemm_tn(x2, w, bias=b, status=_status_for(x2))
     return out.view(*x.shape[:-1], w.shape[0]) if out.is_contiguous() else out.reshape(*x.shape[:-1], w.shape[0])
 
 
@@ -207,7 +207,7 @@ def _tied_unembed(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         from saelens_b200 import ops
 
         x2 = x.reshape(-1, x.shape[-1]).contiguous()
-        out, _ = ops.gemm_tn(x2, w)
+        out, _ = ops.gemm_tn(x2, w, status=_status_for(x2))
         return out.contiguous().view(*x.shape[:-1], w.shape[0])
     return x @ w.T
 
@@ -215,6 +215,21 @@ def _tied_unembed(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
 # Set to True to run the producer on PyTorch ops even on CUDA (the comparison arm of the
 # producer timing case); never needed otherwise.
 FORCE_TORCH = False
+
+# One device status word per CUDA device for the producer's kernels: the GEMMs and attention
+# report a timed-out wait there, and HookedLM.forward reads it once per forward instead of each
+# kernel reading its own (a device synchronisation per call, which would drain the launch queue
+# between every projection).
+_STATUS: dict[torch.device, Any] = {}
+
+
+def _status_for(t: torch.Tensor):
+    st = _STATUS.get(t.device)
+    if st is None:
+        from saelens_b200.ops import StatusWord
+
+        st = _STATUS[t.device] = StatusWord(t.device)
+    return st
 
 
 def _native_ok(t: torch.Tensor) -> bool:
@@ -361,7 +376,8 @@ class Attention(nn.Module):
 
             # tcgen05 prefill attention: K/V heads are read in place by their query-head group,
             # the soft-cap (Gemma-2) is applied to the logits inside the kernel
-            z = ops.attention(q, k, v, self.scale, softcap=self.cfg.attn_softcap, causal=True)
+            z = ops.attention(q, k, v, self.scale, softcap=self.cfg.attn_softcap, causal=True,
+                              status=_status_for(q))
             z = self._hook(self.hook_z, z, 2)
             return self._out(z.reshape(B, S, H * dh))
         qh, kh, vh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
@@ -574,6 +590,14 @@ class HookedLM(HookedRootModule):
     def forward(self, tokens: torch.Tensor, return_type: str | None = "logits",
                 stop_at_layer: int | None = None, start_at_layer: int | None = None,
                 residual: torch.Tensor | None = None) -> torch.Tensor | None:
+        out = self._forward(tokens, return_type, stop_at_layer, start_at_layer, residual)
+        dev = self.embed.weight.device
+        if dev in _STATUS:
+            _STATUS[dev].check("producer LM forward")
+        return out
+
+    def _forward(self, tokens: torch.Tensor, return_type: str | None, stop_at_layer: int | None,
+                 start_at_layer: int | None, residual: torch.Tensor | None) -> torch.Tensor | None:
         if isinstance(tokens, str) or (isinstance(tokens, list) and tokens and isinstance(tokens[0], str)):
             tokens = self.to_tokens(tokens)
         if start_at_layer is None:

@@ -627,7 +627,8 @@ def lm(args: argparse.Namespace) -> None:
     attn = 2 * 2 * (args.ctx + 1) / 2 * H * dh  # causal QK^T and PV per token (mean over positions)
     flops = args.batch * args.ctx * args.stop * (per_tok + attn)
     res = {"model": args.model, "layers_run": args.stop, "batch": args.batch, "ctx": args.ctx}
-    for name, native in (("native", True), ("torch", False)):
+    arms = (("native", True),) if args.native_only else (("native", True), ("torch", False))
+    for name, native in arms:
         T.FORCE_TORCH = not native
         with torch.no_grad():
             for _ in range(2):
@@ -1110,6 +1111,7 @@ def main() -> None:
     lmp.add_argument("--batch", type=int, default=8)
     lmp.add_argument("--ctx", type=int, default=1024)
     lmp.add_argument("--reps", type=int, default=5)
+    lmp.add_argument("--native-only", action="store_true", help="skip the PyTorch-ops arm (launch lists)")
     mpc = sub.add_parser("mp", help="matching-pursuit encode: native kernels vs the PyTorch loop")
     mpc.add_argument("--batch", type=int, default=4096)
     mpc.add_argument("--d-in", type=int, default=768)
