@@ -220,8 +220,6 @@ class LanguageModelSAETrainingRunner:
         the same seed for every hook ("same") or seed + index ("offset"); each SAE records its hook
         in the metadata, is sharded for TP and wrapped for DDP / FSDP like a single SAE."""
         cfg = self.cfg
-        if self.routed:
-            raise ValueError("multi-hook training runs on the streaming or the non-routed data path")
         for idx, hook in enumerate(self.hook_names):
             seed = cfg.seed if cfg.multi_sae_seed_mode == "same" else cfg.seed + idx
             sae_cfg = type(cfg.sae).from_sae_runner_config(cfg)
@@ -426,6 +424,8 @@ class LanguageModelSAETrainingRunner:
         sae = None
         if not self.is_route_consumer:
             run_producer_only(self, n_steps)
+        elif self.is_multi_sae:
+            sae = self._run_routed_multi(n_steps)
         else:
             ex = RoutedExchange(self)
             done = resume_state(self, ex)
@@ -449,6 +449,30 @@ class LanguageModelSAETrainingRunner:
         if self.router is not None:
             self.router.close()
         return sae
+
+    def _run_routed_multi(self, n_steps: int) -> Any:
+        """Routed consumer with one SAE per hook: each routed step's rows carry every hook, and
+        `MultiSAETrainer` trains the hooks' SAEs on them (data parallel over the consumers)."""
+        from saelens_b200.runners.routing import RoutedExchange, RoutedProvider, resume_state
+        from saelens_b200.training.multi_sae_trainer import MultiSAETrainer
+
+        cfg = self.cfg
+        ex = RoutedExchange(self)
+        done = resume_state(self, ex)
+        trainer = MultiSAETrainer(
+            hook_names=self.hook_names, sae_by_hook=self.sae_by_hook, base_sae_by_hook=self.base_sae_by_hook,
+            data_provider=RoutedProvider(ex, n_steps - done, self.hook_names), cfg=cfg.to_sae_trainer_config(),
+            dp_group=self.dp_group, token_count_weighted_dp=self.token_count_weighted_dp,
+            sae_dp_mode=cfg.sae_dp_mode, backward_mode=cfg.multi_sae_backward_mode,
+            seed_mode=cfg.multi_sae_seed_mode)
+        self.trainer = trainer
+        if self.resume_from_checkpoint is not None:
+            trainer.load_trainer_state(self.resume_from_checkpoint)
+        result = trainer.fit()
+        ex.finish()
+        if cfg.output_path is not None:
+            trainer.save_final(cfg.output_path)  # every consumer rank (TP gathers); the first writes
+        return result
 
     def _evaluator(self) -> Any:
         from saelens_b200.evals import LLMSaeEvaluator

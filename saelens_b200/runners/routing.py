@@ -9,6 +9,11 @@ both.  With SAE TP every member of a consumer's TP group needs the same rows: th
 stores them into every member's landing buffer from the producer (no second hop), the collective
 transport sends them to the consumer root, which broadcasts them to its TP group.
 
+Several hooks (`hook_names`, one SAE per hook on every consumer): a producer's row carries the
+hooks' activations side by side ([rows, n_hooks * d_in], every hook of the same width), so the
+routing table, the router and the transports are the ones of a single hook with a wider row; the
+consumer splits each received batch into one [rows, d_in] batch per hook for `MultiSAETrainer`.
+
 Producer tensor parallelism (`vllm_tp_size` > 1): every member of a producer's TP group runs the
 Megatron-split LM (`models/lm/tp.py`) on the same tokens in lockstep; the group's first rank holds
 the full activations after the layer's all-reduces and is the one that sends.
@@ -53,6 +58,8 @@ def routing_init(runner: Any) -> None:
     if (Q * cfg.train_batch_size_tokens) % P:
         raise ValueError("sae_dp_size * train_batch_size_tokens must be divisible by vllm_dp_size")
     runner.route_batch = Q * cfg.train_batch_size_tokens // P
+    runner.route_hooks = list(cfg.hook_names) if cfg.hook_names else [cfg.hook_name]
+    runner.route_width = cfg.sae.d_in * len(runner.route_hooks)  # hooks side by side in one row
     world = dist.get_world_size()
     disjoint = world == P * vtp + Q * stp and world != max(P * vtp, Q * stp)
     v2.init_distributed_v2(P=P, Q=Q, vllm_tp_size=vtp, sae_tp_size=stp, batch_size=runner.route_batch,
@@ -82,16 +89,28 @@ def routing_init(runner: Any) -> None:
             layout = v2.get_layout()
             members = [list(layout.consumer_ranks[c]) for c in range(Q)]
             runner.route_to_members = True
-        runner.router = P2PRowRouter(dist.group.WORLD, producers, consumers, runner.route_batch, cfg.sae.d_in,
-                                     consumer_members=members)
+        runner.router = P2PRowRouter(dist.group.WORLD, producers, consumers, runner.route_batch,
+                                     runner.route_width, consumer_members=members)
 
 
 class _RowSource:
-    """`n` activation rows at a time from a store that yields fixed-size batches."""
+    """`n` activation rows at a time from a store that yields fixed-size batches (a multi-hook
+    store's {hook: rows} batches become rows with the hooks side by side, in `hooks` order)."""
 
-    def __init__(self, store: Any):
+    def __init__(self, store: Any, hooks: list[str] | None = None):
         self.store = store
+        self.hooks = hooks
         self.rest: torch.Tensor | None = None
+
+    def _next(self) -> torch.Tensor:
+        b = next(self.store)
+        if isinstance(b, dict):
+            names = self.hooks or list(b)
+            widths = {b[h].shape[-1] for h in names}
+            if len(widths) != 1:
+                raise ValueError(f"routed multi-hook runs need hooks of one width, got {sorted(widths)}")
+            b = torch.cat([b[h] for h in names], dim=-1)
+        return b
 
     def take(self, n: int) -> torch.Tensor:
         parts, have = [], 0
@@ -99,7 +118,7 @@ class _RowSource:
             parts.append(self.rest)
             have = self.rest.shape[0]
         while have < n:
-            b = next(self.store)
+            b = self._next()
             parts.append(b)
             have += b.shape[0]
         cat = torch.cat(parts) if len(parts) > 1 else parts[0]
@@ -116,7 +135,8 @@ class RoutedExchange:
 
         self.r = runner
         self.cfg = runner.cfg
-        self.source = _RowSource(runner.activations_store) if runner.is_route_producer else None
+        self.source = _RowSource(runner.activations_store, runner.route_hooks) if runner.is_route_producer else None
+        self.width = runner.route_width
         self.routes = v2.get_routing_table()
         self.p_idx = v2.get_producer_idx() if runner.is_route_producer else -1
         self.c_idx = v2.get_consumer_idx() if runner.is_route_consumer else -1
@@ -180,7 +200,7 @@ class RoutedExchange:
         local: dict[int, torch.Tensor] = {}
         recv: dict[int, torch.Tensor] = {}
         is_root = self.c_idx >= 0 and self.rank == self.r.route_consumers[self.c_idx]
-        d = self.cfg.sae.d_in
+        d = self.width
         for rt in self.routes:
             src, dst = self.r.route_producers[rt.producer_idx], self.r.route_consumers[rt.consumer_idx]
             if rt.producer_idx == self.p_idx and rows is not None:
@@ -208,7 +228,7 @@ class RoutedExchange:
             return batch
         root = self.r.route_consumers[self.c_idx]
         if batch is None:
-            batch = torch.empty(self.cfg.train_batch_size_tokens, self.cfg.sae.d_in, dtype=self.dtype, device=self.dev)
+            batch = torch.empty(self.cfg.train_batch_size_tokens, self.width, dtype=self.dtype, device=self.dev)
         dist.broadcast(batch, src=root, group=tp)
         return batch
 
@@ -219,11 +239,13 @@ class RoutedExchange:
 
 
 class RoutedProvider:
-    """DataProvider of a consumer rank: each `next()` is one routed step."""
+    """DataProvider of a consumer rank: each `next()` is one routed step (with `hooks`, a
+    {hook: [rows, d_in]} batch cut from the hooks-side-by-side rows)."""
 
-    def __init__(self, exchange: RoutedExchange, n_steps: int):
+    def __init__(self, exchange: RoutedExchange, n_steps: int, hooks: list[str] | None = None):
         self.ex = exchange
         self.left = n_steps
+        self.hooks = hooks if hooks and len(hooks) > 1 else None
 
     def __iter__(self) -> RoutedProvider:
         return self
@@ -234,7 +256,10 @@ class RoutedProvider:
         self.left -= 1
         batch = self.ex.step()
         assert batch is not None
-        return batch
+        if self.hooks is None:
+            return batch
+        d = batch.shape[1] // len(self.hooks)
+        return {h: batch[:, i * d:(i + 1) * d].contiguous() for i, h in enumerate(self.hooks)}
 
 
 def resume_state(runner: Any, ex: RoutedExchange) -> int:

@@ -19,7 +19,7 @@ def _port() -> int:
     return p
 
 
-def _worker(rank, world, port, tmp, P, Q, tp=1, vtp=1):
+def _worker(rank, world, port, tmp, P, Q, tp=1, vtp=1, hooks=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
     import torch.distributed as dist
@@ -41,7 +41,8 @@ def _worker(rank, world, port, tmp, P, Q, tp=1, vtp=1):
         hook_name="blocks.1.hook_resid_pre", dataset_path="synthetic:uniform:500:32", context_size=16,
         training_tokens=64 * 8, train_batch_size_tokens=64, store_batch_size_prompts=4, n_batches_in_buffer=2,
         output_path=os.path.join(tmp, "out"), logger=LoggingConfig(log_to_wandb=False), device="cpu",
-        save_mse_every_n_steps=1, n_checkpoints=0, verbose=False, routing_transport="collective")
+        save_mse_every_n_steps=1, n_checkpoints=0, verbose=False, routing_transport="collective",
+        **({"hook_names": list(hooks)} if hooks else {}))
     if rank == 1:  # a rank with other paths (e.g. another timestamp) follows rank 0
         cfg.checkpoint_path = os.path.join(tmp, "elsewhere")
     runner = LanguageModelSAETrainingRunner(cfg, override_model=lm, vllm_dp_size=P, sae_dp_size=Q,
@@ -50,7 +51,10 @@ def _worker(rank, world, port, tmp, P, Q, tp=1, vtp=1):
     out = runner.run()
     info = {"role": runner.role, "transport": runner.routing_transport,
             "lm_sharded": getattr(runner.model, "tp", None) is not None}
-    if out is not None:
+    if isinstance(out, dict):
+        info["steps"] = runner.trainer.n_training_steps
+        info["W_dec_sum"] = {h: float(s.W_dec.detach().sum()) for h, s in out.items()}
+    elif out is not None:
         info["steps"] = runner.trainer.n_training_steps
         info["W_dec_sum"] = float(out.W_dec.detach().sum())
     with open(os.path.join(tmp, f"r{rank}.json"), "w") as f:
@@ -180,3 +184,22 @@ def test_routed_colocated_producers_with_tp_dp_consumers(tmp_path):
     r = [json.loads((tmp_path / f"r{i}.json").read_text()) for i in range(4)]
     assert [x["role"] for x in r] == ["producer+consumer", "producer+consumer", "consumer", "consumer"]
     assert all(x["steps"] == 6 and x["W_dec_shard_rows"] == 64 for x in r)
+
+
+@pytest.mark.parametrize("P,Q", [(1, 1), (2, 2)])
+def test_routed_runner_multi_hook(tmp_path, P, Q):
+    """Two hooks routed side by side in one row: every consumer trains one SAE per hook, data
+    parallel replicas stay equal, and the final SAEs are written one directory per hook."""
+    hooks = ["blocks.0.hook_resid_pre", "blocks.1.hook_resid_pre"]
+    mp.spawn(_worker, args=(2, _port(), str(tmp_path), P, Q, 1, 1, hooks), nprocs=2, join=True)
+    r = [json.loads((tmp_path / f"r{i}.json").read_text()) for i in range(2)]
+    trained = [x for x in r if "steps" in x]
+    assert trained and all(x["steps"] == 8 for x in trained)
+    assert all(set(x["W_dec_sum"]) == set(hooks) for x in trained)
+    if (P, Q) == (2, 2):
+        for h in hooks:
+            assert r[0]["W_dec_sum"][h] == pytest.approx(r[1]["W_dec_sum"][h], rel=1e-6)
+    sums = trained[0]["W_dec_sum"]
+    assert sums[hooks[0]] != sums[hooks[1]]  # each hook's SAE trained on its own activations
+    subdirs = [p for p in (tmp_path / "out").iterdir() if p.is_dir()]
+    assert len(subdirs) == 2 and all((d / "sae_weights.safetensors").exists() for d in subdirs)
