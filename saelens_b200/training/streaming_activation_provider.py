@@ -144,7 +144,18 @@ class StreamingActivationProvider:
         if self._n_hooks > 1:
             new = self._regroup_hooks(new)
         elif self._shuffle:
-            new = new[torch.randperm(new.shape[0], device=self._device, generator=self._gen)]
+            perm = torch.randperm(new.shape[0], device=self._device, generator=self._gen)
+            if new.is_cuda:
+                # the leftover pool rows followed by the shuffled new rows, gathered in one pass
+                from saelens_b200 import ops
+
+                rest = self._pool[self._start :] if self._avail() > 0 else None
+                r = 0 if rest is None else rest.shape[0]
+                idx = perm + r if r == 0 else torch.cat([torch.arange(r, device=new.device), perm + r])
+                self._pool = ops.gather_rows(rest, new, idx) if rest is not None else ops.gather_rows(new, None, idx)
+                self._start = 0
+                return
+            new = new[perm]
         if self._avail() > 0:
             assert self._pool is not None
             new = torch.cat([self._pool[self._start :], new])

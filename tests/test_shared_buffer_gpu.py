@@ -81,3 +81,55 @@ def test_refused_registration_keeps_the_staging_path(tmp_path):
     assert torch.equal(next(prov).cpu(), rows)
     cons.close()
     buf.close()
+
+
+def test_shuffled_refill_gathers_pool_and_new_rows_in_one_pass(shm_dir, monkeypatch):
+    """With shuffle on, a CUDA refill serves the leftover pool rows followed by the new rows in a
+    random order through the native two-source gather; the same generator seed gives the same
+    stream as the concatenate-then-index formulation, and every written row is served once."""
+    from saelens_b200 import ops
+    from saelens_b200.training.shared_activation_buffer import SharedActivationBuffer
+    from saelens_b200.training.streaming_activation_provider import StreamingActivationProvider
+
+    T, D, n_chunks, batch = 256, 64, 5, 96  # batch does not divide a chunk: refills keep leftovers
+    g = torch.Generator(device="cuda").manual_seed(3)
+    rows = [torch.randn(T, D, device="cuda", generator=g) for _ in range(n_chunks)]
+
+    def serve(name):
+        kw = dict(name=name, num_chunks=8, chunk_size_tokens=T, d_model=D, num_producers=1,
+                  target_chunks=n_chunks, base_dir=shm_dir)
+        prod = SharedActivationBuffer(create=True, dtype=torch.float32, **kw)
+        cons = SharedActivationBuffer(create=False, **kw)
+        for r in rows:
+            idx, _ = prod.allocate_write_chunk()
+            prod.write_chunk(idx, r.cpu(), T)
+            prod.mark_ready(idx)
+        prod.signal_done()
+        prov = StreamingActivationProvider(cons, batch, prefetch_chunks=2, device="cuda", d_model=D,
+                                           shuffle=True, random_chunks=False,
+                                           generator=torch.Generator(device="cuda").manual_seed(11))
+        got = []
+        while True:
+            try:
+                got.append(next(prov))
+            except StopIteration:
+                break
+        cons.close()
+        prod.close()
+        return torch.cat(got)
+
+    native = serve("ring_shuffle_a")
+
+    def torch_gather(a, b=None, perm=None, out=None):
+        src = a if b is None else torch.cat([a, b])
+        return src[perm] if perm is not None else src.clone()
+
+    monkeypatch.setattr(ops, "gather_rows", torch_gather)
+    reference = serve("ring_shuffle_b")
+    assert torch.equal(native, reference)
+    served = native.shape[0]
+    allrows = torch.cat(rows)
+    # every served row is one of the written rows, and no written row is served twice
+    d = torch.cdist(native, allrows, compute_mode="donot_use_mm_for_euclid_dist")
+    assert bool((d.min(dim=1).values == 0).all())
+    assert int(d.argmin(dim=1).unique().numel()) == served
