@@ -58,7 +58,8 @@ def routing_init(runner: Any) -> None:
     if (Q * cfg.train_batch_size_tokens) % P:
         raise ValueError("sae_dp_size * train_batch_size_tokens must be divisible by vllm_dp_size")
     runner.route_batch = Q * cfg.train_batch_size_tokens // P
-    runner.route_hooks = list(cfg.hook_names) if cfg.hook_names else [cfg.hook_name]
+    hook_names = getattr(cfg, "hook_names", None)
+    runner.route_hooks = list(hook_names) if hook_names else [getattr(cfg, "hook_name", None)]
     runner.route_width = cfg.sae.d_in * len(runner.route_hooks)  # hooks side by side in one row
     world = dist.get_world_size()
     disjoint = world == P * vtp + Q * stp and world != max(P * vtp, Q * stp)
