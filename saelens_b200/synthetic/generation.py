@@ -10,6 +10,8 @@ mapped to a dense hidden vector h = f @ D + b by the feature dictionary D.
 
 from __future__ import annotations
 
+import inspect
+
 import random
 from collections.abc import Callable, Sequence
 from dataclasses import asdict, dataclass, field
@@ -105,18 +107,30 @@ def _modifier_chain(mods: ActivationsModifierInput) -> Callable[[torch.Tensor, A
     if not mods:
         return None
 
-    def call(m: ActivationsModifier, x: torch.Tensor, gen: Any) -> torch.Tensor:
-        try:
-            return m(x, gen)
-        except TypeError:
-            return m(x)
+    takes_gen = [_positional_arity(m) >= 2 for m in mods]
 
     def chained(x: torch.Tensor, gen: Any) -> torch.Tensor:
-        for m in mods:
-            x = call(m, x, gen)
+        for m, two in zip(mods, takes_gen):
+            x = m(x, gen) if two else m(x)
         return x
 
     return chained
+
+
+def _positional_arity(fn: Callable[..., Any]) -> int:
+    """Positional parameters `fn` accepts (a *args parameter counts as many): a modifier taking two
+    receives the generator as its second argument, one taking one only the activations."""
+    try:
+        params = inspect.signature(fn).parameters.values()
+    except (TypeError, ValueError):  # builtins without a signature: activations only
+        return 1
+    n = 0
+    for p in params:
+        if p.kind is inspect.Parameter.VAR_POSITIONAL:
+            return 2
+        if p.kind in (inspect.Parameter.POSITIONAL_ONLY, inspect.Parameter.POSITIONAL_OR_KEYWORD):
+            n += 1
+    return n
 
 
 class ActivationGenerator(nn.Module):
@@ -148,15 +162,20 @@ class ActivationGenerator(nn.Module):
                 if not torch.allclose(c, c.T, atol=1e-5) or not torch.allclose(c.diagonal(), torch.ones_like(c.diagonal()), atol=1e-4):
                     raise ValueError("correlation matrix must be symmetric with a unit diagonal")
                 self.correlation_matrix = c.to(device=device, dtype=torch.float32)
-                self._chol = torch.linalg.cholesky(self.correlation_matrix.double() +
-                                                   1e-9 * torch.eye(num_features, device=device,
-                                                                    dtype=torch.float64)).float()
+                chol, info = torch.linalg.cholesky_ex(self.correlation_matrix.double() +
+                                                      1e-9 * torch.eye(num_features, device=device,
+                                                                       dtype=torch.float64))
+                if int(info) != 0:
+                    raise ValueError("correlation matrix must be positive definite")
+                self._chol = chol.float()
             else:
                 f, d = correlation_matrix[0], correlation_matrix[1]
                 if f.shape[0] != num_features or d.shape != (num_features,):
                     raise ValueError("low-rank correlation must be (factor [n, r], diag [n])")
-                if (d < 0).any():
-                    raise ValueError("low-rank correlation diagonal must be non-negative")
+                if f.dim() != 2 or d.dim() != 1:
+                    raise ValueError("low-rank correlation must be (factor [n, r], diag [n])")
+                if (d <= 0).any():
+                    raise ValueError("low-rank correlation diagonal must be positive")
                 self.low_rank_correlation = (f.to(device=device, dtype=torch.float32),
                                              d.to(device=device, dtype=torch.float32).sqrt())
             self.correlation_thresholds = correlation_thresholds(self.firing_probabilities.float())
