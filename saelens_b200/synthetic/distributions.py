@@ -27,6 +27,8 @@ class _Registry:
         self.items: dict[str, type] = {}
 
     def register(self, name: str, cls: type) -> None:
+        if name in self.items and self.items[name] is not cls:
+            raise ValueError(f"'{name}' is already registered.")
         self.items[name] = cls
 
     def get(self, name: str) -> type:
@@ -37,6 +39,31 @@ class _Registry:
 
 _PROB = _Registry("firing probability")
 _MAG = _Registry("magnitude")
+
+
+def _generator_name(d: dict[str, Any]) -> str:
+    """The registered name in a serialised generator config: "generator_name" (the format the
+    reference writes), or "generator" (earlier files of this package)."""
+    name = d.get("generator_name", d.get("generator"))
+    if name is None:
+        raise ValueError("generator_name required in config dict")
+    return str(name)
+
+
+def _fields(d: dict[str, Any]) -> dict[str, Any]:
+    return {k: v for k, v in d.items() if k not in ("generator_name", "generator")}
+
+
+def _register(registry: _Registry, name_or_class: str | type, config_class: type | None) -> Any:
+    """register(name, cls) as the reference's API, or @register / register(cls) using the class's
+    generator_name(); returns the class (so the one-argument form works as a decorator)."""
+    if isinstance(name_or_class, str):
+        if config_class is None:
+            raise TypeError("register(name, config_class) needs the config class")
+        registry.register(name_or_class, config_class)
+        return config_class
+    registry.register(name_or_class.generator_name(), name_or_class)
+    return name_or_class
 
 
 # ------------------------------------------------------------------------------ probabilities
@@ -89,17 +116,15 @@ class FiringProbabilityConfig(ABC):
     def generate(self, num_features: int, seed: int | None = None) -> torch.Tensor: ...
 
     def to_dict(self) -> dict[str, Any]:
-        return {"generator": self.generator_name(), **asdict(self)}  # type: ignore[call-overload]
+        return {**asdict(self), "generator_name": self.generator_name()}  # type: ignore[call-overload]
 
     @classmethod
     def from_dict(cls, d: dict[str, Any]) -> "FiringProbabilityConfig":
-        d = dict(d)
-        return _PROB.get(d.pop("generator"))(**d)
+        return _PROB.get(_generator_name(d))(**_fields(d))
 
 
-def register_firing_probability(config_class: type) -> type:
-    _PROB.register(config_class.generator_name(), config_class)
-    return config_class
+def register_firing_probability(name_or_class: str | type, config_class: type | None = None) -> Any:
+    return _register(_PROB, name_or_class, config_class)
 
 
 def get_firing_probability_class(name: str) -> type:
@@ -176,17 +201,15 @@ class MagnitudeConfig(ABC):
     def generate(self, num_features: int, seed: int | None = None) -> torch.Tensor: ...
 
     def to_dict(self) -> dict[str, Any]:
-        return {"generator": self.generator_name(), **asdict(self)}  # type: ignore[call-overload]
+        return {**asdict(self), "generator_name": self.generator_name()}  # type: ignore[call-overload]
 
     @classmethod
     def from_dict(cls, d: dict[str, Any]) -> "MagnitudeConfig":
-        d = dict(d)
-        return _MAG.get(d.pop("generator"))(**d)
+        return _MAG.get(_generator_name(d))(**_fields(d))
 
 
-def register_magnitude(config_class: type) -> type:
-    _MAG.register(config_class.generator_name(), config_class)
-    return config_class
+def register_magnitude(name_or_class: str | type, config_class: type | None = None) -> Any:
+    return _register(_MAG, name_or_class, config_class)
 
 
 def get_magnitude_class(name: str) -> type:
