@@ -84,7 +84,10 @@ class L0Calculator:
         self.rows = 0
 
     def add_batch(self, activations: torch.Tensor) -> None:
-        self.total += float((activations != 0).sum())
+        if activations.is_sparse:
+            self.total += float((activations.coalesce().values() != 0).sum())
+        else:
+            self.total += float((activations != 0).sum())
         self.rows += activations.shape[0]
 
     def compute(self) -> float:
@@ -145,7 +148,8 @@ class ExplainedVarianceCalculator:
 
 @dataclass
 class SyntheticDataEvalResult:
-    l0: float
+    true_l0: float  # mean active ground-truth features per sample
+    sae_l0: float  # mean active SAE latents per sample
     dead_latents: int
     shrinkage: float
     explained_variance: float
@@ -164,27 +168,38 @@ class SyntheticDataEvalResult:
 
 @torch.no_grad()
 def eval_sae_on_synthetic_data(sae: Any, feature_dict: Any, activations_generator: Any, num_samples: int = 100_000,
-                               batch_size: int = 4096) -> SyntheticDataEvalResult:
-    """Stream `num_samples` synthetic rows through the SAE and collect every metric above."""
+                               batch_size: int | None = None,
+                               activation_scaler: Any = None) -> SyntheticDataEvalResult:
+    """Stream `num_samples` synthetic rows through the SAE and collect every metric above
+    (sae_lens/synthetic/evals.py:413-502).  With `activation_scaler` the hidden activations are
+    scaled before encoding and the reconstruction unscaled before it is compared with them;
+    `batch_size=None` evaluates all samples in one batch."""
+    if batch_size is None:
+        batch_size = num_samples
     dev = next(iter(sae.parameters())).device
     W_dec = sae.W_dec.detach().float()
     gt = feature_dict.feature_vectors.detach().float()
-    l0, dead = L0Calculator(), DeadLatentsCalculator(W_dec.shape[0])
+    true_l0, l0, dead = L0Calculator(), L0Calculator(), DeadLatentsCalculator(W_dec.shape[0])
     shrink, ev = ShrinkageCalculator(), ExplainedVarianceCalculator(gt.shape[1], dev)
     cls = ClassificationMetricsCalculator(W_dec, gt)
     done = 0
     while done < num_samples:
         n = min(batch_size, num_samples - done)
         f = activations_generator.sample(n)
+        true_l0.add_batch(f)
         h = feature_dict(f).to(dev)
-        lat = sae.encode(h.to(sae.W_enc.dtype))
+        hs = activation_scaler.scale(h) if activation_scaler is not None else h
+        lat = sae.encode(hs.to(sae.W_enc.dtype))
         out = sae.decode(lat).float()
+        if activation_scaler is not None:
+            out = activation_scaler.unscale(out)
         l0.add_batch(lat)
         dead.add_batch(lat)
         shrink.add_batch(out, h)
         ev.add_batch(out, h)
         cls.add_batch(lat.to(f.device) if not f.is_sparse else lat.cpu(), f if not f.is_sparse else f.cpu())
         done += n
-    return SyntheticDataEvalResult(l0=l0.compute(), dead_latents=dead.compute(), shrinkage=shrink.compute(),
+    return SyntheticDataEvalResult(true_l0=true_l0.compute(), sae_l0=l0.compute(), dead_latents=dead.compute(),
+                                   shrinkage=shrink.compute(),
                                    explained_variance=ev.compute(), mcc=mean_correlation_coefficient(W_dec, gt),
                                    uniqueness=feature_uniqueness(W_dec, gt), classification=cls.compute())

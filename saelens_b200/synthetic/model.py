@@ -289,54 +289,89 @@ def train_toy_sae(sae: Any, model: SyntheticModel, training_samples: int = 2_000
 # ---------------------------------------------------------------------------- statistics
 @dataclass
 class SuperpositionStats:
+    """How much the dictionary's directions overlap (sae_lens/synthetic/stats.py:95-110): per
+    feature the largest |cos| to any other feature and chosen percentiles of its |cos| to the
+    others, their means, and the mean |cos| over all pairs."""
+
+    max_abs_cos_sims: torch.Tensor
+    percentile_abs_cos_sims: dict[int, torch.Tensor]
+    mean_max_abs_cos_sim: float
+    mean_percentile_abs_cos_sim: dict[int, float]
+    mean_abs_cos_sim: float
     num_features: int
     hidden_dim: int
-    superposition_ratio: float
-    mean_abs_cosine: float
-    max_abs_cosine: float
-    mean_max_abs_cosine: float
 
 
-def compute_superposition_stats(feature_vectors: torch.Tensor, chunk_size: int = 4096) -> SuperpositionStats:
-    """Off-diagonal |cos| statistics of the dictionary (computed in row chunks)."""
-    n, d = feature_vectors.shape
-    fv = feature_vectors.float()
-    tot, mx, mean_max = 0.0, 0.0, 0.0
-    for s in range(0, n, chunk_size):
-        c = cosine_similarities(fv[s : s + chunk_size], fv).abs()
-        idx = torch.arange(c.shape[0], device=c.device)
-        c[idx, s + idx] = 0.0
-        tot += float(c.sum())
-        mx = max(mx, float(c.max())) if n > 1 else 0.0
-        mean_max += float(c.max(dim=1).values.sum())
-    pairs = max(n * (n - 1), 1)
-    return SuperpositionStats(n, d, n / d, tot / pairs, mx, mean_max / n)
+@torch.no_grad()
+def compute_superposition_stats(feature_dictionary: Any, batch_size: int = 1024,
+                                device: str | torch.device | None = None,
+                                percentiles: list[int] | None = None) -> SuperpositionStats:
+    """`feature_dictionary`: a FeatureDictionary (or its [num_features, hidden_dim] vectors).
+    Rows of the cosine matrix are formed `batch_size` at a time; a feature's similarity to itself
+    is left out of its maximum, its percentiles and the pair mean."""
+    vectors = getattr(feature_dictionary, "feature_vectors", feature_dictionary)
+    pct = [95, 99] if percentiles is None else list(percentiles)
+    n, d = vectors.shape
+    if n < 2:
+        raise ValueError("Need at least 2 features to compute superposition stats")
+    dev = vectors.device if device is None else torch.device(device)
+    unit = vectors.to(dev).float()
+    unit = unit / unit.norm(dim=1, keepdim=True).clamp_min(1e-8)
+    row_max = torch.empty(n, device=dev)
+    row_pct = {p: torch.empty(n, device=dev) for p in pct}
+    total = 0.0
+    for s0 in range(0, n, batch_size):
+        a = (unit[s0 : s0 + batch_size] @ unit.T).abs()
+        r = torch.arange(a.shape[0], device=dev)
+        self_cols = s0 + r
+        total += float(a.sum() - a[r, self_cols].sum())
+        a[r, self_cols] = -1.0  # below every |cos|: never the maximum, sorts first
+        row_max[s0 : s0 + a.shape[0]] = a.max(dim=1).values
+        others = a.sort(dim=1).values[:, 1:]  # drop the self entry; n - 1 values per row
+        for p in pct:  # linear interpolation between order statistics (torch.quantile's default)
+            pos = (p / 100.0) * (n - 2)
+            lo = int(pos)
+            hi = min(lo + 1, n - 2)
+            w = pos - lo
+            row_pct[p][s0 : s0 + a.shape[0]] = others[:, lo] * (1 - w) + others[:, hi] * w
+    return SuperpositionStats(
+        max_abs_cos_sims=row_max.cpu(), percentile_abs_cos_sims={p: v.cpu() for p, v in row_pct.items()},
+        mean_max_abs_cos_sim=float(row_max.mean()),
+        mean_percentile_abs_cos_sim={p: float(v.mean()) for p, v in row_pct.items()},
+        mean_abs_cos_sim=total / (n * (n - 1)), num_features=n, hidden_dim=d)
 
 
 @dataclass
 class CorrelationMatrixStats:
+    """Off-diagonal statistics of a correlation matrix (sae_lens/synthetic/stats.py:9-15)."""
+
+    rms_correlation: float
+    mean_correlation: float
     num_features: int
-    mean_abs_offdiag: float
-    max_abs_offdiag: float
-    frac_nonzero_offdiag: float
 
 
-def compute_correlation_matrix_stats(m: torch.Tensor, tol: float = 1e-6) -> CorrelationMatrixStats:
-    n = m.shape[0]
-    off = m.float() - torch.diag(m.diagonal().float())
-    a = off.abs()
-    cnt = max(n * (n - 1), 1)
-    return CorrelationMatrixStats(n, float(a.sum()) / cnt, float(a.max()) if n > 1 else 0.0,
-                                  float((a > tol).sum()) / cnt)
+@torch.no_grad()
+def compute_correlation_matrix_stats(correlation_matrix: torch.Tensor) -> CorrelationMatrixStats:
+    c = correlation_matrix.double()
+    n = c.shape[0]
+    pairs = n * (n - 1)
+    diag = c.diagonal()
+    off_sum = float(c.sum() - diag.sum())
+    off_sq = float(c.square().sum() - diag.square().sum())
+    return CorrelationMatrixStats(rms_correlation=(off_sq / pairs) ** 0.5 if pairs else 0.0,
+                                  mean_correlation=off_sum / pairs if pairs else 0.0, num_features=n)
 
 
-def compute_low_rank_correlation_matrix_stats(c: LowRankCorrelationMatrix, sample: int = 2048,
-                                              seed: int = 0) -> CorrelationMatrixStats:
-    """Statistics of the implied correlation on a random subset of `sample` features."""
-    n = c.correlation_factor.shape[0]
-    g = torch.Generator().manual_seed(seed)
-    idx = torch.randperm(n, generator=g)[: min(sample, n)].to(c.correlation_factor.device)
-    f = c.correlation_factor[idx].float()
-    m = f @ f.T + torch.diag(c.correlation_diag[idx].float())
-    s = compute_correlation_matrix_stats(m)
-    return CorrelationMatrixStats(n, s.mean_abs_offdiag, s.max_abs_offdiag, s.frac_nonzero_offdiag)
+@torch.no_grad()
+def compute_low_rank_correlation_matrix_stats(correlation_matrix: LowRankCorrelationMatrix) -> CorrelationMatrixStats:
+    """The same statistics for C = F F^T + diag(d) without forming C: its off-diagonal part is
+    F F^T minus its diagonal, so sum(C_off) = |F^T 1|^2 - sum_i |F_i|^2 and
+    sum(C_off^2) = |F^T F|_F^2 - sum_i |F_i|^4 (O(n r^2) time, O(r^2) memory)."""
+    f = correlation_matrix.correlation_factor.double()
+    n = f.shape[0]
+    pairs = n * (n - 1)
+    row_sq = f.square().sum(dim=1)
+    off_sum = float(f.sum(dim=0).square().sum() - row_sq.sum())
+    off_sq = float((f.T @ f).square().sum() - row_sq.square().sum())
+    return CorrelationMatrixStats(rms_correlation=max(off_sq / pairs, 0.0) ** 0.5 if pairs else 0.0,
+                                  mean_correlation=off_sum / pairs if pairs else 0.0, num_features=n)

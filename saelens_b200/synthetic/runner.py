@@ -7,6 +7,8 @@ architecture in the registry is supported; evaluation uses `eval_sae_on_syntheti
 
 from __future__ import annotations
 
+from collections.abc import Iterable
+
 import json
 from dataclasses import asdict, dataclass, field
 from pathlib import Path
@@ -142,25 +144,34 @@ class SyntheticSAERunner:
 
 
 # ------------------------------------------------------------------------------ plotting helpers
-def find_best_feature_ordering(sae_features: torch.Tensor, gt_features: torch.Tensor) -> torch.Tensor:
-    """Permutation of the SAE latents that places each latent at its best-matching ground-truth
-    index (optimal one-to-one assignment first, unmatched latents appended by best match)."""
-    from scipy.optimize import linear_sum_assignment
-
-    sim = cosine_similarities(sae_features.float(), gt_features.float()).abs().cpu()
-    r, c = linear_sum_assignment(-sim.numpy())
-    order = [int(x) for _, x in sorted(zip(c.tolist(), r.tolist()))]
-    rest = [i for i in range(sae_features.shape[0]) if i not in set(order)]
-    rest.sort(key=lambda i: int(sim[i].argmax()))
-    return torch.tensor(order + rest, dtype=torch.long)
+def find_best_feature_ordering(sae_features: torch.Tensor, true_features: torch.Tensor) -> torch.Tensor:
+    """Order of the SAE latents by the index of their best-matching true feature (largest |cos|),
+    so a similarity plot of the reordered latents runs along the diagonal
+    (sae_lens/synthetic/plotting.py:23-43); ties keep the latents' own order."""
+    best = cosine_similarities(sae_features.float(), true_features.float()).abs().argmax(dim=1)
+    return torch.argsort(best, stable=True)
 
 
 def find_best_feature_ordering_from_sae(sae: Any, feature_dict: Any) -> torch.Tensor:
     return find_best_feature_ordering(sae.W_dec.detach(), feature_dict.feature_vectors.detach())
 
 
-def find_best_feature_ordering_across_saes(saes: list[Any], feature_dict: Any) -> list[torch.Tensor]:
-    return [find_best_feature_ordering_from_sae(s, feature_dict) for s in saes]
+def find_best_feature_ordering_across_saes(saes: Iterable[Any], feature_dict: Any) -> torch.Tensor:
+    """One ordering for several SAEs (training snapshots): each SAE's own best ordering, scored by
+    the mean cosine (to two decimals) along the diagonal it produces; the best-scoring one wins."""
+    true = feature_dict.feature_vectors.detach().float()
+    best_score, best_order = float("-inf"), None
+    for sae in saes:
+        w = sae.W_dec.detach().float()
+        order = find_best_feature_ordering(w, true)
+        sims = torch.round(cosine_similarities(w[order], true) * 100) / 100
+        m = min(sims.shape)
+        score = float(sims[torch.arange(m), torch.arange(m)].mean())
+        if score > best_score:
+            best_score, best_order = score, order
+    if best_order is None:
+        raise ValueError("no SAEs given")
+    return best_order
 
 
 def plot_sae_feature_similarity(sae: Any, feature_dict: Any, reorder_features: bool = True,

@@ -114,7 +114,7 @@ def test_metrics():
     ev.add_batch(x, x)
     assert ev.compute() == pytest.approx(1.0)
     st = S.compute_superposition_stats(torch.eye(3))
-    assert st.max_abs_cosine == 0.0 and st.superposition_ratio == 1.0
+    assert st.mean_max_abs_cos_sim == 0.0 and st.mean_abs_cos_sim == 0.0 and st.num_features == 3
 
 
 def test_runner_recovers_features_cpu(tmp_path):
