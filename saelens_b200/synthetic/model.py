@@ -10,7 +10,7 @@ hierarchy, `synthetic_model_hierarchy.json`.
 from __future__ import annotations
 
 import json
-from collections.abc import Iterator
+from collections.abc import Callable, Iterator
 from dataclasses import asdict, dataclass, field
 from pathlib import Path
 from typing import Any
@@ -161,6 +161,30 @@ class SyntheticModel(nn.Module):
             modify_activations=self.hierarchy.modifier if self.hierarchy is not None else None,
             correlation_matrix=corr, device=self.device, dtype=cfg.dtype)
 
+    def to(self, device: str | torch.device | None = None, dtype: torch.dtype | None = None,  # type: ignore[override]
+           non_blocking: bool = False) -> "SyntheticModel":
+        """Move the model to `device` (dtype is ignored, as in sae_lens/synthetic/synthetic_model.py:
+        644-663): the dictionary moves, and the generator is rebuilt there from its current
+        probabilities, magnitudes and correlation (plain tensors that Module.to would not move)."""
+        if device is None:
+            return self
+        self.device = torch.device(device)
+        self.feature_dict = self.feature_dict.to(self.device)
+        g = self.activation_generator
+        corr = None
+        if self.correlation is not None:
+            corr = LowRankCorrelationMatrix(self.correlation.correlation_factor.to(self.device),
+                                            self.correlation.correlation_diag.to(self.device))
+            self.correlation = corr
+        sparse = g.use_sparse_tensors
+        self.activation_generator = ActivationGenerator(
+            self.cfg.num_features, g.firing_probabilities.to(self.device),
+            std_firing_magnitudes=g.std_firing_magnitudes.to(self.device),
+            mean_firing_magnitudes=g.mean_firing_magnitudes.to(self.device),
+            modify_activations=self.hierarchy.modifier if self.hierarchy is not None else None,
+            correlation_matrix=corr, device=self.device, dtype=self.cfg.dtype, use_sparse_tensors=sparse)
+        return self
+
     @property
     def use_sparse_tensors(self) -> bool:
         return self.activation_generator.use_sparse_tensors
@@ -211,13 +235,15 @@ class SyntheticModel(nn.Module):
         return cls(cfg, device=device, _tensors=t, _hierarchy=h)
 
     @classmethod
-    def from_pretrained(cls, repo_id: str, subfolder: str | None = None, device: str | torch.device = "cpu",
-                        revision: str | None = None) -> "SyntheticModel":
+    def from_pretrained(cls, repo_id: str, model_path: str | None = None, device: str | torch.device = "cpu",
+                        force_download: bool = False, revision: str | None = None) -> "SyntheticModel":
+        """A model saved on the Hugging Face hub, at the repo root or in its `model_path`
+        subfolder (sae_lens/synthetic/synthetic_model.py:585-640)."""
         from huggingface_hub import snapshot_download
 
-        root = Path(snapshot_download(repo_id, revision=revision,
-                                      allow_patterns=[f"{subfolder}/*"] if subfolder else None))
-        return cls.load_from_disk(root / subfolder if subfolder else root, device=device)
+        root = Path(snapshot_download(repo_id, revision=revision, force_download=force_download,
+                                      allow_patterns=[f"{model_path}/*"] if model_path else None))
+        return cls.load_from_disk(root / model_path if model_path else root, device=device)
 
     @classmethod
     def load_from_source(cls, source: str | Path, device: str | torch.device = "cpu") -> "SyntheticModel":
@@ -230,19 +256,44 @@ class SyntheticModel(nn.Module):
 
 # ---------------------------------------------------------------------------- training helpers
 class SyntheticActivationIterator(Iterator[torch.Tensor]):
-    """Endless iterator of hidden-activation batches from a SyntheticModel (a data provider)."""
+    """Endless iterator of hidden-activation batches (a data provider): feature activations from an
+    ActivationGenerator mapped through a FeatureDictionary (sae_lens/synthetic/training.py:117-165).
 
-    def __init__(self, model: SyntheticModel, batch_size: int, dtype: torch.dtype | None = None,
+    `SyntheticActivationIterator(feature_dict, activations_generator, batch_size, autocast)` as in
+    the reference, or `SyntheticActivationIterator(model, batch_size)` with a SyntheticModel.  With
+    `autocast` the generator and the dictionary run under bfloat16 autocast; `dtype` / `device`
+    cast the served batches."""
+
+    def __init__(self, feature_dict: Any, activations_generator: Any = None, batch_size: int | None = None,
+                 autocast: bool = False, dtype: torch.dtype | None = None,
                  device: str | torch.device | None = None):
-        self.model, self.batch_size, self.dtype = model, batch_size, dtype
-        self.device = torch.device(device) if device is not None else model.device
+        if isinstance(activations_generator, int) and batch_size is None:  # (model, batch_size)
+            activations_generator, batch_size = None, activations_generator
+        if batch_size is None:
+            raise TypeError("batch_size is required")
+        self.model = feature_dict if activations_generator is None else None
+        if self.model is not None:
+            feature_dict, activations_generator = self.model.feature_dict, self.model.activation_generator
+        self.feature_dict, self.activations_generator = feature_dict, activations_generator
+        self.batch_size, self.autocast, self.dtype = int(batch_size), bool(autocast), dtype
+        self.device = torch.device(device) if device is not None else feature_dict.feature_vectors.device
+
+    @torch.no_grad()
+    def next_batch(self) -> torch.Tensor:
+        dev_type = self.feature_dict.feature_vectors.device.type
+        with torch.autocast(device_type=dev_type, dtype=torch.bfloat16, enabled=self.autocast):
+            if self.model is not None:
+                x = self.model.sample(self.batch_size)
+            else:
+                x = self.feature_dict(self.activations_generator(self.batch_size))
+        x = x.to(self.device)
+        return x.to(self.dtype) if self.dtype is not None else x
 
     def __iter__(self) -> "SyntheticActivationIterator":
         return self
 
     def __next__(self) -> torch.Tensor:
-        x = self.model.sample(self.batch_size).to(self.device)
-        return x.to(self.dtype) if self.dtype is not None else x
+        return self.next_batch()
 
 
 def init_sae_to_match_feature_dict(sae: Any, feature_dict: FeatureDictionary, noise_level: float = 0.0,
@@ -265,25 +316,45 @@ def init_sae_to_match_feature_dict(sae: Any, feature_dict: FeatureDictionary, no
         sae.b_dec.zero_()
 
 
-def train_toy_sae(sae: Any, model: SyntheticModel, training_samples: int = 2_000_000, batch_size: int = 1024,
-                  lr: float = 3e-4, device: str | torch.device | None = None) -> list[float]:
-    """Minimal training loop (Adam on the SAE's own training forward pass) for quick experiments;
-    returns the loss history.  Use SyntheticSAERunner for full trainer features."""
-    from saelens_b200.models.sae import TrainStepInput
+def train_toy_sae(sae: Any, feature_dict: Any, activations_generator: Any = None, training_samples: int = 10_000_000,
+                  batch_size: int = 1024, lr: float = 3e-4, lr_warm_up_steps: int = 0, lr_decay_steps: int = 0,
+                  device: str | torch.device = "cpu", n_snapshots: int = 0,
+                  snapshot_fn: Callable[[Any], None] | None = None, autocast_sae: bool = False,
+                  autocast_data: bool = False) -> None:
+    """Train `sae` on synthetic activations with the framework's SAETrainer (constant LR with
+    optional warm-up / decay, Adam 0.9 / 0.999, no files written): a convenience for small
+    experiments (sae_lens/synthetic/training.py:14-114).  `n_snapshots` evenly spaced points call
+    `snapshot_fn(trainer)`.  `feature_dict` may also be a SyntheticModel (its dictionary and
+    generator are used; `activations_generator` is then omitted)."""
+    from saelens_b200.config import LoggingConfig, SAETrainerConfig
+    from saelens_b200.training.sae_trainer import SAETrainer
 
-    dev = torch.device(device) if device is not None else next(iter(sae.parameters())).device
-    opt = torch.optim.Adam(sae.parameters(), lr=lr)
-    it = SyntheticActivationIterator(model, batch_size, device=dev)
-    losses = []
-    for step in range(max(1, training_samples // batch_size)):
-        x = next(it).to(sae.W_enc.dtype)
-        out = sae.training_forward_pass(TrainStepInput(sae_in=x, coefficients={"l1": 1.0}, dead_neuron_mask=None,
-                                                       n_training_steps=step))
-        opt.zero_grad(set_to_none=True)
-        out.loss.backward()
-        opt.step()
-        losses.append(float(out.loss.detach()))
-    return losses
+    if n_snapshots > 0 and snapshot_fn is None:
+        raise ValueError("snapshot_fn must be provided to take snapshots")
+    if activations_generator is None:
+        data = SyntheticActivationIterator(feature_dict, batch_size, autocast=autocast_data)
+        feature_dict = feature_dict.feature_dict
+    else:
+        data = SyntheticActivationIterator(feature_dict, activations_generator, batch_size, autocast=autocast_data)
+    cfg = SAETrainerConfig(
+        n_checkpoints=n_snapshots, checkpoint_path=None, save_final_checkpoint=False, output_path=None,
+        save_mse_every_n_steps=0, save_timing_every_n_steps=0, save_memory_every_n_steps=0,
+        synchronize_timing=False, multi_sae_backward_order="forward", multi_sae_stats_sync_mode="immediate",
+        multi_sae_stats_sync_interval=1, total_training_samples=training_samples, device=str(device),
+        autocast=autocast_sae, lr=lr, lr_end=lr, lr_scheduler_name="constant", lr_warm_up_steps=lr_warm_up_steps,
+        adam_beta1=0.9, adam_beta2=0.999, lr_decay_steps=lr_decay_steps, n_restart_cycles=1,
+        train_batch_size_samples=batch_size, dead_feature_window=1000, feature_sampling_window=2000,
+        logger=LoggingConfig(log_to_wandb=False, eval_every_n_wandb_logs=2**31 - 1))
+    feature_dict.eval()
+    holder: dict[str, Any] = {}
+
+    def on_checkpoint(checkpoint_path: Any = None) -> None:  # noqa: ARG001 - the trainer's callback form
+        if snapshot_fn is not None:
+            snapshot_fn(holder["trainer"])
+
+    trainer = SAETrainer(cfg, sae, data, save_checkpoint_fn=on_checkpoint)
+    holder["trainer"] = trainer
+    trainer.fit()
 
 
 # ---------------------------------------------------------------------------- statistics

@@ -18,7 +18,12 @@ import torch
 
 from saelens_b200.config import LoggingConfig, SAETrainerConfig
 from saelens_b200.synthetic.evals import SyntheticDataEvalResult, eval_sae_on_synthetic_data
-from saelens_b200.synthetic.model import SyntheticActivationIterator, SyntheticModel, SyntheticModelConfig
+from saelens_b200.synthetic.model import (
+    SYNTHETIC_MODEL_CONFIG_FILENAME,
+    SyntheticActivationIterator,
+    SyntheticModel,
+    SyntheticModelConfig,
+)
 from saelens_b200.utils.misc import cosine_similarities
 
 RUNNER_CONFIG_FILENAME = "synthetic_runner_config.json"
@@ -174,41 +179,105 @@ def find_best_feature_ordering_across_saes(saes: Iterable[Any], feature_dict: An
     return best_order
 
 
-def plot_sae_feature_similarity(sae: Any, feature_dict: Any, reorder_features: bool = True,
-                                title: str | None = None, save_path: str | None = None) -> Any:
-    """Heatmap of |cos(SAE decoder, ground truth)| (requires matplotlib); returns the figure."""
-    import matplotlib
+def feature_similarity_matrices(sae: Any, feature_dict: Any,
+                                reorder_features: bool | torch.Tensor = False) -> tuple[torch.Tensor, torch.Tensor]:
+    """(encoder, decoder) cosine similarities of the SAE latents with the true features, rounded
+    to two decimals, rows reordered by `find_best_feature_ordering` (True) or by the given index
+    tensor: the matrices `plot_sae_feature_similarity` draws."""
+    true = feature_dict.feature_vectors.detach().float()
+    dec = torch.round(cosine_similarities(sae.W_dec.detach().float(), true) * 100) / 100
+    enc = torch.round(cosine_similarities(sae.W_enc.detach().float().T, true) * 100) / 100
+    if reorder_features is not False:
+        order = (find_best_feature_ordering(sae.W_dec.detach(), true) if isinstance(reorder_features, bool)
+                 else reorder_features)
+        dec, enc = dec[order], enc[order]
+    return enc, dec
 
-    matplotlib.use("Agg")
-    import matplotlib.pyplot as plt
 
-    W = sae.W_dec.detach().float()
-    if reorder_features:
-        W = W[find_best_feature_ordering_from_sae(sae, feature_dict)]
-    sim = cosine_similarities(W, feature_dict.feature_vectors.detach().float()).abs().cpu().numpy()
-    fig, ax = plt.subplots(figsize=(6, 5))
-    im = ax.imshow(sim, vmin=0, vmax=1, cmap="viridis", aspect="auto")
-    ax.set_xlabel("ground-truth feature")
-    ax.set_ylabel("SAE latent")
-    ax.set_title(title or "SAE decoder vs ground-truth features (|cos|)")
-    fig.colorbar(im, ax=ax)
+def plot_sae_feature_similarity(sae: Any, feature_dict: Any, title: str | None = None,
+                                reorder_features: bool | torch.Tensor = False, decoder_only: bool = False,
+                                show_values: bool = False, height: int = 400, width: int = 800,
+                                save_path: str | Path | None = None, show_plot: bool = True, dtick: int | None = 1,
+                                scale: float = 1.0) -> Any:
+    """Heatmaps of the SAE encoder's and decoder's cosine similarity with the true features
+    (sae_lens/synthetic/plotting.py:102-230; plotly, an optional dependency as in the reference).
+    Returns the figure."""
+    try:
+        import plotly.graph_objects as go
+        from plotly.subplots import make_subplots
+    except ImportError as e:  # pragma: no cover - depends on the environment
+        raise ImportError("plot_sae_feature_similarity needs plotly (pip install plotly)") from e
+    enc, dec = feature_similarity_matrices(sae, feature_dict, reorder_features)
+    hover = "True feature: %{x}<br>SAE Latent: %{y}<br>Cosine Similarity: %{z:.3f}<extra></extra>"
+
+    def heatmap(z: torch.Tensor, with_scale: bool) -> Any:
+        kw: dict[str, Any] = {"z": z.cpu().numpy(), "zmin": -1, "zmax": 1, "colorscale": "RdBu",
+                              "hovertemplate": hover}
+        if with_scale:
+            kw["colorbar"] = {"title": "cos sim", "x": 1.0, "dtick": 1, "tickvals": [-1, 0, 1]}
+        else:
+            kw["showscale"] = False
+        if show_values:
+            kw.update(texttemplate="%{z:.2f}", textfont={"size": 10})
+        return go.Heatmap(**kw)
+
+    panels = [("SAE decoder", dec, True)] if decoder_only else [("SAE encoder", enc, False), ("SAE decoder", dec, True)]
+    fig = make_subplots(rows=1, cols=len(panels),
+                        subplot_titles=None if decoder_only else tuple(name for name, _, _ in panels))
+    for col, (_, z, with_scale) in enumerate(panels, start=1):
+        fig.add_trace(heatmap(z, with_scale), row=1, col=col)
+        fig.update_xaxes(title_text="True feature", row=1, col=col, dtick=dtick)
+        fig.update_yaxes(title_text="SAE Latent", row=1, col=col, dtick=dtick)
+    fig.update_layout(height=height, width=width, title_text=title or "Cosine similarity with true features")
     if save_path:
-        fig.savefig(save_path, bbox_inches="tight")
+        Path(save_path).parent.mkdir(parents=True, exist_ok=True)
+        fig.write_image(str(save_path), scale=scale)
+    if show_plot:
+        fig.show()
     return fig
 
 
-def upload_synthetic_model_to_huggingface(model: SyntheticModel | str | Path, repo_id: str,
-                                          subfolder: str | None = None, private: bool = False,
-                                          revision: str | None = None) -> None:
-    """Save (if needed) and upload a synthetic model folder to the Hugging Face hub."""
+def upload_synthetic_model_to_huggingface(model: SyntheticModel | str | Path, hf_repo_id: str,
+                                          hf_path: str | None = None, hf_revision: str = "main",
+                                          add_default_readme: bool = True, private: bool = False) -> None:
+    """Save (if given as a model) and upload a synthetic model folder to the Hugging Face hub, at
+    the repo root or in `hf_path`; with `add_default_readme` a README.md describing the model is
+    added when the repo has none (sae_lens/synthetic/upload_synthetic_model.py:24-71)."""
+    import io
     import tempfile
 
     from huggingface_hub import HfApi
 
     api = HfApi()
-    api.create_repo(repo_id, private=private, exist_ok=True)
+    api.create_repo(hf_repo_id, private=private, exist_ok=True)
     with tempfile.TemporaryDirectory() as tmp:
         path = Path(model) if not isinstance(model, SyntheticModel) else Path(tmp) / "model"
         if isinstance(model, SyntheticModel):
             model.save(path)
-        api.upload_folder(folder_path=str(path), repo_id=repo_id, path_in_repo=subfolder or ".", revision=revision)
+        if not (path / SYNTHETIC_MODEL_CONFIG_FILENAME).exists():
+            raise FileNotFoundError(f"{path} holds no {SYNTHETIC_MODEL_CONFIG_FILENAME}")
+        api.upload_folder(folder_path=str(path), repo_id=hf_repo_id, path_in_repo=hf_path or ".",
+                          revision=hf_revision)
+        if add_default_readme and not api.file_exists(hf_repo_id, "README.md", revision=hf_revision):
+            synth = model if isinstance(model, SyntheticModel) else SyntheticModel.load_from_disk(path)
+            text = default_synthetic_model_readme(hf_repo_id, hf_path, synth)
+            api.upload_file(path_or_fileobj=io.BytesIO(text.encode("utf-8")), path_in_repo="README.md",
+                            repo_id=hf_repo_id, revision=hf_revision, commit_message="Add README.md")
+
+
+def default_synthetic_model_readme(repo_id: str, path: str | None, model: SyntheticModel) -> str:
+    """README of an uploaded synthetic model: its sizes, its generators and how to load it."""
+    cfg = model.cfg
+    where = f'"{repo_id}", model_path="{path}"' if path else f'"{repo_id}"'
+    lines = [
+        "---", "library_name: saelens", "tags:", "- synthetic", "- sparse-autoencoder", "---", "",
+        f"# Synthetic model `{repo_id}`" + (f" (`{path}`)" if path else ""), "",
+        "Ground-truth feature dictionary and activation generator for benchmarking sparse autoencoders.", "",
+        f"* features: {cfg.num_features}", f"* hidden dimension: {cfg.hidden_dim}",
+        f"* firing probabilities: {cfg.firing_probability.to_dict()}",
+        f"* hierarchy: {'yes' if cfg.hierarchy is not None else 'no'}",
+        f"* correlation: {'low-rank' if cfg.correlation is not None else 'none'}", "",
+        "```python", "from saelens_b200.synthetic import SyntheticModel", "",
+        f"model = SyntheticModel.from_pretrained({where})", "hidden = model.sample(1024)", "```", "",
+    ]
+    return "\n".join(lines)
