@@ -31,7 +31,7 @@ CorrelationMatrixInput = Union[torch.Tensor, LowRankCorrelationMatrix, tuple[tor
 
 # ------------------------------------------------------------------------------ dictionary
 def orthogonalize_embeddings(embeddings: torch.Tensor, num_steps: int = 200, lr: float = 0.01,
-                             chunk_size: int = 1024) -> torch.Tensor:
+                             show_progress: bool = False, chunk_size: int = 1024) -> torch.Tensor:
     """Reduce pairwise cosine similarity of unit rows by gradient descent on sum_{i != j} (e_i . e_j)^2,
     renormalising after every step.  With n <= d the rows become exactly orthonormal (QR)."""
     n, d = embeddings.shape
@@ -39,7 +39,12 @@ def orthogonalize_embeddings(embeddings: torch.Tensor, num_steps: int = 200, lr:
         q, _ = torch.linalg.qr(embeddings.T.float())
         return q.T.contiguous().to(embeddings.dtype)
     e = (embeddings / embeddings.norm(dim=1, keepdim=True).clamp(min=1e-8)).float().clone()
-    for _ in range(num_steps):
+    steps = range(num_steps)
+    if show_progress:
+        from tqdm.auto import tqdm
+
+        steps = tqdm(steps, desc="orthogonalizing")
+    for _ in steps:
         grad = torch.zeros_like(e)
         for s in range(0, n, chunk_size):
             blk = e[s : s + chunk_size]
@@ -51,10 +56,12 @@ def orthogonalize_embeddings(embeddings: torch.Tensor, num_steps: int = 200, lr:
     return e.to(embeddings.dtype)
 
 
-def orthogonal_initializer(num_steps: int = 200, lr: float = 0.01, chunk_size: int = 1024) -> FeatureDictionaryInitializer:
+def orthogonal_initializer(num_steps: int = 200, lr: float = 0.01, show_progress: bool = False,
+                           chunk_size: int = 1024) -> FeatureDictionaryInitializer:
     def init(fd: "FeatureDictionary") -> None:
         with torch.no_grad():
-            fd.feature_vectors.copy_(orthogonalize_embeddings(fd.feature_vectors.data, num_steps, lr, chunk_size))
+            fd.feature_vectors.copy_(orthogonalize_embeddings(fd.feature_vectors.data, num_steps=num_steps, lr=lr,
+                                                              show_progress=show_progress, chunk_size=chunk_size))
 
     return init
 

@@ -131,7 +131,7 @@ class SyntheticModel(nn.Module):
         init = None
         if "feature_vectors" not in t and cfg.orthogonalization is not None:
             o = cfg.orthogonalization
-            init = orthogonal_initializer(o.num_steps, o.lr, o.chunk_size)
+            init = orthogonal_initializer(num_steps=o.num_steps, lr=o.lr, chunk_size=o.chunk_size)
         self.feature_dict = FeatureDictionary(cfg.num_features, cfg.hidden_dim, bias=cfg.bias, initializer=init,
                                               device=self.device, seed=cfg.seed)
         if "feature_vectors" in t:
