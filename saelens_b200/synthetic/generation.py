@@ -240,7 +240,8 @@ class HierarchyNode:
         self.feature_id = feature_id
 
     @classmethod
-    def from_dict(cls, d: dict[str, Any]) -> "HierarchyNode":
+    def from_dict(cls, tree_dict: dict[str, Any]) -> "HierarchyNode":
+        d = tree_dict
         return cls(feature_index=d.get("feature_index"), children=[cls.from_dict(c) for c in d.get("children", [])],
                    mutually_exclusive_children=d.get("mutually_exclusive_children", False),
                    scale_children_by_parent=d.get("scale_children_by_parent", False), feature_id=d.get("id"))

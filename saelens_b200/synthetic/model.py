@@ -122,19 +122,28 @@ class SyntheticModel(nn.Module):
     """`sample(batch)` -> hidden activations [batch, hidden_dim]; `sample_with_features(batch)` also
     returns the ground-truth feature activations."""
 
-    def __init__(self, cfg: SyntheticModelConfig, device: str | torch.device = "cpu",
-                 _tensors: dict[str, torch.Tensor] | None = None, _hierarchy: Hierarchy | None = None):
+    def __init__(self, cfg: SyntheticModelConfig, feature_dict: FeatureDictionary | None = None,
+                 activation_generator: ActivationGenerator | None = None, hierarchy: Hierarchy | None = None,
+                 correlation_matrix: LowRankCorrelationMatrix | None = None, device: str | torch.device = "cpu",
+                 _tensors: dict[str, torch.Tensor] | None = None):
+        """Built from `cfg` (and its seed); components given explicitly (a feature dictionary, a
+        generator, a hierarchy, a low-rank correlation) are used instead of being generated, as in
+        sae_lens/synthetic/synthetic_model.py's constructor.  `_tensors` restores saved state."""
         super().__init__()
         self.cfg = cfg
         self.device = torch.device(device)
-        t = _tensors or {}
+        _hierarchy = hierarchy
+        t = dict(_tensors or {})
+        if correlation_matrix is not None:
+            t["correlation_factor"] = correlation_matrix.correlation_factor
+            t["correlation_diag"] = correlation_matrix.correlation_diag
         init = None
-        if "feature_vectors" not in t and cfg.orthogonalization is not None:
+        if feature_dict is None and "feature_vectors" not in t and cfg.orthogonalization is not None:
             o = cfg.orthogonalization
             init = orthogonal_initializer(num_steps=o.num_steps, lr=o.lr, chunk_size=o.chunk_size)
-        self.feature_dict = FeatureDictionary(cfg.num_features, cfg.hidden_dim, bias=cfg.bias, initializer=init,
-                                              device=self.device, seed=cfg.seed)
-        if "feature_vectors" in t:
+        self.feature_dict = feature_dict if feature_dict is not None else FeatureDictionary(
+            cfg.num_features, cfg.hidden_dim, bias=cfg.bias, initializer=init, device=self.device, seed=cfg.seed)
+        if feature_dict is None and "feature_vectors" in t:
             with torch.no_grad():
                 self.feature_dict.feature_vectors.copy_(t["feature_vectors"])
                 self.feature_dict.bias.copy_(t["bias"])
@@ -156,7 +165,7 @@ class SyntheticModel(nn.Module):
             corr = generate_random_low_rank_correlation_matrix(cfg.num_features, cfg.correlation.rank,
                                                                cfg.correlation.correlation_scale, seed=cfg.seed + 3)
         self.correlation = corr
-        self.activation_generator = ActivationGenerator(
+        self.activation_generator = activation_generator if activation_generator is not None else ActivationGenerator(
             cfg.num_features, probs, std_firing_magnitudes=std, mean_firing_magnitudes=mean,
             modify_activations=self.hierarchy.modifier if self.hierarchy is not None else None,
             correlation_matrix=corr, device=self.device, dtype=cfg.dtype)
@@ -232,7 +241,7 @@ class SyntheticModel(nn.Module):
         t = {k: v.to(device) for k, v in load_file(str(p / SYNTHETIC_MODEL_WEIGHTS_FILENAME)).items()}
         hp = p / SYNTHETIC_MODEL_HIERARCHY_FILENAME
         h = Hierarchy.from_dict(json.loads(hp.read_text())) if hp.exists() else None
-        return cls(cfg, device=device, _tensors=t, _hierarchy=h)
+        return cls(cfg, hierarchy=h, device=device, _tensors=t)
 
     @classmethod
     def from_pretrained(cls, repo_id: str, model_path: str | None = None, device: str | torch.device = "cpu",

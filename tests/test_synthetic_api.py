@@ -157,3 +157,14 @@ def test_synthetic_model_to_moves_the_generator_state() -> None:
     assert model.to(None) is model
     assert model.activation_generator.firing_probabilities.device.type == "cpu"
     assert model.sample(5).shape == (5, 16)
+
+
+def test_synthetic_model_from_prebuilt_components() -> None:
+    cfg = SyntheticModelConfig(num_features=8, hidden_dim=16, seed=5)
+    fd, gen = _setup(8, 16, seed=6)
+    lr = generate_random_low_rank_correlation_matrix(8, rank=2, correlation_scale=0.2, seed=1)
+    m = SyntheticModel(cfg, feature_dict=fd, activation_generator=gen, correlation_matrix=lr)
+    assert m.feature_dict is fd and m.activation_generator is gen
+    assert torch.equal(m.correlation.correlation_factor, lr.correlation_factor)
+    h, f = m.sample_with_features(12)
+    assert h.shape == (12, 16) and f.shape == (12, 8)
