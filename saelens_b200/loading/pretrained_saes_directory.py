@@ -2,14 +2,17 @@
 
 Same YAML schema as the reference's directory (sae_lens/loading/pretrained_saes_directory.py:
 release keys with `repo_id`, `model`, `conversion_func`, `saes: [{id, path, l0,
-variance_explained, neuronpedia, norm_scaling_factor}]`, `config_overrides`).  The package ships a
-small directory.  The full directory is found, in this order of precedence (later entries
-override earlier ones):
-1. the shipped `pretrained_saes.yaml`;
-2. the `pretrained_saes.yaml` of an installed `sae_lens` package, located on `sys.path` without
-   importing it (the reference's 156-release directory, same schema);
-3. every file named in `SAELENS_B200_PRETRAINED_YAML` (`os.pathsep`-separated);
-4. releases added at runtime with `register_release`.
+variance_explained, neuronpedia, norm_scaling_factor}]`, `config_overrides`).  The package ships
+the full directory of published releases (156 releases, 13k SAEs) as a gzip-compressed columnar
+index (`pretrained_saes_index.json.gz`, read by `pretrained_index.load_index` in about 0.1 s).
+Sources, in this order of precedence (later entries override earlier ones):
+1. the shipped `pretrained_saes.yaml` (a few hand-kept releases);
+2. the shipped index;
+3. the `pretrained_saes.yaml` of an installed `sae_lens` package, located on `sys.path` without
+   importing it (same schema; a newer package brings newer releases);
+4. every file named in `SAELENS_B200_PRETRAINED_YAML` (`os.pathsep`-separated; a `.json.gz`
+   name is read as an index);
+5. releases added at runtime with `register_release`.
 """
 
 from __future__ import annotations
@@ -21,6 +24,8 @@ from importlib.resources import files
 from typing import Any
 
 import yaml
+
+from .pretrained_index import INDEX_NAME, load_index
 
 
 @dataclass
@@ -82,7 +87,11 @@ def installed_sae_lens_directory() -> str | None:
 
 def directory_files() -> list[str]:
     """The YAML files the directory is read from, lowest precedence first."""
-    out = [str(files("saelens_b200.loading").joinpath("pretrained_saes.yaml"))]
+    here = files("saelens_b200.loading")
+    out = [str(here.joinpath("pretrained_saes.yaml"))]
+    index = str(here.joinpath(INDEX_NAME))
+    if os.path.isfile(index):
+        out.append(index)
     ref = installed_sae_lens_directory()
     if ref:
         out.append(ref)
@@ -96,8 +105,11 @@ def directory_files() -> list[str]:
 def _load_files() -> dict[str, PretrainedSAELookup]:
     directory: dict[str, PretrainedSAELookup] = {}
     for path in directory_files():
+        if path.endswith(".json.gz"):
+            directory.update(_parse(load_index(path)))
+            continue
         with open(path) as f:
-            directory.update(_parse(yaml.safe_load(f)))
+            directory.update(_parse(yaml.load(f, Loader=getattr(yaml, "CSafeLoader", yaml.SafeLoader))))
     return directory
 
 

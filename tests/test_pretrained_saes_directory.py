@@ -93,3 +93,70 @@ def test_installed_reference_directory_is_found_without_import(tmp_path, monkeyp
         assert "sae_lens" not in sys.modules
     finally:
         d._load_files.cache_clear()
+
+
+def test_shipped_index_holds_the_full_directory():
+    from saelens_b200.loading.pretrained_saes_directory import directory_files
+
+    assert any(p.endswith("pretrained_saes_index.json.gz") for p in directory_files())
+    d = get_pretrained_saes_directory()
+    assert len(d) >= 150
+    assert sum(len(v.saes_map) for v in d.values()) > 10_000
+    assert len(d["gpt2-small-res-jb"].saes_map) == 13  # every layer's resid_pre, plus the last resid_post
+    assert get_repo_id_and_folder_name("gemma-scope-2b-pt-res-canonical", "layer_12/width_16k/canonical") == \
+        ("google/gemma-scope-2b-pt-res", "layer_12/width_16k/average_l0_82")
+    # A folder name written as a bare number in the source YAML stays a number.
+    assert d["mntss-gemma-2-2b-2.5m-clt-as-per-layer"].saes_map["layer_0"] == 0
+
+
+def _sample_directory():
+    return {
+        "rel-a": {"repo_id": "org/a", "model": "m", "conversion_func": None,
+                  "links": {"model": "https://example.org"},
+                  "config_overrides": {"model_from_pretrained_kwargs": {"center_writing_weights": True}},
+                  "saes": [{"id": "s0", "path": "s0", "l0": 12.0, "neuronpedia": "m/0"},
+                           {"id": "s1", "path": "deep/s1", "variance_explained": 0.7,
+                            "norm_scaling_factor": 3.5},
+                           {"id": "layer_0", "path": 0}]},
+        "rel-b": {"repo_id": "org/b", "model": "m2", "conversion_func": "gemma_2",
+                  "saes": [{"id": "x", "path": "y"}]},
+    }
+
+
+def test_index_round_trip_is_lossless():
+    from saelens_b200.loading.pretrained_index import compact_directory, expand_index
+    from saelens_b200.loading.pretrained_saes_directory import _parse
+
+    data = _sample_directory()
+    back = expand_index(compact_directory(data))
+    assert back == data
+    assert _parse(back) == _parse(data)
+    parsed = _parse(back)["rel-a"]
+    assert parsed.expected_l0 == {"s0": 12.0, "s1": 0.0, "layer_0": 0.0}
+    assert parsed.expected_var_explained["s1"] == 0.7 and parsed.expected_var_explained["s0"] == 1.0
+    assert parsed.norm_scaling_factor == {"s1": 3.5}
+
+
+def test_build_index_from_yaml_and_extra_index_file(tmp_path, monkeypatch):
+    import yaml
+
+    from saelens_b200.loading import pretrained_saes_directory as psd
+    from saelens_b200.loading.pretrained_index import build_index, load_index
+
+    data = _sample_directory()
+    src = tmp_path / "dir.yaml"
+    src.write_text(yaml.safe_dump(data))
+    out = tmp_path / "extra.json.gz"
+    assert build_index(str(src), str(out)) == 2
+    first = out.read_bytes()
+    build_index(str(src), str(out))
+    assert out.read_bytes() == first  # deterministic output
+    assert psd._parse(load_index(str(out))) == psd._parse(data)
+    monkeypatch.setenv("SAELENS_B200_PRETRAINED_YAML", str(out))
+    psd._load_files.cache_clear()
+    try:
+        assert get_repo_id_and_folder_name("rel-b", "x") == ("org/b", "y")
+        assert get_conversion_loader_name("rel-b") == "gemma_2"
+    finally:
+        monkeypatch.delenv("SAELENS_B200_PRETRAINED_YAML")
+        psd._load_files.cache_clear()
